@@ -1,0 +1,141 @@
+"""Generate golden vectors by running the reference implementation itself.
+
+Run from the repository root in a checkout that has the reference project
+available (its ``src`` directory importable as ``pe``)::
+
+    PE_REFERENCE_SRC=<reference>/src python tests/golden/make_golden.py
+
+For every case in ``recipe.CASES`` this builds the reference ``ParallelDrafter``
+from seeded synthetic frozen heads, runs the reference ``mtp_backward`` (and
+``mtp_eval_loss`` / ``forward``) and writes ``tests/golden/<case>.pt`` with the
+losses, the accumulated gradients (full tensors for the tiny cases, random-
+projection sketches for the larger one) and checksums of every input.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import types
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+import recipe  # noqa: E402
+
+_DT = {"float32": torch.float32, "bfloat16": torch.bfloat16}
+
+
+def _reference():
+    src = os.environ.get("PE_REFERENCE_SRC")
+    if not src:
+        raise SystemExit("set PE_REFERENCE_SRC to the reference project's src directory")
+    sys.path.insert(0, src)
+    import pe.drafter
+    import pe.nn
+    import pe.partition
+
+    return pe
+
+
+def _heads_object(pe, c, heads):
+    """The minimal target-heads surface ``ParallelDrafter.from_target`` reads."""
+    H, V = c["hidden"], c["vocab"]
+    embed = torch.nn.Embedding(V, H)
+    embed.weight.data = heads["embed"].clone()
+    head = torch.nn.Linear(H, V, bias=False)
+    head.weight.data = heads["head"].clone()
+    norm = pe.nn.RMSNorm(H, 1e-5)
+    norm.weight.data = heads["norm"].clone()
+    for m in (embed, head, norm):
+        for p in m.parameters():
+            p.requires_grad_(False)
+    cfg = types.SimpleNamespace(
+        num_attention_heads=c["n_heads"], num_key_value_heads=c["n_kv_heads"],
+        intermediate_size=c["intermediate"], rope_theta=10000.0, rms_norm_eps=1e-5,
+        hidden_size=H, vocab_size=V,
+    )
+    return types.SimpleNamespace(
+        config=cfg, hidden_size=H, vocab_size=V, feature_dim=3 * H,
+        get_input_embeddings=lambda: embed, get_lm_head=lambda: head,
+        get_final_norm=lambda: norm,
+    )
+
+
+def build_case(pe, name: str, c: dict) -> dict:
+    from pe.config import DrafterConfig
+    from pe.drafter import ParallelDrafter
+    from pe.partition import mtp_backward, mtp_eval_loss
+
+    dt = _DT[c["dtype"]]
+    heads = recipe.make_heads(c["vocab"], c["hidden"], c["seed"], c["norm_jitter"], dt)
+    target = _heads_object(pe, c, heads)
+    torch.manual_seed(c["seed"])
+    drafter = ParallelDrafter.from_target(
+        target, DrafterConfig(num_layers=c["num_layers"], max_depth=c["max_depth"])
+    ).to(dtype=dt)
+    drafter.train()
+    params = {k: v.detach().clone() for k, v in drafter.state_dict().items()}
+    batch = c.get("batch", 1)
+    seqs = [recipe.make_sequence(c["n"], c["vocab"], 3 * c["hidden"], c["seed"], b) for b in range(batch)]
+
+    out = {"case": name, "config": {k: v for k, v in c.items() if k != "runs"}, "runs": []}
+    out["input_checksum"] = {
+        "ids": [int(ids.sum()) for ids, _ in seqs],
+        "feats": [float(f.double().sum()) for _, f in seqs],
+        "feats_sketch": [recipe.sketch(f, 1) for _, f in seqs],
+    }
+    if c["full"]:
+        out["params"] = params
+    else:
+        out["param_sketch"] = {k: recipe.sketch(v, i) for i, (k, v) in enumerate(params.items())}
+        out["param_sum"] = {k: float(v.double().sum()) for k, v in params.items()}
+
+    for run in c["runs"]:
+        drafter.zero_grad(set_to_none=True)
+        losses = []
+        for ids, feats in seqs:
+            kw = dict(
+                num_segments=run["num_segments"],
+                loss_scale=run.get("loss_scale", 1.0 / batch),
+                prompt_len=run.get("prompt_len", 0),
+            )
+            if run.get("teacher_labels"):
+                kw["teacher_labels"] = recipe.teacher_labels_for(ids)
+            losses.append(mtp_backward(drafter, ids, feats.to(dt), **kw))
+        grads = {k: p.grad.detach().clone() for k, p in drafter.named_parameters() if p.grad is not None}
+        rec = {"run": run, "losses": losses}
+        if c["full"]:
+            rec["grads"] = grads
+        else:
+            rec["grad_sketch"] = {
+                k: recipe.sketch(g, 100 + i) for i, (k, g) in enumerate(grads.items())
+            }
+            rec["grad_norm"] = {k: float(g.double().norm()) for k, g in grads.items()}
+        out["runs"].append(rec)
+
+    ids, feats = seqs[0]
+    out["eval_loss"] = mtp_eval_loss(drafter, ids, feats.to(dt))
+    if c["full"]:
+        # generic forward with an explicit additive bias: the anchor-major packing
+        with torch.no_grad():
+            x, pos, bias, labels = drafter.build_training_packed(ids, feats.to(dt))
+            out["packed"] = {
+                "x": x.clone(), "pos": pos.clone(), "bias": bias.clone(), "labels": labels.clone(),
+                "hidden": drafter(x, pos, bias).clone(),
+            }
+    return out
+
+
+def main():
+    pe = _reference()
+    for name, c in recipe.CASES.items():
+        rec = build_case(pe, name, c)
+        torch.save(rec, HERE / f"{name}.pt")
+        print(name, [r["losses"] for r in rec["runs"]], "eval", rec["eval_loss"])
+
+
+if __name__ == "__main__":
+    main()
