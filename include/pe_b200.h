@@ -1,0 +1,181 @@
+/*
+ * pe_b200.h -- C ABI of the B200 drafter-training-step library (libpe_b200.so).
+ *
+ * Plain pointers, int64 sizes/strides, a dtype code and a cudaStream_t (passed as
+ * void*).  No entry point allocates device memory: callers pass every output and
+ * workspace buffer.  Every entry point returns 0 on success or a nonzero PE_ERR_*
+ * code; pe_last_error() then returns a message (thread-local).
+ *
+ * Kernels that wait on barriers (the tensor-core paths) bound every wait; a wait
+ * that times out writes a nonzero code into the caller's `status` word (device
+ * int32, may be NULL) and the kernel unwinds instead of hanging.
+ *
+ * Reference citations are to the Python reference project (puneethgv/parallel_eagle),
+ * paths relative to its root; each entry point names the reference operation it
+ * replaces.
+ */
+#ifndef PE_B200_H
+#define PE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define PE_F32 0
+#define PE_BF16 1
+
+/* error codes */
+#define PE_OK 0
+#define PE_ERR_ARG 1     /* invalid argument (shape, stride, alignment, dtype) */
+#define PE_ERR_CUDA 2    /* a CUDA runtime/driver call failed */
+#define PE_ERR_UNSUPPORTED 3
+#define PE_ERR_WORKSPACE 4
+
+/* algorithm selection for pe_gemm / pe_attn_* / pe_lmhead_ce */
+#define PE_ALGO_AUTO 0
+#define PE_ALGO_SIMT 1     /* fp32-FMA CUDA-core kernels (fp32 mode and odd shapes) */
+#define PE_ALGO_TCGEN05 2  /* sm_100a tensor-core kernels (bf16) */
+
+/* attention slot layouts (how the kernel re-derives the attend rule) */
+#define PE_LAYOUT_PARTITION 0 /* real 0..a1-1, then anchors a0..a1-1 x depths 1..K-1 */
+#define PE_LAYOUT_INDEXED 1   /* explicit int32 anchor[]/depth[] per slot */
+#define PE_LAYOUT_BIAS 2      /* caller-supplied dense additive bias */
+
+const char* pe_last_error(void);
+int pe_version(void);
+/* number of kernels this library launched since load (for launch accounting) */
+int64_t pe_launch_count(void);
+
+/* ---------------------------------------------------------------------------
+ * RMSNorm  y = (x * rsqrt(mean(x^2) + eps)) * w, computed in fp32.
+ * Replaces reference src/pe/nn.py:22-26 (RMSNorm.forward) and its autograd
+ * backward.  rows x H, row strides ldx/ldy in elements.
+ * ------------------------------------------------------------------------- */
+int pe_rmsnorm_fwd(int dtype, int64_t rows, int64_t H, const void* x, int64_t ldx,
+                   const void* w, void* y, int64_t ldy, float* rstd, float eps,
+                   void* stream);
+/* dx = (residual ? residual : 0) + d/dx ; dw_partial[nblk, H] (fp32) receives the
+ * per-block partial of sum_rows dy * x * rstd (NULL to skip the weight gradient).
+ * nblk is returned by pe_rmsnorm_bwd_blocks(rows). dx may alias residual. */
+int pe_rmsnorm_bwd(int dtype, int64_t rows, int64_t H, const void* dy, int64_t lddy,
+                   const void* x, int64_t ldx, const void* w, const float* rstd,
+                   void* dx, int64_t lddx, const void* residual, int64_t ldres,
+                   float* dw_partial, void* stream);
+int64_t pe_rmsnorm_bwd_blocks(int64_t rows);
+/* dw (dtype) = (accumulate ? dw : 0) + sum over nblk partial rows */
+int pe_colsum_f32(int dtype, int64_t nblk, int64_t H, const float* partial, void* dw,
+                  int accumulate, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Rotary embedding, half-split (rotate_half), in place on `heads` consecutive
+ * head_dim-wide column blocks of each row.  cos/sin from pos (int64) in fp32 and
+ * rounded to dtype before use.  inverse=1 applies the transpose (backward).
+ * Replaces reference src/pe/nn.py:29-49 (build_rope_cache + apply_rope).
+ * ------------------------------------------------------------------------- */
+int pe_rope(int dtype, int64_t rows, int heads, int head_dim, void* x, int64_t ldx,
+            const int64_t* pos, float theta, int inverse, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * GEMM  C[m,n] = alpha * sum_k A(m,k) B(n,k) + beta * Cin[m,n]
+ *   A(m,k) = A[m*a_sm + k*a_sk], B(n,k) = B[n*b_sn + k*b_sk], C row-major (ldc).
+ * Covers nn.Linear forward (A=x, B=W), its input gradient and weight gradient
+ * (reference src/pe/nn.py:66-69,75-80,89,95-100, src/pe/drafter.py:131-137).
+ * Cin may alias C (in-place accumulation, e.g. into .grad).  c_dtype is the
+ * dtype of C and Cin.
+ * ------------------------------------------------------------------------- */
+int pe_gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm,
+            int64_t a_sk, const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc,
+            int c_dtype, const void* Cin, int64_t ldcin, float alpha, float beta, int algo,
+            int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Cross-depth masked attention (GQA, scale = 1/sqrt(head_dim)), flash-style:
+ * no score matrix is materialised.  q/k/v/o rows are slots, heads are
+ * head_dim-wide column blocks; per-batch strides *_sb, per-slot strides *_ss.
+ * lse[b, h, s] (fp32) is written by fwd and read by bwd.
+ * Layout PARTITION uses (a0, a1, kdepth); INDEXED uses anchor/depth[S];
+ * BIAS uses bias (dtype) with batch stride bias_sb (0 = broadcast) and row
+ * stride bias_sq.
+ * Replaces reference src/pe/nn.py:71-89 (Attention core + repeat_kv) with the mask
+ * of src/pe/masks.py:43-61 / partition.py:41-55,97.
+ * ------------------------------------------------------------------------- */
+int pe_attn_fwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
+                const void* q, int64_t q_sb, int64_t q_ss, const void* k, int64_t k_sb,
+                int64_t k_ss, const void* v, int64_t v_sb, int64_t v_ss, void* o,
+                int64_t o_sb, int64_t o_ss, float* lse, int layout, int64_t a0, int64_t a1,
+                int kdepth, const int32_t* anchor, const int32_t* depth, const void* bias,
+                int64_t bias_sb, int64_t bias_sq, int algo, int32_t* status, void* stream);
+/* dq/dk/dv are overwritten.  delta (fp32 [B, Hq, S]) is workspace. */
+int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
+                const void* q, int64_t q_sb, int64_t q_ss, const void* k, int64_t k_sb,
+                int64_t k_ss, const void* v, int64_t v_sb, int64_t v_ss, const void* o,
+                int64_t o_sb, int64_t o_ss, const void* dout, int64_t do_sb, int64_t do_ss,
+                const float* lse, void* dq, int64_t dq_sb, int64_t dq_ss, void* dk,
+                int64_t dk_sb, int64_t dk_ss, void* dv, int64_t dv_sb, int64_t dv_ss,
+                float* delta, int layout, int64_t a0, int64_t a1, int kdepth,
+                const int32_t* anchor, const int32_t* depth, const void* bias,
+                int64_t bias_sb, int64_t bias_sq, int algo, int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Frozen shared LM head fused with the loss and its input gradient, chunked
+ * over the vocabulary: logits for the whole vocabulary are never stored.
+ *   z = h W^T (rounded to dtype), loss_r = lse(z_r) - z_r[label_r]
+ *   (or, with teacher rows t_r: loss_r = -sum_v softmax(t_r W^T)_v log_softmax(z_r)_v)
+ *   loss_sum[0] += sum_r loss_r;  dh = grad_scale * d(sum_r loss_r)/dh
+ * Rows with label < 0 are ignored.  No gradient reaches W (frozen).
+ * Replaces reference src/pe/partition.py:113-115 (lm_head -> float ->
+ * cross_entropy(sum) -> backward) and drafter.py:123-124.
+ * ------------------------------------------------------------------------- */
+size_t pe_lmhead_ce_workspace(int dtype, int64_t R, int64_t H, int64_t V, int soft);
+int pe_lmhead_ce(int dtype, int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh,
+                 const void* W, const int64_t* labels, const void* teacher, int64_t ldt,
+                 float grad_scale, void* dh, int64_t lddh, float* loss_sum, void* workspace,
+                 size_t workspace_bytes, int algo, int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Small fused pieces of the drafter input / MLP (reference src/pe/drafter.py:126-137,
+ * src/pe/nn.py:99-100).
+ * ------------------------------------------------------------------------- */
+/* out[r, 0:H] = embed[ids[r], :] (embed dtype = dtype) */
+int pe_embed_rows(int dtype, int64_t rows, int64_t H, const int64_t* ids, const void* embed,
+                  void* out, int64_t ldo, void* stream);
+/* out[r, :] = vec for rows r in [0, rows) */
+int pe_fill_rows(int dtype, int64_t rows, int64_t H, const void* vec, void* out, int64_t ldo,
+                 void* stream);
+/* a = silu(g) * u with g = gu[:, 0:I], u = gu[:, I:2I] (each rounded to dtype) */
+int pe_swiglu_fwd(int dtype, int64_t rows, int64_t I, const void* gu, int64_t ldgu, void* a,
+                  int64_t lda, void* stream);
+/* dgu[:, 0:I] = da*u*silu'(g), dgu[:, I:2I] = da*silu(g) */
+int pe_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* da, int64_t ldda,
+                  const void* gu, int64_t ldgu, void* dgu, int64_t lddgu, void* stream);
+/* out[c] (fp32) = sum_r x[r, c] (overwrite) */
+int pe_rowsum_cols(int dtype, int64_t rows, int64_t H, const void* x, int64_t ldx, float* out,
+                   void* stream);
+/* dst[idx[r], :] = src[r, :] (scatter, dst rows not listed are left untouched) and the
+ * inverse gather dst[r, :] = src[idx[r], :] */
+int pe_scatter_rows(int dtype, int64_t rows, int64_t H, const int64_t* idx, const void* src,
+                    int64_t lds, void* dst, int64_t ldd, void* stream);
+int pe_gather_rows(int dtype, int64_t rows, int64_t H, const int64_t* idx, const void* src,
+                   int64_t lds, void* dst, int64_t ldd, void* stream);
+/* y (dtype) = x (fp32) elementwise cast, n elements */
+int pe_cast_f32(int dtype, int64_t n, const float* x, void* y, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Optimizer (reference src/pe/train.py:26-34,158-159: clip_grad_norm_(1.0) then
+ * AdamW.step()).  sumsq_out (fp32 [1]) += sum g^2; the step reads it to apply the
+ * clipping coefficient min(1, max_norm / (sqrt(sumsq) + 1e-6)).
+ * m, v are fp32 moment buffers.
+ * ------------------------------------------------------------------------- */
+int pe_sumsq(int dtype, int64_t n, const void* g, float* sumsq_out, void* stream);
+int pe_adamw_step(int dtype, int64_t n, void* p, const void* g, float* m, float* v,
+                  const float* sumsq, float max_norm, float lr, float beta1, float beta2,
+                  float eps, float weight_decay, int64_t step, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PE_B200_H */

@@ -1,0 +1,68 @@
+// Attend-rule reconstruction shared by the attention kernels.
+//
+// The MTP rule (reference src/pe/masks.py:43-61): query slot (i, d) sees key
+// slot (j, e) iff  e == 0 ? j <= i : (j == i && e <= d).  In the partition
+// layout (reference src/pe/partition.py:41-55) slot s < a1 is (s, 0) and slot
+// a1 + t is (a0 + t / (K-1), 1 + t % (K-1)), so nothing but (a0, a1, K) is
+// needed to know which pairs exist.
+#pragma once
+#include "common.cuh"
+
+namespace pe {
+
+struct MaskSpec {
+  int layout;
+  int64_t a0, a1;
+  int kd;
+  const int32_t* anchor;
+  const int32_t* depth;
+  const void* bias;
+  int64_t bias_sb, bias_sq;
+};
+
+__device__ __forceinline__ void slot_decode(const MaskSpec& m, int64_t s, int64_t& anc, int& dep) {
+  if (m.layout == PE_LAYOUT_PARTITION) {
+    if (s < m.a1) {
+      anc = s;
+      dep = 0;
+    } else {
+      const int64_t t = s - m.a1;
+      const int per = m.kd - 1;
+      anc = m.a0 + t / per;
+      dep = 1 + (int)(t % per);
+    }
+  } else {
+    anc = m.anchor[s];
+    dep = m.depth[s];
+  }
+}
+
+__device__ __forceinline__ bool mtp_allowed(int64_t ai, int di, int64_t aj, int dj) {
+  return dj == 0 ? (aj <= ai) : (aj == ai && dj <= di);
+}
+
+int attn_fwd_simt_launch(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd,
+                         const void* q, int64_t q_sb, int64_t q_ss, const void* k, int64_t k_sb,
+                         int64_t k_ss, const void* v, int64_t v_sb, int64_t v_ss, void* o,
+                         int64_t o_sb, int64_t o_ss, float* lse, const MaskSpec& m,
+                         cudaStream_t st);
+int attn_bwd_simt_launch(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd,
+                         const void* q, int64_t q_sb, int64_t q_ss, const void* k, int64_t k_sb,
+                         int64_t k_ss, const void* v, int64_t v_sb, int64_t v_ss, const void* o,
+                         int64_t o_sb, int64_t o_ss, const void* dout, int64_t do_sb,
+                         int64_t do_ss, const float* lse, void* dq, int64_t dq_sb, int64_t dq_ss,
+                         void* dk, int64_t dk_sb, int64_t dk_ss, void* dv, int64_t dv_sb,
+                         int64_t dv_ss, float* delta, const MaskSpec& m, cudaStream_t st);
+bool attn_tc_eligible(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd, int layout,
+                      const void* q, int64_t q_ss, const void* k, int64_t k_ss, const void* v,
+                      int64_t v_ss);
+int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
+                       int64_t k_ss, const void* v, int64_t v_ss, void* o, int64_t o_ss,
+                       float* lse, const MaskSpec& m, int* status, cudaStream_t st);
+int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
+                       int64_t k_ss, const void* v, int64_t v_ss, const void* o, int64_t o_ss,
+                       const void* dout, int64_t do_ss, const float* lse, void* dq,
+                       int64_t dq_ss, void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
+                       float* delta, const MaskSpec& m, int* status, cudaStream_t st);
+
+}  // namespace pe

@@ -1,0 +1,213 @@
+// Small memory-bound pieces of the drafter input and MLP: embedding gather,
+// broadcast of the shared prediction-slot input, SwiGLU (reference
+// src/pe/nn.py:99-100, src/pe/drafter.py:126-137), row scatter/gather for the
+// loss-slot compaction, column sums for the shared-input backward, casts.
+#include "common.cuh"
+
+namespace pe {
+namespace {
+
+template <typename T>
+__global__ void embed_rows_kernel(int64_t rows, int64_t H, const int64_t* __restrict__ ids,
+                                  const T* __restrict__ embed, T* __restrict__ out, int64_t ldo) {
+  const int64_t r = blockIdx.y;
+  const int64_t id = ids[r];
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < H;
+       c += (int64_t)gridDim.x * blockDim.x)
+    out[r * ldo + c] = embed[id * H + c];
+}
+
+template <typename T>
+__global__ void fill_rows_kernel(int64_t rows, int64_t H, const T* __restrict__ vec,
+                                 T* __restrict__ out, int64_t ldo) {
+  const int64_t total = rows * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / H, c = i - r * H;
+    out[r * ldo + c] = vec[c];
+  }
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+template <typename T>
+__global__ void swiglu_fwd_kernel(int64_t rows, int64_t I, const T* __restrict__ gu, int64_t ldgu,
+                                  T* __restrict__ a, int64_t lda) {
+  const int64_t total = rows * I;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / I, c = i - r * I;
+    const float g = to_f(gu[r * ldgu + c]);
+    const float u = to_f(gu[r * ldgu + I + c]);
+    const float act = round_to<T>(g * sigmoidf_(g));
+    a[r * lda + c] = from_f<T>(act * u);
+  }
+}
+
+template <typename T>
+__global__ void swiglu_bwd_kernel(int64_t rows, int64_t I, const T* __restrict__ da, int64_t ldda,
+                                  const T* __restrict__ gu, int64_t ldgu, T* __restrict__ dgu,
+                                  int64_t lddgu) {
+  const int64_t total = rows * I;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / I, c = i - r * I;
+    const float d = to_f(da[r * ldda + c]);
+    const float g = to_f(gu[r * ldgu + c]);
+    const float u = to_f(gu[r * ldgu + I + c]);
+    const float s = sigmoidf_(g);
+    const float act = round_to<T>(g * s);
+    const float dact = round_to<T>(d * u);
+    dgu[r * lddgu + I + c] = from_f<T>(d * act);
+    dgu[r * lddgu + c] = from_f<T>(dact * (s * (1.0f + g * (1.0f - s))));
+  }
+}
+
+// out[c] = sum_r x[r, c]; 32 columns per block, 8 row lanes, fixed order.
+template <typename T>
+__global__ void rowsum_cols_kernel(int64_t rows, int64_t H, const T* __restrict__ x, int64_t ldx,
+                                   float* __restrict__ out) {
+  __shared__ float red[8][33];
+  const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
+  if (c < H)
+    for (int64_t r = threadIdx.y; r < rows; r += 8) s += to_f(x[r * ldx + c]);
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i][threadIdx.x];
+    out[c] = t;
+  }
+}
+
+template <typename T>
+__global__ void move_rows_kernel(int64_t rows, int64_t H, const int64_t* __restrict__ idx,
+                                 const T* __restrict__ src, int64_t lds, T* __restrict__ dst,
+                                 int64_t ldd, int scatter) {
+  const int64_t r = blockIdx.y;
+  const int64_t s_row = scatter ? r : idx[r];
+  const int64_t d_row = scatter ? idx[r] : r;
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < H;
+       c += (int64_t)gridDim.x * blockDim.x)
+    dst[d_row * ldd + c] = src[s_row * lds + c];
+}
+
+template <typename T>
+__global__ void cast_kernel(int64_t n, const float* __restrict__ x, T* __restrict__ y) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = from_f<T>(x[i]);
+}
+
+unsigned grid_for(int64_t n, int threads) {
+  int64_t g = ceil_div(n, threads);
+  const int64_t cap = (int64_t)sm_count() * 16;
+  if (g > cap) g = cap;
+  return (unsigned)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+}  // namespace pe
+
+using namespace pe;
+
+extern "C" int pe_embed_rows(int dtype, int64_t rows, int64_t H, const int64_t* ids,
+                             const void* embed, void* out, int64_t ldo, void* stream) {
+  PE_CHECK_ARG(rows >= 0 && H > 0 && ldo >= H, "embed_rows: bad shape");
+  if (rows == 0) return PE_OK;
+  PE_CHECK_ARG(rows <= 65535, "embed_rows: rows > 65535");
+  dim3 grid((unsigned)ceil_div(H, 256 * 4), (unsigned)rows);
+  return PE_DISPATCH(dtype, T, [&] {
+    embed_rows_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(rows, H, ids, (const T*)embed,
+                                                              (T*)out, ldo);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+extern "C" int pe_fill_rows(int dtype, int64_t rows, int64_t H, const void* vec, void* out,
+                            int64_t ldo, void* stream) {
+  PE_CHECK_ARG(rows >= 0 && H > 0 && ldo >= H, "fill_rows: bad shape");
+  if (rows == 0) return PE_OK;
+  return PE_DISPATCH(dtype, T, [&] {
+    fill_rows_kernel<T><<<grid_for(rows * H, 256), 256, 0, as_stream(stream)>>>(
+        rows, H, (const T*)vec, (T*)out, ldo);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+extern "C" int pe_swiglu_fwd(int dtype, int64_t rows, int64_t I, const void* gu, int64_t ldgu,
+                             void* a, int64_t lda, void* stream) {
+  PE_CHECK_ARG(rows >= 0 && I > 0 && ldgu >= 2 * I && lda >= I, "swiglu_fwd: bad shape");
+  if (rows == 0) return PE_OK;
+  return PE_DISPATCH(dtype, T, [&] {
+    swiglu_fwd_kernel<T><<<grid_for(rows * I, 256), 256, 0, as_stream(stream)>>>(
+        rows, I, (const T*)gu, ldgu, (T*)a, lda);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+extern "C" int pe_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* da, int64_t ldda,
+                             const void* gu, int64_t ldgu, void* dgu, int64_t lddgu,
+                             void* stream) {
+  PE_CHECK_ARG(rows >= 0 && I > 0 && ldgu >= 2 * I && lddgu >= 2 * I && ldda >= I,
+               "swiglu_bwd: bad shape");
+  if (rows == 0) return PE_OK;
+  return PE_DISPATCH(dtype, T, [&] {
+    swiglu_bwd_kernel<T><<<grid_for(rows * I, 256), 256, 0, as_stream(stream)>>>(
+        rows, I, (const T*)da, ldda, (const T*)gu, ldgu, (T*)dgu, lddgu);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+extern "C" int pe_rowsum_cols(int dtype, int64_t rows, int64_t H, const void* x, int64_t ldx,
+                              float* out, void* stream) {
+  PE_CHECK_ARG(rows >= 0 && H > 0 && ldx >= H, "rowsum_cols: bad shape");
+  return PE_DISPATCH(dtype, T, [&] {
+    rowsum_cols_kernel<T><<<(unsigned)ceil_div(H, 32), dim3(32, 8), 0, as_stream(stream)>>>(
+        rows, H, (const T*)x, ldx, out);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+static int move_rows(int dtype, int64_t rows, int64_t H, const int64_t* idx, const void* src,
+                     int64_t lds, void* dst, int64_t ldd, int scatter, void* stream) {
+  PE_CHECK_ARG(rows >= 0 && H > 0 && lds >= H && ldd >= H, "scatter/gather rows: bad shape");
+  if (rows == 0) return PE_OK;
+  PE_CHECK_ARG(rows <= 65535, "scatter/gather rows: rows > 65535");
+  dim3 grid((unsigned)ceil_div(H, 256 * 4), (unsigned)rows);
+  return PE_DISPATCH(dtype, T, [&] {
+    move_rows_kernel<T><<<grid, 256, 0, as_stream(stream)>>>(rows, H, idx, (const T*)src, lds,
+                                                             (T*)dst, ldd, scatter);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+extern "C" int pe_scatter_rows(int dtype, int64_t rows, int64_t H, const int64_t* idx,
+                               const void* src, int64_t lds, void* dst, int64_t ldd,
+                               void* stream) {
+  return move_rows(dtype, rows, H, idx, src, lds, dst, ldd, 1, stream);
+}
+
+extern "C" int pe_gather_rows(int dtype, int64_t rows, int64_t H, const int64_t* idx,
+                              const void* src, int64_t lds, void* dst, int64_t ldd,
+                              void* stream) {
+  return move_rows(dtype, rows, H, idx, src, lds, dst, ldd, 0, stream);
+}
+
+extern "C" int pe_cast_f32(int dtype, int64_t n, const float* x, void* y, void* stream) {
+  PE_CHECK_ARG(n >= 0, "cast: bad size");
+  if (n == 0) return PE_OK;
+  return PE_DISPATCH(dtype, T, [&] {
+    cast_kernel<T><<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(n, x, (T*)y);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}

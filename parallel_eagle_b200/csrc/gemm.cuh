@@ -1,0 +1,29 @@
+// Internal GEMM entry points shared by the dispatcher, the LM-head loss and
+// the attention code.
+#pragma once
+#include "common.cuh"
+
+namespace pe {
+
+int gemm_simt(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm,
+              int64_t a_sk, const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc,
+              int c_dtype, const void* Cin, int64_t ldcin, float alpha, float beta,
+              cudaStream_t stream);
+
+// True when the tcgen05/TMA kernel can take these operands (bf16, unit stride on
+// one side of each operand, 16-byte aligned strides and bases).
+bool gemm_tc_eligible(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm,
+                      int64_t a_sk, const void* B, int64_t b_sn, int64_t b_sk, int c_dtype);
+
+int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
+            const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
+            const void* Cin, int64_t ldcin, float alpha, float beta, int* status,
+            cudaStream_t stream);
+
+// pe_gemm without the C wrapper (used inside the library)
+int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
+         const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
+         const void* Cin, int64_t ldcin, float alpha, float beta, int algo, int* status,
+         cudaStream_t stream);
+
+}  // namespace pe

@@ -1,0 +1,385 @@
+// Persistent warp-specialised bf16 GEMM on the 5th-generation tensor cores.
+//
+//   C[m, n] = alpha * sum_k A(m, k) B(n, k) + beta * Cin[m, n]
+//
+// Each operand may be K-major (unit stride along k: activations and weights in
+// the forward pass) or MN-major (unit stride along m / n: the transposed operands
+// of the input- and weight-gradient GEMMs), so the three GEMMs of every
+// nn.Linear run without transposing anything in HBM.
+//
+// CTA tile 128 x BN (BN = 256 or 128), K slices of 64 (one 128-byte swizzle
+// row of bf16).  Warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
+// warp 1 issues tcgen05.mma (128 x BN x 16) into a double-buffered TMEM
+// accumulator, warps 2-5 drain the other accumulator (tcgen05.ld) and store to
+// HBM, so the epilogue of tile i overlaps the main loop of tile i+1.  The grid
+// is one CTA per SM; tiles are walked in groups of 8 M-tiles for L2 reuse of B.
+#include "gemm.cuh"
+#include "sm100.cuh"
+
+namespace pe {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct TcCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  constexpr int G = 8;
+  const int per_group = G * tiles_n;
+  const int g = tile / per_group;
+  const int first = g * G;
+  const int gsize = min(tiles_m - first, G);
+  const int r = tile - g * per_group;
+  tm = first + r % gsize;
+  tn = r / gsize;
+}
+
+template <typename OutT>
+__device__ __forceinline__ void store_row32(OutT* dst, const OutT* cin, const float* v, float alpha,
+                                            float beta, int valid, bool vec_ok) {
+  float o[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) o[i] = alpha * v[i];
+  if (vec_ok && valid == 32) {
+    if constexpr (sizeof(OutT) == 2) {
+      if (cin) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 u = reinterpret_cast<const uint4*>(cin)[q];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float2 f = __bfloat1622float2(h[j]);
+            o[q * 8 + 2 * j] += beta * f.x;
+            o[q * 8 + 2 * j + 1] += beta * f.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 u;
+        u.x = pack_bf16x2(o[q * 8 + 0], o[q * 8 + 1]);
+        u.y = pack_bf16x2(o[q * 8 + 2], o[q * 8 + 3]);
+        u.z = pack_bf16x2(o[q * 8 + 4], o[q * 8 + 5]);
+        u.w = pack_bf16x2(o[q * 8 + 6], o[q * 8 + 7]);
+        reinterpret_cast<uint4*>(dst)[q] = u;
+      }
+    } else {
+      if (cin) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 f = reinterpret_cast<const float4*>(cin)[q];
+          o[4 * q] += beta * f.x;
+          o[4 * q + 1] += beta * f.y;
+          o[4 * q + 2] += beta * f.z;
+          o[4 * q + 3] += beta * f.w;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(dst)[q] =
+            make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (i < valid) {
+        float t = o[i];
+        if (cin) t += beta * to_f(cin[i]);
+        dst[i] = from_f<OutT>(t);
+      }
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               int M, int N, int K, OutT* C, int64_t ldc, const OutT* Cin, int64_t ldcin,
+               float alpha, float beta, int vec_ok, int* status) {
+  using Cfg = TcCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m = (M + BM - 1) / BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int last_stage = -1;
+      uint32_t last_phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(tile, tiles_m, tiles_n, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, status, 101)) { ok = false; break; }
+          uint8_t* a_dst = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* b_dst = a_dst + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, tm * BM);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], tm * BM, kb * BK);
+            tma_load_2d(a_dst + 8192, &tmA, &full[stage], tm * BM + 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, tn * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], tn * BN + 64 * j, kb * BK);
+          }
+          last_stage = stage;
+          last_phase = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok && last_stage >= 0) {
+        // loads complete in issue order: once the newest one has landed, none of
+        // this CTA's copies is still writing shared memory
+        mbar_wait(&full[last_stage], last_phase, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, status, 102)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, 103)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sw128_desc(a_base + k * 2048, 8192, 1024)
+                                     : sw128_desc(a_base + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sw128_desc(b_base + k * 2048, 8192, 1024)
+                                     : sw128_desc(b_base + k * 32, 16, 1024);
+            mma_bf16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) mma_commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      int tm, tn;
+      tile_coords(tile, tiles_m, tiles_n, tm, tn);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase, status, 104)) break;
+      tc_fence_after();
+      const int64_t gm = (int64_t)tm * BM + row_in_tile;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c0, v);
+        tmem_wait_ld();
+        const int64_t gn0 = (int64_t)tn * BN + c0;
+        if (gm < M && gn0 < N) {
+          const int valid = (N - gn0) < 32 ? (int)(N - gn0) : 32;
+          store_row32<OutT>(C + gm * ldc + gn0, Cin ? Cin + gm * ldcin + gn0 : nullptr, v, alpha,
+                            beta, valid, vec_ok != 0);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int BN, bool A_MN, bool B_MN, typename OutT>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, void* C, int64_t ldc,
+           const void* Cin, int64_t ldcin, float alpha, float beta, int vec_ok, int* status,
+           cudaStream_t stream) {
+  using Cfg = TcCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, OutT>;
+  PE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ta, tb, M, N, K, (OutT*)C, ldc, (const OutT*)Cin,
+                                              ldcin, alpha, beta, vec_ok, status);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
+template <int BN, typename OutT>
+int launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
+                  int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin, float alpha,
+                  float beta, int vec_ok, int* status, cudaStream_t s) {
+  if (!a_mn && !b_mn)
+    return launch<BN, false, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+  if (!a_mn && b_mn)
+    return launch<BN, false, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+  if (a_mn && !b_mn)
+    return launch<BN, true, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+  return launch<BN, true, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+}
+
+}  // namespace
+
+bool gemm_tc_eligible(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm,
+                      int64_t a_sk, const void* B, int64_t b_sn, int64_t b_sk, int c_dtype) {
+  if (dtype != PE_BF16) return false;
+  if (c_dtype != PE_BF16 && c_dtype != PE_F32) return false;
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return false;
+  if (!al16(A) || !al16(B)) return false;
+  // each operand: one unit stride, the other a positive multiple of 8 elements (16 bytes)
+  if (a_sk == 1) {
+    if (a_sm <= 0 || a_sm % 8 != 0) return false;
+  } else if (a_sm == 1) {
+    if (a_sk <= 0 || a_sk % 8 != 0) return false;
+  } else {
+    return false;
+  }
+  if (b_sk == 1) {
+    if (b_sn <= 0 || b_sn % 8 != 0) return false;
+  } else if (b_sn == 1) {
+    if (b_sk <= 0 || b_sk % 8 != 0) return false;
+  } else {
+    return false;
+  }
+  return true;
+}
+
+int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
+            const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
+            const void* Cin, int64_t ldcin, float alpha, float beta, int* status,
+            cudaStream_t stream) {
+  const bool a_mn = a_sk != 1;
+  const bool b_mn = b_sk != 1;
+  const int BN = N > 128 ? 256 : 128;
+  CUtensorMap ta, tb;
+  int rc;
+  if (!a_mn)
+    rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)a_sm * 2, 64, 128);
+  else
+    rc = make_tmap_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)a_sk * 2, 64, 64);
+  if (rc) return rc;
+  if (!b_mn)
+    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)b_sn * 2, 64, (uint32_t)BN);
+  else
+    rc = make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)b_sk * 2, 64, 64);
+  if (rc) return rc;
+  const size_t esz = c_dtype == PE_F32 ? 4 : 2;
+  const int vec_ok = (ldc * esz) % 16 == 0 && al16(C) &&
+                     (!Cin || ((ldcin * esz) % 16 == 0 && al16(Cin)));
+  const int m = (int)M, n = (int)N, k = (int)K;
+  if (c_dtype == PE_F32) {
+    if (BN == 256)
+      return launch_majors<256, float>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
+    return launch_majors<128, float>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
+  }
+  if (BN == 256)
+    return launch_majors<256, __nv_bfloat16>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
+  return launch_majors<128, __nv_bfloat16>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
+}
+
+int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
+         const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
+         const void* Cin, int64_t ldcin, float alpha, float beta, int algo, int* status,
+         cudaStream_t stream) {
+  PE_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "gemm: negative size");
+  PE_CHECK_ARG(ldc >= N, "gemm: ldc < N");
+  if (M == 0 || N == 0) return PE_OK;
+  PE_CHECK_ARG(K > 0, "gemm: K == 0 is not supported");
+  const bool tc_ok = gemm_tc_eligible(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, c_dtype);
+  if (algo == PE_ALGO_TCGEN05) {
+    PE_CHECK_ARG(tc_ok, "gemm: operands not eligible for the tcgen05 path");
+    return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
+                   beta, status, stream);
+  }
+  if (algo == PE_ALGO_AUTO && tc_ok)
+    return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
+                   beta, status, stream);
+  return gemm_simt(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin,
+                   alpha, beta, stream);
+}
+
+}  // namespace pe
+
+extern "C" int pe_gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm,
+                       int64_t a_sk, const void* B, int64_t b_sn, int64_t b_sk, void* C,
+                       int64_t ldc, int c_dtype, const void* Cin, int64_t ldcin, float alpha,
+                       float beta, int algo, int32_t* status, void* stream) {
+  return pe::gemm(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin,
+                  alpha, beta, algo, status, pe::as_stream(stream));
+}

@@ -1,0 +1,297 @@
+// Frozen shared LM head fused with cross-entropy (or soft-target distillation)
+// and its input gradient, chunked over the vocabulary (reference
+// src/pe/partition.py:113-115, src/pe/drafter.py:123-124).
+//
+// Pass 1, per vocabulary chunk: Z = h W_c^T on the tensor cores, then an online
+// (max, sum-exp) update per row and the label logit.  After the last chunk:
+// lse, the loss rows and their sum.  Pass 2, per chunk: recompute Z, form
+// G = scale * (softmax - target) rounded to the storage dtype, and accumulate
+// dH += G W_c in fp32.  Only one chunk of logits exists at a time, so the
+// [rows, vocab] matrix is never stored; the frozen W receives no gradient.
+#include "gemm.cuh"
+
+namespace pe {
+namespace {
+
+constexpr int64_t kChunk = 8192;
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = is_max ? warp_max(v) : warp_sum(v);
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float t = lane < (kThreads / 32) ? sh[lane] : (is_max ? -INFINITY : 0.f);
+    t = is_max ? warp_max(t) : warp_sum(t);
+    if (lane == 0) sh[32] = t;
+  }
+  __syncthreads();
+  const float r = sh[32];
+  __syncthreads();
+  return r;
+}
+
+// online (max, sumexp) update of each row with this chunk; label logit pick;
+// soft targets also carry the teacher's (max, sumexp) and sum_v e^{t-m_t} z_v
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+stats_kernel(int64_t vc, int64_t v0, const float* __restrict__ Z, const float* __restrict__ Zt,
+             int64_t ldz, const int64_t* __restrict__ labels, float* m, float* l, float* zlab,
+             float* mt, float* lt, float* szt) {
+  __shared__ float sh[33];
+  const int64_t r = blockIdx.x;
+  const int64_t lab = labels ? labels[r] : 0;
+  if (labels && lab < 0) return;  // ignored row (uniform per block)
+  const float* z = Z + r * ldz;
+  float cmax = -INFINITY;
+  for (int64_t c = threadIdx.x; c < vc; c += kThreads) cmax = fmaxf(cmax, round_to<T>(z[c]));
+  cmax = block_reduce(cmax, true, sh);
+  const float m_old = m[r];
+  const float m_new = fmaxf(m_old, cmax);
+  float s = 0.f;
+  for (int64_t c = threadIdx.x; c < vc; c += kThreads) s += expf(round_to<T>(z[c]) - m_new);
+  s = block_reduce(s, false, sh);
+  if (Zt) {
+    const float* zt = Zt + r * ldz;
+    float tmax = -INFINITY;
+    for (int64_t c = threadIdx.x; c < vc; c += kThreads) tmax = fmaxf(tmax, round_to<T>(zt[c]));
+    tmax = block_reduce(tmax, true, sh);
+    const float mt_old = mt[r];
+    const float mt_new = fmaxf(mt_old, tmax);
+    float st = 0.f, sz = 0.f;
+    for (int64_t c = threadIdx.x; c < vc; c += kThreads) {
+      const float e = expf(round_to<T>(zt[c]) - mt_new);
+      st += e;
+      sz += e * round_to<T>(z[c]);
+    }
+    st = block_reduce(st, false, sh);
+    sz = block_reduce(sz, false, sh);
+    if (threadIdx.x == 0) {
+      const float f = expf(mt_old - mt_new);
+      lt[r] = lt[r] * f + st;
+      szt[r] = szt[r] * f + sz;
+      mt[r] = mt_new;
+    }
+  }
+  if (threadIdx.x == 0) {
+    l[r] = l[r] * expf(m_old - m_new) + s;
+    m[r] = m_new;
+    if (labels && lab >= v0 && lab < v0 + vc) zlab[r] = round_to<T>(z[lab - v0]);
+  }
+}
+
+__global__ void init_stats_kernel(int64_t R, float* m, float* l, float* zlab, float* mt, float* lt,
+                                  float* szt) {
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < R;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+    zlab[r] = 0.f;
+    if (mt) {
+      mt[r] = -INFINITY;
+      lt[r] = 0.f;
+      szt[r] = 0.f;
+    }
+  }
+}
+
+// lse per row, loss rows summed in a fixed order by one block
+__global__ void __launch_bounds__(kThreads)
+finalize_kernel(int64_t R, const int64_t* labels, const float* m, const float* l, const float* zlab,
+                const float* mt, const float* lt, const float* szt, float* lse, float* lse_t,
+                float* loss_sum) {
+  __shared__ float sh[33];
+  float acc = 0.f;
+  for (int64_t r = threadIdx.x; r < R; r += kThreads) {
+    if (labels && labels[r] < 0) {
+      lse[r] = 0.f;
+      continue;
+    }
+    const float L = m[r] + logf(l[r]);
+    lse[r] = L;
+    if (mt) {
+      lse_t[r] = mt[r] + logf(lt[r]);
+      acc += L - szt[r] / lt[r];
+    } else {
+      acc += L - zlab[r];
+    }
+  }
+  acc = block_reduce(acc, false, sh);
+  if (threadIdx.x == 0) loss_sum[0] += acc;
+}
+
+template <typename T>
+__global__ void grad_kernel(int64_t R, int64_t vc, int64_t v0, const float* __restrict__ Z,
+                            const float* __restrict__ Zt, int64_t ldz,
+                            const int64_t* __restrict__ labels, const float* __restrict__ lse,
+                            const float* __restrict__ lse_t, float scale, T* __restrict__ G,
+                            int64_t ldg) {
+  const int64_t total = R * vc;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / vc, c = i - r * vc;
+    float g = 0.f;
+    const int64_t lab = labels ? labels[r] : 0;
+    if (!(labels && lab < 0)) {
+      const float p = expf(round_to<T>(Z[r * ldz + c]) - lse[r]);
+      float tgt;
+      if (Zt)
+        tgt = expf(round_to<T>(Zt[r * ldz + c]) - lse_t[r]);
+      else
+        tgt = (lab == v0 + c) ? 1.f : 0.f;
+      g = scale * (p - tgt);
+    }
+    G[r * ldg + c] = from_f<T>(g);
+  }
+}
+
+template <typename T>
+__global__ void cast2d_kernel(int64_t R, int64_t H, const float* __restrict__ x, T* y, int64_t ldy) {
+  const int64_t total = R * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / H, c = i - r * H;
+    y[r * ldy + c] = from_f<T>(x[i]);
+  }
+}
+
+int64_t chunk_of(int64_t V) {
+  int64_t c = V < kChunk ? V : kChunk;
+  return (c + 7) / 8 * 8;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {
+  size_t m, l, zlab, lse, mt, lt, szt, lse_t, Z, Zt, G, dH, total;
+};
+
+Layout layout_of(int dtype, int64_t R, int64_t H, int64_t V, int soft) {
+  const int64_t vc = chunk_of(V);
+  const size_t esz = dtype == PE_F32 ? 4 : 2;
+  Layout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += align256(bytes);
+    return o;
+  };
+  L.m = take(4 * R);
+  L.l = take(4 * R);
+  L.zlab = take(4 * R);
+  L.lse = take(4 * R);
+  if (soft) {
+    L.mt = take(4 * R);
+    L.lt = take(4 * R);
+    L.szt = take(4 * R);
+    L.lse_t = take(4 * R);
+  }
+  L.Z = take(4 * (size_t)R * vc);
+  if (soft) L.Zt = take(4 * (size_t)R * vc);
+  L.G = take(esz * (size_t)R * vc);
+  L.dH = take(4 * (size_t)R * H);
+  L.total = off;
+  return L;
+}
+
+unsigned grid_for(int64_t n) {
+  int64_t g = ceil_div(n, 256);
+  const int64_t cap = (int64_t)sm_count() * 16;
+  return (unsigned)(g < 1 ? 1 : (g > cap ? cap : g));
+}
+
+}  // namespace
+}  // namespace pe
+
+using namespace pe;
+
+extern "C" size_t pe_lmhead_ce_workspace(int dtype, int64_t R, int64_t H, int64_t V, int soft) {
+  if (R <= 0 || H <= 0 || V <= 0) return 0;
+  return layout_of(dtype, R, H, V, soft).total;
+}
+
+extern "C" int pe_lmhead_ce(int dtype, int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh,
+                            const void* W, const int64_t* labels, const void* teacher,
+                            int64_t ldt, float grad_scale, void* dh, int64_t lddh,
+                            float* loss_sum, void* workspace, size_t workspace_bytes, int algo,
+                            int32_t* status, void* stream) {
+  PE_CHECK_ARG(R >= 0 && H > 0 && V > 0 && ldh >= H && lddh >= H, "lmhead_ce: bad shape");
+  PE_CHECK_ARG(labels || teacher, "lmhead_ce: needs labels or teacher rows");
+  PE_CHECK_ARG(R <= (1ll << 31) - 1, "lmhead_ce: too many rows");
+  if (R == 0) return PE_OK;
+  const int soft = teacher != nullptr;
+  const Layout L = layout_of(dtype, R, H, V, soft);
+  PE_CHECK_ARG(workspace && workspace_bytes >= L.total,
+               "lmhead_ce: workspace of %zu bytes needed", L.total);
+  cudaStream_t st = as_stream(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* m = (float*)(ws + L.m);
+  float* l = (float*)(ws + L.l);
+  float* zlab = (float*)(ws + L.zlab);
+  float* lse = (float*)(ws + L.lse);
+  float* mt = soft ? (float*)(ws + L.mt) : nullptr;
+  float* lt = soft ? (float*)(ws + L.lt) : nullptr;
+  float* szt = soft ? (float*)(ws + L.szt) : nullptr;
+  float* lse_t = soft ? (float*)(ws + L.lse_t) : nullptr;
+  float* Z = (float*)(ws + L.Z);
+  float* Zt = soft ? (float*)(ws + L.Zt) : nullptr;
+  void* G = ws + L.G;
+  float* dH = (float*)(ws + L.dH);
+  const int64_t VC = chunk_of(V);
+  const size_t esz = dtype == PE_F32 ? 4 : 2;
+  const int64_t* lab = soft ? nullptr : labels;
+
+  init_stats_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, zlab, mt, lt, szt);
+  PE_LAUNCHED();
+  int rc;
+  for (int64_t v0 = 0; v0 < V; v0 += VC) {
+    const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
+    const void* Wc = (const uint8_t*)W + (size_t)v0 * H * esz;
+    rc = gemm(dtype, R, vc, H, h, ldh, 1, Wc, H, 1, Z, VC, PE_F32, nullptr, 0, 1.f, 0.f, algo,
+              status, st);
+    if (rc) return rc;
+    if (soft) {
+      rc = gemm(dtype, R, vc, H, teacher, ldt, 1, Wc, H, 1, Zt, VC, PE_F32, nullptr, 0, 1.f, 0.f,
+                algo, status, st);
+      if (rc) return rc;
+    }
+    rc = PE_DISPATCH(dtype, T, [&] {
+      stats_kernel<T><<<(unsigned)R, kThreads, 0, st>>>(vc, v0, Z, Zt, VC, lab, m, l, zlab, mt,
+                                                        lt, szt);
+      PE_LAUNCHED();
+      return PE_OK;
+    });
+    if (rc) return rc;
+  }
+  finalize_kernel<<<1, kThreads, 0, st>>>(R, lab, m, l, zlab, mt, lt, szt, lse, lse_t, loss_sum);
+  PE_LAUNCHED();
+  for (int64_t v0 = 0; v0 < V; v0 += VC) {
+    const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
+    const void* Wc = (const uint8_t*)W + (size_t)v0 * H * esz;
+    rc = gemm(dtype, R, vc, H, h, ldh, 1, Wc, H, 1, Z, VC, PE_F32, nullptr, 0, 1.f, 0.f, algo,
+              status, st);
+    if (rc) return rc;
+    if (soft) {
+      rc = gemm(dtype, R, vc, H, teacher, ldt, 1, Wc, H, 1, Zt, VC, PE_F32, nullptr, 0, 1.f, 0.f,
+                algo, status, st);
+      if (rc) return rc;
+    }
+    rc = PE_DISPATCH(dtype, T, [&] {
+      grad_kernel<T><<<grid_for(R * vc), 256, 0, st>>>(R, vc, v0, Z, Zt, VC, lab, lse, lse_t,
+                                                       grad_scale, (T*)G, VC);
+      PE_LAUNCHED();
+      return PE_OK;
+    });
+    if (rc) return rc;
+    // dH (+)= G[R, vc] * W_c[vc, H]   (W_c is the MN-major B operand)
+    rc = gemm(dtype, R, H, vc, G, VC, 1, Wc, 1, H, dH, H, PE_F32, v0 > 0 ? dH : nullptr, H, 1.f,
+              v0 > 0 ? 1.f : 0.f, algo, status, st);
+    if (rc) return rc;
+  }
+  return PE_DISPATCH(dtype, T, [&] {
+    cast2d_kernel<T><<<grid_for(R * H), 256, 0, st>>>(R, H, dH, (T*)dh, lddh);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}

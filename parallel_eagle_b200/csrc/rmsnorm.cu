@@ -1,0 +1,233 @@
+// RMSNorm forward/backward (reference src/pe/nn.py:16-26) and the column
+// reduction that turns per-block weight-gradient partials into dw.
+//
+// One warp per row.  The vector path moves 8 elements (16 B of bf16) per lane
+// per access, so a warp touches 512 contiguous bytes per instruction; rows of a
+// few KB stay in L1 between the two passes.  HBM traffic per row: forward reads
+// x once and writes y (+4 B rstd); backward reads dy, x (+residual) once and
+// writes dx.
+#include "common.cuh"
+
+namespace pe {
+namespace {
+
+constexpr int kWarps = 8;
+
+template <typename T, int VEC>
+struct Vec;
+template <typename T>
+struct Vec<T, 1> {
+  __device__ __forceinline__ static void load(const T* p, float* f) { f[0] = to_f(p[0]); }
+  __device__ __forceinline__ static void store(T* p, const float* f) { p[0] = from_f<T>(f[0]); }
+};
+template <>
+struct Vec<__nv_bfloat16, 8> {
+  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float* f) {
+    uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 t = __bfloat1622float2(h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  __device__ __forceinline__ static void store(__nv_bfloat16* p, const float* f) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+};
+template <>
+struct Vec<float, 8> {
+  __device__ __forceinline__ static void load(const float* p, float* f) {
+    float4 a = reinterpret_cast<const float4*>(p)[0];
+    float4 b = reinterpret_cast<const float4*>(p)[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+  __device__ __forceinline__ static void store(float* p, const float* f) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+};
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_fwd_kernel(int64_t rows, int64_t H, const T* __restrict__ x, int64_t ldx,
+                   const T* __restrict__ w, T* __restrict__ y, int64_t ldy,
+                   float* __restrict__ rstd, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * ldx;
+  T* yr = y + row * ldy;
+  float ss = 0.f;
+  for (int64_t c = (int64_t)lane * VEC; c < H; c += 32 * VEC) {
+    float f[VEC];
+    Vec<T, VEC>::load(xr + c, f);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) ss += f[i] * f[i];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)H + eps);
+  if (lane == 0 && rstd) rstd[row] = r;
+  for (int64_t c = (int64_t)lane * VEC; c < H; c += 32 * VEC) {
+    float f[VEC], g[VEC];
+    Vec<T, VEC>::load(xr + c, f);
+    Vec<T, VEC>::load(w + c, g);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) f[i] = (f[i] * r) * g[i];
+    Vec<T, VEC>::store(yr + c, f);
+  }
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_bwd_kernel(int64_t rows, int64_t H, const T* __restrict__ dy, int64_t lddy,
+                   const T* __restrict__ x, int64_t ldx, const T* __restrict__ w,
+                   const float* __restrict__ rstd, T* dx, int64_t lddx, const T* res,
+                   int64_t ldres, float* __restrict__ dw_partial) {
+  extern __shared__ float sdw[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  if (dw_partial) {
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) sdw[c] = 0.f;
+    __syncthreads();
+  }
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
+       row += (int64_t)gridDim.x * kWarps) {
+    const T* dyr = dy + row * lddy;
+    const T* xr = x + row * ldx;
+    const float r = rstd[row];
+    float s = 0.f;
+    for (int64_t c = (int64_t)lane * VEC; c < H; c += 32 * VEC) {
+      float a[VEC], b[VEC], g[VEC];
+      Vec<T, VEC>::load(dyr + c, a);
+      Vec<T, VEC>::load(xr + c, b);
+      Vec<T, VEC>::load(w + c, g);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) s += (a[i] * g[i]) * b[i];
+    }
+    s = warp_sum(s);
+    const float coef = s * r * r * r / (float)H;
+    T* dxr = dx + row * lddx;
+    const T* rr = res ? res + row * ldres : nullptr;
+    for (int64_t c = (int64_t)lane * VEC; c < H; c += 32 * VEC) {
+      float a[VEC], b[VEC], g[VEC], o[VEC];
+      Vec<T, VEC>::load(dyr + c, a);
+      Vec<T, VEC>::load(xr + c, b);
+      Vec<T, VEC>::load(w + c, g);
+      if (rr) {
+        Vec<T, VEC>::load(rr + c, o);
+      } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) o[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) o[i] += r * (a[i] * g[i]) - b[i] * coef;
+      Vec<T, VEC>::store(dxr + c, o);
+      if (dw_partial) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) atomicAdd(&sdw[c + i], a[i] * (b[i] * r));
+      }
+    }
+  }
+  if (dw_partial) {
+    __syncthreads();
+    float* out = dw_partial + (int64_t)blockIdx.x * H;
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) out[c] = sdw[c];
+  }
+}
+
+// out[c] = (acc ? out[c] : 0) + sum_b partial[b, c]; fixed summation order.
+template <typename T>
+__global__ void colsum_kernel(int64_t nblk, int64_t H, const float* __restrict__ partial,
+                              T* out, int accumulate) {
+  __shared__ float red[8][33];
+  const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
+  if (c < H)
+    for (int64_t b = threadIdx.y; b < nblk; b += 8) s += partial[b * H + c];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i][threadIdx.x];
+    if (accumulate) t += to_f(out[c]);
+    out[c] = from_f<T>(t);
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace pe
+
+using namespace pe;
+
+extern "C" int pe_rmsnorm_fwd(int dtype, int64_t rows, int64_t H, const void* x, int64_t ldx,
+                              const void* w, void* y, int64_t ldy, float* rstd, float eps,
+                              void* stream) {
+  PE_CHECK_ARG(rows >= 0 && H > 0 && ldx >= H && ldy >= H, "rmsnorm_fwd: bad shape");
+  if (rows == 0) return PE_OK;
+  const bool vec = H % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(y) &&
+                   aligned16(w);
+  dim3 grid((unsigned)ceil_div(rows, kWarps));
+  return PE_DISPATCH(dtype, T, [&] {
+    if (vec)
+      rmsnorm_fwd_kernel<T, 8><<<grid, kWarps * 32, 0, as_stream(stream)>>>(
+          rows, H, (const T*)x, ldx, (const T*)w, (T*)y, ldy, rstd, eps);
+    else
+      rmsnorm_fwd_kernel<T, 1><<<grid, kWarps * 32, 0, as_stream(stream)>>>(
+          rows, H, (const T*)x, ldx, (const T*)w, (T*)y, ldy, rstd, eps);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+extern "C" int64_t pe_rmsnorm_bwd_blocks(int64_t rows) {
+  int64_t b = ceil_div(rows, 4 * kWarps);
+  return b < 1 ? 1 : (b > 256 ? 256 : b);
+}
+
+extern "C" int pe_rmsnorm_bwd(int dtype, int64_t rows, int64_t H, const void* dy, int64_t lddy,
+                              const void* x, int64_t ldx, const void* w, const float* rstd,
+                              void* dx, int64_t lddx, const void* residual, int64_t ldres,
+                              float* dw_partial, void* stream) {
+  PE_CHECK_ARG(rows >= 0 && H > 0, "rmsnorm_bwd: bad shape");
+  PE_CHECK_ARG(!dw_partial || H * 4 <= 200 * 1024, "rmsnorm_bwd: H too large for dw staging");
+  const int64_t nblk = pe_rmsnorm_bwd_blocks(rows);
+  if (rows == 0) {
+    if (dw_partial) PE_CUDA_TRY(cudaMemsetAsync(dw_partial, 0, nblk * H * 4, as_stream(stream)));
+    return PE_OK;
+  }
+  const bool vec = H % 8 == 0 && lddy % 8 == 0 && ldx % 8 == 0 && lddx % 8 == 0 &&
+                   (!residual || ldres % 8 == 0) && aligned16(dy) && aligned16(x) &&
+                   aligned16(w) && aligned16(dx) && (!residual || aligned16(residual));
+  const size_t smem = dw_partial ? (size_t)H * 4 : 0;
+  return PE_DISPATCH(dtype, T, [&] {
+    auto kern = vec ? rmsnorm_bwd_kernel<T, 8> : rmsnorm_bwd_kernel<T, 1>;
+    if (smem > 48 * 1024)
+      PE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<(unsigned)nblk, kWarps * 32, smem, as_stream(stream)>>>(
+        rows, H, (const T*)dy, lddy, (const T*)x, ldx, (const T*)w, rstd, (T*)dx, lddx,
+        (const T*)residual, ldres, dw_partial);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+extern "C" int pe_colsum_f32(int dtype, int64_t nblk, int64_t H, const float* partial, void* dw,
+                             int accumulate, void* stream) {
+  PE_CHECK_ARG(nblk > 0 && H > 0, "colsum: bad shape");
+  return PE_DISPATCH(dtype, T, [&] {
+    colsum_kernel<T><<<(unsigned)ceil_div(H, 32), dim3(32, 8), 0, as_stream(stream)>>>(
+        nblk, H, partial, (T*)dw, accumulate);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}

@@ -1,0 +1,67 @@
+// Half-split rotary embedding applied in place (reference src/pe/nn.py:29-49).
+//
+// Each thread rotates one (d, d + hd/2) pair of one head of one row.  The
+// angle is pos * inv_freq with inv_freq = 1 / theta^(2p/hd), both in fp32 like
+// the reference's cache; cos/sin are rounded to the storage type before use,
+// and each product/sum is rounded like the reference's element-wise ops.
+// Memory bound: one read and one write of the rotated columns.
+#include "common.cuh"
+
+namespace pe {
+namespace {
+
+template <typename T>
+__global__ void rope_kernel(int64_t rows, int heads, int hd, T* x, int64_t ldx,
+                            const int64_t* __restrict__ pos, float theta, int inverse) {
+  const int half = hd >> 1;
+  const int64_t pairs_per_row = (int64_t)heads * half;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * pairs_per_row) return;
+  const int64_t row = idx / pairs_per_row;
+  const int64_t rem = idx - row * pairs_per_row;
+  const int h = (int)(rem / half);
+  const int p = (int)(rem - (int64_t)h * half);
+  const float expo = (float)(2 * p) / (float)hd;
+  const float inv_freq = 1.0f / powf(theta, expo);
+  const float ang = (float)pos[row] * inv_freq;
+  float s, c;
+  sincosf(ang, &s, &c);
+  c = round_to<T>(c);
+  s = round_to<T>(s);
+  T* base = x + row * ldx + (int64_t)h * hd;
+  const float a = to_f(base[p]);
+  const float b = to_f(base[p + half]);
+  float ya, yb;
+  if (!inverse) {
+    // y1 = x1*c + (-x2)*s ; y2 = x2*c + x1*s
+    ya = round_to<T>(round_to<T>(a * c) + round_to<T>(-b * s));
+    yb = round_to<T>(round_to<T>(b * c) + round_to<T>(a * s));
+  } else {
+    // transpose of the rotation: dx1 = dy1*c + dy2*s ; dx2 = dy2*c - dy1*s
+    ya = round_to<T>(round_to<T>(a * c) + round_to<T>(b * s));
+    yb = round_to<T>(round_to<T>(b * c) - round_to<T>(a * s));
+  }
+  base[p] = from_f<T>(ya);
+  base[p + half] = from_f<T>(yb);
+}
+
+}  // namespace
+}  // namespace pe
+
+using namespace pe;
+
+extern "C" int pe_rope(int dtype, int64_t rows, int heads, int head_dim, void* x, int64_t ldx,
+                       const int64_t* pos, float theta, int inverse, void* stream) {
+  PE_CHECK_ARG(rows >= 0 && heads > 0 && head_dim > 0 && head_dim % 2 == 0,
+               "rope: bad shape");
+  PE_CHECK_ARG(ldx >= (int64_t)heads * head_dim, "rope: ldx too small");
+  if (rows == 0) return PE_OK;
+  const int64_t total = rows * heads * (head_dim / 2);
+  const int threads = 256;
+  return PE_DISPATCH(dtype, T, [&] {
+    rope_kernel<T><<<(unsigned)ceil_div(total, threads), threads, 0, as_stream(stream)>>>(
+        rows, heads, head_dim, (T*)x, ldx, pos, theta, inverse);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
