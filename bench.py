@@ -1,0 +1,435 @@
+"""Drafter training-step throughput on B200 (slot-tokens/s), one process per GPU.
+
+    python bench.py [--gpus N --steps K --warmup W]            # this framework
+    python bench.py --impl reference [...]                      # CPU reference arm
+    torchrun --nproc-per-node N bench.py --gpus N ...           # data parallel
+
+A step is one optimizer update over the global batch: for every local sequence
+``mtp_backward`` (forward + backward of the partitioned MTP loss, BASELINE
+config 2: hidden 3584, 28/4 heads, I 18944, vocab 152064, n 2048, K 5, S 4,
+bf16, batch 8 per GPU), then the gradient all-reduce (N > 1), global-norm clip
+and AdamW.  Inputs are synthetic (seeded) with the BASELINE shapes.
+
+``value`` is device-timed with inputs resident in HBM; ``e2e`` is the same step
+through the public API with ids/features copied from pinned host memory each
+step and the loss read back.  The reference arm times the CPU oracle port of
+the reference step on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIG2 = dict(hidden=3584, n_heads=28, n_kv_heads=4, intermediate=18944, vocab=152064,
+               num_layers=1, max_depth=5, n=2048, segments=4, batch=8)
+METRIC = "drafter train slot-tokens/sec at 1/2/4/8 B200; masked-attn fwd+bwd TFLOP/s vs peak"
+UNIT = "slot-tokens/s"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def attention_pairs(n, k, segments):
+    from parallel_eagle_b200.engine import segment_bounds
+
+    pairs = 0
+    for a0, a1 in segment_bounds(n, segments):
+        pairs += a1 * (a1 + 1) // 2
+        pairs += sum((k - 1) * (i + 1) for i in range(a0, a1)) + (a1 - a0) * k * (k - 1) // 2
+    return pairs
+
+
+def step_flops_per_sequence(c):
+    """Algorithmic FLOPs of one sequence (2 per MAC, counted at S=1, no recompute)."""
+    H, I, V = c["hidden"], c["intermediate"], c["vocab"]
+    hd = H // c["n_heads"]
+    n, k = c["n"], c["max_depth"]
+    r_all = n * k
+    r_valid = n * k - k * (k + 1) // 2
+    layer = 3 * r_all * (2 * H * (2 * c["n_heads"] * hd + 2 * c["n_kv_heads"] * hd) + 6 * H * I)
+    head = 2 * r_valid * 2 * H * V
+    inp = n * (2 * 2 * 3 * H * H + 2 * 2 * 2 * H * H + 2 * H * H)
+    attn = 12 * hd * c["n_heads"] * attention_pairs(n, k, 1)
+    return c["num_layers"] * layer + head + inp + c["num_layers"] * attn
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                     "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                if out.returncode == 0 and out.stdout.strip():
+                    self.rows.append([x.strip() for x in out.stdout.strip().split(",")])
+            except Exception:  # noqa: BLE001 - sampling is best effort
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit())
+        mx = max((float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# --------------------------------------------------------------------------- #
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def make_heads_gpu(c, dev, seed=0):
+    g = torch.Generator(device=dev).manual_seed(10_000 + seed)
+    V, H = c["vocab"], c["hidden"]
+    embed = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    head = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    norm = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    return embed, head, norm
+
+
+def build_drafter(c, dev, seed=0):
+    import types
+
+    from parallel_eagle_b200.config import DrafterConfig
+    from parallel_eagle_b200.drafter import ParallelDrafter
+    from parallel_eagle_b200.nn import RMSNorm
+
+    E, Wh, wn = make_heads_gpu(c, dev, seed)
+    V, H = E.shape
+    embed = torch.nn.Embedding(V, H, _weight=E)
+    head = torch.nn.Linear(H, V, bias=False, device="meta")
+    head.weight = torch.nn.Parameter(Wh, requires_grad=False)
+    norm = RMSNorm(H, 1e-5)
+    norm.weight = torch.nn.Parameter(wn, requires_grad=False)
+    embed.weight.requires_grad_(False)
+    cfg = types.SimpleNamespace(num_attention_heads=c["n_heads"], num_key_value_heads=c["n_kv_heads"],
+                                intermediate_size=c["intermediate"], rope_theta=10000.0,
+                                rms_norm_eps=1e-5)
+    target = types.SimpleNamespace(config=cfg, hidden_size=H, vocab_size=V, feature_dim=3 * H,
+                                   get_input_embeddings=lambda: embed, get_lm_head=lambda: head,
+                                   get_final_norm=lambda: norm)
+    torch.manual_seed(seed)
+    with torch.device(dev):
+        d = ParallelDrafter.from_target(target, DrafterConfig(num_layers=c["num_layers"],
+                                                              max_depth=c["max_depth"]))
+    return d.to(dtype=torch.bfloat16)
+
+
+class Trainer:
+    """One optimizer update over the local sequences (+ all-reduce when N > 1)."""
+
+    def __init__(self, drafter, c, world, lr=1e-4):
+        from parallel_eagle_b200.engine import engine_for
+
+        self.d = drafter
+        self.c = c
+        self.world = world
+        self.eng = engine_for(drafter)
+        fp = self.eng.flat
+        self.m = torch.zeros(fp.numel, dtype=torch.float32, device=fp.device)
+        self.v = torch.zeros_like(self.m)
+        self.sumsq = torch.zeros(1, dtype=torch.float32, device=fp.device)
+        self.loss = torch.zeros(1, dtype=torch.float32, device=fp.device)
+        self.lr = lr
+        self.t = 0
+
+    def step(self, seqs, global_batch):
+        from parallel_eagle_b200 import ops
+
+        fp = self.eng.flat
+        fp.grad.zero_()
+        self.loss.zero_()
+        for ids, feats in seqs:
+            self.eng.run(ids, feats, self.c["segments"], loss_scale=1.0 / global_batch, sync=False)
+            self.loss += self.eng.loss_sum
+        if self.world > 1:
+            torch.distributed.all_reduce(fp.grad)
+        self.sumsq.zero_()
+        ops.sumsq_into(fp.grad, self.sumsq)
+        self.t += 1
+        ops.adamw_step(fp.flat, fp.grad, self.m, self.v, self.sumsq, 1.0, self.lr, 0.9, 0.999,
+                       1e-8, 0.0, self.t)
+        return self.loss
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    from parallel_eagle_b200 import _lib, ops
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=600))
+    c = dict(CONFIG2)
+    if args.n:
+        c["n"] = args.n
+    if args.batch:
+        c["batch"] = args.batch
+    B, n, k = c["batch"], c["n"], c["max_depth"]
+    gb = B * world
+    drafter = build_drafter(c, dev, seed=0)
+    trainer = Trainer(drafter, c, world)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    ids = torch.randint(0, c["vocab"], (B, n), generator=g, device=dev)
+    feats = torch.randn(B, n, 3 * c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    seqs = [(ids[b], feats[b]) for b in range(B)]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        trainer.step(seqs, gb)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = _lib.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            trainer.step(seqs, gb)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    launches = (_lib.launch_count() - l0) // max(1, args.steps)
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = gb * n * k / (ms / 1e3)
+    loss_val = float(trainer.loss.item()) / B
+
+    # ---- end to end through the public API: pinned host inputs, loss read back
+    from parallel_eagle_b200.partition import mtp_backward
+
+    h_ids = ids.cpu().pin_memory()
+    h_feats = feats.cpu().pin_memory()
+    fp = trainer.eng.flat
+
+    def e2e_step():
+        drafter.zero_grad(set_to_none=True)
+        tot = 0.0
+        for b in range(B):
+            tot += mtp_backward(drafter, h_ids[b], h_feats[b], c["segments"], loss_scale=1.0 / gb)
+        if world > 1:
+            dist.all_reduce(fp.grad)
+        trainer.sumsq.zero_()
+        ops.sumsq_into(fp.grad, trainer.sumsq)
+        trainer.t += 1
+        ops.adamw_step(fp.flat, fp.grad, trainer.m, trainer.v, trainer.sumsq, 1.0, trainer.lr,
+                       0.9, 0.999, 1e-8, 0.0, trainer.t)
+        return tot
+
+    e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    wall_ms = (time.perf_counter() - w0) * 1e3 / args.steps
+
+    # ---- roofline of the dominant kernel: the tensor-core GEMM, gate/up shape of the step
+    hbm, peak_burst, peak_sus, src = _peaks()
+    roof = gemm_roofline(c, dev, peak_sus, src)
+    step_tflops = step_flops_per_sequence(c) * B / (ms / 1e3) / 1e12
+
+    if rank == 0:
+        cpu = cpu_baseline(args) if (world == 1 and not args.no_cpu_baseline) else None
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded ids ~ U[0,V), features ~ N(0,1), heads ~ N(0,0.02^2))",
+            "config": {"workload": "BASELINE config 2: 7B-class drafter step", "hidden": c["hidden"],
+                       "heads": [c["n_heads"], c["n_kv_heads"]], "intermediate": c["intermediate"],
+                       "vocab": c["vocab"], "layers": c["num_layers"], "n": n, "K": k,
+                       "S": c["segments"], "batch_per_gpu": B, "global_batch": gb,
+                       "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (features 44 MB/sequence, weights 0.5 GB)"},
+            "loss": round(loss_val, 4),
+            "step_tflops": round(step_tflops, 1),
+            "step_frac_of_peak": round(step_tflops / peak_sus, 4),
+            "e2e": {"value": round(gb * n * k / (e2e_ms / 1e3), 1), "unit": UNIT,
+                    "h2d_bytes_per_step": int(B * (ids[0].numel() * 8 + feats[0].numel() * 2)),
+                    "d2h_bytes_per_step": int(4 * B), "wall_ms_per_step": round(wall_ms, 2)},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def gemm_roofline(c, dev, peak, src):
+    """Time the step's largest GEMM (fused gate/up projection of a 4096-slot
+    segment) with CUDA events on its stream."""
+    from parallel_eagle_b200 import ops
+
+    H, I = c["hidden"], c["intermediate"]
+    M = 4096
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    out = torch.empty(M, 2 * I, dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        ops.linear(x, w, out=out)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    times = []
+    for _ in range(10):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        ops.linear(x, w, out=out)
+        b.record(s)
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    ms = sum(times) / len(times)
+    flops = 2.0 * M * 2 * I * H
+    achieved = flops / (ms / 1e3) / 1e12
+    return {"kernel": "gemm_tc_kernel (gate/up projection, M=4096 N=37888 K=3584)",
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{src} bf16_tflops_sustained",
+            "traffic": None, "ms": round(ms, 4)}
+
+
+def cpu_baseline(args, n=None):
+    """The CPU oracle (a port of the reference step) on one bounded sample of the
+    workload: one config-2 sequence at reduced length, bf16, all host threads."""
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import oracle
+    import recipe
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    c = dict(CONFIG2)
+    n = n or args.cpu_n
+    dims = oracle.OracleDims(hidden=c["hidden"], n_heads=c["n_heads"], n_kv_heads=c["n_kv_heads"],
+                             intermediate=c["intermediate"], vocab=c["vocab"],
+                             num_layers=c["num_layers"], max_depth=c["max_depth"])
+    dt = torch.bfloat16
+    heads = recipe.make_heads(c["vocab"], c["hidden"], 0, 0.0, dt)
+    params = oracle.init_params(dims, 0, dt)
+    ids, feats = recipe.make_sequence(n, c["vocab"], 3 * c["hidden"], 0, 0)
+    feats = feats.to(dt)
+    t0 = time.perf_counter()
+    oracle.mtp_step(params, heads, ids, feats, dims, num_segments=c["segments"])
+    sec = time.perf_counter() - t0
+    return {"value": round(n * c["max_depth"] / sec, 2), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"one sequence, n={n} (config 2 dims, K=5, S=4, bf16), {sec:.1f} s",
+            "seconds": round(sec, 2)}
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    samples = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(args)
+        if i >= args.warmup:
+            samples.append(r)
+    sec = sum(s["seconds"] for s in samples) / len(samples)
+    value = args.cpu_n * CONFIG2["max_depth"] / sec
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 2: 7B-class drafter step", "n": args.cpu_n,
+                   "K": 5, "S": 4, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": samples[0]["cores"],
+                         "kind": "port", "sample": samples[0]["sample"]},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=None, help="override sequence length")
+    ap.add_argument("--batch", type=int, default=None, help="override per-GPU batch")
+    ap.add_argument("--cpu-n", type=int, default=256, help="sequence length of the CPU sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

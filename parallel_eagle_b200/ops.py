@@ -1,0 +1,361 @@
+"""Tensor-level wrappers over the C ABI (one function per kernel entry point).
+
+Each wrapper checks devices/dtypes, passes raw pointers, strides and the current
+CUDA stream, and turns a nonzero status into :class:`PeError`.  Outputs are
+allocated here (torch owns all memory); the library itself never allocates.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word the tensor-core kernels write a code into when a
+    bounded wait times out (0 = healthy)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def check_status(device: torch.device) -> None:
+    """Raise if any tensor-core kernel on ``device`` recorded a timed-out wait."""
+    s = status_word(device)
+    code = int(s.item())
+    if code != 0:
+        s.zero_()
+        raise L.PeError(f"a tensor-core kernel gave up waiting (fault code {code})")
+
+
+def _lib():
+    return L.load()
+
+
+def _row_stride(t: torch.Tensor) -> int:
+    if t.dim() != 2 or (t.stride(1) != 1 and t.shape[1] > 1):
+        raise L.PeError(
+            f"expected a 2-D row-major view, got shape {tuple(t.shape)} strides {t.stride()}"
+        )
+    return t.stride(0) if t.shape[0] > 1 else max(t.stride(0), t.shape[1])
+
+
+# ----------------------------------------------------------------- norms ----
+
+
+def rmsnorm_fwd(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None):
+    L.require_cuda(x, w)
+    rows, H = x.shape
+    if out is None:
+        out = torch.empty(rows, H, dtype=x.dtype, device=x.device)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    rc = _lib().pe_rmsnorm_fwd(
+        L.dtype_code(x.dtype), rows, H, x.data_ptr(), _row_stride(x), w.data_ptr(),
+        out.data_ptr(), _row_stride(out), rstd.data_ptr(), float(eps), L.stream_ptr(x.device),
+    )
+    L.check(rc, "pe_rmsnorm_fwd")
+    return out, rstd
+
+
+def rmsnorm_bwd(dy, x, w, rstd, dx=None, residual=None, want_dw: bool = True):
+    """Returns ``(dx, dw_partial)``; ``dx = residual + d/dx``; ``dw_partial`` is the
+    fp32 per-block partial reduced by :func:`colsum_into`."""
+    L.require_cuda(dy, x, w)
+    rows, H = x.shape
+    if dx is None:
+        dx = torch.empty(rows, H, dtype=x.dtype, device=x.device)
+    lib = _lib()
+    part = None
+    if want_dw:
+        nblk = int(lib.pe_rmsnorm_bwd_blocks(rows))
+        part = torch.empty(nblk, H, dtype=torch.float32, device=x.device)
+    rc = lib.pe_rmsnorm_bwd(
+        L.dtype_code(x.dtype), rows, H, dy.data_ptr(), _row_stride(dy), x.data_ptr(),
+        _row_stride(x), w.data_ptr(), rstd.data_ptr(), dx.data_ptr(), _row_stride(dx),
+        L.ptr(residual), _row_stride(residual) if residual is not None else 0, L.ptr(part),
+        L.stream_ptr(x.device),
+    )
+    L.check(rc, "pe_rmsnorm_bwd")
+    return dx, part
+
+
+def colsum_into(partial: torch.Tensor, out: torch.Tensor, accumulate: bool) -> torch.Tensor:
+    """``out (+)= partial.sum(0)`` with a fixed summation order."""
+    nblk, H = partial.shape
+    rc = _lib().pe_colsum_f32(
+        L.dtype_code(out.dtype), nblk, H, partial.data_ptr(), out.data_ptr(), int(accumulate),
+        L.stream_ptr(out.device),
+    )
+    L.check(rc, "pe_colsum_f32")
+    return out
+
+
+# ------------------------------------------------------------------ rope ----
+
+
+def rope_(x: torch.Tensor, heads: int, head_dim: int, pos: torch.Tensor, theta: float, inverse=False):
+    """In-place rotary embedding on the first ``heads * head_dim`` columns of each row."""
+    L.require_cuda(x, pos)
+    rc = _lib().pe_rope(
+        L.dtype_code(x.dtype), x.shape[0], heads, head_dim, x.data_ptr(), _row_stride(x),
+        pos.data_ptr(), float(theta), int(inverse), L.stream_ptr(x.device),
+    )
+    L.check(rc, "pe_rope")
+    return x
+
+
+# ------------------------------------------------------------------ gemm ----
+
+
+def gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, Cin=None, ldcin=0, alpha=1.0, beta=0.0,
+         algo=L.ALGO_AUTO):
+    """``C = alpha * A B^T + beta * Cin`` on raw element strides (see the C header)."""
+    L.require_cuda(A, B, C)
+    rc = _lib().pe_gemm(
+        L.dtype_code(A.dtype), M, N, K, A.data_ptr(), a_sm, a_sk, B.data_ptr(), b_sn, b_sk,
+        C.data_ptr(), ldc, L.dtype_code(C.dtype), L.ptr(Cin), ldcin, float(alpha), float(beta),
+        algo, status_word(C.device).data_ptr(), L.stream_ptr(C.device),
+    )
+    L.check(rc, "pe_gemm")
+    return C
+
+
+def linear(x, w, out=None, residual=None, algo=L.ALGO_AUTO):
+    """``out = x w^T (+ residual)``; x ``[M, K]`` (row view), w ``[N, K]``."""
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    return gemm(M, N, K, x, _row_stride(x), 1, w, _row_stride(w), 1, out, _row_stride(out),
+                residual, _row_stride(residual) if residual is not None else 0, 1.0,
+                1.0 if residual is not None else 0.0, algo)
+
+
+def linear_dgrad(dy, w, out=None, residual=None, algo=L.ALGO_AUTO):
+    """``out = dy w (+ residual)``; dy ``[M, N]``, w ``[N, K]`` -> ``[M, K]``."""
+    M, N = dy.shape
+    K = w.shape[1]
+    if out is None:
+        out = torch.empty(M, K, dtype=dy.dtype, device=dy.device)
+    return gemm(M, K, N, dy, _row_stride(dy), 1, w, 1, _row_stride(w), out, _row_stride(out),
+                residual, _row_stride(residual) if residual is not None else 0, 1.0,
+                1.0 if residual is not None else 0.0, algo)
+
+
+def linear_wgrad(dy, x, grad=None, accumulate=False, algo=L.ALGO_AUTO):
+    """``grad (+)= dy^T x``; dy ``[M, N]``, x ``[M, K]`` -> ``[N, K]``."""
+    M, N = dy.shape
+    K = x.shape[1]
+    if grad is None:
+        grad = torch.empty(N, K, dtype=dy.dtype, device=dy.device)
+        accumulate = False
+    return gemm(N, K, M, dy, 1, _row_stride(dy), x, 1, _row_stride(x), grad, _row_stride(grad),
+                grad if accumulate else None, _row_stride(grad), 1.0, 1.0 if accumulate else 0.0,
+                algo)
+
+
+# ------------------------------------------------------------- attention ----
+
+
+class AttnLayout:
+    """How the attention kernel re-derives the attend rule of a packed sequence.
+
+    ``LAYOUT_PARTITION``: the segment layout of the partitioned step (reference
+    ``partition.py:41-55``) -- slots ``0..a1-1`` are real, then anchors
+    ``a0..a1-1`` x depths ``1..k-1``; only ``(a0, a1, k)`` is needed.
+    ``LAYOUT_INDEXED``: explicit int32 per-slot ``anchor``/``depth``.
+    ``LAYOUT_BIAS``: a dense additive bias ``[B|1, 1, S, S]`` (the generic
+    ``ParallelDrafter.forward`` contract).
+    """
+
+    def __init__(self, kind: int, a0=0, a1=0, k=1, anchor=None, depth=None, bias=None):
+        self.kind, self.a0, self.a1, self.k = kind, a0, a1, k
+        self.anchor, self.depth, self.bias = anchor, depth, bias
+
+    def bias_strides(self):
+        if self.bias is None:
+            return 0, 0
+        b = self.bias
+        return (b.stride(0) if b.shape[0] > 1 else 0), b.stride(2)
+
+
+def _bsq(t: torch.Tensor):
+    if t.stride(2) != 1:
+        raise L.PeError("attention operands need unit stride along the head dimension")
+    return t.stride(0), t.stride(1)
+
+
+def attn_fwd(q, k, v, n_heads, n_kv_heads, head_dim, layout: AttnLayout, algo=L.ALGO_AUTO):
+    """q ``[B, S, Hq*hd]``, k/v ``[B, S, Hkv*hd]`` (row views; last stride 1)."""
+    L.require_cuda(q, k, v)
+    B, S = q.shape[0], q.shape[1]
+    o = torch.empty(B, S, n_heads * head_dim, dtype=q.dtype, device=q.device)
+    lse = torch.empty(B, n_heads, S, dtype=torch.float32, device=q.device)
+    bsb, bsq = layout.bias_strides()
+    rc = _lib().pe_attn_fwd(
+        L.dtype_code(q.dtype), B, S, n_heads, n_kv_heads, head_dim, q.data_ptr(), *_bsq(q),
+        k.data_ptr(), *_bsq(k), v.data_ptr(), *_bsq(v), o.data_ptr(), *_bsq(o), lse.data_ptr(),
+        layout.kind, layout.a0, layout.a1, layout.k, L.ptr(layout.anchor), L.ptr(layout.depth),
+        L.ptr(layout.bias), bsb, bsq, algo, status_word(q.device).data_ptr(),
+        L.stream_ptr(q.device),
+    )
+    L.check(rc, "pe_attn_fwd")
+    return o, lse
+
+
+def attn_bwd(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, layout: AttnLayout,
+             dq=None, dk=None, dv=None, algo=L.ALGO_AUTO):
+    L.require_cuda(q, k, v, o, do, lse)
+    B, S = q.shape[0], q.shape[1]
+    if dq is None:
+        dq = torch.empty(B, S, n_heads * head_dim, dtype=q.dtype, device=q.device)
+    if dk is None:
+        dk = torch.empty(B, S, n_kv_heads * head_dim, dtype=k.dtype, device=k.device)
+    if dv is None:
+        dv = torch.empty(B, S, n_kv_heads * head_dim, dtype=v.dtype, device=v.device)
+    delta = torch.empty(B, n_heads, S, dtype=torch.float32, device=q.device)
+    bsb, bsq = layout.bias_strides()
+    rc = _lib().pe_attn_bwd(
+        L.dtype_code(q.dtype), B, S, n_heads, n_kv_heads, head_dim, q.data_ptr(), *_bsq(q),
+        k.data_ptr(), *_bsq(k), v.data_ptr(), *_bsq(v), o.data_ptr(), *_bsq(o), do.data_ptr(),
+        *_bsq(do), lse.data_ptr(), dq.data_ptr(), *_bsq(dq), dk.data_ptr(), *_bsq(dk),
+        dv.data_ptr(), *_bsq(dv), delta.data_ptr(), layout.kind, layout.a0, layout.a1,
+        layout.k, L.ptr(layout.anchor), L.ptr(layout.depth), L.ptr(layout.bias), bsb, bsq, algo,
+        status_word(q.device).data_ptr(), L.stream_ptr(q.device),
+    )
+    L.check(rc, "pe_attn_bwd")
+    return dq, dk, dv
+
+
+# --------------------------------------------------------- lm head + loss ----
+
+_ws_cache: dict[int, torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    t = _ws_cache.get(key)
+    if t is None or t.numel() < nbytes:
+        t = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+        _ws_cache[key] = t
+    return t
+
+
+def lmhead_ce(h, W, labels, grad_scale, loss_sum, teacher=None, dh=None, algo=L.ALGO_AUTO):
+    """Fused frozen-head projection + CE (or soft-target) loss + input gradient.
+    ``loss_sum`` (fp32 [1]) is incremented; returns ``dh``."""
+    L.require_cuda(h, W)
+    R, H = h.shape
+    V = W.shape[0]
+    if dh is None:
+        dh = torch.empty(R, H, dtype=h.dtype, device=h.device)
+    lib = _lib()
+    soft = teacher is not None
+    nbytes = int(lib.pe_lmhead_ce_workspace(L.dtype_code(h.dtype), R, H, V, int(soft)))
+    ws = _workspace(h.device, nbytes)
+    rc = lib.pe_lmhead_ce(
+        L.dtype_code(h.dtype), R, H, V, h.data_ptr(), _row_stride(h), W.data_ptr(),
+        L.ptr(labels), L.ptr(teacher), _row_stride(teacher) if soft else 0, float(grad_scale),
+        dh.data_ptr(), _row_stride(dh), loss_sum.data_ptr(), ws.data_ptr(), ws.numel(), algo,
+        status_word(h.device).data_ptr(), L.stream_ptr(h.device),
+    )
+    L.check(rc, "pe_lmhead_ce")
+    return dh
+
+
+# ------------------------------------------------------------ small ops ----
+
+
+def embed_rows(ids, embed, out):
+    rows, H = ids.shape[0], embed.shape[1]
+    rc = _lib().pe_embed_rows(L.dtype_code(embed.dtype), rows, H, ids.data_ptr(), embed.data_ptr(),
+                              out.data_ptr(), _row_stride(out), L.stream_ptr(out.device))
+    L.check(rc, "pe_embed_rows")
+    return out
+
+
+def fill_rows(vec, out):
+    rows, H = out.shape
+    rc = _lib().pe_fill_rows(L.dtype_code(out.dtype), rows, H, vec.data_ptr(), out.data_ptr(),
+                             _row_stride(out), L.stream_ptr(out.device))
+    L.check(rc, "pe_fill_rows")
+    return out
+
+
+def swiglu_fwd(gu, inter, out=None):
+    rows = gu.shape[0]
+    if out is None:
+        out = torch.empty(rows, inter, dtype=gu.dtype, device=gu.device)
+    rc = _lib().pe_swiglu_fwd(L.dtype_code(gu.dtype), rows, inter, gu.data_ptr(), _row_stride(gu),
+                              out.data_ptr(), _row_stride(out), L.stream_ptr(gu.device))
+    L.check(rc, "pe_swiglu_fwd")
+    return out
+
+
+def swiglu_bwd(da, gu, inter, out=None):
+    rows = gu.shape[0]
+    if out is None:
+        out = torch.empty(rows, 2 * inter, dtype=gu.dtype, device=gu.device)
+    rc = _lib().pe_swiglu_bwd(L.dtype_code(gu.dtype), rows, inter, da.data_ptr(), _row_stride(da),
+                              gu.data_ptr(), _row_stride(gu), out.data_ptr(), _row_stride(out),
+                              L.stream_ptr(gu.device))
+    L.check(rc, "pe_swiglu_bwd")
+    return out
+
+
+def rowsum_cols(x, out=None):
+    rows, H = x.shape
+    if out is None:
+        out = torch.empty(H, dtype=torch.float32, device=x.device)
+    rc = _lib().pe_rowsum_cols(L.dtype_code(x.dtype), rows, H, x.data_ptr(), _row_stride(x),
+                               out.data_ptr(), L.stream_ptr(x.device))
+    L.check(rc, "pe_rowsum_cols")
+    return out
+
+
+def gather_rows(src, idx, out=None):
+    rows, H = idx.shape[0], src.shape[1]
+    if out is None:
+        out = torch.empty(rows, H, dtype=src.dtype, device=src.device)
+    rc = _lib().pe_gather_rows(L.dtype_code(src.dtype), rows, H, idx.data_ptr(), src.data_ptr(),
+                               _row_stride(src), out.data_ptr(), _row_stride(out),
+                               L.stream_ptr(src.device))
+    L.check(rc, "pe_gather_rows")
+    return out
+
+
+def scatter_rows(src, idx, out):
+    rows, H = src.shape
+    rc = _lib().pe_scatter_rows(L.dtype_code(src.dtype), rows, H, idx.data_ptr(), src.data_ptr(),
+                                _row_stride(src), out.data_ptr(), _row_stride(out),
+                                L.stream_ptr(src.device))
+    L.check(rc, "pe_scatter_rows")
+    return out
+
+
+def cast_from_f32(x, out):
+    rc = _lib().pe_cast_f32(L.dtype_code(out.dtype), x.numel(), x.data_ptr(), out.data_ptr(),
+                            L.stream_ptr(x.device))
+    L.check(rc, "pe_cast_f32")
+    return out
+
+
+def sumsq_into(g, out):
+    rc = _lib().pe_sumsq(L.dtype_code(g.dtype), g.numel(), g.data_ptr(), out.data_ptr(),
+                         L.stream_ptr(g.device))
+    L.check(rc, "pe_sumsq")
+    return out
+
+
+def adamw_step(p, g, m, v, sumsq, max_norm, lr, beta1, beta2, eps, weight_decay, step):
+    rc = _lib().pe_adamw_step(L.dtype_code(p.dtype), p.numel(), p.data_ptr(), g.data_ptr(),
+                              m.data_ptr(), v.data_ptr(), L.ptr(sumsq), float(max_norm), float(lr),
+                              float(beta1), float(beta2), float(eps), float(weight_decay), int(step),
+                              L.stream_ptr(p.device))
+    L.check(rc, "pe_adamw_step")

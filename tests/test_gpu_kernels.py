@@ -1,0 +1,306 @@
+"""Per-kernel parity on the GPU: each libpe_b200 entry point against a plain
+PyTorch fp32 reference of the same op (bf16 inputs are rounded first, so the
+reference sees exactly what the kernel sees)."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from gpu_harness import oracle, recipe
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover - collected on CPU boxes too
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from parallel_eagle_b200 import _lib as L  # noqa: E402
+from parallel_eagle_b200 import ops  # noqa: E402
+
+DEV = torch.device("cuda")
+rel = recipe.rel_fro
+
+
+def _rand(*shape, dtype=torch.bfloat16, scale=1.0, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(dtype).to(DEV)
+
+
+def _pad8(x):
+    return (x + 7) // 8 * 8
+
+
+# ------------------------------------------------------------------ GEMM ----
+
+
+def _operand(rows, cols, mn_major, dtype, seed):
+    """Logical [rows, cols] operand (rows = M or N, cols = K); returns the tensor,
+    (stride_row, stride_k) and the dense logical fp32 view."""
+    g = torch.Generator().manual_seed(seed)
+    dense = torch.randn(rows, cols, generator=g).to(dtype)
+    if not mn_major:
+        ld = _pad8(cols)
+        store = torch.zeros(rows, ld, dtype=dtype)
+        store[:, :cols] = dense
+        return store.to(DEV), (ld, 1), dense.float()
+    ld = _pad8(rows)
+    store = torch.zeros(cols, ld, dtype=dtype)
+    store[:, :rows] = dense.t()
+    return store.to(DEV), (1, ld), dense.float()
+
+
+@pytest.mark.parametrize("shape", [(128, 256, 64), (300, 200, 136), (1, 512, 256),
+                                   (257, 129, 1000), (512, 640, 384)])
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("out_f32", [False, True])
+def test_gemm_tcgen05_matches_fp32(shape, a_mn, b_mn, out_f32):
+    M, N, K = shape
+    A, (a_sm, a_sk), Ad = _operand(M, K, a_mn, torch.bfloat16, 1)
+    B, (b_sn, b_sk), Bd = _operand(N, K, b_mn, torch.bfloat16, 2)
+    cdt = torch.float32 if out_f32 else torch.bfloat16
+    ldc = _pad8(N)
+    C = torch.full((M, ldc), 7.0, dtype=cdt, device=DEV)
+    ref = Ad @ Bd.t()
+    ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, algo=L.ALGO_TCGEN05)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    got = C[:, :N].float().cpu()
+    assert rel(got, ref) < (1e-5 if out_f32 else 5e-3)
+    assert torch.all(C[:, N:].float() == 7.0)  # untouched padding
+    # accumulate: C = 0.5 * A B^T + 1.0 * C
+    prev = C[:, :N].float().cpu().clone()
+    ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, Cin=C, ldcin=ldc, alpha=0.5,
+             beta=1.0, algo=L.ALGO_TCGEN05)
+    torch.cuda.synchronize()
+    assert rel(C[:, :N].float().cpu(), prev + 0.5 * ref) < (1e-5 if out_f32 else 5e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+def test_gemm_simt_matches_fp32(dtype, a_mn, b_mn):
+    M, N, K = 77, 45, 133
+    A, (a_sm, a_sk), Ad = _operand(M, K, a_mn, dtype, 3)
+    B, (b_sn, b_sk), Bd = _operand(N, K, b_mn, dtype, 4)
+    C = torch.empty(M, N, dtype=dtype, device=DEV)
+    ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, N, algo=L.ALGO_SIMT)
+    torch.cuda.synchronize()
+    assert rel(C.float().cpu(), Ad @ Bd.t()) < (1e-6 if dtype == torch.float32 else 5e-3)
+
+
+def test_gemm_rejects_ineligible_tcgen05():
+    A = torch.zeros(16, 10, dtype=torch.bfloat16, device=DEV)  # row stride 10 elements: not 16 B
+    C = torch.zeros(16, 16, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(L.PeError):
+        ops.gemm(16, 16, 10, A, 10, 1, A, 10, 1, C, 16, algo=L.ALGO_TCGEN05)
+
+
+# --------------------------------------------------------------- RMSNorm ----
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("H", [64, 3584, 100])
+def test_rmsnorm_fwd_bwd(dtype, H):
+    rows = 37
+    x = _rand(rows, H, dtype=dtype, seed=5) * 3
+    w = (1 + 0.1 * _rand(H, dtype=torch.float32, seed=6)).to(dtype)
+    dy = _rand(rows, H, dtype=dtype, seed=7)
+    res = _rand(rows, H, dtype=dtype, seed=8)
+    y, rstd = ops.rmsnorm_fwd(x, w, 1e-5)
+    xr = x.float().cpu().requires_grad_(True)
+    wr = w.float().cpu().requires_grad_(True)
+    yr = oracle.rms_norm(xr, wr, 1e-5)
+    tol = 1e-6 if dtype == torch.float32 else 1e-2
+    assert rel(y.float().cpu(), yr) < tol
+    yr.backward(dy.float().cpu())
+    dx, part = ops.rmsnorm_bwd(dy, x, w, rstd, residual=res)
+    dw = ops.colsum_into(part, torch.zeros(H, dtype=torch.float32, device=DEV), accumulate=False)
+    torch.cuda.synchronize()
+    assert rel(dx.float().cpu() - res.float().cpu(), xr.grad) < (1e-5 if dtype == torch.float32 else 2e-2)
+    assert rel(dw.cpu(), wr.grad) < 1e-5
+
+
+# ------------------------------------------------------------------ RoPE ----
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rope_matches_reference_rotation(dtype):
+    S, heads, hd = 50, 6, 64
+    x = _rand(S, heads * hd + 16, dtype=dtype, seed=9)  # extra columns stay untouched
+    pos = torch.randint(0, 3000, (S,), generator=torch.Generator().manual_seed(1)).to(DEV)
+    y = x.clone()
+    ops.rope_(y, heads, hd, pos, 10000.0)
+    cos, sin = oracle.rope_tables(pos.cpu(), hd, 10000.0)
+    xh = x[:, : heads * hd].cpu().view(S, heads, hd).transpose(0, 1)
+    ref = oracle.drafter_step._rotate(xh, cos, sin).transpose(0, 1).reshape(S, heads * hd)
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert rel(y[:, : heads * hd].float().cpu(), ref.float()) < tol
+    assert torch.equal(y[:, heads * hd:], x[:, heads * hd:])
+    ops.rope_(y, heads, hd, pos, 10000.0, inverse=True)
+    assert rel(y.float().cpu(), x.float().cpu()) < (1e-5 if dtype == torch.float32 else 2e-2)
+
+
+# ------------------------------------------------------------- attention ----
+
+
+def _attn_reference(q, k, v, allow, nh, nkv, hd, do):
+    """fp32 dense-mask attention with autograd (reference nn.py:84-88)."""
+    S = q.shape[0]
+    qf = q.float().cpu().view(S, nh, hd).transpose(0, 1).requires_grad_(True)
+    kf = k.float().cpu().view(S, nkv, hd).transpose(0, 1).requires_grad_(True)
+    vf = v.float().cpu().view(S, nkv, hd).transpose(0, 1).requires_grad_(True)
+    rep = nh // nkv
+    kk = kf.repeat_interleave(rep, 0)
+    vv = vf.repeat_interleave(rep, 0)
+    s = qf @ kk.transpose(-1, -2) / math.sqrt(hd)
+    s = s.masked_fill(~allow, float("-inf"))
+    o = torch.softmax(s, -1) @ vv
+    o.backward(do.float().cpu().view(S, nh, hd).transpose(0, 1))
+    flat = lambda t: t.transpose(0, 1).reshape(S, -1)  # noqa: E731
+    return flat(o.detach()), flat(qf.grad), flat(kf.grad), flat(vf.grad)
+
+
+def _partition_allow(a0, a1, k):
+    anc, dep = oracle.segment_slots(a0, a1, k)
+    return oracle.slot_allow(anc, dep)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("layout_kind", ["partition", "indexed", "bias"])
+@pytest.mark.parametrize("geom", [(0, 9, 4, 4, 2, 8), (12, 40, 5, 4, 2, 64), (0, 33, 1, 2, 1, 128),
+                                  (20, 70, 3, 28, 4, 128)])
+def test_attention_simt_all_layouts(dtype, layout_kind, geom):
+    a0, a1, k, nh, nkv, hd = geom
+    allow = _partition_allow(a0, a1, k)
+    S = allow.shape[0]
+    q = _rand(S, nh * hd, dtype=dtype, seed=10)
+    kt = _rand(S, nkv * hd, dtype=dtype, seed=11)
+    vt = _rand(S, nkv * hd, dtype=dtype, seed=12)
+    do = _rand(S, nh * hd, dtype=dtype, seed=13)
+    if layout_kind == "partition":
+        lay = ops.AttnLayout(L.LAYOUT_PARTITION, a0=a0, a1=a1, k=k)
+    elif layout_kind == "indexed":
+        anc, dep = oracle.segment_slots(a0, a1, k)
+        lay = ops.AttnLayout(L.LAYOUT_INDEXED, anchor=anc.to(torch.int32).to(DEV),
+                             depth=dep.to(torch.int32).to(DEV))
+    else:
+        bias = oracle.drafter_step.additive_bias(allow, dtype)[None, None].to(DEV)
+        lay = ops.AttnLayout(L.LAYOUT_BIAS, bias=bias)
+    o, lse = ops.attn_fwd(q[None], kt[None], vt[None], nh, nkv, hd, lay, algo=L.ALGO_SIMT)
+    dq, dk, dv = ops.attn_bwd(q[None], kt[None], vt[None], o, do[None], lse, nh, nkv, hd, lay,
+                              algo=L.ALGO_SIMT)
+    torch.cuda.synchronize()
+    ro, rdq, rdk, rdv = _attn_reference(q, kt, vt, allow, nh, nkv, hd, do)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert rel(o[0].float().cpu(), ro) < tol
+    assert rel(dq[0].float().cpu(), rdq) < tol
+    assert rel(dk[0].float().cpu(), rdk) < tol
+    assert rel(dv[0].float().cpu(), rdv) < tol
+
+
+# ----------------------------------------------------------- LM head + CE ----
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("soft", [False, True])
+@pytest.mark.parametrize("R,H,V", [(37, 64, 1000), (130, 256, 20000)])
+def test_lmhead_ce(dtype, soft, R, H, V):
+    h = _rand(R, H, dtype=dtype, seed=14)
+    W = _rand(V, H, dtype=dtype, seed=15, scale=0.05)
+    labels = torch.randint(0, V, (R,), generator=torch.Generator().manual_seed(2)).to(DEV)
+    teacher = _rand(R, H, dtype=dtype, seed=16) if soft else None
+    loss = torch.zeros(1, dtype=torch.float32, device=DEV)
+    scale = 0.37
+    dh = ops.lmhead_ce(h, W, None if soft else labels, scale, loss, teacher=teacher)
+    torch.cuda.synchronize()
+    hr = h.float().cpu().requires_grad_(True)
+    z = (hr @ W.float().cpu().t()).to(dtype).float()
+    if soft:
+        pt = torch.softmax((teacher.float().cpu() @ W.float().cpu().t()).to(dtype).float(), -1)
+        lr = -(pt * torch.log_softmax(z, -1)).sum()
+    else:
+        lr = torch.nn.functional.cross_entropy(z, labels.cpu(), reduction="sum")
+    (lr * scale).backward()
+    assert abs(loss.item() - lr.item()) / abs(lr.item()) < 1e-4
+    assert rel(dh.float().cpu(), hr.grad) < (1e-4 if dtype == torch.float32 else 2e-2)
+
+
+def test_lmhead_ignores_negative_labels():
+    R, H, V = 20, 64, 300
+    h = _rand(R, H, seed=17)
+    W = _rand(V, H, seed=18, scale=0.05)
+    labels = torch.randint(0, V, (R,), generator=torch.Generator().manual_seed(3))
+    labels[::3] = -100
+    loss = torch.zeros(1, dtype=torch.float32, device=DEV)
+    dh = ops.lmhead_ce(h, W, labels.to(DEV), 1.0, loss)
+    torch.cuda.synchronize()
+    assert torch.all(dh[::3].float() == 0)
+    keep = labels >= 0
+    z = (h.float().cpu()[keep] @ W.float().cpu().t()).bfloat16().float()
+    ref = torch.nn.functional.cross_entropy(z, labels[keep], reduction="sum")
+    assert abs(loss.item() - ref.item()) / ref.item() < 1e-4
+
+
+# ------------------------------------------------------------- small ops ----
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_swiglu_fwd_bwd(dtype):
+    rows, inter = 33, 96
+    gu = _rand(rows, 2 * inter, dtype=dtype, seed=19)
+    da = _rand(rows, inter, dtype=dtype, seed=20)
+    a = ops.swiglu_fwd(gu, inter)
+    dgu = ops.swiglu_bwd(da, gu, inter)
+    torch.cuda.synchronize()
+    g = gu.float().cpu().requires_grad_(True)
+    ref = torch.nn.functional.silu(g[:, :inter]) * g[:, inter:]
+    ref.backward(da.float().cpu())
+    tol = 1e-6 if dtype == torch.float32 else 2e-2
+    assert rel(a.float().cpu(), ref.detach()) < tol
+    assert rel(dgu.float().cpu(), g.grad) < tol
+
+
+def test_rows_embed_fill_gather_scatter_colsum():
+    H = 40
+    E = _rand(50, H, seed=21)
+    ids = torch.tensor([3, 0, 49, 3], device=DEV)
+    out = torch.zeros(4, 2 * H, dtype=torch.bfloat16, device=DEV)
+    ops.embed_rows(ids, E, out[:, :H])
+    assert torch.equal(out[:, :H], E[ids]) and torch.all(out[:, H:] == 0)
+    vec = _rand(H, seed=22)
+    dst = torch.zeros(5, H, dtype=torch.bfloat16, device=DEV)
+    ops.fill_rows(vec, dst[1:4])
+    assert torch.equal(dst[1:4], vec.expand(3, H)) and torch.all(dst[0] == 0)
+    src = _rand(6, H, seed=23)
+    idx = torch.tensor([5, 1, 2], device=DEV)
+    g = ops.gather_rows(src, idx)
+    assert torch.equal(g, src[idx])
+    back = torch.zeros_like(src)
+    ops.scatter_rows(g, idx, back)
+    assert torch.equal(back[idx], src[idx]) and torch.all(back[0] == 0)
+    s = ops.rowsum_cols(src)
+    assert rel(s.cpu(), src.float().sum(0).cpu()) < 1e-6
+
+
+def test_adamw_with_clipping_matches_torch():
+    n = 5000
+    g = torch.Generator().manual_seed(4)
+    p0 = torch.randn(n, generator=g)
+    grads = [torch.randn(n, generator=g) * 3 for _ in range(3)]
+    p_ref = p0.clone().requires_grad_(True)
+    opt = torch.optim.AdamW([p_ref], lr=1e-2, weight_decay=0.1)
+    p = p0.clone().to(DEV)
+    m = torch.zeros(n, device=DEV)
+    v = torch.zeros(n, device=DEV)
+    for step, gr in enumerate(grads, 1):
+        p_ref.grad = gr.clone()
+        torch.nn.utils.clip_grad_norm_([p_ref], 1.0)
+        opt.step()
+        gd = gr.to(DEV)
+        ss = torch.zeros(1, device=DEV)
+        ops.sumsq_into(gd, ss)
+        ops.adamw_step(p, gd, m, v, ss, 1.0, 1e-2, 0.9, 0.999, 1e-8, 0.1, step)
+    torch.cuda.synchronize()
+    assert rel(p.cpu(), p_ref.detach()) < 1e-5

@@ -1,0 +1,41 @@
+"""The C-ABI library loads without a GPU and exports every entry point that
+``include/pe_b200.h`` declares, with the ctypes signatures the package binds."""
+
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared():
+    text = (ROOT / "include" / "pe_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(pe_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "pe_gemm" in names and "pe_attn_fwd" in names and "pe_lmhead_ce" in names
+
+
+def test_library_exports_every_declared_symbol():
+    from parallel_eagle_b200 import _lib
+
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert set(_declared()) == set(_lib.SIGNATURES), "ctypes table out of sync with the header"
+
+
+def test_host_only_queries_work_without_gpu():
+    from parallel_eagle_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.pe_version() >= 1
+    assert lib.pe_rmsnorm_bwd_blocks(10_000) >= 1
+    assert lib.pe_lmhead_ce_workspace(1, 100, 64, 1000, 0) > 0
+    # argument validation happens before any CUDA call
+    assert lib.pe_rope(1, 4, 2, 7, None, 14, None, 10000.0, 0, None) == 1
+    assert b"rope" in lib.pe_last_error()
