@@ -96,20 +96,31 @@ class FlatParams:
         buf = self.grad if grad else self.flat
         return buf[o0 : o1 + k1].view(-1, cols)
 
-    def attach_grads(self) -> None:
+    def attach_grads(self) -> list[str]:
         """Make every ``p.grad`` a view of the flat gradient buffer, keeping the
-        values already accumulated (``None`` grads start from zero)."""
+        values already accumulated (``None`` grads start from zero).  Returns the
+        names whose grad was ``None``."""
+        fresh = []
         for n, p in zip(self.names, self.params):
             o, k = self.offsets[n]
             region = self.grad[o : o + k]
             g = p.grad
             if g is None:
                 region.zero_()
+                fresh.append(n)
             elif g.data_ptr() != region.data_ptr():
                 region.copy_(g.reshape(-1))
             else:
                 continue
             p.grad = region.view(p.shape)
+        return fresh
+
+    def detach_grads(self, names) -> None:
+        """Return the listed parameters' grads to ``None`` (autograd leaves a
+        parameter outside the graph at ``None``; the step mirrors that)."""
+        for n, p in zip(self.names, self.params):
+            if n in names:
+                p.grad = None
 
 
 @dataclass
@@ -179,7 +190,7 @@ class StepEngine:
         d = self.d
         if not self.flat.valid():
             self.flat = FlatParams(d)
-        self.flat.attach_grads()
+        fresh = self.flat.attach_grads()
         dev = self.flat.device
         dt = self.flat.dtype
         input_ids = input_ids.to(dev, non_blocking=True)
@@ -193,6 +204,7 @@ class StepEngine:
         total = max(1, count_loss_slots(n, k, prompt_len))
         self.loss_sum.zero_()
         scale = loss_scale / total
+        ran = mask_slots = False
         for a0, a1 in segment_bounds(n, num_segments):
             # a segment contributes iff some target t in [a0+1, a1+k-1] is in [prompt_len, n)
             if max(a0 + 1, prompt_len) > min(a1 + k - 1, n - 1):
@@ -201,6 +213,13 @@ class StepEngine:
             if plan.rows == 0:
                 continue
             self._segment(plan, input_ids, features, scale, teacher_labels, teacher_hidden)
+            ran = True
+            mask_slots = mask_slots or plan.q > plan.a1
+        if fresh:
+            untouched = set(fresh) if not ran else (
+                set() if mask_slots else {"mask_emb", "h_shared"} & set(fresh))
+            if untouched:
+                self.flat.detach_grads(untouched)
         if not sync:
             return None
         return float(self.loss_sum.item()) / total

@@ -1,0 +1,133 @@
+"""Host-side logic that needs no GPU: the masks API (reference tests/test_masks.py
+pins), config defaults, segmenting/counting rules, the LR schedule, feature-layer
+resolution and the flat parameter buffer."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import oracle
+from parallel_eagle_b200 import config, engine, masks, partition, target, train
+
+
+def test_mtp_allow_small_exact():
+    # reference tests/test_masks.py:16-28 (n=2 anchors, K=2)
+    expected = torch.tensor([[1, 0, 0, 0], [1, 1, 0, 0], [1, 0, 1, 0], [1, 0, 1, 1]], dtype=torch.bool)
+    assert torch.equal(masks.mtp_allow_mask(2, 2), expected)
+
+
+def test_amortized_equals_naive_and_is_topleft():
+    amort = masks.AmortizedMtpMask(max_anchors=8, k=4)
+    for n in (1, 3, 5, 8):
+        assert torch.equal(amort.allow(n), masks.mtp_allow_mask(n, 4))
+    assert torch.equal(masks.mtp_allow_mask(3, 4), masks.mtp_allow_mask(8, 4)[:12, :12])
+    with pytest.raises(ValueError):
+        amort.allow(9)
+
+
+def test_positions_labels_and_bias():
+    assert masks.mtp_position_ids(4, 3).tolist() == [0, 1, 2, 1, 2, 3, 2, 3, 4, 3, 4, 5]
+    labels = masks.mtp_labels(torch.tensor([10, 11, 12, 13]), 3)
+    assert labels[:3].tolist() == [11, 12, 13] and labels[-3:].tolist() == [-100] * 3
+    allow = masks.mtp_allow_mask(3, 2)
+    b = masks.to_additive_bias(allow, torch.bfloat16)
+    assert b.shape == (1, 1, 6, 6)
+    assert torch.all(b[0, 0][allow] == 0)
+    assert torch.all(b[0, 0][~allow] == torch.finfo(torch.bfloat16).min)
+
+
+def test_allow_rule_matches_oracle_on_random_subsets():
+    g = torch.Generator().manual_seed(0)
+    a = torch.randint(0, 20, (50,), generator=g)
+    d = torch.randint(0, 5, (50,), generator=g)
+    assert torch.equal(masks.allow_from_slots(a, d), oracle.slot_allow(a, d))
+
+
+def test_config_defaults_match_reference():
+    assert config.TrainConfig().num_segments == 1
+    assert config.TargetConfig().feature_layers is None
+    d = config.DrafterConfig()
+    assert d.hidden_size is None and d.vocab_size is None and d.num_layers >= 1 and d.max_depth >= 1
+
+
+@pytest.mark.parametrize("n,k,p", [(20, 4, 7), (9, 4, 0), (2, 3, 0), (2048, 5, 0), (100, 8, 37), (5, 1, 2)])
+def test_loss_slot_count_closed_form(n, k, p):
+    assert partition._total_valid_after(n, k, p) == oracle.count_loss_slots(n, k, p)
+    assert partition._total_valid(n, k) == oracle.count_loss_slots(n, k, 0)
+
+
+@pytest.mark.parametrize("n,s", [(9, 3), (5, 2), (2, 20), (2048, 4), (13, 6), (1, 1)])
+def test_segment_bounds_match_oracle(n, s):
+    assert partition._segment_bounds(n, s) == oracle.segment_edges(n, s)
+
+
+def test_segment_slots_match_oracle():
+    a, d, nr = partition._segment_slots(3, 7, 4, "cpu")
+    oa, od = oracle.segment_slots(3, 7, 4)
+    assert torch.equal(a, oa) and torch.equal(d, od) and nr == 7
+
+
+def test_lr_schedule():
+    assert train.lr_at(0, 100, 1.0, 0.1) == 0.0
+    assert train.lr_at(5, 100, 1.0, 0.1) == 0.5
+    assert train.lr_at(10, 100, 1.0, 0.1) == 1.0
+    assert train.lr_at(100, 100, 1.0, 0.1) == 0.0
+
+
+def test_feature_layer_resolution():
+    assert target.resolve_feature_layers(None, 28) == (7, 15, 27)
+    assert target.resolve_feature_layers((-1, 3), 10) == (10, 3)
+    assert target.resolve_feature_layers(None, 2) == (1, 2, 2)
+
+
+def _tiny_drafter(seed=0):
+    from parallel_eagle_b200.drafter import ParallelDrafter
+    from parallel_eagle_b200.nn import RMSNorm
+
+    H, V = 32, 64
+    embed, head, norm = torch.nn.Embedding(V, H), torch.nn.Linear(H, V, bias=False), RMSNorm(H)
+    torch.manual_seed(seed)
+    return ParallelDrafter(hidden=H, n_heads=4, n_kv_heads=2, intermediate=48, vocab=V,
+                           feature_dim=3 * H, rope_theta=1e4, eps=1e-5, num_layers=2, max_depth=3,
+                           embed_module=embed, lm_head_module=head, final_norm_module=norm)
+
+
+def test_drafter_init_matches_reference_order():
+    # the oracle's init is pinned bit-exactly to the reference's (test_oracle_golden);
+    # the drafter draws its parameters in the same order from the same seed
+    d = _tiny_drafter(seed=5)
+    dims = oracle.OracleDims(hidden=32, n_heads=4, n_kv_heads=2, intermediate=48, vocab=64,
+                             num_layers=2, max_depth=3)
+    ref = oracle.init_params(dims, 5)
+    sd = d.state_dict()
+    assert list(sd) == oracle.param_names(2)
+    for k in sd:
+        assert torch.equal(sd[k], ref[k]), k
+
+
+def test_flat_params_views_and_grad_attachment():
+    d = _tiny_drafter()
+    before = {k: v.clone() for k, v in d.state_dict().items()}
+    fp = engine.FlatParams(d)
+    assert fp.valid()
+    for k, v in d.state_dict().items():
+        assert torch.equal(v, before[k])
+    # q/k/v and gate/up are one contiguous matrix each; mask_emb|h_shared adjacent
+    qkv = fp.span("layers.0.attn.q_proj.weight", "layers.0.attn.v_proj.weight", 32)
+    assert torch.equal(qkv, torch.cat([before[f"layers.0.attn.{n}_proj.weight"] for n in "qkv"]))
+    cat = fp.span("mask_emb", "h_shared", 64)
+    assert torch.equal(cat[0], torch.cat([before["mask_emb"], before["h_shared"]]))
+    assert fp.offsets["feat_proj.weight"][0] % 128 == 0
+    # grads: None -> zero view; foreign tensor -> copied in; view kept as is
+    p0 = d.in_proj.weight
+    p0.grad = torch.ones_like(p0)
+    fp.attach_grads()
+    assert p0.grad.data_ptr() == fp.view("in_proj.weight", grad=True).data_ptr()
+    assert torch.all(p0.grad == 1) and torch.all(d.mask_emb.grad == 0)
+    fp.grad.add_(1)
+    fp.attach_grads()
+    assert torch.all(p0.grad == 2)
+    # moving the module invalidates the flat views
+    d.to(torch.float64)
+    assert not fp.valid()
