@@ -66,7 +66,8 @@ extern "C" int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int
   if (rc) return rc;
   if (S == 0) return PE_OK;
   MaskSpec m{layout, a0, a1, kdepth, anchor, depth, bias, bias_sb, bias_sq};
-  const bool tc = attn_tc_eligible(dtype, B, S, Hq, Hkv, head_dim, layout, q, q_ss, k, k_ss, v,
+  const bool tc = attn_tc_bwd_ready() &&
+                  attn_tc_eligible(dtype, B, S, Hq, Hkv, head_dim, layout, q, q_ss, k, k_ss, v,
                                    v_ss);
   if (algo == PE_ALGO_TCGEN05) PE_CHECK_ARG(tc, "attention: inputs not eligible for tcgen05");
   if (tc && algo != PE_ALGO_SIMT)

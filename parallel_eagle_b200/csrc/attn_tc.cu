@@ -1,26 +1,361 @@
-// Tensor-core (tcgen05) cross-depth masked attention.  Not yet enabled: every
-// call is routed to the CUDA-core kernels.
+// Cross-depth masked flash attention on the 5th-generation tensor cores
+// (forward).  bf16 in/out, fp32 softmax, head_dim 128, partition slot layout
+// (reference src/pe/nn.py:71-89 with the mask of src/pe/masks.py:43-61 and the
+// segment layout of src/pe/partition.py:41-55).
+//
+// One CTA = one 128-slot query tile of one head.  The attend rule leaves each
+// query row (anchor i, depth d) exactly two key intervals: the real keys
+// [0, i] and its own anchor's prediction keys [lo_i, lo_i + d).  A query tile
+// therefore visits only the key tiles under those intervals: the causal band of
+// the real stream plus one or two tiles on the prediction-slot diagonal -- the
+// ~90% of the dense (S x S) score matrix the rule forbids is never computed.
+//
+// Warp roles (192 threads):
+//   warp 0      TMA: Q tile once, then K/V tiles into a 2-stage ring
+//   warp 1      tcgen05.mma issue: S_j = Q K_j^T into a double-buffered TMEM
+//               score tile, O += P_j V_j into the TMEM output tile
+//   warps 2..5  softmax: row per thread, scores from TMEM, online max/sum in
+//               fp32, P (bf16) to shared memory, rescale of O in TMEM
+// TMEM: O [128 x 128 fp32] in columns 0..127, S buffers in 128..383.
 #include "attn.cuh"
+#include "sm100.cuh"
 
 namespace pe {
+namespace {
 
-bool attn_tc_eligible(int, int64_t, int64_t, int, int, int, int, const void*, int64_t,
-                      const void*, int64_t, const void*, int64_t) {
-  return false;
+using namespace sm100;
+
+constexpr int HD = 128;       // head dim
+constexpr int TQ = 128;       // query rows per CTA
+constexpr int TK = 128;       // keys per tile
+constexpr int kThreads = 192;
+constexpr uint32_t TILE_BYTES = TQ * HD * 2;  // 32 KB: two 64-column swizzle chunks
+constexpr uint32_t CHUNK = TILE_BYTES / 2;     // 16 KB
+constexpr size_t SMEM_FWD = 1024 + TILE_BYTES /*Q*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ +
+                            TILE_BYTES /*P*/ + 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct PartGeom {
+  int S, a0, a1, km1;  // km1 = K - 1 (0 when K == 1)
+};
+
+// anchor / depth of slot s in the partition layout
+__device__ __forceinline__ void decode(const PartGeom& g, int s, int& i, int& d) {
+  if (s < g.a1 || g.km1 == 0) {
+    i = s;
+    d = 0;
+  } else {
+    const int t = s - g.a1;
+    i = g.a0 + t / g.km1;
+    d = 1 + t % g.km1;
+  }
 }
 
-int attn_fwd_tc_launch(int64_t, int, int, const void*, int64_t, const void*, int64_t,
-                       const void*, int64_t, void*, int64_t, float*, const MaskSpec&, int*,
-                       cudaStream_t) {
-  set_error("tcgen05 attention not built");
-  return PE_ERR_UNSUPPORTED;
+// Key tiles visited by query tile qt: [0, r_end) then [m_beg, m_end) (may be empty)
+struct TileList {
+  int r_end, m_beg, m_end;
+  __device__ __forceinline__ int count() const { return r_end + (m_end - m_beg); }
+  __device__ __forceinline__ int tile(int j) const { return j < r_end ? j : m_beg + (j - r_end); }
+};
+
+__device__ __forceinline__ TileList tiles_for(const PartGeom& g, int q0) {
+  const int last = min(q0 + TQ, g.S) - 1;
+  int i_last, d_last;
+  decode(g, last, i_last, d_last);
+  TileList L;
+  L.r_end = i_last / TK + 1;
+  L.m_beg = L.m_end = 0;
+  if (last >= g.a1 && g.km1 > 0) {
+    const int first = max(q0, g.a1);
+    int i_first, d_first;
+    decode(g, first, i_first, d_first);
+    const int lo = g.a1 + (i_first - g.a0) * g.km1;
+    const int hi = g.a1 + (i_last - g.a0 + 1) * g.km1;  // exclusive
+    int mb = lo / TK, me = (hi - 1) / TK + 1;
+    if (mb < L.r_end) mb = L.r_end;  // already covered by the real band
+    if (me > mb) {
+      L.m_beg = mb;
+      L.m_end = me;
+    }
+  }
+  return L;
 }
+
+// byte offset of 16-byte unit u (0..7) of row r inside a 128B-swizzled chunk
+__device__ __forceinline__ uint32_t swz(int r, int u) {
+  return (uint32_t)(r * 128 + ((u ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
+                   int64_t o_ss, float* __restrict__ lse, PartGeom g, int Hq, int rep,
+                   float scale_log2, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + TILE_BYTES;                   // stage s: K at +s*2*TILE, V at +TILE
+  uint8_t* sP = sKV + 4 * TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_empty = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_qt = (g.S + TQ - 1) / TQ;
+  const int qt = num_qt - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int h = blockIdx.y;
+  const int kvh = h / rep;
+  const int q0 = qt * TQ;
+  const TileList tl = tiles_for(g, q0);
+  const int n = tl.count();
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem, tS0 = tmem + 128;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      bool ok = true;
+      int last_st = -1;
+      uint32_t last_ph = 0;
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_2d(sQ, &tmQ, q_full, h * HD, q0);
+      tma_load_2d(sQ + CHUNK, &tmQ, q_full, h * HD + 64, q0);
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, status, 201)) { ok = false; break; }
+        const int k0 = tl.tile(j) * TK;
+        uint8_t* k_dst = sKV + st * 2 * TILE_BYTES;
+        uint8_t* v_dst = k_dst + TILE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        tma_load_2d(k_dst, &tmK, &kv_full[st], kvh * HD, k0);
+        tma_load_2d(k_dst + CHUNK, &tmK, &kv_full[st], kvh * HD + 64, k0);
+        tma_load_2d(v_dst, &tmV, &kv_full[st], kvh * HD, k0);
+        tma_load_2d(v_dst + CHUNK, &tmV, &kv_full[st], kvh * HD + 64, k0);
+        last_st = st;
+        last_ph = ph;
+      }
+      if (!ok && last_st >= 0) mbar_wait(&kv_full[last_st], last_ph, nullptr, 0);
+      mbar_wait(q_full, 0, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t IDESC_S = idesc_bf16(TQ, TK, false, false);
+      constexpr uint32_t IDESC_O = idesc_bf16(TQ, HD, false, true);
+      const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, status, 202);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, status, 203)) return false;
+        if (!mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1u, status, 204)) return false;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(sKV + st * 2 * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(tS0 + st * 128, sw128_desc(q_base + off, 16, 1024),
+                      sw128_desc(k_base + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[st]);
+        return true;
+      };
+      if (ok && n > 0) ok = issue_s(0);
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n && !issue_s(j + 1)) { ok = false; break; }
+        if (!mbar_wait(p_full, j & 1, status, 205)) { ok = false; break; }
+        tc_fence_after();
+        const int st = j & 1;
+        const uint32_t v_base = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk) {
+          const uint32_t poff = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(tO, sw128_desc(p_base + poff, 16, 1024),
+                      sw128_desc(v_base + kk * 2048, CHUNK, 1024), IDESC_O,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&kv_empty[st]);
+        mma_commit(pv_done);
+      }
+    }
+  } else {
+    // ---------------- softmax warps ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int s = q0 + row;
+    const bool valid = s < g.S;
+    int qi = 0, qd = 0;
+    if (valid) decode(g, s, qi, qd);
+    const int lo = qd > 0 ? g.a1 + (qi - g.a0) * g.km1 : 0;
+    const int hi = lo + qd;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1, status, 206)) { ok = false; break; }
+      tc_fence_after();
+      float sc[TK];
+#pragma unroll
+      for (int c = 0; c < TK; c += 32) tmem_ld32(tS0 + st * 128 + lane_off + c, sc + c);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[st]);
+      const int k0 = tl.tile(j) * TK;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < TK; ++c) {
+        const int kslot = k0 + c;
+        const bool allow = (kslot <= qi) || (kslot >= lo && kslot < hi);
+        sc[c] = allow ? sc[c] * scale_log2 : -INFINITY;
+        mt = fmaxf(mt, sc[c]);
+      }
+      const float m_new = fmaxf(m, mt);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = (m == m_new) ? 1.f : exp2f(m - m_use);
+      float rs = 0.f;
+      uint32_t pk[TK / 2];
+#pragma unroll
+      for (int c = 0; c < TK; c += 2) {
+        const float p0 = exp2f(sc[c] - m_use), p1 = exp2f(sc[c + 1] - m_use);
+        rs += p0 + p1;
+        pk[c / 2] = pack_bf16x2(p0, p1);
+      }
+      l = l * alpha + rs;
+      m = m_new;
+      if (j > 0) {
+        // O holds sum over tiles < j: wait for PV(j-1) before touching O or P
+        if (!mbar_wait(pv_done, (j - 1) & 1, status, 207)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 32) {
+            float ov[32];
+            tmem_ld32(tO + lane_off + c, ov);
+            tmem_wait_ld();
+            uint32_t ou[32];
+#pragma unroll
+            for (int t = 0; t < 32; ++t) ou[t] = __float_as_uint(ov[t] * alpha);
+            tmem_st16(tO + lane_off + c, ou);
+            tmem_st16(tO + lane_off + c + 16, ou + 16);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row -> shared memory, 128B-swizzled K-major (keys contiguous)
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        uint8_t* base = sP + ch * CHUNK;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int w = ch * 32 + u * 4;
+          *reinterpret_cast<uint4*>(base + swz(row, u)) =
+              make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok && n > 0 && mbar_wait(pv_done, (n - 1) & 1, status, 208)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float ov[32];
+        tmem_ld32(tO + lane_off + c, ov);
+        tmem_wait_ld();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(O + (int64_t)s * o_ss + h * HD + c);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16x2(ov[8 * q] * inv, ov[8 * q + 1] * inv),
+                                pack_bf16x2(ov[8 * q + 2] * inv, ov[8 * q + 3] * inv),
+                                pack_bf16x2(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv),
+                                pack_bf16x2(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv));
+        }
+      }
+      if (valid) lse[(int64_t)h * g.S + s] = (m + log2f(l)) * kLn2;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+bool attn_tc_eligible(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd, int layout,
+                      const void* q, int64_t q_ss, const void* k, int64_t k_ss, const void* v,
+                      int64_t v_ss) {
+  return dtype == PE_BF16 && B == 1 && hd == HD && layout == PE_LAYOUT_PARTITION &&
+         S > 0 && S < (1 << 30) && al16(q) && al16(k) && al16(v) && q_ss % 8 == 0 &&
+         k_ss % 8 == 0 && v_ss % 8 == 0 && q_ss >= (int64_t)Hq * HD && k_ss >= (int64_t)Hkv * HD &&
+         v_ss >= (int64_t)Hkv * HD;
+}
+
+int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
+                       int64_t k_ss, const void* v, int64_t v_ss, void* o, int64_t o_ss,
+                       float* lse, const MaskSpec& m, int* status, cudaStream_t st) {
+  PE_CHECK_ARG(o_ss % 8 == 0 && al16(o), "attention (tcgen05): output must be 16-byte aligned");
+  CUtensorMap tq, tk, tv;
+  int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, TQ);
+  if (!rc) rc = make_tmap_2d(&tk, k, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)k_ss * 2, 64, TK);
+  if (!rc) rc = make_tmap_2d(&tv, v, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)v_ss * 2, 64, TK);
+  if (rc) return rc;
+  PartGeom g{(int)S, (int)m.a0, (int)m.a1, m.kd - 1};
+  const float scale_log2 = kLog2e / sqrtf((float)HD);
+  PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)SMEM_FWD));
+  dim3 grid((unsigned)((S + TQ - 1) / TQ), (unsigned)Hq);
+  attn_fwd_tc_kernel<<<grid, kThreads, SMEM_FWD, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
+                                                       g, Hq, Hq / Hkv, scale_log2, status);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
+bool attn_tc_bwd_ready() { return false; }
 
 int attn_bwd_tc_launch(int64_t, int, int, const void*, int64_t, const void*, int64_t,
                        const void*, int64_t, const void*, int64_t, const void*, int64_t,
                        const float*, void*, int64_t, void*, int64_t, void*, int64_t, float*,
                        const MaskSpec&, int*, cudaStream_t) {
-  set_error("tcgen05 attention not built");
+  set_error("tcgen05 attention backward not built");
   return PE_ERR_UNSUPPORTED;
 }
 

@@ -200,6 +200,34 @@ def test_attention_simt_all_layouts(dtype, layout_kind, geom):
     assert rel(dv[0].float().cpu(), rdv) < tol
 
 
+TC_GEOMS = [(0, 300, 5, 4, 2), (256, 512, 5, 4, 1), (100, 333, 3, 8, 2), (0, 130, 1, 4, 2),
+            (1500, 2048, 5, 2, 1), (0, 64, 8, 2, 2), (37, 41, 4, 4, 4)]
+
+
+def _qkv_view(S, nh, nkv, seed):
+    """q/k/v as column blocks of one fused [S, (nh + 2 nkv) * 128] buffer, as the
+    training step lays them out."""
+    hd = 128
+    cq, ckv = nh * hd, nkv * hd
+    qkv = _rand(S, cq + 2 * ckv, seed=seed)
+    v3 = qkv.view(1, S, -1)
+    return v3[:, :, :cq], v3[:, :, cq:cq + ckv], v3[:, :, cq + ckv:]
+
+
+@pytest.mark.parametrize("geom", TC_GEOMS)
+def test_attention_tcgen05_fwd_matches_simt(geom):
+    a0, a1, k, nh, nkv = geom
+    S = a1 + (a1 - a0) * (k - 1)
+    q, kt, vt = _qkv_view(S, nh, nkv, seed=30)
+    lay = ops.AttnLayout(L.LAYOUT_PARTITION, a0=a0, a1=a1, k=k)
+    o_ref, lse_ref = ops.attn_fwd(q, kt, vt, nh, nkv, 128, lay, algo=L.ALGO_SIMT)
+    o, lse = ops.attn_fwd(q, kt, vt, nh, nkv, 128, lay, algo=L.ALGO_TCGEN05)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert rel(o.float().cpu(), o_ref.float().cpu()) < 1e-2
+    assert torch.allclose(lse.cpu(), lse_ref.cpu(), atol=2e-3, rtol=1e-4)
+
+
 # ----------------------------------------------------------- LM head + CE ----
 
 
