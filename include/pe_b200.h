@@ -109,15 +109,18 @@ int pe_attn_fwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
                 int64_t o_sb, int64_t o_ss, float* lse, int layout, int64_t a0, int64_t a1,
                 int kdepth, const int32_t* anchor, const int32_t* depth, const void* bias,
                 int64_t bias_sb, int64_t bias_sq, int algo, int32_t* status, void* stream);
-/* dq/dk/dv are overwritten.  delta (fp32 [B, Hq, S]) is workspace. */
+/* dq/dk/dv are overwritten.  `workspace` holds per-row softmax deltas and, on
+ * the tensor-core path, an fp32 dQ accumulator; its size comes from
+ * pe_attn_bwd_workspace (same shape arguments). */
+size_t pe_attn_bwd_workspace(int dtype, int64_t B, int64_t S, int Hq, int head_dim);
 int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
                 const void* q, int64_t q_sb, int64_t q_ss, const void* k, int64_t k_sb,
                 int64_t k_ss, const void* v, int64_t v_sb, int64_t v_ss, const void* o,
                 int64_t o_sb, int64_t o_ss, const void* dout, int64_t do_sb, int64_t do_ss,
                 const float* lse, void* dq, int64_t dq_sb, int64_t dq_ss, void* dk,
                 int64_t dk_sb, int64_t dk_ss, void* dv, int64_t dv_sb, int64_t dv_ss,
-                float* delta, int layout, int64_t a0, int64_t a1, int kdepth,
-                const int32_t* anchor, const int32_t* depth, const void* bias,
+                void* workspace, size_t workspace_bytes, int layout, int64_t a0, int64_t a1,
+                int kdepth, const int32_t* anchor, const int32_t* depth, const void* bias,
                 int64_t bias_sb, int64_t bias_sq, int algo, int32_t* status, void* stream);
 
 /* ---------------------------------------------------------------------------

@@ -4,6 +4,8 @@
 
 namespace pe {
 
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
 static int check_common(int64_t B, int64_t S, int Hq, int Hkv, int hd, int layout, int64_t a0,
                         int64_t a1, int kd, const int32_t* anchor, const int32_t* depth,
                         const void* bias) {
@@ -57,25 +59,39 @@ extern "C" int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int
                            int64_t v_ss, const void* o, int64_t o_sb, int64_t o_ss,
                            const void* dout, int64_t do_sb, int64_t do_ss, const float* lse,
                            void* dq, int64_t dq_sb, int64_t dq_ss, void* dk, int64_t dk_sb,
-                           int64_t dk_ss, void* dv, int64_t dv_sb, int64_t dv_ss, float* delta,
-                           int layout, int64_t a0, int64_t a1, int kdepth,
-                           const int32_t* anchor, const int32_t* depth, const void* bias,
-                           int64_t bias_sb, int64_t bias_sq, int algo, int32_t* status,
-                           void* stream) {
+                           int64_t dk_ss, void* dv, int64_t dv_sb, int64_t dv_ss,
+                           void* workspace, size_t workspace_bytes, int layout, int64_t a0,
+                           int64_t a1, int kdepth, const int32_t* anchor, const int32_t* depth,
+                           const void* bias, int64_t bias_sb, int64_t bias_sq, int algo,
+                           int32_t* status, void* stream) {
   int rc = check_common(B, S, Hq, Hkv, head_dim, layout, a0, a1, kdepth, anchor, depth, bias);
   if (rc) return rc;
   if (S == 0) return PE_OK;
+  const size_t delta_bytes = align256((size_t)B * Hq * S * 4);
+  PE_CHECK_ARG(workspace && workspace_bytes >= delta_bytes,
+               "attention backward: workspace too small (see pe_attn_bwd_workspace)");
+  float* delta = static_cast<float*>(workspace);
   MaskSpec m{layout, a0, a1, kdepth, anchor, depth, bias, bias_sb, bias_sq};
   const bool tc = attn_tc_bwd_ready() &&
                   attn_tc_eligible(dtype, B, S, Hq, Hkv, head_dim, layout, q, q_ss, k, k_ss, v,
-                                   v_ss);
+                                   v_ss) &&
+                  workspace_bytes >= delta_bytes + (size_t)S * Hq * head_dim * 4;
   if (algo == PE_ALGO_TCGEN05) PE_CHECK_ARG(tc, "attention: inputs not eligible for tcgen05");
-  if (tc && algo != PE_ALGO_SIMT)
+  if (tc && algo != PE_ALGO_SIMT) {
+    float* dq_acc = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + delta_bytes);
     return attn_bwd_tc_launch(S, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, dout, do_ss, lse,
-                              dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, m, status,
+                              dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, dq_acc, m, status,
                               as_stream(stream));
+  }
   return attn_bwd_simt_launch(dtype, B, S, Hq, Hkv, head_dim, q, q_sb, q_ss, k, k_sb, k_ss, v,
                               v_sb, v_ss, o, o_sb, o_ss, dout, do_sb, do_ss, lse, dq, dq_sb,
                               dq_ss, dk, dk_sb, dk_ss, dv, dv_sb, dv_ss, delta, m,
                               as_stream(stream));
+}
+
+extern "C" size_t pe_attn_bwd_workspace(int dtype, int64_t B, int64_t S, int Hq, int head_dim) {
+  if (B <= 0 || S <= 0 || Hq <= 0 || head_dim <= 0) return 0;
+  size_t bytes = align256((size_t)B * Hq * S * 4);
+  if (dtype == PE_BF16 && B == 1) bytes += align256((size_t)S * Hq * head_dim * 4);
+  return bytes;
 }

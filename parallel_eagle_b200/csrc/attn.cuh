@@ -64,6 +64,7 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
                        int64_t k_ss, const void* v, int64_t v_ss, const void* o, int64_t o_ss,
                        const void* dout, int64_t do_ss, const float* lse, void* dq,
                        int64_t dq_ss, void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
-                       float* delta, const MaskSpec& m, int* status, cudaStream_t st);
+                       float* delta, float* dq_acc, const MaskSpec& m, int* status,
+                       cudaStream_t st);
 
 }  // namespace pe

@@ -17,40 +17,17 @@
 //   warps 2..5  softmax: row per thread, scores from TMEM, online max/sum in
 //               fp32, P (bf16) to shared memory, rescale of O in TMEM
 // TMEM: O [128 x 128 fp32] in columns 0..127, S buffers in 128..383.
-#include "attn.cuh"
-#include "sm100.cuh"
+#include "attn_tc.cuh"
 
 namespace pe {
 namespace {
 
 using namespace sm100;
+using namespace attn_tc;
 
-constexpr int HD = 128;       // head dim
-constexpr int TQ = 128;       // query rows per CTA
-constexpr int TK = 128;       // keys per tile
 constexpr int kThreads = 192;
-constexpr uint32_t TILE_BYTES = TQ * HD * 2;  // 32 KB: two 64-column swizzle chunks
-constexpr uint32_t CHUNK = TILE_BYTES / 2;     // 16 KB
 constexpr size_t SMEM_FWD = 1024 + TILE_BYTES /*Q*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ +
                             TILE_BYTES /*P*/ + 256;
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
-
-struct PartGeom {
-  int S, a0, a1, km1;  // km1 = K - 1 (0 when K == 1)
-};
-
-// anchor / depth of slot s in the partition layout
-__device__ __forceinline__ void decode(const PartGeom& g, int s, int& i, int& d) {
-  if (s < g.a1 || g.km1 == 0) {
-    i = s;
-    d = 0;
-  } else {
-    const int t = s - g.a1;
-    i = g.a0 + t / g.km1;
-    d = 1 + t % g.km1;
-  }
-}
 
 // Key tiles visited by query tile qt: [0, r_end) then [m_beg, m_end) (may be empty)
 struct TileList {
@@ -63,8 +40,11 @@ __device__ __forceinline__ TileList tiles_for(const PartGeom& g, int q0) {
   const int last = min(q0 + TQ, g.S) - 1;
   int i_last, d_last;
   decode(g, last, i_last, d_last);
+  // largest anchor in the tile: the last row's, or -- when the tile straddles the
+  // real/prediction boundary -- the last real row's (anchor a1 - 1 at most)
+  const int i_max = q0 < g.a1 ? max(i_last, min(last, g.a1 - 1)) : i_last;
   TileList L;
-  L.r_end = i_last / TK + 1;
+  L.r_end = i_max / TK + 1;
   L.m_beg = L.m_end = 0;
   if (last >= g.a1 && g.km1 > 0) {
     const int first = max(q0, g.a1);
@@ -80,11 +60,6 @@ __device__ __forceinline__ TileList tiles_for(const PartGeom& g, int q0) {
     }
   }
   return L;
-}
-
-// byte offset of 16-byte unit u (0..7) of row r inside a 128B-swizzled chunk
-__device__ __forceinline__ uint32_t swz(int r, int u) {
-  return (uint32_t)(r * 128 + ((u ^ (r & 7)) << 4));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -316,8 +291,6 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
 }
 
-bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
 }  // namespace
 
 bool attn_tc_eligible(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd, int layout,
@@ -347,16 +320,6 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
                                                        g, Hq, Hq / Hkv, scale_log2, status);
   PE_LAUNCHED();
   return PE_OK;
-}
-
-bool attn_tc_bwd_ready() { return false; }
-
-int attn_bwd_tc_launch(int64_t, int, int, const void*, int64_t, const void*, int64_t,
-                       const void*, int64_t, const void*, int64_t, const void*, int64_t,
-                       const float*, void*, int64_t, void*, int64_t, void*, int64_t, float*,
-                       const MaskSpec&, int*, cudaStream_t) {
-  set_error("tcgen05 attention backward not built");
-  return PE_ERR_UNSUPPORTED;
 }
 
 }  // namespace pe

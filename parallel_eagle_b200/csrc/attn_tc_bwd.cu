@@ -1,0 +1,455 @@
+// Cross-depth masked flash attention on the 5th-generation tensor cores
+// (backward): dQ, dK, dV for bf16, head_dim 128, partition slot layout
+// (the backward of reference src/pe/nn.py:84-88 under the mask of
+// src/pe/masks.py:43-61).
+//
+// One CTA = one 128-slot key tile of one KV head.  It loops over the query heads
+// of its GQA group and, per head, over the query tiles whose rows can see any
+// key of the tile (the rule's key-side view: a real key j is read by the real
+// rows j.. and every prediction row of anchors >= j; a prediction key (i, e) only
+// by the rows (i, d >= e)).  Per (head, query tile), with the key on TMEM lanes:
+//   S^T  = K Q^T          dP^T = V dO^T               (tcgen05, TMEM)
+//   P^T  = exp(scale S^T - lse)   dS^T = P^T (dP^T - delta)   (softmax warps,
+//          bf16 to shared memory; masked pairs are exactly zero)
+//   dV  += P^T dO         dK  += dS^T Q               (TMEM accumulators)
+//   dQ_part = dS K        -> fp32 vector atomics into a dQ accumulator
+// dK and dV never leave TMEM until the CTA is done; the accumulated dQ is
+// scaled and cast by a final pass.  GQA needs no K/V expansion: the group's
+// heads reuse the K/V tile held in shared memory.
+//
+// TMEM columns: dK 0..127, dV 128..255, S^T (then dQ_part) 256..383, dP^T 384..511.
+#include "attn_tc.cuh"
+
+namespace pe {
+namespace {
+
+using namespace sm100;
+using namespace attn_tc;
+
+constexpr int kThreads = 192;
+// K, V, Q, dO, P^T, dS^T tiles + per-query (lse, delta, anchor, depth) x 2 buffers
+constexpr size_t SMEM_BWD = 1024 + 6 * TILE_BYTES + 2 * 4 * TQ * 4 + 256;
+
+struct Ranges {
+  int b[3], e[3], n;
+  __device__ __forceinline__ int count() const {
+    int c = 0;
+    for (int i = 0; i < n; ++i) c += e[i] - b[i];
+    return c;
+  }
+  __device__ __forceinline__ int at(int j) const {
+    for (int i = 0; i < n; ++i) {
+      const int len = e[i] - b[i];
+      if (j < len) return b[i] + j;
+      j -= len;
+    }
+    return 0;
+  }
+};
+
+// query tiles whose rows can read some key of key tile [k0, k0 + TK)
+__device__ __forceinline__ Ranges query_tiles(const PartGeom& g, int k0) {
+  const int k1 = min(k0 + TK, g.S);
+  const int nqt = (g.S + TQ - 1) / TQ;
+  int b[3], e[3], n = 0;
+  if (k0 < g.a1) {
+    // real queries [k0, a1)
+    b[n] = k0 / TQ;
+    e[n] = (g.a1 - 1) / TQ + 1;
+    ++n;
+    // prediction rows of anchors >= max(a0, k0)
+    const int af = max(g.a0, k0);
+    if (g.km1 > 0 && af < g.a1) {
+      b[n] = (g.a1 + (af - g.a0) * g.km1) / TQ;
+      e[n] = nqt;
+      ++n;
+    }
+  }
+  if (k1 > g.a1 && g.km1 > 0) {
+    const int s0 = max(k0, g.a1);
+    const int i_f = g.a0 + (s0 - g.a1) / g.km1;
+    const int i_l = g.a0 + (k1 - 1 - g.a1) / g.km1;
+    b[n] = (g.a1 + (i_f - g.a0) * g.km1) / TQ;
+    e[n] = (g.a1 + (i_l - g.a0 + 1) * g.km1 - 1) / TQ + 1;
+    ++n;
+  }
+  // sort by start (n <= 3) and merge overlapping / adjacent ranges
+  for (int i = 1; i < n; ++i)
+    for (int j = i; j > 0 && b[j] < b[j - 1]; --j) {
+      int t = b[j]; b[j] = b[j - 1]; b[j - 1] = t;
+      t = e[j]; e[j] = e[j - 1]; e[j - 1] = t;
+    }
+  Ranges R;
+  R.n = 0;
+  for (int i = 0; i < n; ++i) {
+    if (R.n > 0 && b[i] <= R.e[R.n - 1]) {
+      R.e[R.n - 1] = max(R.e[R.n - 1], e[i]);
+    } else {
+      R.b[R.n] = b[i];
+      R.e[R.n] = e[i];
+      ++R.n;
+    }
+  }
+  return R;
+}
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                   const float* __restrict__ lse, const float* __restrict__ delta,
+                   float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dk, int64_t dk_ss,
+                   __nv_bfloat16* __restrict__ dv, int64_t dv_ss, PartGeom g, int Hq, int rep,
+                   float scale, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE_BYTES;
+  uint8_t* sQ = sV + TILE_BYTES;
+  uint8_t* sDO = sQ + TILE_BYTES;
+  uint8_t* sP = sDO + TILE_BYTES;   // P^T  [key rows][query cols]
+  uint8_t* sDS = sP + TILE_BYTES;   // dS^T [key rows][query cols]
+  float* sL = reinterpret_cast<float*>(sDS + TILE_BYTES);  // [2][TQ] lse * log2(e)
+  float* sD = sL + 2 * TQ;                                  // [2][TQ] delta
+  int* sA = reinterpret_cast<int*>(sD + 2 * TQ);            // [2][TQ] query anchor
+  int* sDp = sA + 2 * TQ;                                   // [2][TQ] query depth
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDp + 2 * TQ);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* p_full = bars + 4;
+  uint64_t* mm_done = bars + 5;
+  uint64_t* dq_read = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x;  // low key tiles are read by the most query tiles: first
+  const int kvh = blockIdx.y;
+  const int k0 = kt * TK;
+  const Ranges qr = query_tiles(g, k0);
+  const int nq = qr.count();
+  const int n_it = nq * rep;  // iteration it -> head kvh*rep + it / nq, query tile qr.at(it % nq)
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qdo_full, 1);
+    mbar_init(qdo_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(mm_done, 1);
+    mbar_init(dq_read, 4);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tDK = tmem, tDV = tmem + 128, tS = tmem + 256, tDP = tmem + 384;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      bool ok = true;
+      int issued = 0;
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_2d(sK, &tmK, kv_full, kvh * HD, k0);
+      tma_load_2d(sK + CHUNK, &tmK, kv_full, kvh * HD + 64, k0);
+      tma_load_2d(sV, &tmV, kv_full, kvh * HD, k0);
+      tma_load_2d(sV + CHUNK, &tmV, kv_full, kvh * HD + 64, k0);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (!mbar_wait(qdo_empty, (it & 1) ^ 1u, status, 301)) { ok = false; break; }
+        const int h = kvh * rep + it / nq;
+        const int q0 = qr.at(it % nq) * TQ;
+        mbar_arrive_expect_tx(qdo_full, 2 * TILE_BYTES);
+        tma_load_2d(sQ, &tmQ, qdo_full, h * HD, q0);
+        tma_load_2d(sQ + CHUNK, &tmQ, qdo_full, h * HD + 64, q0);
+        tma_load_2d(sDO, &tmDO, qdo_full, h * HD, q0);
+        tma_load_2d(sDO + CHUNK, &tmDO, qdo_full, h * HD + 64, q0);
+        issued = it + 1;
+      }
+      mbar_wait(kv_full, 0, nullptr, 0);
+      if (issued > 0) mbar_wait(qdo_full, (issued - 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t ID_KK = idesc_bf16(TK, TQ, false, false);  // S^T, dP^T
+      constexpr uint32_t ID_KM = idesc_bf16(TK, HD, false, true);   // dV, dK
+      constexpr uint32_t ID_MM = idesc_bf16(TQ, HD, true, true);    // dQ
+      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV), q_base = smem_u32(sQ);
+      const uint32_t do_base = smem_u32(sDO), p_base = smem_u32(sP), ds_base = smem_u32(sDS);
+      bool ok = mbar_wait(kv_full, 0, status, 302);
+      for (int it = 0; it < n_it && ok; ++it) {
+        if (!mbar_wait(qdo_full, it & 1, status, 303)) { ok = false; break; }
+        if (it > 0 && !mbar_wait(dq_read, (it - 1) & 1, status, 304)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(tS, sw128_desc(k_base + off, 16, 1024), sw128_desc(q_base + off, 16, 1024),
+                      ID_KK, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(tDP, sw128_desc(v_base + off, 16, 1024), sw128_desc(do_base + off, 16, 1024),
+                      ID_KK, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(s_full);
+        if (!mbar_wait(p_full, it & 1, status, 305)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TQ / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * CHUNK + (kk & 3) * 32;  // K-major over queries
+          const uint32_t boff = kk * 2048;                          // MN-major, 16 rows per step
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          mma_bf16_ss(tDV, sw128_desc(p_base + aoff, 16, 1024),
+                      sw128_desc(do_base + boff, CHUNK, 1024), ID_KM, acc);
+          mma_bf16_ss(tDK, sw128_desc(ds_base + aoff, 16, 1024),
+                      sw128_desc(q_base + boff, CHUNK, 1024), ID_KM, acc);
+        }
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk) {
+          const uint32_t off = kk * 2048;  // both MN-major, 16 key rows per step
+          mma_bf16_ss(tS, sw128_desc(ds_base + off, CHUNK, 1024),
+                      sw128_desc(k_base + off, CHUNK, 1024), ID_MM, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(qdo_empty);
+        mma_commit(mm_done);
+      }
+    }
+  } else {
+    // ---------------- softmax / epilogue warps (128 threads) ----------------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // TMEM lane: key row (S^T, dP^T, dK, dV) / query row (dQ)
+    const int tid = row;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int kj = k0 + row;
+    const bool kvalid = kj < g.S;
+    int ka = 0, ke = 0;
+    if (kvalid) decode(g, kj, ka, ke);
+    const float scale_log2 = scale * kLog2e;
+    const int64_t dq_ld = (int64_t)Hq * HD;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = kvh * rep + it / nq;
+      const int q0 = qr.at(it % nq) * TQ;
+      const int buf = it & 1;
+      {
+        // per-query operands of this tile, one per thread
+        const int q = q0 + tid;
+        float lv = INFINITY, dl = 0.f;
+        int qa = -1, qd = 0;
+        if (q < g.S) {
+          lv = lse[(int64_t)h * g.S + q] * kLog2e;
+          dl = delta[(int64_t)h * g.S + q];
+          decode(g, q, qa, qd);
+        }
+        sL[buf * TQ + tid] = lv;
+        sD[buf * TQ + tid] = dl;
+        sA[buf * TQ + tid] = qa;
+        sDp[buf * TQ + tid] = qd;
+      }
+      named_sync(1, 128);
+      if (!mbar_wait(s_full, it & 1, status, 306)) { ok = false; break; }
+      tc_fence_after();
+      const float* L2 = sL + buf * TQ;
+      const float* DL = sD + buf * TQ;
+      const int* QA = sA + buf * TQ;
+      const int* QD = sDp + buf * TQ;
+#pragma unroll 1
+      for (int c0 = 0; c0 < TQ; c0 += 32) {
+        float sv[32], dpv[32];
+        tmem_ld32(tS + lane_off + c0, sv);
+        tmem_ld32(tDP + lane_off + c0, dpv);
+        tmem_wait_ld();
+        uint32_t pw[16], dw[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float pp[2], dd[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int qc = c0 + c + t;
+            const int qa = QA[qc];
+            const bool allow = kvalid && qa >= 0 &&
+                               (ke == 0 ? (ka <= qa) : (ka == qa && ke <= QD[qc]));
+            const float p = allow ? exp2f(sv[c + t] * scale_log2 - L2[qc]) : 0.f;
+            pp[t] = p;
+            dd[t] = p * (dpv[c + t] - DL[qc]);
+          }
+          pw[c / 2] = pack_bf16x2(pp[0], pp[1]);
+          dw[c / 2] = pack_bf16x2(dd[0], dd[1]);
+        }
+        const int ch = c0 >> 6;
+        const int u0 = (c0 & 63) >> 3;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t off = ch * CHUNK + swz(row, u0 + u);
+          *reinterpret_cast<uint4*>(sP + off) =
+              make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
+          *reinterpret_cast<uint4*>(sDS + off) =
+              make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // dQ partial (query row per TMEM lane) -> fp32 atomics
+      if (!mbar_wait(mm_done, it & 1, status, 307)) { ok = false; break; }
+      tc_fence_after();
+      const int q = q0 + row;
+#pragma unroll 1
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        float v[32];
+        tmem_ld32(tS + lane_off + c0, v);
+        tmem_wait_ld();
+        if (q < g.S) {
+          float4* dst = reinterpret_cast<float4*>(dq_acc + (int64_t)q * dq_ld + h * HD + c0);
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            atomicAdd(dst + t, make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_read);
+    }
+    // dK, dV (key row per TMEM lane) -> bf16
+    if (ok) {
+#pragma unroll 1
+      for (int part = 0; part < 2; ++part) {
+        const uint32_t tsrc = part == 0 ? tDK : tDV;
+        const float mul = part == 0 ? scale : 1.f;
+        __nv_bfloat16* dst = part == 0 ? dk + (int64_t)kj * dk_ss + kvh * HD
+                                       : dv + (int64_t)kj * dv_ss + kvh * HD;
+#pragma unroll 1
+        for (int c0 = 0; c0 < HD; c0 += 32) {
+          float v[32];
+          if (n_it > 0) {
+            tmem_ld32(tsrc + lane_off + c0, v);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) v[t] = 0.f;
+          }
+          if (kvalid) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              d4[t] = make_uint4(pack_bf16x2(v[8 * t] * mul, v[8 * t + 1] * mul),
+                                 pack_bf16x2(v[8 * t + 2] * mul, v[8 * t + 3] * mul),
+                                 pack_bf16x2(v[8 * t + 4] * mul, v[8 * t + 5] * mul),
+                                 pack_bf16x2(v[8 * t + 6] * mul, v[8 * t + 7] * mul));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[h, s] = sum_d dO * O (fp32) and zero the dQ accumulator row
+__global__ void attn_bwd_prep_kernel(int S, int Hq, const __nv_bfloat16* __restrict__ o,
+                                     int64_t o_ss, const __nv_bfloat16* __restrict__ dout,
+                                     int64_t do_ss, float* __restrict__ delta,
+                                     float* __restrict__ dq_acc) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= S * Hq) return;
+  const int s = w / Hq, h = w - (w / Hq) * Hq;
+  // 128 dims: 4 per lane (8 bytes)
+  const uint2 a = *reinterpret_cast<const uint2*>(o + (int64_t)s * o_ss + h * HD + lane * 4);
+  const uint2 b = *reinterpret_cast<const uint2*>(dout + (int64_t)s * do_ss + h * HD + lane * 4);
+  const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(b2[i]);
+    acc += x.x * y.x + x.y * y.y;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) delta[(int64_t)h * S + s] = acc;
+  reinterpret_cast<float4*>(dq_acc + (int64_t)s * Hq * HD + h * HD)[lane] =
+      make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// dq (bf16, row stride dq_ss) = scale * dq_acc
+__global__ void attn_dq_cast_kernel(int S, int Hq, const float* __restrict__ dq_acc, float scale,
+                                    __nv_bfloat16* __restrict__ dq, int64_t dq_ss) {
+  const int64_t total = (int64_t)S * Hq * HD / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i * 8;
+    const int64_t s = e / (Hq * HD), c = e - s * (Hq * HD);
+    const float4 x = reinterpret_cast<const float4*>(dq_acc + e)[0];
+    const float4 y = reinterpret_cast<const float4*>(dq_acc + e)[1];
+    *reinterpret_cast<uint4*>(dq + s * dq_ss + c) =
+        make_uint4(pack_bf16x2(x.x * scale, x.y * scale), pack_bf16x2(x.z * scale, x.w * scale),
+                   pack_bf16x2(y.x * scale, y.y * scale), pack_bf16x2(y.z * scale, y.w * scale));
+  }
+}
+
+}  // namespace
+
+bool attn_tc_bwd_ready() { return true; }
+
+int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
+                       int64_t k_ss, const void* v, int64_t v_ss, const void* o, int64_t o_ss,
+                       const void* dout, int64_t do_ss, const float* lse, void* dq,
+                       int64_t dq_ss, void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
+                       float* delta, float* dq_acc, const MaskSpec& m, int* status,
+                       cudaStream_t st) {
+  PE_CHECK_ARG(o_ss % 8 == 0 && do_ss % 8 == 0 && dq_ss % 8 == 0 && dk_ss % 8 == 0 &&
+                   dv_ss % 8 == 0 && al16(o) && al16(dout) && al16(dq) && al16(dk) && al16(dv),
+               "attention backward (tcgen05): operands must be 16-byte aligned");
+  CUtensorMap tq, tk, tv, tdo;
+  int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, TQ);
+  if (!rc) rc = make_tmap_2d(&tk, k, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)k_ss * 2, 64, TK);
+  if (!rc) rc = make_tmap_2d(&tv, v, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)v_ss * 2, 64, TK);
+  if (!rc)
+    rc = make_tmap_2d(&tdo, dout, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)do_ss * 2, 64, TQ);
+  if (rc) return rc;
+  const int Si = (int)S;
+  {
+    const int warps = Si * Hq;
+    attn_bwd_prep_kernel<<<(warps + 7) / 8, 256, 0, st>>>(
+        Si, Hq, (const __nv_bfloat16*)o, o_ss, (const __nv_bfloat16*)dout, do_ss, delta, dq_acc);
+    PE_LAUNCHED();
+  }
+  PartGeom g{Si, (int)m.a0, (int)m.a1, m.kd - 1};
+  const float scale = 1.0f / sqrtf((float)HD);
+  PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)SMEM_BWD));
+  dim3 grid((unsigned)((S + TK - 1) / TK), (unsigned)Hkv);
+  attn_bwd_tc_kernel<<<grid, kThreads, SMEM_BWD, st>>>(
+      tq, tk, tv, tdo, lse, delta, dq_acc, (__nv_bfloat16*)dk, dk_ss, (__nv_bfloat16*)dv, dv_ss,
+      g, Hq, Hq / Hkv, scale, status);
+  PE_LAUNCHED();
+  {
+    const int64_t total = S * Hq * HD / 8;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
+    attn_dq_cast_kernel<<<(unsigned)blocks, 256, 0, st>>>(Si, Hq, dq_acc, scale,
+                                                           (__nv_bfloat16*)dq, dq_ss);
+    PE_LAUNCHED();
+  }
+  return PE_OK;
+}
+
+}  // namespace pe

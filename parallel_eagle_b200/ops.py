@@ -219,13 +219,15 @@ def attn_bwd(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, layout: AttnLay
         dk = torch.empty(B, S, n_kv_heads * head_dim, dtype=k.dtype, device=k.device)
     if dv is None:
         dv = torch.empty(B, S, n_kv_heads * head_dim, dtype=v.dtype, device=v.device)
-    delta = torch.empty(B, n_heads, S, dtype=torch.float32, device=q.device)
+    lib = _lib()
+    nbytes = int(lib.pe_attn_bwd_workspace(L.dtype_code(q.dtype), B, S, n_heads, head_dim))
+    ws = _workspace(q.device, nbytes, "attn_bwd")
     bsb, bsq = layout.bias_strides()
-    rc = _lib().pe_attn_bwd(
+    rc = lib.pe_attn_bwd(
         L.dtype_code(q.dtype), B, S, n_heads, n_kv_heads, head_dim, q.data_ptr(), *_bsq(q),
         k.data_ptr(), *_bsq(k), v.data_ptr(), *_bsq(v), o.data_ptr(), *_bsq(o), do.data_ptr(),
         *_bsq(do), lse.data_ptr(), dq.data_ptr(), *_bsq(dq), dk.data_ptr(), *_bsq(dk),
-        dv.data_ptr(), *_bsq(dv), delta.data_ptr(), layout.kind, layout.a0, layout.a1,
+        dv.data_ptr(), *_bsq(dv), ws.data_ptr(), ws.numel(), layout.kind, layout.a0, layout.a1,
         layout.k, L.ptr(layout.anchor), L.ptr(layout.depth), L.ptr(layout.bias), bsb, bsq, algo,
         status_word(q.device).data_ptr(), L.stream_ptr(q.device),
     )
@@ -235,11 +237,13 @@ def attn_bwd(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, layout: AttnLay
 
 # --------------------------------------------------------- lm head + loss ----
 
-_ws_cache: dict[int, torch.Tensor] = {}
+_ws_cache: dict[tuple, torch.Tensor] = {}
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    key = device.index if device.index is not None else torch.cuda.current_device()
+def _workspace(device: torch.device, nbytes: int, purpose: str = "lmhead") -> torch.Tensor:
+    """Grow-only per-device scratch buffer for one kernel family (reused across
+    calls on the same stream; callers never hold it past the call)."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(), purpose)
     t = _ws_cache.get(key)
     if t is None or t.numel() < nbytes:
         t = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)

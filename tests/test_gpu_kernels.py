@@ -228,6 +228,27 @@ def test_attention_tcgen05_fwd_matches_simt(geom):
     assert torch.allclose(lse.cpu(), lse_ref.cpu(), atol=2e-3, rtol=1e-4)
 
 
+@pytest.mark.parametrize("geom", TC_GEOMS)
+def test_attention_tcgen05_bwd_matches_simt(geom):
+    a0, a1, k, nh, nkv = geom
+    S = a1 + (a1 - a0) * (k - 1)
+    q, kt, vt = _qkv_view(S, nh, nkv, seed=31)
+    do = _rand(1, S, nh * 128, seed=32)
+    lay = ops.AttnLayout(L.LAYOUT_PARTITION, a0=a0, a1=a1, k=k)
+    o, lse = ops.attn_fwd(q, kt, vt, nh, nkv, 128, lay, algo=L.ALGO_SIMT)
+    ref = ops.attn_bwd(q, kt, vt, o, do, lse, nh, nkv, 128, lay, algo=L.ALGO_SIMT)
+    # gradients written straight into a fused [S, q|k|v] buffer, as the training step does
+    dqkv = torch.full((1, S, (nh + 2 * nkv) * 128), float("nan"), dtype=torch.bfloat16, device=DEV)
+    cq, ckv = nh * 128, nkv * 128
+    got = ops.attn_bwd(q, kt, vt, o, do, lse, nh, nkv, 128, lay, dq=dqkv[:, :, :cq],
+                       dk=dqkv[:, :, cq:cq + ckv], dv=dqkv[:, :, cq + ckv:], algo=L.ALGO_TCGEN05)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    for name, a, b in zip(("dq", "dk", "dv"), got, ref):
+        assert not torch.isnan(a).any(), name
+        assert rel(a.float().cpu(), b.float().cpu()) < 2e-2, name
+
+
 # ----------------------------------------------------------- LM head + CE ----
 
 
