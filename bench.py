@@ -295,6 +295,7 @@ def run_ours(args):
     # ---- roofline of the dominant kernel: the tensor-core GEMM, gate/up shape of the step
     hbm, peak_burst, peak_sus, src = _peaks()
     roof = gemm_roofline(c, dev, peak_sus, src)
+    attn = attention_roofline(c, dev, peak_burst, src)
     step_tflops = step_flops_per_sequence(c) * B / (ms / 1e3) / 1e12
 
     if rank == 0:
@@ -317,6 +318,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": int(B * (ids[0].numel() * 8 + feats[0].numel() * 2)),
                     "d2h_bytes_per_step": int(4 * B), "wall_ms_per_step": round(wall_ms, 2)},
             "roofline": roof,
+            "attention": attn,
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
@@ -358,6 +360,49 @@ def gemm_roofline(c, dev, peak, src):
             "bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4), "peak_source": f"{src} bf16_tflops_sustained",
             "traffic": None, "ms": round(ms, 4)}
+
+
+def attention_roofline(c, dev, peak, src):
+    """Masked-attention fwd+bwd over the S segments of one config-2 sequence,
+    timed with CUDA events; FLOPs = 12 * hd * Hq * allowed pairs (no recompute)."""
+    from parallel_eagle_b200 import _lib, ops
+    from parallel_eagle_b200.engine import segment_bounds
+
+    nh, nkv, hd, k = c["n_heads"], c["n_kv_heads"], c["hidden"] // c["n_heads"], c["max_depth"]
+    cols = (nh + 2 * nkv) * hd
+    g = torch.Generator(device=dev).manual_seed(11)
+    segs = []
+    for a0, a1 in segment_bounds(c["n"], c["segments"]):
+        S = a1 + (a1 - a0) * (k - 1)
+        qkv = torch.randn(1, S, cols, generator=g, device=dev).to(torch.bfloat16)
+        do = torch.randn(1, S, nh * hd, generator=g, device=dev).to(torch.bfloat16)
+        lay = ops.AttnLayout(_lib.LAYOUT_PARTITION, a0=a0, a1=a1, k=k)
+        segs.append((qkv, do, lay))
+
+    def run():
+        for qkv, do, lay in segs:
+            q, kk, vv = qkv[:, :, : nh * hd], qkv[:, :, nh * hd:(nh + nkv) * hd], qkv[:, :, (nh + nkv) * hd:]
+            o, lse = ops.attn_fwd(q, kk, vv, nh, nkv, hd, lay)
+            ops.attn_bwd(q, kk, vv, o, do, lse, nh, nkv, hd, lay)
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    a.record(s)
+    for _ in range(reps):
+        run()
+    b.record(s)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    flops = 12.0 * hd * nh * attention_pairs(c["n"], k, c["segments"])
+    achieved = flops / (ms / 1e3) / 1e12
+    return {"kernels": "attn_fwd_tc_kernel + attn_bwd_tc_kernel (+ prep/cast)",
+            "segments": c["segments"], "ms_per_sequence": round(ms, 3),
+            "tflops": round(achieved, 1), "peak": peak, "frac": round(achieved / peak, 4),
+            "peak_source": f"{src} bf16_tflops (burst)", "flops_per_sequence": flops}
 
 
 def cpu_baseline(args, n=None):

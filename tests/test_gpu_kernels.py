@@ -126,16 +126,20 @@ def test_rmsnorm_fwd_bwd(dtype, H):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_rope_matches_reference_rotation(dtype):
+@pytest.mark.parametrize("max_pos", [256, 12000])
+def test_rope_matches_reference_rotation(dtype, max_pos):
+    # fp32 tolerance grows with the position: the angle pos * inv_freq is an fp32
+    # product (as in the reference), so one ulp of inv_freq between two libms moves
+    # it by ~pos * 6e-8 rad.
     S, heads, hd = 50, 6, 64
     x = _rand(S, heads * hd + 16, dtype=dtype, seed=9)  # extra columns stay untouched
-    pos = torch.randint(0, 3000, (S,), generator=torch.Generator().manual_seed(1)).to(DEV)
+    pos = torch.randint(0, max_pos, (S,), generator=torch.Generator().manual_seed(1)).to(DEV)
     y = x.clone()
     ops.rope_(y, heads, hd, pos, 10000.0)
     cos, sin = oracle.rope_tables(pos.cpu(), hd, 10000.0)
     xh = x[:, : heads * hd].cpu().view(S, heads, hd).transpose(0, 1)
     ref = oracle.drafter_step._rotate(xh, cos, sin).transpose(0, 1).reshape(S, heads * hd)
-    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    tol = (2e-5 if max_pos <= 256 else 3e-4) if dtype == torch.float32 else 1e-2
     assert rel(y[:, : heads * hd].float().cpu(), ref.float()) < tol
     assert torch.equal(y[:, heads * hd:], x[:, heads * hd:])
     ops.rope_(y, heads, hd, pos, 10000.0, inverse=True)
