@@ -112,7 +112,7 @@ int pe_attn_fwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
 /* dq/dk/dv are overwritten.  `workspace` holds per-row softmax deltas and, on
  * the tensor-core path, an fp32 dQ accumulator; its size comes from
  * pe_attn_bwd_workspace (same shape arguments). */
-size_t pe_attn_bwd_workspace(int dtype, int64_t B, int64_t S, int Hq, int head_dim);
+size_t pe_attn_bwd_workspace(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim);
 int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
                 const void* q, int64_t q_sb, int64_t q_ss, const void* k, int64_t k_sb,
                 int64_t k_ss, const void* v, int64_t v_sb, int64_t v_ss, const void* o,

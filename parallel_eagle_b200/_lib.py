@@ -43,7 +43,7 @@ SIGNATURES: dict[str, tuple] = {
         [_int, _i64, _i64, _int, _int, _int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64,
          _vp, _i64, _i64, _vp, _int, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _int, _vp, _vp],
     ),
-    "pe_attn_bwd_workspace": (_sz, [_int, _i64, _i64, _int, _int]),
+    "pe_attn_bwd_workspace": (_sz, [_int, _i64, _i64, _int, _int, _int]),
     "pe_attn_bwd": (
         _int,
         [_int, _i64, _i64, _int, _int, _int, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64,

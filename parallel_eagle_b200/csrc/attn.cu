@@ -75,7 +75,7 @@ extern "C" int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int
   const bool tc = attn_tc_bwd_ready() &&
                   attn_tc_eligible(dtype, B, S, Hq, Hkv, head_dim, layout, q, q_ss, k, k_ss, v,
                                    v_ss) &&
-                  workspace_bytes >= delta_bytes + (size_t)S * Hq * head_dim * 4;
+                  workspace_bytes >= delta_bytes + attn_tc_bwd_acc_bytes(S, Hq, Hkv);
   if (algo == PE_ALGO_TCGEN05) PE_CHECK_ARG(tc, "attention: inputs not eligible for tcgen05");
   if (tc && algo != PE_ALGO_SIMT) {
     float* dq_acc = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + delta_bytes);
@@ -89,9 +89,11 @@ extern "C" int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int
                               as_stream(stream));
 }
 
-extern "C" size_t pe_attn_bwd_workspace(int dtype, int64_t B, int64_t S, int Hq, int head_dim) {
-  if (B <= 0 || S <= 0 || Hq <= 0 || head_dim <= 0) return 0;
+extern "C" size_t pe_attn_bwd_workspace(int dtype, int64_t B, int64_t S, int Hq, int Hkv,
+                                        int head_dim) {
+  if (B <= 0 || S <= 0 || Hq <= 0 || Hkv <= 0 || head_dim <= 0) return 0;
   size_t bytes = align256((size_t)B * Hq * S * 4);
-  if (dtype == PE_BF16 && B == 1) bytes += align256((size_t)S * Hq * head_dim * 4);
+  if (dtype == PE_BF16 && B == 1 && head_dim == 128)
+    bytes += align256(attn_tc_bwd_acc_bytes(S, Hq, Hkv));
   return bytes;
 }

@@ -57,6 +57,8 @@ bool attn_tc_eligible(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd, 
                       const void* q, int64_t q_ss, const void* k, int64_t k_ss, const void* v,
                       int64_t v_ss);
 bool attn_tc_bwd_ready();
+// fp32 dQ / dK / dV accumulators of the tensor-core backward
+size_t attn_tc_bwd_acc_bytes(int64_t S, int Hq, int Hkv);
 int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
                        int64_t k_ss, const void* v, int64_t v_ss, void* o, int64_t o_ss,
                        float* lse, const MaskSpec& m, int* status, cudaStream_t st);

@@ -3,19 +3,20 @@
 // (the backward of reference src/pe/nn.py:84-88 under the mask of
 // src/pe/masks.py:43-61).
 //
-// One CTA = one 128-slot key tile of one KV head.  It loops over the query heads
-// of its GQA group and, per head, over the query tiles whose rows can see any
-// key of the tile (the rule's key-side view: a real key j is read by the real
-// rows j.. and every prediction row of anchors >= j; a prediction key (i, e) only
-// by the rows (i, d >= e)).  Per (head, query tile), with the key on TMEM lanes:
+// One CTA = one 128-slot key tile x one query head.  It loops over the query
+// tiles whose rows can see any key of the tile (the rule's key-side view: a real
+// key j is read by the real rows j.. and every prediction row of anchors >= j;
+// a prediction key (i, e) only by the rows (i, d >= e)).  Per query tile, with
+// the key on TMEM lanes:
 //   S^T  = K Q^T          dP^T = V dO^T               (tcgen05, TMEM)
 //   P^T  = exp(scale S^T - lse)   dS^T = P^T (dP^T - delta)   (softmax warps,
-//          bf16 to shared memory; masked pairs are exactly zero)
+//          bf16 to shared memory; masked pairs are exactly zero; tiles the rule
+//          fully allows skip the per-pair test)
 //   dV  += P^T dO         dK  += dS^T Q               (TMEM accumulators)
 //   dQ_part = dS K        -> fp32 vector atomics into a dQ accumulator
-// dK and dV never leave TMEM until the CTA is done; the accumulated dQ is
-// scaled and cast by a final pass.  GQA needs no K/V expansion: the group's
-// heads reuse the K/V tile held in shared memory.
+// At the end the head's dK/dV tile is added (fp32 atomics) into the KV head's
+// accumulator, so the 7 query heads of a GQA group reduce without any K/V
+// expansion; a final pass scales and casts dQ, dK, dV to bf16.
 //
 // TMEM columns: dK 0..127, dV 128..255, S^T (then dQ_part) 256..383, dP^T 384..511.
 #include "attn_tc.cuh"
@@ -53,12 +54,10 @@ __device__ __forceinline__ Ranges query_tiles(const PartGeom& g, int k0) {
   const int nqt = (g.S + TQ - 1) / TQ;
   int b[3], e[3], n = 0;
   if (k0 < g.a1) {
-    // real queries [k0, a1)
-    b[n] = k0 / TQ;
+    b[n] = k0 / TQ;  // real rows [k0, a1)
     e[n] = (g.a1 - 1) / TQ + 1;
     ++n;
-    // prediction rows of anchors >= max(a0, k0)
-    const int af = max(g.a0, k0);
+    const int af = max(g.a0, k0);  // prediction rows of anchors >= max(a0, k0)
     if (g.km1 > 0 && af < g.a1) {
       b[n] = (g.a1 + (af - g.a0) * g.km1) / TQ;
       e[n] = nqt;
@@ -73,7 +72,6 @@ __device__ __forceinline__ Ranges query_tiles(const PartGeom& g, int k0) {
     e[n] = (g.a1 + (i_l - g.a0 + 1) * g.km1 - 1) / TQ + 1;
     ++n;
   }
-  // sort by start (n <= 3) and merge overlapping / adjacent ranges
   for (int i = 1; i < n; ++i)
     for (int j = i; j > 0 && b[j] < b[j - 1]; --j) {
       int t = b[j]; b[j] = b[j - 1]; b[j - 1] = t;
@@ -93,17 +91,40 @@ __device__ __forceinline__ Ranges query_tiles(const PartGeom& g, int k0) {
   return R;
 }
 
+// true when every (query in [q0, q0+TQ), key in [k0, k0+TK)) pair is allowed:
+// all keys real and no query row's anchor below the last key
+__device__ __forceinline__ bool tile_fully_allowed(const PartGeom& g, int q0, int k0) {
+  const int k_last = k0 + TK - 1;
+  if (k_last >= g.a1 || q0 + TQ > g.S) return false;
+  int min_anchor = 1 << 30;
+  if (q0 < g.a1) min_anchor = q0;
+  if (q0 + TQ > g.a1) {
+    int i, d;
+    decode(g, max(q0, g.a1), i, d);
+    min_anchor = min(min_anchor, i);
+  }
+  return min_anchor >= k_last;
+}
+
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ void atomic_add_row32(float* dst, const float* v, float mul) {
+  float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int t = 0; t < 8; ++t)
+    atomicAdd(d4 + t, make_float4(v[4 * t] * mul, v[4 * t + 1] * mul, v[4 * t + 2] * mul,
+                                  v[4 * t + 3] * mul));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                    const float* __restrict__ lse, const float* __restrict__ delta,
-                   float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dk, int64_t dk_ss,
-                   __nv_bfloat16* __restrict__ dv, int64_t dv_ss, PartGeom g, int Hq, int rep,
-                   float scale, int* status) {
+                   float* __restrict__ dq_acc, float* __restrict__ dk_acc,
+                   float* __restrict__ dv_acc, PartGeom g, int Hq, int Hkv, int rep, float scale,
+                   int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -129,11 +150,11 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x;  // low key tiles are read by the most query tiles: first
-  const int kvh = blockIdx.y;
+  const int h = blockIdx.y;
+  const int kvh = h / rep;
   const int k0 = kt * TK;
   const Ranges qr = query_tiles(g, k0);
-  const int nq = qr.count();
-  const int n_it = nq * rep;  // iteration it -> head kvh*rep + it / nq, query tile qr.at(it % nq)
+  const int n_it = qr.count();
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -167,8 +188,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       tma_load_2d(sV + CHUNK, &tmV, kv_full, kvh * HD + 64, k0);
       for (int it = 0; it < n_it && ok; ++it) {
         if (!mbar_wait(qdo_empty, (it & 1) ^ 1u, status, 301)) { ok = false; break; }
-        const int h = kvh * rep + it / nq;
-        const int q0 = qr.at(it % nq) * TQ;
+        const int q0 = qr.at(it) * TQ;
         mbar_arrive_expect_tx(qdo_full, 2 * TILE_BYTES);
         tma_load_2d(sQ, &tmQ, qdo_full, h * HD, q0);
         tma_load_2d(sQ + CHUNK, &tmQ, qdo_full, h * HD + 64, q0);
@@ -230,7 +250,6 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     // ---------------- softmax / epilogue warps (128 threads) ----------------
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane: key row (S^T, dP^T, dK, dV) / query row (dQ)
-    const int tid = row;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int kj = k0 + row;
     const bool kvalid = kj < g.S;
@@ -240,12 +259,12 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const int64_t dq_ld = (int64_t)Hq * HD;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
-      const int h = kvh * rep + it / nq;
-      const int q0 = qr.at(it % nq) * TQ;
+      const int q0 = qr.at(it) * TQ;
       const int buf = it & 1;
+      const bool full = tile_fully_allowed(g, q0, k0);
       {
         // per-query operands of this tile, one per thread
-        const int q = q0 + tid;
+        const int q = q0 + row;
         float lv = INFINITY, dl = 0.f;
         int qa = -1, qd = 0;
         if (q < g.S) {
@@ -253,10 +272,10 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
           dl = delta[(int64_t)h * g.S + q];
           decode(g, q, qa, qd);
         }
-        sL[buf * TQ + tid] = lv;
-        sD[buf * TQ + tid] = dl;
-        sA[buf * TQ + tid] = qa;
-        sDp[buf * TQ + tid] = qd;
+        sL[buf * TQ + row] = lv;
+        sD[buf * TQ + row] = dl;
+        sA[buf * TQ + row] = qa;
+        sDp[buf * TQ + row] = qd;
       }
       named_sync(1, 128);
       if (!mbar_wait(s_full, it & 1, status, 306)) { ok = false; break; }
@@ -272,21 +291,31 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         tmem_ld32(tDP + lane_off + c0, dpv);
         tmem_wait_ld();
         uint32_t pw[16], dw[16];
+        if (full) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float pp[2], dd[2];
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int qc = c0 + c + t;
-            const int qa = QA[qc];
-            const bool allow = kvalid && qa >= 0 &&
-                               (ke == 0 ? (ka <= qa) : (ka == qa && ke <= QD[qc]));
-            const float p = allow ? exp2f(sv[c + t] * scale_log2 - L2[qc]) : 0.f;
-            pp[t] = p;
-            dd[t] = p * (dpv[c + t] - DL[qc]);
+          for (int c = 0; c < 32; c += 2) {
+            const float p0 = exp2f(sv[c] * scale_log2 - L2[c0 + c]);
+            const float p1 = exp2f(sv[c + 1] * scale_log2 - L2[c0 + c + 1]);
+            pw[c / 2] = pack_bf16x2(p0, p1);
+            dw[c / 2] = pack_bf16x2(p0 * (dpv[c] - DL[c0 + c]), p1 * (dpv[c + 1] - DL[c0 + c + 1]));
           }
-          pw[c / 2] = pack_bf16x2(pp[0], pp[1]);
-          dw[c / 2] = pack_bf16x2(dd[0], dd[1]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float pp[2], dd[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int qc = c0 + c + t;
+              const int qa = QA[qc];
+              const bool allow = kvalid && qa >= 0 &&
+                                 (ke == 0 ? (ka <= qa) : (ka == qa && ke <= QD[qc]));
+              const float p = allow ? exp2f(sv[c + t] * scale_log2 - L2[qc]) : 0.f;
+              pp[t] = p;
+              dd[t] = p * (dpv[c + t] - DL[qc]);
+            }
+            pw[c / 2] = pack_bf16x2(pp[0], pp[1]);
+            dw[c / 2] = pack_bf16x2(dd[0], dd[1]);
+          }
         }
         const int ch = c0 >> 6;
         const int u0 = (c0 & 63) >> 3;
@@ -312,45 +341,24 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         float v[32];
         tmem_ld32(tS + lane_off + c0, v);
         tmem_wait_ld();
-        if (q < g.S) {
-          float4* dst = reinterpret_cast<float4*>(dq_acc + (int64_t)q * dq_ld + h * HD + c0);
-#pragma unroll
-          for (int t = 0; t < 8; ++t)
-            atomicAdd(dst + t, make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]));
-        }
+        if (q < g.S) atomic_add_row32(dq_acc + (int64_t)q * dq_ld + h * HD + c0, v, 1.f);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_read);
     }
-    // dK, dV (key row per TMEM lane) -> bf16
-    if (ok) {
+    // this head's dK, dV tile (key row per TMEM lane) -> the KV head's fp32 accumulators
+    if (ok && n_it > 0) {
+      const int64_t kv_ld = (int64_t)Hkv * HD;
 #pragma unroll 1
-      for (int part = 0; part < 2; ++part) {
-        const uint32_t tsrc = part == 0 ? tDK : tDV;
-        const float mul = part == 0 ? scale : 1.f;
-        __nv_bfloat16* dst = part == 0 ? dk + (int64_t)kj * dk_ss + kvh * HD
-                                       : dv + (int64_t)kj * dv_ss + kvh * HD;
-#pragma unroll 1
-        for (int c0 = 0; c0 < HD; c0 += 32) {
-          float v[32];
-          if (n_it > 0) {
-            tmem_ld32(tsrc + lane_off + c0, v);
-            tmem_wait_ld();
-          } else {
-#pragma unroll
-            for (int t = 0; t < 32; ++t) v[t] = 0.f;
-          }
-          if (kvalid) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c0);
-#pragma unroll
-            for (int t = 0; t < 4; ++t)
-              d4[t] = make_uint4(pack_bf16x2(v[8 * t] * mul, v[8 * t + 1] * mul),
-                                 pack_bf16x2(v[8 * t + 2] * mul, v[8 * t + 3] * mul),
-                                 pack_bf16x2(v[8 * t + 4] * mul, v[8 * t + 5] * mul),
-                                 pack_bf16x2(v[8 * t + 6] * mul, v[8 * t + 7] * mul));
-          }
-        }
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        float v[32];
+        tmem_ld32(tDK + lane_off + c0, v);
+        tmem_wait_ld();
+        if (kvalid) atomic_add_row32(dk_acc + (int64_t)kj * kv_ld + kvh * HD + c0, v, 1.f);
+        tmem_ld32(tDV + lane_off + c0, v);
+        tmem_wait_ld();
+        if (kvalid) atomic_add_row32(dv_acc + (int64_t)kj * kv_ld + kvh * HD + c0, v, 1.f);
       }
     }
   }
@@ -363,16 +371,17 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
 }
 
-// delta[h, s] = sum_d dO * O (fp32) and zero the dQ accumulator row
-__global__ void attn_bwd_prep_kernel(int S, int Hq, const __nv_bfloat16* __restrict__ o,
+// delta[h, s] = sum_d dO * O (fp32); zero the dQ accumulator row and, for the
+// first Hkv heads, the dK / dV accumulator rows
+__global__ void attn_bwd_prep_kernel(int S, int Hq, int Hkv, const __nv_bfloat16* __restrict__ o,
                                      int64_t o_ss, const __nv_bfloat16* __restrict__ dout,
                                      int64_t do_ss, float* __restrict__ delta,
-                                     float* __restrict__ dq_acc) {
+                                     float* __restrict__ dq_acc, float* __restrict__ dk_acc,
+                                     float* __restrict__ dv_acc) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= S * Hq) return;
   const int s = w / Hq, h = w - (w / Hq) * Hq;
-  // 128 dims: 4 per lane (8 bytes)
   const uint2 a = *reinterpret_cast<const uint2*>(o + (int64_t)s * o_ss + h * HD + lane * 4);
   const uint2 b = *reinterpret_cast<const uint2*>(dout + (int64_t)s * do_ss + h * HD + lane * 4);
   const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
@@ -385,35 +394,54 @@ __global__ void attn_bwd_prep_kernel(int S, int Hq, const __nv_bfloat16* __restr
   }
   acc = warp_sum(acc);
   if (lane == 0) delta[(int64_t)h * S + s] = acc;
-  reinterpret_cast<float4*>(dq_acc + (int64_t)s * Hq * HD + h * HD)[lane] =
-      make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  reinterpret_cast<float4*>(dq_acc + (int64_t)s * Hq * HD + h * HD)[lane] = z;
+  if (h < Hkv) {
+    reinterpret_cast<float4*>(dk_acc + (int64_t)s * Hkv * HD + h * HD)[lane] = z;
+    reinterpret_cast<float4*>(dv_acc + (int64_t)s * Hkv * HD + h * HD)[lane] = z;
+  }
 }
 
-// dq (bf16, row stride dq_ss) = scale * dq_acc
-__global__ void attn_dq_cast_kernel(int S, int Hq, const float* __restrict__ dq_acc, float scale,
-                                    __nv_bfloat16* __restrict__ dq, int64_t dq_ss) {
-  const int64_t total = (int64_t)S * Hq * HD / 8;
+// out (bf16, row stride ld) = mul * acc ([S, cols] fp32, contiguous)
+__global__ void attn_cast_kernel(int S, int cols, const float* __restrict__ acc, float mul,
+                                 __nv_bfloat16* __restrict__ out, int64_t ld) {
+  const int64_t total = (int64_t)S * cols / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i * 8;
-    const int64_t s = e / (Hq * HD), c = e - s * (Hq * HD);
-    const float4 x = reinterpret_cast<const float4*>(dq_acc + e)[0];
-    const float4 y = reinterpret_cast<const float4*>(dq_acc + e)[1];
-    *reinterpret_cast<uint4*>(dq + s * dq_ss + c) =
-        make_uint4(pack_bf16x2(x.x * scale, x.y * scale), pack_bf16x2(x.z * scale, x.w * scale),
-                   pack_bf16x2(y.x * scale, y.y * scale), pack_bf16x2(y.z * scale, y.w * scale));
+    const int64_t s = e / cols, c = e - s * cols;
+    const float4 x = reinterpret_cast<const float4*>(acc + e)[0];
+    const float4 y = reinterpret_cast<const float4*>(acc + e)[1];
+    *reinterpret_cast<uint4*>(out + s * ld + c) =
+        make_uint4(pack_bf16x2(x.x * mul, x.y * mul), pack_bf16x2(x.z * mul, x.w * mul),
+                   pack_bf16x2(y.x * mul, y.y * mul), pack_bf16x2(y.z * mul, y.w * mul));
   }
+}
+
+int launch_cast(int S, int cols, const float* acc, float mul, void* out, int64_t ld,
+                cudaStream_t st) {
+  const int64_t total = (int64_t)S * cols / 8;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
+  attn_cast_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, st>>>(
+      S, cols, acc, mul, (__nv_bfloat16*)out, ld);
+  PE_LAUNCHED();
+  return PE_OK;
 }
 
 }  // namespace
 
 bool attn_tc_bwd_ready() { return true; }
 
+size_t attn_tc_bwd_acc_bytes(int64_t S, int Hq, int Hkv) {
+  return (size_t)S * (Hq + 2 * Hkv) * HD * 4;
+}
+
 int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
                        int64_t k_ss, const void* v, int64_t v_ss, const void* o, int64_t o_ss,
                        const void* dout, int64_t do_ss, const float* lse, void* dq,
                        int64_t dq_ss, void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
-                       float* delta, float* dq_acc, const MaskSpec& m, int* status,
+                       float* delta, float* acc, const MaskSpec& m, int* status,
                        cudaStream_t st) {
   PE_CHECK_ARG(o_ss % 8 == 0 && do_ss % 8 == 0 && dq_ss % 8 == 0 && dk_ss % 8 == 0 &&
                    dv_ss % 8 == 0 && al16(o) && al16(dout) && al16(dq) && al16(dk) && al16(dv),
@@ -426,30 +454,28 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
     rc = make_tmap_2d(&tdo, dout, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)do_ss * 2, 64, TQ);
   if (rc) return rc;
   const int Si = (int)S;
+  float* dq_acc = acc;
+  float* dk_acc = dq_acc + (int64_t)S * Hq * HD;
+  float* dv_acc = dk_acc + (int64_t)S * Hkv * HD;
   {
     const int warps = Si * Hq;
     attn_bwd_prep_kernel<<<(warps + 7) / 8, 256, 0, st>>>(
-        Si, Hq, (const __nv_bfloat16*)o, o_ss, (const __nv_bfloat16*)dout, do_ss, delta, dq_acc);
+        Si, Hq, Hkv, (const __nv_bfloat16*)o, o_ss, (const __nv_bfloat16*)dout, do_ss, delta,
+        dq_acc, dk_acc, dv_acc);
     PE_LAUNCHED();
   }
   PartGeom g{Si, (int)m.a0, (int)m.a1, m.kd - 1};
   const float scale = 1.0f / sqrtf((float)HD);
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)SMEM_BWD));
-  dim3 grid((unsigned)((S + TK - 1) / TK), (unsigned)Hkv);
-  attn_bwd_tc_kernel<<<grid, kThreads, SMEM_BWD, st>>>(
-      tq, tk, tv, tdo, lse, delta, dq_acc, (__nv_bfloat16*)dk, dk_ss, (__nv_bfloat16*)dv, dv_ss,
-      g, Hq, Hq / Hkv, scale, status);
+  dim3 grid((unsigned)((S + TK - 1) / TK), (unsigned)Hq);
+  attn_bwd_tc_kernel<<<grid, kThreads, SMEM_BWD, st>>>(tq, tk, tv, tdo, lse, delta, dq_acc, dk_acc,
+                                                       dv_acc, g, Hq, Hkv, Hq / Hkv, scale, status);
   PE_LAUNCHED();
-  {
-    const int64_t total = S * Hq * HD / 8;
-    int64_t blocks = (total + 255) / 256;
-    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
-    attn_dq_cast_kernel<<<(unsigned)blocks, 256, 0, st>>>(Si, Hq, dq_acc, scale,
-                                                           (__nv_bfloat16*)dq, dq_ss);
-    PE_LAUNCHED();
-  }
-  return PE_OK;
+  rc = launch_cast(Si, Hq * HD, dq_acc, scale, dq, dq_ss, st);
+  if (!rc) rc = launch_cast(Si, Hkv * HD, dk_acc, scale, dk, dk_ss, st);
+  if (!rc) rc = launch_cast(Si, Hkv * HD, dv_acc, 1.f, dv, dv_ss, st);
+  return rc;
 }
 
 }  // namespace pe

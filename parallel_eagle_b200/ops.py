@@ -220,7 +220,8 @@ def attn_bwd(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, layout: AttnLay
     if dv is None:
         dv = torch.empty(B, S, n_kv_heads * head_dim, dtype=v.dtype, device=v.device)
     lib = _lib()
-    nbytes = int(lib.pe_attn_bwd_workspace(L.dtype_code(q.dtype), B, S, n_heads, head_dim))
+    nbytes = int(lib.pe_attn_bwd_workspace(L.dtype_code(q.dtype), B, S, n_heads, n_kv_heads,
+                                           head_dim))
     ws = _workspace(q.device, nbytes, "attn_bwd")
     bsb, bsq = layout.bias_strides()
     rc = lib.pe_attn_bwd(
