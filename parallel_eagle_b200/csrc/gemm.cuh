@@ -20,6 +20,19 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
             const void* Cin, int64_t ldcin, float alpha, float beta, int* status,
             cudaStream_t stream);
 
+// Logits GEMM for the fused LM-head loss: C (bf16, [M, N]) = A[M, K] B[N, K]^T with
+// both operands K-major, and per (row, 256-column tile) the pair (max, sum exp(c - max))
+// of the stored (rounded) values in stats[row * stats_ld + tile].
+int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                         const void* B, int64_t ldb, void* C, int64_t ldc, float2* stats,
+                         int stats_ld, int* status, cudaStream_t stream);
+
+// C (fp32) = A[M, K] B + rowscale[row] * Cin, A K-major, B (n, k) at B[n + k * b_sk]
+// (MN-major): the online-softmax rescaled accumulation of the LM-head input gradient.
+int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                         const void* B, int64_t b_sk, float* C, int64_t ldc, const float* Cin,
+                         const float* rowscale, int* status, cudaStream_t stream);
+
 // pe_gemm without the C wrapper (used inside the library)
 int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
          const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,

@@ -24,6 +24,18 @@ using namespace sm100;
 constexpr int BM = 128, BK = 64;
 constexpr int kThreads = 192;
 
+// epilogue variants
+enum : int {
+  EPI_STORE = 0,     // C = alpha * acc + beta * Cin
+  EPI_STATS = 1,     // C = round(alpha * acc); stats[row, n_tile] = (max, sum exp(c - max))
+  EPI_ROWSCALE = 2,  // C = alpha * acc + rowscale[row] * Cin
+};
+struct EpiArgs {
+  float2* stats;
+  int stats_ld;
+  const float* rowscale;
+};
+
 template <int BN>
 struct TcCfg {
   static constexpr int STAGES = BN == 256 ? 4 : 6;
@@ -103,11 +115,11 @@ __device__ __forceinline__ void store_row32(OutT* dst, const OutT* cin, const fl
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, typename OutT>
+template <int BN, bool A_MN, bool B_MN, typename OutT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                int M, int N, int K, OutT* C, int64_t ldc, const OutT* Cin, int64_t ldcin,
-               float alpha, float beta, int vec_ok, int* status) {
+               float alpha, float beta, int vec_ok, EpiArgs ea, int* status) {
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
@@ -237,6 +249,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!mbar_wait(&acc_full[acc], acc_phase, status, 104)) break;
       tc_fence_after();
       const int64_t gm = (int64_t)tm * BM + row_in_tile;
+      // EPI_ROWSCALE: the accumulated input is scaled per row (online-softmax correction)
+      const float beta_row = (EPI == EPI_ROWSCALE && gm < M) ? ea.rowscale[gm] : beta;
+      float m_run = -INFINITY, s_run = 0.f;  // EPI_STATS: running row max / sum-exp
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
@@ -245,9 +260,31 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int64_t gn0 = (int64_t)tn * BN + c0;
         if (gm < M && gn0 < N) {
           const int valid = (N - gn0) < 32 ? (int)(N - gn0) : 32;
-          store_row32<OutT>(C + gm * ldc + gn0, Cin ? Cin + gm * ldcin + gn0 : nullptr, v, alpha,
-                            beta, valid, vec_ok != 0);
+          if constexpr (EPI == EPI_STATS) {
+            // stats of the values as stored (rounded to the output type)
+            float cm = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              v[i] = round_to<OutT>(alpha * v[i]);
+              if (i < valid) cm = fmaxf(cm, v[i]);
+            }
+            const float mn = fmaxf(m_run, cm);
+            float cs = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < valid) cs += __expf(v[i] - mn);
+            s_run = s_run * __expf(m_run - mn) + cs;
+            m_run = mn;
+            store_row32<OutT>(C + gm * ldc + gn0, nullptr, v, 1.f, 0.f, valid, vec_ok != 0);
+          } else {
+            store_row32<OutT>(C + gm * ldc + gn0, Cin ? Cin + gm * ldcin + gn0 : nullptr, v,
+                              alpha, beta_row, valid, vec_ok != 0);
+          }
         }
+      }
+      if constexpr (EPI == EPI_STATS) {
+        if (gm < M && (int64_t)tn * BN < N)
+          ea.stats[gm * ea.stats_ld + tn] = make_float2(m_run, s_run);
       }
       tc_fence_before();
       __syncwarp();
@@ -265,17 +302,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <int BN, bool A_MN, bool B_MN, typename OutT>
+template <int BN, bool A_MN, bool B_MN, typename OutT, int EPI = EPI_STORE>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, void* C, int64_t ldc,
            const void* Cin, int64_t ldcin, float alpha, float beta, int vec_ok, int* status,
-           cudaStream_t stream) {
+           cudaStream_t stream, EpiArgs ea = EpiArgs{}) {
   using Cfg = TcCfg<BN>;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, OutT>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, OutT, EPI>;
   PE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ta, tb, M, N, K, (OutT*)C, ldc, (const OutT*)Cin,
-                                              ldcin, alpha, beta, vec_ok, status);
+                                              ldcin, alpha, beta, vec_ok, ea, status);
   PE_LAUNCHED();
   return PE_OK;
 }
@@ -351,6 +388,38 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
   if (BN == 256)
     return launch_majors<256, __nv_bfloat16>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
   return launch_majors<128, __nv_bfloat16>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
+}
+
+int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                         const void* B, int64_t ldb, void* C, int64_t ldc, float2* stats,
+                         int stats_ld, int* status, cudaStream_t stream) {
+  PE_CHECK_ARG(M > 0 && N > 0 && K > 0 && lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 &&
+                   al16(A) && al16(B) && al16(C),
+               "gemm (logits + row stats): operands must be 16-byte aligned bf16");
+  PE_CHECK_ARG(stats_ld >= (N + 255) / 256, "gemm (logits + row stats): stats_ld too small");
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
+  if (!rc) rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, 64, 256);
+  if (rc) return rc;
+  EpiArgs ea{stats, stats_ld, nullptr};
+  return launch<256, false, false, __nv_bfloat16, EPI_STATS>(ta, tb, (int)M, (int)N, (int)K, C, ldc,
+                                                             nullptr, 0, 1.f, 0.f, 1, status,
+                                                             stream, ea);
+}
+
+int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                         const void* B, int64_t b_sk, float* C, int64_t ldc, const float* Cin,
+                         const float* rowscale, int* status, cudaStream_t stream) {
+  PE_CHECK_ARG(M > 0 && N > 0 && K > 0 && lda % 8 == 0 && b_sk % 8 == 0 && ldc % 4 == 0 &&
+                   al16(A) && al16(B) && al16(C),
+               "gemm (row-scaled accumulate): operands must be 16-byte aligned");
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
+  if (!rc) rc = make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)b_sk * 2, 64, 64);
+  if (rc) return rc;
+  EpiArgs ea{nullptr, 0, rowscale};
+  return launch<256, false, true, float, EPI_ROWSCALE>(ta, tb, (int)M, (int)N, (int)K, C, ldc, Cin,
+                                                       ldc, 1.f, 0.f, 1, status, stream, ea);
 }
 
 int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,

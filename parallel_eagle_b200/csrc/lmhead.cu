@@ -204,11 +204,186 @@ unsigned grid_for(int64_t n) {
 }  // namespace
 }  // namespace pe
 
+// ------------------------------------------------------------------------ //
+// Fused path (bf16, hard labels): one logits GEMM per vocabulary chunk, no
+// recompute.  Per chunk c:
+//   Zc = h W_c^T (bf16) with per-(row, 256-col tile) (max, sum-exp) from the
+//        GEMM epilogue;
+//   combine: running (m, l) per row, alpha = exp(m_old - m_new), the label logit,
+//        and Zc <- exp(Zc - m_new) in place;
+//   dH = Zc W_c + alpha * dH  (fp32, row-scaled accumulate in the GEMM epilogue).
+// At the end dh = scale * (dH / l - W[label]): the softmax-minus-one-hot product
+// without ever forming the normalised probabilities for the whole vocabulary.
+// ------------------------------------------------------------------------ //
+namespace pe {
+namespace {
+
+constexpr int64_t kFastChunk = 16384;
+constexpr int kStatTile = 256;
+
+struct FastLayout {
+  size_t m, l, zlab, lse, alpha, stats, Z, dH, total;
+};
+
+FastLayout fast_layout_of(int64_t R, int64_t H, int64_t V) {
+  const int64_t vc = V < kFastChunk ? (V + 7) / 8 * 8 : kFastChunk;
+  const int64_t nt = (vc + kStatTile - 1) / kStatTile;
+  FastLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += align256(bytes);
+    return o;
+  };
+  L.m = take(4 * R);
+  L.l = take(4 * R);
+  L.zlab = take(4 * R);
+  L.lse = take(4 * R);
+  L.alpha = take(4 * R);
+  L.stats = take(8 * (size_t)R * nt);
+  L.Z = take(2 * (size_t)R * vc);
+  L.dH = take(4 * (size_t)R * H);
+  L.total = off;
+  return L;
+}
+
+// per row: fold this chunk's tile stats into (m, l), record the rescale factor,
+// pick the label logit, and overwrite the chunk's logits with exp(z - m_new)
+__global__ void __launch_bounds__(256)
+combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __restrict__ stats,
+               __nv_bfloat16* __restrict__ Z, int64_t ldz, const int64_t* __restrict__ labels,
+               float* m, float* l, float* zlab, float* alpha) {
+  __shared__ float s_mnew;
+  const int64_t r = blockIdx.x;
+  const int64_t lab = labels[r];
+  __nv_bfloat16* z = Z + r * ldz;
+  if (threadIdx.x == 0) {
+    const float2* st = stats + r * stats_ld;
+    const float m_old = m[r];
+    float mn = m_old;
+    for (int t = 0; t < nt; ++t) mn = fmaxf(mn, st[t].x);
+    float acc = m_old == -INFINITY ? 0.f : l[r] * expf(m_old - mn);
+    for (int t = 0; t < nt; ++t) acc += st[t].y * expf(st[t].x - mn);
+    l[r] = acc;
+    alpha[r] = m_old == -INFINITY ? 0.f : expf(m_old - mn);
+    m[r] = mn;
+    if (lab >= v0 && lab < v0 + vc) zlab[r] = __bfloat162float(z[lab - v0]);
+    s_mnew = mn;
+  }
+  __syncthreads();
+  const float mn = s_mnew;
+  const bool ignored = lab < 0;
+  for (int64_t c = (int64_t)threadIdx.x * 8; c < vc; c += 256 * 8) {
+    uint4 u = *reinterpret_cast<const uint4*>(z + c);
+    __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(h2[i]);
+      f.x = ignored ? 0.f : __expf(f.x - mn);
+      f.y = ignored ? 0.f : __expf(f.y - mn);
+      h2[i] = __floats2bfloat162_rn(f.x, f.y);
+    }
+    *reinterpret_cast<uint4*>(z + c) = u;
+  }
+}
+
+__global__ void fast_init_kernel(int64_t R, float* m, float* l, float* zlab) {
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < R;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+    zlab[r] = 0.f;
+  }
+}
+
+// dh = scale * (dH / l - W[label])
+__global__ void fast_dh_kernel(int64_t R, int64_t H, const float* __restrict__ dH,
+                               const float* __restrict__ l, const int64_t* __restrict__ labels,
+                               const __nv_bfloat16* __restrict__ W, float scale,
+                               __nv_bfloat16* __restrict__ dh, int64_t lddh) {
+  const int64_t total = R * H / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i * 8;
+    const int64_t r = e / H, c = e - r * H;
+    const int64_t lab = labels[r];
+    uint4 out = make_uint4(0, 0, 0, 0);
+    if (lab >= 0) {
+      const float inv = 1.f / l[r];
+      const float4 a = reinterpret_cast<const float4*>(dH + e)[0];
+      const float4 b = reinterpret_cast<const float4*>(dH + e)[1];
+      const uint4 wu = *reinterpret_cast<const uint4*>(W + lab * H + c);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wu);
+      const float2 w0 = __bfloat1622float2(w2[0]), w1 = __bfloat1622float2(w2[1]);
+      const float2 w2f = __bfloat1622float2(w2[2]), w3 = __bfloat1622float2(w2[3]);
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
+      o2[0] = __floats2bfloat162_rn(scale * (a.x * inv - w0.x), scale * (a.y * inv - w0.y));
+      o2[1] = __floats2bfloat162_rn(scale * (a.z * inv - w1.x), scale * (a.w * inv - w1.y));
+      o2[2] = __floats2bfloat162_rn(scale * (b.x * inv - w2f.x), scale * (b.y * inv - w2f.y));
+      o2[3] = __floats2bfloat162_rn(scale * (b.z * inv - w3.x), scale * (b.w * inv - w3.y));
+    }
+    *reinterpret_cast<uint4*>(dh + r * lddh + c) = out;
+  }
+}
+
+bool fast_eligible(int dtype, int64_t H, int64_t V, const void* h, int64_t ldh, const void* W,
+                   const void* teacher, void* dh, int64_t lddh, int algo) {
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return dtype == PE_BF16 && teacher == nullptr && algo != PE_ALGO_SIMT && H % 8 == 0 &&
+         V % 8 == 0 && ldh % 8 == 0 && lddh % 8 == 0 && a16(h) && a16(W) && a16(dh);
+}
+
+int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, const void* W,
+                const int64_t* labels, float grad_scale, void* dh, int64_t lddh, float* loss_sum,
+                uint8_t* ws, int* status, cudaStream_t st) {
+  const FastLayout L = fast_layout_of(R, H, V);
+  float* m = (float*)(ws + L.m);
+  float* l = (float*)(ws + L.l);
+  float* zlab = (float*)(ws + L.zlab);
+  float* lse = (float*)(ws + L.lse);
+  float* alpha = (float*)(ws + L.alpha);
+  float2* stats = (float2*)(ws + L.stats);
+  __nv_bfloat16* Z = (__nv_bfloat16*)(ws + L.Z);
+  float* dH = (float*)(ws + L.dH);
+  const int64_t VC = V < kFastChunk ? (V + 7) / 8 * 8 : kFastChunk;
+  const int nt_max = (int)((VC + kStatTile - 1) / kStatTile);
+  fast_init_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, zlab);
+  PE_LAUNCHED();
+  for (int64_t v0 = 0; v0 < V; v0 += VC) {
+    const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
+    const int nt = (int)((vc + kStatTile - 1) / kStatTile);
+    const __nv_bfloat16* Wc = (const __nv_bfloat16*)W + v0 * H;
+    int rc = gemm_tc_logits_stats(R, vc, H, h, ldh, Wc, H, Z, VC, stats, nt_max, status, st);
+    if (rc) return rc;
+    combine_kernel<<<(unsigned)R, 256, 0, st>>>(vc, v0, nt, nt_max, stats, Z, VC, labels, m, l,
+                                                zlab, alpha);
+    PE_LAUNCHED();
+    rc = gemm_tc_rowscale_acc(R, H, vc, Z, VC, Wc, H, dH, H, v0 > 0 ? dH : nullptr, alpha, status,
+                              st);
+    if (rc) return rc;
+  }
+  finalize_kernel<<<1, kThreads, 0, st>>>(R, labels, m, l, zlab, nullptr, nullptr, nullptr, lse,
+                                          nullptr, loss_sum);
+  PE_LAUNCHED();
+  fast_dh_kernel<<<grid_for(R * H / 8), 256, 0, st>>>(R, H, dH, l, labels, (const __nv_bfloat16*)W,
+                                                      grad_scale, (__nv_bfloat16*)dh, lddh);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
+}  // namespace
+}  // namespace pe
+
 using namespace pe;
 
 extern "C" size_t pe_lmhead_ce_workspace(int dtype, int64_t R, int64_t H, int64_t V, int soft) {
   if (R <= 0 || H <= 0 || V <= 0) return 0;
-  return layout_of(dtype, R, H, V, soft).total;
+  size_t bytes = layout_of(dtype, R, H, V, soft).total;
+  if (dtype == PE_BF16 && !soft) {
+    const size_t f = fast_layout_of(R, H, V).total;
+    if (f > bytes) bytes = f;
+  }
+  return bytes;
 }
 
 extern "C" int pe_lmhead_ce(int dtype, int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh,
@@ -221,10 +396,17 @@ extern "C" int pe_lmhead_ce(int dtype, int64_t R, int64_t H, int64_t V, const vo
   PE_CHECK_ARG(R <= (1ll << 31) - 1, "lmhead_ce: too many rows");
   if (R == 0) return PE_OK;
   const int soft = teacher != nullptr;
+  cudaStream_t st = as_stream(stream);
+  if (fast_eligible(dtype, H, V, h, ldh, W, teacher, dh, lddh, algo)) {
+    const size_t need = fast_layout_of(R, H, V).total;
+    PE_CHECK_ARG(workspace && workspace_bytes >= need, "lmhead_ce: workspace of %zu bytes needed",
+                 need);
+    return lmhead_fast(R, H, V, h, ldh, W, labels, grad_scale, dh, lddh, loss_sum,
+                       static_cast<uint8_t*>(workspace), status, st);
+  }
   const Layout L = layout_of(dtype, R, H, V, soft);
   PE_CHECK_ARG(workspace && workspace_bytes >= L.total,
                "lmhead_ce: workspace of %zu bytes needed", L.total);
-  cudaStream_t st = as_stream(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* m = (float*)(ws + L.m);
   float* l = (float*)(ws + L.l);

@@ -280,8 +280,28 @@ def test_lmhead_ce(dtype, soft, R, H, V):
     assert rel(dh.float().cpu(), hr.grad) < (1e-4 if dtype == torch.float32 else 2e-2)
 
 
-def test_lmhead_ignores_negative_labels():
-    R, H, V = 20, 64, 300
+def test_lmhead_ce_full_vocab_against_torch():
+    # the 7B-class head (vocab 152064) over a segment's worth of loss rows: the
+    # fused one-GEMM path against torch's dense logits -> cross-entropy -> backward
+    R, H, V = 1100, 3584, 152064
+    h = _rand(R, H, seed=40)
+    W = _rand(V, H, seed=41, scale=0.02)
+    labels = torch.randint(0, V, (R,), generator=torch.Generator().manual_seed(5)).to(DEV)
+    loss = torch.zeros(1, dtype=torch.float32, device=DEV)
+    scale = 1.0 / 3000
+    dh = ops.lmhead_ce(h, W, labels, scale, loss)
+    hr = h.detach().clone().requires_grad_(True)
+    z = (hr @ W.t()).float()
+    lr = torch.nn.functional.cross_entropy(z, labels, reduction="sum")
+    (lr * scale).backward()
+    torch.cuda.synchronize()
+    assert abs(loss.item() - lr.item()) / lr.item() < 1e-4
+    assert rel(dh.float(), hr.grad.float()) < 2e-2
+
+
+@pytest.mark.parametrize("V", [300, 304])
+def test_lmhead_ignores_negative_labels(V):
+    R, H = 20, 64
     h = _rand(R, H, seed=17)
     W = _rand(V, H, seed=18, scale=0.05)
     labels = torch.randint(0, V, (R,), generator=torch.Generator().manual_seed(3))
