@@ -66,6 +66,17 @@ int pe_rmsnorm_bwd(int dtype, int64_t rows, int64_t H, const void* dy, int64_t l
                    void* dx, int64_t lddx, const void* residual, int64_t ldres,
                    float* dw_partial, void* stream);
 int64_t pe_rmsnorm_bwd_blocks(int64_t rows);
+/* No counterpart in the reference.  For callers that cannot allocate device memory
+ * (a host that owns the whole device budget, or a hot path where cudaMalloc's device
+ * synchronisation is not allowed): the same dx as pe_rmsnorm_bwd plus
+ * dw = (accumulate ? dw : 0) + sum_rows dy * x * rstd, with the per-block partials
+ * kept in a 2 MiB array inside the library (H <= 8192; larger H is rejected with
+ * PE_ERR_ARG).  The first call on a device looks the array up -- make it before any
+ * stream capture.  Calls share the array: calls that overlap on the GPU race. */
+int pe_rmsnorm_bwd_noalloc(int dtype, int64_t rows, int64_t H, const void* dy, int64_t lddy,
+                           const void* x, int64_t ldx, const void* w, const float* rstd,
+                           void* dx, int64_t lddx, const void* residual, int64_t ldres,
+                           void* dw, int accumulate, void* stream);
 /* dw (dtype) = (accumulate ? dw : 0) + sum over nblk partial rows */
 int pe_colsum_f32(int dtype, int64_t nblk, int64_t H, const float* partial, void* dw,
                   int accumulate, void* stream);

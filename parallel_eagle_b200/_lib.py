@@ -31,6 +31,9 @@ SIGNATURES: dict[str, tuple] = {
         [_int, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp],
     ),
     "pe_rmsnorm_bwd_blocks": (_i64, [_i64]),
+    "pe_rmsnorm_bwd_noalloc": (
+        _int, [_int, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _int, _vp]
+    ),
     "pe_colsum_f32": (_int, [_int, _i64, _i64, _vp, _vp, _int, _vp]),
     "pe_rope": (_int, [_int, _i64, _int, _int, _vp, _i64, _vp, _f32, _int, _vp]),
     "pe_gemm": (
