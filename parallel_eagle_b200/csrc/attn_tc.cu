@@ -10,12 +10,14 @@
 // the real stream plus one or two tiles on the prediction-slot diagonal -- the
 // ~90% of the dense (S x S) score matrix the rule forbids is never computed.
 //
-// Warp roles (192 threads):
+// Warp roles (320 threads):
 //   warp 0      TMA: Q tile once, then K/V tiles into a 2-stage ring
 //   warp 1      tcgen05.mma issue: S_j = Q K_j^T into a double-buffered TMEM
 //               score tile, O += P_j V_j into the TMEM output tile
-//   warps 2..5  softmax: row per thread, scores from TMEM, online max/sum in
-//               fp32, P (bf16) to shared memory, rescale of O in TMEM
+//   warps 2..9  softmax: two warps per TMEM lane quarter, each owning 64 of the
+//               128 key columns (and 64 of the 128 output columns), so every
+//               scheduler has two independent softmax warps to hide latency;
+//               the pair exchanges its row maxima through shared memory
 // TMEM: O [128 x 128 fp32] in columns 0..127, S buffers in 128..383.
 #include "attn_tc.cuh"
 
@@ -25,9 +27,11 @@ namespace {
 using namespace sm100;
 using namespace attn_tc;
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 256;
 constexpr size_t SMEM_FWD = 1024 + TILE_BYTES /*Q*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ +
-                            TILE_BYTES /*P*/ + 256;
+                            TILE_BYTES /*P*/ + 2 * 2 * TQ * 4 /*row max exchange*/ +
+                            2 * TQ * 4 /*row sums*/ + 256;
 
 // Key tiles visited by query tile qt: [0, r_end) then [m_beg, m_end) (may be empty)
 struct TileList {
@@ -62,6 +66,10 @@ __device__ __forceinline__ TileList tiles_for(const PartGeom& g, int q0) {
   return L;
 }
 
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
@@ -71,9 +79,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + TILE_BYTES;                   // stage s: K at +s*2*TILE, V at +TILE
+  uint8_t* sKV = sQ + TILE_BYTES;  // stage s: K at +s*2*TILE, V at +TILE
   uint8_t* sP = sKV + 4 * TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE_BYTES);
+  float* sMax = reinterpret_cast<float*>(sP + TILE_BYTES);  // [tile parity][half][TQ]
+  float* sSum = sMax + 2 * 2 * TQ;                          // [half][TQ]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSum + 2 * TQ);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
@@ -98,9 +108,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+      mbar_init(&s_empty[i], 8);
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(pv_done, 1);
     fence_barrier_init();
     fence_proxy_async();
@@ -181,8 +191,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
     }
   } else {
-    // ---------------- softmax warps ----------------
+    // ---------------- softmax warps: row (TMEM lane) x half of the columns ----------------
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // warps 2..5 -> 0, 6..9 -> 1
+    const int cb = half * 64;          // key columns / output columns owned
     const int row = quarter * 32 + lane;
     const int s = q0 + row;
     const bool valid = s < g.S;
@@ -197,29 +209,34 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const int st = j & 1;
       if (!mbar_wait(&s_full[st], (j >> 1) & 1, status, 206)) { ok = false; break; }
       tc_fence_after();
-      float sc[TK];
-#pragma unroll
-      for (int c = 0; c < TK; c += 32) tmem_ld32(tS0 + st * 128 + lane_off + c, sc + c);
+      float sc[64];
+      tmem_ld32(tS0 + st * 128 + lane_off + cb, sc);
+      tmem_ld32(tS0 + st * 128 + lane_off + cb + 32, sc + 32);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[st]);
-      const int k0 = tl.tile(j) * TK;
+      const int k0 = tl.tile(j) * TK + cb;
       float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < TK; ++c) {
+      for (int c = 0; c < 64; ++c) {
         const int kslot = k0 + c;
         const bool allow = (kslot <= qi) || (kslot >= lo && kslot < hi);
         sc[c] = allow ? sc[c] * scale_log2 : -INFINITY;
         mt = fmaxf(mt, sc[c]);
       }
+      // combine the row maximum with the partner warp (other half of the columns)
+      float* xm = sMax + (j & 1) * 2 * TQ;
+      xm[half * TQ + row] = mt;
+      named_sync(1, kSoftmaxThreads);
+      mt = fmaxf(mt, xm[(half ^ 1) * TQ + row]);
       const float m_new = fmaxf(m, mt);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = (m == m_new) ? 1.f : exp2f(m - m_use);
       float rs = 0.f;
-      uint32_t pk[TK / 2];
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < TK; c += 2) {
+      for (int c = 0; c < 64; c += 2) {
         const float p0 = exp2f(sc[c] - m_use), p1 = exp2f(sc[c + 1] - m_use);
         rs += p0 + p1;
         pk[c / 2] = pack_bf16x2(p0, p1);
@@ -227,50 +244,49 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       l = l * alpha + rs;
       m = m_new;
       if (j > 0) {
-        // O holds sum over tiles < j: wait for PV(j-1) before touching O or P
+        // O holds the sum over tiles < j: wait for PV(j-1) before touching O or P
         if (!mbar_wait(pv_done, (j - 1) & 1, status, 207)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < HD; c += 32) {
+          for (int c = 0; c < 64; c += 32) {
             float ov[32];
-            tmem_ld32(tO + lane_off + c, ov);
+            tmem_ld32(tO + lane_off + cb + c, ov);
             tmem_wait_ld();
             uint32_t ou[32];
 #pragma unroll
             for (int t = 0; t < 32; ++t) ou[t] = __float_as_uint(ov[t] * alpha);
-            tmem_st16(tO + lane_off + c, ou);
-            tmem_st16(tO + lane_off + c + 16, ou + 16);
+            tmem_st16(tO + lane_off + cb + c, ou);
+            tmem_st16(tO + lane_off + cb + c + 16, ou + 16);
           }
           tmem_wait_st();
         }
       }
-      // P row -> shared memory, 128B-swizzled K-major (keys contiguous)
+      // this half's 64 keys of the P row -> shared memory (one 128B-swizzled chunk)
+      uint8_t* base = sP + half * CHUNK;
 #pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        uint8_t* base = sP + ch * CHUNK;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int w = ch * 32 + u * 4;
-          *reinterpret_cast<uint4*>(base + swz(row, u)) =
-              make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
-        }
-      }
+      for (int u = 0; u < 8; ++u)
+        *reinterpret_cast<uint4*>(base + swz(row, u)) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
       fence_proxy_async();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
+    // row sums: each half accumulated its own columns
+    sSum[half * TQ + row] = l;
+    named_sync(1, kSoftmaxThreads);
+    l += sSum[(half ^ 1) * TQ + row];
     if (ok && n > 0 && mbar_wait(pv_done, (n - 1) & 1, status, 208)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         float ov[32];
-        tmem_ld32(tO + lane_off + c, ov);
+        tmem_ld32(tO + lane_off + cb + c, ov);
         tmem_wait_ld();
         if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(O + (int64_t)s * o_ss + h * HD + c);
+          uint4* dst = reinterpret_cast<uint4*>(O + (int64_t)s * o_ss + h * HD + cb + c);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             dst[q] = make_uint4(pack_bf16x2(ov[8 * q] * inv, ov[8 * q + 1] * inv),
@@ -279,7 +295,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                                 pack_bf16x2(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv));
         }
       }
-      if (valid) lse[(int64_t)h * g.S + s] = (m + log2f(l)) * kLn2;
+      if (valid && half == 0) lse[(int64_t)h * g.S + s] = (m + log2f(l)) * kLn2;
     }
   }
 

@@ -27,7 +27,10 @@ namespace {
 using namespace sm100;
 using namespace attn_tc;
 
-constexpr int kThreads = 192;
+// warp 0 TMA, warp 1 MMA, warps 2..9 softmax/epilogue: two warps per TMEM lane
+// quarter, each owning 64 of the 128 query (or head-dim) columns
+constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 256;
 // K, V, Q, dO, P^T, dS^T tiles + per-query (lse, delta, anchor, depth) x 2 buffers
 constexpr size_t SMEM_BWD = 1024 + 6 * TILE_BYTES + 2 * 4 * TQ * 4 + 256;
 
@@ -161,9 +164,9 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     mbar_init(qdo_full, 1);
     mbar_init(qdo_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(mm_done, 1);
-    mbar_init(dq_read, 4);
+    mbar_init(dq_read, 8);
     fence_barrier_init();
     fence_proxy_async();
   }
@@ -247,8 +250,10 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       }
     }
   } else {
-    // ---------------- softmax / epilogue warps (128 threads) ----------------
+    // ---------------- softmax / epilogue warps (256 threads) ----------------
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // warps 2..5 -> 0, 6..9 -> 1
+    const int cb = half * 64;          // query columns (softmax) / head-dim columns (epilogues)
     const int row = quarter * 32 + lane;  // TMEM lane: key row (S^T, dP^T, dK, dV) / query row (dQ)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int kj = k0 + row;
@@ -262,8 +267,8 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const int q0 = qr.at(it) * TQ;
       const int buf = it & 1;
       const bool full = tile_fully_allowed(g, q0, k0);
-      {
-        // per-query operands of this tile, one per thread
+      if (half == 0) {
+        // per-query operands of this tile, one per thread of the first half
         const int q = q0 + row;
         float lv = INFINITY, dl = 0.f;
         int qa = -1, qd = 0;
@@ -277,7 +282,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         sA[buf * TQ + row] = qa;
         sDp[buf * TQ + row] = qd;
       }
-      named_sync(1, 128);
+      named_sync(1, kSoftmaxThreads);
       if (!mbar_wait(s_full, it & 1, status, 306)) { ok = false; break; }
       tc_fence_after();
       const float* L2 = sL + buf * TQ;
@@ -285,7 +290,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       const int* QA = sA + buf * TQ;
       const int* QD = sDp + buf * TQ;
 #pragma unroll 1
-      for (int c0 = 0; c0 < TQ; c0 += 32) {
+      for (int c0 = cb; c0 < cb + 64; c0 += 32) {
         float sv[32], dpv[32];
         tmem_ld32(tS + lane_off + c0, sv);
         tmem_ld32(tDP + lane_off + c0, dpv);
@@ -337,7 +342,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       tc_fence_after();
       const int q = q0 + row;
 #pragma unroll 1
-      for (int c0 = 0; c0 < HD; c0 += 32) {
+      for (int c0 = cb; c0 < cb + 64; c0 += 32) {
         float v[32];
         tmem_ld32(tS + lane_off + c0, v);
         tmem_wait_ld();
@@ -351,7 +356,7 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     if (ok && n_it > 0) {
       const int64_t kv_ld = (int64_t)Hkv * HD;
 #pragma unroll 1
-      for (int c0 = 0; c0 < HD; c0 += 32) {
+      for (int c0 = cb; c0 < cb + 64; c0 += 32) {
         float v[32];
         tmem_ld32(tDK + lane_off + c0, v);
         tmem_wait_ld();

@@ -12,7 +12,8 @@
 // warp 1 issues tcgen05.mma (128 x BN x 16) into a double-buffered TMEM
 // accumulator, warps 2-5 drain the other accumulator (tcgen05.ld) and store to
 // HBM, so the epilogue of tile i overlaps the main loop of tile i+1.  The grid
-// is one CTA per SM; tiles are walked in groups of 8 M-tiles for L2 reuse of B.
+// is one CTA per SM; tiles are walked in L2-sized groups of M-tiles so each
+// operand streams from HBM about once.
 #include "gemm.cuh"
 #include "sm100.cuh"
 
@@ -46,8 +47,11 @@ struct TcCfg {
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
-  constexpr int G = 8;
+// Tiles are walked in groups of G M-tiles (all N-tiles of a group before the next
+// group): the group's A panel and the B panels in flight stay in L2, so each
+// operand is read from HBM about once when the A panel of a group fits in L2.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int G, int& tm,
+                                            int& tn) {
   const int per_group = G * tiles_n;
   const int g = tile / per_group;
   const int first = g * G;
@@ -165,6 +169,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int tiles_n = (N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = (K + BK - 1) / BK;
+  // group as many M-tiles as keep ~40 MB of A panels resident, at least 8
+  const int64_t a_panel = (int64_t)BM * K * 2;
+  const int group_m = min(tiles_m, max(8, (int)((40ll << 20) / a_panel)));
 
   if (warp == 0) {
     if (elect_one()) {
@@ -175,7 +182,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t last_phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int tm, tn;
-        tile_coords(tile, tiles_m, tiles_n, tm, tn);
+        tile_coords(tile, tiles_m, tiles_n, group_m, tm, tn);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, status, 101)) { ok = false; break; }
           uint8_t* a_dst = smem + stage * Cfg::STAGE_BYTES;
@@ -243,7 +250,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       int tm, tn;
-      tile_coords(tile, tiles_m, tiles_n, tm, tn);
+      tile_coords(tile, tiles_m, tiles_n, group_m, tm, tn);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[acc], acc_phase, status, 104)) break;
