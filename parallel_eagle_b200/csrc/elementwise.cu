@@ -63,6 +63,66 @@ __global__ void swiglu_bwd_kernel(int64_t rows, int64_t I, const T* __restrict__
   }
 }
 
+// Vectorised SwiGLU for bf16 rows with I % 8 == 0: 8 columns (16 B) per thread,
+// blockIdx.y = row, so no per-element index division.
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* f) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__global__ void swiglu_fwd_vec_kernel(int64_t I, const __nv_bfloat16* __restrict__ gu,
+                                      int64_t ldgu, __nv_bfloat16* __restrict__ a, int64_t lda) {
+  const int64_t r = blockIdx.y;
+  const int64_t c = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= I) return;
+  float g[8], u[8], o[8];
+  load8(gu + r * ldgu + c, g);
+  load8(gu + r * ldgu + I + c, u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = round_to<__nv_bfloat16>(g[i] * sigmoidf_(g[i])) * u[i];
+  store8(a + r * lda + c, o);
+}
+
+__global__ void swiglu_bwd_vec_kernel(int64_t I, const __nv_bfloat16* __restrict__ da,
+                                      int64_t ldda, const __nv_bfloat16* __restrict__ gu,
+                                      int64_t ldgu, __nv_bfloat16* __restrict__ dgu,
+                                      int64_t lddgu) {
+  const int64_t r = blockIdx.y;
+  const int64_t c = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= I) return;
+  float d[8], g[8], u[8], dg[8], du[8];
+  load8(da + r * ldda + c, d);
+  load8(gu + r * ldgu + c, g);
+  load8(gu + r * ldgu + I + c, u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float s = sigmoidf_(g[i]);
+    const float act = round_to<__nv_bfloat16>(g[i] * s);
+    const float dact = round_to<__nv_bfloat16>(d[i] * u[i]);
+    du[i] = d[i] * act;
+    dg[i] = dact * (s * (1.0f + g[i] * (1.0f - s)));
+  }
+  store8(dgu + r * lddgu + c, dg);
+  store8(dgu + r * lddgu + I + c, du);
+}
+
+bool vec8_ok(const void* p, int64_t ld) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && ld % 8 == 0;
+}
+
 // out[c] = sum_r x[r, c]; 32 columns per block, 8 row lanes, fixed order.
 template <typename T>
 __global__ void rowsum_cols_kernel(int64_t rows, int64_t H, const T* __restrict__ x, int64_t ldx,
@@ -143,6 +203,13 @@ extern "C" int pe_swiglu_fwd(int dtype, int64_t rows, int64_t I, const void* gu,
                              void* a, int64_t lda, void* stream) {
   PE_CHECK_ARG(rows >= 0 && I > 0 && ldgu >= 2 * I && lda >= I, "swiglu_fwd: bad shape");
   if (rows == 0) return PE_OK;
+  if (dtype == PE_BF16 && I % 8 == 0 && rows <= 65535 && vec8_ok(gu, ldgu) && vec8_ok(a, lda)) {
+    dim3 grid((unsigned)ceil_div(I / 8, 256), (unsigned)rows);
+    swiglu_fwd_vec_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+        I, (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)a, lda);
+    PE_LAUNCHED();
+    return PE_OK;
+  }
   return PE_DISPATCH(dtype, T, [&] {
     swiglu_fwd_kernel<T><<<grid_for(rows * I, 256), 256, 0, as_stream(stream)>>>(
         rows, I, (const T*)gu, ldgu, (T*)a, lda);
@@ -157,6 +224,15 @@ extern "C" int pe_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* da,
   PE_CHECK_ARG(rows >= 0 && I > 0 && ldgu >= 2 * I && lddgu >= 2 * I && ldda >= I,
                "swiglu_bwd: bad shape");
   if (rows == 0) return PE_OK;
+  if (dtype == PE_BF16 && I % 8 == 0 && rows <= 65535 && vec8_ok(da, ldda) && vec8_ok(gu, ldgu) &&
+      vec8_ok(dgu, lddgu)) {
+    dim3 grid((unsigned)ceil_div(I / 8, 256), (unsigned)rows);
+    swiglu_bwd_vec_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+        I, (const __nv_bfloat16*)da, ldda, (const __nv_bfloat16*)gu, ldgu, (__nv_bfloat16*)dgu,
+        lddgu);
+    PE_LAUNCHED();
+    return PE_OK;
+  }
   return PE_DISPATCH(dtype, T, [&] {
     swiglu_bwd_kernel<T><<<grid_for(rows * I, 256), 256, 0, as_stream(stream)>>>(
         rows, I, (const T*)da, ldda, (const T*)gu, ldgu, (T*)dgu, lddgu);

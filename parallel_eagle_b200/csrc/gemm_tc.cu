@@ -7,7 +7,8 @@
 // of the input- and weight-gradient GEMMs), so the three GEMMs of every
 // nn.Linear run without transposing anything in HBM.
 //
-// CTA tile 128 x BN (BN = 256 or 128), K slices of 64 (one 128-byte swizzle
+// CTA tile 128 x BN (BN in 128..256, chosen per shape to avoid a nearly empty
+// last wave), K slices of 64 (one 128-byte swizzle
 // row of bf16).  Warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
 // warp 1 issues tcgen05.mma (128 x BN x 16) into a double-buffered TMEM
 // accumulator, warps 2-5 drain the other accumulator (tcgen05.ld) and store to
@@ -37,15 +38,50 @@ struct EpiArgs {
   const float* rowscale;
 };
 
+constexpr uint32_t pow2_at_least(uint32_t x) {
+  uint32_t p = 32;
+  while (p < x) p <<= 1;
+  return p;
+}
+
 template <int BN>
 struct TcCfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "tile width");
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // as many ring stages as fit in ~220 KB of shared memory (at most 8)
+  static constexpr int STAGES = (220u * 1024u / STAGE_BYTES) > 8 ? 8 : (220u * 1024u / STAGE_BYTES);
+  static constexpr uint32_t TMEM_COLS = pow2_at_least(2 * BN);  // double-buffered accumulator
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 };
+
+// Tile width for an M x N problem: the candidate that minimises the predicted
+// time ceil(tiles / SMs) * per-tile cost, so a problem of 3.03 waves at 256 wide
+// does not pay for a nearly empty fourth wave.  Narrower tiles stream more
+// operand bytes per FLOP; the factors below are their relative per-tile speed.
+// MN-major B is loaded in 64-column boxes, so its width must be a multiple of 64.
+int choose_bn(int64_t M, int64_t N, bool b_mn, int sms) {
+  struct Cand {
+    int bn;
+    float speed;
+  };
+  static const Cand cands[] = {{256, 1.00f}, {224, 0.97f}, {192, 0.95f}, {160, 0.93f}, {128, 0.88f}};
+  const int64_t tm = (M + BM - 1) / BM;
+  int best = 256;
+  double best_t = 1e30;
+  for (const Cand& c : cands) {
+    if (b_mn && c.bn % 64 != 0) continue;
+    const int64_t tiles = tm * ((N + c.bn - 1) / c.bn);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const double t = (double)waves * c.bn / c.speed;
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = c.bn;
+    }
+  }
+  return best;
+}
 
 // Tiles are walked in groups of G M-tiles (all N-tiles of a group before the next
 // group): the group's A panel and the B panels in flight stay in L2, so each
@@ -364,13 +400,50 @@ bool gemm_tc_eligible(int dtype, int64_t M, int64_t N, int64_t K, const void* A,
   return true;
 }
 
+template <int BN, typename OutT>
+int launch_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
+              int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin, float alpha,
+              float beta, int vec_ok, int* status, cudaStream_t s) {
+  if constexpr (BN % 64 == 0) {
+    return launch_majors<BN, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
+                                   vec_ok, status, s);
+  } else {
+    if (b_mn) {
+      set_error("gemm: tile width %d needs a K-major B operand", BN);
+      return PE_ERR_ARG;
+    }
+    if (a_mn)
+      return launch<BN, true, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
+                                           vec_ok, status, s);
+    return launch<BN, false, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok,
+                                          status, s);
+  }
+}
+
+template <typename OutT>
+int launch_any_bn(int BN, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                  int M, int N, int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin,
+                  float alpha, float beta, int vec_ok, int* status, cudaStream_t s) {
+  switch (BN) {
+    case 256: return launch_bn<256, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    case 224: return launch_bn<224, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    case 192: return launch_bn<192, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    case 160: return launch_bn<160, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    case 128: return launch_bn<128, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    default: break;
+  }
+  set_error("gemm: unsupported tile width %d", BN);
+  return PE_ERR_ARG;
+}
+
 int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
             const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
             const void* Cin, int64_t ldcin, float alpha, float beta, int* status,
-            cudaStream_t stream) {
+            cudaStream_t stream, int force_bn) {
   const bool a_mn = a_sk != 1;
   const bool b_mn = b_sk != 1;
-  const int BN = N > 128 ? 256 : 128;
+  const int BN = force_bn > 0 ? force_bn : choose_bn(M, N, b_mn, sm_count());
+  PE_CHECK_ARG(!(b_mn && BN % 64 != 0), "gemm: tile width %d needs a K-major B operand", BN);
   CUtensorMap ta, tb;
   int rc;
   if (!a_mn)
@@ -387,14 +460,11 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
   const int vec_ok = (ldc * esz) % 16 == 0 && al16(C) &&
                      (!Cin || ((ldcin * esz) % 16 == 0 && al16(Cin)));
   const int m = (int)M, n = (int)N, k = (int)K;
-  if (c_dtype == PE_F32) {
-    if (BN == 256)
-      return launch_majors<256, float>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
-    return launch_majors<128, float>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
-  }
-  if (BN == 256)
-    return launch_majors<256, __nv_bfloat16>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
-  return launch_majors<128, __nv_bfloat16>(a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, stream);
+  if (c_dtype == PE_F32)
+    return launch_any_bn<float>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta,
+                                vec_ok, status, stream);
+  return launch_any_bn<__nv_bfloat16>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha,
+                                      beta, vec_ok, status, stream);
 }
 
 int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
@@ -437,15 +507,20 @@ int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm
   PE_CHECK_ARG(ldc >= N, "gemm: ldc < N");
   if (M == 0 || N == 0) return PE_OK;
   PE_CHECK_ARG(K > 0, "gemm: K == 0 is not supported");
+  const int force_bn = algo >> 8;
+  algo &= 0xff;
+  PE_CHECK_ARG(force_bn == 0 || force_bn == 128 || force_bn == 160 || force_bn == 192 ||
+                   force_bn == 224 || force_bn == 256,
+               "gemm: forced tile width %d not one of 128/160/192/224/256", force_bn);
   const bool tc_ok = gemm_tc_eligible(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, c_dtype);
   if (algo == PE_ALGO_TCGEN05) {
     PE_CHECK_ARG(tc_ok, "gemm: operands not eligible for the tcgen05 path");
     return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
-                   beta, status, stream);
+                   beta, status, stream, force_bn);
   }
   if (algo == PE_ALGO_AUTO && tc_ok)
     return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
-                   beta, status, stream);
+                   beta, status, stream, force_bn);
   return gemm_simt(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin,
                    alpha, beta, stream);
 }

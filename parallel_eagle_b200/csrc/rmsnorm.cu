@@ -142,6 +142,90 @@ rmsnorm_bwd_kernel(int64_t rows, int64_t H, const T* __restrict__ dy, int64_t ld
   }
 }
 
+// Backward for rows whose width is a multiple of 256 (up to 4096): lane l owns
+// the 8 contiguous columns c*256 + 8l.. of every 256-column chunk c, so the
+// weight-gradient partial stays in registers across all rows a warp handles and
+// the block reduces it through shared memory once at the end (no per-element
+// shared-memory atomics).  Two passes over each row; the second re-reads dy and x
+// from L1.
+constexpr int kMaxChunks = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_bwd_chunked_kernel(int64_t rows, int64_t H, int nch, const T* __restrict__ dy,
+                           int64_t lddy, const T* __restrict__ x, int64_t ldx,
+                           const T* __restrict__ w, const float* __restrict__ rstd, T* dx,
+                           int64_t lddx, const T* res, int64_t ldres,
+                           float* __restrict__ dw_partial) {
+  extern __shared__ float sdw[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float acc[kMaxChunks][8];
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[i][k] = 0.f;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
+       row += (int64_t)gridDim.x * kWarps) {
+    const T* dyr = dy + row * lddy;
+    const T* xr = x + row * ldx;
+    const float r = rstd[row];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      if (i < nch) {
+        const int64_t c = (int64_t)i * 256 + lane * 8;
+        float a[8], b[8], g[8];
+        Vec<T, 8>::load(dyr + c, a);
+        Vec<T, 8>::load(xr + c, b);
+        Vec<T, 8>::load(w + c, g);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += (a[k] * g[k]) * b[k];
+      }
+    }
+    s = warp_sum(s);
+    const float coef = s * r * r * r / (float)H;
+    T* dxr = dx + row * lddx;
+    const T* rr = res ? res + row * ldres : nullptr;
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      if (i < nch) {
+        const int64_t c = (int64_t)i * 256 + lane * 8;
+        float a[8], b[8], g[8], o[8];
+        Vec<T, 8>::load(dyr + c, a);
+        Vec<T, 8>::load(xr + c, b);
+        Vec<T, 8>::load(w + c, g);
+        if (rr) {
+          Vec<T, 8>::load(rr + c, o);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          o[k] += r * (a[k] * g[k]) - b[k] * coef;
+          acc[i][k] += a[k] * (b[k] * r);
+        }
+        Vec<T, 8>::store(dxr + c, o);
+      }
+    }
+  }
+  if (dw_partial) {
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) sdw[c] = 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      if (i < nch) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) atomicAdd(&sdw[i * 256 + lane * 8 + k], acc[i][k]);
+      }
+    }
+    __syncthreads();
+    float* out = dw_partial + (int64_t)blockIdx.x * H;
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) out[c] = sdw[c];
+  }
+}
+
 // out[c] = (acc ? out[c] : 0) + sum_b partial[b, c]; fixed summation order.
 template <typename T>
 __global__ void colsum_kernel(int64_t nblk, int64_t H, const float* __restrict__ partial,
@@ -209,6 +293,19 @@ extern "C" int pe_rmsnorm_bwd(int dtype, int64_t rows, int64_t H, const void* dy
                    (!residual || ldres % 8 == 0) && aligned16(dy) && aligned16(x) &&
                    aligned16(w) && aligned16(dx) && (!residual || aligned16(residual));
   const size_t smem = dw_partial ? (size_t)H * 4 : 0;
+  const bool chunked = vec && H % 256 == 0 && H / 256 <= kMaxChunks;
+  if (chunked) {
+    return PE_DISPATCH(dtype, T, [&] {
+      auto kern = rmsnorm_bwd_chunked_kernel<T>;
+      if (smem > 48 * 1024)
+        PE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      kern<<<(unsigned)nblk, kWarps * 32, smem, as_stream(stream)>>>(
+          rows, H, (int)(H / 256), (const T*)dy, lddy, (const T*)x, ldx, (const T*)w, rstd,
+          (T*)dx, lddx, (const T*)residual, ldres, dw_partial);
+      PE_LAUNCHED();
+      return PE_OK;
+    });
+  }
   return PE_DISPATCH(dtype, T, [&] {
     auto kern = vec ? rmsnorm_bwd_kernel<T, 8> : rmsnorm_bwd_kernel<T, 1>;
     if (smem > 48 * 1024)

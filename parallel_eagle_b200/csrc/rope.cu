@@ -45,6 +45,41 @@ __global__ void rope_kernel(int64_t rows, int heads, int hd, T* x, int64_t ldx,
   base[p + half] = from_f<T>(yb);
 }
 
+// One thread per (row, pair): the angle, cos and sin are computed once and applied
+// to the pair in every head of the row (q and k heads share positions).  Threads of
+// a warp cover consecutive pairs, so each head's two half-rows are read and
+// written as contiguous segments.
+template <typename T>
+__global__ void rope_rowpair_kernel(int64_t rows, int heads, int hd, T* x, int64_t ldx,
+                                    const int64_t* __restrict__ pos, float theta, int inverse) {
+  const int half = hd >> 1;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * half) return;
+  const int64_t row = idx / half;
+  const int p = (int)(idx - row * half);
+  const float inv_freq = 1.0f / powf(theta, (float)(2 * p) / (float)hd);
+  float s, c;
+  sincosf((float)pos[row] * inv_freq, &s, &c);
+  c = round_to<T>(c);
+  s = round_to<T>(s);
+  T* base = x + row * ldx + p;
+  for (int h = 0; h < heads; ++h) {
+    T* hp = base + (int64_t)h * hd;
+    const float a = to_f(hp[0]);
+    const float b = to_f(hp[half]);
+    float ya, yb;
+    if (!inverse) {
+      ya = round_to<T>(round_to<T>(a * c) + round_to<T>(-b * s));
+      yb = round_to<T>(round_to<T>(b * c) + round_to<T>(a * s));
+    } else {
+      ya = round_to<T>(round_to<T>(a * c) + round_to<T>(b * s));
+      yb = round_to<T>(round_to<T>(b * c) - round_to<T>(a * s));
+    }
+    hp[0] = from_f<T>(ya);
+    hp[half] = from_f<T>(yb);
+  }
+}
+
 }  // namespace
 }  // namespace pe
 
@@ -56,8 +91,17 @@ extern "C" int pe_rope(int dtype, int64_t rows, int heads, int head_dim, void* x
                "rope: bad shape");
   PE_CHECK_ARG(ldx >= (int64_t)heads * head_dim, "rope: ldx too small");
   if (rows == 0) return PE_OK;
-  const int64_t total = rows * heads * (head_dim / 2);
   const int threads = 256;
+  if (heads >= 4) {
+    const int64_t total = rows * (head_dim / 2);
+    return PE_DISPATCH(dtype, T, [&] {
+      rope_rowpair_kernel<T><<<(unsigned)ceil_div(total, threads), threads, 0, as_stream(stream)>>>(
+          rows, heads, head_dim, (T*)x, ldx, pos, theta, inverse);
+      PE_LAUNCHED();
+      return PE_OK;
+    });
+  }
+  const int64_t total = rows * heads * (head_dim / 2);
   return PE_DISPATCH(dtype, T, [&] {
     rope_kernel<T><<<(unsigned)ceil_div(total, threads), threads, 0, as_stream(stream)>>>(
         rows, heads, head_dim, (T*)x, ldx, pos, theta, inverse);

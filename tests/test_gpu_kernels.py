@@ -78,6 +78,21 @@ def test_gemm_tcgen05_matches_fp32(shape, a_mn, b_mn, out_f32):
     assert rel(C[:, :N].float().cpu(), prev + 0.5 * ref) < (1e-5 if out_f32 else 5e-3)
 
 
+@pytest.mark.parametrize("bn", [128, 160, 192, 224, 256])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, False), (False, True), (True, True)])
+def test_gemm_tcgen05_every_tile_width(bn, a_mn, b_mn):
+    if b_mn and bn % 64:
+        pytest.skip("MN-major B needs a tile width that is a multiple of 64")
+    M, N, K = 300, 3584 // 4 + 40, 520
+    A, (a_sm, a_sk), Ad = _operand(M, K, a_mn, torch.bfloat16, 5)
+    B, (b_sn, b_sk), Bd = _operand(N, K, b_mn, torch.bfloat16, 6)
+    C = torch.zeros(M, N, dtype=torch.float32, device=DEV)
+    ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, N, algo=L.ALGO_TCGEN05 | (bn << 8))
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert rel(C.cpu(), Ad @ Bd.t()) < 1e-5
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
 def test_gemm_simt_matches_fp32(dtype, a_mn, b_mn):
