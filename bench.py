@@ -242,7 +242,10 @@ def run_ours(args):
     with ClockSampler(local) as clocks:
         e0.record(stream)
         for _ in range(args.steps):
+            # the NVTX range lets a profiler select exactly the timed steps' launches
+            torch.cuda.nvtx.range_push("pe_step")
             trainer.step(seqs, gb)
+            torch.cuda.nvtx.range_pop()
         e1.record(stream)
         torch.cuda.synchronize()
     barrier()
@@ -328,9 +331,9 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def gemm_roofline(c, dev, peak, src):
-    """Time the step's largest GEMM (fused gate/up projection of a 4096-slot
-    segment) with CUDA events on its stream."""
+def gemm_case(c, dev):
+    """The step's largest GEMM: the fused gate/up projection of a 4096-slot segment
+    (M=4096, N=2*I, K=H).  Returns (run, flops per run, algorithmic bytes per run)."""
     from parallel_eagle_b200 import ops
 
     H, I = c["hidden"], c["intermediate"]
@@ -339,32 +342,16 @@ def gemm_roofline(c, dev, peak, src):
     x = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
     w = (torch.randn(2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
     out = torch.empty(M, 2 * I, dtype=torch.bfloat16, device=dev)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    for _ in range(3):
+
+    def run():
         ops.linear(x, w, out=out)
-    torch.cuda.synchronize()
-    s = torch.cuda.current_stream()
-    times = []
-    for _ in range(10):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(s)
-        ops.linear(x, w, out=out)
-        b.record(s)
-        torch.cuda.synchronize()
-        times.append(a.elapsed_time(b))
-    ms = sum(times) / len(times)
-    flops = 2.0 * M * 2 * I * H
-    achieved = flops / (ms / 1e3) / 1e12
-    return {"kernel": "gemm_tc_kernel (gate/up projection, M=4096 N=37888 K=3584)",
-            "bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-            "frac": round(achieved / peak, 4), "peak_source": f"{src} bf16_tflops_sustained",
-            "traffic": None, "ms": round(ms, 4)}
+
+    return run, 2.0 * M * 2 * I * H, 2.0 * (M * H + 2 * I * H + M * 2 * I)
 
 
-def attention_roofline(c, dev, peak, src):
-    """Masked-attention fwd+bwd over the S segments of one config-2 sequence,
-    timed with CUDA events; FLOPs = 12 * hd * Hq * allowed pairs (no recompute)."""
+def attention_case(c, dev):
+    """Masked-attention fwd+bwd over the S segments of one config-2 sequence.
+    FLOPs = 12 * hd * Hq * allowed pairs (no recompute)."""
     from parallel_eagle_b200 import _lib, ops
     from parallel_eagle_b200.engine import segment_bounds
 
@@ -385,24 +372,99 @@ def attention_roofline(c, dev, peak, src):
             o, lse = ops.attn_fwd(q, kk, vv, nh, nkv, hd, lay)
             ops.attn_bwd(q, kk, vv, o, do, lse, nh, nkv, hd, lay)
 
-    for _ in range(3):
+    return run, 12.0 * hd * nh * attention_pairs(c["n"], k, c["segments"]), None
+
+
+def lmhead_case(c, dev):
+    """Fused LM-head cross entropy (loss + input gradient) over the 2560 loss slots
+    of one 512-token segment at K=5 against the full 152064-row head."""
+    from parallel_eagle_b200 import ops
+
+    R, H, V = 2560, c["hidden"], c["vocab"]
+    g = torch.Generator(device=dev).manual_seed(13)
+    h = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
+    W = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    lab = torch.randint(0, V, (R,), generator=g, device=dev)
+    loss = torch.zeros(1, device=dev)
+
+    def run():
+        ops.lmhead_ce(h, W, lab, 1e-4, loss)
+
+    return run, 2.0 * 2 * R * V * H, None
+
+
+def time_case(run, reps, warmup=3, flush=None):
+    """Average milliseconds of ``run`` over ``reps`` CUDA-event-timed calls on the
+    current stream; ``flush`` (a buffer larger than L2) is rewritten before each."""
+    for _ in range(warmup):
         run()
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 5
-    a.record(s)
+    times = []
     for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
         run()
-    b.record(s)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
-    flops = 12.0 * hd * nh * attention_pairs(c["n"], k, c["segments"])
+        b.record(s)
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    return sum(times) / len(times)
+
+
+def profiled_traffic(name):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/<name>
+    (the ``traffic_bytes_per_launch:`` line), or None."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return int(float(line.split(":", 1)[1].split()[0]))
+    return None
+
+
+GEMM_PROFILE = "gemm_tc_gateup_4096x37888x3584.txt"
+
+
+def gemm_roofline(c, dev, peak, src):
+    """Time the step's largest GEMM with CUDA events on its stream, L2 flushed
+    between launches."""
+    run, flops, nbytes = gemm_case(c, dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    ms = time_case(run, 10, flush=flush)
+    achieved = flops / (ms / 1e3) / 1e12
+    return {"kernel": "gemm_tc_kernel (gate/up projection, M=4096 N=37888 K=3584)",
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{src} bf16_tflops_sustained",
+            "traffic": profiled_traffic(GEMM_PROFILE), "algorithmic_bytes": int(nbytes),
+            "ms": round(ms, 4)}
+
+
+def attention_roofline(c, dev, peak, src):
+    run, flops, _ = attention_case(c, dev)
+    ms = time_case(run, 5)
     achieved = flops / (ms / 1e3) / 1e12
     return {"kernels": "attn_fwd_tc_kernel + attn_bwd_tc_kernel (+ prep/cast)",
             "segments": c["segments"], "ms_per_sequence": round(ms, 3),
             "tflops": round(achieved, 1), "peak": peak, "frac": round(achieved / peak, 4),
             "peak_source": f"{src} bf16_tflops (burst)", "flops_per_sequence": flops}
+
+
+def run_kernel(args):
+    """One kernel family on its bench-sized case (the unit an ncu capture covers)."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from parallel_eagle_b200 import ops
+
+    c = dict(CONFIG2)
+    case = {"gemm": gemm_case, "attn": attention_case, "lmhead": lmhead_case}[args.kernel]
+    run, flops, _ = case(c, dev)
+    ms = time_case(run, args.steps, warmup=args.warmup)
+    ops.check_status(dev)
+    print(json.dumps({"kernel": args.kernel, "ms": round(ms, 4),
+                      "tflops": round(flops / (ms / 1e3) / 1e12, 1)}), flush=True)
 
 
 def cpu_baseline(args, n=None):
@@ -469,8 +531,12 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=None, help="override per-GPU batch")
     ap.add_argument("--cpu-n", type=int, default=256, help="sequence length of the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["gemm", "attn", "lmhead"], default=None,
+                    help="time one kernel family on its bench-sized case instead of the step")
     args = ap.parse_args(argv)
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
