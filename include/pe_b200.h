@@ -141,6 +141,9 @@ int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
  *   (or, with teacher rows t_r: loss_r = -sum_v softmax(t_r W^T)_v log_softmax(z_r)_v)
  *   loss_sum[0] += sum_r loss_r;  dh = grad_scale * d(sum_r loss_r)/dh
  * Rows with label < 0 are ignored.  No gradient reaches W (frozen).
+ * For the bf16 hard-label path, algo bits 8-15 set the vocabulary chunk (units of
+ * 1024 rows of W, at most 16) and bits 16-23 the loss-row group (units of 256
+ * rows, at most 32); zero keeps the defaults (16384 and 4096).
  * Replaces reference src/pe/partition.py:113-115 (lm_head -> float ->
  * cross_entropy(sum) -> backward) and drafter.py:123-124.
  * ------------------------------------------------------------------------- */

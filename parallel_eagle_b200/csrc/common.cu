@@ -1,6 +1,8 @@
 // Library-wide state: thread-local error message, launch counter, device queries.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace pe {
 
 static thread_local std::string g_last_error;
@@ -28,6 +30,40 @@ int sm_count() {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+namespace {
+constexpr int kMaxDev = 64, kSlots = 4, kEvents = 32;
+std::mutex g_stream_mu;
+cudaStream_t g_streams[kMaxDev][kSlots];
+cudaEvent_t g_events[kMaxDev][kEvents];
+}  // namespace
+
+cudaStream_t side_stream(int slot) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev || slot < 0 ||
+      slot >= kSlots)
+    return nullptr;
+  std::lock_guard<std::mutex> lk(g_stream_mu);
+  if (!g_streams[dev][slot]) {
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    g_streams[dev][slot] = s;
+  }
+  return g_streams[dev][slot];
+}
+
+cudaEvent_t pool_event(int i) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev || i < 0 || i >= kEvents)
+    return nullptr;
+  std::lock_guard<std::mutex> lk(g_stream_mu);
+  if (!g_events[dev][i]) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+    g_events[dev][i] = e;
+  }
+  return g_events[dev][i];
 }
 
 }  // namespace pe

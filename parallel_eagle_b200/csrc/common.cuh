@@ -84,6 +84,13 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // number of SMs of the current device (cached per device)
 int sm_count();
 
+// Library-owned non-blocking stream of the current device (slot 0..3), created on
+// first use; kernels independent of the caller's stream run there and are joined
+// back with events, so callers still see one ordered stream.
+cudaStream_t side_stream(int slot);
+// Timing-disabled event i (0..31) of the current device, reused across calls.
+cudaEvent_t pool_event(int i);
+
 // dispatch a lambda templated on the storage type
 #define PE_DISPATCH(dtype, T, ...)                                   \
   [&]() -> int {                                                    \

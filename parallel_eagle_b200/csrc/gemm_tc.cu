@@ -83,6 +83,30 @@ int choose_bn(int64_t M, int64_t N, bool b_mn, int sms) {
   return best;
 }
 
+// Pair tile width (tiles 256 x BN over the resident clusters): same wave model as
+// choose_bn.  MN-major B halves are loaded in 64-column boxes (BN/2 % 64 == 0).
+int choose_bn_pair(int64_t M, int64_t N, bool b_mn, int clusters) {
+  struct Cand {
+    int bn;
+    float speed;
+  };
+  static const Cand cands[] = {{256, 1.00f}, {192, 0.96f}, {128, 0.90f}};
+  const int64_t tm = (M + 2 * BM - 1) / (2 * BM);
+  int best = 256;
+  double best_t = 1e30;
+  for (const Cand& c : cands) {
+    if (b_mn && (c.bn / 2) % 64 != 0) continue;
+    const int64_t tiles = tm * ((N + c.bn - 1) / c.bn);
+    const int64_t waves = (tiles + clusters - 1) / clusters;
+    const double t = (double)waves * c.bn / c.speed;
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = c.bn;
+    }
+  }
+  return best;
+}
+
 // Tiles are walked in groups of G M-tiles (all N-tiles of a group before the next
 // group): the group's A panel and the B panels in flight stay in L2, so each
 // operand is read from HBM about once when the A panel of a group fits in L2.
@@ -152,6 +176,51 @@ __device__ __forceinline__ void store_row32(OutT* dst, const OutT* cin, const fl
         dst[i] = from_f<OutT>(t);
       }
     }
+  }
+}
+
+// Drains one accumulator -- TMEM lanes of this warp, BN fp32 columns starting at
+// column `acc_tmem` -- into row `gm` of C (tile column tn), applying the epilogue.
+template <int BN, typename OutT, int EPI>
+__device__ __forceinline__ void epilogue_tile(uint32_t acc_tmem, int64_t gm, int tn, int M, int N,
+                                              OutT* C, int64_t ldc, const OutT* Cin,
+                                              int64_t ldcin, float alpha, float beta, int vec_ok,
+                                              const EpiArgs& ea) {
+  // EPI_ROWSCALE: the accumulated input is scaled per row (online-softmax correction)
+  const float beta_row = (EPI == EPI_ROWSCALE && gm < M) ? ea.rowscale[gm] : beta;
+  float m_run = -INFINITY, s_run = 0.f;  // EPI_STATS: running row max / sum-exp
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    float v[32];
+    tmem_ld32(acc_tmem + c0, v);
+    tmem_wait_ld();
+    const int64_t gn0 = (int64_t)tn * BN + c0;
+    if (gm < M && gn0 < N) {
+      const int valid = (N - gn0) < 32 ? (int)(N - gn0) : 32;
+      if constexpr (EPI == EPI_STATS) {
+        // stats of the values as stored (rounded to the output type)
+        float cm = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = round_to<OutT>(alpha * v[i]);
+          if (i < valid) cm = fmaxf(cm, v[i]);
+        }
+        const float mn = fmaxf(m_run, cm);
+        float cs = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < valid) cs += __expf(v[i] - mn);
+        s_run = s_run * __expf(m_run - mn) + cs;
+        m_run = mn;
+        store_row32<OutT>(C + gm * ldc + gn0, nullptr, v, 1.f, 0.f, valid, vec_ok != 0);
+      } else {
+        store_row32<OutT>(C + gm * ldc + gn0, Cin ? Cin + gm * ldcin + gn0 : nullptr, v, alpha,
+                          beta_row, valid, vec_ok != 0);
+      }
+    }
+  }
+  if constexpr (EPI == EPI_STATS) {
+    if (gm < M && (int64_t)tn * BN < N) ea.stats[gm * ea.stats_ld + tn] = make_float2(m_run, s_run);
   }
 }
 
@@ -291,44 +360,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[acc], acc_phase, status, 104)) break;
       tc_fence_after();
-      const int64_t gm = (int64_t)tm * BM + row_in_tile;
-      // EPI_ROWSCALE: the accumulated input is scaled per row (online-softmax correction)
-      const float beta_row = (EPI == EPI_ROWSCALE && gm < M) ? ea.rowscale[gm] : beta;
-      float m_run = -INFINITY, s_run = 0.f;  // EPI_STATS: running row max / sum-exp
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c0, v);
-        tmem_wait_ld();
-        const int64_t gn0 = (int64_t)tn * BN + c0;
-        if (gm < M && gn0 < N) {
-          const int valid = (N - gn0) < 32 ? (int)(N - gn0) : 32;
-          if constexpr (EPI == EPI_STATS) {
-            // stats of the values as stored (rounded to the output type)
-            float cm = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              v[i] = round_to<OutT>(alpha * v[i]);
-              if (i < valid) cm = fmaxf(cm, v[i]);
-            }
-            const float mn = fmaxf(m_run, cm);
-            float cs = 0.f;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < valid) cs += __expf(v[i] - mn);
-            s_run = s_run * __expf(m_run - mn) + cs;
-            m_run = mn;
-            store_row32<OutT>(C + gm * ldc + gn0, nullptr, v, 1.f, 0.f, valid, vec_ok != 0);
-          } else {
-            store_row32<OutT>(C + gm * ldc + gn0, Cin ? Cin + gm * ldcin + gn0 : nullptr, v,
-                              alpha, beta_row, valid, vec_ok != 0);
-          }
-        }
-      }
-      if constexpr (EPI == EPI_STATS) {
-        if (gm < M && (int64_t)tn * BN < N)
-          ea.stats[gm * ea.stats_ld + tn] = make_float2(m_run, s_run);
-      }
+      epilogue_tile<BN, OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
+                                   (int64_t)tm * BM + row_in_tile, tn, M, N, C, ldc, Cin, ldcin,
+                                   alpha, beta, vec_ok, ea);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -340,6 +374,199 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------ //
+// CTA-pair variant: a cluster of two CTAs computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2.  CTA r of the pair loads A rows [128 r, 128 r + 128)
+// and B columns [BN/2 r, BN/2 r + BN/2) of the tile into its own shared memory
+// (both loads counted on the leader's `full` barrier), the leader issues the
+// MMAs, and each CTA's TMEM receives its 128 accumulator rows.  Per FLOP this
+// stages a third fewer operand bytes through L2 and shared memory than the
+// single-CTA 128 x 256 tile.
+// ------------------------------------------------------------------------ //
+template <int BN>
+struct PairCfg {
+  static_assert(BN % 32 == 0 && BN >= 128 && BN <= 256, "pair tile width");
+  static constexpr int BNH = BN / 2;  // B columns held by each CTA
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BNH * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200u * 1024u / STAGE_BYTES) > 8 ? 8 : (200u * 1024u / STAGE_BYTES);
+  static constexpr uint32_t TMEM_COLS = pow2_at_least(2 * BN);
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
+};
+
+template <int BN, bool A_MN, bool B_MN, typename OutT, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    int M, int N, int K, OutT* C, int64_t ldc, const OutT* Cin, int64_t ldcin,
+                    float alpha, float beta, int vec_ok, EpiArgs ea, int* status) {
+  using Cfg = PairCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int BNH = Cfg::BNH;
+  constexpr uint32_t IDESC = idesc_bf16(2 * BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);   // leader: its own arrive + both CTAs' bytes
+      mbar_init(&empty[s], 1);  // one MMA commit per consumed stage
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(mma_done, 1);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m = (M + 2 * BM - 1) / (2 * BM);
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+  const int64_t a_panel = (int64_t)2 * BM * K * 2;
+  const int group_m = min(tiles_m, max(4, (int)((40ll << 20) / a_panel)));
+  const int cid = (int)cluster_id_x();
+  const int ncl = (int)nclusters_x();
+
+  if (warp == 0) {
+    if (elect_one()) {
+      const uint32_t full_leader = mapa_shared(&full[0], 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
+        int tm, tn;
+        tile_coords(tile, tiles_m, tiles_n, group_m, tm, tn);
+        const int row0 = tm * 2 * BM + (int)rank * BM;
+        const int bcol0 = tn * BN + (int)rank * BNH;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, status, 111)) { ok = false; break; }
+          uint8_t* a_dst = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* b_dst = a_dst + Cfg::A_BYTES;
+          const uint32_t bar = full_leader + 8u * (uint32_t)stage;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, bar, kb * BK, row0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, bar, row0, kb * BK);
+            tma_load_2d_pair(a_dst + 8192, &tmA, bar, row0 + 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, bar, kb * BK, bcol0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BNH / 64; ++j)
+              tma_load_2d_pair(b_dst + j * 8192, &tmB, bar, bcol0 + 64 * j, kb * BK);
+          }
+          issued = true;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok && issued) {
+        // completions are counted on the leader's barrier: give this CTA's copies
+        // in flight a bounded moment to land before the CTA can exit
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 200000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = cid; tile < num_tiles && ok; tile += ncl, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, status, 112)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, status, 113)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_base = a_base + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sw128_desc(a_base + k * 2048, 8192, 1024)
+                                     : sw128_desc(a_base + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sw128_desc(b_base + k * 2048, 8192, 1024)
+                                     : sw128_desc(b_base + k * 32, 16, 1024);
+            mma_bf16_ss_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) mma_commit_pair(&acc_full[acc], 0x3);
+      }
+      if (issued) {
+        // every MMA of this pair has finished before TMEM is released
+        mma_commit_pair(mma_done, 0x1);
+        mbar_wait(mma_done, 0, status, 115);
+      }
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 of this CTA's 128 rows
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t acc_empty_leader = mapa_shared(&acc_empty[0], 0);
+    int local = 0;
+    for (int tile = cid; tile < num_tiles; tile += ncl, ++local) {
+      int tm, tn;
+      tile_coords(tile, tiles_m, tiles_n, group_m, tm, tn);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase, status, 114)) break;
+      tc_fence_after();
+      epilogue_tile<BN, OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
+                                   (int64_t)tm * 2 * BM + rank * BM + row_in_tile, tn, M, N, C,
+                                   ldc, Cin, ldcin, alpha, beta, vec_ok, ea);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader + 8u * (uint32_t)acc);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // neither CTA still touches the other's shared memory or TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -356,6 +583,63 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, vo
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kern<<<grid, kThreads, Cfg::SMEM, stream>>>(ta, tb, M, N, K, (OutT*)C, ldc, (const OutT*)Cin,
                                               ldcin, alpha, beta, vec_ok, ea, status);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
+// Clusters the pair kernel can keep resident at once (one CTA per SM), queried once
+// per instantiation; the persistent grid never exceeds it.
+template <typename Kern>
+int pair_capacity(Kern kern, size_t smem) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (unsigned)(sm_count() / 2), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    n = sm_count() / 2;
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, typename OutT, int EPI = EPI_STORE>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, void* C,
+                int64_t ldc, const void* Cin, int64_t ldcin, float alpha, float beta, int vec_ok,
+                int* status, cudaStream_t stream, EpiArgs ea = EpiArgs{}) {
+  using Cfg = PairCfg<BN>;
+  auto kern = gemm_tc_pair_kernel<BN, A_MN, B_MN, OutT, EPI>;
+  static int capacity[64] = {0};
+  int dev = 0;
+  PE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (capacity[dev] == 0) {
+    PE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM));
+    capacity[dev] = pair_capacity(kern, Cfg::SMEM);
+  }
+  const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
+  const int clusters = tiles < capacity[dev] ? tiles : capacity[dev];
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (unsigned)clusters, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, (OutT*)C, ldc, (const OutT*)Cin,
+                                 ldcin, alpha, beta, vec_ok, ea, status));
   PE_LAUNCHED();
   return PE_OK;
 }
@@ -436,14 +720,73 @@ int launch_any_bn(int BN, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUt
   return PE_ERR_ARG;
 }
 
+template <int BN, typename OutT>
+int launch_pair_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, int M,
+                       int N, int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin,
+                       float alpha, float beta, int vec_ok, int* status, cudaStream_t s) {
+  if constexpr ((BN / 2) % 64 == 0) {
+    if (b_mn) {
+      if (a_mn)
+        return launch_pair<BN, true, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
+                                                 vec_ok, status, s);
+      return launch_pair<BN, false, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
+                                                vec_ok, status, s);
+    }
+  } else {
+    if (b_mn) {
+      set_error("gemm: pair tile width %d needs a K-major B operand", BN);
+      return PE_ERR_ARG;
+    }
+  }
+  if (a_mn)
+    return launch_pair<BN, true, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
+                                              vec_ok, status, s);
+  return launch_pair<BN, false, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
+                                             vec_ok, status, s);
+}
+
+template <typename OutT>
+int launch_pair_any_bn(int BN, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                       int M, int N, int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin,
+                       float alpha, float beta, int vec_ok, int* status, cudaStream_t s) {
+  switch (BN) {
+    case 256: return launch_pair_majors<256, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    case 192: return launch_pair_majors<192, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    case 128: return launch_pair_majors<128, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    default: break;
+  }
+  set_error("gemm: unsupported pair tile width %d", BN);
+  return PE_ERR_ARG;
+}
+
+// The CTA-pair kernel takes problems with at least this many rows (below it half
+// of a 256-row pair tile would mostly be padding).
+constexpr int64_t kPairMinRows = 512;
+
+bool use_pair(int64_t M, int mode) {
+  if (mode == 1) return false;
+  if (mode == 2) return true;
+  return M >= kPairMinRows;
+}
+
 int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
             const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
             const void* Cin, int64_t ldcin, float alpha, float beta, int* status,
-            cudaStream_t stream, int force_bn) {
+            cudaStream_t stream, int force_bn, int mode) {
   const bool a_mn = a_sk != 1;
   const bool b_mn = b_sk != 1;
-  const int BN = force_bn > 0 ? force_bn : choose_bn(M, N, b_mn, sm_count());
-  PE_CHECK_ARG(!(b_mn && BN % 64 != 0), "gemm: tile width %d needs a K-major B operand", BN);
+  const bool pair = use_pair(M, mode);
+  int BN;
+  if (pair) {
+    BN = force_bn > 0 ? force_bn : choose_bn_pair(M, N, b_mn, sm_count() / 2);
+    PE_CHECK_ARG(BN == 128 || BN == 192 || BN == 256, "gemm: pair tile width %d not 128/192/256",
+                 BN);
+    PE_CHECK_ARG(!(b_mn && (BN / 2) % 64 != 0), "gemm: pair tile width %d needs a K-major B", BN);
+  } else {
+    BN = force_bn > 0 ? force_bn : choose_bn(M, N, b_mn, sm_count());
+    PE_CHECK_ARG(!(b_mn && BN % 64 != 0), "gemm: tile width %d needs a K-major B operand", BN);
+  }
+  const uint32_t b_box = pair ? (uint32_t)(BN / 2) : (uint32_t)BN;
   CUtensorMap ta, tb;
   int rc;
   if (!a_mn)
@@ -452,7 +795,7 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
     rc = make_tmap_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)a_sk * 2, 64, 64);
   if (rc) return rc;
   if (!b_mn)
-    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)b_sn * 2, 64, (uint32_t)BN);
+    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)b_sn * 2, 64, b_box);
   else
     rc = make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)b_sk * 2, 64, 64);
   if (rc) return rc;
@@ -460,6 +803,13 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
   const int vec_ok = (ldc * esz) % 16 == 0 && al16(C) &&
                      (!Cin || ((ldcin * esz) % 16 == 0 && al16(Cin)));
   const int m = (int)M, n = (int)N, k = (int)K;
+  if (pair) {
+    if (c_dtype == PE_F32)
+      return launch_pair_any_bn<float>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha,
+                                       beta, vec_ok, status, stream);
+    return launch_pair_any_bn<__nv_bfloat16>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin,
+                                             alpha, beta, vec_ok, status, stream);
+  }
   if (c_dtype == PE_F32)
     return launch_any_bn<float>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta,
                                 vec_ok, status, stream);
@@ -474,11 +824,16 @@ int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t
                    al16(A) && al16(B) && al16(C),
                "gemm (logits + row stats): operands must be 16-byte aligned bf16");
   PE_CHECK_ARG(stats_ld >= (N + 255) / 256, "gemm (logits + row stats): stats_ld too small");
+  const bool pair = use_pair(M, 0);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
-  if (!rc) rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, 64, 256);
+  if (!rc)
+    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, 64, pair ? 128 : 256);
   if (rc) return rc;
   EpiArgs ea{stats, stats_ld, nullptr};
+  if (pair)
+    return launch_pair<256, false, false, __nv_bfloat16, EPI_STATS>(
+        ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
   return launch<256, false, false, __nv_bfloat16, EPI_STATS>(ta, tb, (int)M, (int)N, (int)K, C, ldc,
                                                              nullptr, 0, 1.f, 0.f, 1, status,
                                                              stream, ea);
@@ -495,6 +850,9 @@ int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t
   if (!rc) rc = make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)b_sk * 2, 64, 64);
   if (rc) return rc;
   EpiArgs ea{nullptr, 0, rowscale};
+  if (use_pair(M, 0))
+    return launch_pair<256, false, true, float, EPI_ROWSCALE>(
+        ta, tb, (int)M, (int)N, (int)K, C, ldc, Cin, ldc, 1.f, 0.f, 1, status, stream, ea);
   return launch<256, false, true, float, EPI_ROWSCALE>(ta, tb, (int)M, (int)N, (int)K, C, ldc, Cin,
                                                        ldc, 1.f, 0.f, 1, status, stream, ea);
 }
@@ -507,20 +865,22 @@ int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm
   PE_CHECK_ARG(ldc >= N, "gemm: ldc < N");
   if (M == 0 || N == 0) return PE_OK;
   PE_CHECK_ARG(K > 0, "gemm: K == 0 is not supported");
-  const int force_bn = algo >> 8;
+  const int force_bn = (algo >> 8) & 0x1ff;
+  const int mode = (algo >> 20) & 3;  // 0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles
   algo &= 0xff;
   PE_CHECK_ARG(force_bn == 0 || force_bn == 128 || force_bn == 160 || force_bn == 192 ||
                    force_bn == 224 || force_bn == 256,
                "gemm: forced tile width %d not one of 128/160/192/224/256", force_bn);
+  PE_CHECK_ARG(mode != 3, "gemm: tile mode 3 is not defined");
   const bool tc_ok = gemm_tc_eligible(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, c_dtype);
   if (algo == PE_ALGO_TCGEN05) {
     PE_CHECK_ARG(tc_ok, "gemm: operands not eligible for the tcgen05 path");
     return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
-                   beta, status, stream, force_bn);
+                   beta, status, stream, force_bn, mode);
   }
   if (algo == PE_ALGO_AUTO && tc_ok)
     return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
-                   beta, status, stream, force_bn);
+                   beta, status, stream, force_bn, mode);
   return gemm_simt(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin,
                    alpha, beta, stream);
 }

@@ -218,15 +218,44 @@ unsigned grid_for(int64_t n) {
 namespace pe {
 namespace {
 
-constexpr int64_t kFastChunk = 16384;
+constexpr int64_t kFastChunk = 16384;  // vocabulary rows per logits chunk (default)
+constexpr int64_t kRowGroup = 4096;    // loss rows per group (default)
+constexpr int64_t kMaxChunk = 16384;
+constexpr int64_t kMaxGroup = 8192;
 constexpr int kStatTile = 256;
+static_assert(kMaxChunk / kStatTile <= 64, "combine_kernel folds at most 64 tile stats");
 
-struct FastLayout {
-  size_t m, l, zlab, lse, alpha, stats, Z, dH, total;
+// Rows of the loss are processed in groups so one group's logits chunk
+// (group x chunk bf16) stays mostly resident in L2 between the logits GEMM, the
+// combine pass and the dH GEMM.  ``algo`` bits 8-15 override the chunk (units of
+// 1024 vocabulary rows) and bits 16-23 the group (units of 256 loss rows).
+struct FastPlan {
+  int64_t vc, rg;
 };
 
+FastPlan fast_plan_of(int64_t R, int64_t V, int algo) {
+  int64_t vc = ((algo >> 8) & 0xff) ? ((algo >> 8) & 0xff) * 1024 : kFastChunk;
+  int64_t rg = ((algo >> 16) & 0xff) ? ((algo >> 16) & 0xff) * 256 : kRowGroup;
+  vc = vc > kMaxChunk ? kMaxChunk : vc;
+  rg = rg > kMaxGroup ? kMaxGroup : rg;
+  if (V < vc) vc = (V + 7) / 8 * 8;
+  if (R <= rg) {
+    rg = R;
+  } else {  // equal groups, each a multiple of the 128-row tile
+    const int64_t ng = (R + rg - 1) / rg;
+    rg = ((R + ng - 1) / ng + 127) / 128 * 128;
+  }
+  return {vc, rg};
+}
+
+struct FastLayout {
+  size_t m, l, zlab, lse, alpha, stats[2], Z[2], dH, total;
+};
+
+// sized for the largest plan any ``algo`` can select, so one workspace serves all
 FastLayout fast_layout_of(int64_t R, int64_t H, int64_t V) {
-  const int64_t vc = V < kFastChunk ? (V + 7) / 8 * 8 : kFastChunk;
+  const int64_t vc = V < kMaxChunk ? (V + 7) / 8 * 8 : kMaxChunk;
+  const int64_t rg = R < kMaxGroup ? R : kMaxGroup;
   const int64_t nt = (vc + kStatTile - 1) / kStatTile;
   FastLayout L{};
   size_t off = 0;
@@ -240,15 +269,18 @@ FastLayout fast_layout_of(int64_t R, int64_t H, int64_t V) {
   L.zlab = take(4 * R);
   L.lse = take(4 * R);
   L.alpha = take(4 * R);
-  L.stats = take(8 * (size_t)R * nt);
-  L.Z = take(2 * (size_t)R * vc);
+  for (int b = 0; b < 2; ++b) {  // double-buffered: chunk j+1's logits overlap chunk j
+    L.stats[b] = take(8 * (size_t)rg * nt);
+    L.Z[b] = take(2 * (size_t)rg * vc);
+  }
   L.dH = take(4 * (size_t)R * H);
   L.total = off;
   return L;
 }
 
 // per row: fold this chunk's tile stats into (m, l), record the rescale factor,
-// pick the label logit, and overwrite the chunk's logits with exp(z - m_new)
+// pick the label logit, and overwrite the chunk's logits with exp(z - m_new).
+// Warp 0 folds the (at most 64) tile stats two per lane.
 __global__ void __launch_bounds__(256)
 combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __restrict__ stats,
                __nv_bfloat16* __restrict__ Z, int64_t ldz, const int64_t* __restrict__ labels,
@@ -257,18 +289,26 @@ combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __res
   const int64_t r = blockIdx.x;
   const int64_t lab = labels[r];
   __nv_bfloat16* z = Z + r * ldz;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     const float2* st = stats + r * stats_ld;
     const float m_old = m[r];
-    float mn = m_old;
-    for (int t = 0; t < nt; ++t) mn = fmaxf(mn, st[t].x);
-    float acc = m_old == -INFINITY ? 0.f : l[r] * expf(m_old - mn);
-    for (int t = 0; t < nt; ++t) acc += st[t].y * expf(st[t].x - mn);
-    l[r] = acc;
-    alpha[r] = m_old == -INFINITY ? 0.f : expf(m_old - mn);
-    m[r] = mn;
-    if (lab >= v0 && lab < v0 + vc) zlab[r] = __bfloat162float(z[lab - v0]);
-    s_mnew = mn;
+    // nt <= 64 (kMaxChunk / kStatTile): lanes take tiles lane and lane + 32
+    const float2 s0 = lane < nt ? st[lane] : make_float2(-INFINITY, 0.f);
+    const float2 s1 = lane + 32 < nt ? st[lane + 32] : make_float2(-INFINITY, 0.f);
+    const float mn = fmaxf(m_old, warp_max(fmaxf(s0.x, s1.x)));
+    float part = 0.f;
+    if (s0.x != -INFINITY) part += s0.y * expf(s0.x - mn);
+    if (s1.x != -INFINITY) part += s1.y * expf(s1.x - mn);
+    const float tile_sum = warp_sum(part);
+    if (lane == 0) {
+      const float keep = m_old == -INFINITY ? 0.f : expf(m_old - mn);
+      l[r] = l[r] * keep + tile_sum;
+      alpha[r] = keep;
+      m[r] = mn;
+      if (lab >= v0 && lab < v0 + vc) zlab[r] = __bfloat162float(z[lab - v0]);
+      s_mnew = mn;
+    }
   }
   __syncthreads();
   const float mn = s_mnew;
@@ -333,35 +373,66 @@ bool fast_eligible(int dtype, int64_t H, int64_t V, const void* h, int64_t ldh, 
          V % 8 == 0 && ldh % 8 == 0 && lddh % 8 == 0 && a16(h) && a16(W) && a16(dh);
 }
 
+// Software pipeline over (row group, vocabulary chunk) steps t: the logits GEMM of
+// step t runs on the caller's stream while the combine pass and dH GEMM of step
+// t-1 run on a side stream, so one GEMM's last partial wave and the combine pass
+// overlap the other GEMM.  Z and the tile stats are double-buffered; the logits
+// GEMM of step t waits for the dH GEMM of step t-2 (same buffer).
 int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, const void* W,
                 const int64_t* labels, float grad_scale, void* dh, int64_t lddh, float* loss_sum,
-                uint8_t* ws, int* status, cudaStream_t st) {
+                uint8_t* ws, int algo, int* status, cudaStream_t st) {
   const FastLayout L = fast_layout_of(R, H, V);
+  const FastPlan P = fast_plan_of(R, V, algo);
   float* m = (float*)(ws + L.m);
   float* l = (float*)(ws + L.l);
   float* zlab = (float*)(ws + L.zlab);
   float* lse = (float*)(ws + L.lse);
   float* alpha = (float*)(ws + L.alpha);
-  float2* stats = (float2*)(ws + L.stats);
-  __nv_bfloat16* Z = (__nv_bfloat16*)(ws + L.Z);
+  float2* stats[2] = {(float2*)(ws + L.stats[0]), (float2*)(ws + L.stats[1])};
+  __nv_bfloat16* Z[2] = {(__nv_bfloat16*)(ws + L.Z[0]), (__nv_bfloat16*)(ws + L.Z[1])};
   float* dH = (float*)(ws + L.dH);
-  const int64_t VC = V < kFastChunk ? (V + 7) / 8 * 8 : kFastChunk;
+  const int64_t VC = P.vc;
   const int nt_max = (int)((VC + kStatTile - 1) / kStatTile);
+  cudaStream_t side = side_stream(0);
+  cudaEvent_t ev_fork = pool_event(0), ev_join = pool_event(1);
+  cudaEvent_t ev_logits[2] = {pool_event(2), pool_event(3)};
+  cudaEvent_t ev_dh[2] = {pool_event(4), pool_event(5)};
+  if (!side || !ev_fork || !ev_join || !ev_logits[0] || !ev_logits[1] || !ev_dh[0] || !ev_dh[1]) {
+    set_error("lmhead_ce: could not create the side stream or its events");
+    return PE_ERR_CUDA;
+  }
   fast_init_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, zlab);
   PE_LAUNCHED();
-  for (int64_t v0 = 0; v0 < V; v0 += VC) {
-    const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
-    const int nt = (int)((vc + kStatTile - 1) / kStatTile);
-    const __nv_bfloat16* Wc = (const __nv_bfloat16*)W + v0 * H;
-    int rc = gemm_tc_logits_stats(R, vc, H, h, ldh, Wc, H, Z, VC, stats, nt_max, status, st);
-    if (rc) return rc;
-    combine_kernel<<<(unsigned)R, 256, 0, st>>>(vc, v0, nt, nt_max, stats, Z, VC, labels, m, l,
-                                                zlab, alpha);
-    PE_LAUNCHED();
-    rc = gemm_tc_rowscale_acc(R, H, vc, Z, VC, Wc, H, dH, H, v0 > 0 ? dH : nullptr, alpha, status,
-                              st);
-    if (rc) return rc;
+  PE_CUDA_TRY(cudaEventRecord(ev_fork, st));
+  PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_fork, 0));
+  int64_t t = 0;
+  for (int64_t r0 = 0; r0 < R; r0 += P.rg) {
+    const int64_t rg = (R - r0) < P.rg ? (R - r0) : P.rg;
+    const void* hg = (const __nv_bfloat16*)h + r0 * ldh;
+    float* dHg = dH + r0 * H;
+    for (int64_t v0 = 0; v0 < V; v0 += VC, ++t) {
+      const int b = (int)(t & 1);
+      const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
+      const int nt = (int)((vc + kStatTile - 1) / kStatTile);
+      const __nv_bfloat16* Wc = (const __nv_bfloat16*)W + v0 * H;
+      if (t >= 2) PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_dh[b], 0));
+      int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Z[b], VC, stats[b], nt_max,
+                                    status, st);
+      if (rc) return rc;
+      PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
+      PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
+      combine_kernel<<<(unsigned)rg, 256, 0, side>>>(vc, v0, nt, nt_max, stats[b], Z[b], VC,
+                                                     labels + r0, m + r0, l + r0, zlab + r0,
+                                                     alpha + r0);
+      PE_LAUNCHED();
+      rc = gemm_tc_rowscale_acc(rg, H, vc, Z[b], VC, Wc, H, dHg, H, v0 > 0 ? dHg : nullptr,
+                                alpha + r0, status, side);
+      if (rc) return rc;
+      PE_CUDA_TRY(cudaEventRecord(ev_dh[b], side));
+    }
   }
+  PE_CUDA_TRY(cudaEventRecord(ev_join, side));
+  PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_join, 0));
   finalize_kernel<<<1, kThreads, 0, st>>>(R, labels, m, l, zlab, nullptr, nullptr, nullptr, lse,
                                           nullptr, loss_sum);
   PE_LAUNCHED();
@@ -397,12 +468,14 @@ extern "C" int pe_lmhead_ce(int dtype, int64_t R, int64_t H, int64_t V, const vo
   if (R == 0) return PE_OK;
   const int soft = teacher != nullptr;
   cudaStream_t st = as_stream(stream);
+  const int tuning = algo;  // chunk / row-group overrides of the fast path
+  algo &= 0xff;
   if (fast_eligible(dtype, H, V, h, ldh, W, teacher, dh, lddh, algo)) {
     const size_t need = fast_layout_of(R, H, V).total;
     PE_CHECK_ARG(workspace && workspace_bytes >= need, "lmhead_ce: workspace of %zu bytes needed",
                  need);
     return lmhead_fast(R, H, V, h, ldh, W, labels, grad_scale, dh, lddh, loss_sum,
-                       static_cast<uint8_t*>(workspace), status, st);
+                       static_cast<uint8_t*>(workspace), tuning, status, st);
   }
   const Layout L = layout_of(dtype, R, H, V, soft);
   PE_CHECK_ARG(workspace && workspace_bytes >= L.total,

@@ -124,14 +124,20 @@ class FlatParams:
 
 
 @dataclass
-class _SegmentPlan:
-    a0: int
-    a1: int
-    q: int
-    pos: torch.Tensor  # int64 [Q] rotary position per slot
-    loss_idx: torch.Tensor  # int64 [R] slots carrying a loss
-    tgt: torch.Tensor  # int64 [R] target position of each loss slot
-    rows: int
+class _PassPlan:
+    """Segments executed together: their slot rows stacked segment after segment
+    (each segment's rows stay contiguous, ``[real 0..a1) | MTP anchor-major]``)."""
+
+    segs: list  # (a0, a1, Q, row offset) per segment
+    q: int  # stacked rows
+    pos: torch.Tensor  # int64 [q] rotary position per row
+    loss_idx: torch.Tensor  # int64 [R] stacked rows carrying a loss
+    tgt: torch.Tensor  # int64 [R] target position of each loss row
+    rows: int  # R
+    real_tok: torch.Tensor  # int64 [Rt] token index of each stacked real row
+    real_row: torch.Tensor  # int64 [Rt] its row in the stack
+    nreal: int  # Rt
+    has_pred: bool  # some segment has MTP slots
 
 
 def count_loss_slots(n: int, k: int, prompt_len: int = 0) -> int:
@@ -154,33 +160,79 @@ class StepEngine:
     def __init__(self, drafter):
         self.d = drafter
         self.flat = FlatParams(drafter)
-        self._plans: dict[tuple, _SegmentPlan] = {}
+        self._plans: dict[tuple, _PassPlan] = {}
+        # device bytes of activations one pass of stacked segments may hold
+        self.pass_bytes = 24 << 30
         self.loss_sum = torch.zeros(1, dtype=torch.float32, device=self.flat.device)
 
     # --------------------------------------------------------------- plans --
-    def _plan(self, a0: int, a1: int, n: int, prompt_len: int) -> _SegmentPlan:
-        key = (a0, a1, n, prompt_len)
-        p = self._plans.get(key)
-        if p is not None:
-            return p
+    def _segment_arrays(self, a0: int, a1: int, n: int, prompt_len: int):
+        """Slots of one segment (reference ``partition.py:41-55``, ``:101-104``):
+        rotary positions, loss-slot indices and their target positions."""
         k = self.d.max_depth
         anchor = np.concatenate([np.arange(a1), np.repeat(np.arange(a0, a1), k - 1)])
         depth = np.concatenate([np.zeros(a1, dtype=np.int64), np.tile(np.arange(1, k), a1 - a0)])
         tgt = anchor + 1 + depth
         keep = (anchor >= a0) & (tgt < n) & (tgt >= prompt_len)
         idx = np.nonzero(keep)[0].astype(np.int64)
+        return (anchor + depth).astype(np.int64), idx, tgt[idx].astype(np.int64)
+
+    def _pass_plan(self, bounds: tuple, n: int, prompt_len: int) -> _PassPlan:
+        key = (bounds, n, prompt_len)
+        p = self._plans.get(key)
+        if p is not None:
+            return p
+        segs, pos, idx, tgt, rtok, rrow = [], [], [], [], [], []
+        off = 0
+        for a0, a1 in bounds:
+            sp, si, st = self._segment_arrays(a0, a1, n, prompt_len)
+            q = int(sp.shape[0])
+            segs.append((a0, a1, q, off))
+            pos.append(sp)
+            idx.append(si + off)
+            tgt.append(st)
+            rtok.append(np.arange(a1, dtype=np.int64))
+            rrow.append(off + np.arange(a1, dtype=np.int64))
+            off += q
         dev = self.flat.device
-        p = _SegmentPlan(
-            a0, a1, int(anchor.shape[0]),
-            torch.from_numpy((anchor + depth).astype(np.int64)).to(dev),
-            torch.from_numpy(idx).to(dev),
-            torch.from_numpy(tgt[idx].astype(np.int64)).to(dev),
-            int(idx.size),
-        )
+
+        def t(parts):
+            return torch.from_numpy(np.concatenate(parts)).to(dev)
+
+        loss_idx = t(idx)
+        real_tok = t(rtok)
+        p = _PassPlan(segs, off, t(pos), loss_idx, t(tgt), int(loss_idx.numel()), real_tok,
+                      t(rrow), int(real_tok.numel()), any(q > a1 for _, a1, q, _ in segs))
         if len(self._plans) > 256:
             self._plans.clear()
         self._plans[key] = p
         return p
+
+    def _row_bytes(self) -> int:
+        """Device bytes one stacked slot row holds during a pass: the saved layer
+        activations plus the widest transient gradients."""
+        d, esz = self.d, self.flat.grad.element_size()
+        H, I = d.hidden, d.intermediate
+        cqkv = (d.n_heads + 2 * d.n_kv_heads) * d.head_dim
+        per_layer = esz * (4 * H + cqkv + d.n_heads * d.head_dim + 3 * I) + 4 * (2 + d.n_heads)
+        return per_layer * len(d.layers) + esz * (3 * I + cqkv + 4 * H) + 8 * H
+
+    def _passes(self, bounds: list) -> list:
+        """Consecutive segments grouped so each pass stays within ``pass_bytes``
+        (a single segment larger than the budget runs alone)."""
+        k = self.d.max_depth
+        limit = max(1, self.pass_bytes // self._row_bytes())
+        groups, cur, rows = [], [], 0
+        for a0, a1 in bounds:
+            q = a1 + (a1 - a0) * (k - 1)
+            if cur and rows + q > limit:
+                groups.append(cur)
+                cur, rows = [], 0
+            cur.append((a0, a1))
+            rows += q
+        if cur:
+            groups.append(cur)
+        return groups
 
     # ---------------------------------------------------------------- step --
     def run(self, input_ids, features, num_segments=1, loss_scale=1.0, prompt_len=0,
@@ -205,16 +257,17 @@ class StepEngine:
         self.loss_sum.zero_()
         scale = loss_scale / total
         ran = mask_slots = False
+        live = []
         for a0, a1 in segment_bounds(n, num_segments):
             # a segment contributes iff some target t in [a0+1, a1+k-1] is in [prompt_len, n)
             if max(a0 + 1, prompt_len) > min(a1 + k - 1, n - 1):
                 continue
-            plan = self._plan(a0, a1, n, prompt_len)
-            if plan.rows == 0:
-                continue
-            self._segment(plan, input_ids, features, scale, teacher_labels, teacher_hidden)
+            live.append((a0, a1))
+        for group in self._passes(live):
+            plan = self._pass_plan(tuple(group), n, prompt_len)
+            self._pass(plan, input_ids, features, scale, teacher_labels, teacher_hidden)
             ran = True
-            mask_slots = mask_slots or plan.q > plan.a1
+            mask_slots = mask_slots or plan.has_pred
         if fresh:
             untouched = set(fresh) if not ran else (
                 set() if mask_slots else {"mask_emb", "h_shared"} & set(fresh))
@@ -224,8 +277,11 @@ class StepEngine:
             return None
         return float(self.loss_sum.item()) / total
 
-    # ------------------------------------------------------------- segment --
-    def _segment(self, plan: _SegmentPlan, ids, feats, scale, teacher_labels, teacher_hidden):
+    # ---------------------------------------------------------------- pass --
+    def _pass(self, plan: _PassPlan, ids, feats, scale, teacher_labels, teacher_hidden):
+        """Forward and backward of the stacked segments of one pass.  Every GEMM,
+        norm and element-wise op runs once over all stacked rows; attention runs
+        per segment on its row range with that segment's mask."""
         d, fp = self.d, self.flat
         dt, dev = fp.dtype, fp.device
         H, I = d.hidden, d.intermediate
@@ -233,11 +289,13 @@ class StepEngine:
         qc, kc = nh * hd, nkv * hd
         cqkv = qc + 2 * kc
         k = d.max_depth
-        a0, a1, Q = plan.a0, plan.a1, plan.q
+        Q, Rt = plan.q, plan.nreal
         nfl = d.num_feature_layers
         eps = d.eps
         E, Wh, wfinal = d.frozen_heads()
-        layout = ops.AttnLayout(L.LAYOUT_PARTITION, a0=a0, a1=a1, k=k)
+        single = len(plan.segs) == 1
+        layouts = [(ops.AttnLayout(L.LAYOUT_PARTITION, a0=a0, a1=a1, k=k), q, off)
+                   for a0, a1, q, off in plan.segs]
 
         def W(name, shape=None):
             return fp.view(name, shape)
@@ -246,19 +304,30 @@ class StepEngine:
             return fp.view(name, shape, grad=True)
 
         # ---------------- input (reference drafter.py:126-137) ----------------
+        # real rows of every segment: [embedding | feat_proj(RMSNorm(features))] -> in_proj
         x = torch.empty(Q, H, dtype=dt, device=dev)
-        u = torch.empty(a1, 2 * H, dtype=dt, device=dev)
-        ops.embed_rows(ids[:a1], E, u[:, :H])
-        f_in = feats[:a1].reshape(a1 * nfl, H)
+        u = torch.empty(Rt, 2 * H, dtype=dt, device=dev)
+        if single:
+            a1 = plan.segs[0][1]
+            ops.embed_rows(ids[:a1], E, u[:, :H])
+            f_in = feats[:a1].reshape(a1 * nfl, H)
+        else:
+            ops.embed_rows(ids.index_select(0, plan.real_tok), E, u[:, :H])
+            f_in = ops.gather_rows(feats, plan.real_tok).view(Rt * nfl, H)
         fn, rstd_f = ops.rmsnorm_fwd(f_in, W("feat_norm.weight"), eps)
         w_fp = W("feat_proj.weight", (H, nfl * H))
         w_in = W("in_proj.weight", (H, 2 * H))
-        ops.linear(fn.view(a1, nfl * H), w_fp, out=u[:, H:])
-        ops.linear(u, w_in, out=x[:a1])
+        ops.linear(fn.view(Rt, nfl * H), w_fp, out=u[:, H:])
+        if single:
+            ops.linear(u, w_in, out=x[:Rt])
+        else:
+            ops.scatter_rows(ops.linear(u, w_in), plan.real_row, x)
         cat_vec = fp.span("mask_emb", "h_shared", 2 * H)  # [1, 2H], adjacent in the flat buffer
-        if Q > a1:
+        if plan.has_pred:
             vec = ops.linear(cat_vec, w_in)  # [1, H]
-            ops.fill_rows(vec[0], x[a1:])
+            for _, a1, q, off in plan.segs:
+                if q > a1:
+                    ops.fill_rows(vec[0], x[off + a1 : off + q])
 
         # ---------------- layers (reference nn.py:119-124) ----------------
         saved = []
@@ -271,15 +340,19 @@ class StepEngine:
             xn, r1 = ops.rmsnorm_fwd(x, W(p + "input_norm.weight"), eps)
             qkv = ops.linear(xn, w_qkv)
             ops.rope_(qkv, nh + nkv, hd, plan.pos, d.rope_theta)
-            q3 = qkv.view(1, Q, cqkv)
-            o, lse = ops.attn_fwd(q3[:, :, :qc], q3[:, :, qc : qc + kc], q3[:, :, qc + kc :],
-                                  nh, nkv, hd, layout)
-            x2 = ops.linear(o.view(Q, qc), w_o, residual=x)
+            o = torch.empty(Q, qc, dtype=dt, device=dev)
+            lses = []
+            for layout, q, off in layouts:
+                q3 = qkv[off : off + q].view(1, q, cqkv)
+                _, lse = ops.attn_fwd(q3[:, :, :qc], q3[:, :, qc : qc + kc], q3[:, :, qc + kc :],
+                                      nh, nkv, hd, layout, o=o[off : off + q].view(1, q, qc))
+                lses.append(lse)
+            x2 = ops.linear(o, w_o, residual=x)
             xn2, r2 = ops.rmsnorm_fwd(x2, W(p + "post_norm.weight"), eps)
             gu = ops.linear(xn2, w_gu)
             act = ops.swiglu_fwd(gu, I)
             x3 = ops.linear(act, w_dn, residual=x2)
-            saved.append((x, xn, r1, qkv, o, lse, x2, xn2, r2, gu, act))
+            saved.append((x, xn, r1, qkv, o, lses, x2, xn2, r2, gu, act))
             x = x3
         hf, rf = ops.rmsnorm_fwd(x, wfinal, eps)
 
@@ -302,7 +375,7 @@ class StepEngine:
         # ---------------- layers backward ----------------
         for li in reversed(range(len(d.layers))):
             p = f"layers.{li}."
-            x_in, xn, r1, qkv, o, lse, x2, xn2, r2, gu, act = saved[li]
+            x_in, xn, r1, qkv, o, lses, x2, xn2, r2, gu, act = saved[li]
             w_qkv = fp.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight", H)
             w_o = W(p + "attn.o_proj.weight", (H, qc))
             w_gu = fp.span(p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight", H)
@@ -320,14 +393,15 @@ class StepEngine:
             ops.colsum_into(part, G(p + "post_norm.weight"), accumulate=True)
             # x2 = x + o @ W_o^T
             do = ops.linear_dgrad(dx2, w_o)
-            ops.linear_wgrad(dx2, o.view(Q, qc), grad=G(p + "attn.o_proj.weight", (H, qc)),
-                             accumulate=True)
+            ops.linear_wgrad(dx2, o, grad=G(p + "attn.o_proj.weight", (H, qc)), accumulate=True)
             dqkv = torch.empty(Q, cqkv, dtype=dt, device=dev)
-            q3 = qkv.view(1, Q, cqkv)
-            d3 = dqkv.view(1, Q, cqkv)
-            ops.attn_bwd(q3[:, :, :qc], q3[:, :, qc : qc + kc], q3[:, :, qc + kc :], o,
-                         do.view(1, Q, qc), lse, nh, nkv, hd, layout,
-                         dq=d3[:, :, :qc], dk=d3[:, :, qc : qc + kc], dv=d3[:, :, qc + kc :])
+            for (layout, q, off), lse in zip(layouts, lses):
+                q3 = qkv[off : off + q].view(1, q, cqkv)
+                d3 = dqkv[off : off + q].view(1, q, cqkv)
+                ops.attn_bwd(q3[:, :, :qc], q3[:, :, qc : qc + kc], q3[:, :, qc + kc :],
+                             o[off : off + q].view(1, q, qc), do[off : off + q].view(1, q, qc),
+                             lse, nh, nkv, hd, layout,
+                             dq=d3[:, :, :qc], dk=d3[:, :, qc : qc + kc], dv=d3[:, :, qc + kc :])
             ops.rope_(dqkv, nh + nkv, hd, plan.pos, d.rope_theta, inverse=True)
             dxn = ops.linear_dgrad(dqkv, w_qkv)
             ops.linear_wgrad(
@@ -339,22 +413,25 @@ class StepEngine:
 
         # ---------------- input backward ----------------
         g_in = G("in_proj.weight", (H, 2 * H))
-        if Q > a1:
+        if plan.has_pred:
             # the shared row is broadcast to every prediction slot: its gradient is the
-            # column sum, rounded to the parameter dtype like autograd's expand backward
-            dvec32 = ops.rowsum_cols(dx[a1:])
+            # column sum over those slots, rounded to the parameter dtype like
+            # autograd's expand backward
+            sums = [ops.rowsum_cols(dx[off + a1 : off + q])
+                    for _, a1, q, off in plan.segs if q > a1]
+            dvec32 = sums[0] if len(sums) == 1 else torch.stack(sums).sum(0)
             dvec = torch.empty(1, H, dtype=dt, device=dev)
             ops.cast_from_f32(dvec32, dvec)
             ops.linear_wgrad(dvec, cat_vec, grad=g_in, accumulate=True)
             g_cat = fp.span("mask_emb", "h_shared", 2 * H, grad=True)
             ops.linear_dgrad(dvec, w_in, out=g_cat, residual=g_cat)
-        dreal = dx[:a1]
+        dreal = dx[:Rt] if single else ops.gather_rows(dx, plan.real_row)
         dfeat = ops.linear_dgrad(dreal, w_in[:, H:])
         ops.linear_wgrad(dreal, u, grad=g_in, accumulate=True)
         dfn = ops.linear_dgrad(dfeat, w_fp)
-        ops.linear_wgrad(dfeat, fn.view(a1, nfl * H), grad=G("feat_proj.weight", (H, nfl * H)),
+        ops.linear_wgrad(dfeat, fn.view(Rt, nfl * H), grad=G("feat_proj.weight", (H, nfl * H)),
                          accumulate=True)
-        _, part = ops.rmsnorm_bwd(dfn.view(a1 * nfl, H), f_in, W("feat_norm.weight"), rstd_f)
+        _, part = ops.rmsnorm_bwd(dfn.view(Rt * nfl, H), f_in, W("feat_norm.weight"), rstd_f)
         ops.colsum_into(part, G("feat_norm.weight"), accumulate=True)
 
 

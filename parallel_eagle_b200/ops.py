@@ -191,12 +191,16 @@ def _bsq(t: torch.Tensor):
     return t.stride(0), t.stride(1)
 
 
-def attn_fwd(q, k, v, n_heads, n_kv_heads, head_dim, layout: AttnLayout, algo=L.ALGO_AUTO):
-    """q ``[B, S, Hq*hd]``, k/v ``[B, S, Hkv*hd]`` (row views; last stride 1)."""
+def attn_fwd(q, k, v, n_heads, n_kv_heads, head_dim, layout: AttnLayout, algo=L.ALGO_AUTO,
+             o=None, lse=None):
+    """q ``[B, S, Hq*hd]``, k/v ``[B, S, Hkv*hd]`` (row views; last stride 1).  ``o``
+    (a row view like q) and ``lse`` (fp32 ``[B, Hq, S]``, contiguous) may be given."""
     L.require_cuda(q, k, v)
     B, S = q.shape[0], q.shape[1]
-    o = torch.empty(B, S, n_heads * head_dim, dtype=q.dtype, device=q.device)
-    lse = torch.empty(B, n_heads, S, dtype=torch.float32, device=q.device)
+    if o is None:
+        o = torch.empty(B, S, n_heads * head_dim, dtype=q.dtype, device=q.device)
+    if lse is None:
+        lse = torch.empty(B, n_heads, S, dtype=torch.float32, device=q.device)
     bsb, bsq = layout.bias_strides()
     rc = _lib().pe_attn_fwd(
         L.dtype_code(q.dtype), B, S, n_heads, n_kv_heads, head_dim, q.data_ptr(), *_bsq(q),

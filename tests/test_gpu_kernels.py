@@ -56,15 +56,17 @@ def _operand(rows, cols, mn_major, dtype, seed):
 @pytest.mark.parametrize("a_mn", [False, True])
 @pytest.mark.parametrize("b_mn", [False, True])
 @pytest.mark.parametrize("out_f32", [False, True])
-def test_gemm_tcgen05_matches_fp32(shape, a_mn, b_mn, out_f32):
+@pytest.mark.parametrize("mode", [1, 2])  # 1: single-CTA tiles, 2: CTA-pair (cta_group::2) tiles
+def test_gemm_tcgen05_matches_fp32(shape, a_mn, b_mn, out_f32, mode):
     M, N, K = shape
+    algo = L.ALGO_TCGEN05 | (mode << 20)
     A, (a_sm, a_sk), Ad = _operand(M, K, a_mn, torch.bfloat16, 1)
     B, (b_sn, b_sk), Bd = _operand(N, K, b_mn, torch.bfloat16, 2)
     cdt = torch.float32 if out_f32 else torch.bfloat16
     ldc = _pad8(N)
     C = torch.full((M, ldc), 7.0, dtype=cdt, device=DEV)
     ref = Ad @ Bd.t()
-    ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, algo=L.ALGO_TCGEN05)
+    ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, algo=algo)
     torch.cuda.synchronize()
     ops.check_status(DEV)
     got = C[:, :N].float().cpu()
@@ -73,7 +75,7 @@ def test_gemm_tcgen05_matches_fp32(shape, a_mn, b_mn, out_f32):
     # accumulate: C = 0.5 * A B^T + 1.0 * C
     prev = C[:, :N].float().cpu().clone()
     ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, Cin=C, ldcin=ldc, alpha=0.5,
-             beta=1.0, algo=L.ALGO_TCGEN05)
+             beta=1.0, algo=algo)
     torch.cuda.synchronize()
     assert rel(C[:, :N].float().cpu(), prev + 0.5 * ref) < (1e-5 if out_f32 else 5e-3)
 
@@ -88,6 +90,25 @@ def test_gemm_tcgen05_every_tile_width(bn, a_mn, b_mn):
     B, (b_sn, b_sk), Bd = _operand(N, K, b_mn, torch.bfloat16, 6)
     C = torch.zeros(M, N, dtype=torch.float32, device=DEV)
     ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, N, algo=L.ALGO_TCGEN05 | (bn << 8))
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert rel(C.cpu(), Ad @ Bd.t()) < 1e-5
+
+
+@pytest.mark.parametrize("bn", [128, 192, 256])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M", [300, 1100])
+def test_gemm_tcgen05_pair_tile_widths(bn, a_mn, b_mn, M):
+    # CTA-pair tiles (256 x bn): ragged M leaves the second CTA's rows partly or wholly
+    # outside the matrix; ragged N leaves part of the last tile's B halves empty
+    if b_mn and (bn // 2) % 64:
+        pytest.skip("MN-major B needs a pair tile width whose half is a multiple of 64")
+    N, K = 3584 // 4 + 40, 520
+    A, (a_sm, a_sk), Ad = _operand(M, K, a_mn, torch.bfloat16, 7)
+    B, (b_sn, b_sk), Bd = _operand(N, K, b_mn, torch.bfloat16, 8)
+    C = torch.zeros(M, N, dtype=torch.float32, device=DEV)
+    ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, N,
+             algo=L.ALGO_TCGEN05 | (bn << 8) | (2 << 20))
     torch.cuda.synchronize()
     ops.check_status(DEV)
     assert rel(C.cpu(), Ad @ Bd.t()) < 1e-5
@@ -312,6 +333,28 @@ def test_lmhead_ce_full_vocab_against_torch():
     torch.cuda.synchronize()
     assert abs(loss.item() - lr.item()) / lr.item() < 1e-4
     assert rel(dh.float(), hr.grad.float()) < 2e-2
+
+
+@pytest.mark.parametrize("chunk_k,group_r", [(1, 1), (3, 2), (0, 0)])
+def test_lmhead_ce_row_groups_and_chunks(chunk_k, group_r):
+    # the fast path over several loss-row groups (ragged last group) and several
+    # vocabulary chunks (ragged last chunk): same loss and gradient as one pass
+    R, H, V = 700, 256, 5000
+    h = _rand(R, H, seed=42)
+    W = _rand(V, H, seed=43, scale=0.05)
+    labels = torch.randint(0, V, (R,), generator=torch.Generator().manual_seed(6))
+    labels[5::7] = -100
+    loss = torch.zeros(1, dtype=torch.float32, device=DEV)
+    algo = L.ALGO_AUTO | (chunk_k << 8) | (group_r << 16)
+    dh = ops.lmhead_ce(h, W, labels.to(DEV), 0.01, loss, algo=algo)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    hr = h.float().cpu().requires_grad_(True)
+    z = (hr @ W.float().cpu().t()).bfloat16().float()
+    lr = torch.nn.functional.cross_entropy(z, labels, reduction="sum", ignore_index=-100)
+    (lr * 0.01).backward()
+    assert abs(loss.item() - lr.item()) / lr.item() < 1e-4
+    assert rel(dh.float().cpu(), hr.grad) < 2e-2
 
 
 @pytest.mark.parametrize("V", [300, 304])
