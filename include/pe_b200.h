@@ -97,6 +97,10 @@ int pe_rope(int dtype, int64_t rows, int heads, int head_dim, void* x, int64_t l
  * (reference src/pe/nn.py:66-69,75-80,89,95-100, src/pe/drafter.py:131-137).
  * Cin may alias C (in-place accumulation, e.g. into .grad).  c_dtype is the
  * dtype of C and Cin.
+ * Tuning bits of `algo` above the algorithm code (0 = automatic for each):
+ *   bits 8-17  tile width: 128/160/192/224/256 single-CTA, 128/192/256/384/512 pair
+ *   bits 20-21 1 = single-CTA 128-row tiles, 2 = CTA-pair 256-row tiles (cta_group::2)
+ *   bits 24-29 tile-group size of the L2-aware tile order; bit 30 groups N-tiles
  * ------------------------------------------------------------------------- */
 int pe_gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm,
             int64_t a_sk, const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc,

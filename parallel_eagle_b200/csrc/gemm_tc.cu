@@ -36,6 +36,9 @@ struct EpiArgs {
   float2* stats;
   int stats_ld;
   const float* rowscale;
+  // tile order: 0 automatic; G > 0 groups of G M-tiles (all N-tiles of a group
+  // before the next); G < 0 groups of -G N-tiles (all M-tiles of a group first)
+  int raster;
 };
 
 constexpr uint32_t pow2_at_least(uint32_t x) {
@@ -83,22 +86,30 @@ int choose_bn(int64_t M, int64_t N, bool b_mn, int sms) {
   return best;
 }
 
-// Pair tile width (tiles 256 x BN over the resident clusters): same wave model as
-// choose_bn.  MN-major B halves are loaded in 64-column boxes (BN/2 % 64 == 0).
-int choose_bn_pair(int64_t M, int64_t N, bool b_mn, int clusters) {
+// Pair tile width (tiles 256 x BN over the resident clusters): predicted time =
+// waves x per-tile cost.  Wider tiles stage fewer operand bytes per FLOP through
+// L2 and shared memory, which under the power cap buys clock (the speed factors),
+// but tiles wider than 256 use all of TMEM for one accumulator, so their epilogue
+// is not hidden behind the next tile's main loop: measured on B200, a 512-wide
+// tile's drain costs as much as ~740 K-steps of its main loop with bf16 output
+// (twice that with fp32), so wide tiles win only for long K.  MN-major B
+// sub-tiles need 64-column boxes.
+int choose_bn_pair(int64_t M, int64_t N, int64_t K, bool b_mn, int out_bytes, int clusters) {
   struct Cand {
     int bn;
     float speed;
   };
-  static const Cand cands[] = {{256, 1.00f}, {192, 0.96f}, {128, 0.90f}};
+  static const Cand cands[] = {{512, 1.00f}, {384, 0.97f}, {256, 0.88f}, {192, 0.84f}, {128, 0.78f}};
   const int64_t tm = (M + 2 * BM - 1) / (2 * BM);
   int best = 256;
   double best_t = 1e30;
   for (const Cand& c : cands) {
-    if (b_mn && (c.bn / 2) % 64 != 0) continue;
+    const int nj = c.bn > 256 ? c.bn / 2 : c.bn;
+    if (b_mn && (nj / 2) % 64 != 0) continue;
     const int64_t tiles = tm * ((N + c.bn - 1) / c.bn);
     const int64_t waves = (tiles + clusters - 1) / clusters;
-    const double t = (double)waves * c.bn / c.speed;
+    const double bubble = c.bn > 256 ? 740.0 * (out_bytes / 2.0) * c.bn / 512.0 : 0.0;
+    const double t = (double)waves * c.bn * ((double)K + bubble) / c.speed;
     if (t < best_t - 1e-9) {
       best_t = t;
       best = c.bn;
@@ -108,17 +119,29 @@ int choose_bn_pair(int64_t M, int64_t N, bool b_mn, int clusters) {
 }
 
 // Tiles are walked in groups of G M-tiles (all N-tiles of a group before the next
-// group): the group's A panel and the B panels in flight stay in L2, so each
-// operand is read from HBM about once when the A panel of a group fits in L2.
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int G, int& tm,
-                                            int& tn) {
-  const int per_group = G * tiles_n;
+// group) or, with n_major, groups of G N-tiles: the group's panels of one operand
+// stay in L2 while the other operand streams past them.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int G, bool n_major,
+                                            int& tm, int& tn) {
+  const int outer = n_major ? tiles_n : tiles_m;
+  const int inner = n_major ? tiles_m : tiles_n;
+  const int per_group = G * inner;
   const int g = tile / per_group;
   const int first = g * G;
-  const int gsize = min(tiles_m - first, G);
+  const int gsize = min(outer - first, G);
   const int r = tile - g * per_group;
-  tm = first + r % gsize;
-  tn = r / gsize;
+  const int o = first + r % gsize, i = r / gsize;
+  tm = n_major ? i : o;
+  tn = n_major ? o : i;
+}
+
+// Group size for the tile order: an explicit EpiArgs::raster, else as many M-tiles
+// as keep ~40 MB of A panels resident (at least `min_g`).
+__device__ __forceinline__ int raster_group(int raster, int tiles_m, int tiles_n, int64_t a_panel,
+                                            int min_g, bool& n_major) {
+  n_major = raster < 0;
+  if (raster != 0) return max(1, min(n_major ? -raster : raster, n_major ? tiles_n : tiles_m));
+  return min(tiles_m, max(min_g, (int)((40ll << 20) / a_panel)));
 }
 
 template <typename OutT>
@@ -179,22 +202,24 @@ __device__ __forceinline__ void store_row32(OutT* dst, const OutT* cin, const fl
   }
 }
 
-// Drains one accumulator -- TMEM lanes of this warp, BN fp32 columns starting at
-// column `acc_tmem` -- into row `gm` of C (tile column tn), applying the epilogue.
-template <int BN, typename OutT, int EPI>
-__device__ __forceinline__ void epilogue_tile(uint32_t acc_tmem, int64_t gm, int tn, int M, int N,
-                                              OutT* C, int64_t ldc, const OutT* Cin,
-                                              int64_t ldcin, float alpha, float beta, int vec_ok,
-                                              const EpiArgs& ea) {
+// Drains accumulator columns [c_begin, c_end) -- TMEM lanes of this warp, starting
+// at TMEM column `acc_tmem` -- into row `gm` of C (tile columns from col0),
+// applying the epilogue.  EPI_STATS writes one (max, sum-exp) pair per 128 columns,
+// so c_begin and c_end must then be multiples of 128.
+template <typename OutT, int EPI>
+__device__ __forceinline__ void epilogue_cols(uint32_t acc_tmem, int c_begin, int c_end, int64_t gm,
+                                              int64_t col0, int M, int N, OutT* C, int64_t ldc,
+                                              const OutT* Cin, int64_t ldcin, float alpha,
+                                              float beta, int vec_ok, const EpiArgs& ea) {
   // EPI_ROWSCALE: the accumulated input is scaled per row (online-softmax correction)
   const float beta_row = (EPI == EPI_ROWSCALE && gm < M) ? ea.rowscale[gm] : beta;
-  float m_run = -INFINITY, s_run = 0.f;  // EPI_STATS: running row max / sum-exp
+  float m_run = -INFINITY, s_run = 0.f;  // EPI_STATS: running max / sum-exp of a 128-col chunk
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
+  for (int c0 = c_begin; c0 < c_end; c0 += 32) {
     float v[32];
     tmem_ld32(acc_tmem + c0, v);
     tmem_wait_ld();
-    const int64_t gn0 = (int64_t)tn * BN + c0;
+    const int64_t gn0 = col0 + c0;
     if (gm < M && gn0 < N) {
       const int valid = (N - gn0) < 32 ? (int)(N - gn0) : 32;
       if constexpr (EPI == EPI_STATS) {
@@ -218,9 +243,14 @@ __device__ __forceinline__ void epilogue_tile(uint32_t acc_tmem, int64_t gm, int
                           beta_row, valid, vec_ok != 0);
       }
     }
-  }
-  if constexpr (EPI == EPI_STATS) {
-    if (gm < M && (int64_t)tn * BN < N) ea.stats[gm * ea.stats_ld + tn] = make_float2(m_run, s_run);
+    if constexpr (EPI == EPI_STATS) {
+      if ((c0 & 127) == 96) {  // end of a 128-column chunk
+        const int64_t chunk0 = gn0 - 96;
+        if (gm < M && chunk0 < N) ea.stats[gm * ea.stats_ld + chunk0 / 128] = make_float2(m_run, s_run);
+        m_run = -INFINITY;
+        s_run = 0.f;
+      }
+    }
   }
 }
 
@@ -274,9 +304,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int tiles_n = (N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = (K + BK - 1) / BK;
-  // group as many M-tiles as keep ~40 MB of A panels resident, at least 8
-  const int64_t a_panel = (int64_t)BM * K * 2;
-  const int group_m = min(tiles_m, max(8, (int)((40ll << 20) / a_panel)));
+  bool n_major;
+  const int group_m = raster_group(ea.raster, tiles_m, tiles_n, (int64_t)BM * K * 2, 8, n_major);
 
   if (warp == 0) {
     if (elect_one()) {
@@ -287,7 +316,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t last_phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int tm, tn;
-        tile_coords(tile, tiles_m, tiles_n, group_m, tm, tn);
+        tile_coords(tile, tiles_m, tiles_n, group_m, n_major, tm, tn);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, status, 101)) { ok = false; break; }
           uint8_t* a_dst = smem + stage * Cfg::STAGE_BYTES;
@@ -355,14 +384,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       int tm, tn;
-      tile_coords(tile, tiles_m, tiles_n, group_m, tm, tn);
+      tile_coords(tile, tiles_m, tiles_n, group_m, n_major, tm, tn);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[acc], acc_phase, status, 104)) break;
       tc_fence_after();
-      epilogue_tile<BN, OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
-                                   (int64_t)tm * BM + row_in_tile, tn, M, N, C, ldc, Cin, ldcin,
-                                   alpha, beta, vec_ok, ea);
+      epilogue_cols<OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, 0, BN,
+                               (int64_t)tm * BM + row_in_tile, (int64_t)tn * BN, M, N, C, ldc, Cin,
+                               ldcin, alpha, beta, vec_ok, ea);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -386,28 +415,35 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // stages a third fewer operand bytes through L2 and shared memory than the
 // single-CTA 128 x 256 tile.
 // ------------------------------------------------------------------------ //
+constexpr int kPairThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
+
 template <int BN>
 struct PairCfg {
-  static_assert(BN % 32 == 0 && BN >= 128 && BN <= 256, "pair tile width");
-  static constexpr int BNH = BN / 2;  // B columns held by each CTA
+  static_assert(BN % 64 == 0 && BN >= 128 && BN <= 512, "pair tile width");
+  static constexpr int NMMA = BN > 256 ? 2 : 1;  // MMAs per K step (N <= 256 each)
+  static constexpr int NJ = BN / NMMA;            // N of one MMA
+  static constexpr int NJH = NJ / 2;              // B rows of one MMA held by each CTA
+  static constexpr int NACC = 2 * BN <= 512 ? 2 : 1;  // TMEM accumulator buffers
   static constexpr uint32_t A_BYTES = BM * BK * 2;
-  static constexpr uint32_t B_BYTES = BNH * BK * 2;
+  static constexpr uint32_t BJ_BYTES = NJH * BK * 2;  // one MMA's B sub-tile
+  static constexpr uint32_t B_BYTES = NMMA * BJ_BYTES;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (200u * 1024u / STAGE_BYTES) > 8 ? 8 : (200u * 1024u / STAGE_BYTES);
-  static constexpr uint32_t TMEM_COLS = pow2_at_least(2 * BN);
+  static constexpr uint32_t TMEM_COLS = NACC == 2 ? pow2_at_least(2 * BN) : 512;
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
-  static_assert(STAGE_BYTES % 1024 == 0, "stages must stay 1024-byte aligned");
+  static_assert(STAGE_BYTES % 1024 == 0 && BJ_BYTES % 1024 == 0, "1024-byte aligned tiles");
 };
 
 template <int BN, bool A_MN, bool B_MN, typename OutT, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     int M, int N, int K, OutT* C, int64_t ldc, const OutT* Cin, int64_t ldcin,
                     float alpha, float beta, int vec_ok, EpiArgs ea, int* status) {
   using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr int BNH = Cfg::BNH;
-  constexpr uint32_t IDESC = idesc_bf16(2 * BM, BN, A_MN, B_MN);
+  constexpr int NMMA = Cfg::NMMA, NJ = Cfg::NJ, NJH = Cfg::NJH, NACC = Cfg::NACC;
+  static_assert(!B_MN || NJH % 64 == 0, "MN-major B sub-tiles are loaded in 64-column boxes");
+  constexpr uint32_t IDESC = idesc_bf16(2 * BM, NJ, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -431,7 +467,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 8);  // 4 epilogue warps in each CTA of the pair
+      mbar_init(&acc_empty[i], 16);  // 8 epilogue warps in each CTA of the pair
     }
     mbar_init(mma_done, 1);
     fence_barrier_init();
@@ -454,8 +490,9 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   const int tiles_n = (N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = (K + BK - 1) / BK;
-  const int64_t a_panel = (int64_t)2 * BM * K * 2;
-  const int group_m = min(tiles_m, max(4, (int)((40ll << 20) / a_panel)));
+  bool n_major;
+  const int group_m =
+      raster_group(ea.raster, tiles_m, tiles_n, (int64_t)2 * BM * K * 2, 4, n_major);
   const int cid = (int)cluster_id_x();
   const int ncl = (int)nclusters_x();
 
@@ -468,9 +505,8 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       bool issued = false;
       for (int tile = cid; tile < num_tiles && ok; tile += ncl) {
         int tm, tn;
-        tile_coords(tile, tiles_m, tiles_n, group_m, tm, tn);
+        tile_coords(tile, tiles_m, tiles_n, group_m, n_major, tm, tn);
         const int row0 = tm * 2 * BM + (int)rank * BM;
-        const int bcol0 = tn * BN + (int)rank * BNH;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, status, 111)) { ok = false; break; }
           uint8_t* a_dst = smem + stage * Cfg::STAGE_BYTES;
@@ -483,12 +519,18 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             tma_load_2d_pair(a_dst, &tmA, bar, row0, kb * BK);
             tma_load_2d_pair(a_dst + 8192, &tmA, bar, row0 + 64, kb * BK);
           }
-          if constexpr (!B_MN) {
-            tma_load_2d_pair(b_dst, &tmB, bar, kb * BK, bcol0);
-          } else {
 #pragma unroll
-            for (int j = 0; j < BNH / 64; ++j)
-              tma_load_2d_pair(b_dst + j * 8192, &tmB, bar, bcol0 + 64 * j, kb * BK);
+          for (int j = 0; j < NMMA; ++j) {
+            // MMA j covers tile columns [j NJ, j NJ + NJ); this CTA holds half of them
+            const int bcol0 = tn * BN + j * NJ + (int)rank * NJH;
+            uint8_t* bj = b_dst + j * Cfg::BJ_BYTES;
+            if constexpr (!B_MN) {
+              tma_load_2d_pair(bj, &tmB, bar, kb * BK, bcol0);
+            } else {
+#pragma unroll
+              for (int q = 0; q < NJH / 64; ++q)
+                tma_load_2d_pair(bj + q * 8192, &tmB, bar, bcol0 + 64 * q, kb * BK);
+            }
           }
           issued = true;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -510,8 +552,8 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       bool ok = true;
       bool issued = false;
       for (int tile = cid; tile < num_tiles && ok; tile += ncl, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        const int acc = NACC == 2 ? (local & 1) : 0;
+        const uint32_t acc_phase = NACC == 2 ? ((local >> 1) & 1) : (local & 1);
         if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, status, 112)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -524,9 +566,13 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = A_MN ? sw128_desc(a_base + k * 2048, 8192, 1024)
                                      : sw128_desc(a_base + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? sw128_desc(b_base + k * 2048, 8192, 1024)
-                                     : sw128_desc(b_base + k * 32, 16, 1024);
-            mma_bf16_ss_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int j = 0; j < NMMA; ++j) {
+              const uint32_t bj = b_base + j * Cfg::BJ_BYTES;
+              const uint64_t bd = B_MN ? sw128_desc(bj + k * 2048, 8192, 1024)
+                                       : sw128_desc(bj + k * 32, 16, 1024);
+              mma_bf16_ss_pair(d_tmem + j * NJ, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            }
           }
           issued = true;
           mma_commit_pair(&empty[stage], 0x3);
@@ -541,21 +587,24 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       }
     }
   } else {
-    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 of this CTA's 128 rows
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 of this CTA's 128 rows;
+    // warps 2-5 drain the first half of the columns, warps 6-9 the second
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t acc_empty_leader = mapa_shared(&acc_empty[0], 0);
     int local = 0;
     for (int tile = cid; tile < num_tiles; tile += ncl, ++local) {
       int tm, tn;
-      tile_coords(tile, tiles_m, tiles_n, group_m, tm, tn);
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      tile_coords(tile, tiles_m, tiles_n, group_m, n_major, tm, tn);
+      const int acc = NACC == 2 ? (local & 1) : 0;
+      const uint32_t acc_phase = NACC == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!mbar_wait(&acc_full[acc], acc_phase, status, 114)) break;
       tc_fence_after();
-      epilogue_tile<BN, OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
-                                   (int64_t)tm * 2 * BM + rank * BM + row_in_tile, tn, M, N, C,
-                                   ldc, Cin, ldcin, alpha, beta, vec_ok, ea);
+      epilogue_cols<OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
+                               half * (BN / 2), (half + 1) * (BN / 2),
+                               (int64_t)tm * 2 * BM + rank * BM + row_in_tile, (int64_t)tn * BN, M,
+                               N, C, ldc, Cin, ldcin, alpha, beta, vec_ok, ea);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty_leader + 8u * (uint32_t)acc);
@@ -598,7 +647,7 @@ int pair_capacity(Kern kern, size_t smem) {
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(2 * (unsigned)(sm_count() / 2), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -633,7 +682,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(2 * (unsigned)clusters, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM;
   cfg.stream = stream;
   cfg.attrs = attr;
@@ -647,14 +696,14 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
 template <int BN, typename OutT>
 int launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
                   int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin, float alpha,
-                  float beta, int vec_ok, int* status, cudaStream_t s) {
+                  float beta, int vec_ok, int* status, cudaStream_t s, EpiArgs ea) {
   if (!a_mn && !b_mn)
-    return launch<BN, false, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    return launch<BN, false, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
   if (!a_mn && b_mn)
-    return launch<BN, false, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    return launch<BN, false, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
   if (a_mn && !b_mn)
-    return launch<BN, true, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
-  return launch<BN, true, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    return launch<BN, true, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+  return launch<BN, true, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
 }
 
 }  // namespace
@@ -687,10 +736,10 @@ bool gemm_tc_eligible(int dtype, int64_t M, int64_t N, int64_t K, const void* A,
 template <int BN, typename OutT>
 int launch_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
               int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin, float alpha,
-              float beta, int vec_ok, int* status, cudaStream_t s) {
+              float beta, int vec_ok, int* status, cudaStream_t s, EpiArgs ea) {
   if constexpr (BN % 64 == 0) {
     return launch_majors<BN, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
-                                   vec_ok, status, s);
+                                   vec_ok, status, s, ea);
   } else {
     if (b_mn) {
       set_error("gemm: tile width %d needs a K-major B operand", BN);
@@ -698,22 +747,22 @@ int launch_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb
     }
     if (a_mn)
       return launch<BN, true, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
-                                           vec_ok, status, s);
+                                           vec_ok, status, s, ea);
     return launch<BN, false, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok,
-                                          status, s);
+                                          status, s, ea);
   }
 }
 
 template <typename OutT>
 int launch_any_bn(int BN, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                   int M, int N, int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin,
-                  float alpha, float beta, int vec_ok, int* status, cudaStream_t s) {
+                  float alpha, float beta, int vec_ok, int* status, cudaStream_t s, EpiArgs ea) {
   switch (BN) {
-    case 256: return launch_bn<256, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
-    case 224: return launch_bn<224, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
-    case 192: return launch_bn<192, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
-    case 160: return launch_bn<160, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
-    case 128: return launch_bn<128, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    case 256: return launch_bn<256, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+    case 224: return launch_bn<224, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+    case 192: return launch_bn<192, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+    case 160: return launch_bn<160, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+    case 128: return launch_bn<128, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
     default: break;
   }
   set_error("gemm: unsupported tile width %d", BN);
@@ -723,14 +772,14 @@ int launch_any_bn(int BN, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUt
 template <int BN, typename OutT>
 int launch_pair_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, int M,
                        int N, int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin,
-                       float alpha, float beta, int vec_ok, int* status, cudaStream_t s) {
-  if constexpr ((BN / 2) % 64 == 0) {
+                       float alpha, float beta, int vec_ok, int* status, cudaStream_t s, EpiArgs ea) {
+  if constexpr (PairCfg<BN>::NJH % 64 == 0) {
     if (b_mn) {
       if (a_mn)
         return launch_pair<BN, true, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
-                                                 vec_ok, status, s);
+                                                 vec_ok, status, s, ea);
       return launch_pair<BN, false, true, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
-                                                vec_ok, status, s);
+                                                vec_ok, status, s, ea);
     }
   } else {
     if (b_mn) {
@@ -740,24 +789,29 @@ int launch_pair_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtens
   }
   if (a_mn)
     return launch_pair<BN, true, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
-                                              vec_ok, status, s);
+                                              vec_ok, status, s, ea);
   return launch_pair<BN, false, false, OutT>(ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta,
-                                             vec_ok, status, s);
+                                             vec_ok, status, s, ea);
 }
 
 template <typename OutT>
 int launch_pair_any_bn(int BN, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
                        int M, int N, int K, void* C, int64_t ldc, const void* Cin, int64_t ldcin,
-                       float alpha, float beta, int vec_ok, int* status, cudaStream_t s) {
+                       float alpha, float beta, int vec_ok, int* status, cudaStream_t s, EpiArgs ea) {
   switch (BN) {
-    case 256: return launch_pair_majors<256, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
-    case 192: return launch_pair_majors<192, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
-    case 128: return launch_pair_majors<128, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s);
+    case 512: return launch_pair_majors<512, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+    case 384: return launch_pair_majors<384, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+    case 256: return launch_pair_majors<256, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+    case 192: return launch_pair_majors<192, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
+    case 128: return launch_pair_majors<128, OutT>(a_mn, b_mn, ta, tb, M, N, K, C, ldc, Cin, ldcin, alpha, beta, vec_ok, status, s, ea);
     default: break;
   }
   set_error("gemm: unsupported pair tile width %d", BN);
   return PE_ERR_ARG;
 }
+
+// B rows of one MMA held by each CTA of the pair (the TMA box height for K-major B)
+int pair_b_box(int bn) { return (bn > 256 ? bn / 2 : bn) / 2; }
 
 // The CTA-pair kernel takes problems with at least this many rows (below it half
 // of a 256-row pair tile would mostly be padding).
@@ -772,21 +826,23 @@ bool use_pair(int64_t M, int mode) {
 int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
             const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
             const void* Cin, int64_t ldcin, float alpha, float beta, int* status,
-            cudaStream_t stream, int force_bn, int mode) {
+            cudaStream_t stream, int force_bn, int mode, int raster) {
   const bool a_mn = a_sk != 1;
   const bool b_mn = b_sk != 1;
   const bool pair = use_pair(M, mode);
   int BN;
   if (pair) {
-    BN = force_bn > 0 ? force_bn : choose_bn_pair(M, N, b_mn, sm_count() / 2);
-    PE_CHECK_ARG(BN == 128 || BN == 192 || BN == 256, "gemm: pair tile width %d not 128/192/256",
+    BN = force_bn > 0 ? force_bn
+                      : choose_bn_pair(M, N, K, b_mn, c_dtype == PE_F32 ? 4 : 2, sm_count() / 2);
+    PE_CHECK_ARG(BN == 128 || BN == 192 || BN == 256 || BN == 384 || BN == 512,
+                 "gemm: pair tile width %d not 128/192/256/384/512", BN);
+    PE_CHECK_ARG(!(b_mn && pair_b_box(BN) % 64 != 0), "gemm: pair tile width %d needs a K-major B",
                  BN);
-    PE_CHECK_ARG(!(b_mn && (BN / 2) % 64 != 0), "gemm: pair tile width %d needs a K-major B", BN);
   } else {
     BN = force_bn > 0 ? force_bn : choose_bn(M, N, b_mn, sm_count());
     PE_CHECK_ARG(!(b_mn && BN % 64 != 0), "gemm: tile width %d needs a K-major B operand", BN);
   }
-  const uint32_t b_box = pair ? (uint32_t)(BN / 2) : (uint32_t)BN;
+  const uint32_t b_box = pair ? (uint32_t)pair_b_box(BN) : (uint32_t)BN;
   CUtensorMap ta, tb;
   int rc;
   if (!a_mn)
@@ -803,18 +859,19 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
   const int vec_ok = (ldc * esz) % 16 == 0 && al16(C) &&
                      (!Cin || ((ldcin * esz) % 16 == 0 && al16(Cin)));
   const int m = (int)M, n = (int)N, k = (int)K;
+  const EpiArgs ea{nullptr, 0, nullptr, raster};
   if (pair) {
     if (c_dtype == PE_F32)
       return launch_pair_any_bn<float>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha,
-                                       beta, vec_ok, status, stream);
+                                       beta, vec_ok, status, stream, ea);
     return launch_pair_any_bn<__nv_bfloat16>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin,
-                                             alpha, beta, vec_ok, status, stream);
+                                             alpha, beta, vec_ok, status, stream, ea);
   }
   if (c_dtype == PE_F32)
     return launch_any_bn<float>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha, beta,
-                                vec_ok, status, stream);
+                                vec_ok, status, stream, ea);
   return launch_any_bn<__nv_bfloat16>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha,
-                                      beta, vec_ok, status, stream);
+                                      beta, vec_ok, status, stream, ea);
 }
 
 int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
@@ -823,14 +880,20 @@ int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t
   PE_CHECK_ARG(M > 0 && N > 0 && K > 0 && lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 &&
                    al16(A) && al16(B) && al16(C),
                "gemm (logits + row stats): operands must be 16-byte aligned bf16");
-  PE_CHECK_ARG(stats_ld >= (N + 255) / 256, "gemm (logits + row stats): stats_ld too small");
+  PE_CHECK_ARG(stats_ld >= (N + 127) / 128, "gemm (logits + row stats): stats_ld too small");
   const bool pair = use_pair(M, 0);
+  // pair tiles 256 x 512 or 256 x 256 (the stats need 128-column aligned halves)
+  const int pbn = pair ? (choose_bn_pair(M, N, K, false, 2, sm_count() / 2) > 256 ? 512 : 256) : 256;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
   if (!rc)
-    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, 64, pair ? 128 : 256);
+    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, 64,
+                      pair ? (uint32_t)pair_b_box(pbn) : 256u);
   if (rc) return rc;
-  EpiArgs ea{stats, stats_ld, nullptr};
+  EpiArgs ea{stats, stats_ld, nullptr, 0};
+  if (pair && pbn == 512)
+    return launch_pair<512, false, false, __nv_bfloat16, EPI_STATS>(
+        ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
   if (pair)
     return launch_pair<256, false, false, __nv_bfloat16, EPI_STATS>(
         ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
@@ -849,10 +912,14 @@ int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t
   int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
   if (!rc) rc = make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)b_sk * 2, 64, 64);
   if (rc) return rc;
-  EpiArgs ea{nullptr, 0, rowscale};
-  if (use_pair(M, 0))
+  EpiArgs ea{nullptr, 0, rowscale, 0};
+  if (use_pair(M, 0)) {
+    if (choose_bn_pair(M, N, K, true, 4, sm_count() / 2) == 512)
+      return launch_pair<512, false, true, float, EPI_ROWSCALE>(
+          ta, tb, (int)M, (int)N, (int)K, C, ldc, Cin, ldc, 1.f, 0.f, 1, status, stream, ea);
     return launch_pair<256, false, true, float, EPI_ROWSCALE>(
         ta, tb, (int)M, (int)N, (int)K, C, ldc, Cin, ldc, 1.f, 0.f, 1, status, stream, ea);
+  }
   return launch<256, false, true, float, EPI_ROWSCALE>(ta, tb, (int)M, (int)N, (int)K, C, ldc, Cin,
                                                        ldc, 1.f, 0.f, 1, status, stream, ea);
 }
@@ -865,22 +932,26 @@ int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm
   PE_CHECK_ARG(ldc >= N, "gemm: ldc < N");
   if (M == 0 || N == 0) return PE_OK;
   PE_CHECK_ARG(K > 0, "gemm: K == 0 is not supported");
-  const int force_bn = (algo >> 8) & 0x1ff;
+  const int algo_bits = algo;
+  const int force_bn = (algo >> 8) & 0x3ff;
   const int mode = (algo >> 20) & 3;  // 0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles
   algo &= 0xff;
   PE_CHECK_ARG(force_bn == 0 || force_bn == 128 || force_bn == 160 || force_bn == 192 ||
-                   force_bn == 224 || force_bn == 256,
-               "gemm: forced tile width %d not one of 128/160/192/224/256", force_bn);
+                   force_bn == 224 || force_bn == 256 || force_bn == 384 || force_bn == 512,
+               "gemm: forced tile width %d not one of 128/160/192/224/256/384/512", force_bn);
   PE_CHECK_ARG(mode != 3, "gemm: tile mode 3 is not defined");
+  // bits 24-29: tile-group size (0 automatic); bit 30: group along N instead of M
+  const int group = (algo_bits >> 24) & 0x3f;
+  const int raster = ((algo_bits >> 30) & 1) ? -group : group;
   const bool tc_ok = gemm_tc_eligible(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, c_dtype);
   if (algo == PE_ALGO_TCGEN05) {
     PE_CHECK_ARG(tc_ok, "gemm: operands not eligible for the tcgen05 path");
     return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
-                   beta, status, stream, force_bn, mode);
+                   beta, status, stream, force_bn, mode, raster);
   }
   if (algo == PE_ALGO_AUTO && tc_ok)
     return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
-                   beta, status, stream, force_bn, mode);
+                   beta, status, stream, force_bn, mode, raster);
   return gemm_simt(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin,
                    alpha, beta, stream);
 }

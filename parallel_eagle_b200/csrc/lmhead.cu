@@ -207,7 +207,7 @@ unsigned grid_for(int64_t n) {
 // ------------------------------------------------------------------------ //
 // Fused path (bf16, hard labels): one logits GEMM per vocabulary chunk, no
 // recompute.  Per chunk c:
-//   Zc = h W_c^T (bf16) with per-(row, 256-col tile) (max, sum-exp) from the
+//   Zc = h W_c^T (bf16) with per-(row, 128-col chunk) (max, sum-exp) from the
 //        GEMM epilogue;
 //   combine: running (m, l) per row, alpha = exp(m_old - m_new), the label logit,
 //        and Zc <- exp(Zc - m_new) in place;
@@ -222,8 +222,8 @@ constexpr int64_t kFastChunk = 16384;  // vocabulary rows per logits chunk (defa
 constexpr int64_t kRowGroup = 4096;    // loss rows per group (default)
 constexpr int64_t kMaxChunk = 16384;
 constexpr int64_t kMaxGroup = 8192;
-constexpr int kStatTile = 256;
-static_assert(kMaxChunk / kStatTile <= 64, "combine_kernel folds at most 64 tile stats");
+constexpr int kStatTile = 128;  // columns per (max, sum-exp) pair of the logits GEMM
+static_assert(kMaxChunk / kStatTile <= 128, "combine_kernel folds at most 128 tile stats");
 
 // Rows of the loss are processed in groups so one group's logits chunk
 // (group x chunk bf16) stays mostly resident in L2 between the logits GEMM, the
@@ -293,13 +293,20 @@ combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __res
     const int lane = threadIdx.x;
     const float2* st = stats + r * stats_ld;
     const float m_old = m[r];
-    // nt <= 64 (kMaxChunk / kStatTile): lanes take tiles lane and lane + 32
-    const float2 s0 = lane < nt ? st[lane] : make_float2(-INFINITY, 0.f);
-    const float2 s1 = lane + 32 < nt ? st[lane + 32] : make_float2(-INFINITY, 0.f);
-    const float mn = fmaxf(m_old, warp_max(fmaxf(s0.x, s1.x)));
+    // nt <= 128 (kMaxChunk / kStatTile): lane takes tiles lane, lane + 32, ...
+    float2 sv[4];
+    float lm = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int t = lane + 32 * q;
+      sv[q] = t < nt ? st[t] : make_float2(-INFINITY, 0.f);
+      lm = fmaxf(lm, sv[q].x);
+    }
+    const float mn = fmaxf(m_old, warp_max(lm));
     float part = 0.f;
-    if (s0.x != -INFINITY) part += s0.y * expf(s0.x - mn);
-    if (s1.x != -INFINITY) part += s1.y * expf(s1.x - mn);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (sv[q].x != -INFINITY) part += sv[q].y * expf(sv[q].x - mn);
     const float tile_sum = warp_sum(part);
     if (lane == 0) {
       const float keep = m_old == -INFINITY ? 0.f : expf(m_old - mn);

@@ -95,14 +95,16 @@ def test_gemm_tcgen05_every_tile_width(bn, a_mn, b_mn):
     assert rel(C.cpu(), Ad @ Bd.t()) < 1e-5
 
 
-@pytest.mark.parametrize("bn", [128, 192, 256])
+@pytest.mark.parametrize("bn", [128, 192, 256, 384, 512])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, False), (False, True), (True, True)])
 @pytest.mark.parametrize("M", [300, 1100])
 def test_gemm_tcgen05_pair_tile_widths(bn, a_mn, b_mn, M):
-    # CTA-pair tiles (256 x bn): ragged M leaves the second CTA's rows partly or wholly
-    # outside the matrix; ragged N leaves part of the last tile's B halves empty
-    if b_mn and (bn // 2) % 64:
-        pytest.skip("MN-major B needs a pair tile width whose half is a multiple of 64")
+    # CTA-pair tiles (256 x bn; above 256 two MMAs per K step into one 512-column
+    # accumulator): ragged M leaves the second CTA's rows partly or wholly outside the
+    # matrix; ragged N leaves part of the last tile's B sub-tiles empty
+    b_rows = (bn // 2 if bn > 256 else bn) // 2  # B rows of one MMA held by each CTA
+    if b_mn and b_rows % 64:
+        pytest.skip("MN-major B needs 64-column B sub-tiles")
     N, K = 3584 // 4 + 40, 520
     A, (a_sm, a_sk), Ad = _operand(M, K, a_mn, torch.bfloat16, 7)
     B, (b_sn, b_sk), Bd = _operand(N, K, b_mn, torch.bfloat16, 8)
@@ -111,6 +113,24 @@ def test_gemm_tcgen05_pair_tile_widths(bn, a_mn, b_mn, M):
              algo=L.ALGO_TCGEN05 | (bn << 8) | (2 << 20))
     torch.cuda.synchronize()
     ops.check_status(DEV)
+    assert rel(C.cpu(), Ad @ Bd.t()) < 1e-5
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("raster", [1, 3, 64 - 1, -1, -2, -5])
+def test_gemm_tcgen05_tile_orders(mode, raster):
+    # every tile order (groups of M-tiles or of N-tiles, ragged last group) covers
+    # each output tile exactly once
+    M, N, K = 1300, 2000, 200
+    A, (a_sm, a_sk), Ad = _operand(M, K, False, torch.bfloat16, 9)
+    B, (b_sn, b_sk), Bd = _operand(N, K, True, torch.bfloat16, 10)
+    C = torch.full((M, N), float("nan"), dtype=torch.float32, device=DEV)
+    bits = ((abs(raster) & 0x3F) << 24) | ((1 << 30) if raster < 0 else 0)
+    ops.gemm(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, N,
+             algo=L.ALGO_TCGEN05 | (mode << 20) | bits)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert not torch.isnan(C).any()
     assert rel(C.cpu(), Ad @ Bd.t()) < 1e-5
 
 
