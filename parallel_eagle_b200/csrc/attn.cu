@@ -45,10 +45,14 @@ extern "C" int pe_attn_fwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int
   MaskSpec m{layout, a0, a1, kdepth, anchor, depth, bias, bias_sb, bias_sq};
   const bool tc = attn_tc_eligible(dtype, B, S, Hq, Hkv, head_dim, layout, q, q_ss, k, k_ss, v,
                                    v_ss);
+  // algo bits 8-15: tensor-core kernel variant (0 two query tiles per CTA, 1 one)
+  const int variant = (algo >> 8) & 0xff;
+  algo &= 0xff;
+  PE_CHECK_ARG(variant <= 1, "attention: unknown kernel variant %d", variant);
   if (algo == PE_ALGO_TCGEN05) PE_CHECK_ARG(tc, "attention: inputs not eligible for tcgen05");
   if (tc && algo != PE_ALGO_SIMT)
     return attn_fwd_tc_launch(S, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, lse, m, status,
-                              as_stream(stream));
+                              as_stream(stream), variant);
   return attn_fwd_simt_launch(dtype, B, S, Hq, Hkv, head_dim, q, q_sb, q_ss, k, k_sb, k_ss, v,
                               v_sb, v_ss, o, o_sb, o_ss, lse, m, as_stream(stream));
 }

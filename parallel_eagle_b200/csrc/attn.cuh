@@ -61,7 +61,8 @@ bool attn_tc_bwd_ready();
 size_t attn_tc_bwd_acc_bytes(int64_t S, int Hq, int Hkv);
 int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
                        int64_t k_ss, const void* v, int64_t v_ss, void* o, int64_t o_ss,
-                       float* lse, const MaskSpec& m, int* status, cudaStream_t st);
+                       float* lse, const MaskSpec& m, int* status, cudaStream_t st,
+                       int variant = 0);
 int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
                        int64_t k_ss, const void* v, int64_t v_ss, const void* o, int64_t o_ss,
                        const void* dout, int64_t do_ss, const float* lse, void* dq,

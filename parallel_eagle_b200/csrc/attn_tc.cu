@@ -307,6 +307,321 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
 }
 
+// ------------------------------------------------------------------------ //
+// Two query tiles per CTA (rows q0 .. q0 + 255 of one head), so the tensor core
+// always has one tile's MMAs to run while the other tile's softmax executes:
+//
+//   warp 0      TMA: both Q tiles once, then K/V tiles into a 2-stage ring
+//   warp 1      MMA issue, per key tile j:  PV_A(j-1) S_A(j) PV_B(j-1) S_B(j)
+//               (S_t = Q_t K^T into TMEM; PV_t: O_t += P_t V with P_t read from
+//               TMEM -- the tcgen05 A-from-TMEM form -- so P never touches
+//               shared memory)
+//   warps 2..5  softmax of tile A, one thread per query row (TMEM lane)
+//   warps 6..9  softmax of tile B
+//
+// TMEM: O_A cols 0..127, O_B 128..255, S_A 256..383, S_B 384..511; P_t is
+// written as packed bf16 pairs over the first 64 columns of S_t.
+//
+// The CTA walks the union of both tiles' key-tile lists; for a key tile one of
+// the tiles does not need, that tile's MMAs are skipped (its barriers still
+// advance, keeping every role in lockstep).  The running row maximum is only
+// raised (and O rescaled) when it grows by more than 2^8: until then
+// P = 2^(x - m) <= 256 against the stale maximum, and O and the row sum stay
+// consistent because both are relative to the same m.
+// ------------------------------------------------------------------------ //
+constexpr size_t SMEM_FWD2 = 1024 + 2 * TILE_BYTES /*Q_A, Q_B*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ + 256;
+constexpr float kRescaleLog2 = 8.f;
+
+struct PairTiles {
+  TileList a, b;  // b empty (count 0) when the second query tile lies past the sequence
+  __device__ __forceinline__ static bool in(const TileList& l, int t) {
+    return t < l.r_end || (t >= l.m_beg && t < l.m_end);
+  }
+  __device__ __forceinline__ bool use_a(int t) const { return in(a, t); }
+  __device__ __forceinline__ bool use_b(int t) const { return in(b, t); }
+  // smallest key tile > t that either query tile visits, or -1
+  __device__ __forceinline__ int next(int t) const {
+    int best = 0x7fffffff;
+    auto cand = [&](int lo, int hi) {
+      const int c = max(t + 1, lo);
+      if (c < hi && c < best) best = c;
+    };
+    cand(0, max(a.r_end, b.r_end));
+    cand(a.m_beg, a.m_end);
+    cand(b.m_beg, b.m_end);
+    return best == 0x7fffffff ? -1 : best;
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
+                    int64_t o_ss, float* __restrict__ lse, PartGeom g, int Hq, int rep,
+                    float scale_log2, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem;                  // tile t at + t * TILE_BYTES
+  uint8_t* sKV = sQ + 2 * TILE_BYTES;  // stage s: K at + s * 2 * TILE, V at + TILE
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + 4 * TILE_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [query tile]
+  uint64_t* p_full = bars + 7;    // [query tile]
+  uint64_t* o_full = bars + 9;    // [query tile]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_pairs = (g.S + 2 * TQ - 1) / (2 * TQ);
+  const int pr = num_pairs - 1 - (int)blockIdx.x;  // heaviest pairs first
+  const int h = blockIdx.y;
+  const int kvh = h / rep;
+  const int q0 = pr * 2 * TQ;
+  PairTiles pt;
+  pt.a = tiles_for(g, q0);
+  if (q0 + TQ < g.S) {
+    pt.b = tiles_for(g, q0 + TQ);
+  } else {
+    pt.b.r_end = pt.b.m_beg = pt.b.m_end = 0;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+    }
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      bool ok = true;
+      int last_st = -1;
+      uint32_t last_ph = 0;
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        tma_load_2d(sQ + t * TILE_BYTES, &tmQ, q_full, h * HD, q0 + t * TQ);
+        tma_load_2d(sQ + t * TILE_BYTES + CHUNK, &tmQ, q_full, h * HD + 64, q0 + t * TQ);
+      }
+      int j = 0;
+      for (int kt = 0; kt >= 0 && ok; kt = pt.next(kt), ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, status, 211)) { ok = false; break; }
+        const int k0 = kt * TK;
+        uint8_t* k_dst = sKV + st * 2 * TILE_BYTES;
+        uint8_t* v_dst = k_dst + TILE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        tma_load_2d(k_dst, &tmK, &kv_full[st], kvh * HD, k0);
+        tma_load_2d(k_dst + CHUNK, &tmK, &kv_full[st], kvh * HD + 64, k0);
+        tma_load_2d(v_dst, &tmV, &kv_full[st], kvh * HD, k0);
+        tma_load_2d(v_dst + CHUNK, &tmV, &kv_full[st], kvh * HD + 64, k0);
+        last_st = st;
+        last_ph = ph;
+      }
+      if (!ok && last_st >= 0) mbar_wait(&kv_full[last_st], last_ph, nullptr, 0);
+      mbar_wait(q_full, 0, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t IDESC_S = idesc_bf16(TQ, TK, false, false);
+      constexpr uint32_t IDESC_O = idesc_bf16(TQ, HD, false, true);
+      bool ok = mbar_wait(q_full, 0, status, 212);
+      auto issue_s = [&](int t, int st) {
+        const uint32_t q_base = smem_u32(sQ + t * TILE_BYTES);
+        const uint32_t k_base = smem_u32(sKV + st * 2 * TILE_BYTES);
+        const uint32_t d = tmem + 256 + t * 128;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(d, sw128_desc(q_base + off, 16, 1024), sw128_desc(k_base + off, 16, 1024),
+                      IDESC_S, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int st, bool first) {
+        const uint32_t v_base = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
+        const uint32_t p = tmem + 256 + t * 128;
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk)
+          mma_bf16_ts(tmem + t * 128, p + kk * 8, sw128_desc(v_base + kk * 2048, CHUNK, 1024),
+                      IDESC_O, (!first || kk > 0) ? 1u : 0u);
+      };
+      // step 0: S of both tiles for key tile 0 (every query row sees key 0)
+      if (ok) ok = mbar_wait(&kv_full[0], 0, status, 213);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        mma_commit(&s_full[0]);
+        if (pt.use_b(0)) issue_s(1, 0);
+        mma_commit(&s_full[1]);
+      }
+      bool pv_a = false, pv_b = false;
+      int j = 0;
+      for (int kt = 0; kt >= 0 && ok; ++j) {
+        const int st = j & 1;
+        const int kn = pt.next(kt);
+        const int stn = (j + 1) & 1;
+        // tile A: PV of key tile kt, then S of the next key tile
+        if (!mbar_wait(&p_full[0], j & 1, status, 214)) { ok = false; break; }
+        tc_fence_after();
+        if (pt.use_a(kt)) {
+          issue_pv(0, st, !pv_a);
+          pv_a = true;
+        }
+        if (kn >= 0) {
+          if (!mbar_wait(&kv_full[stn], ((j + 1) >> 1) & 1, status, 215)) { ok = false; break; }
+          tc_fence_after();
+          if (pt.use_a(kn)) issue_s(0, stn);
+          mma_commit(&s_full[0]);
+        }
+        // tile B
+        if (!mbar_wait(&p_full[1], j & 1, status, 216)) { ok = false; break; }
+        tc_fence_after();
+        if (pt.use_b(kt)) {
+          issue_pv(1, st, !pv_b);
+          pv_b = true;
+        }
+        if (kn >= 0) {
+          if (pt.use_b(kn)) issue_s(1, stn);
+          mma_commit(&s_full[1]);
+        }
+        mma_commit(&kv_empty[st]);
+        kt = kn;
+      }
+      if (ok) {
+        mma_commit(&o_full[0]);
+        mma_commit(&o_full[1]);
+      }
+    }
+  } else {
+    // ---------------- softmax: warps 2..5 tile A, 6..9 tile B; thread = query row ----
+    const int t = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int s = q0 + t * TQ + row;
+    const bool valid = s < g.S;
+    int qi = -1, qd = 0;
+    if (valid) decode(g, s, qi, qd);
+    const int lo = qd > 0 ? g.a1 + (qi - g.a0) * g.km1 : 0;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + 256 + t * 128 + lane_off;
+    const uint32_t tO = tmem + t * 128 + lane_off;
+    const TileList& mine = t == 0 ? pt.a : pt.b;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    int j = 0;
+    for (int kt = 0; kt >= 0; kt = pt.next(kt), ++j) {
+      if (!mbar_wait(&s_full[t], j & 1, status, 217)) { ok = false; break; }
+      tc_fence_after();
+      if (PairTiles::in(mine, kt)) {
+        float x[128];
+#pragma unroll
+        for (int c = 0; c < 128; c += 32) tmem_ld32(tS + c, x + c);
+        tmem_wait_ld();
+        const int k0 = kt * TK;
+        float mt = -INFINITY;
+        if (k0 + TK - 1 <= qi) {  // every key of the tile is a real key <= the row's anchor
+#pragma unroll
+          for (int c = 0; c < 128; ++c) {
+            x[c] *= scale_log2;
+            mt = fmaxf(mt, x[c]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) {
+            const int ks = k0 + c;
+            const bool allow = ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
+            x[c] = allow ? x[c] * scale_log2 : -INFINITY;
+            mt = fmaxf(mt, x[c]);
+          }
+        }
+        // raise the reference maximum only when the tile exceeds it by > 2^8
+        float alpha = 1.f;
+        if (mt > m + kRescaleLog2) {
+          alpha = m == -INFINITY ? 0.f : ex2_approx(m - mt);
+          m = mt;
+          l *= alpha;
+        }
+        const float m_use = m == -INFINITY ? 0.f : m;
+        // P_t over the first 64 columns of S_t (packed bf16 pairs)
+        float rs = 0.f;
+#pragma unroll
+        for (int c0 = 0; c0 < 128; c0 += 64) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) {
+            const float p0 = ex2_approx(x[c0 + c] - m_use), p1 = ex2_approx(x[c0 + c + 1] - m_use);
+            rs += p0 + p1;
+            pk[c / 2] = pack_bf16x2(p0, p1);
+          }
+          tmem_st32(tS + c0 / 2, pk);
+        }
+        l += rs;
+        // O holds the tiles before this one (their PV completed before this S did):
+        // rescale it when the maximum moved
+        if (__any_sync(0xffffffffu, alpha != 1.f) && j > 0) {
+#pragma unroll 1
+          for (int c = 0; c < 128; c += 32) {
+            float ov[32];
+            tmem_ld32(tO + c, ov);
+            tmem_wait_ld();
+            uint32_t ou[32];
+#pragma unroll
+            for (int u = 0; u < 32; ++u) ou[u] = __float_as_uint(ov[u] * alpha);
+            tmem_st32(tO + c, ou);
+          }
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok && mbar_wait(&o_full[t], 0, status, 218)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        float ov[32];
+        tmem_ld32(tO + c, ov);
+        tmem_wait_ld();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(O + (int64_t)s * o_ss + h * HD + c);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16x2(ov[8 * q] * inv, ov[8 * q + 1] * inv),
+                                pack_bf16x2(ov[8 * q + 2] * inv, ov[8 * q + 3] * inv),
+                                pack_bf16x2(ov[8 * q + 4] * inv, ov[8 * q + 5] * inv),
+                                pack_bf16x2(ov[8 * q + 6] * inv, ov[8 * q + 7] * inv));
+        }
+      }
+      if (valid) lse[(int64_t)h * g.S + s] = (m + log2f(l)) * kLn2;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace
 
 bool attn_tc_eligible(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd, int layout,
@@ -320,7 +635,7 @@ bool attn_tc_eligible(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd, 
 
 int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
                        int64_t k_ss, const void* v, int64_t v_ss, void* o, int64_t o_ss,
-                       float* lse, const MaskSpec& m, int* status, cudaStream_t st) {
+                       float* lse, const MaskSpec& m, int* status, cudaStream_t st, int variant) {
   PE_CHECK_ARG(o_ss % 8 == 0 && al16(o), "attention (tcgen05): output must be 16-byte aligned");
   CUtensorMap tq, tk, tv;
   int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, TQ);
@@ -329,11 +644,20 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   if (rc) return rc;
   PartGeom g{(int)S, (int)m.a0, (int)m.a1, m.kd - 1};
   const float scale_log2 = kLog2e / sqrtf((float)HD);
-  PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)SMEM_FWD));
-  dim3 grid((unsigned)((S + TQ - 1) / TQ), (unsigned)Hq);
-  attn_fwd_tc_kernel<<<grid, kThreads, SMEM_FWD, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
-                                                       g, Hq, Hq / Hkv, scale_log2, status);
+  if (variant == 1) {
+    PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_FWD));
+    dim3 grid((unsigned)((S + TQ - 1) / TQ), (unsigned)Hq);
+    attn_fwd_tc_kernel<<<grid, kThreads, SMEM_FWD, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
+                                                         g, Hq, Hq / Hkv, scale_log2, status);
+    PE_LAUNCHED();
+    return PE_OK;
+  }
+  PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc2_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_FWD2));
+  dim3 grid((unsigned)((S + 2 * TQ - 1) / (2 * TQ)), (unsigned)Hq);
+  attn_fwd_tc2_kernel<<<grid, kThreads, SMEM_FWD2, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
+                                                         g, Hq, Hq / Hkv, scale_log2, status);
   PE_LAUNCHED();
   return PE_OK;
 }
