@@ -76,6 +76,11 @@ extern "C" int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int
                "attention backward: workspace too small (see pe_attn_bwd_workspace)");
   float* delta = static_cast<float*>(workspace);
   MaskSpec m{layout, a0, a1, kdepth, anchor, depth, bias, bias_sb, bias_sq};
+  // algo bits 8-15: tensor-core kernel variant (0 split dQ / dK-dV kernels, 1 fused
+  // kernel with dQ atomics)
+  const int variant = (algo >> 8) & 0xff;
+  algo &= 0xff;
+  PE_CHECK_ARG(variant <= 1, "attention backward: unknown kernel variant %d", variant);
   const bool tc = attn_tc_bwd_ready() &&
                   attn_tc_eligible(dtype, B, S, Hq, Hkv, head_dim, layout, q, q_ss, k, k_ss, v,
                                    v_ss) &&
@@ -85,7 +90,7 @@ extern "C" int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int
     float* dq_acc = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + delta_bytes);
     return attn_bwd_tc_launch(S, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, dout, do_ss, lse,
                               dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, dq_acc, m, status,
-                              as_stream(stream));
+                              as_stream(stream), variant);
   }
   return attn_bwd_simt_launch(dtype, B, S, Hq, Hkv, head_dim, q, q_sb, q_ss, k, k_sb, k_ss, v,
                               v_sb, v_ss, o, o_sb, o_ss, dout, do_sb, do_ss, lse, dq, dq_sb,

@@ -68,6 +68,6 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
                        const void* dout, int64_t do_ss, const float* lse, void* dq,
                        int64_t dq_ss, void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
                        float* delta, float* dq_acc, const MaskSpec& m, int* status,
-                       cudaStream_t st);
+                       cudaStream_t st, int variant = 0);
 
 }  // namespace pe

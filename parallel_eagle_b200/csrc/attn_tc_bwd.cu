@@ -376,7 +376,583 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
 }
 
-// delta[h, s] = sum_d dO * O (fp32); zero the dQ accumulator row and, for the
+// ------------------------------------------------------------------------ //
+// Split backward (no dQ atomics):
+//
+// attn_bwd_q_kernel: one CTA = one 128-row query tile of one head, walking the
+// key tiles the tile reads (the forward's list).  Per key tile:
+//   S = Q K^T, dP = dO V^T (TMEM);  P = 2^(S c - lse'), dS = P (dP - delta) in
+//   registers (query row per TMEM lane); dS (bf16) written back over S and read
+//   by the A-from-TMEM MMA  dQ += dS K;  dQ stays in TMEM for the whole tile and
+//   is stored once, scaled, in bf16.  S is double-buffered, so S(j+1) runs while
+//   the softmax warps work on tile j.
+//   TMEM: dQ 0..127, dP 128..255, S 256..383 / 384..511.
+//
+// attn_bwd_kv_kernel: one CTA = one 128-key tile of one query head, walking the
+// query tiles that read it.  Per query tile:
+//   S^T = K Q^T, dP^T = V dO^T (TMEM); P^T written back over S^T, then
+//   dS^T = P^T (dP^T - delta) over dP^T; dV += P^T dO starts as soon as P^T is
+//   in place and overlaps the dS^T arithmetic, then dK += dS^T Q.  The head's
+//   dK / dV tile is added (fp32) into the KV head's accumulator at the end.
+//   TMEM: dK 0..127, dV 128..255, S^T 256..383, dP^T 384..511.
+// ------------------------------------------------------------------------ //
+constexpr size_t SMEM_BWD_Q = 1024 + 2 * TILE_BYTES /*Q, dO*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ + 256;
+constexpr size_t SMEM_BWD_KV = 1024 + 2 * TILE_BYTES /*K, V*/ + 2 * 2 * TILE_BYTES /*Q,dO x2*/ +
+                               2 * 4 * TQ * 4 /*per-query operands x2*/ + 256;
+
+// key tiles read by query tile [q0, q0 + TQ): [0, r_end) then [m_beg, m_end)
+__device__ __forceinline__ void key_tiles(const PartGeom& g, int q0, int& r_end, int& m_beg,
+                                          int& m_end) {
+  const int last = min(q0 + TQ, g.S) - 1;
+  int i_last, d_last;
+  decode(g, last, i_last, d_last);
+  const int i_max = q0 < g.a1 ? max(i_last, min(last, g.a1 - 1)) : i_last;
+  r_end = i_max / TK + 1;
+  m_beg = m_end = 0;
+  if (last >= g.a1 && g.km1 > 0) {
+    const int first = max(q0, g.a1);
+    int i_first, d_first;
+    decode(g, first, i_first, d_first);
+    const int lo = g.a1 + (i_first - g.a0) * g.km1;
+    const int hi = g.a1 + (i_last - g.a0 + 1) * g.km1;
+    int mb = lo / TK, me = (hi - 1) / TK + 1;
+    if (mb < r_end) mb = r_end;
+    if (me > mb) {
+      m_beg = mb;
+      m_end = me;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                  const float* __restrict__ lse, const float* __restrict__ delta,
+                  __nv_bfloat16* __restrict__ dq, int64_t dq_ss, PartGeom g, int rep, float scale,
+                  int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sDO = sQ + TILE_BYTES;
+  uint8_t* sKV = sDO + TILE_BYTES;  // stage s: K at + s * 2 * TILE, V at + TILE
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + 4 * TILE_BYTES);
+  uint64_t* qdo_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2] S(j) and dP(j) computed
+  uint64_t* dp_free = bars + 7;   // dP(j) read by the softmax warps
+  uint64_t* ds_full = bars + 8;   // dS(j) written over S(j)
+  uint64_t* dq_full = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_qt = (g.S + TQ - 1) / TQ;
+  const int qt = num_qt - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int h = blockIdx.y;
+  const int kvh = h / rep;
+  const int q0 = qt * TQ;
+  int r_end, m_beg, m_end;
+  key_tiles(g, q0, r_end, m_beg, m_end);
+  const int n = r_end + (m_end - m_beg);
+  auto tile_at = [&](int j) { return j < r_end ? j : m_beg + (j - r_end); };
+
+  if (threadIdx.x == 0) {
+    mbar_init(qdo_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+    }
+    mbar_init(dp_free, 8);
+    mbar_init(ds_full, 8);
+    mbar_init(dq_full, 1);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tDQ = tmem, tDP = tmem + 128, tS = tmem + 256;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      bool ok = true;
+      int last_st = -1;
+      uint32_t last_ph = 0;
+      mbar_arrive_expect_tx(qdo_full, 2 * TILE_BYTES);
+      tma_load_2d(sQ, &tmQ, qdo_full, h * HD, q0);
+      tma_load_2d(sQ + CHUNK, &tmQ, qdo_full, h * HD + 64, q0);
+      tma_load_2d(sDO, &tmDO, qdo_full, h * HD, q0);
+      tma_load_2d(sDO + CHUNK, &tmDO, qdo_full, h * HD + 64, q0);
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, status, 311)) { ok = false; break; }
+        const int k0 = tile_at(j) * TK;
+        uint8_t* k_dst = sKV + st * 2 * TILE_BYTES;
+        uint8_t* v_dst = k_dst + TILE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        tma_load_2d(k_dst, &tmK, &kv_full[st], kvh * HD, k0);
+        tma_load_2d(k_dst + CHUNK, &tmK, &kv_full[st], kvh * HD + 64, k0);
+        tma_load_2d(v_dst, &tmV, &kv_full[st], kvh * HD, k0);
+        tma_load_2d(v_dst + CHUNK, &tmV, &kv_full[st], kvh * HD + 64, k0);
+        last_st = st;
+        last_ph = ph;
+      }
+      if (!ok && last_st >= 0) mbar_wait(&kv_full[last_st], last_ph, nullptr, 0);
+      mbar_wait(qdo_full, 0, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t ID_SS = idesc_bf16(TQ, TK, false, false);  // S, dP
+      constexpr uint32_t ID_DQ = idesc_bf16(TQ, HD, false, true);   // dQ += dS K
+      const uint32_t q_base = smem_u32(sQ), do_base = smem_u32(sDO);
+      auto issue_s = [&](int j) {
+        const uint32_t k_base = smem_u32(sKV + (j & 1) * 2 * TILE_BYTES);
+        const uint32_t d = tS + (j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(d, sw128_desc(q_base + off, 16, 1024), sw128_desc(k_base + off, 16, 1024),
+                      ID_SS, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_dp = [&](int j) {
+        const uint32_t v_base = smem_u32(sKV + (j & 1) * 2 * TILE_BYTES + TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(tDP, sw128_desc(do_base + off, 16, 1024), sw128_desc(v_base + off, 16, 1024),
+                      ID_SS, kk > 0 ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(qdo_full, 0, status, 312);
+      if (ok && n > 0) {
+        ok = mbar_wait(&kv_full[0], 0, status, 313);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0);
+          issue_dp(0);
+          mma_commit(&s_full[0]);
+        }
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n) {
+          if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, status, 314)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(j + 1);  // other S buffer: its dS(j-1) was consumed by dQ(j-1) before
+          if (!mbar_wait(dp_free, j & 1, status, 315)) { ok = false; break; }
+          tc_fence_after();
+          issue_dp(j + 1);
+          mma_commit(&s_full[(j + 1) & 1]);
+        }
+        if (!mbar_wait(ds_full, j & 1, status, 316)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(sKV + (j & 1) * 2 * TILE_BYTES);
+        const uint32_t a = tS + (j & 1) * 128;
+        // packed dS: keys 0..63 in columns 0..31, keys 64..127 in columns 64..95
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk)
+          mma_bf16_ts(tDQ, a + (kk >> 2) * 64 + (kk & 3) * 8,
+                      sw128_desc(k_base + kk * 2048, CHUNK, 1024), ID_DQ,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&kv_empty[j & 1]);
+      }
+      if (ok) mma_commit(dq_full);
+    }
+  } else {
+    // ---------------- softmax warps: query row per TMEM lane, half of the key columns ----
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int cb = half * 64;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int s = q0 + row;
+    const bool valid = s < g.S;
+    int qi = -1, qd = 0;
+    float l2 = 0.f, dl = 0.f;
+    if (valid) {
+      decode(g, s, qi, qd);
+      l2 = lse[(int64_t)h * g.S + s] * kLog2e;
+      dl = delta[(int64_t)h * g.S + s];
+    }
+    const int lo = qd > 0 ? g.a1 + (qi - g.a0) * g.km1 : 0;
+    const float scale_log2 = scale * kLog2e;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, status, 317)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tSj = tS + (j & 1) * 128 + lane_off;
+      float sv[64], dpv[64];
+      tmem_ld32(tSj + cb, sv);
+      tmem_ld32(tSj + cb + 32, sv + 32);
+      tmem_ld32(tDP + lane_off + cb, dpv);
+      tmem_ld32(tDP + lane_off + cb + 32, dpv + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dp_free);
+      const int k0 = tile_at(j) * TK + cb;
+      const bool full = k0 + 63 <= qi;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 64; c += 2) {
+        float dd[2];
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int ks = k0 + c + t;
+          const bool allow = full || ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
+          const float p = allow ? ex2_approx(sv[c + t] * scale_log2 - l2) : 0.f;
+          dd[t] = p * (dpv[c + t] - dl);
+        }
+        pk[c / 2] = pack_bf16x2(dd[0], dd[1]);
+      }
+      // packed dS over the first 32 of this half's own S columns (already in registers)
+      tmem_st32(tSj + cb, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+    if (ok && n > 0 && mbar_wait(dq_full, 0, status, 318)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = cb; c < cb + 64; c += 32) {
+        float v[32];
+        tmem_ld32(tDQ + lane_off + c, v);
+        tmem_wait_ld();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(dq + (int64_t)s * dq_ss + h * HD + c);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16x2(v[8 * q] * scale, v[8 * q + 1] * scale),
+                                pack_bf16x2(v[8 * q + 2] * scale, v[8 * q + 3] * scale),
+                                pack_bf16x2(v[8 * q + 4] * scale, v[8 * q + 5] * scale),
+                                pack_bf16x2(v[8 * q + 6] * scale, v[8 * q + 7] * scale));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                   const float* __restrict__ lse, const float* __restrict__ delta,
+                   float* __restrict__ dk_acc, float* __restrict__ dv_acc, PartGeom g, int Hkv,
+                   int rep, float scale, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE_BYTES;
+  uint8_t* sQD = sV + TILE_BYTES;  // stage s: Q at + s * 2 * TILE, dO at + TILE
+  float* sL = reinterpret_cast<float*>(sQD + 4 * TILE_BYTES);  // [2][TQ] lse * log2(e)
+  float* sD = sL + 2 * TQ;                                       // [2][TQ] delta
+  int* sA = reinterpret_cast<int*>(sD + 2 * TQ);                 // [2][TQ] query anchor
+  int* sDp = sA + 2 * TQ;                                        // [2][TQ] query depth
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDp + 2 * TQ);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* st_full = bars + 5;    // S^T(it) computed
+  uint64_t* dpt_full = bars + 6;   // dP^T(it) computed
+  uint64_t* p_full = bars + 7;     // P^T(it) written over S^T
+  uint64_t* ds_full = bars + 8;    // dS^T(it) written over dP^T
+  uint64_t* acc_full = bars + 9;
+  uint64_t* meta_free = bars + 10;  // [2] per-query operands of a stage consumed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x;  // low key tiles are read by the most query tiles: first
+  const int h = blockIdx.y;
+  const int kvh = h / rep;
+  const int k0 = kt * TK;
+  const Ranges qr = query_tiles(g, k0);
+  const int n_it = qr.count();
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&meta_free[i], 8);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(dpt_full, 1);
+    mbar_init(p_full, 8);
+    mbar_init(ds_full, 8);
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tDK = tmem, tDV = tmem + 128, tS = tmem + 256, tDP = tmem + 384;
+
+  if (warp == 0) {
+    // TMA of K, V and the Q / dO ring; the whole warp stages each query tile's
+    // (lse, delta, anchor, depth) once it may overwrite that stage's copy
+    bool ok = true;
+    int last_st = -1;
+    uint32_t last_ph = 0;
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_2d(sK, &tmK, kv_full, kvh * HD, k0);
+      tma_load_2d(sK + CHUNK, &tmK, kv_full, kvh * HD + 64, k0);
+      tma_load_2d(sV, &tmV, kv_full, kvh * HD, k0);
+      tma_load_2d(sV + CHUNK, &tmV, kv_full, kvh * HD + 64, k0);
+    }
+    __syncwarp();
+    for (int it = 0; it < n_it && ok; ++it) {
+      const int st = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      const int q0 = qr.at(it) * TQ;
+      // per-query operands: lanes cover the tile's 128 queries, 4 each
+      if (!mbar_wait(&meta_free[st], ph ^ 1u, status, 320)) { ok = false; }
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int r = u * 32 + lane;
+        const int q = q0 + r;
+        float lv = INFINITY, dl = 0.f;
+        int qa = -1, qd = 0;
+        if (q < g.S) {
+          lv = lse[(int64_t)h * g.S + q] * kLog2e;
+          dl = delta[(int64_t)h * g.S + q];
+          decode(g, q, qa, qd);
+        }
+        sL[st * TQ + r] = lv;
+        sD[st * TQ + r] = dl;
+        sA[st * TQ + r] = qa;
+        sDp[st * TQ + r] = qd;
+      }
+      __syncwarp();
+      if (elect_one()) {
+        // the stage's shared-memory operand writes precede the consumers' waits
+        if (!mbar_wait(&qdo_empty[st], ph ^ 1u, status, 321)) ok = false;
+        if (ok) {
+          uint8_t* q_dst = sQD + st * 2 * TILE_BYTES;
+          uint8_t* do_dst = q_dst + TILE_BYTES;
+          mbar_arrive_expect_tx(&qdo_full[st], 2 * TILE_BYTES);  // release: covers sL..sDp
+          tma_load_2d(q_dst, &tmQ, &qdo_full[st], h * HD, q0);
+          tma_load_2d(q_dst + CHUNK, &tmQ, &qdo_full[st], h * HD + 64, q0);
+          tma_load_2d(do_dst, &tmDO, &qdo_full[st], h * HD, q0);
+          tma_load_2d(do_dst + CHUNK, &tmDO, &qdo_full[st], h * HD + 64, q0);
+          last_st = st;
+          last_ph = ph;
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (elect_one()) {
+      mbar_wait(kv_full, 0, nullptr, 0);
+      if (last_st >= 0) mbar_wait(&qdo_full[last_st], last_ph, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t ID_KK = idesc_bf16(TK, TQ, false, false);  // S^T, dP^T
+      constexpr uint32_t ID_KM = idesc_bf16(TK, HD, false, true);   // dV, dK (A from TMEM)
+      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
+      auto issue_st = [&](int it) {
+        const uint32_t q_base = smem_u32(sQD + (it & 1) * 2 * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(tS, sw128_desc(k_base + off, 16, 1024), sw128_desc(q_base + off, 16, 1024),
+                      ID_KK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_dpt = [&](int it) {
+        const uint32_t do_base = smem_u32(sQD + (it & 1) * 2 * TILE_BYTES) + TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+          mma_bf16_ss(tDP, sw128_desc(v_base + off, 16, 1024), sw128_desc(do_base + off, 16, 1024),
+                      ID_KK, kk > 0 ? 1u : 0u);
+        }
+      };
+      // packed P^T / dS^T: queries 0..63 in columns 0..31, 64..127 in 64..95
+      auto a_col = [](int kk) { return (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8); };
+      bool ok = mbar_wait(kv_full, 0, status, 322);
+      if (ok && n_it > 0) {
+        ok = mbar_wait(&qdo_full[0], 0, status, 323);
+        if (ok) {
+          tc_fence_after();
+          issue_st(0);
+          mma_commit(st_full);
+          issue_dpt(0);
+          mma_commit(dpt_full);
+        }
+      }
+      for (int it = 0; it < n_it && ok; ++it) {
+        const uint32_t q_base = smem_u32(sQD + (it & 1) * 2 * TILE_BYTES);
+        const uint32_t do_base = q_base + TILE_BYTES;
+        const uint32_t acc = it > 0 ? 1u : 0u;
+        const bool more = it + 1 < n_it;
+        if (!mbar_wait(p_full, it & 1, status, 324)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TQ / 16; ++kk)
+          mma_bf16_ts(tDV, tS + a_col(kk), sw128_desc(do_base + kk * 2048, CHUNK, 1024), ID_KM,
+                      (acc | kk) != 0 ? 1u : 0u);
+        if (more) {
+          // S^T of the next query tile overlaps the dS^T arithmetic of this one
+          if (!mbar_wait(&qdo_full[(it + 1) & 1], ((it + 1) >> 1) & 1, status, 326)) { ok = false; break; }
+          tc_fence_after();
+          issue_st(it + 1);
+          mma_commit(st_full);
+        }
+        if (!mbar_wait(ds_full, it & 1, status, 325)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < TQ / 16; ++kk)
+          mma_bf16_ts(tDK, tDP + a_col(kk), sw128_desc(q_base + kk * 2048, CHUNK, 1024), ID_KM,
+                      (acc | kk) != 0 ? 1u : 0u);
+        mma_commit(&qdo_empty[it & 1]);
+        if (more) {
+          issue_dpt(it + 1);  // after dK of this tile read dS^T (in-order tcgen05)
+          mma_commit(dpt_full);
+        }
+      }
+      if (ok) mma_commit(acc_full);
+    }
+  } else {
+    // ---------------- softmax / epilogue warps (256 threads) ----------------
+    // thread = key row (TMEM lane); `half` owns query columns [64 half, 64 half + 64)
+    // and writes its packed P^T / dS^T into the first 32 of those columns
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int cb = half * 64;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int kj = k0 + row;
+    const bool kvalid = kj < g.S;
+    int ka = 0, ke = 0;
+    if (kvalid) decode(g, kj, ka, ke);
+    const float scale_log2 = scale * kLog2e;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = qr.at(it) * TQ;
+      const int buf = it & 1;
+      const bool full = tile_fully_allowed(g, q0, k0);
+      // ---- P^T = 2^(S^T c - lse') ----
+      // the stage's per-query operands were written before its TMA was armed
+      if (!mbar_wait(&qdo_full[buf], (it >> 1) & 1, status, 330)) { ok = false; break; }
+      if (!mbar_wait(st_full, it & 1, status, 327)) { ok = false; break; }
+      tc_fence_after();
+      float pv[64];
+      tmem_ld32(tS + lane_off + cb, pv);
+      tmem_ld32(tS + lane_off + cb + 32, pv + 32);
+      tmem_wait_ld();
+      const float4* L4 = reinterpret_cast<const float4*>(sL + buf * TQ + cb);
+      if (full) {
+#pragma unroll
+        for (int c = 0; c < 64; c += 4) {
+          const float4 l4 = L4[c / 4];
+          pv[c] = ex2_approx(pv[c] * scale_log2 - l4.x);
+          pv[c + 1] = ex2_approx(pv[c + 1] * scale_log2 - l4.y);
+          pv[c + 2] = ex2_approx(pv[c + 2] * scale_log2 - l4.z);
+          pv[c + 3] = ex2_approx(pv[c + 3] * scale_log2 - l4.w);
+        }
+      } else {
+        const float* L = sL + buf * TQ + cb;
+        const int* QA = sA + buf * TQ + cb;
+        const int* QD = sDp + buf * TQ + cb;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const int qa = QA[c];
+          const bool allow =
+              kvalid && qa >= 0 && (ke == 0 ? (ka <= qa) : (ka == qa && ke <= QD[c]));
+          pv[c] = allow ? ex2_approx(pv[c] * scale_log2 - L[c]) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 32) {
+        uint32_t pw[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) pw[c / 2] = pack_bf16x2(pv[c0 + c], pv[c0 + c + 1]);
+        tmem_st16(tS + lane_off + cb + c0 / 2, pw);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // ---- dS^T = P^T (dP^T - delta) ----
+      if (!mbar_wait(dpt_full, it & 1, status, 328)) { ok = false; break; }
+      tc_fence_after();
+      const float4* D4 = reinterpret_cast<const float4*>(sD + buf * TQ + cb);
+      // 16 columns at a time: packed dS^T for columns [c0, c0 + 16) lands in packed
+      // columns [c0 / 2, c0 / 2 + 8), which this thread has already read
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 16) {
+        float dv[16];
+        tmem_ld16(tDP + lane_off + cb + c0, dv);
+        tmem_wait_ld();
+        uint32_t pw[8];
+#pragma unroll
+        for (int c = 0; c < 16; c += 4) {
+          const float4 d4 = D4[(c0 + c) / 4];
+          pw[c / 2] = pack_bf16x2(pv[c0 + c] * (dv[c] - d4.x), pv[c0 + c + 1] * (dv[c + 1] - d4.y));
+          pw[c / 2 + 1] =
+              pack_bf16x2(pv[c0 + c + 2] * (dv[c + 2] - d4.z), pv[c0 + c + 3] * (dv[c + 3] - d4.w));
+        }
+        tmem_st8(tDP + lane_off + cb + c0 / 2, pw);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(ds_full);
+        mbar_arrive(&meta_free[buf]);
+      }
+    }
+    // this head's dK, dV tile (key row per TMEM lane) -> the KV head's fp32 accumulators
+    if (ok && n_it > 0 && mbar_wait(acc_full, 0, status, 329)) {
+      tc_fence_after();
+      const int64_t kv_ld = (int64_t)Hkv * HD;
+#pragma unroll 1
+      for (int c0 = cb; c0 < cb + 64; c0 += 32) {
+        float v[32];
+        tmem_ld32(tDK + lane_off + c0, v);
+        tmem_wait_ld();
+        if (kvalid) atomic_add_row32(dk_acc + (int64_t)kj * kv_ld + kvh * HD + c0, v, 1.f);
+        tmem_ld32(tDV + lane_off + c0, v);
+        tmem_wait_ld();
+        if (kvalid) atomic_add_row32(dv_acc + (int64_t)kj * kv_ld + kvh * HD + c0, v, 1.f);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[h, s] = sum_d dO * O (fp32); zero the dQ accumulator row (when given) and, for the
 // first Hkv heads, the dK / dV accumulator rows
 __global__ void attn_bwd_prep_kernel(int S, int Hq, int Hkv, const __nv_bfloat16* __restrict__ o,
                                      int64_t o_ss, const __nv_bfloat16* __restrict__ dout,
@@ -400,7 +976,7 @@ __global__ void attn_bwd_prep_kernel(int S, int Hq, int Hkv, const __nv_bfloat16
   acc = warp_sum(acc);
   if (lane == 0) delta[(int64_t)h * S + s] = acc;
   const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-  reinterpret_cast<float4*>(dq_acc + (int64_t)s * Hq * HD + h * HD)[lane] = z;
+  if (dq_acc) reinterpret_cast<float4*>(dq_acc + (int64_t)s * Hq * HD + h * HD)[lane] = z;
   if (h < Hkv) {
     reinterpret_cast<float4*>(dk_acc + (int64_t)s * Hkv * HD + h * HD)[lane] = z;
     reinterpret_cast<float4*>(dv_acc + (int64_t)s * Hkv * HD + h * HD)[lane] = z;
@@ -447,7 +1023,7 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
                        const void* dout, int64_t do_ss, const float* lse, void* dq,
                        int64_t dq_ss, void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
                        float* delta, float* acc, const MaskSpec& m, int* status,
-                       cudaStream_t st) {
+                       cudaStream_t st, int variant) {
   PE_CHECK_ARG(o_ss % 8 == 0 && do_ss % 8 == 0 && dq_ss % 8 == 0 && dk_ss % 8 == 0 &&
                    dv_ss % 8 == 0 && al16(o) && al16(dout) && al16(dq) && al16(dk) && al16(dv),
                "attention backward (tcgen05): operands must be 16-byte aligned");
@@ -466,11 +1042,29 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
     const int warps = Si * Hq;
     attn_bwd_prep_kernel<<<(warps + 7) / 8, 256, 0, st>>>(
         Si, Hq, Hkv, (const __nv_bfloat16*)o, o_ss, (const __nv_bfloat16*)dout, do_ss, delta,
-        dq_acc, dk_acc, dv_acc);
+        variant == 0 ? nullptr : dq_acc, dk_acc, dv_acc);
     PE_LAUNCHED();
   }
   PartGeom g{Si, (int)m.a0, (int)m.a1, m.kd - 1};
   const float scale = 1.0f / sqrtf((float)HD);
+  if (variant == 0) {
+    PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_q_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BWD_Q));
+    PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BWD_KV));
+    dim3 gq((unsigned)((S + TQ - 1) / TQ), (unsigned)Hq);
+    attn_bwd_q_kernel<<<gq, kThreads, SMEM_BWD_Q, st>>>(tq, tk, tv, tdo, lse, delta,
+                                                        (__nv_bfloat16*)dq, dq_ss, g, Hq / Hkv,
+                                                        scale, status);
+    PE_LAUNCHED();
+    dim3 gkv((unsigned)((S + TK - 1) / TK), (unsigned)Hq);
+    attn_bwd_kv_kernel<<<gkv, kThreads, SMEM_BWD_KV, st>>>(tq, tk, tv, tdo, lse, delta, dk_acc,
+                                                           dv_acc, g, Hkv, Hq / Hkv, scale, status);
+    PE_LAUNCHED();
+    rc = launch_cast(Si, Hkv * HD, dk_acc, scale, dk, dk_ss, st);
+    if (!rc) rc = launch_cast(Si, Hkv * HD, dv_acc, 1.f, dv, dv_ss, st);
+    return rc;
+  }
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)SMEM_BWD));
   dim3 grid((unsigned)((S + TK - 1) / TK), (unsigned)Hq);
