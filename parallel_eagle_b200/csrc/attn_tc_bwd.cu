@@ -396,6 +396,11 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 //   dK / dV tile is added (fp32) into the KV head's accumulator at the end.
 //   TMEM: dK 0..127, dV 128..255, S^T 256..383, dP^T 384..511.
 // ------------------------------------------------------------------------ //
+// dK/dV kernel: four compute warps per TMEM lane quarter, each owning 32 of the
+// 128 query columns (more warps in flight to hide TMEM and SFU latency)
+constexpr int kKvParts = 4;
+constexpr int kKvThreads = 64 + 128 * kKvParts;
+constexpr int kKvCols = TQ / kKvParts;
 constexpr size_t SMEM_BWD_Q = 1024 + 2 * TILE_BYTES /*Q, dO*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ + 256;
 constexpr size_t SMEM_BWD_KV = 1024 + 2 * TILE_BYTES /*K, V*/ + 2 * 2 * TILE_BYTES /*Q,dO x2*/ +
                                2 * 4 * TQ * 4 /*per-query operands x2*/ + 256;
@@ -424,7 +429,7 @@ __device__ __forceinline__ void key_tiles(const PartGeom& g, int q0, int& r_end,
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kKvThreads, 1)
 attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                   const float* __restrict__ lse, const float* __restrict__ delta,
@@ -464,8 +469,8 @@ attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
     }
-    mbar_init(dp_free, 8);
-    mbar_init(ds_full, 8);
+    mbar_init(dp_free, 4 * kKvParts);
+    mbar_init(ds_full, 4 * kKvParts);
     mbar_init(dq_full, 1);
     fence_barrier_init();
     fence_proxy_async();
@@ -556,10 +561,12 @@ attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
         tc_fence_after();
         const uint32_t k_base = smem_u32(sKV + (j & 1) * 2 * TILE_BYTES);
         const uint32_t a = tS + (j & 1) * 128;
-        // packed dS: keys 0..63 in columns 0..31, keys 64..127 in columns 64..95
+        // packed dS: the keys of softmax part p (columns [p C, p C + C), C = kKvCols)
+        // in columns [p C, p C + C / 2)
+        constexpr int steps = kKvCols / 16;
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk)
-          mma_bf16_ts(tDQ, a + (kk >> 2) * 64 + (kk & 3) * 8,
+          mma_bf16_ts(tDQ, a + (kk / steps) * kKvCols + (kk % steps) * 8,
                       sw128_desc(k_base + kk * 2048, CHUNK, 1024), ID_DQ,
                       (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&kv_empty[j & 1]);
@@ -567,10 +574,13 @@ attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
       if (ok) mma_commit(dq_full);
     }
   } else {
-    // ---------------- softmax warps: query row per TMEM lane, half of the key columns ----
+    // ---------------- softmax warps (4 x kKvParts): query row per TMEM lane ----
+    // part p owns key columns [p C, p C + C) and writes its packed dS into the first
+    // C / 2 of them, which only it reads
+    constexpr int C = kKvCols;
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int cb = half * 64;
+    const int part = (warp - 2) >> 2;
+    const int cb = part * C;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int s = q0 + row;
@@ -589,32 +599,35 @@ attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
       if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, status, 317)) { ok = false; break; }
       tc_fence_after();
       const uint32_t tSj = tS + (j & 1) * 128 + lane_off;
-      float sv[64], dpv[64];
-      tmem_ld32(tSj + cb, sv);
-      tmem_ld32(tSj + cb + 32, sv + 32);
-      tmem_ld32(tDP + lane_off + cb, dpv);
-      tmem_ld32(tDP + lane_off + cb + 32, dpv + 32);
+      float sv[C], dpv[C];
+#pragma unroll
+      for (int c = 0; c < C; c += 32) {
+        tmem_ld32(tSj + cb + c, sv + c);
+        tmem_ld32(tDP + lane_off + cb + c, dpv + c);
+      }
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dp_free);
       const int k0 = tile_at(j) * TK + cb;
-      const bool full = k0 + 63 <= qi;
-      uint32_t pk[32];
+      const bool full = k0 + C - 1 <= qi;
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        float dd[2];
+      for (int c0 = 0; c0 < C; c0 += 16) {
+        uint32_t pk[8];
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const int ks = k0 + c + t;
-          const bool allow = full || ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
-          const float p = allow ? ex2_approx(sv[c + t] * scale_log2 - l2) : 0.f;
-          dd[t] = p * (dpv[c + t] - dl);
+        for (int c = 0; c < 16; c += 2) {
+          float dd[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int ks = k0 + c0 + c + t;
+            const bool allow = full || ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
+            const float p = allow ? ex2_approx(sv[c0 + c + t] * scale_log2 - l2) : 0.f;
+            dd[t] = p * (dpv[c0 + c + t] - dl);
+          }
+          pk[c / 2] = pack_bf16x2(dd[0], dd[1]);
         }
-        pk[c / 2] = pack_bf16x2(dd[0], dd[1]);
+        tmem_st8(tSj + cb + c0 / 2, pk);
       }
-      // packed dS over the first 32 of this half's own S columns (already in registers)
-      tmem_st32(tSj + cb, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -623,18 +636,18 @@ attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
     if (ok && n > 0 && mbar_wait(dq_full, 0, status, 318)) {
       tc_fence_after();
 #pragma unroll 1
-      for (int c = cb; c < cb + 64; c += 32) {
+      for (int c = cb; c < cb + C; c += 32) {
         float v[32];
         tmem_ld32(tDQ + lane_off + c, v);
         tmem_wait_ld();
         if (valid) {
           uint4* dst = reinterpret_cast<uint4*>(dq + (int64_t)s * dq_ss + h * HD + c);
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(pack_bf16x2(v[8 * q] * scale, v[8 * q + 1] * scale),
-                                pack_bf16x2(v[8 * q + 2] * scale, v[8 * q + 3] * scale),
-                                pack_bf16x2(v[8 * q + 4] * scale, v[8 * q + 5] * scale),
-                                pack_bf16x2(v[8 * q + 6] * scale, v[8 * q + 7] * scale));
+          for (int u = 0; u < 4; ++u)
+            dst[u] = make_uint4(pack_bf16x2(v[8 * u] * scale, v[8 * u + 1] * scale),
+                                pack_bf16x2(v[8 * u + 2] * scale, v[8 * u + 3] * scale),
+                                pack_bf16x2(v[8 * u + 4] * scale, v[8 * u + 5] * scale),
+                                pack_bf16x2(v[8 * u + 6] * scale, v[8 * u + 7] * scale));
         }
       }
     }
@@ -648,7 +661,7 @@ attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kKvThreads, 1)
 attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                    const float* __restrict__ lse, const float* __restrict__ delta,
@@ -689,12 +702,12 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qdo_full[i], 1);
       mbar_init(&qdo_empty[i], 1);
-      mbar_init(&meta_free[i], 8);
+      mbar_init(&meta_free[i], 4 * kKvParts);
     }
     mbar_init(st_full, 1);
     mbar_init(dpt_full, 1);
-    mbar_init(p_full, 8);
-    mbar_init(ds_full, 8);
+    mbar_init(p_full, 4 * kKvParts);
+    mbar_init(ds_full, 4 * kKvParts);
     mbar_init(acc_full, 1);
     fence_barrier_init();
     fence_proxy_async();
@@ -792,8 +805,12 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
                       ID_KK, kk > 0 ? 1u : 0u);
         }
       };
-      // packed P^T / dS^T: queries 0..63 in columns 0..31, 64..127 in 64..95
-      auto a_col = [](int kk) { return (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8); };
+      // packed P^T / dS^T: the queries of compute part p (columns [p C, p C + C),
+      // C = kKvCols) in columns [p C, p C + C / 2)
+      auto a_col = [](int kk) {
+        constexpr int steps = kKvCols / 16;  // 16-query K steps per part
+        return (uint32_t)((kk / steps) * kKvCols + (kk % steps) * 8);
+      };
       bool ok = mbar_wait(kv_full, 0, status, 322);
       if (ok && n_it > 0) {
         ok = mbar_wait(&qdo_full[0], 0, status, 323);
@@ -838,12 +855,13 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       if (ok) mma_commit(acc_full);
     }
   } else {
-    // ---------------- softmax / epilogue warps (256 threads) ----------------
-    // thread = key row (TMEM lane); `half` owns query columns [64 half, 64 half + 64)
-    // and writes its packed P^T / dS^T into the first 32 of those columns
+    // ---------------- compute warps (4 x kKvParts): thread = key row (TMEM lane) ----
+    // part p owns query columns [p C, p C + C) and writes its packed P^T / dS^T into
+    // the first C / 2 of those columns, which only it reads
+    constexpr int C = kKvCols;
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int cb = half * 64;
+    const int part = (warp - 2) >> 2;
+    const int cb = part * C;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int kj = k0 + row;
@@ -861,14 +879,14 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       if (!mbar_wait(&qdo_full[buf], (it >> 1) & 1, status, 330)) { ok = false; break; }
       if (!mbar_wait(st_full, it & 1, status, 327)) { ok = false; break; }
       tc_fence_after();
-      float pv[64];
-      tmem_ld32(tS + lane_off + cb, pv);
-      tmem_ld32(tS + lane_off + cb + 32, pv + 32);
-      tmem_wait_ld();
-      const float4* L4 = reinterpret_cast<const float4*>(sL + buf * TQ + cb);
-      if (full) {
+      float pv[C];
 #pragma unroll
-        for (int c = 0; c < 64; c += 4) {
+      for (int c = 0; c < C; c += 32) tmem_ld32(tS + lane_off + cb + c, pv + c);
+      tmem_wait_ld();
+      if (full) {
+        const float4* L4 = reinterpret_cast<const float4*>(sL + buf * TQ + cb);
+#pragma unroll
+        for (int c = 0; c < C; c += 4) {
           const float4 l4 = L4[c / 4];
           pv[c] = ex2_approx(pv[c] * scale_log2 - l4.x);
           pv[c + 1] = ex2_approx(pv[c + 1] * scale_log2 - l4.y);
@@ -880,7 +898,7 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         const int* QA = sA + buf * TQ + cb;
         const int* QD = sDp + buf * TQ + cb;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < C; ++c) {
           const int qa = QA[c];
           const bool allow =
               kvalid && qa >= 0 && (ke == 0 ? (ka <= qa) : (ka == qa && ke <= QD[c]));
@@ -888,11 +906,11 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
         }
       }
 #pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 32) {
-        uint32_t pw[16];
+      for (int c0 = 0; c0 < C; c0 += 16) {
+        uint32_t pw[8];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) pw[c / 2] = pack_bf16x2(pv[c0 + c], pv[c0 + c + 1]);
-        tmem_st16(tS + lane_off + cb + c0 / 2, pw);
+        for (int c = 0; c < 16; c += 2) pw[c / 2] = pack_bf16x2(pv[c0 + c], pv[c0 + c + 1]);
+        tmem_st8(tS + lane_off + cb + c0 / 2, pw);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -905,7 +923,7 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       // 16 columns at a time: packed dS^T for columns [c0, c0 + 16) lands in packed
       // columns [c0 / 2, c0 / 2 + 8), which this thread has already read
 #pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 16) {
+      for (int c0 = 0; c0 < C; c0 += 16) {
         float dv[16];
         tmem_ld16(tDP + lane_off + cb + c0, dv);
         tmem_wait_ld();
@@ -932,7 +950,7 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       tc_fence_after();
       const int64_t kv_ld = (int64_t)Hkv * HD;
 #pragma unroll 1
-      for (int c0 = cb; c0 < cb + 64; c0 += 32) {
+      for (int c0 = cb; c0 < cb + C; c0 += 32) {
         float v[32];
         tmem_ld32(tDK + lane_off + c0, v);
         tmem_wait_ld();
@@ -1053,12 +1071,12 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
     PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BWD_KV));
     dim3 gq((unsigned)((S + TQ - 1) / TQ), (unsigned)Hq);
-    attn_bwd_q_kernel<<<gq, kThreads, SMEM_BWD_Q, st>>>(tq, tk, tv, tdo, lse, delta,
+    attn_bwd_q_kernel<<<gq, kKvThreads, SMEM_BWD_Q, st>>>(tq, tk, tv, tdo, lse, delta,
                                                         (__nv_bfloat16*)dq, dq_ss, g, Hq / Hkv,
                                                         scale, status);
     PE_LAUNCHED();
     dim3 gkv((unsigned)((S + TK - 1) / TK), (unsigned)Hq);
-    attn_bwd_kv_kernel<<<gkv, kThreads, SMEM_BWD_KV, st>>>(tq, tk, tv, tdo, lse, delta, dk_acc,
+    attn_bwd_kv_kernel<<<gkv, kKvThreads, SMEM_BWD_KV, st>>>(tq, tk, tv, tdo, lse, delta, dk_acc,
                                                            dv_acc, g, Hkv, Hq / Hkv, scale, status);
     PE_LAUNCHED();
     rc = launch_cast(Si, Hkv * HD, dk_acc, scale, dk, dk_ss, st);
