@@ -296,8 +296,12 @@ def run_ours(args):
     wall_ms = (time.perf_counter() - w0) * 1e3 / args.steps
 
     # ---- roofline of the dominant kernel: the tensor-core GEMM, gate/up shape of the step
+    # both rooflines time one kernel family alone, so they are set against the burst
+    # peak; a short idle first lets the clocks leave the step loop's power-capped state
     hbm, peak_burst, peak_sus, src = _peaks()
-    roof = gemm_roofline(c, dev, peak_sus, src)
+    time.sleep(1.0)
+    roof = gemm_roofline(c, dev, peak_burst, src)
+    time.sleep(1.0)
     attn = attention_roofline(c, dev, peak_burst, src)
     step_tflops = step_flops_per_sequence(c) * B / (ms / 1e3) / 1e12
 
@@ -393,6 +397,38 @@ def lmhead_case(c, dev):
     return run, 2.0 * 2 * R * V * H, None
 
 
+def elementwise_cases(c, dev):
+    """The step's memory-bound kernels on one stacked pass of a config-2 sequence
+    (13312 slot rows): name -> (run, algorithmic HBM bytes per run)."""
+    from parallel_eagle_b200 import ops
+
+    H, I = c["hidden"], c["intermediate"]
+    nh, nkv, hd = c["n_heads"], c["n_kv_heads"], c["hidden"] // c["n_heads"]
+    R = 13312
+    g = torch.Generator(device=dev).manual_seed(17)
+    bf = torch.bfloat16
+    x = torch.randn(R, H, generator=g, device=dev).to(bf)
+    dy = torch.randn(R, H, generator=g, device=dev).to(bf)
+    res = torch.randn(R, H, generator=g, device=dev).to(bf)
+    w = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(bf)
+    y, rstd = ops.rmsnorm_fwd(x, w, 1e-5)
+    gu = torch.randn(R, 2 * I, generator=g, device=dev).to(bf)
+    da = torch.randn(R, I, generator=g, device=dev).to(bf)
+    act = torch.empty(R, I, dtype=bf, device=dev)
+    dgu = torch.empty(R, 2 * I, dtype=bf, device=dev)
+    qkv = torch.randn(R, (nh + 2 * nkv) * hd, generator=g, device=dev).to(bf)
+    pos = torch.randint(0, 4096, (R,), generator=g, device=dev)
+    e = 2  # bytes per bf16 element
+    return {
+        "rmsnorm_fwd": (lambda: ops.rmsnorm_fwd(x, w, 1e-5, out=y), R * H * 2 * e + R * 4),
+        "rmsnorm_bwd": (lambda: ops.rmsnorm_bwd(dy, x, w, rstd, dx=y, residual=res),
+                        R * H * 4 * e + R * 4),
+        "swiglu_fwd": (lambda: ops.swiglu_fwd(gu, I, out=act), R * I * 3 * e),
+        "swiglu_bwd": (lambda: ops.swiglu_bwd(da, gu, I, out=dgu), R * I * 5 * e),
+        "rope": (lambda: ops.rope_(qkv, nh + nkv, hd, pos, 10000.0), R * (nh + nkv) * hd * 2 * e + R * 8),
+    }
+
+
 def time_case(run, reps, warmup=3, flush=None):
     """Average milliseconds of ``run`` over ``reps`` CUDA-event-timed calls on the
     current stream; ``flush`` (a buffer larger than L2) is rewritten before each."""
@@ -435,9 +471,10 @@ def gemm_roofline(c, dev, peak, src):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     ms = time_case(run, 10, flush=flush)
     achieved = flops / (ms / 1e3) / 1e12
-    return {"kernel": "gemm_tc_kernel (gate/up projection, M=4096 N=37888 K=3584)",
+    return {"kernel": "gemm_tc_pair_kernel (gate/up projection, M=4096 N=37888 K=3584; "
+                      "CTA-pair 256x256 tiles)",
             "bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-            "frac": round(achieved / peak, 4), "peak_source": f"{src} bf16_tflops_sustained",
+            "frac": round(achieved / peak, 4), "peak_source": f"{src} bf16_tflops (burst)",
             "traffic": profiled_traffic(GEMM_PROFILE), "algorithmic_bytes": int(nbytes),
             "ms": round(ms, 4)}
 
@@ -446,7 +483,7 @@ def attention_roofline(c, dev, peak, src):
     run, flops, _ = attention_case(c, dev)
     ms = time_case(run, 5)
     achieved = flops / (ms / 1e3) / 1e12
-    return {"kernels": "attn_fwd_tc_kernel + attn_bwd_tc_kernel (+ prep/cast)",
+    return {"kernels": "attn_fwd_tc2_kernel + attn_bwd_q_kernel + attn_bwd_kv_kernel (+ prep/cast)",
             "segments": c["segments"], "ms_per_sequence": round(ms, 3),
             "tflops": round(achieved, 1), "peak": peak, "frac": round(achieved / peak, 4),
             "peak_source": f"{src} bf16_tflops (burst)", "flops_per_sequence": flops}
@@ -459,6 +496,18 @@ def run_kernel(args):
     from parallel_eagle_b200 import ops
 
     c = dict(CONFIG2)
+    if args.kernel == "elementwise":
+        hbm, _, _, src = _peaks()
+        out = {}
+        for name, (run, nbytes) in elementwise_cases(c, dev).items():
+            ms = time_case(run, args.steps, warmup=args.warmup)
+            gbs = nbytes / (ms / 1e3) / 1e9
+            out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
+                         "frac_of_hbm": round(gbs / hbm, 3)}
+        ops.check_status(dev)
+        print(json.dumps({"kernel": "elementwise", "hbm_peak_gbs": hbm, "peak_source": src,
+                          "results": out}), flush=True)
+        return
     case = {"gemm": gemm_case, "attn": attention_case, "lmhead": lmhead_case}[args.kernel]
     run, flops, _ = case(c, dev)
     ms = time_case(run, args.steps, warmup=args.warmup)
@@ -531,7 +580,7 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=None, help="override per-GPU batch")
     ap.add_argument("--cpu-n", type=int, default=256, help="sequence length of the CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["gemm", "attn", "lmhead"], default=None,
+    ap.add_argument("--kernel", choices=["gemm", "attn", "lmhead", "elementwise"], default=None,
                     help="time one kernel family on its bench-sized case instead of the step")
     args = ap.parse_args(argv)
     if args.kernel:

@@ -84,6 +84,63 @@ rmsnorm_fwd_kernel(int64_t rows, int64_t H, const T* __restrict__ x, int64_t ldx
   }
 }
 
+// bf16 rows of up to 4096 columns (H % 8 == 0): one warp per row keeps the whole
+// row in registers (16-byte chunks), so x is read from HBM exactly once.
+constexpr int kFwdRegChunks = 16;
+
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_fwd_reg_kernel(int64_t rows, int64_t H, const __nv_bfloat16* __restrict__ x,
+                       int64_t ldx, const __nv_bfloat16* __restrict__ w,
+                       __nv_bfloat16* __restrict__ y, int64_t ldy, float* __restrict__ rstd,
+                       float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int ngroups = (int)(H / 8);
+  const __nv_bfloat16* xr = x + row * ldx;
+  __nv_bfloat16* yr = y + row * ldy;
+  uint4 raw[kFwdRegChunks];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kFwdRegChunks; ++i) {
+    const int gi = lane + 32 * i;
+    if (gi < ngroups) raw[i] = *reinterpret_cast<const uint4*>(xr + gi * 8);
+  }
+#pragma unroll
+  for (int i = 0; i < kFwdRegChunks; ++i) {
+    const int gi = lane + 32 * i;
+    if (gi < ngroups) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)H + eps);
+  if (lane == 0 && rstd) rstd[row] = r;
+#pragma unroll
+  for (int i = 0; i < kFwdRegChunks; ++i) {
+    const int gi = lane + 32 * i;
+    if (gi < ngroups) {
+      float f[8], g[8];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 t = __bfloat1622float2(h[k]);
+        f[2 * k] = t.x;
+        f[2 * k + 1] = t.y;
+      }
+      Vec<__nv_bfloat16, 8>::load(w + gi * 8, g);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) f[k] = (f[k] * r) * g[k];
+      Vec<__nv_bfloat16, 8>::store(yr + gi * 8, f);
+    }
+  }
+}
+
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_bwd_kernel(int64_t rows, int64_t H, const T* __restrict__ dy, int64_t lddy,
@@ -226,6 +283,102 @@ rmsnorm_bwd_chunked_kernel(int64_t rows, int64_t H, int nch, const T* __restrict
   }
 }
 
+// Backward over tiles of kTileRows rows, persistent blocks.  Per tile: one warp
+// per row reduces s = sum_c dy w x into the row coefficient; then the block walks
+// the tile row by row with thread t owning 8 contiguous columns (coalesced 16-byte
+// accesses), writing dx and keeping those columns' dW partial in 8 registers
+// across every tile it visits.  The second read of the tile's dy / x comes from
+// L2: a block's tile is a few hundred KB and only ~2 blocks per SM are in flight.
+constexpr int kTileRows = 16;
+constexpr int kTiledThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kTiledThreads)
+rmsnorm_bwd_tiled_kernel(int64_t rows, int64_t H, const T* __restrict__ dy, int64_t lddy,
+                         const T* __restrict__ x, int64_t ldx, const T* __restrict__ w,
+                         const float* __restrict__ rstd, T* dx, int64_t lddx, const T* res,
+                         int64_t ldres, float* __restrict__ dw_partial) {
+  __shared__ float s_coef[kTileRows], s_rstd[kTileRows];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ngroups = (int)(H / 8);
+  const int64_t ntiles = (rows + kTileRows - 1) / kTileRows;
+  // this thread's column groups: threadIdx.x, + blockDim.x (at most 2 for H <= 4096)
+  constexpr int kMaxGroups = 2;
+  float acc[kMaxGroups][8];
+#pragma unroll
+  for (int q = 0; q < kMaxGroups; ++q)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[q][k] = 0.f;
+  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int64_t r0 = t * kTileRows;
+    const int nr = (int)((rows - r0) < kTileRows ? (rows - r0) : kTileRows);
+    for (int i = warp; i < nr; i += kTiledThreads / 32) {
+      const int64_t r = r0 + i;
+      const T* dyr = dy + r * lddy;
+      const T* xr = x + r * ldx;
+      // all of the row's loads issue before the first multiply-add (fully unrolled,
+      // H <= 16 * 32 * 8): the row costs one memory latency, not one per chunk
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int gi = lane + 32 * i;
+        if (gi < ngroups) {
+          float a[8], b[8], g[8];
+          Vec<T, 8>::load(dyr + gi * 8, a);
+          Vec<T, 8>::load(xr + gi * 8, b);
+          Vec<T, 8>::load(w + gi * 8, g);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) s += (a[k] * g[k]) * b[k];
+        }
+      }
+      s = warp_sum(s);
+      if (lane == 0) {
+        const float rr = rstd[r];
+        s_rstd[i] = rr;
+        s_coef[i] = s * rr * rr * rr / (float)H;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < kMaxGroups; ++q) {
+      const int gi = threadIdx.x + q * kTiledThreads;
+      if (gi < ngroups) {
+        const int64_t c = (int64_t)gi * 8;
+        float g[8];
+        Vec<T, 8>::load(w + c, g);
+#pragma unroll 4
+        for (int i = 0; i < nr; ++i) {
+          const int64_t r = r0 + i;
+          float a[8], b[8], o[8];
+          Vec<T, 8>::load(dy + r * lddy + c, a);
+          Vec<T, 8>::load(x + r * ldx + c, b);
+          if (res) {
+            Vec<T, 8>::load(res + r * ldres + c, o);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) o[k] = 0.f;
+          }
+          const float rr = s_rstd[i], cf = s_coef[i];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            o[k] += rr * (a[k] * g[k]) - b[k] * cf;
+            acc[q][k] += a[k] * (b[k] * rr);
+          }
+          Vec<T, 8>::store(dx + r * lddx + c, o);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (dw_partial) {
+#pragma unroll
+    for (int q = 0; q < kMaxGroups; ++q) {
+      const int gi = threadIdx.x + q * kTiledThreads;
+      if (gi < ngroups) Vec<float, 8>::store(dw_partial + (int64_t)blockIdx.x * H + gi * 8, acc[q]);
+    }
+  }
+}
+
 // out[c] = (acc ? out[c] : 0) + sum_b partial[b, c]; fixed summation order.
 template <typename T>
 __global__ void colsum_kernel(int64_t nblk, int64_t H, const float* __restrict__ partial,
@@ -261,6 +414,13 @@ extern "C" int pe_rmsnorm_fwd(int dtype, int64_t rows, int64_t H, const void* x,
   const bool vec = H % 8 == 0 && ldx % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(y) &&
                    aligned16(w);
   dim3 grid((unsigned)ceil_div(rows, kWarps));
+  if (vec && dtype == PE_BF16 && H <= (int64_t)kFwdRegChunks * 32 * 8) {
+    rmsnorm_fwd_reg_kernel<<<grid, kWarps * 32, 0, as_stream(stream)>>>(
+        rows, H, (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, ldy,
+        rstd, eps);
+    PE_LAUNCHED();
+    return PE_OK;
+  }
   return PE_DISPATCH(dtype, T, [&] {
     if (vec)
       rmsnorm_fwd_kernel<T, 8><<<grid, kWarps * 32, 0, as_stream(stream)>>>(
@@ -274,8 +434,10 @@ extern "C" int pe_rmsnorm_fwd(int dtype, int64_t rows, int64_t H, const void* x,
 }
 
 extern "C" int64_t pe_rmsnorm_bwd_blocks(int64_t rows) {
-  int64_t b = ceil_div(rows, 4 * kWarps);
-  return b < 1 ? 1 : (b > 256 ? 256 : b);
+  // persistent tiled backward: about two blocks per SM, one tile of rows at least
+  const int64_t cap = 2 * (int64_t)sm_count();
+  int64_t b = ceil_div(rows, kTileRows);
+  return b < 1 ? 1 : (b > cap ? cap : b);
 }
 
 extern "C" int pe_rmsnorm_bwd(int dtype, int64_t rows, int64_t H, const void* dy, int64_t lddy,
@@ -293,6 +455,15 @@ extern "C" int pe_rmsnorm_bwd(int dtype, int64_t rows, int64_t H, const void* dy
                    (!residual || ldres % 8 == 0) && aligned16(dy) && aligned16(x) &&
                    aligned16(w) && aligned16(dx) && (!residual || aligned16(residual));
   const size_t smem = dw_partial ? (size_t)H * 4 : 0;
+  if (vec && H <= 8 * 2 * kTiledThreads) {
+    return PE_DISPATCH(dtype, T, [&] {
+      rmsnorm_bwd_tiled_kernel<T><<<(unsigned)nblk, kTiledThreads, 0, as_stream(stream)>>>(
+          rows, H, (const T*)dy, lddy, (const T*)x, ldx, (const T*)w, rstd, (T*)dx, lddx,
+          (const T*)residual, ldres, dw_partial);
+      PE_LAUNCHED();
+      return PE_OK;
+    });
+  }
   const bool chunked = vec && H % 256 == 0 && H / 256 <= kMaxChunks;
   if (chunked) {
     return PE_DISPATCH(dtype, T, [&] {

@@ -80,6 +80,58 @@ __global__ void rope_rowpair_kernel(int64_t rows, int heads, int hd, T* x, int64
   }
 }
 
+// bf16, half-width a multiple of 8: one thread per (row, 8 consecutive pairs); the
+// 8 angles' cos / sin once, then every head's two 16-byte half-row segments.
+__global__ void rope_vec8_kernel(int64_t rows, int heads, int hd, __nv_bfloat16* x, int64_t ldx,
+                                 const int64_t* __restrict__ pos, float theta, int inverse) {
+  using T = __nv_bfloat16;
+  const int half = hd >> 1;
+  const int groups = half >> 3;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * groups) return;
+  const int64_t row = idx / groups;
+  const int p0 = (int)(idx - row * groups) * 8;
+  const float pr = (float)pos[row];
+  float cs[8], sn[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float inv_freq = 1.0f / powf(theta, (float)(2 * (p0 + k)) / (float)hd);
+    float sv, cv;
+    sincosf(pr * inv_freq, &sv, &cv);
+    cs[k] = round_to<T>(cv);
+    sn[k] = round_to<T>(sv);
+  }
+  T* base = x + row * ldx + p0;
+  for (int h = 0; h < heads; ++h) {
+    T* hp = base + (int64_t)h * hd;
+    uint4 ua = *reinterpret_cast<const uint4*>(hp);
+    uint4 ub = *reinterpret_cast<const uint4*>(hp + half);
+    __nv_bfloat162* a2 = reinterpret_cast<__nv_bfloat162*>(&ua);
+    __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&ub);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 a = __bfloat1622float2(a2[i]), b = __bfloat1622float2(b2[i]);
+      const float c0 = cs[2 * i], c1 = cs[2 * i + 1], s0 = sn[2 * i], s1 = sn[2 * i + 1];
+      float ya0, ya1, yb0, yb1;
+      if (!inverse) {
+        ya0 = round_to<T>(round_to<T>(a.x * c0) + round_to<T>(-b.x * s0));
+        ya1 = round_to<T>(round_to<T>(a.y * c1) + round_to<T>(-b.y * s1));
+        yb0 = round_to<T>(round_to<T>(b.x * c0) + round_to<T>(a.x * s0));
+        yb1 = round_to<T>(round_to<T>(b.y * c1) + round_to<T>(a.y * s1));
+      } else {
+        ya0 = round_to<T>(round_to<T>(a.x * c0) + round_to<T>(b.x * s0));
+        ya1 = round_to<T>(round_to<T>(a.y * c1) + round_to<T>(b.y * s1));
+        yb0 = round_to<T>(round_to<T>(b.x * c0) - round_to<T>(a.x * s0));
+        yb1 = round_to<T>(round_to<T>(b.y * c1) - round_to<T>(a.y * s1));
+      }
+      a2[i] = __floats2bfloat162_rn(ya0, ya1);
+      b2[i] = __floats2bfloat162_rn(yb0, yb1);
+    }
+    *reinterpret_cast<uint4*>(hp) = ua;
+    *reinterpret_cast<uint4*>(hp + half) = ub;
+  }
+}
+
 }  // namespace
 }  // namespace pe
 
@@ -92,6 +144,15 @@ extern "C" int pe_rope(int dtype, int64_t rows, int heads, int head_dim, void* x
   PE_CHECK_ARG(ldx >= (int64_t)heads * head_dim, "rope: ldx too small");
   if (rows == 0) return PE_OK;
   const int threads = 256;
+  const bool vec8 = dtype == PE_BF16 && (head_dim / 2) % 8 == 0 && ldx % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  if (vec8) {
+    const int64_t total = rows * (head_dim / 16);
+    rope_vec8_kernel<<<(unsigned)ceil_div(total, threads), threads, 0, as_stream(stream)>>>(
+        rows, heads, head_dim, (__nv_bfloat16*)x, ldx, pos, theta, inverse);
+    PE_LAUNCHED();
+    return PE_OK;
+  }
   if (heads >= 4) {
     const int64_t total = rows * (head_dim / 2);
     return PE_DISPATCH(dtype, T, [&] {

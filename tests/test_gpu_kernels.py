@@ -157,9 +157,9 @@ def test_gemm_rejects_ineligible_tcgen05():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("H", [64, 3584, 100])
-def test_rmsnorm_fwd_bwd(dtype, H):
-    rows = 37
+@pytest.mark.parametrize("H,rows", [(64, 37), (3584, 37), (100, 37), (3584, 5003), (4096, 700)])
+def test_rmsnorm_fwd_bwd(dtype, H, rows):
+    # 5003 rows: more row tiles than persistent blocks, ragged last tile
     x = _rand(rows, H, dtype=dtype, seed=5) * 3
     w = (1 + 0.1 * _rand(H, dtype=torch.float32, seed=6)).to(dtype)
     dy = _rand(rows, H, dtype=dtype, seed=7)
