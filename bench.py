@@ -461,7 +461,7 @@ def profiled_traffic(name):
     return None
 
 
-GEMM_PROFILE = "gemm_tc_gateup_4096x37888x3584.txt"
+GEMM_PROFILE = "gemm_tc_pair_gateup_4096x37888x3584.txt"
 
 
 def gemm_roofline(c, dev, peak, src):
