@@ -95,8 +95,10 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_qt = (g.S + TQ - 1) / TQ;
-  const int qt = num_qt - 1 - (int)blockIdx.x;  // heaviest tiles first
-  const int h = blockIdx.y;
+  // grid (head, tile): blocks dispatch head-fastest, so the heaviest tiles of every
+  // head start first
+  const int qt = num_qt - 1 - (int)blockIdx.y;
+  const int h = blockIdx.x;
   const int kvh = h / rep;
   const int q0 = qt * TQ;
   const TileList tl = tiles_for(g, q0);
@@ -374,8 +376,10 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_pairs = (g.S + 2 * TQ - 1) / (2 * TQ);
-  const int pr = num_pairs - 1 - (int)blockIdx.x;  // heaviest pairs first
-  const int h = blockIdx.y;
+  // grid (head, pair): blocks dispatch head-fastest, so the heaviest pairs of every
+  // head start first
+  const int pr = num_pairs - 1 - (int)blockIdx.y;
+  const int h = blockIdx.x;
   const int kvh = h / rep;
   const int q0 = pr * 2 * TQ;
   PairTiles pt;
@@ -627,8 +631,9 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
 bool attn_tc_eligible(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int hd, int layout,
                       const void* q, int64_t q_ss, const void* k, int64_t k_ss, const void* v,
                       int64_t v_ss) {
+  // (tiles of 128 slots index gridDim.y, at most 65535)
   return dtype == PE_BF16 && B == 1 && hd == HD && layout == PE_LAYOUT_PARTITION &&
-         S > 0 && S < (1 << 30) && al16(q) && al16(k) && al16(v) && q_ss % 8 == 0 &&
+         S > 0 && S <= 65535ll * TQ && al16(q) && al16(k) && al16(v) && q_ss % 8 == 0 &&
          k_ss % 8 == 0 && v_ss % 8 == 0 && q_ss >= (int64_t)Hq * HD && k_ss >= (int64_t)Hkv * HD &&
          v_ss >= (int64_t)Hkv * HD;
 }
@@ -647,7 +652,7 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   if (variant == 1) {
     PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_FWD));
-    dim3 grid((unsigned)((S + TQ - 1) / TQ), (unsigned)Hq);
+    dim3 grid((unsigned)Hq, (unsigned)((S + TQ - 1) / TQ));
     attn_fwd_tc_kernel<<<grid, kThreads, SMEM_FWD, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
                                                          g, Hq, Hq / Hkv, scale_log2, status);
     PE_LAUNCHED();
@@ -655,7 +660,7 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   }
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc2_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_FWD2));
-  dim3 grid((unsigned)((S + 2 * TQ - 1) / (2 * TQ)), (unsigned)Hq);
+  dim3 grid((unsigned)Hq, (unsigned)((S + 2 * TQ - 1) / (2 * TQ)));
   attn_fwd_tc2_kernel<<<grid, kThreads, SMEM_FWD2, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
                                                          g, Hq, Hq / Hkv, scale_log2, status);
   PE_LAUNCHED();

@@ -152,8 +152,10 @@ attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x;  // low key tiles are read by the most query tiles: first
-  const int h = blockIdx.y;
+  // grid (head, key tile): low key tiles are read by the most query tiles, and blocks
+  // dispatch head-fastest, so the heaviest tiles of every head start first
+  const int kt = blockIdx.y;
+  const int h = blockIdx.x;
   const int kvh = h / rep;
   const int k0 = kt * TK;
   const Ranges qr = query_tiles(g, k0);
@@ -453,8 +455,10 @@ attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_qt = (g.S + TQ - 1) / TQ;
-  const int qt = num_qt - 1 - (int)blockIdx.x;  // heaviest tiles first
-  const int h = blockIdx.y;
+  // grid (head, tile): blocks dispatch head-fastest, so the heaviest tiles of every
+  // head start first
+  const int qt = num_qt - 1 - (int)blockIdx.y;
+  const int h = blockIdx.x;
   const int kvh = h / rep;
   const int q0 = qt * TQ;
   int r_end, m_beg, m_end;
@@ -690,8 +694,10 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x;  // low key tiles are read by the most query tiles: first
-  const int h = blockIdx.y;
+  // grid (head, key tile): low key tiles are read by the most query tiles, and blocks
+  // dispatch head-fastest, so the heaviest tiles of every head start first
+  const int kt = blockIdx.y;
+  const int h = blockIdx.x;
   const int kvh = h / rep;
   const int k0 = kt * TK;
   const Ranges qr = query_tiles(g, k0);
@@ -1070,12 +1076,12 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BWD_Q));
     PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BWD_KV));
-    dim3 gq((unsigned)((S + TQ - 1) / TQ), (unsigned)Hq);
+    dim3 gq((unsigned)Hq, (unsigned)((S + TQ - 1) / TQ));
     attn_bwd_q_kernel<<<gq, kKvThreads, SMEM_BWD_Q, st>>>(tq, tk, tv, tdo, lse, delta,
                                                         (__nv_bfloat16*)dq, dq_ss, g, Hq / Hkv,
                                                         scale, status);
     PE_LAUNCHED();
-    dim3 gkv((unsigned)((S + TK - 1) / TK), (unsigned)Hq);
+    dim3 gkv((unsigned)Hq, (unsigned)((S + TK - 1) / TK));
     attn_bwd_kv_kernel<<<gkv, kKvThreads, SMEM_BWD_KV, st>>>(tq, tk, tv, tdo, lse, delta, dk_acc,
                                                            dv_acc, g, Hkv, Hq / Hkv, scale, status);
     PE_LAUNCHED();
@@ -1085,7 +1091,7 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   }
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)SMEM_BWD));
-  dim3 grid((unsigned)((S + TK - 1) / TK), (unsigned)Hq);
+  dim3 grid((unsigned)Hq, (unsigned)((S + TK - 1) / TK));
   attn_bwd_tc_kernel<<<grid, kThreads, SMEM_BWD, st>>>(tq, tk, tv, tdo, lse, delta, dq_acc, dk_acc,
                                                        dv_acc, g, Hq, Hkv, Hq / Hkv, scale, status);
   PE_LAUNCHED();
