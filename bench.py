@@ -181,6 +181,11 @@ class Trainer:
         self.loss = torch.zeros(1, dtype=torch.float32, device=fp.device)
         self.lr = lr
         self.t = 0
+        self.overlap = None
+        if world > 1:
+            from parallel_eagle_b200.train import OverlappedAllReduce
+
+            self.overlap = OverlappedAllReduce(drafter)
 
     def step(self, seqs, global_batch):
         from parallel_eagle_b200 import ops
@@ -188,11 +193,13 @@ class Trainer:
         fp = self.eng.flat
         fp.grad.zero_()
         self.loss.zero_()
-        for ids, feats in seqs:
+        for i, (ids, feats) in enumerate(seqs):
+            if self.overlap is not None and i == len(seqs) - 1:
+                self.overlap.arm()  # reduce the layers' gradients during the last backward
             self.eng.run(ids, feats, self.c["segments"], loss_scale=1.0 / global_batch, sync=False)
             self.loss += self.eng.loss_sum
-        if self.world > 1:
-            torch.distributed.all_reduce(fp.grad)
+        if self.overlap is not None:
+            self.overlap.finish()
         self.sumsq.zero_()
         ops.sumsq_into(fp.grad, self.sumsq)
         self.t += 1
@@ -269,9 +276,11 @@ def run_ours(args):
         drafter.zero_grad(set_to_none=True)
         tot = 0.0
         for b in range(B):
+            if trainer.overlap is not None and b == B - 1:
+                trainer.overlap.arm()
             tot += mtp_backward(drafter, h_ids[b], h_feats[b], c["segments"], loss_scale=1.0 / gb)
-        if world > 1:
-            dist.all_reduce(fp.grad)
+        if trainer.overlap is not None:
+            trainer.overlap.finish()
         trainer.sumsq.zero_()
         ops.sumsq_into(fp.grad, trainer.sumsq)
         trainer.t += 1

@@ -163,6 +163,10 @@ class StepEngine:
         self._plans: dict[tuple, _PassPlan] = {}
         # device bytes of activations one pass of stacked segments may hold
         self.pass_bytes = 24 << 30
+        # called (no arguments) once the decoder layers' weight gradients of the current
+        # sequence are final -- after its last pass's layer backward, before the input
+        # projections' backward -- so a data-parallel caller can start reducing them
+        self.after_layers = None
         self.loss_sum = torch.zeros(1, dtype=torch.float32, device=self.flat.device)
 
     # --------------------------------------------------------------- plans --
@@ -263,9 +267,11 @@ class StepEngine:
             if max(a0 + 1, prompt_len) > min(a1 + k - 1, n - 1):
                 continue
             live.append((a0, a1))
-        for group in self._passes(live):
+        groups = self._passes(live)
+        for gi, group in enumerate(groups):
             plan = self._pass_plan(tuple(group), n, prompt_len)
-            self._pass(plan, input_ids, features, scale, teacher_labels, teacher_hidden)
+            self._pass(plan, input_ids, features, scale, teacher_labels, teacher_hidden,
+                       last=gi == len(groups) - 1)
             ran = True
             mask_slots = mask_slots or plan.has_pred
         if fresh:
@@ -278,7 +284,19 @@ class StepEngine:
         return float(self.loss_sum.item()) / total
 
     # ---------------------------------------------------------------- pass --
-    def _pass(self, plan: _PassPlan, ids, feats, scale, teacher_labels, teacher_hidden):
+    def layer_grad_region(self) -> tuple[int, int]:
+        """``[start, end)`` of the flat gradient buffer holding the decoder layers'
+        parameters: a contiguous suffix (``named_parameters`` lists the drafter's own
+        parameters and the input projections before ``layers``)."""
+        spans = [self.flat.offsets[n] for n in self.flat.names if n.startswith("layers.")]
+        start = min(o for o, _ in spans)
+        end = max(o + k for o, k in spans)
+        if any(o >= start for n, (o, _) in self.flat.offsets.items() if not n.startswith("layers.")):
+            raise L.PeError("layer parameters are not a contiguous suffix of the flat buffer")
+        return start, self.flat.numel  # the alignment tail after `end` is zero padding
+
+    def _pass(self, plan: _PassPlan, ids, feats, scale, teacher_labels, teacher_hidden,
+              last=True):
         """Forward and backward of the stacked segments of one pass.  Every GEMM,
         norm and element-wise op runs once over all stacked rows; attention runs
         per segment on its row range with that segment's mask."""
@@ -410,6 +428,9 @@ class StepEngine:
             )
             dx, part = ops.rmsnorm_bwd(dxn, x_in, W(p + "input_norm.weight"), r1, residual=dx2)
             ops.colsum_into(part, G(p + "input_norm.weight"), accumulate=True)
+
+        if last and self.after_layers is not None:
+            self.after_layers()
 
         # ---------------- input backward ----------------
         g_in = G("in_proj.weight", (H, 2 * H))

@@ -159,6 +159,42 @@ def allreduce_gradients(drafter) -> None:
         torch.distributed.all_reduce(p.grad)
 
 
+class OverlappedAllReduce:
+    """Data-parallel gradient reduction overlapped with backward.  Armed before a
+    rank's last local sequence of an update: the decoder layers' region of the flat
+    gradient buffer starts its NCCL all-reduce (asynchronously, on NCCL's stream) as
+    soon as the step engine reports those gradients final, while the input
+    projections' backward still runs; ``finish`` then reduces the input projections'
+    region and waits.  Every rank issues the same two collectives in the same order
+    (layers, then inputs) whether or not its hook fired."""
+
+    def __init__(self, drafter):
+        from .engine import engine_for
+
+        self.eng = engine_for(drafter)
+        self.work = None
+
+    def arm(self) -> None:
+        eng = self.eng
+        o0, o1 = eng.layer_grad_region()
+
+        def launch():
+            self.work = torch.distributed.all_reduce(eng.flat.grad[o0:o1], async_op=True)
+
+        eng.after_layers = launch
+
+    def finish(self) -> None:
+        eng = self.eng
+        eng.after_layers = None
+        o0, o1 = eng.layer_grad_region()
+        if self.work is None:
+            torch.distributed.all_reduce(eng.flat.grad[o0:o1])
+        torch.distributed.all_reduce(eng.flat.grad[:o0])
+        if self.work is not None:
+            self.work.wait()
+            self.work = None
+
+
 def train(tcfg: TargetConfig, dcfg: DrafterConfig, tr: TrainConfig, dtype: str = "float32",
           on_save=None):
     """Train the drafter on cached features (reference ``train.py:45-173``).
@@ -186,6 +222,9 @@ def train(tcfg: TargetConfig, dcfg: DrafterConfig, tr: TrainConfig, dtype: str =
 
     opt = build_optimizer(drafter.trainable_parameters(), tr.lr, tr.weight_decay, tr.use_8bit_adam)
     fused_clip = isinstance(opt, FusedAdamW)
+    # data-parallel runs on CUDA overlap the gradient all-reduce with the backward
+    overlap = (OverlappedAllReduce(drafter)
+               if world > 1 and drafter.device.type == "cuda" else None)
     total_updates = max(1, math.ceil(len(data) * tr.epochs / tr.grad_accum))
 
     Path(tr.out_dir).mkdir(parents=True, exist_ok=True)
@@ -239,6 +278,10 @@ def train(tcfg: TargetConfig, dcfg: DrafterConfig, tr: TrainConfig, dtype: str =
                 continue
 
             if micro % world == rank:
+                # last sequence of this update on this rank: overlap the reduction
+                boundary = (micro // tr.grad_accum + 1) * tr.grad_accum
+                if overlap is not None and micro + world >= boundary:
+                    overlap.arm()
                 running += mtp_backward(
                     drafter, input_ids, features, tr.num_segments,
                     loss_scale=1.0 / tr.grad_accum,
@@ -249,7 +292,10 @@ def train(tcfg: TargetConfig, dcfg: DrafterConfig, tr: TrainConfig, dtype: str =
             if micro % tr.grad_accum != 0:
                 continue
 
-            allreduce_gradients(drafter)
+            if overlap is not None:
+                overlap.finish()
+            else:
+                allreduce_gradients(drafter)
             for g in opt.param_groups:
                 g["lr"] = lr_at(update, total_updates, tr.lr, tr.warmup_ratio)
             if not fused_clip:
