@@ -449,6 +449,246 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
   return PE_OK;
 }
 
+// ------------------------------------------------------------------------ //
+// Fused soft-target path (bf16, teacher rows t_r): per (row group, chunk) step
+//   Zs = h W_c^T, Zt = t W_c^T (bf16, per-128-column (max, sum-exp) stats from the
+//   GEMM epilogues);
+//   combine_soft: running (m_s, l_s) and (m_t, l_t), rescale factors alpha_s /
+//   alpha_t, S_tz = sum_v e^{t_v - m_t} z_v (online), and in place
+//   Zs <- e^{z - m_s}, Zt <- e^{t - m_t};
+//   dH_s = Zs W_c + alpha_s dH_s,  dH_t = Zt W_c + alpha_t dH_t  (fp32).
+// loss_r = (m_s + ln l_s) - S_tz / l_t ;  dh = scale (dH_s / l_s - dH_t / l_t).
+// Four GEMMs per chunk, every logits chunk bf16 and L2-sized, one pass over W.
+// ------------------------------------------------------------------------ //
+struct SoftLayout {
+  size_t m, l, zlab, lse, alpha, mt, lt, szt, alpha_t, lse_t, stats_s[2], stats_t[2], Zs[2],
+      Zt[2], dHs, dHt, total;
+};
+
+SoftLayout soft_layout_of(int64_t R, int64_t H, int64_t V) {
+  const int64_t vc = V < kMaxChunk ? (V + 7) / 8 * 8 : kMaxChunk;
+  const int64_t rg = R < kMaxGroup ? R : kMaxGroup;
+  const int64_t nt = (vc + kStatTile - 1) / kStatTile;
+  SoftLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += align256(bytes);
+    return o;
+  };
+  L.m = take(4 * R);
+  L.l = take(4 * R);
+  L.zlab = take(4 * R);
+  L.lse = take(4 * R);
+  L.alpha = take(4 * R);
+  L.mt = take(4 * R);
+  L.lt = take(4 * R);
+  L.szt = take(4 * R);
+  L.alpha_t = take(4 * R);
+  L.lse_t = take(4 * R);
+  for (int b = 0; b < 2; ++b) {
+    L.stats_s[b] = take(8 * (size_t)rg * nt);
+    L.stats_t[b] = take(8 * (size_t)rg * nt);
+    L.Zs[b] = take(2 * (size_t)rg * vc);
+    L.Zt[b] = take(2 * (size_t)rg * vc);
+  }
+  L.dHs = take(4 * (size_t)R * H);
+  L.dHt = take(4 * (size_t)R * H);
+  L.total = off;
+  return L;
+}
+
+// fold one chunk's tile stats (at most 128 tiles, lane takes tiles lane + 32 q) into
+// a running (m, l); returns the new maximum, writes l and the rescale factor
+__device__ __forceinline__ float fold_stats(const float2* st, int nt, float* m, float* l,
+                                            float* alpha, int lane) {
+  float2 sv[4];
+  float lm = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int t = lane + 32 * q;
+    sv[q] = t < nt ? st[t] : make_float2(-INFINITY, 0.f);
+    lm = fmaxf(lm, sv[q].x);
+  }
+  const float m_old = *m;
+  const float mn = fmaxf(m_old, warp_max(lm));
+  float part = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    if (sv[q].x != -INFINITY) part += sv[q].y * expf(sv[q].x - mn);
+  const float tile_sum = warp_sum(part);
+  const float keep = m_old == -INFINITY ? 0.f : expf(m_old - mn);
+  if (lane == 0) {
+    *l = *l * keep + tile_sum;
+    *alpha = keep;
+    *m = mn;
+  }
+  return __shfl_sync(0xffffffffu, mn, 0);
+}
+
+__global__ void __launch_bounds__(256)
+combine_soft_kernel(int64_t vc, int nt, int stats_ld, const float2* __restrict__ stats_s,
+                    const float2* __restrict__ stats_t, __nv_bfloat16* __restrict__ Zs,
+                    __nv_bfloat16* __restrict__ Zt, int64_t ldz, float* m, float* l,
+                    float* alpha, float* mt, float* lt, float* szt, float* alpha_t) {
+  __shared__ float s_m[2];
+  __shared__ float s_red[8];
+  const int64_t r = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp == 0) {
+    const float ms = fold_stats(stats_s + r * stats_ld, nt, m + r, l + r, alpha + r, lane);
+    if (lane == 0) s_m[0] = ms;
+  } else if (warp == 1) {
+    const float mtn = fold_stats(stats_t + r * stats_ld, nt, mt + r, lt + r, alpha_t + r, lane);
+    if (lane == 0) s_m[1] = mtn;
+  }
+  __syncthreads();
+  const float ms = s_m[0], mtn = s_m[1];
+  __nv_bfloat16* zs = Zs + r * ldz;
+  __nv_bfloat16* zt = Zt + r * ldz;
+  float acc = 0.f;
+  for (int64_t c = (int64_t)threadIdx.x * 8; c < vc; c += 256 * 8) {
+    uint4 us = *reinterpret_cast<const uint4*>(zs + c);
+    uint4 ut = *reinterpret_cast<const uint4*>(zt + c);
+    __nv_bfloat162* hs = reinterpret_cast<__nv_bfloat162*>(&us);
+    __nv_bfloat162* ht = reinterpret_cast<__nv_bfloat162*>(&ut);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 z = __bfloat1622float2(hs[i]), t = __bfloat1622float2(ht[i]);
+      const float p0 = __expf(t.x - mtn), p1 = __expf(t.y - mtn);
+      acc += p0 * z.x + p1 * z.y;
+      hs[i] = __floats2bfloat162_rn(__expf(z.x - ms), __expf(z.y - ms));
+      ht[i] = __floats2bfloat162_rn(p0, p1);
+    }
+    *reinterpret_cast<uint4*>(zs + c) = us;
+    *reinterpret_cast<uint4*>(zt + c) = ut;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) s_red[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += s_red[w];
+    szt[r] = szt[r] * alpha_t[r] + t;
+  }
+}
+
+// dh = scale * (dH_s / l_s - dH_t / l_t)
+__global__ void soft_dh_kernel(int64_t R, int64_t H, const float* __restrict__ dHs,
+                               const float* __restrict__ dHt, const float* __restrict__ l,
+                               const float* __restrict__ lt, float scale,
+                               __nv_bfloat16* __restrict__ dh, int64_t lddh) {
+  const int64_t total = R * H / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i * 8;
+    const int64_t r = e / H, c = e - r * H;
+    const float is = 1.f / l[r], it = 1.f / lt[r];
+    float o[8];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const float4 a = reinterpret_cast<const float4*>(dHs + e)[q];
+      const float4 b = reinterpret_cast<const float4*>(dHt + e)[q];
+      o[4 * q] = scale * (a.x * is - b.x * it);
+      o[4 * q + 1] = scale * (a.y * is - b.y * it);
+      o[4 * q + 2] = scale * (a.z * is - b.z * it);
+      o[4 * q + 3] = scale * (a.w * is - b.w * it);
+    }
+    uint4 out;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o2[k] = __floats2bfloat162_rn(o[2 * k], o[2 * k + 1]);
+    *reinterpret_cast<uint4*>(dh + r * lddh + c) = out;
+  }
+}
+
+bool soft_fast_eligible(int dtype, int64_t H, int64_t V, const void* h, int64_t ldh,
+                        const void* W, const void* teacher, int64_t ldt, void* dh, int64_t lddh,
+                        int algo) {
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return dtype == PE_BF16 && teacher != nullptr && algo != PE_ALGO_SIMT && H % 8 == 0 &&
+         V % 8 == 0 && ldh % 8 == 0 && ldt % 8 == 0 && lddh % 8 == 0 && a16(h) && a16(W) &&
+         a16(teacher) && a16(dh);
+}
+
+// Same two-stream chunk pipeline as lmhead_fast, with the teacher's logits GEMM next
+// to the student's and two dH accumulations on the side stream.
+int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, const void* W,
+                     const void* teacher, int64_t ldt, float grad_scale, void* dh, int64_t lddh,
+                     float* loss_sum, uint8_t* ws, int algo, int* status, cudaStream_t st) {
+  const SoftLayout L = soft_layout_of(R, H, V);
+  const FastPlan P = fast_plan_of(R, V, algo);
+  float* m = (float*)(ws + L.m);
+  float* l = (float*)(ws + L.l);
+  float* zlab = (float*)(ws + L.zlab);
+  float* lse = (float*)(ws + L.lse);
+  float* alpha = (float*)(ws + L.alpha);
+  float* mt = (float*)(ws + L.mt);
+  float* lt = (float*)(ws + L.lt);
+  float* szt = (float*)(ws + L.szt);
+  float* alpha_t = (float*)(ws + L.alpha_t);
+  float* lse_t = (float*)(ws + L.lse_t);
+  float* dHs = (float*)(ws + L.dHs);
+  float* dHt = (float*)(ws + L.dHt);
+  const int64_t VC = P.vc;
+  const int nt_max = (int)((VC + kStatTile - 1) / kStatTile);
+  cudaStream_t side = side_stream(0);
+  cudaEvent_t ev_fork = pool_event(0), ev_join = pool_event(1);
+  cudaEvent_t ev_logits[2] = {pool_event(2), pool_event(3)};
+  cudaEvent_t ev_dh[2] = {pool_event(4), pool_event(5)};
+  if (!side || !ev_fork || !ev_join || !ev_logits[0] || !ev_logits[1] || !ev_dh[0] || !ev_dh[1]) {
+    set_error("lmhead_ce: could not create the side stream or its events");
+    return PE_ERR_CUDA;
+  }
+  init_stats_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, zlab, mt, lt, szt);
+  PE_LAUNCHED();
+  PE_CUDA_TRY(cudaEventRecord(ev_fork, st));
+  PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_fork, 0));
+  int64_t t = 0;
+  for (int64_t r0 = 0; r0 < R; r0 += P.rg) {
+    const int64_t rg = (R - r0) < P.rg ? (R - r0) : P.rg;
+    const void* hg = (const __nv_bfloat16*)h + r0 * ldh;
+    const void* tg = (const __nv_bfloat16*)teacher + r0 * ldt;
+    for (int64_t v0 = 0; v0 < V; v0 += VC, ++t) {
+      const int b = (int)(t & 1);
+      const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
+      const int nt = (int)((vc + kStatTile - 1) / kStatTile);
+      const __nv_bfloat16* Wc = (const __nv_bfloat16*)W + v0 * H;
+      __nv_bfloat16* Zs = (__nv_bfloat16*)(ws + L.Zs[b]);
+      __nv_bfloat16* Zt = (__nv_bfloat16*)(ws + L.Zt[b]);
+      float2* ss = (float2*)(ws + L.stats_s[b]);
+      float2* stt = (float2*)(ws + L.stats_t[b]);
+      if (t >= 2) PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_dh[b], 0));
+      int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Zs, VC, ss, nt_max, status, st);
+      if (!rc) rc = gemm_tc_logits_stats(rg, vc, H, tg, ldt, Wc, H, Zt, VC, stt, nt_max, status, st);
+      if (rc) return rc;
+      PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
+      PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
+      combine_soft_kernel<<<(unsigned)rg, 256, 0, side>>>(vc, nt, nt_max, ss, stt, Zs, Zt, VC,
+                                                          m + r0, l + r0, alpha + r0, mt + r0,
+                                                          lt + r0, szt + r0, alpha_t + r0);
+      PE_LAUNCHED();
+      rc = gemm_tc_rowscale_acc(rg, H, vc, Zs, VC, Wc, H, dHs + r0 * H, H,
+                                v0 > 0 ? dHs + r0 * H : nullptr, alpha + r0, status, side);
+      if (!rc)
+        rc = gemm_tc_rowscale_acc(rg, H, vc, Zt, VC, Wc, H, dHt + r0 * H, H,
+                                  v0 > 0 ? dHt + r0 * H : nullptr, alpha_t + r0, status, side);
+      if (rc) return rc;
+      PE_CUDA_TRY(cudaEventRecord(ev_dh[b], side));
+    }
+  }
+  PE_CUDA_TRY(cudaEventRecord(ev_join, side));
+  PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_join, 0));
+  finalize_kernel<<<1, kThreads, 0, st>>>(R, nullptr, m, l, zlab, mt, lt, szt, lse, lse_t,
+                                          loss_sum);
+  PE_LAUNCHED();
+  soft_dh_kernel<<<grid_for(R * H / 8), 256, 0, st>>>(R, H, dHs, dHt, l, lt, grad_scale,
+                                                      (__nv_bfloat16*)dh, lddh);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
 }  // namespace
 }  // namespace pe
 
@@ -457,8 +697,8 @@ using namespace pe;
 extern "C" size_t pe_lmhead_ce_workspace(int dtype, int64_t R, int64_t H, int64_t V, int soft) {
   if (R <= 0 || H <= 0 || V <= 0) return 0;
   size_t bytes = layout_of(dtype, R, H, V, soft).total;
-  if (dtype == PE_BF16 && !soft) {
-    const size_t f = fast_layout_of(R, H, V).total;
+  if (dtype == PE_BF16) {
+    const size_t f = soft ? soft_layout_of(R, H, V).total : fast_layout_of(R, H, V).total;
     if (f > bytes) bytes = f;
   }
   return bytes;
@@ -483,6 +723,13 @@ extern "C" int pe_lmhead_ce(int dtype, int64_t R, int64_t H, int64_t V, const vo
                  need);
     return lmhead_fast(R, H, V, h, ldh, W, labels, grad_scale, dh, lddh, loss_sum,
                        static_cast<uint8_t*>(workspace), tuning, status, st);
+  }
+  if (soft_fast_eligible(dtype, H, V, h, ldh, W, teacher, ldt, dh, lddh, algo)) {
+    const size_t need = soft_layout_of(R, H, V).total;
+    PE_CHECK_ARG(workspace && workspace_bytes >= need, "lmhead_ce: workspace of %zu bytes needed",
+                 need);
+    return lmhead_fast_soft(R, H, V, h, ldh, W, teacher, ldt, grad_scale, dh, lddh, loss_sum,
+                            static_cast<uint8_t*>(workspace), tuning, status, st);
   }
   const Layout L = layout_of(dtype, R, H, V, soft);
   PE_CHECK_ARG(workspace && workspace_bytes >= L.total,

@@ -314,7 +314,7 @@ def test_attention_tcgen05_bwd_matches_simt(geom):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("soft", [False, True])
-@pytest.mark.parametrize("R,H,V", [(37, 64, 1000), (130, 256, 20000)])
+@pytest.mark.parametrize("R,H,V", [(37, 64, 1000), (130, 256, 20000), (700, 256, 40000)])
 def test_lmhead_ce(dtype, soft, R, H, V):
     h = _rand(R, H, dtype=dtype, seed=14)
     W = _rand(V, H, dtype=dtype, seed=15, scale=0.05)
