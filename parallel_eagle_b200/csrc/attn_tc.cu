@@ -538,12 +538,15 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
         for (int c = 0; c < 128; c += 32) tmem_ld32(tS + c, x + c);
         tmem_wait_ld();
         const int k0 = kt * TK;
-        float mt = -INFINITY;
+        // 8 independent partial maxima (short dependency chains), combined at the end
+        float mp[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
         if (k0 + TK - 1 <= qi) {  // every key of the tile is a real key <= the row's anchor
 #pragma unroll
           for (int c = 0; c < 128; ++c) {
             x[c] *= scale_log2;
-            mt = fmaxf(mt, x[c]);
+            mp[c & 7] = fmaxf(mp[c & 7], x[c]);
           }
         } else {
 #pragma unroll
@@ -551,9 +554,11 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
             const int ks = k0 + c;
             const bool allow = ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
             x[c] = allow ? x[c] * scale_log2 : -INFINITY;
-            mt = fmaxf(mt, x[c]);
+            mp[c & 7] = fmaxf(mp[c & 7], x[c]);
           }
         }
+        const float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                               fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
         // raise the reference maximum only when the tile exceeds it by > 2^8
         float alpha = 1.f;
         if (mt > m + kRescaleLog2) {
@@ -562,20 +567,22 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           l *= alpha;
         }
         const float m_use = m == -INFINITY ? 0.f : m;
-        // P_t over the first 64 columns of S_t (packed bf16 pairs)
-        float rs = 0.f;
+        // P_t over the first 64 columns of S_t (packed bf16 pairs); 8 partial row sums
+        float rp[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) rp[u] = 0.f;
 #pragma unroll
         for (int c0 = 0; c0 < 128; c0 += 64) {
           uint32_t pk[32];
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
             const float p0 = ex2_approx(x[c0 + c] - m_use), p1 = ex2_approx(x[c0 + c + 1] - m_use);
-            rs += p0 + p1;
+            rp[(c >> 1) & 7] += p0 + p1;
             pk[c / 2] = pack_bf16x2(p0, p1);
           }
           tmem_st32(tS + c0 / 2, pk);
         }
-        l += rs;
+        l += ((rp[0] + rp[1]) + (rp[2] + rp[3])) + ((rp[4] + rp[5]) + (rp[6] + rp[7]));
         // O holds the tiles before this one (their PV completed before this S did):
         // rescale it when the maximum moved
         if (__any_sync(0xffffffffu, alpha != 1.f) && j > 0) {
