@@ -125,8 +125,12 @@ int pe_attn_fwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
                 int kdepth, const int32_t* anchor, const int32_t* depth, const void* bias,
                 int64_t bias_sb, int64_t bias_sq, int algo, int32_t* status, void* stream);
 /* dq/dk/dv are overwritten.  `workspace` holds per-row softmax deltas and, on
- * the tensor-core path, an fp32 dQ accumulator; its size comes from
- * pe_attn_bwd_workspace (same shape arguments). */
+ * the tensor-core path, fp32 dQ / dK / dV accumulators and a work counter; its
+ * size comes from pe_attn_bwd_workspace (same shape arguments).  On the
+ * tensor-core path, algo bits 8-15 pick the kernel variant: 0 (default) a dQ
+ * kernel plus a persistent dK/dV kernel, 1 one fused kernel with dQ atomics,
+ * 2 a dQ kernel plus one dK/dV CTA per key tile.  The forward's bits 8-15: 0
+ * (default) two query tiles per CTA, 1 one. */
 size_t pe_attn_bwd_workspace(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim);
 int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
                 const void* q, int64_t q_sb, int64_t q_ss, const void* k, int64_t k_sb,

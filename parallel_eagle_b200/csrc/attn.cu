@@ -76,11 +76,11 @@ extern "C" int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int
                "attention backward: workspace too small (see pe_attn_bwd_workspace)");
   float* delta = static_cast<float*>(workspace);
   MaskSpec m{layout, a0, a1, kdepth, anchor, depth, bias, bias_sb, bias_sq};
-  // algo bits 8-15: tensor-core kernel variant (0 split dQ / dK-dV kernels, 1 fused
-  // kernel with dQ atomics)
+  // algo bits 8-15: tensor-core kernel variant (0 dQ kernel + persistent dK-dV kernel,
+  // 1 fused kernel with dQ atomics, 2 dQ kernel + one-CTA-per-tile dK-dV kernel)
   const int variant = (algo >> 8) & 0xff;
   algo &= 0xff;
-  PE_CHECK_ARG(variant <= 1, "attention backward: unknown kernel variant %d", variant);
+  PE_CHECK_ARG(variant <= 2, "attention backward: unknown kernel variant %d", variant);
   const bool tc = attn_tc_bwd_ready() &&
                   attn_tc_eligible(dtype, B, S, Hq, Hkv, head_dim, layout, q, q_ss, k, k_ss, v,
                                    v_ss) &&

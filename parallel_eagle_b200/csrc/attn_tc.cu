@@ -318,8 +318,13 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 //               (S_t = Q_t K^T into TMEM; PV_t: O_t += P_t V with P_t read from
 //               TMEM -- the tcgen05 A-from-TMEM form -- so P never touches
 //               shared memory)
-//   warps 2..5  softmax of tile A, one thread per query row (TMEM lane)
-//   warps 6..9  softmax of tile B
+//   warps 2..3  idle (they complete warpgroup 0, whose registers go to the softmax)
+//   warps 4..7  softmax of tile A, one thread per query row (TMEM lane)
+//   warps 8..11 softmax of tile B
+//
+// Warpgroup 0 (TMA, MMA) drops to 56 registers per thread and the two softmax
+// warpgroups rise to 224, enough to hold a full 128-score row plus the packed
+// probabilities without spilling (the CTA launches with 384 x 168).
 //
 // TMEM: O_A cols 0..127, O_B 128..255, S_A 256..383, S_B 384..511; P_t is
 // written as packed bf16 pairs over the first 64 columns of S_t.
@@ -331,8 +336,17 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 // P = 2^(x - m) <= 256 against the stale maximum, and O and the row sum stay
 // consistent because both are relative to the same m.
 // ------------------------------------------------------------------------ //
+constexpr int kThreads2 = 384;
+constexpr int kRegsLow = 56, kRegsHigh = 224;  // 128 x 56 + 256 x 224 = 384 x 168
 constexpr size_t SMEM_FWD2 = 1024 + 2 * TILE_BYTES /*Q_A, Q_B*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ + 256;
 constexpr float kRescaleLog2 = 8.f;
+// one pair of scores in kEmuEvery takes its exponential from the FMA-pipe
+// polynomial (0: all on the SFU); the SFU alone runs one exp per score, which at
+// head_dim 128 takes as long as the tile's two MMAs
+#ifndef PE_FWD_EMU_EVERY
+#define PE_FWD_EMU_EVERY 4
+#endif
+constexpr int kEmuEvery = PE_FWD_EMU_EVERY;
 
 struct PairTiles {
   TileList a, b;  // b empty (count 0) when the second query tile lies past the sequence
@@ -355,7 +369,7 @@ struct PairTiles {
   }
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads2, 1)
 attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
                     int64_t o_ss, float* __restrict__ lse, PartGeom g, int Hq, int rep,
@@ -410,111 +424,114 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    if (elect_one()) {
-      bool ok = true;
-      int last_st = -1;
-      uint32_t last_ph = 0;
-      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+  if (warp < 4) {
+    setmaxnreg_dec<kRegsLow>();
+    if (warp == 0) {
+      if (elect_one()) {
+        bool ok = true;
+        int last_st = -1;
+        uint32_t last_ph = 0;
+        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        tma_load_2d(sQ + t * TILE_BYTES, &tmQ, q_full, h * HD, q0 + t * TQ);
-        tma_load_2d(sQ + t * TILE_BYTES + CHUNK, &tmQ, q_full, h * HD + 64, q0 + t * TQ);
-      }
-      int j = 0;
-      for (int kt = 0; kt >= 0 && ok; kt = pt.next(kt), ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, status, 211)) { ok = false; break; }
-        const int k0 = kt * TK;
-        uint8_t* k_dst = sKV + st * 2 * TILE_BYTES;
-        uint8_t* v_dst = k_dst + TILE_BYTES;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
-        tma_load_2d(k_dst, &tmK, &kv_full[st], kvh * HD, k0);
-        tma_load_2d(k_dst + CHUNK, &tmK, &kv_full[st], kvh * HD + 64, k0);
-        tma_load_2d(v_dst, &tmV, &kv_full[st], kvh * HD, k0);
-        tma_load_2d(v_dst + CHUNK, &tmV, &kv_full[st], kvh * HD + 64, k0);
-        last_st = st;
-        last_ph = ph;
-      }
-      if (!ok && last_st >= 0) mbar_wait(&kv_full[last_st], last_ph, nullptr, 0);
-      mbar_wait(q_full, 0, nullptr, 0);
-    }
-  } else if (warp == 1) {
-    if (elect_one()) {
-      constexpr uint32_t IDESC_S = idesc_bf16(TQ, TK, false, false);
-      constexpr uint32_t IDESC_O = idesc_bf16(TQ, HD, false, true);
-      bool ok = mbar_wait(q_full, 0, status, 212);
-      auto issue_s = [&](int t, int st) {
-        const uint32_t q_base = smem_u32(sQ + t * TILE_BYTES);
-        const uint32_t k_base = smem_u32(sKV + st * 2 * TILE_BYTES);
-        const uint32_t d = tmem + 256 + t * 128;
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
-          mma_bf16_ss(d, sw128_desc(q_base + off, 16, 1024), sw128_desc(k_base + off, 16, 1024),
-                      IDESC_S, kk > 0 ? 1u : 0u);
+        for (int t = 0; t < 2; ++t) {
+          tma_load_2d(sQ + t * TILE_BYTES, &tmQ, q_full, h * HD, q0 + t * TQ);
+          tma_load_2d(sQ + t * TILE_BYTES + CHUNK, &tmQ, q_full, h * HD + 64, q0 + t * TQ);
         }
-      };
-      auto issue_pv = [&](int t, int st, bool first) {
-        const uint32_t v_base = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
-        const uint32_t p = tmem + 256 + t * 128;
-#pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk)
-          mma_bf16_ts(tmem + t * 128, p + kk * 8, sw128_desc(v_base + kk * 2048, CHUNK, 1024),
-                      IDESC_O, (!first || kk > 0) ? 1u : 0u);
-      };
-      // step 0: S of both tiles for key tile 0 (every query row sees key 0)
-      if (ok) ok = mbar_wait(&kv_full[0], 0, status, 213);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        mma_commit(&s_full[0]);
-        if (pt.use_b(0)) issue_s(1, 0);
-        mma_commit(&s_full[1]);
-      }
-      bool pv_a = false, pv_b = false;
-      int j = 0;
-      for (int kt = 0; kt >= 0 && ok; ++j) {
-        const int st = j & 1;
-        const int kn = pt.next(kt);
-        const int stn = (j + 1) & 1;
-        // tile A: PV of key tile kt, then S of the next key tile
-        if (!mbar_wait(&p_full[0], j & 1, status, 214)) { ok = false; break; }
-        tc_fence_after();
-        if (pt.use_a(kt)) {
-          issue_pv(0, st, !pv_a);
-          pv_a = true;
+        int j = 0;
+        for (int kt = 0; kt >= 0 && ok; kt = pt.next(kt), ++j) {
+          const int st = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1u, status, 211)) { ok = false; break; }
+          const int k0 = kt * TK;
+          uint8_t* k_dst = sKV + st * 2 * TILE_BYTES;
+          uint8_t* v_dst = k_dst + TILE_BYTES;
+          mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+          tma_load_2d(k_dst, &tmK, &kv_full[st], kvh * HD, k0);
+          tma_load_2d(k_dst + CHUNK, &tmK, &kv_full[st], kvh * HD + 64, k0);
+          tma_load_2d(v_dst, &tmV, &kv_full[st], kvh * HD, k0);
+          tma_load_2d(v_dst + CHUNK, &tmV, &kv_full[st], kvh * HD + 64, k0);
+          last_st = st;
+          last_ph = ph;
         }
-        if (kn >= 0) {
-          if (!mbar_wait(&kv_full[stn], ((j + 1) >> 1) & 1, status, 215)) { ok = false; break; }
+        if (!ok && last_st >= 0) mbar_wait(&kv_full[last_st], last_ph, nullptr, 0);
+        mbar_wait(q_full, 0, nullptr, 0);
+      }
+    } else if (warp == 1) {
+      if (elect_one()) {
+        constexpr uint32_t IDESC_S = idesc_bf16(TQ, TK, false, false);
+        constexpr uint32_t IDESC_O = idesc_bf16(TQ, HD, false, true);
+        bool ok = mbar_wait(q_full, 0, status, 212);
+        auto issue_s = [&](int t, int st) {
+          const uint32_t q_base = smem_u32(sQ + t * TILE_BYTES);
+          const uint32_t k_base = smem_u32(sKV + st * 2 * TILE_BYTES);
+          const uint32_t d = tmem + 256 + t * 128;
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * CHUNK + (kk & 3) * 32;
+            mma_bf16_ss(d, sw128_desc(q_base + off, 16, 1024), sw128_desc(k_base + off, 16, 1024),
+                        IDESC_S, kk > 0 ? 1u : 0u);
+          }
+        };
+        auto issue_pv = [&](int t, int st, bool first) {
+          const uint32_t v_base = smem_u32(sKV + st * 2 * TILE_BYTES + TILE_BYTES);
+          const uint32_t p = tmem + 256 + t * 128;
+#pragma unroll
+          for (int kk = 0; kk < TK / 16; ++kk)
+            mma_bf16_ts(tmem + t * 128, p + kk * 8, sw128_desc(v_base + kk * 2048, CHUNK, 1024),
+                        IDESC_O, (!first || kk > 0) ? 1u : 0u);
+        };
+        // step 0: S of both tiles for key tile 0 (every query row sees key 0)
+        if (ok) ok = mbar_wait(&kv_full[0], 0, status, 213);
+        if (ok) {
           tc_fence_after();
-          if (pt.use_a(kn)) issue_s(0, stn);
+          issue_s(0, 0);
           mma_commit(&s_full[0]);
-        }
-        // tile B
-        if (!mbar_wait(&p_full[1], j & 1, status, 216)) { ok = false; break; }
-        tc_fence_after();
-        if (pt.use_b(kt)) {
-          issue_pv(1, st, !pv_b);
-          pv_b = true;
-        }
-        if (kn >= 0) {
-          if (pt.use_b(kn)) issue_s(1, stn);
+          if (pt.use_b(0)) issue_s(1, 0);
           mma_commit(&s_full[1]);
         }
-        mma_commit(&kv_empty[st]);
-        kt = kn;
-      }
-      if (ok) {
-        mma_commit(&o_full[0]);
-        mma_commit(&o_full[1]);
+        bool pv_a = false, pv_b = false;
+        int j = 0;
+        for (int kt = 0; kt >= 0 && ok; ++j) {
+          const int st = j & 1;
+          const int kn = pt.next(kt);
+          const int stn = (j + 1) & 1;
+          // tile A: PV of key tile kt, then S of the next key tile
+          if (!mbar_wait(&p_full[0], j & 1, status, 214)) { ok = false; break; }
+          tc_fence_after();
+          if (pt.use_a(kt)) {
+            issue_pv(0, st, !pv_a);
+            pv_a = true;
+          }
+          if (kn >= 0) {
+            if (!mbar_wait(&kv_full[stn], ((j + 1) >> 1) & 1, status, 215)) { ok = false; break; }
+            tc_fence_after();
+            if (pt.use_a(kn)) issue_s(0, stn);
+            mma_commit(&s_full[0]);
+          }
+          // tile B
+          if (!mbar_wait(&p_full[1], j & 1, status, 216)) { ok = false; break; }
+          tc_fence_after();
+          if (pt.use_b(kt)) {
+            issue_pv(1, st, !pv_b);
+            pv_b = true;
+          }
+          if (kn >= 0) {
+            if (pt.use_b(kn)) issue_s(1, stn);
+            mma_commit(&s_full[1]);
+          }
+          mma_commit(&kv_empty[st]);
+          kt = kn;
+        }
+        if (ok) {
+          mma_commit(&o_full[0]);
+          mma_commit(&o_full[1]);
+        }
       }
     }
   } else {
-    // ---------------- softmax: warps 2..5 tile A, 6..9 tile B; thread = query row ----
-    const int t = (warp - 2) >> 2;
+    setmaxnreg_inc<kRegsHigh>();
+    // ---------------- softmax: warps 4..7 tile A, 8..11 tile B; thread = query row ----
+    const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int s = q0 + t * TQ + row;
@@ -538,27 +555,25 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
         for (int c = 0; c < 128; c += 32) tmem_ld32(tS + c, x + c);
         tmem_wait_ld();
         const int k0 = kt * TK;
-        // 8 independent partial maxima (short dependency chains), combined at the end
-        float mp[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
-        if (k0 + TK - 1 <= qi) {  // every key of the tile is a real key <= the row's anchor
-#pragma unroll
-          for (int c = 0; c < 128; ++c) {
-            x[c] *= scale_log2;
-            mp[c & 7] = fmaxf(mp[c & 7], x[c]);
-          }
-        } else {
+        if (k0 + TK - 1 > qi) {  // not every key is a real key <= the row's anchor: mask
 #pragma unroll
           for (int c = 0; c < 128; ++c) {
             const int ks = k0 + c;
             const bool allow = ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
-            x[c] = allow ? x[c] * scale_log2 : -INFINITY;
-            mp[c & 7] = fmaxf(mp[c & 7], x[c]);
+            x[c] = allow ? x[c] : -INFINITY;
           }
         }
-        const float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                               fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+        // maximum of the raw scores (the scale is positive, so it commutes with the
+        // maximum): 4 independent chains of 3-input maxima
+        float mp[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) mp[u] = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; c += 8) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) mp[u] = max3f(mp[u], x[c + 2 * u], x[c + 2 * u + 1]);
+        }
+        const float mt = max3f(mp[0], mp[1], fmaxf(mp[2], mp[3])) * scale_log2;
         // raise the reference maximum only when the tile exceeds it by > 2^8
         float alpha = 1.f;
         if (mt > m + kRescaleLog2) {
@@ -566,23 +581,34 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           m = mt;
           l *= alpha;
         }
-        const float m_use = m == -INFINITY ? 0.f : m;
-        // P_t over the first 64 columns of S_t (packed bf16 pairs); 8 partial row sums
-        float rp[8];
+        const float nm = m == -INFINITY ? 0.f : -m;
+        // P_t = 2^(x c - m) over the first 64 columns of S_t (packed bf16 pairs): the
+        // scale-and-subtract and the 4 partial row sums run as packed f32x2 operations,
+        // and every kEmuEvery-th pair's exponential runs on the FMA pipe
+        float2 rs[4];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) rp[u] = 0.f;
+        for (int u = 0; u < 4; ++u) rs[u] = make_float2(0.f, 0.f);
+        const float2 sc = make_float2(scale_log2, scale_log2), off = make_float2(nm, nm);
 #pragma unroll
-        for (int c0 = 0; c0 < 128; c0 += 64) {
-          uint32_t pk[32];
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) {
-            const float p0 = ex2_approx(x[c0 + c] - m_use), p1 = ex2_approx(x[c0 + c + 1] - m_use);
-            rp[(c >> 1) & 7] += p0 + p1;
-            pk[c / 2] = pack_bf16x2(p0, p1);
+          for (int c = 0; c < 32; c += 2) {
+            const float2 y = fma2(make_float2(x[c0 + c], x[c0 + c + 1]), sc, off);
+            float2 p;
+            if (kEmuEvery > 0 && (c / 2) % kEmuEvery == kEmuEvery - 1) {
+              p = exp2_poly2(y);
+            } else {
+              p.x = ex2_approx(y.x);
+              p.y = ex2_approx(y.y);
+            }
+            rs[(c >> 1) & 3] = add2(rs[(c >> 1) & 3], p);
+            pk[c / 2] = pack_bf16x2(p.x, p.y);
           }
-          tmem_st32(tS + c0 / 2, pk);
+          tmem_st16(tS + c0 / 2, pk);
         }
-        l += ((rp[0] + rp[1]) + (rp[2] + rp[3])) + ((rp[4] + rp[5]) + (rp[6] + rp[7]));
+        const float2 rsum = add2(add2(rs[0], rs[1]), add2(rs[2], rs[3]));
+        l += rsum.x + rsum.y;
         // O holds the tiles before this one (their PV completed before this S did):
         // rescale it when the maximum moved
         if (__any_sync(0xffffffffu, alpha != 1.f) && j > 0) {
@@ -667,8 +693,16 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   }
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc2_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_FWD2));
+  {
+    // the warpgroups' register re-split assumes the launch grants 168 per thread:
+    // with fewer, setmaxnreg.inc would wait for registers that never free up
+    cudaFuncAttributes fa;
+    PE_CUDA_TRY(cudaFuncGetAttributes(&fa, attn_fwd_tc2_kernel));
+    PE_CHECK_ARG(fa.numRegs * kThreads2 >= 4 * 32 * kRegsLow + 8 * 32 * kRegsHigh,
+                 "attention (tcgen05): forward kernel compiled with too few registers");
+  }
   dim3 grid((unsigned)Hq, (unsigned)((S + 2 * TQ - 1) / (2 * TQ)));
-  attn_fwd_tc2_kernel<<<grid, kThreads, SMEM_FWD2, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
+  attn_fwd_tc2_kernel<<<grid, kThreads2, SMEM_FWD2, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
                                                          g, Hq, Hq / Hkv, scale_log2, status);
   PE_LAUNCHED();
   return PE_OK;

@@ -39,5 +39,134 @@ __device__ __forceinline__ uint32_t swz(int r, int u) {
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ---------------------------------------------------- backward tile lists ----
+// Up to three disjoint, ascending index ranges [b_i, e_i) (empty ranges are
+// b = e = kEmpty and sort last).  Every member is indexed statically, so the
+// struct lives in registers.
+struct Ranges {
+  static constexpr int kEmpty = 0x3fffffff;
+  int b0, e0, b1, e1, b2, e2;
+  __device__ __forceinline__ int count() const { return (e0 - b0) + (e1 - b1) + (e2 - b2); }
+  __device__ __forceinline__ int at(int j) const {
+    if (j < e0 - b0) return b0 + j;
+    j -= e0 - b0;
+    if (j < e1 - b1) return b1 + j;
+    return b2 + (j - (e1 - b1));
+  }
+};
+
+__device__ __forceinline__ void sort2(int& b0, int& e0, int& b1, int& e1) {
+  if (b1 < b0) {
+    const int tb = b0, te = e0;
+    b0 = b1; e0 = e1;
+    b1 = tb; e1 = te;
+  }
+}
+
+// query tiles (of tq rows) whose rows can read some key of key tile [k0, k0 + TK)
+__device__ __forceinline__ Ranges query_tiles(const PartGeom& g, int k0, int tq = TQ) {
+  constexpr int E = Ranges::kEmpty;
+  const int k1 = min(k0 + TK, g.S);
+  const int nqt = (g.S + tq - 1) / tq;
+  int b0 = E, e0 = E, b1 = E, e1 = E, b2 = E, e2 = E;
+  if (k0 < g.a1) {
+    b0 = k0 / tq;  // real rows [k0, a1)
+    e0 = (g.a1 - 1) / tq + 1;
+    const int af = max(g.a0, k0);  // prediction rows of anchors >= max(a0, k0)
+    if (g.km1 > 0 && af < g.a1) {
+      b1 = (g.a1 + (af - g.a0) * g.km1) / tq;
+      e1 = nqt;
+    }
+  }
+  if (k1 > g.a1 && g.km1 > 0) {  // the prediction keys' own rows
+    const int s0 = max(k0, g.a1);
+    const int i_f = g.a0 + (s0 - g.a1) / g.km1;
+    const int i_l = g.a0 + (k1 - 1 - g.a1) / g.km1;
+    b2 = (g.a1 + (i_f - g.a0) * g.km1) / tq;
+    e2 = (g.a1 + (i_l - g.a0 + 1) * g.km1 - 1) / tq + 1;
+  }
+  // sort by start, then merge overlapping / touching neighbours
+  sort2(b0, e0, b1, e1);
+  sort2(b1, e1, b2, e2);
+  sort2(b0, e0, b1, e1);
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    if (b1 != E && b1 <= e0) {
+      e0 = max(e0, e1);
+      b1 = b2; e1 = e2;
+      b2 = e2 = E;
+    }
+  }
+  if (b2 != E && b2 <= e1) {
+    e1 = max(e1, e2);
+    b2 = e2 = E;
+  }
+  Ranges R;
+  R.b0 = b0; R.e0 = e0; R.b1 = b1; R.e1 = e1; R.b2 = b2; R.e2 = e2;
+  return R;
+}
+
+// true when every (query in [q0, q0+tq), key in [k0, k0+TK)) pair is allowed:
+// all keys real and no query row's anchor below the last key
+__device__ __forceinline__ bool tile_fully_allowed(const PartGeom& g, int q0, int k0,
+                                                   int tq = TQ) {
+  const int k_last = k0 + TK - 1;
+  if (k_last >= g.a1 || q0 + tq > g.S) return false;
+  int min_anchor = 1 << 30;
+  if (q0 < g.a1) min_anchor = q0;
+  if (q0 + tq > g.a1) {
+    int i, d;
+    decode(g, max(q0, g.a1), i, d);
+    min_anchor = min(min_anchor, i);
+  }
+  return min_anchor >= k_last;
+}
+
+// key tiles (of tk keys) read by query tile [q0, q0 + TQ): [0, r_end) then [m_beg, m_end)
+__device__ __forceinline__ void key_tiles(const PartGeom& g, int q0, int& r_end, int& m_beg,
+                                          int& m_end, int tk = TK) {
+  const int last = min(q0 + TQ, g.S) - 1;
+  int i_last, d_last;
+  decode(g, last, i_last, d_last);
+  const int i_max = q0 < g.a1 ? max(i_last, min(last, g.a1 - 1)) : i_last;
+  r_end = i_max / tk + 1;
+  m_beg = m_end = 0;
+  if (last >= g.a1 && g.km1 > 0) {
+    const int first = max(q0, g.a1);
+    int i_first, d_first;
+    decode(g, first, i_first, d_first);
+    const int lo = g.a1 + (i_first - g.a0) * g.km1;
+    const int hi = g.a1 + (i_last - g.a0 + 1) * g.km1;
+    int mb = lo / tk, me = (hi - 1) / tk + 1;
+    if (mb < r_end) mb = r_end;
+    if (me > mb) {
+      m_beg = mb;
+      m_end = me;
+    }
+  }
+}
+
+__device__ __forceinline__ void atomic_add_row32(float* dst, const float* v, float mul) {
+  float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int t = 0; t < 8; ++t)
+    atomicAdd(d4 + t, make_float4(v[4 * t] * mul, v[4 * t + 1] * mul, v[4 * t + 2] * mul,
+                                  v[4 * t + 3] * mul));
+}
+
 }  // namespace attn_tc
+
+// dQ kernel (attn_tc_bwd_q.cu): dq (bf16) = scale * sum dS K per query tile
+int attn_bwd_q2_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
+                       int64_t k_ss, const void* v, int64_t v_ss, const void* dout, int64_t do_ss,
+                       const float* lse, const float* delta, void* dq, int64_t dq_ss,
+                       const attn_tc::PartGeom& g, int* status, cudaStream_t st);
+// persistent dK / dV kernel (attn_tc_bwd_kv.cu): accumulates fp32 dK, dV of every
+// query head into the KV-head accumulators (zeroed beforehand), items claimed from
+// *work_counter (zeroed beforehand)
+int attn_bwd_kv2_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
+                        int64_t k_ss, const void* v, int64_t v_ss, const void* dout,
+                        int64_t do_ss, const float* lse, const float* delta, float* dk_acc,
+                        float* dv_acc, int* work_counter, const attn_tc::PartGeom& g,
+                        int* status, cudaStream_t st);
 }  // namespace pe

@@ -34,91 +34,8 @@ constexpr int kSoftmaxThreads = 256;
 // K, V, Q, dO, P^T, dS^T tiles + per-query (lse, delta, anchor, depth) x 2 buffers
 constexpr size_t SMEM_BWD = 1024 + 6 * TILE_BYTES + 2 * 4 * TQ * 4 + 256;
 
-struct Ranges {
-  int b[3], e[3], n;
-  __device__ __forceinline__ int count() const {
-    int c = 0;
-    for (int i = 0; i < n; ++i) c += e[i] - b[i];
-    return c;
-  }
-  __device__ __forceinline__ int at(int j) const {
-    for (int i = 0; i < n; ++i) {
-      const int len = e[i] - b[i];
-      if (j < len) return b[i] + j;
-      j -= len;
-    }
-    return 0;
-  }
-};
-
-// query tiles whose rows can read some key of key tile [k0, k0 + TK)
-__device__ __forceinline__ Ranges query_tiles(const PartGeom& g, int k0) {
-  const int k1 = min(k0 + TK, g.S);
-  const int nqt = (g.S + TQ - 1) / TQ;
-  int b[3], e[3], n = 0;
-  if (k0 < g.a1) {
-    b[n] = k0 / TQ;  // real rows [k0, a1)
-    e[n] = (g.a1 - 1) / TQ + 1;
-    ++n;
-    const int af = max(g.a0, k0);  // prediction rows of anchors >= max(a0, k0)
-    if (g.km1 > 0 && af < g.a1) {
-      b[n] = (g.a1 + (af - g.a0) * g.km1) / TQ;
-      e[n] = nqt;
-      ++n;
-    }
-  }
-  if (k1 > g.a1 && g.km1 > 0) {
-    const int s0 = max(k0, g.a1);
-    const int i_f = g.a0 + (s0 - g.a1) / g.km1;
-    const int i_l = g.a0 + (k1 - 1 - g.a1) / g.km1;
-    b[n] = (g.a1 + (i_f - g.a0) * g.km1) / TQ;
-    e[n] = (g.a1 + (i_l - g.a0 + 1) * g.km1 - 1) / TQ + 1;
-    ++n;
-  }
-  for (int i = 1; i < n; ++i)
-    for (int j = i; j > 0 && b[j] < b[j - 1]; --j) {
-      int t = b[j]; b[j] = b[j - 1]; b[j - 1] = t;
-      t = e[j]; e[j] = e[j - 1]; e[j - 1] = t;
-    }
-  Ranges R;
-  R.n = 0;
-  for (int i = 0; i < n; ++i) {
-    if (R.n > 0 && b[i] <= R.e[R.n - 1]) {
-      R.e[R.n - 1] = max(R.e[R.n - 1], e[i]);
-    } else {
-      R.b[R.n] = b[i];
-      R.e[R.n] = e[i];
-      ++R.n;
-    }
-  }
-  return R;
-}
-
-// true when every (query in [q0, q0+TQ), key in [k0, k0+TK)) pair is allowed:
-// all keys real and no query row's anchor below the last key
-__device__ __forceinline__ bool tile_fully_allowed(const PartGeom& g, int q0, int k0) {
-  const int k_last = k0 + TK - 1;
-  if (k_last >= g.a1 || q0 + TQ > g.S) return false;
-  int min_anchor = 1 << 30;
-  if (q0 < g.a1) min_anchor = q0;
-  if (q0 + TQ > g.a1) {
-    int i, d;
-    decode(g, max(q0, g.a1), i, d);
-    min_anchor = min(min_anchor, i);
-  }
-  return min_anchor >= k_last;
-}
-
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-__device__ __forceinline__ void atomic_add_row32(float* dst, const float* v, float mul) {
-  float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-  for (int t = 0; t < 8; ++t)
-    atomicAdd(d4 + t, make_float4(v[4 * t] * mul, v[4 * t + 1] * mul, v[4 * t + 2] * mul,
-                                  v[4 * t + 3] * mul));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -406,30 +323,6 @@ constexpr int kKvCols = TQ / kKvParts;
 constexpr size_t SMEM_BWD_Q = 1024 + 2 * TILE_BYTES /*Q, dO*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ + 256;
 constexpr size_t SMEM_BWD_KV = 1024 + 2 * TILE_BYTES /*K, V*/ + 2 * 2 * TILE_BYTES /*Q,dO x2*/ +
                                2 * 4 * TQ * 4 /*per-query operands x2*/ + 256;
-
-// key tiles read by query tile [q0, q0 + TQ): [0, r_end) then [m_beg, m_end)
-__device__ __forceinline__ void key_tiles(const PartGeom& g, int q0, int& r_end, int& m_beg,
-                                          int& m_end) {
-  const int last = min(q0 + TQ, g.S) - 1;
-  int i_last, d_last;
-  decode(g, last, i_last, d_last);
-  const int i_max = q0 < g.a1 ? max(i_last, min(last, g.a1 - 1)) : i_last;
-  r_end = i_max / TK + 1;
-  m_beg = m_end = 0;
-  if (last >= g.a1 && g.km1 > 0) {
-    const int first = max(q0, g.a1);
-    int i_first, d_first;
-    decode(g, first, i_first, d_first);
-    const int lo = g.a1 + (i_first - g.a0) * g.km1;
-    const int hi = g.a1 + (i_last - g.a0 + 1) * g.km1;
-    int mb = lo / TK, me = (hi - 1) / TK + 1;
-    if (mb < r_end) mb = r_end;
-    if (me > mb) {
-      m_beg = mb;
-      m_end = me;
-    }
-  }
-}
 
 __global__ void __launch_bounds__(kKvThreads, 1)
 attn_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -977,12 +870,13 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 }
 
 // delta[h, s] = sum_d dO * O (fp32); zero the dQ accumulator row (when given) and, for the
-// first Hkv heads, the dK / dV accumulator rows
+// first Hkv heads, the dK / dV accumulator rows; zero the work counter
 __global__ void attn_bwd_prep_kernel(int S, int Hq, int Hkv, const __nv_bfloat16* __restrict__ o,
                                      int64_t o_ss, const __nv_bfloat16* __restrict__ dout,
                                      int64_t do_ss, float* __restrict__ delta,
                                      float* __restrict__ dq_acc, float* __restrict__ dk_acc,
-                                     float* __restrict__ dv_acc) {
+                                     float* __restrict__ dv_acc, int* __restrict__ counter) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) *counter = 0;
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= S * Hq) return;
@@ -1039,7 +933,7 @@ int launch_cast(int S, int cols, const float* acc, float mul, void* out, int64_t
 bool attn_tc_bwd_ready() { return true; }
 
 size_t attn_tc_bwd_acc_bytes(int64_t S, int Hq, int Hkv) {
-  return (size_t)S * (Hq + 2 * Hkv) * HD * 4;
+  return (size_t)S * (Hq + 2 * Hkv) * HD * 4 + 256;  // + the work counter
 }
 
 int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
@@ -1062,29 +956,45 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   float* dq_acc = acc;
   float* dk_acc = dq_acc + (int64_t)S * Hq * HD;
   float* dv_acc = dk_acc + (int64_t)S * Hkv * HD;
+  int* counter = reinterpret_cast<int*>(dv_acc + (int64_t)S * Hkv * HD);
   {
     const int warps = Si * Hq;
     attn_bwd_prep_kernel<<<(warps + 7) / 8, 256, 0, st>>>(
         Si, Hq, Hkv, (const __nv_bfloat16*)o, o_ss, (const __nv_bfloat16*)dout, do_ss, delta,
-        variant == 0 ? nullptr : dq_acc, dk_acc, dv_acc);
+        variant == 1 ? dq_acc : nullptr, dk_acc, dv_acc, counter);
     PE_LAUNCHED();
   }
   PartGeom g{Si, (int)m.a0, (int)m.a1, m.kd - 1};
   const float scale = 1.0f / sqrtf((float)HD);
-  if (variant == 0) {
-    PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_q_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BWD_Q));
-    PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BWD_KV));
-    dim3 gq((unsigned)Hq, (unsigned)((S + TQ - 1) / TQ));
-    attn_bwd_q_kernel<<<gq, kKvThreads, SMEM_BWD_Q, st>>>(tq, tk, tv, tdo, lse, delta,
-                                                        (__nv_bfloat16*)dq, dq_ss, g, Hq / Hkv,
-                                                        scale, status);
-    PE_LAUNCHED();
-    dim3 gkv((unsigned)Hq, (unsigned)((S + TK - 1) / TK));
-    attn_bwd_kv_kernel<<<gkv, kKvThreads, SMEM_BWD_KV, st>>>(tq, tk, tv, tdo, lse, delta, dk_acc,
-                                                           dv_acc, g, Hkv, Hq / Hkv, scale, status);
-    PE_LAUNCHED();
+  if (variant == 0 || variant == 2) {
+    if (variant == 0) {
+      rc = attn_bwd_q2_launch(S, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, dout, do_ss, lse, delta, dq,
+                              dq_ss, g, status, st);
+      if (rc) return rc;
+    } else {
+      PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_q_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)SMEM_BWD_Q));
+      dim3 gq((unsigned)Hq, (unsigned)((S + TQ - 1) / TQ));
+      attn_bwd_q_kernel<<<gq, kKvThreads, SMEM_BWD_Q, st>>>(tq, tk, tv, tdo, lse, delta,
+                                                          (__nv_bfloat16*)dq, dq_ss, g, Hq / Hkv,
+                                                          scale, status);
+      PE_LAUNCHED();
+    }
+    if (variant == 0) {
+      rc = attn_bwd_kv2_launch(S, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, dout, do_ss, lse, delta,
+                               dk_acc, dv_acc, counter, g, status, st);
+      if (rc) return rc;
+    } else {
+      PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)SMEM_BWD_KV));
+      dim3 gkv((unsigned)Hq, (unsigned)((S + TK - 1) / TK));
+      attn_bwd_kv_kernel<<<gkv, kKvThreads, SMEM_BWD_KV, st>>>(tq, tk, tv, tdo, lse, delta,
+                                                             dk_acc, dv_acc, g, Hkv, Hq / Hkv,
+                                                             scale, status);
+      PE_LAUNCHED();
+    }
     rc = launch_cast(Si, Hkv * HD, dk_acc, scale, dk, dk_ss, st);
     if (!rc) rc = launch_cast(Si, Hkv * HD, dv_acc, 1.f, dv, dv_ss, st);
     return rc;

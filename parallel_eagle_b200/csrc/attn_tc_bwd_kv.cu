@@ -1,0 +1,545 @@
+// Cross-depth masked flash attention backward, dK / dV half (tcgen05), as a
+// persistent kernel: the backward of reference src/pe/nn.py:84-88 under the
+// mask of src/pe/masks.py:43-61, partition slot layout (src/pe/partition.py:41-55).
+//
+// Work item = (query head h, 128-key tile).  One CTA per SM takes items from a
+// global counter in order of decreasing work (key tiles ascending, heads
+// fastest), so TMEM allocation, barrier set-up and the first loads happen once
+// per CTA and the next item's K / V / Q / dO loads overlap the current item.
+// For an item it walks, in 64-query steps, the query rows that can read the key
+// tile (keys on TMEM lanes):
+//   S^T  = K Q^T           dP^T = V dO^T           (N = 64)
+//   P^T  = 2^(S^T c - lse')  dS^T = P^T (dP^T - delta)   (compute warps; bf16
+//          packed back over S^T / dP^T; masked pairs exactly zero)
+//   dV  += P^T dO           dK  += dS^T Q
+// Operand placement follows the shared-memory bandwidth (128 B per clock per
+// SM): an MMA with both operands in shared memory needs (4 KB + N x 32 B) per
+// N / 2 clocks at M = 128 -- a third short of its rate at N = 64 -- while one
+// with A in TMEM reads only B, 64 B per clock.  dP^T, dV and dK take A from
+// TMEM (V copied there once per item, P^T / dS^T written by the compute
+// warps); S^T keeps both operands in shared memory but is double-buffered and
+// issued two steps ahead, off the critical path, while the single dP^T tile is
+// recomputed right after dK consumed dS^T.  Per step the MMAs issue as
+//   dV(i), dK(i), dP^T(i+1), S^T(i+2).
+// The item's dK / dV tile is added (fp32) into the KV head's accumulators,
+// reducing the query heads of a GQA group without expanding K / V.
+//
+// Warp roles (384 threads):
+//   warp 0      scheduler + TMA: claims items; K per item (two buffers), V per
+//               item (one buffer, refilled once the compute warps copied it into
+//               TMEM); Q / dO per step into 4- and 3-deep rings
+//   warp 1      tcgen05.mma issue
+//   warp 2      per-query operands (lse * log2 e, delta, anchor, depth) per step
+//   warp 3      idle
+//   warps 4-11  compute: two per TMEM lane quarter, each owning 32 of the 64
+//               query columns; per item each copies its half of V into TMEM,
+//               and part 0 drains dK, part 1 dV
+// TMEM: dK 0..127, dV 128..255, V 256..319 (bf16 pairs), S^T 320..383 /
+//       384..447, dP^T 448..511.
+#include "attn_tc.cuh"
+
+namespace pe {
+namespace {
+
+using namespace sm100;
+using namespace attn_tc;
+
+constexpr int QT = 64;                          // queries per step
+constexpr uint32_t SUB_BYTES = QT * HD * 2;      // 16 KB: 64 rows x 128 bf16
+constexpr uint32_t SUB_CHUNK = SUB_BYTES / 2;    // 8 KB: 64 rows x 128 B
+constexpr int QS = 4, DS = 3, MS = 4;           // ring depths: Q, dO, per-query operands
+constexpr int kThreads = 384;
+constexpr int kComputeWarps = 8;
+constexpr int kCols = QT / 2;                   // query columns per compute warp
+
+// shared memory (offsets from the 1024-aligned base)
+constexpr uint32_t OFF_K = 0;                        // [2] K tiles
+constexpr uint32_t OFF_V = OFF_K + 2 * TILE_BYTES;
+constexpr uint32_t OFF_Q = OFF_V + TILE_BYTES;
+constexpr uint32_t OFF_DO = OFF_Q + QS * SUB_BYTES;
+constexpr uint32_t OFF_L = OFF_DO + DS * SUB_BYTES;   // float [MS][QT]  lse * log2 e
+constexpr uint32_t OFF_D = OFF_L + MS * QT * 4;       // float [MS][QT]  delta
+constexpr uint32_t OFF_A = OFF_D + MS * QT * 4;       // int   [MS][QT]  anchor (-1: no row)
+constexpr uint32_t OFF_E = OFF_A + MS * QT * 4;       // int   [MS][QT]  depth
+constexpr uint32_t OFF_ITEM = OFF_E + MS * QT * 4;    // int   [2]
+constexpr uint32_t OFF_BAR = OFF_ITEM + 16;
+constexpr int NBARS = 2 + 2 + 2 + 2 + 1 + 1 + 2 * QS + 2 * DS + 2 * MS + 2 + 2 + 1 + 1 + 1;
+constexpr uint32_t OFF_TMEM = OFF_BAR + NBARS * 8;
+constexpr size_t SMEM_KV2 = 1024 + OFF_TMEM + 16;
+
+struct Bars {
+  uint64_t *item_full, *item_empty, *k_full, *k_empty, *v_full, *v_copied, *q_full, *q_empty,
+      *do_full, *do_empty, *meta_full, *meta_empty, *st_full, *p_full, *dpt_full, *ds_full,
+      *acc_full;
+  __device__ explicit Bars(uint64_t* b) {
+    item_full = b; b += 2;
+    item_empty = b; b += 2;
+    k_full = b; b += 2;      // K tile (per item parity) landed
+    k_empty = b; b += 2;     // the item's last S^T read it
+    v_full = b; b += 1;      // V tile landed in shared memory
+    v_copied = b; b += 1;    // compute warps copied it into TMEM (smem free, TMEM ready)
+    q_full = b; b += QS;
+    q_empty = b; b += QS;
+    do_full = b; b += DS;
+    do_empty = b; b += DS;
+    meta_full = b; b += MS;
+    meta_empty = b; b += MS;
+    st_full = b; b += 2;
+    p_full = b; b += 2;
+    dpt_full = b; b += 1;
+    ds_full = b; b += 1;
+    acc_full = b; b += 1;
+  }
+};
+
+// the item's key tile and the 64-query steps that read it
+struct Item {
+  int h, kvh, k0;
+  Ranges qr;
+  int n;
+  __device__ Item(int w, int Hq, int rep, const PartGeom& g) {
+    const int kt = w / Hq;
+    h = w - kt * Hq;
+    kvh = h / rep;
+    k0 = kt * TK;
+    qr = query_tiles(g, k0, QT);
+    n = qr.count();
+  }
+};
+
+// packed P^T / dS^T: the queries of compute part p (columns [p C, p C + C)) sit in
+// columns [p C, p C + C / 2) of their tile, which only part p writes
+__device__ __forceinline__ uint32_t a_col(int kk) {
+  constexpr int steps = kCols / 16;
+  return (uint32_t)((kk / steps) * kCols + (kk % steps) * 8);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const float* __restrict__ lse, const float* __restrict__ delta,
+                    float* __restrict__ dk_acc, float* __restrict__ dv_acc, int* work_counter,
+                    PartGeom g, int Hq, int Hkv, int rep, float scale, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sK = smem + OFF_K;
+  uint8_t* sV = smem + OFF_V;
+  float* sL = reinterpret_cast<float*>(smem + OFF_L);
+  float* sD = reinterpret_cast<float*>(smem + OFF_D);
+  int* sA = reinterpret_cast<int*>(smem + OFF_A);
+  int* sE = reinterpret_cast<int*>(smem + OFF_E);
+  volatile int* sItem = reinterpret_cast<volatile int*>(smem + OFF_ITEM);
+  Bars B(reinterpret_cast<uint64_t*>(smem + OFF_BAR));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkt = (g.S + TK - 1) / TK;
+  const int total = Hq * nkt;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.item_full[i], 1);
+      mbar_init(&B.item_empty[i], 2 + kComputeWarps);  // MMA, operands, compute warps
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.k_full[i], 1);
+      mbar_init(&B.k_empty[i], 1);
+      // S^T is two steps ahead, so a fast warp may reach step i + 1 before a slow
+      // one arrives for step i (never step i + 2): one P^T barrier per S^T buffer
+      mbar_init(&B.st_full[i], 1);
+      mbar_init(&B.p_full[i], kComputeWarps);
+    }
+    mbar_init(B.v_full, 1);
+    mbar_init(B.v_copied, kComputeWarps);
+    for (int i = 0; i < QS; ++i) {
+      mbar_init(&B.q_full[i], 1);
+      mbar_init(&B.q_empty[i], 1);
+    }
+    for (int i = 0; i < DS; ++i) {
+      mbar_init(&B.do_full[i], 1);
+      mbar_init(&B.do_empty[i], 1);
+    }
+    for (int i = 0; i < MS; ++i) {
+      mbar_init(&B.meta_full[i], 32);
+      mbar_init(&B.meta_empty[i], kComputeWarps);
+    }
+    // dP^T(i + 1) is computed only after every warp arrived for dS^T(i)
+    mbar_init(B.dpt_full, 1);
+    mbar_init(B.ds_full, kComputeWarps);
+    mbar_init(B.acc_full, 1);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tDK = tmem, tDV = tmem + 128, tV = tmem + 256;
+  const uint32_t tS = tmem + 320, tDP = tmem + 448;  // S^T buffer b at tS + b * QT
+
+  // every role walks the same item sequence; `ic` counts items, `gs` steps
+  auto read_item = [&](int ic, bool& ok) -> int {
+    if (!mbar_wait(&B.item_full[ic & 1], (ic >> 1) & 1, status, 340)) {
+      ok = false;
+      return -1;
+    }
+    const int w = sItem[ic & 1];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&B.item_empty[ic & 1]);
+    return w;
+  };
+
+  if (warp == 0) {
+    // ---------------- scheduler + TMA ----------------
+    if (elect_one()) {
+      bool ok = true;
+      uint64_t* last_bar = nullptr;
+      uint32_t last_ph = 0;
+      int gs = 0;
+      for (int ic = 0;; ++ic) {
+        int w = atomicAdd(work_counter, 1);
+        if (w >= total) w = -1;
+        if (!mbar_wait(&B.item_empty[ic & 1], ((ic >> 1) & 1) ^ 1u, status, 341)) { ok = false; break; }
+        sItem[ic & 1] = w;
+        mbar_arrive(&B.item_full[ic & 1]);  // release: publishes the slot write
+        if (w < 0) break;
+        const Item it(w, Hq, rep, g);
+        // K into buffer ic & 1 once the item two back issued its last S^T
+        const int kb = ic & 1;
+        if (!mbar_wait(&B.k_empty[kb], ((ic >> 1) & 1) ^ 1u, status, 342)) { ok = false; break; }
+        uint8_t* kd = sK + kb * TILE_BYTES;
+        mbar_arrive_expect_tx(&B.k_full[kb], TILE_BYTES);
+        tma_load_2d(kd, &tmK, &B.k_full[kb], it.kvh * HD, it.k0);
+        tma_load_2d(kd + CHUNK, &tmK, &B.k_full[kb], it.kvh * HD + 64, it.k0);
+        last_bar = &B.k_full[kb];
+        last_ph = (ic >> 1) & 1;
+        // V once the previous item's V left shared memory for TMEM
+        if (!mbar_wait(B.v_copied, (ic & 1) ^ 1u, status, 357)) { ok = false; break; }
+        mbar_arrive_expect_tx(B.v_full, TILE_BYTES);
+        tma_load_2d(sV, &tmV, B.v_full, it.kvh * HD, it.k0);
+        tma_load_2d(sV + CHUNK, &tmV, B.v_full, it.kvh * HD + 64, it.k0);
+        last_bar = B.v_full;
+        last_ph = ic & 1;
+        for (int i = 0; i < it.n && ok; ++i) {
+          const int gi = gs + i;
+          const int q0 = it.qr.at(i) * QT;
+          const int qs = gi % QS, ds = gi % DS;
+          if (!mbar_wait(&B.q_empty[qs], ((gi / QS) & 1) ^ 1u, status, 343)) { ok = false; break; }
+          uint8_t* qd = smem + OFF_Q + qs * SUB_BYTES;
+          mbar_arrive_expect_tx(&B.q_full[qs], SUB_BYTES);
+          tma_load_2d(qd, &tmQ, &B.q_full[qs], it.h * HD, q0);
+          tma_load_2d(qd + SUB_CHUNK, &tmQ, &B.q_full[qs], it.h * HD + 64, q0);
+          last_bar = &B.q_full[qs];
+          last_ph = (gi / QS) & 1;
+          if (!mbar_wait(&B.do_empty[ds], ((gi / DS) & 1) ^ 1u, status, 344)) { ok = false; break; }
+          uint8_t* dd = smem + OFF_DO + ds * SUB_BYTES;
+          mbar_arrive_expect_tx(&B.do_full[ds], SUB_BYTES);
+          tma_load_2d(dd, &tmDO, &B.do_full[ds], it.h * HD, q0);
+          tma_load_2d(dd + SUB_CHUNK, &tmDO, &B.do_full[ds], it.h * HD + 64, q0);
+          last_bar = &B.do_full[ds];
+          last_ph = (gi / DS) & 1;
+        }
+        if (!ok) break;
+        gs += it.n;
+      }
+      // on a failed wait, let this thread's last copy land before the CTA exits
+      if (!ok && last_bar) mbar_wait(last_bar, last_ph, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue ----------------
+    bool ok = true;
+    int gs = 0;
+    constexpr uint32_t ID_KQ = idesc_bf16(TK, QT, false, false);  // S^T, dP^T
+    constexpr uint32_t ID_KM = idesc_bf16(TK, HD, false, true);   // dV, dK (A = P^T / dS^T)
+    for (int ic = 0; ok; ++ic) {
+      const int w = read_item(ic, ok);
+      if (w < 0) break;
+      const bool leader = elect_one();
+      const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
+      if (leader) {
+        const Item it(w, Hq, rep, g);
+        const int kb = ic & 1, last = gs + it.n - 1;
+        const uint32_t k_base = smem_u32(sK + kb * TILE_BYTES);
+        // S^T(gi) = K Q(gi)^T into buffer gi & 1, both operands in shared memory
+        auto issue_st = [&](int gi) -> bool {
+          const int qs = gi % QS;
+          if (!mbar_wait(&B.q_full[qs], (gi / QS) & 1, status, 345)) return false;
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(smem + OFF_Q + qs * SUB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk)
+            mma_bf16_ss(tS + (gi & 1) * QT,
+                        sw128_desc(k_base + (kk >> 2) * CHUNK + (kk & 3) * 32, 16, 1024),
+                        sw128_desc(q_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024),
+                        ID_KQ, kk > 0 ? 1u : 0u);
+          mma_commit(&B.st_full[gi & 1]);
+          if (gi == last) mma_commit(&B.k_empty[kb]);  // the item's last read of K
+          return true;
+        };
+        // dP^T(gi) = V dO(gi)^T, A (V) from TMEM
+        auto issue_dpt = [&](int gi) -> bool {
+          const int ds = gi % DS;
+          if (!mbar_wait(&B.do_full[ds], (gi / DS) & 1, status, 346)) return false;
+          tc_fence_after();
+          const uint32_t do_base = smem_u32(smem + OFF_DO + ds * SUB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk)
+            mma_bf16_ts(tDP, tV + kk * 8,
+                        sw128_desc(do_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024),
+                        ID_KQ, kk > 0 ? 1u : 0u);
+          mma_commit(B.dpt_full);
+          return true;
+        };
+        ok = mbar_wait(&B.k_full[kb], (ic >> 1) & 1, status, 347);
+        if (ok) {
+          tc_fence_after();
+          ok = issue_st(gs);
+        }
+        if (ok && it.n > 1) ok = issue_st(gs + 1);
+        // V of this item in TMEM (copied after the previous item's MMAs completed)
+        if (ok) ok = mbar_wait(B.v_copied, ic & 1, status, 358);
+        if (ok) {
+          tc_fence_after();
+          ok = issue_dpt(gs);
+        }
+        for (int i = 0; i < it.n && ok; ++i) {
+          const int gi = gs + i, b = gi & 1;
+          const uint32_t acc = i > 0 ? 1u : 0u;
+          if (!mbar_wait(&B.p_full[b], (gi >> 1) & 1, status, 348)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t do_base = smem_u32(smem + OFF_DO + (gi % DS) * SUB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < QT / 16; ++kk)
+            mma_bf16_ts(tDV, tS + b * QT + a_col(kk),
+                        sw128_desc(do_base + kk * 2048, SUB_CHUNK, 1024), ID_KM,
+                        (acc | kk) != 0 ? 1u : 0u);
+          mma_commit(&B.do_empty[gi % DS]);
+          if (!mbar_wait(B.ds_full, gi & 1, status, 349)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(smem + OFF_Q + (gi % QS) * SUB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < QT / 16; ++kk)
+            mma_bf16_ts(tDK, tDP + a_col(kk), sw128_desc(q_base + kk * 2048, SUB_CHUNK, 1024),
+                        ID_KM, (acc | kk) != 0 ? 1u : 0u);
+          mma_commit(&B.q_empty[gi % QS]);
+          // dP^T(i+1) overwrites dS^T(i) after dK(i) read it, S^T(i+2) overwrites
+          // P^T(i) after dV(i) read it (tcgen05 executes in issue order)
+          if (i + 1 < it.n && !issue_dpt(gi + 1)) { ok = false; break; }
+          if (i + 2 < it.n && !issue_st(gi + 2)) { ok = false; break; }
+        }
+        if (ok) mma_commit(B.acc_full);
+        gs += it.n;
+      }
+      __syncwarp();
+      ok = __shfl_sync(0xffffffffu, ok, leader_lane);
+      gs = __shfl_sync(0xffffffffu, gs, leader_lane);
+    }
+  } else if (warp == 2) {
+    // ---------------- per-query operands ----------------
+    bool ok = true;
+    int gs = 0;
+    for (int ic = 0; ok; ++ic) {
+      const int w = read_item(ic, ok);
+      if (w < 0) break;
+      const Item it(w, Hq, rep, g);
+      for (int i = 0; i < it.n; ++i) {
+        const int gi = gs + i, slot = gi % MS;
+        const int q0 = it.qr.at(i) * QT;
+        if (!mbar_wait(&B.meta_empty[slot], ((gi / MS) & 1) ^ 1u, status, 350)) ok = false;
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+#pragma unroll
+        for (int u = 0; u < QT / 32; ++u) {
+          const int r = u * 32 + lane, q = q0 + r;
+          float lv = INFINITY, dl = 0.f;
+          int qa = -1, qd = 0;
+          if (q < g.S) {
+            lv = lse[(int64_t)it.h * g.S + q] * kLog2e;
+            dl = delta[(int64_t)it.h * g.S + q];
+            decode(g, q, qa, qd);
+          }
+          sL[slot * QT + r] = lv;
+          sD[slot * QT + r] = dl;
+          sA[slot * QT + r] = qa;
+          sE[slot * QT + r] = qd;
+        }
+        mbar_arrive(&B.meta_full[slot]);  // every lane: release of its own writes
+      }
+      gs += it.n;
+    }
+  } else if (warp >= 4) {
+    // ---------------- compute: thread = key row (TMEM lane) ----------------
+    constexpr int C = kCols;
+    const int quarter = warp & 3;
+    const int part = (warp - 4) >> 2;
+    const int cb = part * C;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const float scale_log2 = scale * kLog2e;
+    const int64_t kv_ld = (int64_t)Hkv * HD;
+    bool ok = true;
+    int gs = 0;
+    // the previous item's dK (part 0) / dV (part 1) row, drained after the next
+    // item's K / V copy so that item's first MMAs overlap the drain
+    float* pending = nullptr;
+    bool have_pending = false;
+    auto drain = [&](int ic_prev) -> bool {
+      if (!mbar_wait(B.acc_full, ic_prev & 1, status, 354)) return false;
+      tc_fence_after();
+      const uint32_t src = (part == 0 ? tDK : tDV) + lane_off;
+#pragma unroll 1
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        float v[32];
+        tmem_ld32(src + c0, v);
+        tmem_wait_ld();
+        if (pending) atomic_add_row32(pending + c0, v, 1.f);
+      }
+      return true;
+    };
+    int ic = 0;
+    for (; ok; ++ic) {
+      const int w = read_item(ic, ok);
+      if (w < 0) break;
+      const Item it(w, Hq, rep, g);
+      const int kj = it.k0 + row;
+      const bool kvalid = kj < g.S;
+      int ka = 0, ke = 0;
+      if (kvalid) decode(g, kj, ka, ke);
+      // ---- this warp's half of the V row (head dims [64 part, 64 part + 64)):
+      // shared memory -> TMEM, after the previous item's MMAs (which read the TMEM
+      // copy) all completed ----
+      if (have_pending && !mbar_wait(B.acc_full, (ic - 1) & 1, status, 355)) { ok = false; break; }
+      if (!mbar_wait(B.v_full, ic & 1, status, 356)) { ok = false; break; }
+      {
+        uint32_t r32[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint4 x = *reinterpret_cast<const uint4*>(sV + part * CHUNK + swz(row, u));
+          r32[u * 4 + 0] = x.x;
+          r32[u * 4 + 1] = x.y;
+          r32[u * 4 + 2] = x.z;
+          r32[u * 4 + 3] = x.w;
+        }
+        tmem_st32(tV + lane_off + part * 32, r32);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B.v_copied);
+      if (have_pending && !drain(ic - 1)) { ok = false; break; }
+      pending = kvalid ? (part == 0 ? dk_acc : dv_acc) + (int64_t)kj * kv_ld + it.kvh * HD : nullptr;
+      have_pending = true;
+      for (int i = 0; i < it.n; ++i) {
+        const int gi = gs + i, slot = gi % MS, b = gi & 1;
+        const int q0 = it.qr.at(i) * QT;
+        const bool full = tile_fully_allowed(g, q0, it.k0, QT);
+        // ---- P^T = 2^(S^T c - lse') ----
+        if (!mbar_wait(&B.meta_full[slot], (gi / MS) & 1, status, 351)) { ok = false; break; }
+        if (!mbar_wait(&B.st_full[b], (gi >> 1) & 1, status, 352)) { ok = false; break; }
+        tc_fence_after();
+        float pv[C];
+        tmem_ld32(tS + b * QT + lane_off + cb, pv);
+        tmem_wait_ld();
+        const float* L = sL + slot * QT + cb;
+        if (full) {
+#pragma unroll
+          for (int c = 0; c < C; c += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(L + c);
+            pv[c] = ex2_approx(fmaf(pv[c], scale_log2, -l4.x));
+            pv[c + 1] = ex2_approx(fmaf(pv[c + 1], scale_log2, -l4.y));
+            pv[c + 2] = ex2_approx(fmaf(pv[c + 2], scale_log2, -l4.z));
+            pv[c + 3] = ex2_approx(fmaf(pv[c + 3], scale_log2, -l4.w));
+          }
+        } else {
+          const int* QA = sA + slot * QT + cb;
+          const int* QE = sE + slot * QT + cb;
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            const int qa = QA[c];
+            const bool allow =
+                kvalid && qa >= 0 && (ke == 0 ? (ka <= qa) : (ka == qa && ke <= QE[c]));
+            pv[c] = allow ? ex2_approx(fmaf(pv[c], scale_log2, -L[c])) : 0.f;
+          }
+        }
+        {
+          uint32_t pw[C / 2];
+#pragma unroll
+          for (int c = 0; c < C; c += 2) pw[c / 2] = pack_bf16x2(pv[c], pv[c + 1]);
+          tmem_st16(tS + b * QT + lane_off + cb, pw);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B.p_full[b]);
+        // ---- dS^T = P^T (dP^T - delta) ----
+        if (!mbar_wait(B.dpt_full, gi & 1, status, 353)) { ok = false; break; }
+        tc_fence_after();
+        float dv[C];
+        tmem_ld32(tDP + lane_off + cb, dv);
+        tmem_wait_ld();
+        const float* D = sD + slot * QT + cb;
+        {
+          uint32_t pw[C / 2];
+#pragma unroll
+          for (int c = 0; c < C; c += 4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(D + c);
+            pw[c / 2] = pack_bf16x2(pv[c] * (dv[c] - d4.x), pv[c + 1] * (dv[c + 1] - d4.y));
+            pw[c / 2 + 1] =
+                pack_bf16x2(pv[c + 2] * (dv[c + 2] - d4.z), pv[c + 3] * (dv[c + 3] - d4.w));
+          }
+          tmem_st16(tDP + lane_off + cb, pw);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(B.ds_full);
+          mbar_arrive(&B.meta_empty[slot]);
+        }
+      }
+      if (!ok) break;
+      gs += it.n;
+    }
+    // the last item's dK / dV
+    if (ok && have_pending) drain(ic - 1);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+int attn_bwd_kv2_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
+                        int64_t k_ss, const void* v, int64_t v_ss, const void* dout,
+                        int64_t do_ss, const float* lse, const float* delta, float* dk_acc,
+                        float* dv_acc, int* work_counter, const PartGeom& g, int* status,
+                        cudaStream_t st) {
+  CUtensorMap tq, tk, tv, tdo;
+  int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, QT);
+  if (!rc) rc = make_tmap_2d(&tk, k, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)k_ss * 2, 64, TK);
+  if (!rc) rc = make_tmap_2d(&tv, v, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)v_ss * 2, 64, TK);
+  if (!rc)
+    rc = make_tmap_2d(&tdo, dout, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)do_ss * 2, 64, QT);
+  if (rc) return rc;
+  PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)SMEM_KV2));
+  const int64_t items = (int64_t)Hq * ((S + TK - 1) / TK);
+  const int grid = (int)(items < sm_count() ? items : sm_count());
+  attn_bwd_kv2_kernel<<<grid, kThreads, SMEM_KV2, st>>>(tq, tk, tv, tdo, lse, delta, dk_acc,
+                                                        dv_acc, work_counter, g, Hq, Hkv,
+                                                        Hq / Hkv, 1.0f / sqrtf((float)HD), status);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
+}  // namespace pe

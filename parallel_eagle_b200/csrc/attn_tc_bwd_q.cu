@@ -1,0 +1,344 @@
+// Cross-depth masked flash attention backward, dQ half (tcgen05): the backward
+// of reference src/pe/nn.py:84-88 under the mask of src/pe/masks.py:43-61,
+// partition slot layout (src/pe/partition.py:41-55).
+//
+// One CTA = one 128-row query tile of one head, walking the keys the tile reads
+// (the forward's key list) in 64-key steps, query row per TMEM lane:
+//   S = Q K^T,  dP = dO V^T                        (N = 64)
+//   dS = P (dP - delta),  P = 2^(S c - lse')      (compute warps; bf16 dS
+//                                                  packed back over S)
+//   dQ += dS K                                     (TMEM accumulator)
+// Every MMA takes its A operand from TMEM -- Q and dO are copied there once,
+// dS is written there -- so only B (K, V) streams from shared memory, 64 B per
+// clock at the full MMA rate; with both operands in shared memory an M = 128
+// MMA needs 96-192 B per clock against a shared-memory bandwidth of 128.  The
+// 64-key step leaves room to double-buffer S and dP (4 x 64 columns), so the
+// MMAs of step j + 1 (and j + 2) run while the compute warps work on step j.
+// At the end dQ is scaled and stored in bf16 straight from TMEM.
+//
+// Warp roles (384 threads):
+//   warp 0      TMA: Q / dO tile once, K / V per step into 4- and 3-deep rings
+//   warp 1      tcgen05.mma issue:  dQ(j), S(j+2), dP(j+2) per step
+//   warps 2, 3  idle
+//   warps 4-11  compute: two per TMEM lane quarter, each owning 32 of the 64
+//               key columns; part 0 also copies Q, part 1 dO into TMEM
+// TMEM: dQ 0..127, Q 128..191, dO 192..255 (bf16 pairs), S buffers 256 / 320,
+//       dP buffers 384 / 448.
+#include "attn_tc.cuh"
+
+namespace pe {
+namespace {
+
+using namespace sm100;
+using namespace attn_tc;
+
+constexpr int KT = 64;                         // keys per step
+constexpr uint32_t SUB_BYTES = KT * HD * 2;     // 16 KB: 64 rows x 128 bf16
+constexpr uint32_t SUB_CHUNK = SUB_BYTES / 2;   // 8 KB: 64 rows x 128 B
+constexpr int KS = 4, VS = 3;                  // ring depths
+constexpr int kThreads = 384;
+constexpr int kComputeWarps = 8;
+constexpr int kCols = KT / 2;                  // key columns per compute warp
+
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_DO = OFF_Q + TILE_BYTES;
+constexpr uint32_t OFF_K = OFF_DO + TILE_BYTES;
+constexpr uint32_t OFF_V = OFF_K + KS * SUB_BYTES;
+constexpr uint32_t OFF_BAR = OFF_V + VS * SUB_BYTES;
+constexpr int NBARS = 1 + 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
+constexpr uint32_t OFF_TMEM = OFF_BAR + NBARS * 8;
+constexpr size_t SMEM_Q2 = 1024 + OFF_TMEM + 16;
+
+struct Bars {
+  uint64_t *qdo_full, *qdo_copied, *k_full, *k_empty, *v_full, *v_empty, *s_full, *dp_full,
+      *ds_full, *dq_full;
+  __device__ explicit Bars(uint64_t* b) {
+    qdo_full = b; b += 1;
+    qdo_copied = b; b += 1;
+    k_full = b; b += KS;
+    k_empty = b; b += KS;
+    v_full = b; b += VS;
+    v_empty = b; b += VS;
+    s_full = b; b += 2;
+    dp_full = b; b += 2;
+    ds_full = b; b += 2;
+    dq_full = b; b += 1;
+  }
+};
+
+// packed dS: the keys of compute part p (columns [p C, p C + C)) sit in columns
+// [p C, p C + C / 2) of their S buffer, which only part p writes
+__device__ __forceinline__ uint32_t a_col(int kk) {
+  constexpr int steps = kCols / 16;
+  return (uint32_t)((kk / steps) * kCols + (kk % steps) * 8);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+attn_bwd_q2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                   const float* __restrict__ lse, const float* __restrict__ delta,
+                   __nv_bfloat16* __restrict__ dq, int64_t dq_ss, PartGeom g, int rep, float scale,
+                   int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  Bars B(reinterpret_cast<uint64_t*>(smem + OFF_BAR));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_qt = (g.S + TQ - 1) / TQ;
+  // grid (head, tile): blocks dispatch head-fastest, heaviest query tiles first
+  const int qt = num_qt - 1 - (int)blockIdx.y;
+  const int h = blockIdx.x;
+  const int kvh = h / rep;
+  const int q0 = qt * TQ;
+  int r_end, m_beg, m_end;
+  key_tiles(g, q0, r_end, m_beg, m_end, KT);
+  const int n = r_end + (m_end - m_beg);
+  auto step_key = [&](int j) { return (j < r_end ? j : m_beg + (j - r_end)) * KT; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(B.qdo_full, 1);
+    mbar_init(B.qdo_copied, kComputeWarps);
+    for (int i = 0; i < KS; ++i) {
+      mbar_init(&B.k_full[i], 1);
+      mbar_init(&B.k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
+      mbar_init(&B.v_full[i], 1);
+      mbar_init(&B.v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.s_full[i], 1);
+      mbar_init(&B.dp_full[i], 1);
+      // scores run up to two steps ahead, so a fast warp may reach step j + 1
+      // before a slow one arrives for step j (never step j + 2)
+      mbar_init(&B.ds_full[i], kComputeWarps);
+    }
+    mbar_init(B.dq_full, 1);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tDQ = tmem, tQ = tmem + 128, tDO = tmem + 192, tS = tmem + 256,
+                 tDP = tmem + 384;
+
+  if (warp == 0) {
+    // ---------------- TMA ----------------
+    if (elect_one()) {
+      bool ok = true;
+      uint64_t* last_bar = B.qdo_full;
+      uint32_t last_ph = 0;
+      mbar_arrive_expect_tx(B.qdo_full, 2 * TILE_BYTES);
+      tma_load_2d(smem + OFF_Q, &tmQ, B.qdo_full, h * HD, q0);
+      tma_load_2d(smem + OFF_Q + CHUNK, &tmQ, B.qdo_full, h * HD + 64, q0);
+      tma_load_2d(smem + OFF_DO, &tmDO, B.qdo_full, h * HD, q0);
+      tma_load_2d(smem + OFF_DO + CHUNK, &tmDO, B.qdo_full, h * HD + 64, q0);
+      for (int j = 0; j < n && ok; ++j) {
+        const int k0 = step_key(j);
+        const int ks = j % KS, vs = j % VS;
+        if (!mbar_wait(&B.k_empty[ks], ((j / KS) & 1) ^ 1u, status, 360)) { ok = false; break; }
+        uint8_t* kd = smem + OFF_K + ks * SUB_BYTES;
+        mbar_arrive_expect_tx(&B.k_full[ks], SUB_BYTES);
+        tma_load_2d(kd, &tmK, &B.k_full[ks], kvh * HD, k0);
+        tma_load_2d(kd + SUB_CHUNK, &tmK, &B.k_full[ks], kvh * HD + 64, k0);
+        last_bar = &B.k_full[ks];
+        last_ph = (j / KS) & 1;
+        if (!mbar_wait(&B.v_empty[vs], ((j / VS) & 1) ^ 1u, status, 361)) { ok = false; break; }
+        uint8_t* vd = smem + OFF_V + vs * SUB_BYTES;
+        mbar_arrive_expect_tx(&B.v_full[vs], SUB_BYTES);
+        tma_load_2d(vd, &tmV, &B.v_full[vs], kvh * HD, k0);
+        tma_load_2d(vd + SUB_CHUNK, &tmV, &B.v_full[vs], kvh * HD + 64, k0);
+        last_bar = &B.v_full[vs];
+        last_ph = (j / VS) & 1;
+      }
+      // let the last copy land before the CTA can exit
+      mbar_wait(last_bar, last_ph, ok ? status : nullptr, 362);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue ----------------
+    if (elect_one()) {
+      constexpr uint32_t ID_SP = idesc_bf16(TQ, KT, false, false);  // S, dP (A = Q / dO)
+      constexpr uint32_t ID_DQ = idesc_bf16(TQ, HD, false, true);   // dQ += dS K
+      // S(j) = Q K(j)^T and dP(j) = dO V(j)^T into buffers j & 1
+      auto issue_scores = [&](int j) -> bool {
+        const int ks = j % KS, vs = j % VS, b = j & 1;
+        if (!mbar_wait(&B.k_full[ks], (j / KS) & 1, status, 363)) return false;
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(smem + OFF_K + ks * SUB_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          mma_bf16_ts(tS + b * KT, tQ + kk * 8,
+                      sw128_desc(k_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024), ID_SP,
+                      kk > 0 ? 1u : 0u);
+        mma_commit(&B.s_full[b]);
+        if (!mbar_wait(&B.v_full[vs], (j / VS) & 1, status, 364)) return false;
+        tc_fence_after();
+        const uint32_t v_base = smem_u32(smem + OFF_V + vs * SUB_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk)
+          mma_bf16_ts(tDP + b * KT, tDO + kk * 8,
+                      sw128_desc(v_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024), ID_SP,
+                      kk > 0 ? 1u : 0u);
+        mma_commit(&B.dp_full[b]);
+        mma_commit(&B.v_empty[vs]);  // V(j) has no other reader
+        return true;
+      };
+      bool ok = mbar_wait(B.qdo_copied, 0, status, 365);
+      if (ok) {
+        tc_fence_after();
+        for (int j = 0; j < 2 && j < n && ok; ++j) ok = issue_scores(j);
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        const int b = j & 1, ks = j % KS;
+        if (!mbar_wait(&B.ds_full[b], (j >> 1) & 1, status, 366)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(smem + OFF_K + ks * SUB_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk)
+          mma_bf16_ts(tDQ, tS + b * KT + a_col(kk),
+                      sw128_desc(k_base + kk * 2048, SUB_CHUNK, 1024), ID_DQ,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&B.k_empty[ks]);
+        // S(j+2) / dP(j+2) overwrite buffer b after dQ(j) read dS(j) (in order)
+        if (j + 2 < n && !issue_scores(j + 2)) { ok = false; break; }
+      }
+      if (ok) mma_commit(B.dq_full);
+    }
+  } else if (warp >= 4) {
+    // ---------------- compute: thread = query row (TMEM lane) ----------------
+    constexpr int C = kCols;
+    const int quarter = warp & 3;
+    const int part = (warp - 4) >> 2;
+    const int cb = part * C;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int s = q0 + row;
+    const bool valid = s < g.S;
+    int qi = -1, qd = 0;
+    float l2 = 0.f, dl = 0.f;
+    if (valid) {
+      decode(g, s, qi, qd);
+      l2 = lse[(int64_t)h * g.S + s] * kLog2e;
+      dl = delta[(int64_t)h * g.S + s];
+    }
+    const int lo = qd > 0 ? g.a1 + (qi - g.a0) * g.km1 : 0;
+    const float scale_log2 = scale * kLog2e;
+    bool ok = mbar_wait(B.qdo_full, 0, status, 367);
+    if (ok) {
+      // Q (part 0) / dO (part 1) row -> TMEM as bf16 pairs (A operand)
+      const uint8_t* src = smem + (part == 0 ? OFF_Q : OFF_DO);
+      uint32_t r32[64];
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint4 x = *reinterpret_cast<const uint4*>(src + ch * CHUNK + swz(row, u));
+          r32[ch * 32 + u * 4 + 0] = x.x;
+          r32[ch * 32 + u * 4 + 1] = x.y;
+          r32[ch * 32 + u * 4 + 2] = x.z;
+          r32[ch * 32 + u * 4 + 3] = x.w;
+        }
+      const uint32_t dst = (part == 0 ? tQ : tDO) + lane_off;
+      tmem_st32(dst, r32);
+      tmem_st32(dst + 32, r32 + 32);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(B.qdo_copied);
+    }
+    for (int j = 0; j < n && ok; ++j) {
+      const int b = j & 1;
+      const int k0 = step_key(j) + cb;
+      if (!mbar_wait(&B.s_full[b], (j >> 1) & 1, status, 368)) { ok = false; break; }
+      tc_fence_after();
+      float sv[C];
+      tmem_ld32(tS + b * KT + lane_off + cb, sv);
+      tmem_wait_ld();
+      // P = 2^(S c - lse') (masked pairs exactly 0)
+      if (k0 + C - 1 <= qi) {  // every key of this warp's slice is real and <= the anchor
+#pragma unroll
+        for (int c = 0; c < C; ++c) sv[c] = ex2_approx(fmaf(sv[c], scale_log2, -l2));
+      } else {
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          const int ks = k0 + c;
+          const bool allow = ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
+          sv[c] = allow ? ex2_approx(fmaf(sv[c], scale_log2, -l2)) : 0.f;
+        }
+      }
+      if (!mbar_wait(&B.dp_full[b], (j >> 1) & 1, status, 369)) { ok = false; break; }
+      tc_fence_after();
+      float dv[C];
+      tmem_ld32(tDP + b * KT + lane_off + cb, dv);
+      tmem_wait_ld();
+      uint32_t pw[C / 2];
+#pragma unroll
+      for (int c = 0; c < C; c += 2)
+        pw[c / 2] = pack_bf16x2(sv[c] * (dv[c] - dl), sv[c + 1] * (dv[c + 1] - dl));
+      tmem_st16(tS + b * KT + lane_off + cb, pw);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.ds_full[b]);
+    }
+    // dQ (query row per lane): part p stores head dims [64 p, 64 p + 64)
+    if (ok && n > 0 && mbar_wait(B.dq_full, 0, status, 370)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = part * 64; c < part * 64 + 64; c += 32) {
+        float v[32];
+        tmem_ld32(tDQ + lane_off + c, v);
+        tmem_wait_ld();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(dq + (int64_t)s * dq_ss + h * HD + c);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            dst[u] = make_uint4(pack_bf16x2(v[8 * u] * scale, v[8 * u + 1] * scale),
+                                pack_bf16x2(v[8 * u + 2] * scale, v[8 * u + 3] * scale),
+                                pack_bf16x2(v[8 * u + 4] * scale, v[8 * u + 5] * scale),
+                                pack_bf16x2(v[8 * u + 6] * scale, v[8 * u + 7] * scale));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+int attn_bwd_q2_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
+                       int64_t k_ss, const void* v, int64_t v_ss, const void* dout, int64_t do_ss,
+                       const float* lse, const float* delta, void* dq, int64_t dq_ss,
+                       const PartGeom& g, int* status, cudaStream_t st) {
+  CUtensorMap tq, tk, tv, tdo;
+  int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, TQ);
+  if (!rc) rc = make_tmap_2d(&tk, k, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)k_ss * 2, 64, KT);
+  if (!rc) rc = make_tmap_2d(&tv, v, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)v_ss * 2, 64, KT);
+  if (!rc)
+    rc = make_tmap_2d(&tdo, dout, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)do_ss * 2, 64, TQ);
+  if (rc) return rc;
+  PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_q2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)SMEM_Q2));
+  dim3 grid((unsigned)Hq, (unsigned)((S + TQ - 1) / TQ));
+  attn_bwd_q2_kernel<<<grid, kThreads, SMEM_Q2, st>>>(tq, tk, tv, tdo, lse, delta,
+                                                      (__nv_bfloat16*)dq, dq_ss, g, Hq / Hkv,
+                                                      1.0f / sqrtf((float)HD), status);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
+}  // namespace pe

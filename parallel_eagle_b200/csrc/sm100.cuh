@@ -309,6 +309,84 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// ------------------------------------------------- register re-split ------
+// Per-warpgroup register budget change (all 4 warps of a warpgroup execute it).
+// The CTA's pool is what it launched with (threads x registers per thread), so
+// the decreases and increases of all warpgroups must sum to no more than that.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg count");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg count");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// ------------------------------------------------ packed fp32 (f32x2) -------
+// sm_100 executes these as one instruction per pair of lanes' worth of fp32
+// work, halving the issue slots of elementwise softmax arithmetic.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+      "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// max of three (one instruction on sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of finite x on the FMA pipe instead of the SFU (which the
+// softmax otherwise saturates at one exp per score).  Cody-Waite style range
+// reduction: n = round(x) through the 1.5 * 2^23 shifter, f = x - n in
+// [-1/2, 1/2]; 2^f from a degree-3 polynomial (a relative-error minimax fit on
+// that interval by Remez exchange, max relative error 7.5e-5 -- far below the
+// bf16 rounding of the probabilities it feeds; exp2_poly_fit.py derives the
+// coefficients); 2^n is added into the exponent field.  x is clamped to
+// >= -125 so the exponent never underflows (the result there, ~2^-125, stands
+// in for a probability that is 0 at any precision that follows).
+// Valid for x <= 127; x < -125 (including -inf) gives exactly 0, as the SFU's
+// flush-to-zero ex2 does below 2^-126.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kShift = 12582912.f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.055171669f;
+  const float2 t = add2(x, make_float2(kShift, kShift));   // n in the low mantissa bits
+  const float2 n = add2(t, make_float2(-kShift, -kShift));
+  const float2 f = fma2(n, make_float2(-1.f, -1.f), x);     // x - n
+  float2 p = fma2(make_float2(c3, c3), f, make_float2(c2, c2));
+  p = fma2(p, f, make_float2(c1, c1));
+  p = fma2(p, f, make_float2(c0, c0));
+  // bits(t) = bits(1.5 * 2^23) + n, and bits(1.5 * 2^23) << 23 vanishes mod 2^32
+  const float rx = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  const float ry = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  return make_float2(x.x < -125.f ? 0.f : rx, x.y < -125.f ? 0.f : ry);
+}
+
 // ---------------------------------------------------- smem descriptors ------
 // Shared-memory matrix descriptor for a 128-byte-swizzled tile (sm_100 format:
 // start>>4 in [0,14), LBO>>4 in [16,30), SBO>>4 in [32,46), version 1 in [46,48),

@@ -261,7 +261,9 @@ def test_attention_simt_all_layouts(dtype, layout_kind, geom):
 
 
 TC_GEOMS = [(0, 300, 5, 4, 2), (256, 512, 5, 4, 1), (100, 333, 3, 8, 2), (0, 130, 1, 4, 2),
-            (1500, 2048, 5, 2, 1), (0, 64, 8, 2, 2), (37, 41, 4, 4, 4)]
+            (1500, 2048, 5, 2, 1), (0, 64, 8, 2, 2), (37, 41, 4, 4, 4),
+            # 28 x 32 key-tile work items: several per CTA of the persistent dK/dV kernel
+            (256, 1024, 5, 28, 4)]
 
 
 def _qkv_view(S, nh, nkv, seed):
@@ -288,8 +290,9 @@ def test_attention_tcgen05_fwd_matches_simt(geom):
     assert torch.allclose(lse.cpu(), lse_ref.cpu(), atol=2e-3, rtol=1e-4)
 
 
+@pytest.mark.parametrize("variant", [0, 1, 2])
 @pytest.mark.parametrize("geom", TC_GEOMS)
-def test_attention_tcgen05_bwd_matches_simt(geom):
+def test_attention_tcgen05_bwd_matches_simt(geom, variant):
     a0, a1, k, nh, nkv = geom
     S = a1 + (a1 - a0) * (k - 1)
     q, kt, vt = _qkv_view(S, nh, nkv, seed=31)
@@ -301,7 +304,8 @@ def test_attention_tcgen05_bwd_matches_simt(geom):
     dqkv = torch.full((1, S, (nh + 2 * nkv) * 128), float("nan"), dtype=torch.bfloat16, device=DEV)
     cq, ckv = nh * 128, nkv * 128
     got = ops.attn_bwd(q, kt, vt, o, do, lse, nh, nkv, 128, lay, dq=dqkv[:, :, :cq],
-                       dk=dqkv[:, :, cq:cq + ckv], dv=dqkv[:, :, cq + ckv:], algo=L.ALGO_TCGEN05)
+                       dk=dqkv[:, :, cq:cq + ckv], dv=dqkv[:, :, cq + ckv:],
+                       algo=L.ALGO_TCGEN05 | (variant << 8))
     torch.cuda.synchronize()
     ops.check_status(DEV)
     for name, a, b in zip(("dq", "dk", "dv"), got, ref):
