@@ -517,7 +517,7 @@ def attention_roofline(c, dev, peak, src):
     run, flops, _ = attention_case(c, dev)
     ms = time_case(run, 5)
     achieved = flops / (ms / 1e3) / 1e12
-    return {"kernels": "attn_fwd_tc2_kernel + attn_bwd_q_kernel + attn_bwd_kv_kernel (+ prep/cast)",
+    return {"kernels": "attn_fwd_tc2_kernel + attn_bwd_q2_kernel + attn_bwd_kv2_kernel (+ prep/cast)",
             "segments": c["segments"], "ms_per_sequence": round(ms, 3),
             "tflops": round(achieved, 1), "peak": peak, "frac": round(achieved / peak, 4),
             "peak_source": f"{src} bf16_tflops (burst)", "flops_per_sequence": flops}
