@@ -16,12 +16,15 @@
 // MMAs of step j + 1 (and j + 2) run while the compute warps work on step j.
 // At the end dQ is scaled and stored in bf16 straight from TMEM.
 //
-// Warp roles (384 threads):
+// Warp roles (640 threads):
 //   warp 0      TMA: Q / dO tile once, K / V per step into 4- and 3-deep rings
 //   warp 1      tcgen05.mma issue:  dQ(j), S(j+2), dP(j+2) per step
 //   warps 2, 3  idle
-//   warps 4-11  compute: two per TMEM lane quarter, each owning 32 of the 64
-//               key columns; part 0 also copies Q, part 1 dO into TMEM
+//   warps 4-19  compute: four per TMEM lane quarter, each owning 16 of the 64
+//               key columns (four warps per scheduler hide the TMEM and SFU
+//               latency of a step); part p also copies one 64-column half of Q
+//               (p = 0, 1) or dO (p = 2, 3) into TMEM and stores 32 of dQ's 128
+//               head dims
 // TMEM: dQ 0..127, Q 128..191, dO 192..255 (bf16 pairs), S buffers 256 / 320,
 //       dP buffers 384 / 448.
 #include "attn_tc.cuh"
@@ -36,9 +39,10 @@ constexpr int KT = 64;                         // keys per step
 constexpr uint32_t SUB_BYTES = KT * HD * 2;     // 16 KB: 64 rows x 128 bf16
 constexpr uint32_t SUB_CHUNK = SUB_BYTES / 2;   // 8 KB: 64 rows x 128 B
 constexpr int KS = 4, VS = 3;                  // ring depths
-constexpr int kThreads = 384;
-constexpr int kComputeWarps = 8;
-constexpr int kCols = KT / 2;                  // key columns per compute warp
+constexpr int kComputeWarps = 16;              // four per TMEM lane quarter
+constexpr int kThreads = 128 + 32 * kComputeWarps;
+constexpr int kParts = kComputeWarps / 4;
+constexpr int kCols = KT / kParts;             // key columns per compute warp
 
 constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_DO = OFF_Q + TILE_BYTES;
@@ -233,22 +237,20 @@ attn_bwd_q2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
     const float scale_log2 = scale * kLog2e;
     bool ok = mbar_wait(B.qdo_full, 0, status, 367);
     if (ok) {
-      // Q (part 0) / dO (part 1) row -> TMEM as bf16 pairs (A operand)
-      const uint8_t* src = smem + (part == 0 ? OFF_Q : OFF_DO);
-      uint32_t r32[64];
+      // one 64-column half of the Q (parts 0, 1) or dO (parts 2, 3) row -> TMEM as
+      // bf16 pairs (A operand)
+      const int ch = part & 1;
+      const uint8_t* src = smem + (part < 2 ? OFF_Q : OFF_DO) + ch * CHUNK;
+      uint32_t r32[32];
 #pragma unroll
-      for (int ch = 0; ch < 2; ++ch)
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint4 x = *reinterpret_cast<const uint4*>(src + ch * CHUNK + swz(row, u));
-          r32[ch * 32 + u * 4 + 0] = x.x;
-          r32[ch * 32 + u * 4 + 1] = x.y;
-          r32[ch * 32 + u * 4 + 2] = x.z;
-          r32[ch * 32 + u * 4 + 3] = x.w;
-        }
-      const uint32_t dst = (part == 0 ? tQ : tDO) + lane_off;
-      tmem_st32(dst, r32);
-      tmem_st32(dst + 32, r32 + 32);
+      for (int u = 0; u < 8; ++u) {
+        const uint4 x = *reinterpret_cast<const uint4*>(src + swz(row, u));
+        r32[u * 4 + 0] = x.x;
+        r32[u * 4 + 1] = x.y;
+        r32[u * 4 + 2] = x.z;
+        r32[u * 4 + 3] = x.w;
+      }
+      tmem_st32((part < 2 ? tQ : tDO) + lane_off + ch * 32, r32);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -260,7 +262,7 @@ attn_bwd_q2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       if (!mbar_wait(&B.s_full[b], (j >> 1) & 1, status, 368)) { ok = false; break; }
       tc_fence_after();
       float sv[C];
-      tmem_ld32(tS + b * KT + lane_off + cb, sv);
+      tmem_ld16(tS + b * KT + lane_off + cb, sv);
       tmem_wait_ld();
       // P = 2^(S c - lse') (masked pairs exactly 0)
       if (k0 + C - 1 <= qi) {  // every key of this warp's slice is real and <= the anchor
@@ -277,23 +279,23 @@ attn_bwd_q2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       if (!mbar_wait(&B.dp_full[b], (j >> 1) & 1, status, 369)) { ok = false; break; }
       tc_fence_after();
       float dv[C];
-      tmem_ld32(tDP + b * KT + lane_off + cb, dv);
+      tmem_ld16(tDP + b * KT + lane_off + cb, dv);
       tmem_wait_ld();
       uint32_t pw[C / 2];
 #pragma unroll
       for (int c = 0; c < C; c += 2)
         pw[c / 2] = pack_bf16x2(sv[c] * (dv[c] - dl), sv[c + 1] * (dv[c + 1] - dl));
-      tmem_st16(tS + b * KT + lane_off + cb, pw);
+      tmem_st8(tS + b * KT + lane_off + cb, pw);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&B.ds_full[b]);
     }
-    // dQ (query row per lane): part p stores head dims [64 p, 64 p + 64)
+    // dQ (query row per lane): part p stores head dims [32 p, 32 p + 32)
     if (ok && n > 0 && mbar_wait(B.dq_full, 0, status, 370)) {
       tc_fence_after();
 #pragma unroll 1
-      for (int c = part * 64; c < part * 64 + 64; c += 32) {
+      for (int c = part * 32; c < part * 32 + 32; c += 32) {
         float v[32];
         tmem_ld32(tDQ + lane_off + c, v);
         tmem_wait_ld();
