@@ -24,16 +24,16 @@
 // The item's dK / dV tile is added (fp32) into the KV head's accumulators,
 // reducing the query heads of a GQA group without expanding K / V.
 //
-// Warp roles (384 threads):
+// Warp roles (640 threads):
 //   warp 0      scheduler + TMA: claims items; K per item (two buffers), V per
 //               item (one buffer, refilled once the compute warps copied it into
 //               TMEM); Q / dO per step into 4- and 3-deep rings
 //   warp 1      tcgen05.mma issue
 //   warp 2      per-query operands (lse * log2 e, delta, anchor, depth) per step
 //   warp 3      idle
-//   warps 4-11  compute: two per TMEM lane quarter, each owning 32 of the 64
-//               query columns; per item each copies its half of V into TMEM,
-//               and part 0 drains dK, part 1 dV
+//   warps 4-19  compute: four per TMEM lane quarter, each owning 16 of the 64
+//               query columns; per item each copies a quarter of the V row into
+//               TMEM, and parts 0 / 1 drain the two halves of dK, parts 2 / 3 of dV
 // TMEM: dK 0..127, dV 128..255, V 256..319 (bf16 pairs), S^T 320..383 /
 //       384..447, dP^T 448..511.
 #include "attn_tc.cuh"
@@ -48,9 +48,10 @@ constexpr int QT = 64;                          // queries per step
 constexpr uint32_t SUB_BYTES = QT * HD * 2;      // 16 KB: 64 rows x 128 bf16
 constexpr uint32_t SUB_CHUNK = SUB_BYTES / 2;    // 8 KB: 64 rows x 128 B
 constexpr int QS = 4, DS = 3, MS = 4;           // ring depths: Q, dO, per-query operands
-constexpr int kThreads = 384;
-constexpr int kComputeWarps = 8;
-constexpr int kCols = QT / 2;                   // query columns per compute warp
+constexpr int kComputeWarps = 16;               // four per TMEM lane quarter
+constexpr int kThreads = 128 + 32 * kComputeWarps;
+constexpr int kParts = kComputeWarps / 4;
+constexpr int kCols = QT / kParts;              // query columns per compute warp
 
 // shared memory (offsets from the 1024-aligned base)
 constexpr uint32_t OFF_K = 0;                        // [2] K tiles
@@ -384,20 +385,21 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     const int64_t kv_ld = (int64_t)Hkv * HD;
     bool ok = true;
     int gs = 0;
-    // the previous item's dK (part 0) / dV (part 1) row, drained after the next
+    // the previous item's dK (parts 0, 1) / dV (parts 2, 3) row, drained after the next
     // item's K / V copy so that item's first MMAs overlap the drain
     float* pending = nullptr;
     bool have_pending = false;
     auto drain = [&](int ic_prev) -> bool {
       if (!mbar_wait(B.acc_full, ic_prev & 1, status, 354)) return false;
       tc_fence_after();
-      const uint32_t src = (part == 0 ? tDK : tDV) + lane_off;
+      const int half = (part & 1) * (HD / 2);
+      const uint32_t src = (part < 2 ? tDK : tDV) + lane_off + half;
 #pragma unroll 1
-      for (int c0 = 0; c0 < HD; c0 += 32) {
+      for (int c0 = 0; c0 < HD / 2; c0 += 32) {
         float v[32];
         tmem_ld32(src + c0, v);
         tmem_wait_ld();
-        if (pending) atomic_add_row32(pending + c0, v, 1.f);
+        if (pending) atomic_add_row32(pending + half + c0, v, 1.f);
       }
       return true;
     };
@@ -410,29 +412,30 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       const bool kvalid = kj < g.S;
       int ka = 0, ke = 0;
       if (kvalid) decode(g, kj, ka, ke);
-      // ---- this warp's half of the V row (head dims [64 part, 64 part + 64)):
+      // ---- this warp's quarter of the V row (head dims [32 part, 32 part + 32)):
       // shared memory -> TMEM, after the previous item's MMAs (which read the TMEM
       // copy) all completed ----
       if (have_pending && !mbar_wait(B.acc_full, (ic - 1) & 1, status, 355)) { ok = false; break; }
       if (!mbar_wait(B.v_full, ic & 1, status, 356)) { ok = false; break; }
       {
-        uint32_t r32[32];
+        uint32_t r16[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint4 x = *reinterpret_cast<const uint4*>(sV + part * CHUNK + swz(row, u));
-          r32[u * 4 + 0] = x.x;
-          r32[u * 4 + 1] = x.y;
-          r32[u * 4 + 2] = x.z;
-          r32[u * 4 + 3] = x.w;
+        for (int u = 0; u < 4; ++u) {
+          const uint4 x = *reinterpret_cast<const uint4*>(sV + (part >> 1) * CHUNK +
+                                                          swz(row, (part & 1) * 4 + u));
+          r16[u * 4 + 0] = x.x;
+          r16[u * 4 + 1] = x.y;
+          r16[u * 4 + 2] = x.z;
+          r16[u * 4 + 3] = x.w;
         }
-        tmem_st32(tV + lane_off + part * 32, r32);
+        tmem_st16(tV + lane_off + part * 16, r16);
         tmem_wait_st();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(B.v_copied);
       if (have_pending && !drain(ic - 1)) { ok = false; break; }
-      pending = kvalid ? (part == 0 ? dk_acc : dv_acc) + (int64_t)kj * kv_ld + it.kvh * HD : nullptr;
+      pending = kvalid ? (part < 2 ? dk_acc : dv_acc) + (int64_t)kj * kv_ld + it.kvh * HD : nullptr;
       have_pending = true;
       for (int i = 0; i < it.n; ++i) {
         const int gi = gs + i, slot = gi % MS, b = gi & 1;
@@ -443,7 +446,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
         if (!mbar_wait(&B.st_full[b], (gi >> 1) & 1, status, 352)) { ok = false; break; }
         tc_fence_after();
         float pv[C];
-        tmem_ld32(tS + b * QT + lane_off + cb, pv);
+        tmem_ld16(tS + b * QT + lane_off + cb, pv);
         tmem_wait_ld();
         const float* L = sL + slot * QT + cb;
         if (full) {
@@ -470,7 +473,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           uint32_t pw[C / 2];
 #pragma unroll
           for (int c = 0; c < C; c += 2) pw[c / 2] = pack_bf16x2(pv[c], pv[c + 1]);
-          tmem_st16(tS + b * QT + lane_off + cb, pw);
+          tmem_st8(tS + b * QT + lane_off + cb, pw);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -480,7 +483,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
         if (!mbar_wait(B.dpt_full, gi & 1, status, 353)) { ok = false; break; }
         tc_fence_after();
         float dv[C];
-        tmem_ld32(tDP + lane_off + cb, dv);
+        tmem_ld16(tDP + lane_off + cb, dv);
         tmem_wait_ld();
         const float* D = sD + slot * QT + cb;
         {
@@ -492,7 +495,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
             pw[c / 2 + 1] =
                 pack_bf16x2(pv[c + 2] * (dv[c + 2] - d4.z), pv[c + 3] * (dv[c + 3] - d4.w));
           }
-          tmem_st16(tDP + lane_off + cb, pw);
+          tmem_st8(tDP + lane_off + cb, pw);
         }
         tmem_wait_st();
         tc_fence_before();
