@@ -384,27 +384,27 @@ def gemm_case(c, dev):
 
 
 def attention_case(c, dev):
-    """Masked-attention fwd+bwd over the S segments of one config-2 sequence.
+    """Masked-attention fwd+bwd over the S segments of one config-2 sequence, stacked
+    in one row space and run by one call each way (as the step engine does).
     FLOPs = 12 * hd * Hq * allowed pairs (no recompute)."""
-    from parallel_eagle_b200 import _lib, ops
+    from parallel_eagle_b200 import ops
     from parallel_eagle_b200.engine import segment_bounds
 
     nh, nkv, hd, k = c["n_heads"], c["n_kv_heads"], c["hidden"] // c["n_heads"], c["max_depth"]
     cols = (nh + 2 * nkv) * hd
     g = torch.Generator(device=dev).manual_seed(11)
-    segs = []
-    for a0, a1 in segment_bounds(c["n"], c["segments"]):
-        S = a1 + (a1 - a0) * (k - 1)
-        qkv = torch.randn(1, S, cols, generator=g, device=dev).to(torch.bfloat16)
-        do = torch.randn(1, S, nh * hd, generator=g, device=dev).to(torch.bfloat16)
-        lay = ops.AttnLayout(_lib.LAYOUT_PARTITION, a0=a0, a1=a1, k=k)
-        segs.append((qkv, do, lay))
+    bounds = segment_bounds(c["n"], c["segments"])
+    R = sum(ops.segment_rows(bounds, k))
+    qkv = torch.randn(R, cols, generator=g, device=dev).to(torch.bfloat16)
+    do = torch.randn(R, nh * hd, generator=g, device=dev).to(torch.bfloat16)
+    q, kk, vv = qkv[:, : nh * hd], qkv[:, nh * hd:(nh + nkv) * hd], qkv[:, (nh + nkv) * hd:]
+    dqkv = torch.empty_like(qkv)
 
     def run():
-        for qkv, do, lay in segs:
-            q, kk, vv = qkv[:, :, : nh * hd], qkv[:, :, nh * hd:(nh + nkv) * hd], qkv[:, :, (nh + nkv) * hd:]
-            o, lse = ops.attn_fwd(q, kk, vv, nh, nkv, hd, lay)
-            ops.attn_bwd(q, kk, vv, o, do, lse, nh, nkv, hd, lay)
+        o, lse = ops.attn_fwd_segments(q, kk, vv, nh, nkv, hd, bounds, k)
+        ops.attn_bwd_segments(q, kk, vv, o, do, lse, nh, nkv, hd, bounds, k,
+                              dq=dqkv[:, : nh * hd], dk=dqkv[:, nh * hd:(nh + nkv) * hd],
+                              dv=dqkv[:, (nh + nkv) * hd:])
 
     return run, 12.0 * hd * nh * attention_pairs(c["n"], k, c["segments"]), None
 

@@ -143,6 +143,36 @@ int pe_attn_bwd(int dtype, int64_t B, int64_t S, int Hq, int Hkv, int head_dim,
                 int64_t bias_sb, int64_t bias_sq, int algo, int32_t* status, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Masked attention over all segments of one sequence in one call (partition
+ * layout).  Segment s spans anchors [a0, a1) = (bounds[2s], bounds[2s + 1]) and
+ * has S_s = a1 + (a1 - a0)(kdepth - 1) slots, stored in rows
+ * [row0_s, row0_s + S_s) of every row operand with row0_0 = 0 and
+ * row0_{s+1} = row0_s + S_s (the segments stacked one after another).  lse
+ * (and the backward's deltas) hold one [Hq, S_s] fp32 block per segment,
+ * starting at element Hq * row0_s.  On the tensor-core path one launch per
+ * kernel covers every segment (the largest segment's units first, heaviest
+ * first within a segment, so a segment's tail overlaps the next segment's
+ * start); otherwise the segments run one after another.  Kernel-variant bits
+ * are not accepted here.  Results equal per-segment pe_attn_fwd / pe_attn_bwd
+ * calls.  Replaces the per-segment attention of reference
+ * src/pe/partition.py:86-117 (one ParallelDrafter.forward / backward per
+ * segment, each reaching src/pe/nn.py:71-89).
+ * ------------------------------------------------------------------------- */
+int pe_attn_fwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth, int Hq,
+                         int Hkv, int head_dim, const void* q, int64_t q_ss, const void* k,
+                         int64_t k_ss, const void* v, int64_t v_ss, void* o, int64_t o_ss,
+                         float* lse, int algo, int32_t* status, void* stream);
+size_t pe_attn_bwd_segments_workspace(int dtype, int nseg, const int64_t* bounds, int kdepth,
+                                      int Hq, int Hkv, int head_dim);
+int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth, int Hq,
+                         int Hkv, int head_dim, const void* q, int64_t q_ss, const void* k,
+                         int64_t k_ss, const void* v, int64_t v_ss, const void* o,
+                         int64_t o_ss, const void* dout, int64_t do_ss, const float* lse,
+                         void* dq, int64_t dq_ss, void* dk, int64_t dk_ss, void* dv,
+                         int64_t dv_ss, void* workspace, size_t workspace_bytes, int algo,
+                         int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Frozen shared LM head fused with the loss and its input gradient, chunked
  * over the vocabulary: logits for the whole vocabulary are never stored.
  *   z = h W^T (rounded to dtype), loss_r = lse(z_r) - z_r[label_r]

@@ -53,6 +53,17 @@ SIGNATURES: dict[str, tuple] = {
          _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
          _i64, _vp, _sz, _int, _i64, _i64, _int, _vp, _vp, _vp, _i64, _i64, _int, _vp, _vp],
     ),
+    "pe_attn_fwd_segments": (
+        _int,
+        [_int, _int, _vp, _int, _int, _int, _int, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64,
+         _vp, _int, _vp, _vp],
+    ),
+    "pe_attn_bwd_segments_workspace": (_sz, [_int, _int, _vp, _int, _int, _int, _int]),
+    "pe_attn_bwd_segments": (
+        _int,
+        [_int, _int, _vp, _int, _int, _int, _int, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64,
+         _vp, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _sz, _int, _vp, _vp],
+    ),
     "pe_lmhead_ce_workspace": (_sz, [_int, _i64, _i64, _i64, _int]),
     "pe_lmhead_ce": (
         _int,

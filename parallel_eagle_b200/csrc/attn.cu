@@ -1,5 +1,7 @@
 // Attention entry points: argument checks and dispatch between the tensor-core
 // kernels (bf16, head_dim 128, partition layout) and the CUDA-core kernels.
+#include <vector>
+
 #include "attn.cuh"
 
 namespace pe {
@@ -105,4 +107,139 @@ extern "C" size_t pe_attn_bwd_workspace(int dtype, int64_t B, int64_t S, int Hq,
   if (dtype == PE_BF16 && B == 1 && head_dim == 128)
     bytes += align256(attn_tc_bwd_acc_bytes(S, Hq, Hkv));
   return bytes;
+}
+
+// ------------------------------------------------------ stacked segments ----
+
+namespace pe {
+
+// geometry of the stacked segments; false (with the error set) on a bad table
+static bool seg_geoms(int nseg, const int64_t* bounds, int kdepth,
+                      std::vector<attn_tc::PartGeom>& g, int64_t& rows) {
+  if (nseg < 1 || !bounds || kdepth < 1) {
+    set_error("attention segments: need nseg >= 1, bounds and kdepth >= 1");
+    return false;
+  }
+  g.resize(nseg);
+  rows = 0;
+  for (int s = 0; s < nseg; ++s) {
+    const int64_t a0 = bounds[2 * s], a1 = bounds[2 * s + 1];
+    const int64_t S = a1 + (a1 - a0) * (kdepth - 1);
+    if (!(0 <= a0 && a0 < a1) || S > 65535ll * 128) {
+      set_error("attention segments: bad segment %d (a0 %lld, a1 %lld)", s, (long long)a0,
+                (long long)a1);
+      return false;
+    }
+    g[s] = attn_tc::PartGeom{(int)S, (int)a0, (int)a1, kdepth - 1};
+    rows += S;
+  }
+  return true;
+}
+
+static size_t elem_bytes(int dtype) { return dtype == PE_F32 ? 4 : 2; }
+
+static size_t seg_workspace(int dtype, int64_t rows, int Hq, int Hkv, int head_dim) {
+  size_t bytes = align256((size_t)Hq * rows * 4);  // deltas
+  if (dtype == PE_BF16 && head_dim == 128) bytes += align256(attn_tc_seg_acc_bytes(rows, Hkv));
+  return bytes;
+}
+
+}  // namespace pe
+
+extern "C" int pe_attn_fwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth,
+                                    int Hq, int Hkv, int head_dim, const void* q, int64_t q_ss,
+                                    const void* k, int64_t k_ss, const void* v, int64_t v_ss,
+                                    void* o, int64_t o_ss, float* lse, int algo,
+                                    int32_t* status, void* stream) {
+  std::vector<attn_tc::PartGeom> g;
+  int64_t rows = 0;
+  if (!seg_geoms(nseg, bounds, kdepth, g, rows)) return PE_ERR_ARG;
+  PE_CHECK_ARG(Hq >= 1 && Hkv >= 1 && head_dim >= 1 && Hq % Hkv == 0 && Hq <= 65535,
+               "attention segments: bad head counts");
+  PE_CHECK_ARG((algo >> 8) == 0, "attention segments: kernel-variant bits are not accepted");
+  bool tc = true;
+  for (int s = 0; s < nseg; ++s)
+    tc = tc && attn_tc_eligible(dtype, 1, g[s].S, Hq, Hkv, head_dim, PE_LAYOUT_PARTITION, q, q_ss,
+                                k, k_ss, v, v_ss);
+  if (algo == PE_ALGO_TCGEN05) PE_CHECK_ARG(tc, "attention: inputs not eligible for tcgen05");
+  if (tc && algo != PE_ALGO_SIMT)
+    return attn_fwd_tc_segments(nseg, g.data(), Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, lse,
+                                status, as_stream(stream));
+  PE_CHECK_ARG(dtype == PE_F32 || dtype == PE_BF16, "attention segments: unknown dtype %d", dtype);
+  const size_t es = elem_bytes(dtype);
+  int64_t row0 = 0;
+  for (int s = 0; s < nseg; ++s) {
+    const int64_t S = g[s].S;
+    MaskSpec m{PE_LAYOUT_PARTITION, g[s].a0, g[s].a1, kdepth, nullptr, nullptr, nullptr, 0, 0};
+    const int rc = attn_fwd_simt_launch(
+        dtype, 1, S, Hq, Hkv, head_dim, static_cast<const uint8_t*>(q) + row0 * q_ss * es, 0,
+        q_ss, static_cast<const uint8_t*>(k) + row0 * k_ss * es, 0, k_ss,
+        static_cast<const uint8_t*>(v) + row0 * v_ss * es, 0, v_ss,
+        static_cast<uint8_t*>(o) + row0 * o_ss * es, 0, o_ss, lse + Hq * row0, m,
+        as_stream(stream));
+    if (rc) return rc;
+    row0 += S;
+  }
+  return PE_OK;
+}
+
+extern "C" size_t pe_attn_bwd_segments_workspace(int dtype, int nseg, const int64_t* bounds,
+                                                 int kdepth, int Hq, int Hkv, int head_dim) {
+  std::vector<attn_tc::PartGeom> g;
+  int64_t rows = 0;
+  if (Hq <= 0 || Hkv <= 0 || head_dim <= 0 || !seg_geoms(nseg, bounds, kdepth, g, rows)) return 0;
+  return seg_workspace(dtype, rows, Hq, Hkv, head_dim);
+}
+
+extern "C" int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth,
+                                    int Hq, int Hkv, int head_dim, const void* q, int64_t q_ss,
+                                    const void* k, int64_t k_ss, const void* v, int64_t v_ss,
+                                    const void* o, int64_t o_ss, const void* dout,
+                                    int64_t do_ss, const float* lse, void* dq, int64_t dq_ss,
+                                    void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
+                                    void* workspace, size_t workspace_bytes, int algo,
+                                    int32_t* status, void* stream) {
+  std::vector<attn_tc::PartGeom> g;
+  int64_t rows = 0;
+  if (!seg_geoms(nseg, bounds, kdepth, g, rows)) return PE_ERR_ARG;
+  PE_CHECK_ARG(Hq >= 1 && Hkv >= 1 && head_dim >= 1 && Hq % Hkv == 0 && Hq <= 65535,
+               "attention segments: bad head counts");
+  PE_CHECK_ARG((algo >> 8) == 0, "attention segments: kernel-variant bits are not accepted");
+  const size_t delta_bytes = align256((size_t)Hq * rows * 4);
+  PE_CHECK_ARG(workspace && workspace_bytes >= delta_bytes,
+               "attention backward: workspace too small (see pe_attn_bwd_segments_workspace)");
+  float* delta = static_cast<float*>(workspace);
+  bool tc = attn_tc_bwd_ready() &&
+            workspace_bytes >= delta_bytes + attn_tc_seg_acc_bytes(rows, Hkv);
+  for (int s = 0; s < nseg; ++s)
+    tc = tc && attn_tc_eligible(dtype, 1, g[s].S, Hq, Hkv, head_dim, PE_LAYOUT_PARTITION, q, q_ss,
+                                k, k_ss, v, v_ss);
+  if (algo == PE_ALGO_TCGEN05) PE_CHECK_ARG(tc, "attention: inputs not eligible for tcgen05");
+  if (tc && algo != PE_ALGO_SIMT) {
+    float* acc = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + delta_bytes);
+    return attn_bwd_tc_segments(nseg, g.data(), Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, dout,
+                                do_ss, lse, dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, acc, status,
+                                as_stream(stream));
+  }
+  PE_CHECK_ARG(dtype == PE_F32 || dtype == PE_BF16, "attention segments: unknown dtype %d", dtype);
+  const size_t es = elem_bytes(dtype);
+  auto at = [es](const void* p, int64_t row, int64_t ss) {
+    return static_cast<const uint8_t*>(p) + row * ss * es;
+  };
+  auto at_mut = [es](void* p, int64_t row, int64_t ss) {
+    return static_cast<uint8_t*>(p) + row * ss * es;
+  };
+  int64_t row0 = 0;
+  for (int s = 0; s < nseg; ++s) {
+    const int64_t S = g[s].S;
+    MaskSpec m{PE_LAYOUT_PARTITION, g[s].a0, g[s].a1, kdepth, nullptr, nullptr, nullptr, 0, 0};
+    const int rc = attn_bwd_simt_launch(
+        dtype, 1, S, Hq, Hkv, head_dim, at(q, row0, q_ss), 0, q_ss, at(k, row0, k_ss), 0, k_ss,
+        at(v, row0, v_ss), 0, v_ss, at(o, row0, o_ss), 0, o_ss, at(dout, row0, do_ss), 0, do_ss,
+        lse + Hq * row0, at_mut(dq, row0, dq_ss), 0, dq_ss, at_mut(dk, row0, dk_ss), 0, dk_ss,
+        at_mut(dv, row0, dv_ss), 0, dv_ss, delta + Hq * row0, m, as_stream(stream));
+    if (rc) return rc;
+    row0 += S;
+  }
+  return PE_OK;
 }

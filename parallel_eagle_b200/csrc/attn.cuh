@@ -10,6 +10,13 @@
 
 namespace pe {
 
+namespace attn_tc {
+// one segment of the partition layout: S = a1 + (a1 - a0) * km1 slots
+struct PartGeom {
+  int S, a0, a1, km1;  // km1 = K - 1 (0 when K == 1)
+};
+}  // namespace attn_tc
+
 struct MaskSpec {
   int layout;
   int64_t a0, a1;
@@ -69,5 +76,19 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
                        int64_t dq_ss, void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
                        float* delta, float* dq_acc, const MaskSpec& m, int* status,
                        cudaStream_t st, int variant = 0);
+// Stacked segments (tensor cores): segment s occupies rows [row0_s, row0_s + g[s].S)
+// of every row operand, row0_0 = 0 and row0_{s+1} = row0_s + g[s].S; lse / delta hold
+// one [Hq, g[s].S] block per segment starting at element Hq * row0_s.
+int attn_fwd_tc_segments(int nseg, const attn_tc::PartGeom* g, int Hq, int Hkv, const void* q,
+                         int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
+                         void* o, int64_t o_ss, float* lse, int* status, cudaStream_t st);
+// acc: fp32 dK / dV accumulators and the work counter, attn_tc_seg_acc_bytes(rows)
+size_t attn_tc_seg_acc_bytes(int64_t rows, int Hkv);
+int attn_bwd_tc_segments(int nseg, const attn_tc::PartGeom* g, int Hq, int Hkv, const void* q,
+                         int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
+                         const void* o, int64_t o_ss, const void* dout, int64_t do_ss,
+                         const float* lse, void* dq, int64_t dq_ss, void* dk, int64_t dk_ss,
+                         void* dv, int64_t dv_ss, float* delta, float* acc, int* status,
+                         cudaStream_t st);
 
 }  // namespace pe

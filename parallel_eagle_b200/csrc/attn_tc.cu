@@ -370,10 +370,9 @@ struct PairTiles {
 };
 
 __global__ void __launch_bounds__(kThreads2, 1)
-attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
-                    int64_t o_ss, float* __restrict__ lse, PartGeom g, int Hq, int rep,
-                    float scale_log2, int* status) {
+attn_fwd_tc2_kernel(const __grid_constant__ SegTable tab, __nv_bfloat16* __restrict__ O,
+                    int64_t o_ss, float* __restrict__ lse, int Hq, int rep, float scale_log2,
+                    int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -389,10 +388,22 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_pairs = (g.S + 2 * TQ - 1) / (2 * TQ);
-  // grid (head, pair): blocks dispatch head-fastest, so the heaviest pairs of every
-  // head start first
-  const int pr = num_pairs - 1 - (int)blockIdx.y;
+  // grid (head, unit): blocks dispatch head-fastest, so the heaviest pairs of every
+  // head start first -- stacked segments in the work list's order, a lone segment
+  // from its last pair down
+  int sg, pr;
+  if (tab.nwork > 0) {
+    unpack_work(tab.work[blockIdx.y], sg, pr);
+  } else {
+    sg = 0;
+    pr = (tab.g[0].S + 2 * TQ - 1) / (2 * TQ) - 1 - (int)blockIdx.y;
+  }
+  const PartGeom g = tab.g[sg];
+  const CUtensorMap* tmQ = &tab.tm[sg][0];
+  const CUtensorMap* tmK = &tab.tm[sg][1];
+  const CUtensorMap* tmV = &tab.tm[sg][2];
+  O += (int64_t)tab.row0[sg] * o_ss;
+  lse += (int64_t)Hq * tab.row0[sg];
   const int h = blockIdx.x;
   const int kvh = h / rep;
   const int q0 = pr * 2 * TQ;
@@ -434,8 +445,8 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
         mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
-          tma_load_2d(sQ + t * TILE_BYTES, &tmQ, q_full, h * HD, q0 + t * TQ);
-          tma_load_2d(sQ + t * TILE_BYTES + CHUNK, &tmQ, q_full, h * HD + 64, q0 + t * TQ);
+          tma_load_2d(sQ + t * TILE_BYTES, tmQ, q_full, h * HD, q0 + t * TQ);
+          tma_load_2d(sQ + t * TILE_BYTES + CHUNK, tmQ, q_full, h * HD + 64, q0 + t * TQ);
         }
         int j = 0;
         for (int kt = 0; kt >= 0 && ok; kt = pt.next(kt), ++j) {
@@ -446,10 +457,10 @@ attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           uint8_t* k_dst = sKV + st * 2 * TILE_BYTES;
           uint8_t* v_dst = k_dst + TILE_BYTES;
           mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
-          tma_load_2d(k_dst, &tmK, &kv_full[st], kvh * HD, k0);
-          tma_load_2d(k_dst + CHUNK, &tmK, &kv_full[st], kvh * HD + 64, k0);
-          tma_load_2d(v_dst, &tmV, &kv_full[st], kvh * HD, k0);
-          tma_load_2d(v_dst + CHUNK, &tmV, &kv_full[st], kvh * HD + 64, k0);
+          tma_load_2d(k_dst, tmK, &kv_full[st], kvh * HD, k0);
+          tma_load_2d(k_dst + CHUNK, tmK, &kv_full[st], kvh * HD + 64, k0);
+          tma_load_2d(v_dst, tmV, &kv_full[st], kvh * HD, k0);
+          tma_load_2d(v_dst + CHUNK, tmV, &kv_full[st], kvh * HD + 64, k0);
           last_st = st;
           last_ph = ph;
         }
@@ -675,14 +686,14 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
                        int64_t k_ss, const void* v, int64_t v_ss, void* o, int64_t o_ss,
                        float* lse, const MaskSpec& m, int* status, cudaStream_t st, int variant) {
   PE_CHECK_ARG(o_ss % 8 == 0 && al16(o), "attention (tcgen05): output must be 16-byte aligned");
-  CUtensorMap tq, tk, tv;
-  int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, TQ);
-  if (!rc) rc = make_tmap_2d(&tk, k, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)k_ss * 2, 64, TK);
-  if (!rc) rc = make_tmap_2d(&tv, v, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)v_ss * 2, 64, TK);
-  if (rc) return rc;
   PartGeom g{(int)S, (int)m.a0, (int)m.a1, m.kd - 1};
-  const float scale_log2 = kLog2e / sqrtf((float)HD);
   if (variant == 1) {
+    CUtensorMap tq, tk, tv;
+    int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, TQ);
+    if (!rc) rc = make_tmap_2d(&tk, k, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)k_ss * 2, 64, TK);
+    if (!rc) rc = make_tmap_2d(&tv, v, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)v_ss * 2, 64, TK);
+    if (rc) return rc;
+    const float scale_log2 = kLog2e / sqrtf((float)HD);
     PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_FWD));
     dim3 grid((unsigned)Hq, (unsigned)((S + TQ - 1) / TQ));
@@ -691,6 +702,13 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
     PE_LAUNCHED();
     return PE_OK;
   }
+  return attn_fwd_tc_segments(1, &g, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, lse, status, st);
+}
+
+int attn_fwd_tc_segments(int nseg, const PartGeom* g, int Hq, int Hkv, const void* q,
+                         int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
+                         void* o, int64_t o_ss, float* lse, int* status, cudaStream_t st) {
+  PE_CHECK_ARG(o_ss % 8 == 0 && al16(o), "attention (tcgen05): output must be 16-byte aligned");
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc2_kernel,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_FWD2));
   {
@@ -701,10 +719,48 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
     PE_CHECK_ARG(fa.numRegs * kThreads2 >= 4 * 32 * kRegsLow + 8 * 32 * kRegsHigh,
                  "attention (tcgen05): forward kernel compiled with too few registers");
   }
-  dim3 grid((unsigned)Hq, (unsigned)((S + 2 * TQ - 1) / (2 * TQ)));
-  attn_fwd_tc2_kernel<<<grid, kThreads2, SMEM_FWD2, st>>>(tq, tk, tv, (__nv_bfloat16*)o, o_ss, lse,
-                                                         g, Hq, Hq / Hkv, scale_log2, status);
-  PE_LAUNCHED();
+  const float scale_log2 = kLog2e / sqrtf((float)HD);
+  // a unit is a pair of query tiles; its cost the key tiles both tiles visit
+  auto units = [](const PartGeom& sg) { return (sg.S + 2 * TQ - 1) / (2 * TQ); };
+  auto cost = [](const PartGeom& sg, int pr) {
+    int c = 0;
+    for (int t = 0; t < 2; ++t) {
+      const int q0 = (2 * pr + t) * TQ;
+      if (q0 >= sg.S) break;
+      int r_end, m_beg, m_end;
+      key_tiles(sg, q0, r_end, m_beg, m_end, TK);
+      c += r_end + (m_end - m_beg);
+    }
+    return c;
+  };
+  std::vector<int64_t> rows(nseg + 1, 0);  // first stacked row of every segment
+  for (int s = 0; s < nseg; ++s) rows[s + 1] = rows[s] + g[s].S;
+  for (auto [b, e] : seg_groups(nseg, g)) {
+    SegTable tab;
+    memset(&tab, 0, sizeof(tab));
+    tab.nseg = e - b;
+    int max_units = 0;
+    for (int s = b; s < e; ++s) {
+      const int i = s - b;
+      PE_CHECK_ARG(rows[s] - rows[b] < (1ll << 31), "attention: stacked rows exceed int range");
+      tab.g[i] = g[s];
+      tab.row0[i] = (int)(rows[s] - rows[b]);
+      int rc = seg_map(&tab.tm[i][0], q, rows[s], q_ss, (int64_t)Hq * HD, g[s].S, TQ);
+      if (!rc) rc = seg_map(&tab.tm[i][1], k, rows[s], k_ss, (int64_t)Hkv * HD, g[s].S, TK);
+      if (!rc) rc = seg_map(&tab.tm[i][2], v, rows[s], v_ss, (int64_t)Hkv * HD, g[s].S, TK);
+      if (rc) return rc;
+      max_units = std::max(max_units, units(g[s]));
+    }
+    int rc = seg_table_order(tab, units, cost);
+    if (rc) return rc;
+    const int ny = tab.nwork > 0 ? tab.nwork : max_units;
+    PE_CHECK_ARG(ny <= 65535, "attention: too many query tiles for one launch");
+    dim3 grid((unsigned)Hq, (unsigned)ny);
+    __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(o) + rows[b] * o_ss;
+    attn_fwd_tc2_kernel<<<grid, kThreads2, SMEM_FWD2, st>>>(tab, ob, o_ss, lse + (int64_t)Hq * rows[b],
+                                                           Hq, Hq / Hkv, scale_log2, status);
+    PE_LAUNCHED();
+  }
   return PE_OK;
 }
 

@@ -869,35 +869,58 @@ attn_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
 }
 
-// delta[h, s] = sum_d dO * O (fp32); zero the dQ accumulator row (when given) and, for the
-// first Hkv heads, the dK / dV accumulator rows; zero the work counter
-__global__ void attn_bwd_prep_kernel(int S, int Hq, int Hkv, const __nv_bfloat16* __restrict__ o,
-                                     int64_t o_ss, const __nv_bfloat16* __restrict__ dout,
-                                     int64_t do_ss, float* __restrict__ delta,
-                                     float* __restrict__ dq_acc, float* __restrict__ dk_acc,
-                                     float* __restrict__ dv_acc, int* __restrict__ counter) {
+// first stacked row of each segment of a launch group (row0[n] = total rows)
+struct SegRows {
+  int n;
+  int row0[kMaxSeg + 1];
+};
+
+// delta (fp32, one [Hq, S_seg] block per segment at element Hq * row0_seg) =
+// sum_d dO * O per (stacked row, head); zero the dQ accumulator row (when given) and,
+// for the first Hkv heads, the dK / dV accumulator rows; zero the work counter.
+// Sixteen threads per (row, head), each reading 16 bytes of O and of dO.
+__global__ void attn_bwd_prep_kernel(const __grid_constant__ SegRows sr, int Hq, int Hkv,
+                                     const __nv_bfloat16* __restrict__ o, int64_t o_ss,
+                                     const __nv_bfloat16* __restrict__ dout, int64_t do_ss,
+                                     float* __restrict__ delta, float* __restrict__ dq_acc,
+                                     float* __restrict__ dk_acc, float* __restrict__ dv_acc,
+                                     int* __restrict__ counter) {
   if (blockIdx.x == 0 && threadIdx.x == 0) *counter = 0;
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= S * Hq) return;
-  const int s = w / Hq, h = w - (w / Hq) * Hq;
-  const uint2 a = *reinterpret_cast<const uint2*>(o + (int64_t)s * o_ss + h * HD + lane * 4);
-  const uint2 b = *reinterpret_cast<const uint2*>(dout + (int64_t)s * do_ss + h * HD + lane * 4);
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t pair = t >> 4;  // (stacked row, head), heads fastest
+  const int sub = threadIdx.x & 15;
+  if (pair >= (int64_t)sr.row0[sr.n] * Hq) return;
+  const int s = (int)(pair / Hq), h = (int)(pair - (int64_t)s * Hq);
+  int sg = 0;
+  while (sg + 1 < sr.n && s >= sr.row0[sg + 1]) ++sg;
+  const int r0 = sr.row0[sg], S = sr.row0[sg + 1] - r0;
+  const uint4 a = *reinterpret_cast<const uint4*>(o + (int64_t)s * o_ss + h * HD + sub * 8);
+  const uint4 b = *reinterpret_cast<const uint4*>(dout + (int64_t)s * do_ss + h * HD + sub * 8);
   const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
   const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
   float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
+  for (int i = 0; i < 4; ++i) {
     const float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(b2[i]);
-    acc += x.x * y.x + x.y * y.y;
+    acc = fmaf(x.x, y.x, acc);
+    acc = fmaf(x.y, y.y, acc);
   }
-  acc = warp_sum(acc);
-  if (lane == 0) delta[(int64_t)h * S + s] = acc;
+#pragma unroll
+  for (int m = 8; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+  if (sub == 0) delta[(int64_t)Hq * r0 + (int64_t)h * S + (s - r0)] = acc;
   const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (dq_acc) reinterpret_cast<float4*>(dq_acc + (int64_t)s * Hq * HD + h * HD)[lane] = z;
+  if (dq_acc) {
+    float4* d = reinterpret_cast<float4*>(dq_acc + (int64_t)s * Hq * HD + h * HD) + sub * 2;
+    d[0] = z;
+    d[1] = z;
+  }
   if (h < Hkv) {
-    reinterpret_cast<float4*>(dk_acc + (int64_t)s * Hkv * HD + h * HD)[lane] = z;
-    reinterpret_cast<float4*>(dv_acc + (int64_t)s * Hkv * HD + h * HD)[lane] = z;
+    float4* dk4 = reinterpret_cast<float4*>(dk_acc + (int64_t)s * Hkv * HD + h * HD) + sub * 2;
+    float4* dv4 = reinterpret_cast<float4*>(dv_acc + (int64_t)s * Hkv * HD + h * HD) + sub * 2;
+    dk4[0] = z;
+    dk4[1] = z;
+    dv4[0] = z;
+    dv4[1] = z;
   }
 }
 
@@ -957,21 +980,23 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   float* dk_acc = dq_acc + (int64_t)S * Hq * HD;
   float* dv_acc = dk_acc + (int64_t)S * Hkv * HD;
   int* counter = reinterpret_cast<int*>(dv_acc + (int64_t)S * Hkv * HD);
+  PartGeom g{Si, (int)m.a0, (int)m.a1, m.kd - 1};
+  if (variant == 0)
+    return attn_bwd_tc_segments(1, &g, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, dout, do_ss,
+                                lse, dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, dk_acc, status, st);
   {
-    const int warps = Si * Hq;
-    attn_bwd_prep_kernel<<<(warps + 7) / 8, 256, 0, st>>>(
-        Si, Hq, Hkv, (const __nv_bfloat16*)o, o_ss, (const __nv_bfloat16*)dout, do_ss, delta,
+    SegRows sr{};
+    sr.n = 1;
+    sr.row0[1] = Si;
+    const int64_t threads = (int64_t)Si * Hq * 16;
+    attn_bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+        sr, Hq, Hkv, (const __nv_bfloat16*)o, o_ss, (const __nv_bfloat16*)dout, do_ss, delta,
         variant == 1 ? dq_acc : nullptr, dk_acc, dv_acc, counter);
     PE_LAUNCHED();
   }
-  PartGeom g{Si, (int)m.a0, (int)m.a1, m.kd - 1};
   const float scale = 1.0f / sqrtf((float)HD);
-  if (variant == 0 || variant == 2) {
-    if (variant == 0) {
-      rc = attn_bwd_q2_launch(S, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, dout, do_ss, lse, delta, dq,
-                              dq_ss, g, status, st);
-      if (rc) return rc;
-    } else {
+  if (variant == 2) {
+    {
       PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_q_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)SMEM_BWD_Q));
@@ -981,11 +1006,7 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
                                                           scale, status);
       PE_LAUNCHED();
     }
-    if (variant == 0) {
-      rc = attn_bwd_kv2_launch(S, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, dout, do_ss, lse, delta,
-                               dk_acc, dv_acc, counter, g, status, st);
-      if (rc) return rc;
-    } else {
+    {
       PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)SMEM_BWD_KV));
@@ -1009,6 +1030,61 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   if (!rc) rc = launch_cast(Si, Hkv * HD, dk_acc, scale, dk, dk_ss, st);
   if (!rc) rc = launch_cast(Si, Hkv * HD, dv_acc, 1.f, dv, dv_ss, st);
   return rc;
+}
+
+size_t attn_tc_seg_acc_bytes(int64_t rows, int Hkv) {
+  return (size_t)rows * 2 * Hkv * HD * 4 + 256;  // dK, dV accumulators + the work counter
+}
+
+int attn_bwd_tc_segments(int nseg, const PartGeom* g, int Hq, int Hkv, const void* q,
+                         int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
+                         const void* o, int64_t o_ss, const void* dout, int64_t do_ss,
+                         const float* lse, void* dq, int64_t dq_ss, void* dk, int64_t dk_ss,
+                         void* dv, int64_t dv_ss, float* delta, float* acc, int* status,
+                         cudaStream_t st) {
+  PE_CHECK_ARG(o_ss % 8 == 0 && do_ss % 8 == 0 && dq_ss % 8 == 0 && dk_ss % 8 == 0 &&
+                   dv_ss % 8 == 0 && al16(o) && al16(dout) && al16(dq) && al16(dk) && al16(dv),
+               "attention backward (tcgen05): operands must be 16-byte aligned");
+  std::vector<int64_t> rows(nseg + 1, 0);
+  for (int s = 0; s < nseg; ++s) rows[s + 1] = rows[s] + g[s].S;
+  const float scale = 1.0f / sqrtf((float)HD);
+  // every launch group reuses the accumulators from their start: its prep zeroes
+  // them after the previous group's casts (stream order)
+  for (auto [b, e] : seg_groups(nseg, g)) {
+    const int64_t rb = rows[b], R = rows[e] - rows[b];
+    PE_CHECK_ARG(R * Hq < (1ll << 31), "attention backward: too many stacked rows");
+    float* dk_acc = acc;
+    float* dv_acc = dk_acc + R * Hkv * HD;
+    int* counter = reinterpret_cast<int*>(dv_acc + R * Hkv * HD);
+    auto at = [rb](const void* p, int64_t ss) {
+      return static_cast<const uint8_t*>(p) + rb * ss * 2;
+    };
+    auto at_mut = [rb](void* p, int64_t ss) { return static_cast<uint8_t*>(p) + rb * ss * 2; };
+    const float* lse_g = lse + Hq * rb;
+    float* delta_g = delta + Hq * rb;
+    {
+      SegRows sr{};
+      sr.n = e - b;
+      for (int s = b; s < e; ++s) sr.row0[s - b + 1] = (int)(rows[s + 1] - rb);
+      const int64_t threads = R * Hq * 16;
+      attn_bwd_prep_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+          sr, Hq, Hkv, (const __nv_bfloat16*)at(o, o_ss), o_ss,
+          (const __nv_bfloat16*)at(dout, do_ss), do_ss, delta_g, nullptr, dk_acc, dv_acc,
+          counter);
+      PE_LAUNCHED();
+    }
+    int rc = attn_bwd_q2_launch(e - b, g + b, Hq, Hkv, at(q, q_ss), q_ss, at(k, k_ss), k_ss,
+                                at(v, v_ss), v_ss, at(dout, do_ss), do_ss, lse_g, delta_g,
+                                at_mut(dq, dq_ss), dq_ss, status, st);
+    if (!rc)
+      rc = attn_bwd_kv2_launch(e - b, g + b, Hq, Hkv, at(q, q_ss), q_ss, at(k, k_ss), k_ss,
+                               at(v, v_ss), v_ss, at(dout, do_ss), do_ss, lse_g, delta_g, dk_acc,
+                               dv_acc, counter, status, st);
+    if (!rc) rc = launch_cast((int)R, Hkv * HD, dk_acc, scale, at_mut(dk, dk_ss), dk_ss, st);
+    if (!rc) rc = launch_cast((int)R, Hkv * HD, dv_acc, 1.f, at_mut(dv, dv_ss), dv_ss, st);
+    if (rc) return rc;
+  }
+  return PE_OK;
 }
 
 }  // namespace pe

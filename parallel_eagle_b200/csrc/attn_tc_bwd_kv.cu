@@ -93,14 +93,27 @@ struct Bars {
   }
 };
 
-// the item's key tile and the 64-query steps that read it
+// the item's segment, key tile and the 64-query steps that read it
 struct Item {
-  int h, kvh, k0;
+  int seg, h, kvh, k0;
+  PartGeom g;
+  int64_t ml;  // first lse / delta element of the segment: Hq * its first stacked row
+  int64_t r0;  // its first stacked row
   Ranges qr;
   int n;
-  __device__ Item(int w, int Hq, int rep, const PartGeom& g) {
-    const int kt = w / Hq;
-    h = w - kt * Hq;
+  __device__ Item(int w, int Hq, int rep, const SegTable& tab) {
+    const int e = w / Hq;
+    h = w - e * Hq;
+    int kt;
+    if (tab.nwork > 0) {
+      unpack_work(tab.work[e], seg, kt);
+    } else {
+      seg = 0;
+      kt = e;
+    }
+    g = tab.g[seg];
+    r0 = tab.row0[seg];
+    ml = (int64_t)Hq * r0;
     kvh = h / rep;
     k0 = kt * TK;
     qr = query_tiles(g, k0, QT);
@@ -116,11 +129,10 @@ __device__ __forceinline__ uint32_t a_col(int kk) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const float* __restrict__ lse, const float* __restrict__ delta,
-                    float* __restrict__ dk_acc, float* __restrict__ dv_acc, int* work_counter,
-                    PartGeom g, int Hq, int Hkv, int rep, float scale, int* status) {
+attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restrict__ lse,
+                    const float* __restrict__ delta, float* __restrict__ dk_acc,
+                    float* __restrict__ dv_acc, int* work_counter, int Hq, int Hkv, int rep,
+                    float scale, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -135,8 +147,8 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nkt = (g.S + TK - 1) / TK;
-  const int total = Hq * nkt;
+  // items: (work-list entry or, for a lone segment, key tile) x query head
+  const int total = Hq * (tab.nwork > 0 ? tab.nwork : (tab.g[0].S + TK - 1) / TK);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -209,21 +221,21 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
         sItem[ic & 1] = w;
         mbar_arrive(&B.item_full[ic & 1]);  // release: publishes the slot write
         if (w < 0) break;
-        const Item it(w, Hq, rep, g);
+        const Item it(w, Hq, rep, tab);
         // K into buffer ic & 1 once the item two back issued its last S^T
         const int kb = ic & 1;
         if (!mbar_wait(&B.k_empty[kb], ((ic >> 1) & 1) ^ 1u, status, 342)) { ok = false; break; }
         uint8_t* kd = sK + kb * TILE_BYTES;
         mbar_arrive_expect_tx(&B.k_full[kb], TILE_BYTES);
-        tma_load_2d(kd, &tmK, &B.k_full[kb], it.kvh * HD, it.k0);
-        tma_load_2d(kd + CHUNK, &tmK, &B.k_full[kb], it.kvh * HD + 64, it.k0);
+        tma_load_2d(kd, &tab.tm[it.seg][1], &B.k_full[kb], it.kvh * HD, it.k0);
+        tma_load_2d(kd + CHUNK, &tab.tm[it.seg][1], &B.k_full[kb], it.kvh * HD + 64, it.k0);
         last_bar = &B.k_full[kb];
         last_ph = (ic >> 1) & 1;
         // V once the previous item's V left shared memory for TMEM
         if (!mbar_wait(B.v_copied, (ic & 1) ^ 1u, status, 357)) { ok = false; break; }
         mbar_arrive_expect_tx(B.v_full, TILE_BYTES);
-        tma_load_2d(sV, &tmV, B.v_full, it.kvh * HD, it.k0);
-        tma_load_2d(sV + CHUNK, &tmV, B.v_full, it.kvh * HD + 64, it.k0);
+        tma_load_2d(sV, &tab.tm[it.seg][2], B.v_full, it.kvh * HD, it.k0);
+        tma_load_2d(sV + CHUNK, &tab.tm[it.seg][2], B.v_full, it.kvh * HD + 64, it.k0);
         last_bar = B.v_full;
         last_ph = ic & 1;
         for (int i = 0; i < it.n && ok; ++i) {
@@ -233,15 +245,15 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           if (!mbar_wait(&B.q_empty[qs], ((gi / QS) & 1) ^ 1u, status, 343)) { ok = false; break; }
           uint8_t* qd = smem + OFF_Q + qs * SUB_BYTES;
           mbar_arrive_expect_tx(&B.q_full[qs], SUB_BYTES);
-          tma_load_2d(qd, &tmQ, &B.q_full[qs], it.h * HD, q0);
-          tma_load_2d(qd + SUB_CHUNK, &tmQ, &B.q_full[qs], it.h * HD + 64, q0);
+          tma_load_2d(qd, &tab.tm[it.seg][0], &B.q_full[qs], it.h * HD, q0);
+          tma_load_2d(qd + SUB_CHUNK, &tab.tm[it.seg][0], &B.q_full[qs], it.h * HD + 64, q0);
           last_bar = &B.q_full[qs];
           last_ph = (gi / QS) & 1;
           if (!mbar_wait(&B.do_empty[ds], ((gi / DS) & 1) ^ 1u, status, 344)) { ok = false; break; }
           uint8_t* dd = smem + OFF_DO + ds * SUB_BYTES;
           mbar_arrive_expect_tx(&B.do_full[ds], SUB_BYTES);
-          tma_load_2d(dd, &tmDO, &B.do_full[ds], it.h * HD, q0);
-          tma_load_2d(dd + SUB_CHUNK, &tmDO, &B.do_full[ds], it.h * HD + 64, q0);
+          tma_load_2d(dd, &tab.tm[it.seg][3], &B.do_full[ds], it.h * HD, q0);
+          tma_load_2d(dd + SUB_CHUNK, &tab.tm[it.seg][3], &B.do_full[ds], it.h * HD + 64, q0);
           last_bar = &B.do_full[ds];
           last_ph = (gi / DS) & 1;
         }
@@ -263,7 +275,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       const bool leader = elect_one();
       const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
       if (leader) {
-        const Item it(w, Hq, rep, g);
+        const Item it(w, Hq, rep, tab);
         const int kb = ic & 1, last = gs + it.n - 1;
         const uint32_t k_base = smem_u32(sK + kb * TILE_BYTES);
         // S^T(gi) = K Q(gi)^T into buffer gi & 1, both operands in shared memory
@@ -347,7 +359,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     for (int ic = 0; ok; ++ic) {
       const int w = read_item(ic, ok);
       if (w < 0) break;
-      const Item it(w, Hq, rep, g);
+      const Item it(w, Hq, rep, tab);
       for (int i = 0; i < it.n; ++i) {
         const int gi = gs + i, slot = gi % MS;
         const int q0 = it.qr.at(i) * QT;
@@ -359,10 +371,10 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           const int r = u * 32 + lane, q = q0 + r;
           float lv = INFINITY, dl = 0.f;
           int qa = -1, qd = 0;
-          if (q < g.S) {
-            lv = lse[(int64_t)it.h * g.S + q] * kLog2e;
-            dl = delta[(int64_t)it.h * g.S + q];
-            decode(g, q, qa, qd);
+          if (q < it.g.S) {
+            lv = lse[it.ml + (int64_t)it.h * it.g.S + q] * kLog2e;
+            dl = delta[it.ml + (int64_t)it.h * it.g.S + q];
+            decode(it.g, q, qa, qd);
           }
           sL[slot * QT + r] = lv;
           sD[slot * QT + r] = dl;
@@ -407,11 +419,11 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     for (; ok; ++ic) {
       const int w = read_item(ic, ok);
       if (w < 0) break;
-      const Item it(w, Hq, rep, g);
+      const Item it(w, Hq, rep, tab);
       const int kj = it.k0 + row;
-      const bool kvalid = kj < g.S;
+      const bool kvalid = kj < it.g.S;
       int ka = 0, ke = 0;
-      if (kvalid) decode(g, kj, ka, ke);
+      if (kvalid) decode(it.g, kj, ka, ke);
       // ---- this warp's quarter of the V row (head dims [32 part, 32 part + 32)):
       // shared memory -> TMEM, after the previous item's MMAs (which read the TMEM
       // copy) all completed ----
@@ -435,12 +447,13 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(B.v_copied);
       if (have_pending && !drain(ic - 1)) { ok = false; break; }
-      pending = kvalid ? (part < 2 ? dk_acc : dv_acc) + (int64_t)kj * kv_ld + it.kvh * HD : nullptr;
+      pending = kvalid ? (part < 2 ? dk_acc : dv_acc) + (it.r0 + kj) * kv_ld + it.kvh * HD
+                       : nullptr;
       have_pending = true;
       for (int i = 0; i < it.n; ++i) {
         const int gi = gs + i, slot = gi % MS, b = gi & 1;
         const int q0 = it.qr.at(i) * QT;
-        const bool full = tile_fully_allowed(g, q0, it.k0, QT);
+        const bool full = tile_fully_allowed(it.g, q0, it.k0, QT);
         // ---- P^T = 2^(S^T c - lse') ----
         if (!mbar_wait(&B.meta_full[slot], (gi / MS) & 1, status, 351)) { ok = false; break; }
         if (!mbar_wait(&B.st_full[b], (gi >> 1) & 1, status, 352)) { ok = false; break; }
@@ -522,25 +535,40 @@ attn_bwd_kv2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
 
 }  // namespace
 
-int attn_bwd_kv2_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
-                        int64_t k_ss, const void* v, int64_t v_ss, const void* dout,
-                        int64_t do_ss, const float* lse, const float* delta, float* dk_acc,
-                        float* dv_acc, int* work_counter, const PartGeom& g, int* status,
+int attn_bwd_kv2_launch(int nseg, const PartGeom* g, int Hq, int Hkv, const void* q,
+                        int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
+                        const void* dout, int64_t do_ss, const float* lse, const float* delta,
+                        float* dk_acc, float* dv_acc, int* work_counter, int* status,
                         cudaStream_t st) {
-  CUtensorMap tq, tk, tv, tdo;
-  int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, QT);
-  if (!rc) rc = make_tmap_2d(&tk, k, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)k_ss * 2, 64, TK);
-  if (!rc) rc = make_tmap_2d(&tv, v, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)v_ss * 2, 64, TK);
-  if (!rc)
-    rc = make_tmap_2d(&tdo, dout, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)do_ss * 2, 64, QT);
+  PE_CHECK_ARG(nseg >= 1 && nseg <= kMaxSeg, "attention backward: bad segment count");
+  SegTable tab;
+  memset(&tab, 0, sizeof(tab));
+  tab.nseg = nseg;
+  int64_t row = 0, lone_tiles = 0;
+  for (int s = 0; s < nseg; ++s) {
+    tab.g[s] = g[s];
+    tab.row0[s] = (int)row;
+    int rc = seg_map(&tab.tm[s][0], q, row, q_ss, (int64_t)Hq * HD, g[s].S, QT);
+    if (!rc) rc = seg_map(&tab.tm[s][1], k, row, k_ss, (int64_t)Hkv * HD, g[s].S, TK);
+    if (!rc) rc = seg_map(&tab.tm[s][2], v, row, v_ss, (int64_t)Hkv * HD, g[s].S, TK);
+    if (!rc) rc = seg_map(&tab.tm[s][3], dout, row, do_ss, (int64_t)Hq * HD, g[s].S, QT);
+    if (rc) return rc;
+    row += g[s].S;
+    lone_tiles = seg_tiles(g[s]);
+  }
+  // a unit is a key tile (items: unit x query head, heads fastest); its cost the
+  // 64-query steps that read it
+  auto cost = [](const PartGeom& sg, int kt) { return query_tiles(sg, kt * TK, QT).count(); };
+  int rc = seg_table_order(tab, [](const PartGeom& sg) { return seg_tiles(sg); }, cost);
   if (rc) return rc;
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)SMEM_KV2));
-  const int64_t items = (int64_t)Hq * ((S + TK - 1) / TK);
+  const int64_t items = (int64_t)Hq * (tab.nwork > 0 ? tab.nwork : lone_tiles);
+  PE_CHECK_ARG(items < (1ll << 31), "attention backward: too many work items");
   const int grid = (int)(items < sm_count() ? items : sm_count());
-  attn_bwd_kv2_kernel<<<grid, kThreads, SMEM_KV2, st>>>(tq, tk, tv, tdo, lse, delta, dk_acc,
-                                                        dv_acc, work_counter, g, Hq, Hkv,
-                                                        Hq / Hkv, 1.0f / sqrtf((float)HD), status);
+  attn_bwd_kv2_kernel<<<grid, kThreads, SMEM_KV2, st>>>(tab, lse, delta, dk_acc, dv_acc,
+                                                        work_counter, Hq, Hkv, Hq / Hkv,
+                                                        1.0f / sqrtf((float)HD), status);
   PE_LAUNCHED();
   return PE_OK;
 }

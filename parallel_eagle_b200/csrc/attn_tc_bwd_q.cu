@@ -78,11 +78,9 @@ __device__ __forceinline__ uint32_t a_col(int kk) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-attn_bwd_q2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                   const float* __restrict__ lse, const float* __restrict__ delta,
-                   __nv_bfloat16* __restrict__ dq, int64_t dq_ss, PartGeom g, int rep, float scale,
-                   int* status) {
+attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict__ lse,
+                   const float* __restrict__ delta, __nv_bfloat16* __restrict__ dq, int64_t dq_ss,
+                   int Hq, int rep, float scale, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -90,9 +88,23 @@ attn_bwd_q2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_qt = (g.S + TQ - 1) / TQ;
-  // grid (head, tile): blocks dispatch head-fastest, heaviest query tiles first
-  const int qt = num_qt - 1 - (int)blockIdx.y;
+  // grid (head, unit): blocks dispatch head-fastest, heaviest query tiles first --
+  // stacked segments in the work list's order, a lone segment from its last tile down
+  int sg, qt;
+  if (tab.nwork > 0) {
+    unpack_work(tab.work[blockIdx.y], sg, qt);
+  } else {
+    sg = 0;
+    qt = (tab.g[0].S + TQ - 1) / TQ - 1 - (int)blockIdx.y;
+  }
+  const PartGeom g = tab.g[sg];
+  const CUtensorMap* tmQ = &tab.tm[sg][0];
+  const CUtensorMap* tmK = &tab.tm[sg][1];
+  const CUtensorMap* tmV = &tab.tm[sg][2];
+  const CUtensorMap* tmDO = &tab.tm[sg][3];
+  lse += (int64_t)Hq * tab.row0[sg];
+  delta += (int64_t)Hq * tab.row0[sg];
+  dq += (int64_t)tab.row0[sg] * dq_ss;
   const int h = blockIdx.x;
   const int kvh = h / rep;
   const int q0 = qt * TQ;
@@ -141,25 +153,25 @@ attn_bwd_q2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
       uint64_t* last_bar = B.qdo_full;
       uint32_t last_ph = 0;
       mbar_arrive_expect_tx(B.qdo_full, 2 * TILE_BYTES);
-      tma_load_2d(smem + OFF_Q, &tmQ, B.qdo_full, h * HD, q0);
-      tma_load_2d(smem + OFF_Q + CHUNK, &tmQ, B.qdo_full, h * HD + 64, q0);
-      tma_load_2d(smem + OFF_DO, &tmDO, B.qdo_full, h * HD, q0);
-      tma_load_2d(smem + OFF_DO + CHUNK, &tmDO, B.qdo_full, h * HD + 64, q0);
+      tma_load_2d(smem + OFF_Q, tmQ, B.qdo_full, h * HD, q0);
+      tma_load_2d(smem + OFF_Q + CHUNK, tmQ, B.qdo_full, h * HD + 64, q0);
+      tma_load_2d(smem + OFF_DO, tmDO, B.qdo_full, h * HD, q0);
+      tma_load_2d(smem + OFF_DO + CHUNK, tmDO, B.qdo_full, h * HD + 64, q0);
       for (int j = 0; j < n && ok; ++j) {
         const int k0 = step_key(j);
         const int ks = j % KS, vs = j % VS;
         if (!mbar_wait(&B.k_empty[ks], ((j / KS) & 1) ^ 1u, status, 360)) { ok = false; break; }
         uint8_t* kd = smem + OFF_K + ks * SUB_BYTES;
         mbar_arrive_expect_tx(&B.k_full[ks], SUB_BYTES);
-        tma_load_2d(kd, &tmK, &B.k_full[ks], kvh * HD, k0);
-        tma_load_2d(kd + SUB_CHUNK, &tmK, &B.k_full[ks], kvh * HD + 64, k0);
+        tma_load_2d(kd, tmK, &B.k_full[ks], kvh * HD, k0);
+        tma_load_2d(kd + SUB_CHUNK, tmK, &B.k_full[ks], kvh * HD + 64, k0);
         last_bar = &B.k_full[ks];
         last_ph = (j / KS) & 1;
         if (!mbar_wait(&B.v_empty[vs], ((j / VS) & 1) ^ 1u, status, 361)) { ok = false; break; }
         uint8_t* vd = smem + OFF_V + vs * SUB_BYTES;
         mbar_arrive_expect_tx(&B.v_full[vs], SUB_BYTES);
-        tma_load_2d(vd, &tmV, &B.v_full[vs], kvh * HD, k0);
-        tma_load_2d(vd + SUB_CHUNK, &tmV, &B.v_full[vs], kvh * HD + 64, k0);
+        tma_load_2d(vd, tmV, &B.v_full[vs], kvh * HD, k0);
+        tma_load_2d(vd + SUB_CHUNK, tmV, &B.v_full[vs], kvh * HD + 64, k0);
         last_bar = &B.v_full[vs];
         last_ph = (j / VS) & 1;
       }
@@ -322,23 +334,43 @@ attn_bwd_q2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
 }  // namespace
 
-int attn_bwd_q2_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, const void* k,
-                       int64_t k_ss, const void* v, int64_t v_ss, const void* dout, int64_t do_ss,
-                       const float* lse, const float* delta, void* dq, int64_t dq_ss,
-                       const PartGeom& g, int* status, cudaStream_t st) {
-  CUtensorMap tq, tk, tv, tdo;
-  int rc = make_tmap_2d(&tq, q, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)q_ss * 2, 64, TQ);
-  if (!rc) rc = make_tmap_2d(&tk, k, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)k_ss * 2, 64, KT);
-  if (!rc) rc = make_tmap_2d(&tv, v, (uint64_t)Hkv * HD, (uint64_t)S, (uint64_t)v_ss * 2, 64, KT);
-  if (!rc)
-    rc = make_tmap_2d(&tdo, dout, (uint64_t)Hq * HD, (uint64_t)S, (uint64_t)do_ss * 2, 64, TQ);
+int attn_bwd_q2_launch(int nseg, const PartGeom* g, int Hq, int Hkv, const void* q,
+                       int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
+                       const void* dout, int64_t do_ss, const float* lse, const float* delta,
+                       void* dq, int64_t dq_ss, int* status, cudaStream_t st) {
+  PE_CHECK_ARG(nseg >= 1 && nseg <= kMaxSeg, "attention backward: bad segment count");
+  SegTable tab;
+  memset(&tab, 0, sizeof(tab));
+  tab.nseg = nseg;
+  int64_t row = 0;
+  int max_units = 0;
+  for (int s = 0; s < nseg; ++s) {
+    tab.g[s] = g[s];
+    tab.row0[s] = (int)row;
+    int rc = seg_map(&tab.tm[s][0], q, row, q_ss, (int64_t)Hq * HD, g[s].S, TQ);
+    if (!rc) rc = seg_map(&tab.tm[s][1], k, row, k_ss, (int64_t)Hkv * HD, g[s].S, KT);
+    if (!rc) rc = seg_map(&tab.tm[s][2], v, row, v_ss, (int64_t)Hkv * HD, g[s].S, KT);
+    if (!rc) rc = seg_map(&tab.tm[s][3], dout, row, do_ss, (int64_t)Hq * HD, g[s].S, TQ);
+    if (rc) return rc;
+    row += g[s].S;
+    max_units = std::max(max_units, seg_tiles(g[s]));
+  }
+  // a unit is a query tile; its cost the 64-key steps it walks
+  auto cost = [](const PartGeom& sg, int qt) {
+    int r_end, m_beg, m_end;
+    key_tiles(sg, qt * TQ, r_end, m_beg, m_end, KT);
+    return r_end + (m_end - m_beg);
+  };
+  int rc = seg_table_order(tab, [](const PartGeom& sg) { return seg_tiles(sg); }, cost);
   if (rc) return rc;
+  const int ny = tab.nwork > 0 ? tab.nwork : max_units;
+  PE_CHECK_ARG(ny <= 65535, "attention backward: too many query tiles for one launch");
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_q2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)SMEM_Q2));
-  dim3 grid((unsigned)Hq, (unsigned)((S + TQ - 1) / TQ));
-  attn_bwd_q2_kernel<<<grid, kThreads, SMEM_Q2, st>>>(tq, tk, tv, tdo, lse, delta,
-                                                      (__nv_bfloat16*)dq, dq_ss, g, Hq / Hkv,
-                                                      1.0f / sqrtf((float)HD), status);
+  dim3 grid((unsigned)Hq, (unsigned)ny);
+  attn_bwd_q2_kernel<<<grid, kThreads, SMEM_Q2, st>>>(tab, lse, delta, (__nv_bfloat16*)dq, dq_ss,
+                                                      Hq, Hq / Hkv, 1.0f / sqrtf((float)HD),
+                                                      status);
   PE_LAUNCHED();
   return PE_OK;
 }

@@ -299,7 +299,7 @@ class StepEngine:
               last=True):
         """Forward and backward of the stacked segments of one pass.  Every GEMM,
         norm and element-wise op runs once over all stacked rows; attention runs
-        per segment on its row range with that segment's mask."""
+        once too, each segment on its row range with that segment's mask."""
         d, fp = self.d, self.flat
         dt, dev = fp.dtype, fp.device
         H, I = d.hidden, d.intermediate
@@ -312,8 +312,8 @@ class StepEngine:
         eps = d.eps
         E, Wh, wfinal = d.frozen_heads()
         single = len(plan.segs) == 1
-        layouts = [(ops.AttnLayout(L.LAYOUT_PARTITION, a0=a0, a1=a1, k=k), q, off)
-                   for a0, a1, q, off in plan.segs]
+        # every segment's attention runs in one call over the stacked rows
+        bounds = [(a0, a1) for a0, a1, _, _ in plan.segs]
 
         def W(name, shape=None):
             return fp.view(name, shape)
@@ -358,19 +358,14 @@ class StepEngine:
             xn, r1 = ops.rmsnorm_fwd(x, W(p + "input_norm.weight"), eps)
             qkv = ops.linear(xn, w_qkv)
             ops.rope_(qkv, nh + nkv, hd, plan.pos, d.rope_theta)
-            o = torch.empty(Q, qc, dtype=dt, device=dev)
-            lses = []
-            for layout, q, off in layouts:
-                q3 = qkv[off : off + q].view(1, q, cqkv)
-                _, lse = ops.attn_fwd(q3[:, :, :qc], q3[:, :, qc : qc + kc], q3[:, :, qc + kc :],
-                                      nh, nkv, hd, layout, o=o[off : off + q].view(1, q, qc))
-                lses.append(lse)
+            o, lse = ops.attn_fwd_segments(qkv[:, :qc], qkv[:, qc : qc + kc], qkv[:, qc + kc :],
+                                           nh, nkv, hd, bounds, k)
             x2 = ops.linear(o, w_o, residual=x)
             xn2, r2 = ops.rmsnorm_fwd(x2, W(p + "post_norm.weight"), eps)
             gu = ops.linear(xn2, w_gu)
             act = ops.swiglu_fwd(gu, I)
             x3 = ops.linear(act, w_dn, residual=x2)
-            saved.append((x, xn, r1, qkv, o, lses, x2, xn2, r2, gu, act))
+            saved.append((x, xn, r1, qkv, o, lse, x2, xn2, r2, gu, act))
             x = x3
         hf, rf = ops.rmsnorm_fwd(x, wfinal, eps)
 
@@ -393,7 +388,7 @@ class StepEngine:
         # ---------------- layers backward ----------------
         for li in reversed(range(len(d.layers))):
             p = f"layers.{li}."
-            x_in, xn, r1, qkv, o, lses, x2, xn2, r2, gu, act = saved[li]
+            x_in, xn, r1, qkv, o, lse, x2, xn2, r2, gu, act = saved[li]
             w_qkv = fp.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight", H)
             w_o = W(p + "attn.o_proj.weight", (H, qc))
             w_gu = fp.span(p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight", H)
@@ -413,13 +408,9 @@ class StepEngine:
             do = ops.linear_dgrad(dx2, w_o)
             ops.linear_wgrad(dx2, o, grad=G(p + "attn.o_proj.weight", (H, qc)), accumulate=True)
             dqkv = torch.empty(Q, cqkv, dtype=dt, device=dev)
-            for (layout, q, off), lse in zip(layouts, lses):
-                q3 = qkv[off : off + q].view(1, q, cqkv)
-                d3 = dqkv[off : off + q].view(1, q, cqkv)
-                ops.attn_bwd(q3[:, :, :qc], q3[:, :, qc : qc + kc], q3[:, :, qc + kc :],
-                             o[off : off + q].view(1, q, qc), do[off : off + q].view(1, q, qc),
-                             lse, nh, nkv, hd, layout,
-                             dq=d3[:, :, :qc], dk=d3[:, :, qc : qc + kc], dv=d3[:, :, qc + kc :])
+            ops.attn_bwd_segments(qkv[:, :qc], qkv[:, qc : qc + kc], qkv[:, qc + kc :], o, do, lse,
+                                  nh, nkv, hd, bounds, k, dq=dqkv[:, :qc],
+                                  dk=dqkv[:, qc : qc + kc], dv=dqkv[:, qc + kc :])
             ops.rope_(dqkv, nh + nkv, hd, plan.pos, d.rope_theta, inverse=True)
             dxn = ops.linear_dgrad(dqkv, w_qkv)
             ops.linear_wgrad(

@@ -7,6 +7,7 @@ allocated here (torch owns all memory); the library itself never allocates.
 
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from . import _lib as L
@@ -237,6 +238,82 @@ def attn_bwd(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, layout: AttnLay
         status_word(q.device).data_ptr(), L.stream_ptr(q.device),
     )
     L.check(rc, "pe_attn_bwd")
+    return dq, dk, dv
+
+
+def _seg_bounds(bounds) -> np.ndarray:
+    """(a0, a1) per segment as a contiguous int64 host array (kept alive by the caller)."""
+    arr = np.ascontiguousarray(np.asarray(bounds, dtype=np.int64).reshape(-1, 2))
+    if arr.shape[0] < 1:
+        raise L.PeError("attention segments: no segments")
+    return arr
+
+
+def _row_ss(t: torch.Tensor) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise L.PeError("attention segments: operands are [rows, cols] views with unit column stride")
+    return t.stride(0)
+
+
+def segment_rows(bounds, k: int) -> list[int]:
+    """Slot count a1 + (a1 - a0)(K - 1) of every segment (its rows in the stack)."""
+    return [int(a1 + (a1 - a0) * (k - 1)) for a0, a1 in bounds]
+
+
+def attn_fwd_segments(q, k, v, n_heads, n_kv_heads, head_dim, bounds, kdepth, o=None, lse=None,
+                      algo=L.ALGO_AUTO):
+    """Masked attention of all segments of one sequence in one call.  q ``[R, Hq*hd]``,
+    k/v ``[R, Hkv*hd]`` row views holding the segments one after another (segment s
+    in rows ``[row0_s, row0_s + S_s)``, S_s = a1 + (a1 - a0)(K - 1)).  Returns o (like
+    q) and lse: fp32 ``[Hq * R]`` holding one ``[Hq, S_s]`` block per segment at
+    ``Hq * row0_s``."""
+    L.require_cuda(q, k, v)
+    b = _seg_bounds(bounds)
+    R = q.shape[0]
+    if R != sum(segment_rows(b.tolist(), kdepth)):
+        raise L.PeError("attention segments: rows != sum of segment slot counts")
+    if o is None:
+        o = torch.empty(R, n_heads * head_dim, dtype=q.dtype, device=q.device)
+    if lse is None:
+        lse = torch.empty(n_heads * R, dtype=torch.float32, device=q.device)
+    rc = _lib().pe_attn_fwd_segments(
+        L.dtype_code(q.dtype), b.shape[0], b.ctypes.data, kdepth, n_heads, n_kv_heads, head_dim,
+        q.data_ptr(), _row_ss(q), k.data_ptr(), _row_ss(k), v.data_ptr(), _row_ss(v),
+        o.data_ptr(), _row_ss(o), lse.data_ptr(), algo, status_word(q.device).data_ptr(),
+        L.stream_ptr(q.device),
+    )
+    L.check(rc, "pe_attn_fwd_segments")
+    return o, lse
+
+
+def attn_bwd_segments(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, bounds, kdepth,
+                      dq=None, dk=None, dv=None, algo=L.ALGO_AUTO):
+    """Backward of :func:`attn_fwd_segments` (same row and lse conventions); dq/dk/dv
+    are overwritten."""
+    L.require_cuda(q, k, v, o, do, lse)
+    b = _seg_bounds(bounds)
+    R = q.shape[0]
+    if R != sum(segment_rows(b.tolist(), kdepth)):
+        raise L.PeError("attention segments: rows != sum of segment slot counts")
+    if dq is None:
+        dq = torch.empty(R, n_heads * head_dim, dtype=q.dtype, device=q.device)
+    if dk is None:
+        dk = torch.empty(R, n_kv_heads * head_dim, dtype=k.dtype, device=k.device)
+    if dv is None:
+        dv = torch.empty(R, n_kv_heads * head_dim, dtype=v.dtype, device=v.device)
+    lib = _lib()
+    dt = L.dtype_code(q.dtype)
+    nbytes = int(lib.pe_attn_bwd_segments_workspace(dt, b.shape[0], b.ctypes.data, kdepth,
+                                                    n_heads, n_kv_heads, head_dim))
+    ws = _workspace(q.device, nbytes, "attn_bwd")
+    rc = lib.pe_attn_bwd_segments(
+        dt, b.shape[0], b.ctypes.data, kdepth, n_heads, n_kv_heads, head_dim, q.data_ptr(),
+        _row_ss(q), k.data_ptr(), _row_ss(k), v.data_ptr(), _row_ss(v), o.data_ptr(), _row_ss(o),
+        do.data_ptr(), _row_ss(do), lse.data_ptr(), dq.data_ptr(), _row_ss(dq), dk.data_ptr(),
+        _row_ss(dk), dv.data_ptr(), _row_ss(dv), ws.data_ptr(), ws.numel(), algo,
+        status_word(q.device).data_ptr(), L.stream_ptr(q.device),
+    )
+    L.check(rc, "pe_attn_bwd_segments")
     return dq, dk, dv
 
 

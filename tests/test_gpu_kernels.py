@@ -313,6 +313,65 @@ def test_attention_tcgen05_bwd_matches_simt(geom, variant):
         assert rel(a.float().cpu(), b.float().cpu()) < 2e-2, name
 
 
+# (n, segments, K, Hq, Hkv): every segment of one sequence stacked in one row space
+SEG_CASES = [(300, 4, 5, 4, 2), (2048, 4, 5, 28, 4), (100, 3, 1, 4, 2),
+             # ten segments: two launch groups (at most eight segments per launch)
+             (90, 10, 3, 2, 1), (700, 2, 8, 8, 2)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("case", SEG_CASES)
+def test_attention_segments_match_per_segment_calls(case, dtype):
+    """One call over the stacked segments equals one call per segment: forward, lse
+    and dQ bit for bit (the same tiles, only scheduled together); dK / dV up to the
+    order of the fp32 GQA-group additions."""
+    from parallel_eagle_b200.engine import segment_bounds
+
+    n, nseg, k, nh, nkv = case
+    if dtype == torch.float32 and n > 1000:
+        pytest.skip("CUDA-core fp32 path: small cases only")
+    hd = 128
+    bounds = segment_bounds(n, nseg)
+    rows = ops.segment_rows(bounds, k)
+    R = sum(rows)
+    cq, ckv = nh * hd, nkv * hd
+    qkv = _rand(R, cq + 2 * ckv, dtype=dtype, seed=40)
+    do = _rand(R, cq, dtype=dtype, seed=41)
+    q, kt, vt = qkv[:, :cq], qkv[:, cq:cq + ckv], qkv[:, cq + ckv:]
+    algo = L.ALGO_TCGEN05 if dtype == torch.bfloat16 else L.ALGO_SIMT
+    o, lse = ops.attn_fwd_segments(q, kt, vt, nh, nkv, hd, bounds, k, algo=algo)
+    dqkv = torch.full((R, cq + 2 * ckv), float("nan"), dtype=dtype, device=DEV)
+    ops.attn_bwd_segments(q, kt, vt, o, do, lse, nh, nkv, hd, bounds, k, dq=dqkv[:, :cq],
+                          dk=dqkv[:, cq:cq + ckv], dv=dqkv[:, cq + ckv:], algo=algo)
+    off = 0
+    for (a0, a1), S in zip(bounds, rows):
+        lay = ops.AttnLayout(L.LAYOUT_PARTITION, a0=a0, a1=a1, k=k)
+        sl = slice(off, off + S)
+        o1, lse1 = ops.attn_fwd(q[None, sl], kt[None, sl], vt[None, sl], nh, nkv, hd, lay,
+                                algo=algo)
+        d1 = ops.attn_bwd(q[None, sl], kt[None, sl], vt[None, sl], o1, do[None, sl], lse1, nh,
+                          nkv, hd, lay, algo=algo)
+        torch.cuda.synchronize()
+        ops.check_status(DEV)
+        assert torch.equal(o[sl], o1[0]), (a0, a1)
+        assert torch.equal(lse[nh * off : nh * (off + S)], lse1.reshape(-1)), (a0, a1)
+        assert torch.equal(dqkv[sl, :cq], d1[0][0]), (a0, a1)
+        for name, got, ref in (("dk", dqkv[sl, cq:cq + ckv], d1[1][0]),
+                               ("dv", dqkv[sl, cq + ckv:], d1[2][0])):
+            assert not torch.isnan(got).any(), name
+            assert rel(got.float().cpu(), ref.float().cpu()) < 5e-3, (name, a0, a1)
+        off += S
+
+
+def test_attention_segments_reject_bad_rows():
+    bounds = [(0, 64), (64, 128)]
+    R = sum(ops.segment_rows(bounds, 3)) - 1
+    q = torch.zeros(R, 256, dtype=torch.bfloat16, device=DEV)
+    kv = torch.zeros(R, 128, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(L.PeError):
+        ops.attn_fwd_segments(q, kv, kv, 2, 1, 128, bounds, 3)
+
+
 # ----------------------------------------------------------- LM head + CE ----
 
 
