@@ -220,6 +220,17 @@ int pe_gather_rows(int dtype, int64_t rows, int64_t H, const int64_t* idx, const
 int pe_cast_f32(int dtype, int64_t n, const float* x, void* y, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Draft-time selection: per row of logits (dtype, row stride ld), the log-
+ * probabilities lp = (z - max z) - log(sum exp(z - max z)) in fp32 (raw = 1:
+ * the logits themselves) and the k best columns in order (value descending,
+ * then column ascending): idx[r, 0..k) (int64), val[r, 0..k) (fp32).  Replaces
+ * log_softmax(logits.float()).topk of reference src/pe/decode/tree.py:33-41 and
+ * logits.argmax of src/pe/decode/chain.py:22-23 / src/pe/drafter.py:268.
+ * ------------------------------------------------------------------------- */
+int pe_topk_logprobs(int dtype, int64_t rows, int64_t V, const void* logits, int64_t ld, int k,
+                     int raw, int64_t* idx, float* val, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Optimizer (reference src/pe/train.py:26-34,158-159: clip_grad_norm_(1.0) then
  * AdamW.step()).  sumsq_out (fp32 [1]) += sum g^2; the step reads it to apply the
  * clipping coefficient min(1, max_norm / (sqrt(sumsq) + 1e-6)).

@@ -1,7 +1,8 @@
 """CPU oracle for the drafter training step -- TEST INFRASTRUCTURE ONLY.
 
 This package restates, in plain PyTorch on the CPU, the reference's drafter
-training step (``pe.partition.mtp_backward`` and everything it calls).  It is the
+training step (``pe.partition.mtp_backward`` and everything it calls) and its
+draft-time path (``draft_logits`` and the tree / chain proposals).  It is the
 checker that the CUDA path is compared against, and the "port" timed as the CPU
 baseline.  Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
 baseline leg may import it; the product package never does, and has no CPU
@@ -29,4 +30,11 @@ from .drafter_step import (  # noqa: F401
     segment_edges,
     segment_slots,
     slot_allow,
+)
+from .draft import (  # noqa: F401
+    draft_logits,
+    draft_logits_sequential,
+    propose_chain_from_logits,
+    propose_tree_from_logits,
+    token_shared_input,
 )

@@ -1,0 +1,142 @@
+// Per-row log-softmax + top-k of draft logits: the selection step of the
+// drafter's tree / chain proposals (reference src/pe/decode/tree.py:33-41 and
+// src/pe/decode/chain.py:22-23, i.e. log_softmax(logits.float()) then topk /
+// argmax per prediction depth).
+//
+// One CTA per row.  Pass 1 reduces the row maximum m and s = sum exp(z - m) in
+// fp32; the log-probability of column v is lp_v = (z_v - m) - log(s), the same
+// two roundings torch's log_softmax applies (with raw = 1 the ranking value is the
+// logit itself, as for argmax, and pass 1 is skipped).  Pass 2 picks the k best columns
+// in k rounds: round r takes the first column after the previous winner in the
+// order (lp descending, column ascending) -- a scan of the row from L2 per
+// round, with no per-thread candidate lists, so k is limited only by the
+// caller's buffers.  The row (at most a vocabulary of ~150K bf16) stays in L2
+// across the rounds.
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace pe {
+namespace {
+
+constexpr int kThreads = 512;
+
+__device__ __forceinline__ float load_f(const float* p) { return *p; }
+__device__ __forceinline__ float load_f(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+// (value, column) ordered by value descending, then column ascending
+struct Cand {
+  float v;
+  int64_t i;
+};
+__device__ __forceinline__ bool before(const Cand& a, const Cand& b) {
+  return a.v > b.v || (a.v == b.v && a.i < b.i);
+}
+
+__device__ Cand block_best(Cand c, Cand* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Cand x;
+    x.v = __shfl_xor_sync(0xffffffffu, c.v, o);
+    x.i = __shfl_xor_sync(0xffffffffu, c.i, o);
+    if (before(x, c)) c = x;
+  }
+  if (lane == 0) red[warp] = c;
+  __syncthreads();
+  if (warp == 0) {
+    c = lane < kThreads / 32 ? red[lane] : Cand{-INFINITY, INT64_MAX};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      Cand x;
+      x.v = __shfl_xor_sync(0xffffffffu, c.v, o);
+      x.i = __shfl_xor_sync(0xffffffffu, c.i, o);
+      if (before(x, c)) c = x;
+    }
+    if (lane == 0) red[0] = c;
+  }
+  __syncthreads();
+  const Cand out = red[0];
+  __syncthreads();  // red is reused by the next round
+  return out;
+}
+
+__device__ float block_reduce(float v, float* red, bool is_max) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float x = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, x) : v + x;
+  }
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < kThreads / 32 ? red[lane] : (is_max ? -INFINITY : 0.f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float x = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, x) : v + x;
+    }
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float out = red[0];
+  __syncthreads();
+  return out;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+topk_logprobs_kernel(int64_t V, const T* __restrict__ logits, int64_t ld, int k, int raw,
+                     int64_t* __restrict__ idx, float* __restrict__ val) {
+  __shared__ Cand cred[kThreads / 32];
+  __shared__ float fred[kThreads / 32];
+  const T* z = logits + (int64_t)blockIdx.x * ld;
+  float m = 0.f, logs = 0.f;
+  if (!raw) {
+    m = -INFINITY;
+    for (int64_t v = threadIdx.x; v < V; v += kThreads) m = fmaxf(m, load_f(z + v));
+    m = block_reduce(m, fred, true);
+    float s = 0.f;
+    for (int64_t v = threadIdx.x; v < V; v += kThreads) s += expf(load_f(z + v) - m);
+    s = block_reduce(s, fred, false);
+    logs = logf(s);
+  }
+  Cand prev{INFINITY, -1};  // everything comes after it
+  for (int r = 0; r < k; ++r) {
+    Cand best{-INFINITY, INT64_MAX};
+    for (int64_t v = threadIdx.x; v < V; v += kThreads) {
+      const float x = load_f(z + v);
+      const Cand c{raw ? x : (x - m) - logs, v};
+      if (before(prev, c) && before(c, best)) best = c;
+    }
+    best = block_best(best, cred);
+    if (threadIdx.x == 0) {
+      idx[(int64_t)blockIdx.x * k + r] = best.i;
+      val[(int64_t)blockIdx.x * k + r] = best.v;
+    }
+    prev = best;
+  }
+}
+
+}  // namespace
+}  // namespace pe
+
+using namespace pe;
+
+extern "C" int pe_topk_logprobs(int dtype, int64_t rows, int64_t V, const void* logits,
+                                int64_t ld, int k, int raw, int64_t* idx, float* val,
+                                void* stream) {
+  PE_CHECK_ARG(rows >= 0 && V >= 1 && ld >= V && k >= 1 && k <= V,
+               "topk_logprobs: need V >= 1, ld >= V and 1 <= k <= V");
+  PE_CHECK_ARG(rows <= 0x7fffffff, "topk_logprobs: too many rows");
+  if (rows == 0) return PE_OK;
+  PE_CHECK_ARG(logits && idx && val, "topk_logprobs: null pointer");
+  cudaStream_t st = as_stream(stream);
+  return PE_DISPATCH(dtype, T, [&] {
+    topk_logprobs_kernel<T><<<(unsigned)rows, kThreads, 0, st>>>(V, (const T*)logits, ld, k, raw,
+                                                                 idx, val);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}

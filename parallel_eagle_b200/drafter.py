@@ -20,6 +20,7 @@ import torch
 from torch import nn
 
 from . import _lib as L
+from . import ops
 from .config import DrafterConfig
 from .masks import mtp_allow_mask, mtp_labels, mtp_position_ids, to_additive_bias
 from .nn import DecoderLayer, RMSNorm, build_rope_cache, linear, rms_norm
@@ -138,6 +139,69 @@ class ParallelDrafter(nn.Module):
         cat = torch.cat([self.mask_emb, self.h_shared], dim=-1)[None]
         vec = linear(cat, self.in_proj.weight)[0]
         return vec.unsqueeze(0).expand(n, -1)
+
+    def token_shared_input(self, token_ids: torch.Tensor) -> torch.Tensor:
+        """``in_proj([emb(token); h_shared])`` for a drafted token whose target feature
+        does not exist yet (reference ``drafter.py:139-145``)."""
+        L.require_cuda(token_ids)
+        emb = self._embed_tokens(token_ids).to(self.param_dtype)
+        shared = self.h_shared.unsqueeze(0).expand(emb.shape[0], -1)
+        return linear(torch.cat([emb, shared], dim=-1), self.in_proj.weight)
+
+    @torch.no_grad()
+    def draft_logits(self, context_ids: torch.Tensor, context_feats: torch.Tensor,
+                     k: int) -> torch.Tensor:
+        """Logits ``(k, V)`` for the ``k`` tokens following ``context_ids`` (reference
+        ``drafter.py:195-236``).
+
+        The packed sequence is the real context followed by ``k - 1`` prediction
+        slots anchored at the last context position -- the partition layout with
+        ``(a0, a1, K) = (p - 1, p, k)`` -- so the attention kernels re-derive the
+        mask instead of reading a dense bias.  The frozen LM head runs on the ``k``
+        prediction rows only: the last real slot (depth 0) and the prediction slots.
+        """
+        dev = self.device
+        p = int(context_ids.shape[0])
+        if p < 1 or k < 1:
+            raise ValueError("draft_logits needs a non-empty context and k >= 1")
+        m = p + (k - 1)
+        x = torch.empty(m, self.hidden, dtype=self.param_dtype, device=dev)
+        x[:p] = self.real_input(context_ids.to(dev), context_feats.to(dev))
+        if k > 1:
+            x[p:] = self.mask_input(k - 1)
+        pos = torch.arange(m, device=dev)
+        pos[p:] = (p - 1) + torch.arange(1, k, device=dev)
+        layout = ops.AttnLayout(L.LAYOUT_PARTITION, a0=p - 1, a1=p, k=k)
+        hidden = self.forward(x.unsqueeze(0), pos.unsqueeze(0), layout)[0]
+        # depth 0 is predicted at the last real slot, depth d at slot p + d - 1
+        return linear(hidden[p - 1 :], self._lm_head[0].weight)
+
+    @torch.no_grad()
+    def draft_logits_sequential(self, context_ids: torch.Tensor, context_feats: torch.Tensor,
+                                k: int) -> torch.Tensor:
+        """Greedy drafting by ``k`` causal forward passes, each appending the previous
+        argmax token as :meth:`token_shared_input` (reference ``drafter.py:239-269``);
+        the baseline parallel drafting replaces."""
+        dev = self.device
+        real_x = self.real_input(context_ids.to(dev), context_feats.to(dev))
+        head = self._lm_head[0].weight
+        drafted: list[int] = []
+        out = []
+        for _ in range(k):
+            if drafted:
+                tok = torch.tensor(drafted, device=dev)
+                x = torch.cat([real_x, self.token_shared_input(tok)], dim=0)
+            else:
+                x = real_x
+            s = x.shape[0]
+            pos = torch.arange(s, device=dev).unsqueeze(0)
+            causal = ops.AttnLayout(L.LAYOUT_PARTITION, a0=0, a1=s, k=1)
+            hidden = self.forward(x.unsqueeze(0), pos, causal)[0]
+            logits = linear(hidden[-1:], head)
+            out.append(logits[0])
+            # argmax with the first maximal column, as torch.argmax
+            drafted.append(int(ops.topk_logprobs(logits, 1, raw=True)[1][0, 0]))
+        return torch.stack(out)
 
     def forward(self, x: torch.Tensor, position_ids: torch.Tensor, bias) -> torch.Tensor:
         """``x`` (B, S, H), ``position_ids`` (B, S), ``bias`` (B|1, 1, S, S) additive

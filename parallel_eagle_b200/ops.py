@@ -317,6 +317,24 @@ def attn_bwd_segments(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, bounds
     return dq, dk, dv
 
 
+def topk_logprobs(logits: torch.Tensor, k: int, raw: bool = False):
+    """``(values, indices)`` of the ``k`` largest log-softmax entries of every row of
+    ``logits`` ``[rows, V]`` (fp32 log-probabilities, int64 columns), ordered by value
+    descending then column ascending; ``raw=True`` ranks the logits themselves
+    (``k = 1``: argmax with the first maximal column)."""
+    L.require_cuda(logits)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise L.PeError("topk_logprobs: logits must be [rows, V] with unit column stride")
+    rows, V = logits.shape
+    idx = torch.empty(rows, k, dtype=torch.int64, device=logits.device)
+    val = torch.empty(rows, k, dtype=torch.float32, device=logits.device)
+    rc = _lib().pe_topk_logprobs(L.dtype_code(logits.dtype), rows, V, logits.data_ptr(),
+                                 logits.stride(0), k, int(raw), idx.data_ptr(), val.data_ptr(),
+                                 L.stream_ptr(logits.device))
+    L.check(rc, "pe_topk_logprobs")
+    return val, idx
+
+
 # --------------------------------------------------------- lm head + loss ----
 
 _ws_cache: dict[tuple, torch.Tensor] = {}

@@ -3,13 +3,15 @@
 Run from the repository root in a checkout that has the reference project
 available (its ``src`` directory importable as ``pe``)::
 
-    PE_REFERENCE_SRC=<reference>/src python tests/golden/make_golden.py
+    PE_REFERENCE_SRC=<reference>/src python tests/golden/make_golden.py [--draft]
 
 For every case in ``recipe.CASES`` this builds the reference ``ParallelDrafter``
 from seeded synthetic frozen heads, runs the reference ``mtp_backward`` (and
 ``mtp_eval_loss`` / ``forward``) and writes ``tests/golden/<case>.pt`` with the
 losses, the accumulated gradients (full tensors for the tiny cases, random-
-projection sketches for the larger one) and checksums of every input.
+projection sketches for the larger one) and checksums of every input.  For the
+cases that store full tensors it also writes ``<case>_draft.pt`` with the
+reference's draft-time outputs (``--draft`` writes only those).
 """
 
 from __future__ import annotations
@@ -129,12 +131,55 @@ def build_case(pe, name: str, c: dict) -> dict:
     return out
 
 
+def build_draft_case(pe, name: str, c: dict) -> dict:
+    """Draft-time outputs of the reference on the same seeded drafter:
+    ``draft_logits`` (src/pe/drafter.py:195-236), ``draft_logits_sequential``
+    (:239-269), ``propose_tree`` (src/pe/decode/tree.py:19-57) and ``propose_chain``
+    (src/pe/decode/chain.py:15-23) for every entry of ``recipe.DRAFT_RUNS``."""
+    from pe.config import DrafterConfig
+    from pe.decode.chain import propose_chain
+    from pe.decode.tree import propose_tree
+    from pe.drafter import ParallelDrafter
+
+    dt = _DT[c["dtype"]]
+    heads = recipe.make_heads(c["vocab"], c["hidden"], c["seed"], c["norm_jitter"], dt)
+    target = _heads_object(pe, c, heads)
+    torch.manual_seed(c["seed"])
+    drafter = ParallelDrafter.from_target(
+        target, DrafterConfig(num_layers=c["num_layers"], max_depth=c["max_depth"])
+    ).to(dtype=dt)
+    drafter.eval()
+    ids, feats = recipe.make_sequence(c["n"], c["vocab"], 3 * c["hidden"], c["seed"], 0)
+    feats = feats.to(dt)
+    out = {"case": name, "params": {k: v.detach().clone() for k, v in drafter.state_dict().items()},
+           "runs": []}
+    for run in recipe.DRAFT_RUNS:
+        p, k = run["p"], run["k"]
+        rec = {"run": dict(run)}
+        with torch.no_grad():
+            rec["logits"] = drafter.draft_logits(ids[:p], feats[:p], k).clone()
+            if run.get("sequential"):
+                rec["logits_sequential"] = drafter.draft_logits_sequential(ids[:p], feats[:p], k).clone()
+            kt, pend = k - run["pending"], run["pending"]
+            rec["tree"] = propose_tree(drafter, ids[:p], feats[:p], kt, run["top_k"],
+                                       run["max_nodes"], pending=pend)
+            rec["chain"] = propose_chain(drafter, ids[:p], feats[:p], kt, pending=pend)
+        out["runs"].append(rec)
+    return out
+
+
 def main():
     pe = _reference()
+    draft_only = "--draft" in sys.argv[1:]
     for name, c in recipe.CASES.items():
-        rec = build_case(pe, name, c)
-        torch.save(rec, HERE / f"{name}.pt")
-        print(name, [r["losses"] for r in rec["runs"]], "eval", rec["eval_loss"])
+        if not draft_only:
+            rec = build_case(pe, name, c)
+            torch.save(rec, HERE / f"{name}.pt")
+            print(name, [r["losses"] for r in rec["runs"]], "eval", rec["eval_loss"])
+        if c["full"]:
+            rec = build_draft_case(pe, name, c)
+            torch.save(rec, HERE / f"{name}_draft.pt")
+            print(name, "draft", [r["tree"] for r in rec["runs"]])
 
 
 if __name__ == "__main__":

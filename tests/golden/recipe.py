@@ -46,6 +46,15 @@ CASES = {
     ),
 }
 
+# Draft-time runs on the first sequence of each full case: context length p, drafted
+# depths k (k - pending fresh ones for the tree / chain), tree beam parameters.
+DRAFT_RUNS = [
+    dict(p=1, k=1, pending=0, top_k=3, max_nodes=4),
+    dict(p=5, k=4, pending=0, top_k=3, max_nodes=9, sequential=True),
+    dict(p=6, k=3, pending=1, top_k=2, max_nodes=8),
+    dict(p=9, k=5, pending=0, top_k=4, max_nodes=20),
+]
+
 SKETCH_ROWS = 64
 
 

@@ -1,0 +1,96 @@
+"""Draft-time path on the GPU: ``ParallelDrafter.draft_logits`` /
+``draft_logits_sequential`` and the tree / chain proposals.
+
+* fp32 against the reference's own outputs (``tests/golden/*_draft.pt``): logits
+  within 1e-4 relative Frobenius, trees and chains token for token.
+* bf16 at head_dim 128 (tensor-core attention, partition layout ``(p-1, p, k)``)
+  against the CPU oracle within 2e-2.
+* The selection kernel against ``log_softmax`` + ``topk`` / ``argmax``.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from gpu_harness import ROOT, build_drafter, make_case, oracle, recipe
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+_DT = {"float32": torch.float32, "bfloat16": torch.bfloat16}
+DEV = torch.device("cuda")
+
+
+def _golden_case(name):
+    c = recipe.CASES[name]
+    dt = _DT[c["dtype"]]
+    case = make_case(c["hidden"], c["n_heads"], c["n_kv_heads"], c["intermediate"], c["vocab"],
+                     c["num_layers"], c["max_depth"], c["n"], dtype=dt, seed=c["seed"],
+                     norm_jitter=c["norm_jitter"])
+    g = torch.load(ROOT / "tests" / "golden" / f"{name}_draft.pt", weights_only=False)
+    case["params"] = g["params"]
+    return case, g
+
+
+@pytest.mark.parametrize("name", [n for n, c in recipe.CASES.items() if c["full"]])
+def test_draft_path_matches_reference_golden(name):
+    from parallel_eagle_b200 import decode
+
+    case, g = _golden_case(name)
+    dt = case["dtype"]
+    tol = 1e-4 if dt == torch.float32 else 2e-2
+    model = build_drafter(case)
+    ids, feats = case["seqs"][0]
+    ids, feats = ids.to(DEV), feats.to(DEV)
+    for rec in g["runs"]:
+        run = rec["run"]
+        p, k, pend = run["p"], run["k"], run["pending"]
+        logits = model.draft_logits(ids[:p], feats[:p], k)
+        assert logits.shape == rec["logits"].shape and logits.dtype == rec["logits"].dtype
+        assert recipe.rel_fro(logits.float().cpu(), rec["logits"].float()) < tol, run
+        if "logits_sequential" in rec:
+            seq = model.draft_logits_sequential(ids[:p], feats[:p], k)
+            assert recipe.rel_fro(seq.float().cpu(), rec["logits_sequential"].float()) < tol, run
+        if dt == torch.float32:
+            tree = decode.propose_tree(model, ids[:p], feats[:p], k - pend, run["top_k"],
+                                       run["max_nodes"], pending=pend)
+            assert tuple(tree) == tuple(rec["tree"]), run
+            chain = decode.propose_chain(model, ids[:p], feats[:p], k - pend, pending=pend)
+            assert chain == rec["chain"], run
+
+
+@pytest.mark.parametrize("p,k", [(1, 5), (300, 5), (129, 8), (256, 1)])
+def test_draft_logits_tensor_cores_match_oracle(p, k):
+    """hidden 256 / 2 query heads / 1 KV head: head_dim 128, so the draft forward's
+    attention runs on the tcgen05 kernels with the partition layout (p-1, p, k)."""
+    case = make_case(256, 2, 1, 512, 1000, 1, 5, 300, dtype=torch.bfloat16, seed=7)
+    model = build_drafter(case)
+    ids, feats = case["seqs"][0]
+    got = model.draft_logits(ids[:p].to(DEV), feats[:p].to(DEV), k)
+    torch.cuda.synchronize()
+    ref = oracle.draft_logits(case["params"], case["heads"], ids[:p], feats[:p], k, case["dims"])
+    assert got.shape == (k, 1000)
+    assert recipe.rel_fro(got.float().cpu(), ref.float()) < 2e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,V,k", [(5, 152064, 8), (3, 1000, 1), (2, 7, 7)])
+def test_topk_logprobs_matches_torch(dtype, rows, V, k):
+    from parallel_eagle_b200 import ops
+
+    g = torch.Generator().manual_seed(rows * 31 + V)
+    z = (torch.randn(rows, V, generator=g) * 3).to(dtype)
+    vals, idx = ops.topk_logprobs(z.to(DEV), k)
+    lp = torch.log_softmax(z.float(), dim=-1)
+    for r in range(rows):
+        rv, ri = lp[r].topk(k)
+        assert torch.allclose(vals[r].cpu(), rv, atol=1e-5, rtol=1e-6), r
+        # the selected columns carry the selected values (ties may swap columns)
+        assert torch.allclose(lp[r][idx[r].cpu()], vals[r].cpu(), atol=1e-5, rtol=1e-6), r
+        assert len(set(idx[r].tolist())) == k
+    am_val, am = ops.topk_logprobs(z.to(DEV), 1, raw=True)
+    assert torch.equal(am[:, 0].cpu(), z.float().argmax(-1))
+    assert torch.equal(am_val[:, 0].cpu(), z.float().max(-1).values)
