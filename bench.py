@@ -594,6 +594,64 @@ def run_kernel(args):
                       "tflops": round(flops / (ms / 1e3) / 1e12, 1)}), flush=True)
 
 
+def run_draft(args):
+    """The draft path (reference drafter.py:195-269, decode/tree.py:19-57):
+    config-2 dims, one context of ``--n`` (default 2048) confirmed tokens, k = 5.
+    Times, with CUDA events on the launching stream, ``draft_logits`` (one forward
+    over p + k - 1 slots + the LM head on k rows), ``propose_tree`` (k 5, top_k 4,
+    max_nodes 20; includes the host beam and its device reads) and the sequential
+    baseline ``draft_logits_sequential``; the CPU oracle's ``draft_logits`` on a
+    bounded context is reported beside it."""
+    from parallel_eagle_b200 import decode, ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    c = dict(CONFIG2)
+    p, k = args.n or 2048, c["max_depth"]
+    d = build_drafter(c, dev)
+    d.eval()
+    g = torch.Generator(device=dev).manual_seed(5)
+    ids = torch.randint(0, c["vocab"], (p,), generator=g, device=dev)
+    feats = torch.randn(p, 3 * c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    runs = {
+        "draft_logits": lambda: d.draft_logits(ids, feats, k),
+        "propose_tree": lambda: decode.propose_tree(d, ids, feats, k, 4, 20),
+        "draft_logits_sequential": lambda: d.draft_logits_sequential(ids, feats, k),
+    }
+    out = {}
+    for name, fn in runs.items():
+        ms = time_case(fn, args.steps, warmup=args.warmup)
+        out[name] = {"ms": round(ms, 3), "draft_tokens_per_s": round(k / (ms / 1e3), 1)}
+    ops.check_status(dev)
+    line = {"metric": "draft latency (k=5 tokens after a confirmed context)", "unit": "ms",
+            "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config-2 drafter, draft path", "context": p, "k": k},
+            "results": out,
+            "parallel_vs_sequential": round(out["draft_logits_sequential"]["ms"]
+                                            / out["draft_logits"]["ms"], 2)}
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT / "tests" / "golden"))
+        import oracle
+        import recipe
+
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        dims = oracle.OracleDims(hidden=c["hidden"], n_heads=c["n_heads"],
+                                 n_kv_heads=c["n_kv_heads"], intermediate=c["intermediate"],
+                                 vocab=c["vocab"], num_layers=c["num_layers"], max_depth=k)
+        heads = recipe.make_heads(c["vocab"], c["hidden"], 0, 0.0, torch.bfloat16)
+        params = oracle.init_params(dims, 0, torch.bfloat16)
+        cp = min(p, args.cpu_n)
+        cids, cfeats = recipe.make_sequence(cp, c["vocab"], 3 * c["hidden"], 0, 0)
+        t0 = time.perf_counter()
+        oracle.draft_logits(params, heads, cids, cfeats.to(torch.bfloat16), k, dims)
+        sec = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(sec * 1e3, 1), "unit": "ms", "cores": threads,
+                                "kind": "port",
+                                "sample": f"oracle draft_logits, context {cp}, k {k}, bf16"}
+    print(json.dumps(line), flush=True)
+
+
 def cpu_baseline(args, n=None):
     """The CPU oracle (a port of the reference step) on one bounded sample of the
     workload: one config-2 sequence at reduced length, bf16, all host threads."""
@@ -664,8 +722,12 @@ def main(argv=None):
                     help="BASELINE config 5: peak HBM / throughput over n, K, S (1 GPU)")
     ap.add_argument("--kernel", choices=["gemm", "attn", "lmhead", "elementwise"], default=None,
                     help="time one kernel family on its bench-sized case instead of the step")
+    ap.add_argument("--draft", action="store_true",
+                    help="time the draft path (draft_logits / propose_tree) on config-2 dims")
     args = ap.parse_args(argv)
-    if args.sweep:
+    if args.draft:
+        run_draft(args)
+    elif args.sweep:
         run_sweep(args)
     elif args.kernel:
         run_kernel(args)
