@@ -12,30 +12,31 @@
 //   P^T  = 2^(S^T c - lse')  dS^T = P^T (dP^T - delta)   (compute warps; bf16
 //          packed back over S^T / dP^T; masked pairs exactly zero)
 //   dV  += P^T dO           dK  += dS^T Q
-// Operand placement follows the shared-memory bandwidth (128 B per clock per
-// SM): an MMA with both operands in shared memory needs (4 KB + N x 32 B) per
-// N / 2 clocks at M = 128 -- a third short of its rate at N = 64 -- while one
-// with A in TMEM reads only B, 64 B per clock.  dP^T, dV and dK take A from
-// TMEM (V copied there once per item, P^T / dS^T written by the compute
-// warps); S^T keeps both operands in shared memory but is double-buffered and
-// issued two steps ahead, off the critical path, while the single dP^T tile is
-// recomputed right after dK consumed dS^T.  Per step the MMAs issue as
-//   dV(i), dK(i), dP^T(i+1), S^T(i+2).
+// Both score tiles are double-buffered in TMEM, so no MMA that feeds the
+// compute warps waits for the step before it: per step the MMAs issue as
+//   dV(i), dP^T(i+1), dK(i), S^T(i+2)
+// -- dP^T(i+1) goes out as soon as P^T(i) is in (it overwrites dS^T(i-1), which
+// dK(i-1) has read), not after dK(i), so the compute warps' dS(i+1) never waits
+// for their own dS(i).  dV and dK take A from TMEM (P^T / dS^T written by the
+// compute warps, 64 B of shared memory per clock for B); S^T = K Q^T and
+// dP^T = V dO^T keep both operands in shared memory (an M = 128, N = 64 MMA
+// then runs at ~2/3 rate on shared-memory bandwidth), which leaves TMEM room
+// for the second dP^T buffer.
 // The item's dK / dV tile is added (fp32) into the KV head's accumulators,
 // reducing the query heads of a GQA group without expanding K / V.
 //
 // Warp roles (640 threads):
 //   warp 0      scheduler + TMA: claims items; K per item (two buffers), V per
-//               item (one buffer, refilled once the compute warps copied it into
-//               TMEM); Q / dO per step into 4- and 3-deep rings
+//               item (one buffer, refilled once the item's last dP^T read it);
+//               Q / dO per step into 4- and 3-deep rings
 //   warp 1      tcgen05.mma issue
 //   warp 2      per-query operands (lse * log2 e, delta, anchor, depth) per step
 //   warp 3      idle
 //   warps 4-19  compute: four per TMEM lane quarter, each owning 16 of the 64
-//               query columns; per item each copies a quarter of the V row into
-//               TMEM, and parts 0 / 1 drain the two halves of dK, parts 2 / 3 of dV
-// TMEM: dK 0..127, dV 128..255, V 256..319 (bf16 pairs), S^T 320..383 /
-//       384..447, dP^T 448..511.
+//               query columns; parts 0 / 1 drain the two halves of the previous
+//               item's dK, parts 2 / 3 of its dV, before the item's first P^T
+// TMEM: dK 0..127, dV 128..255, S^T 256..319 / 320..383, dP^T 384..447 /
+//       448..511.
 #include "attn_tc.cuh"
 
 namespace pe {
@@ -64,12 +65,12 @@ constexpr uint32_t OFF_A = OFF_D + MS * QT * 4;       // int   [MS][QT]  anchor 
 constexpr uint32_t OFF_E = OFF_A + MS * QT * 4;       // int   [MS][QT]  depth
 constexpr uint32_t OFF_ITEM = OFF_E + MS * QT * 4;    // int   [2]
 constexpr uint32_t OFF_BAR = OFF_ITEM + 16;
-constexpr int NBARS = 2 + 2 + 2 + 2 + 1 + 1 + 2 * QS + 2 * DS + 2 * MS + 2 + 2 + 1 + 1 + 1;
+constexpr int NBARS = 2 + 2 + 2 + 2 + 1 + 1 + 2 * QS + 2 * DS + 2 * MS + 2 + 2 + 2 + 2 + 1;
 constexpr uint32_t OFF_TMEM = OFF_BAR + NBARS * 8;
 constexpr size_t SMEM_KV2 = 1024 + OFF_TMEM + 16;
 
 struct Bars {
-  uint64_t *item_full, *item_empty, *k_full, *k_empty, *v_full, *v_copied, *q_full, *q_empty,
+  uint64_t *item_full, *item_empty, *k_full, *k_empty, *v_full, *v_empty, *q_full, *q_empty,
       *do_full, *do_empty, *meta_full, *meta_empty, *st_full, *p_full, *dpt_full, *ds_full,
       *acc_full;
   __device__ explicit Bars(uint64_t* b) {
@@ -78,7 +79,7 @@ struct Bars {
     k_full = b; b += 2;      // K tile (per item parity) landed
     k_empty = b; b += 2;     // the item's last S^T read it
     v_full = b; b += 1;      // V tile landed in shared memory
-    v_copied = b; b += 1;    // compute warps copied it into TMEM (smem free, TMEM ready)
+    v_empty = b; b += 1;     // the item's last dP^T read it
     q_full = b; b += QS;
     q_empty = b; b += QS;
     do_full = b; b += DS;
@@ -87,8 +88,8 @@ struct Bars {
     meta_empty = b; b += MS;
     st_full = b; b += 2;
     p_full = b; b += 2;
-    dpt_full = b; b += 1;
-    ds_full = b; b += 1;
+    dpt_full = b; b += 2;    // per dP^T buffer
+    ds_full = b; b += 2;     // per dP^T buffer (dS^T written over dP^T)
     acc_full = b; b += 1;
   }
 };
@@ -164,7 +165,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
       mbar_init(&B.p_full[i], kComputeWarps);
     }
     mbar_init(B.v_full, 1);
-    mbar_init(B.v_copied, kComputeWarps);
+    mbar_init(B.v_empty, 1);
     for (int i = 0; i < QS; ++i) {
       mbar_init(&B.q_full[i], 1);
       mbar_init(&B.q_empty[i], 1);
@@ -177,9 +178,12 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
       mbar_init(&B.meta_full[i], 32);
       mbar_init(&B.meta_empty[i], kComputeWarps);
     }
-    // dP^T(i + 1) is computed only after every warp arrived for dS^T(i)
-    mbar_init(B.dpt_full, 1);
-    mbar_init(B.ds_full, kComputeWarps);
+    // like S^T / P^T: one dP^T / dS^T barrier pair per buffer, because dP^T runs
+    // ahead of the compute warps' dS^T
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.dpt_full[i], 1);
+      mbar_init(&B.ds_full[i], kComputeWarps);
+    }
     mbar_init(B.acc_full, 1);
     fence_barrier_init();
     fence_proxy_async();
@@ -192,8 +196,8 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tDK = tmem, tDV = tmem + 128, tV = tmem + 256;
-  const uint32_t tS = tmem + 320, tDP = tmem + 448;  // S^T buffer b at tS + b * QT
+  const uint32_t tDK = tmem, tDV = tmem + 128;
+  const uint32_t tS = tmem + 256, tDP = tmem + 384;  // buffer b at + b * QT
 
   // every role walks the same item sequence; `ic` counts items, `gs` steps
   auto read_item = [&](int ic, bool& ok) -> int {
@@ -231,8 +235,8 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
         tma_load_2d(kd + CHUNK, &tab.tm[it.seg][1], &B.k_full[kb], it.kvh * HD + 64, it.k0);
         last_bar = &B.k_full[kb];
         last_ph = (ic >> 1) & 1;
-        // V once the previous item's V left shared memory for TMEM
-        if (!mbar_wait(B.v_copied, (ic & 1) ^ 1u, status, 357)) { ok = false; break; }
+        // V once the previous item's last dP^T read it
+        if (!mbar_wait(B.v_empty, (ic & 1) ^ 1u, status, 357)) { ok = false; break; }
         mbar_arrive_expect_tx(B.v_full, TILE_BYTES);
         tma_load_2d(sV, &tab.tm[it.seg][2], B.v_full, it.kvh * HD, it.k0);
         tma_load_2d(sV + CHUNK, &tab.tm[it.seg][2], B.v_full, it.kvh * HD + 64, it.k0);
@@ -294,7 +298,8 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
           if (gi == last) mma_commit(&B.k_empty[kb]);  // the item's last read of K
           return true;
         };
-        // dP^T(gi) = V dO(gi)^T, A (V) from TMEM
+        // dP^T(gi) = V dO(gi)^T into buffer gi & 1, both operands in shared memory
+        const uint32_t v_base = smem_u32(sV);
         auto issue_dpt = [&](int gi) -> bool {
           const int ds = gi % DS;
           if (!mbar_wait(&B.do_full[ds], (gi / DS) & 1, status, 346)) return false;
@@ -302,21 +307,28 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
           const uint32_t do_base = smem_u32(smem + OFF_DO + ds * SUB_BYTES);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk)
-            mma_bf16_ts(tDP, tV + kk * 8,
+            mma_bf16_ss(tDP + (gi & 1) * QT,
+                        sw128_desc(v_base + (kk >> 2) * CHUNK + (kk & 3) * 32, 16, 1024),
                         sw128_desc(do_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024),
                         ID_KQ, kk > 0 ? 1u : 0u);
-          mma_commit(B.dpt_full);
+          mma_commit(&B.dpt_full[gi & 1]);
+          if (gi == last) mma_commit(B.v_empty);  // the item's last read of V
           return true;
         };
         ok = mbar_wait(&B.k_full[kb], (ic >> 1) & 1, status, 347);
-        if (ok) {
+        if (ok && it.n == 0) {
+          // nothing reads this key tile: release K and V without MMAs
+          mma_commit(&B.k_empty[kb]);
+          ok = mbar_wait(B.v_full, ic & 1, status, 358);
+          if (ok) mma_commit(B.v_empty);
+        }
+        if (ok && it.n > 0) {
           tc_fence_after();
           ok = issue_st(gs);
         }
         if (ok && it.n > 1) ok = issue_st(gs + 1);
-        // V of this item in TMEM (copied after the previous item's MMAs completed)
-        if (ok) ok = mbar_wait(B.v_copied, ic & 1, status, 358);
-        if (ok) {
+        if (ok && it.n > 0) ok = mbar_wait(B.v_full, ic & 1, status, 358);
+        if (ok && it.n > 0) {
           tc_fence_after();
           ok = issue_dpt(gs);
         }
@@ -331,18 +343,20 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
             mma_bf16_ts(tDV, tS + b * QT + a_col(kk),
                         sw128_desc(do_base + kk * 2048, SUB_CHUNK, 1024), ID_KM,
                         (acc | kk) != 0 ? 1u : 0u);
-          mma_commit(&B.do_empty[gi % DS]);
-          if (!mbar_wait(B.ds_full, gi & 1, status, 349)) { ok = false; break; }
+          mma_commit(&B.do_empty[gi % DS]);  // dO(gi): dP^T(gi) and dV(gi) issued
+          // dP^T(i+1) into the other buffer, whose dS^T(i-1) dK(i-1) has read
+          // (tcgen05 executes in issue order); it does not wait for dS^T(i)
+          if (i + 1 < it.n && !issue_dpt(gi + 1)) { ok = false; break; }
+          if (!mbar_wait(&B.ds_full[b], (gi >> 1) & 1, status, 349)) { ok = false; break; }
           tc_fence_after();
           const uint32_t q_base = smem_u32(smem + OFF_Q + (gi % QS) * SUB_BYTES);
 #pragma unroll
           for (int kk = 0; kk < QT / 16; ++kk)
-            mma_bf16_ts(tDK, tDP + a_col(kk), sw128_desc(q_base + kk * 2048, SUB_CHUNK, 1024),
-                        ID_KM, (acc | kk) != 0 ? 1u : 0u);
+            mma_bf16_ts(tDK, tDP + b * QT + a_col(kk),
+                        sw128_desc(q_base + kk * 2048, SUB_CHUNK, 1024), ID_KM,
+                        (acc | kk) != 0 ? 1u : 0u);
           mma_commit(&B.q_empty[gi % QS]);
-          // dP^T(i+1) overwrites dS^T(i) after dK(i) read it, S^T(i+2) overwrites
-          // P^T(i) after dV(i) read it (tcgen05 executes in issue order)
-          if (i + 1 < it.n && !issue_dpt(gi + 1)) { ok = false; break; }
+          // S^T(i+2) overwrites P^T(i) after dV(i) read it
           if (i + 2 < it.n && !issue_st(gi + 2)) { ok = false; break; }
         }
         if (ok) mma_commit(B.acc_full);
@@ -397,8 +411,9 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
     const int64_t kv_ld = (int64_t)Hkv * HD;
     bool ok = true;
     int gs = 0;
-    // the previous item's dK (parts 0, 1) / dV (parts 2, 3) row, drained after the next
-    // item's K / V copy so that item's first MMAs overlap the drain
+    // the previous item's dK (parts 0, 1) / dV (parts 2, 3) row, drained before this
+    // item's first P^T: the item's first dV / dK MMAs (which overwrite the
+    // accumulators) wait for that P^T, while its first S^T / dP^T already run
     float* pending = nullptr;
     bool have_pending = false;
     auto drain = [&](int ic_prev) -> bool {
@@ -424,31 +439,11 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
       const bool kvalid = kj < it.g.S;
       int ka = 0, ke = 0;
       if (kvalid) decode(it.g, kj, ka, ke);
-      // ---- this warp's quarter of the V row (head dims [32 part, 32 part + 32)):
-      // shared memory -> TMEM, after the previous item's MMAs (which read the TMEM
-      // copy) all completed ----
-      if (have_pending && !mbar_wait(B.acc_full, (ic - 1) & 1, status, 355)) { ok = false; break; }
-      if (!mbar_wait(B.v_full, ic & 1, status, 356)) { ok = false; break; }
-      {
-        uint32_t r16[16];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint4 x = *reinterpret_cast<const uint4*>(sV + (part >> 1) * CHUNK +
-                                                          swz(row, (part & 1) * 4 + u));
-          r16[u * 4 + 0] = x.x;
-          r16[u * 4 + 1] = x.y;
-          r16[u * 4 + 2] = x.z;
-          r16[u * 4 + 3] = x.w;
-        }
-        tmem_st16(tV + lane_off + part * 16, r16);
-        tmem_wait_st();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(B.v_copied);
       if (have_pending && !drain(ic - 1)) { ok = false; break; }
-      pending = kvalid ? (part < 2 ? dk_acc : dv_acc) + (it.r0 + kj) * kv_ld + it.kvh * HD
-                       : nullptr;
+      // (an item no query reads leaves the accumulators untouched: nothing to add)
+      pending = kvalid && it.n > 0
+                    ? (part < 2 ? dk_acc : dv_acc) + (it.r0 + kj) * kv_ld + it.kvh * HD
+                    : nullptr;
       have_pending = true;
       for (int i = 0; i < it.n; ++i) {
         const int gi = gs + i, slot = gi % MS, b = gi & 1;
@@ -493,10 +488,10 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
         __syncwarp();
         if (lane == 0) mbar_arrive(&B.p_full[b]);
         // ---- dS^T = P^T (dP^T - delta) ----
-        if (!mbar_wait(B.dpt_full, gi & 1, status, 353)) { ok = false; break; }
+        if (!mbar_wait(&B.dpt_full[b], (gi >> 1) & 1, status, 353)) { ok = false; break; }
         tc_fence_after();
         float dv[C];
-        tmem_ld16(tDP + lane_off + cb, dv);
+        tmem_ld16(tDP + b * QT + lane_off + cb, dv);
         tmem_wait_ld();
         const float* D = sD + slot * QT + cb;
         {
@@ -508,13 +503,13 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
             pw[c / 2 + 1] =
                 pack_bf16x2(pv[c + 2] * (dv[c + 2] - d4.z), pv[c + 3] * (dv[c + 3] - d4.w));
           }
-          tmem_st8(tDP + lane_off + cb, pw);
+          tmem_st8(tDP + b * QT + lane_off + cb, pw);
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(B.ds_full);
+          mbar_arrive(&B.ds_full[b]);
           mbar_arrive(&B.meta_empty[slot]);
         }
       }
