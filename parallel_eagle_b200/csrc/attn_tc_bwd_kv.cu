@@ -59,8 +59,8 @@ constexpr uint32_t OFF_K = 0;                        // [2] K tiles
 constexpr uint32_t OFF_V = OFF_K + 2 * TILE_BYTES;
 constexpr uint32_t OFF_Q = OFF_V + TILE_BYTES;
 constexpr uint32_t OFF_DO = OFF_Q + QS * SUB_BYTES;
-constexpr uint32_t OFF_L = OFF_DO + DS * SUB_BYTES;   // float [MS][QT]  lse * log2 e
-constexpr uint32_t OFF_D = OFF_L + MS * QT * 4;       // float [MS][QT]  delta
+constexpr uint32_t OFF_L = OFF_DO + DS * SUB_BYTES;   // float [MS][QT]  -lse * log2 e
+constexpr uint32_t OFF_D = OFF_L + MS * QT * 4;       // float [MS][QT]  -delta
 constexpr uint32_t OFF_A = OFF_D + MS * QT * 4;       // int   [MS][QT]  anchor (-1: no row)
 constexpr uint32_t OFF_E = OFF_A + MS * QT * 4;       // int   [MS][QT]  depth
 constexpr uint32_t OFF_ITEM = OFF_E + MS * QT * 4;    // int   [2]
@@ -383,11 +383,12 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
 #pragma unroll
         for (int u = 0; u < QT / 32; ++u) {
           const int r = u * 32 + lane, q = q0 + r;
-          float lv = INFINITY, dl = 0.f;
+          // staged negated, so the compute warps add them with packed f32x2 ops
+          float lv = -INFINITY, dl = 0.f;
           int qa = -1, qd = 0;
           if (q < it.g.S) {
-            lv = lse[it.ml + (int64_t)it.h * it.g.S + q] * kLog2e;
-            dl = delta[it.ml + (int64_t)it.h * it.g.S + q];
+            lv = -lse[it.ml + (int64_t)it.h * it.g.S + q] * kLog2e;
+            dl = -delta[it.ml + (int64_t)it.h * it.g.S + q];
             decode(it.g, q, qa, qd);
           }
           sL[slot * QT + r] = lv;
@@ -408,6 +409,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float scale_log2 = scale * kLog2e;
+    const float2 sc2 = make_float2(scale_log2, scale_log2);
     const int64_t kv_ld = (int64_t)Hkv * HD;
     bool ok = true;
     int gs = 0;
@@ -461,10 +463,12 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
 #pragma unroll
           for (int c = 0; c < C; c += 4) {
             const float4 l4 = *reinterpret_cast<const float4*>(L + c);
-            pv[c] = ex2_approx(fmaf(pv[c], scale_log2, -l4.x));
-            pv[c + 1] = ex2_approx(fmaf(pv[c + 1], scale_log2, -l4.y));
-            pv[c + 2] = ex2_approx(fmaf(pv[c + 2], scale_log2, -l4.z));
-            pv[c + 3] = ex2_approx(fmaf(pv[c + 3], scale_log2, -l4.w));
+            const float2 a = fma2(make_float2(pv[c], pv[c + 1]), sc2, make_float2(l4.x, l4.y));
+            const float2 b = fma2(make_float2(pv[c + 2], pv[c + 3]), sc2, make_float2(l4.z, l4.w));
+            pv[c] = ex2_approx(a.x);
+            pv[c + 1] = ex2_approx(a.y);
+            pv[c + 2] = ex2_approx(b.x);
+            pv[c + 3] = ex2_approx(b.y);
           }
         } else {
           const int* QA = sA + slot * QT + cb;
@@ -474,7 +478,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
             const int qa = QA[c];
             const bool allow =
                 kvalid && qa >= 0 && (ke == 0 ? (ka <= qa) : (ka == qa && ke <= QE[c]));
-            pv[c] = allow ? ex2_approx(fmaf(pv[c], scale_log2, -L[c])) : 0.f;
+            pv[c] = allow ? ex2_approx(fmaf(pv[c], scale_log2, L[c])) : 0.f;
           }
         }
         {
@@ -499,9 +503,12 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
 #pragma unroll
           for (int c = 0; c < C; c += 4) {
             const float4 d4 = *reinterpret_cast<const float4*>(D + c);
-            pw[c / 2] = pack_bf16x2(pv[c] * (dv[c] - d4.x), pv[c + 1] * (dv[c + 1] - d4.y));
-            pw[c / 2 + 1] =
-                pack_bf16x2(pv[c + 2] * (dv[c + 2] - d4.z), pv[c + 3] * (dv[c + 3] - d4.w));
+            const float2 a = mul2(make_float2(pv[c], pv[c + 1]),
+                                  add2(make_float2(dv[c], dv[c + 1]), make_float2(d4.x, d4.y)));
+            const float2 b = mul2(make_float2(pv[c + 2], pv[c + 3]),
+                                  add2(make_float2(dv[c + 2], dv[c + 3]), make_float2(d4.z, d4.w)));
+            pw[c / 2] = pack_bf16x2(a.x, a.y);
+            pw[c / 2 + 1] = pack_bf16x2(b.x, b.y);
           }
           tmem_st8(tDP + b * QT + lane_off + cb, pw);
         }

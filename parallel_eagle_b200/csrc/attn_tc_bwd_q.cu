@@ -247,6 +247,8 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
     }
     const int lo = qd > 0 ? g.a1 + (qi - g.a0) * g.km1 : 0;
     const float scale_log2 = scale * kLog2e;
+    const float2 sc2 = make_float2(scale_log2, scale_log2), nl2 = make_float2(-l2, -l2),
+                 ndl2 = make_float2(-dl, -dl);
     bool ok = mbar_wait(B.qdo_full, 0, status, 367);
     if (ok) {
       // one 64-column half of the Q (parts 0, 1) or dO (parts 2, 3) row -> TMEM as
@@ -279,7 +281,11 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
       // P = 2^(S c - lse') (masked pairs exactly 0)
       if (k0 + C - 1 <= qi) {  // every key of this warp's slice is real and <= the anchor
 #pragma unroll
-        for (int c = 0; c < C; ++c) sv[c] = ex2_approx(fmaf(sv[c], scale_log2, -l2));
+        for (int c = 0; c < C; c += 2) {
+          const float2 a = fma2(make_float2(sv[c], sv[c + 1]), sc2, nl2);
+          sv[c] = ex2_approx(a.x);
+          sv[c + 1] = ex2_approx(a.y);
+        }
       } else {
 #pragma unroll
         for (int c = 0; c < C; ++c) {
@@ -295,8 +301,11 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
       tmem_wait_ld();
       uint32_t pw[C / 2];
 #pragma unroll
-      for (int c = 0; c < C; c += 2)
-        pw[c / 2] = pack_bf16x2(sv[c] * (dv[c] - dl), sv[c + 1] * (dv[c + 1] - dl));
+      for (int c = 0; c < C; c += 2) {
+        const float2 a =
+            mul2(make_float2(sv[c], sv[c + 1]), add2(make_float2(dv[c], dv[c + 1]), ndl2));
+        pw[c / 2] = pack_bf16x2(a.x, a.y);
+      }
       tmem_st8(tS + b * KT + lane_off + cb, pw);
       tmem_wait_st();
       tc_fence_before();
