@@ -12,12 +12,13 @@
 //   P^T  = 2^(S^T c - lse')  dS^T = P^T (dP^T - delta)   (compute warps; bf16
 //          packed back over S^T / dP^T; masked pairs exactly zero)
 //   dV  += P^T dO           dK  += dS^T Q
-// Both score tiles are double-buffered in TMEM, so no MMA that feeds the
-// compute warps waits for the step before it: per step the MMAs issue as
-//   dV(i), dP^T(i+1), dK(i), S^T(i+2)
-// -- dP^T(i+1) goes out as soon as P^T(i) is in (it overwrites dS^T(i-1), which
-// dK(i-1) has read), not after dK(i), so the compute warps' dS(i+1) never waits
-// for their own dS(i).  dV and dK take A from TMEM (P^T / dS^T written by the
+// Both score tiles are double-buffered in TMEM and issued together two steps
+// ahead: per step the MMAs issue as
+//   dV(i), dK(i), S^T(i+2), dP^T(i+2)
+// once every compute warp has written P^T(i) and dS^T(i), so a compute warp's
+// step is one wait, one pair of TMEM loads and one pair of stores, and step
+// i + 1 (whose scores are in since step i - 1) overlaps the MMAs of step i.
+// dV and dK take A from TMEM (P^T / dS^T written by the
 // compute warps, 64 B of shared memory per clock for B); S^T = K Q^T and
 // dP^T = V dO^T keep both operands in shared memory (an M = 128, N = 64 MMA
 // then runs at ~2/3 rate on shared-memory bandwidth), which leaves TMEM room
@@ -65,13 +66,13 @@ constexpr uint32_t OFF_A = OFF_D + MS * QT * 4;       // int   [MS][QT]  anchor 
 constexpr uint32_t OFF_E = OFF_A + MS * QT * 4;       // int   [MS][QT]  depth
 constexpr uint32_t OFF_ITEM = OFF_E + MS * QT * 4;    // int   [2]
 constexpr uint32_t OFF_BAR = OFF_ITEM + 16;
-constexpr int NBARS = 2 + 2 + 2 + 2 + 1 + 1 + 2 * QS + 2 * DS + 2 * MS + 2 + 2 + 2 + 2 + 1;
+constexpr int NBARS = 2 + 2 + 2 + 2 + 1 + 1 + 2 * QS + 2 * DS + 2 * MS + 2 + 2 + 2 + 1;
 constexpr uint32_t OFF_TMEM = OFF_BAR + NBARS * 8;
 constexpr size_t SMEM_KV2 = 1024 + OFF_TMEM + 16;
 
 struct Bars {
   uint64_t *item_full, *item_empty, *k_full, *k_empty, *v_full, *v_empty, *q_full, *q_empty,
-      *do_full, *do_empty, *meta_full, *meta_empty, *st_full, *p_full, *dpt_full, *ds_full,
+      *do_full, *do_empty, *meta_full, *meta_empty, *st_full, *dpt_full, *ds_full,
       *acc_full;
   __device__ explicit Bars(uint64_t* b) {
     item_full = b; b += 2;
@@ -86,10 +87,9 @@ struct Bars {
     do_empty = b; b += DS;
     meta_full = b; b += MS;
     meta_empty = b; b += MS;
-    st_full = b; b += 2;
-    p_full = b; b += 2;
-    dpt_full = b; b += 2;    // per dP^T buffer
-    ds_full = b; b += 2;     // per dP^T buffer (dS^T written over dP^T)
+    st_full = b; b += 2;     // per score buffer: S^T landed
+    dpt_full = b; b += 2;    // per score buffer: dP^T landed
+    ds_full = b; b += 2;     // per score buffer: P^T and dS^T written back
     acc_full = b; b += 1;
   }
 };
@@ -159,10 +159,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
     for (int i = 0; i < 2; ++i) {
       mbar_init(&B.k_full[i], 1);
       mbar_init(&B.k_empty[i], 1);
-      // S^T is two steps ahead, so a fast warp may reach step i + 1 before a slow
-      // one arrives for step i (never step i + 2): one P^T barrier per S^T buffer
       mbar_init(&B.st_full[i], 1);
-      mbar_init(&B.p_full[i], kComputeWarps);
     }
     mbar_init(B.v_full, 1);
     mbar_init(B.v_empty, 1);
@@ -178,8 +175,8 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
       mbar_init(&B.meta_full[i], 32);
       mbar_init(&B.meta_empty[i], kComputeWarps);
     }
-    // like S^T / P^T: one dP^T / dS^T barrier pair per buffer, because dP^T runs
-    // ahead of the compute warps' dS^T
+    // the scores run two steps ahead, so a fast warp may reach step i + 1 before a
+    // slow one arrives for step i (never step i + 2): one barrier set per buffer
     for (int i = 0; i < 2; ++i) {
       mbar_init(&B.dpt_full[i], 1);
       mbar_init(&B.ds_full[i], kComputeWarps);
@@ -332,10 +329,12 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
           tc_fence_after();
           ok = issue_dpt(gs);
         }
+        if (ok && it.n > 1) ok = issue_dpt(gs + 1);
         for (int i = 0; i < it.n && ok; ++i) {
           const int gi = gs + i, b = gi & 1;
           const uint32_t acc = i > 0 ? 1u : 0u;
-          if (!mbar_wait(&B.p_full[b], (gi >> 1) & 1, status, 348)) { ok = false; break; }
+          // P^T(i) and dS^T(i) written by every compute warp
+          if (!mbar_wait(&B.ds_full[b], (gi >> 1) & 1, status, 348)) { ok = false; break; }
           tc_fence_after();
           const uint32_t do_base = smem_u32(smem + OFF_DO + (gi % DS) * SUB_BYTES);
 #pragma unroll
@@ -344,20 +343,17 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
                         sw128_desc(do_base + kk * 2048, SUB_CHUNK, 1024), ID_KM,
                         (acc | kk) != 0 ? 1u : 0u);
           mma_commit(&B.do_empty[gi % DS]);  // dO(gi): dP^T(gi) and dV(gi) issued
-          // dP^T(i+1) into the other buffer, whose dS^T(i-1) dK(i-1) has read
-          // (tcgen05 executes in issue order); it does not wait for dS^T(i)
-          if (i + 1 < it.n && !issue_dpt(gi + 1)) { ok = false; break; }
-          if (!mbar_wait(&B.ds_full[b], (gi >> 1) & 1, status, 349)) { ok = false; break; }
-          tc_fence_after();
           const uint32_t q_base = smem_u32(smem + OFF_Q + (gi % QS) * SUB_BYTES);
 #pragma unroll
           for (int kk = 0; kk < QT / 16; ++kk)
             mma_bf16_ts(tDK, tDP + b * QT + a_col(kk),
                         sw128_desc(q_base + kk * 2048, SUB_CHUNK, 1024), ID_KM,
                         (acc | kk) != 0 ? 1u : 0u);
-          mma_commit(&B.q_empty[gi % QS]);
-          // S^T(i+2) overwrites P^T(i) after dV(i) read it
+          mma_commit(&B.q_empty[gi % QS]);  // Q(gi): S^T(gi) and dK(gi) issued
+          // S^T(i+2) / dP^T(i+2) overwrite P^T(i) / dS^T(i) after dV(i) / dK(i) read
+          // them (tcgen05 executes in issue order)
           if (i + 2 < it.n && !issue_st(gi + 2)) { ok = false; break; }
+          if (i + 2 < it.n && !issue_dpt(gi + 2)) { ok = false; break; }
         }
         if (ok) mma_commit(B.acc_full);
         gs += it.n;
@@ -451,24 +447,29 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
         const int gi = gs + i, slot = gi % MS, b = gi & 1;
         const int q0 = it.qr.at(i) * QT;
         const bool full = tile_fully_allowed(it.g, q0, it.k0, QT);
-        // ---- P^T = 2^(S^T c - lse') ----
+        // ---- P^T = 2^(S^T c - lse') and dS^T = P^T (dP^T - delta): S^T(i) and
+        // dP^T(i) were issued together two steps ahead, so one wait, one pair of TMEM
+        // loads and one pair of stores cover the step ----
         if (!mbar_wait(&B.meta_full[slot], (gi / MS) & 1, status, 351)) { ok = false; break; }
         if (!mbar_wait(&B.st_full[b], (gi >> 1) & 1, status, 352)) { ok = false; break; }
+        if (!mbar_wait(&B.dpt_full[b], (gi >> 1) & 1, status, 353)) { ok = false; break; }
         tc_fence_after();
-        float pv[C];
+        float pv[C], dv[C];
         tmem_ld16(tS + b * QT + lane_off + cb, pv);
+        tmem_ld16(tDP + b * QT + lane_off + cb, dv);
         tmem_wait_ld();
         const float* L = sL + slot * QT + cb;
         if (full) {
 #pragma unroll
           for (int c = 0; c < C; c += 4) {
             const float4 l4 = *reinterpret_cast<const float4*>(L + c);
-            const float2 a = fma2(make_float2(pv[c], pv[c + 1]), sc2, make_float2(l4.x, l4.y));
-            const float2 b = fma2(make_float2(pv[c + 2], pv[c + 3]), sc2, make_float2(l4.z, l4.w));
-            pv[c] = ex2_approx(a.x);
-            pv[c + 1] = ex2_approx(a.y);
-            pv[c + 2] = ex2_approx(b.x);
-            pv[c + 3] = ex2_approx(b.y);
+            const float2 e0 = fma2(make_float2(pv[c], pv[c + 1]), sc2, make_float2(l4.x, l4.y));
+            const float2 e1 =
+                fma2(make_float2(pv[c + 2], pv[c + 3]), sc2, make_float2(l4.z, l4.w));
+            pv[c] = ex2_approx(e0.x);
+            pv[c + 1] = ex2_approx(e0.y);
+            pv[c + 2] = ex2_approx(e1.x);
+            pv[c + 3] = ex2_approx(e1.y);
           }
         } else {
           const int* QA = sA + slot * QT + cb;
@@ -481,37 +482,22 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
             pv[c] = allow ? ex2_approx(fmaf(pv[c], scale_log2, L[c])) : 0.f;
           }
         }
-        {
-          uint32_t pw[C / 2];
-#pragma unroll
-          for (int c = 0; c < C; c += 2) pw[c / 2] = pack_bf16x2(pv[c], pv[c + 1]);
-          tmem_st8(tS + b * QT + lane_off + cb, pw);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&B.p_full[b]);
-        // ---- dS^T = P^T (dP^T - delta) ----
-        if (!mbar_wait(&B.dpt_full[b], (gi >> 1) & 1, status, 353)) { ok = false; break; }
-        tc_fence_after();
-        float dv[C];
-        tmem_ld16(tDP + b * QT + lane_off + cb, dv);
-        tmem_wait_ld();
         const float* D = sD + slot * QT + cb;
-        {
-          uint32_t pw[C / 2];
+        uint32_t pw[C / 2], sw[C / 2];
 #pragma unroll
-          for (int c = 0; c < C; c += 4) {
-            const float4 d4 = *reinterpret_cast<const float4*>(D + c);
-            const float2 a = mul2(make_float2(pv[c], pv[c + 1]),
-                                  add2(make_float2(dv[c], dv[c + 1]), make_float2(d4.x, d4.y)));
-            const float2 b = mul2(make_float2(pv[c + 2], pv[c + 3]),
-                                  add2(make_float2(dv[c + 2], dv[c + 3]), make_float2(d4.z, d4.w)));
-            pw[c / 2] = pack_bf16x2(a.x, a.y);
-            pw[c / 2 + 1] = pack_bf16x2(b.x, b.y);
-          }
-          tmem_st8(tDP + b * QT + lane_off + cb, pw);
+        for (int c = 0; c < C; c += 4) {
+          const float4 d4 = *reinterpret_cast<const float4*>(D + c);
+          const float2 s0 = mul2(make_float2(pv[c], pv[c + 1]),
+                                 add2(make_float2(dv[c], dv[c + 1]), make_float2(d4.x, d4.y)));
+          const float2 s1 = mul2(make_float2(pv[c + 2], pv[c + 3]),
+                                 add2(make_float2(dv[c + 2], dv[c + 3]), make_float2(d4.z, d4.w)));
+          pw[c / 2] = pack_bf16x2(pv[c], pv[c + 1]);
+          pw[c / 2 + 1] = pack_bf16x2(pv[c + 2], pv[c + 3]);
+          sw[c / 2] = pack_bf16x2(s0.x, s0.y);
+          sw[c / 2 + 1] = pack_bf16x2(s1.x, s1.y);
         }
+        tmem_st8(tS + b * QT + lane_off + cb, pw);
+        tmem_st8(tDP + b * QT + lane_off + cb, sw);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
