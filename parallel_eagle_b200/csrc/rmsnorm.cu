@@ -379,6 +379,108 @@ rmsnorm_bwd_tiled_kernel(int64_t rows, int64_t H, const T* __restrict__ dy, int6
   }
 }
 
+// bf16 backward for rows of H = 256 m <= 4096 columns: one warp per row holds the
+// row's dy and x in registers (16-byte chunks; lane l owns columns 8 (32 i + l) ..
+// + 8 of chunk i), so each is read from HBM once and no second pass touches L2;
+// the residual is loaded once the row coefficient is known.  The weight-gradient
+// partial of each warp lives in its own shared-memory row (no atomics) and the
+// block sums its warps' rows at the end.  Four warps per block, two blocks per SM:
+// the row registers cost ~200 per thread.
+constexpr int kRowRegWarps = 4;
+constexpr int kRowRegChunks = 16;
+
+__global__ void __launch_bounds__(kRowRegWarps * 32, 2)
+rmsnorm_bwd_rowreg_kernel(int64_t rows, int H, const __nv_bfloat16* __restrict__ dy,
+                          int64_t lddy, const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                          const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                          __nv_bfloat16* dx, int64_t lddx, const __nv_bfloat16* res,
+                          int64_t ldres, float* __restrict__ dw_partial) {
+  extern __shared__ float sdw[];  // [kRowRegWarps][H] when dw_partial
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nch = H / 256;
+  float* mydw = sdw + (int64_t)warp * H;
+  if (dw_partial)
+    for (int c = lane * 4; c < H; c += 128)
+      *reinterpret_cast<float4*>(mydw + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
+  const int64_t step = (int64_t)gridDim.x * kRowRegWarps;
+  for (int64_t r = (int64_t)blockIdx.x * kRowRegWarps + warp; r < rows; r += step) {
+    const __nv_bfloat16* dyr = dy + r * lddy;
+    const __nv_bfloat16* xr = x + r * ldx;
+    uint4 a[kRowRegChunks], b[kRowRegChunks];
+#pragma unroll
+    for (int i = 0; i < kRowRegChunks; ++i) {
+      if (i < nch) {
+        const int c = (i * 32 + lane) * 8;
+        a[i] = *reinterpret_cast<const uint4*>(dyr + c);
+        b[i] = *reinterpret_cast<const uint4*>(xr + c);
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRowRegChunks; ++i) {
+      if (i < nch) {
+        float fa[8], fb[8], g[8];
+        Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&a[i]), fa);
+        Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&b[i]), fb);
+        Vec<__nv_bfloat16, 8>::load(w + (i * 32 + lane) * 8, g);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += (fa[k] * g[k]) * fb[k];
+      }
+    }
+    s = warp_sum(s);
+    const float rr = rstd[r];
+    const float cf = s * rr * rr * rr / (float)H;
+    uint4 o[kRowRegChunks];
+    if (res) {
+      const __nv_bfloat16* rrow = res + r * ldres;
+#pragma unroll
+      for (int i = 0; i < kRowRegChunks; ++i)
+        if (i < nch) o[i] = *reinterpret_cast<const uint4*>(rrow + (i * 32 + lane) * 8);
+    }
+    __nv_bfloat16* dxr = dx + r * lddx;
+#pragma unroll
+    for (int i = 0; i < kRowRegChunks; ++i) {
+      if (i < nch) {
+        const int c = (i * 32 + lane) * 8;
+        float fa[8], fb[8], g[8], fo[8];
+        Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&a[i]), fa);
+        Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&b[i]), fb);
+        Vec<__nv_bfloat16, 8>::load(w + c, g);
+        if (res) {
+          Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&o[i]), fo);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) fo[k] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) fo[k] += rr * (fa[k] * g[k]) - fb[k] * cf;
+        Vec<__nv_bfloat16, 8>::store(dxr + c, fo);
+        if (dw_partial) {
+          float4* d4 = reinterpret_cast<float4*>(mydw + c);
+          float4 p = d4[0], q = d4[1];
+          p.x += fa[0] * (fb[0] * rr); p.y += fa[1] * (fb[1] * rr);
+          p.z += fa[2] * (fb[2] * rr); p.w += fa[3] * (fb[3] * rr);
+          q.x += fa[4] * (fb[4] * rr); q.y += fa[5] * (fb[5] * rr);
+          q.z += fa[6] * (fb[6] * rr); q.w += fa[7] * (fb[7] * rr);
+          d4[0] = p;
+          d4[1] = q;
+        }
+      }
+    }
+  }
+  if (dw_partial) {
+    __syncthreads();
+    float* out = dw_partial + (int64_t)blockIdx.x * H;
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < kRowRegWarps; ++k) t += sdw[k * H + c];
+      out[c] = t;
+    }
+  }
+}
+
 // out[c] = (acc ? out[c] : 0) + sum_b partial[b, c]; fixed summation order.
 template <typename T>
 __global__ void colsum_kernel(int64_t nblk, int64_t H, const float* __restrict__ partial,
@@ -455,6 +557,18 @@ extern "C" int pe_rmsnorm_bwd(int dtype, int64_t rows, int64_t H, const void* dy
                    (!residual || ldres % 8 == 0) && aligned16(dy) && aligned16(x) &&
                    aligned16(w) && aligned16(dx) && (!residual || aligned16(residual));
   const size_t smem = dw_partial ? (size_t)H * 4 : 0;
+  if (vec && dtype == PE_BF16 && H % 256 == 0 && H <= 256 * kRowRegChunks) {
+    const size_t sm_rr = dw_partial ? (size_t)kRowRegWarps * H * 4 : 0;
+    if (sm_rr > 48 * 1024)
+      PE_CUDA_TRY(cudaFuncSetAttribute(rmsnorm_bwd_rowreg_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_rr));
+    rmsnorm_bwd_rowreg_kernel<<<(unsigned)nblk, kRowRegWarps * 32, sm_rr, as_stream(stream)>>>(
+        rows, (int)H, (const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x, ldx,
+        (const __nv_bfloat16*)w, rstd, (__nv_bfloat16*)dx, lddx,
+        (const __nv_bfloat16*)residual, ldres, dw_partial);
+    PE_LAUNCHED();
+    return PE_OK;
+  }
   if (vec && H <= 8 * 2 * kTiledThreads) {
     return PE_DISPATCH(dtype, T, [&] {
       rmsnorm_bwd_tiled_kernel<T><<<(unsigned)nblk, kTiledThreads, 0, as_stream(stream)>>>(
