@@ -877,7 +877,7 @@ struct SegRows {
 
 // delta (fp32, one [Hq, S_seg] block per segment at element Hq * row0_seg) =
 // sum_d dO * O per (stacked row, head); zero the dQ accumulator row (when given) and,
-// for the first Hkv heads, the dK / dV accumulator rows; zero the work counter.
+// for the first Hkv heads, the dK / dV accumulator rows; zero the two work counters.
 // Sixteen threads per (row, head), each reading 16 bytes of O and of dO.
 __global__ void attn_bwd_prep_kernel(const __grid_constant__ SegRows sr, int Hq, int Hkv,
                                      const __nv_bfloat16* __restrict__ o, int64_t o_ss,
@@ -885,7 +885,7 @@ __global__ void attn_bwd_prep_kernel(const __grid_constant__ SegRows sr, int Hq,
                                      float* __restrict__ delta, float* __restrict__ dq_acc,
                                      float* __restrict__ dk_acc, float* __restrict__ dv_acc,
                                      int* __restrict__ counter) {
-  if (blockIdx.x == 0 && threadIdx.x == 0) *counter = 0;
+  if (blockIdx.x == 0 && threadIdx.x < 2) counter[threadIdx.x] = 0;  // dK/dV, dQ kernels
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t pair = t >> 4;  // (stacked row, head), heads fastest
   const int sub = threadIdx.x & 15;
@@ -1033,7 +1033,7 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
 }
 
 size_t attn_tc_seg_acc_bytes(int64_t rows, int Hkv) {
-  return (size_t)rows * 2 * Hkv * HD * 4 + 256;  // dK, dV accumulators + the work counter
+  return (size_t)rows * 2 * Hkv * HD * 4 + 256;  // dK, dV accumulators + the work counters
 }
 
 int attn_bwd_tc_segments(int nseg, const PartGeom* g, int Hq, int Hkv, const void* q,
@@ -1075,7 +1075,7 @@ int attn_bwd_tc_segments(int nseg, const PartGeom* g, int Hq, int Hkv, const voi
     }
     int rc = attn_bwd_q2_launch(e - b, g + b, Hq, Hkv, at(q, q_ss), q_ss, at(k, k_ss), k_ss,
                                 at(v, v_ss), v_ss, at(dout, do_ss), do_ss, lse_g, delta_g,
-                                at_mut(dq, dq_ss), dq_ss, status, st);
+                                at_mut(dq, dq_ss), dq_ss, counter + 1, status, st);
     if (!rc)
       rc = attn_bwd_kv2_launch(e - b, g + b, Hq, Hkv, at(q, q_ss), q_ss, at(k, k_ss), k_ss,
                                at(v, v_ss), v_ss, at(dout, do_ss), do_ss, lse_g, delta_g, dk_acc,

@@ -2,8 +2,9 @@
 // of reference src/pe/nn.py:84-88 under the mask of src/pe/masks.py:43-61,
 // partition slot layout (src/pe/partition.py:41-55).
 //
-// One CTA = one 128-row query tile of one head, walking the keys the tile reads
-// (the forward's key list) in 64-key steps, query row per TMEM lane:
+// Persistent: one CTA per SM claims units (segment, 128-row query tile, query
+// head) from a global counter in work-list order and walks the keys each unit's
+// tile reads (the forward's key list) in 64-key steps, query row per TMEM lane:
 //   S = Q K^T,  dP = dO V^T                        (N = 64)
 //   dS = P (dP - delta),  P = 2^(S c - lse')      (compute warps; bf16 dS
 //                                                  packed back over S)
@@ -14,10 +15,13 @@
 // MMA needs 96-192 B per clock against a shared-memory bandwidth of 128.  The
 // 64-key step leaves room to double-buffer S and dP (4 x 64 columns), so the
 // MMAs of step j + 1 (and j + 2) run while the compute warps work on step j.
-// At the end dQ is scaled and stored in bf16 straight from TMEM.
+// Across units: the next unit's Q / dO are loaded while the current one runs
+// (the shared-memory copy is free once it is in TMEM), and a unit's dQ is scaled
+// and stored in bf16 straight from TMEM while the next unit's first S / dP run.
 //
 // Warp roles (640 threads):
-//   warp 0      TMA: Q / dO tile once, K / V per step into 4- and 3-deep rings
+//   warp 0      scheduler + TMA: claims units; Q / dO tile per unit, K / V per
+//               step into 4- and 3-deep rings
 //   warp 1      tcgen05.mma issue:  dQ(j), S(j+2), dP(j+2) per step
 //   warps 2, 3  idle
 //   warps 4-19  compute: four per TMEM lane quarter, each owning 16 of the 64
@@ -48,15 +52,18 @@ constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_DO = OFF_Q + TILE_BYTES;
 constexpr uint32_t OFF_K = OFF_DO + TILE_BYTES;
 constexpr uint32_t OFF_V = OFF_K + KS * SUB_BYTES;
-constexpr uint32_t OFF_BAR = OFF_V + VS * SUB_BYTES;
-constexpr int NBARS = 1 + 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
+constexpr uint32_t OFF_ITEM = OFF_V + VS * SUB_BYTES;  // int [2]
+constexpr uint32_t OFF_BAR = OFF_ITEM + 16;
+constexpr int NBARS = 2 + 2 + 1 + 1 + 2 * KS + 2 * VS + 2 + 2 + 2 + 1;
 constexpr uint32_t OFF_TMEM = OFF_BAR + NBARS * 8;
 constexpr size_t SMEM_Q2 = 1024 + OFF_TMEM + 16;
 
 struct Bars {
-  uint64_t *qdo_full, *qdo_copied, *k_full, *k_empty, *v_full, *v_empty, *s_full, *dp_full,
-      *ds_full, *dq_full;
+  uint64_t *item_full, *item_empty, *qdo_full, *qdo_copied, *k_full, *k_empty, *v_full,
+      *v_empty, *s_full, *dp_full, *ds_full, *dq_full;
   __device__ explicit Bars(uint64_t* b) {
+    item_full = b; b += 2;
+    item_empty = b; b += 2;
     qdo_full = b; b += 1;
     qdo_copied = b; b += 1;
     k_full = b; b += KS;
@@ -77,43 +84,49 @@ __device__ __forceinline__ uint32_t a_col(int kk) {
   return (uint32_t)((kk / steps) * kCols + (kk % steps) * 8);
 }
 
+// a work unit (segment, 128-row query tile, query head) and the 64-key steps it walks
+struct Unit {
+  int seg, h, q0, r_end, m_beg, m_end, n;
+  PartGeom g;
+  int64_t r0;  // first stacked row of the segment
+  __device__ Unit(int w, int Hq, const SegTable& tab) {
+    const int e = w / Hq;
+    h = w - e * Hq;
+    int qt;
+    if (tab.nwork > 0) {
+      unpack_work(tab.work[e], seg, qt);
+    } else {  // a lone segment: its last (heaviest) tile first
+      seg = 0;
+      qt = (tab.g[0].S + TQ - 1) / TQ - 1 - e;
+    }
+    g = tab.g[seg];
+    r0 = tab.row0[seg];
+    q0 = qt * TQ;
+    key_tiles(g, q0, r_end, m_beg, m_end, KT);
+    n = r_end + (m_end - m_beg);
+  }
+  __device__ __forceinline__ int key(int j) const {
+    return (j < r_end ? j : m_beg + (j - r_end)) * KT;
+  }
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict__ lse,
                    const float* __restrict__ delta, __nv_bfloat16* __restrict__ dq, int64_t dq_ss,
-                   int Hq, int rep, float scale, int* status) {
+                   int Hq, int rep, float scale, int total, int* work_counter, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   Bars B(reinterpret_cast<uint64_t*>(smem + OFF_BAR));
+  volatile int* sItem = reinterpret_cast<volatile int*>(smem + OFF_ITEM);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // grid (head, unit): blocks dispatch head-fastest, heaviest query tiles first --
-  // stacked segments in the work list's order, a lone segment from its last tile down
-  int sg, qt;
-  if (tab.nwork > 0) {
-    unpack_work(tab.work[blockIdx.y], sg, qt);
-  } else {
-    sg = 0;
-    qt = (tab.g[0].S + TQ - 1) / TQ - 1 - (int)blockIdx.y;
-  }
-  const PartGeom g = tab.g[sg];
-  const CUtensorMap* tmQ = &tab.tm[sg][0];
-  const CUtensorMap* tmK = &tab.tm[sg][1];
-  const CUtensorMap* tmV = &tab.tm[sg][2];
-  const CUtensorMap* tmDO = &tab.tm[sg][3];
-  lse += (int64_t)Hq * tab.row0[sg];
-  delta += (int64_t)Hq * tab.row0[sg];
-  dq += (int64_t)tab.row0[sg] * dq_ss;
-  const int h = blockIdx.x;
-  const int kvh = h / rep;
-  const int q0 = qt * TQ;
-  int r_end, m_beg, m_end;
-  key_tiles(g, q0, r_end, m_beg, m_end, KT);
-  const int n = r_end + (m_end - m_beg);
-  auto step_key = [&](int j) { return (j < r_end ? j : m_beg + (j - r_end)) * KT; };
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B.item_full[i], 1);
+      mbar_init(&B.item_empty[i], 1 + kComputeWarps);  // MMA warp, compute warps
+    }
     mbar_init(B.qdo_full, 1);
     mbar_init(B.qdo_copied, kComputeWarps);
     for (int i = 0; i < KS; ++i) {
@@ -146,87 +159,137 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
   const uint32_t tDQ = tmem, tQ = tmem + 128, tDO = tmem + 192, tS = tmem + 256,
                  tDP = tmem + 384;
 
+  // every role walks the same unit sequence; `ic` counts units, `gs` steps
+  auto read_item = [&](int ic, bool& ok) -> int {
+    if (!mbar_wait(&B.item_full[ic & 1], (ic >> 1) & 1, status, 371)) {
+      ok = false;
+      return -1;
+    }
+    const int w = sItem[ic & 1];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&B.item_empty[ic & 1]);
+    return w;
+  };
+
   if (warp == 0) {
-    // ---------------- TMA ----------------
+    // ---------------- scheduler + TMA ----------------
     if (elect_one()) {
       bool ok = true;
-      uint64_t* last_bar = B.qdo_full;
+      uint64_t* last_bar = nullptr;
       uint32_t last_ph = 0;
-      mbar_arrive_expect_tx(B.qdo_full, 2 * TILE_BYTES);
-      tma_load_2d(smem + OFF_Q, tmQ, B.qdo_full, h * HD, q0);
-      tma_load_2d(smem + OFF_Q + CHUNK, tmQ, B.qdo_full, h * HD + 64, q0);
-      tma_load_2d(smem + OFF_DO, tmDO, B.qdo_full, h * HD, q0);
-      tma_load_2d(smem + OFF_DO + CHUNK, tmDO, B.qdo_full, h * HD + 64, q0);
-      for (int j = 0; j < n && ok; ++j) {
-        const int k0 = step_key(j);
-        const int ks = j % KS, vs = j % VS;
-        if (!mbar_wait(&B.k_empty[ks], ((j / KS) & 1) ^ 1u, status, 360)) { ok = false; break; }
-        uint8_t* kd = smem + OFF_K + ks * SUB_BYTES;
-        mbar_arrive_expect_tx(&B.k_full[ks], SUB_BYTES);
-        tma_load_2d(kd, tmK, &B.k_full[ks], kvh * HD, k0);
-        tma_load_2d(kd + SUB_CHUNK, tmK, &B.k_full[ks], kvh * HD + 64, k0);
-        last_bar = &B.k_full[ks];
-        last_ph = (j / KS) & 1;
-        if (!mbar_wait(&B.v_empty[vs], ((j / VS) & 1) ^ 1u, status, 361)) { ok = false; break; }
-        uint8_t* vd = smem + OFF_V + vs * SUB_BYTES;
-        mbar_arrive_expect_tx(&B.v_full[vs], SUB_BYTES);
-        tma_load_2d(vd, tmV, &B.v_full[vs], kvh * HD, k0);
-        tma_load_2d(vd + SUB_CHUNK, tmV, &B.v_full[vs], kvh * HD + 64, k0);
-        last_bar = &B.v_full[vs];
-        last_ph = (j / VS) & 1;
+      int gs = 0;
+      for (int ic = 0;; ++ic) {
+        int w = atomicAdd(work_counter, 1);
+        if (w >= total) w = -1;
+        if (!mbar_wait(&B.item_empty[ic & 1], ((ic >> 1) & 1) ^ 1u, status, 372)) { ok = false; break; }
+        sItem[ic & 1] = w;
+        mbar_arrive(&B.item_full[ic & 1]);  // release: publishes the slot write
+        if (w < 0) break;
+        const Unit u(w, Hq, tab);
+        const CUtensorMap* tmQ = &tab.tm[u.seg][0];
+        const CUtensorMap* tmK = &tab.tm[u.seg][1];
+        const CUtensorMap* tmV = &tab.tm[u.seg][2];
+        const CUtensorMap* tmDO = &tab.tm[u.seg][3];
+        const int kvh = u.h / rep;
+        // Q / dO once the compute warps copied the previous unit's into TMEM
+        if (!mbar_wait(B.qdo_copied, (ic & 1) ^ 1u, status, 373)) { ok = false; break; }
+        mbar_arrive_expect_tx(B.qdo_full, 2 * TILE_BYTES);
+        tma_load_2d(smem + OFF_Q, tmQ, B.qdo_full, u.h * HD, u.q0);
+        tma_load_2d(smem + OFF_Q + CHUNK, tmQ, B.qdo_full, u.h * HD + 64, u.q0);
+        tma_load_2d(smem + OFF_DO, tmDO, B.qdo_full, u.h * HD, u.q0);
+        tma_load_2d(smem + OFF_DO + CHUNK, tmDO, B.qdo_full, u.h * HD + 64, u.q0);
+        last_bar = B.qdo_full;
+        last_ph = ic & 1;
+        for (int j = 0; j < u.n && ok; ++j) {
+          const int gj = gs + j, k0 = u.key(j);
+          const int ks = gj % KS, vs = gj % VS;
+          if (!mbar_wait(&B.k_empty[ks], ((gj / KS) & 1) ^ 1u, status, 360)) { ok = false; break; }
+          uint8_t* kd = smem + OFF_K + ks * SUB_BYTES;
+          mbar_arrive_expect_tx(&B.k_full[ks], SUB_BYTES);
+          tma_load_2d(kd, tmK, &B.k_full[ks], kvh * HD, k0);
+          tma_load_2d(kd + SUB_CHUNK, tmK, &B.k_full[ks], kvh * HD + 64, k0);
+          last_bar = &B.k_full[ks];
+          last_ph = (gj / KS) & 1;
+          if (!mbar_wait(&B.v_empty[vs], ((gj / VS) & 1) ^ 1u, status, 361)) { ok = false; break; }
+          uint8_t* vd = smem + OFF_V + vs * SUB_BYTES;
+          mbar_arrive_expect_tx(&B.v_full[vs], SUB_BYTES);
+          tma_load_2d(vd, tmV, &B.v_full[vs], kvh * HD, k0);
+          tma_load_2d(vd + SUB_CHUNK, tmV, &B.v_full[vs], kvh * HD + 64, k0);
+          last_bar = &B.v_full[vs];
+          last_ph = (gj / VS) & 1;
+        }
+        if (!ok) break;
+        gs += u.n;
       }
-      // let the last copy land before the CTA can exit
-      mbar_wait(last_bar, last_ph, ok ? status : nullptr, 362);
+      // on a failed wait, let this thread's last copy land before the CTA exits
+      if (!ok && last_bar) mbar_wait(last_bar, last_ph, nullptr, 0);
     }
   } else if (warp == 1) {
     // ---------------- MMA issue ----------------
-    if (elect_one()) {
-      constexpr uint32_t ID_SP = idesc_bf16(TQ, KT, false, false);  // S, dP (A = Q / dO)
-      constexpr uint32_t ID_DQ = idesc_bf16(TQ, HD, false, true);   // dQ += dS K
-      // S(j) = Q K(j)^T and dP(j) = dO V(j)^T into buffers j & 1
-      auto issue_scores = [&](int j) -> bool {
-        const int ks = j % KS, vs = j % VS, b = j & 1;
-        if (!mbar_wait(&B.k_full[ks], (j / KS) & 1, status, 363)) return false;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(smem + OFF_K + ks * SUB_BYTES);
+    constexpr uint32_t ID_SP = idesc_bf16(TQ, KT, false, false);  // S, dP (A = Q / dO)
+    constexpr uint32_t ID_DQ = idesc_bf16(TQ, HD, false, true);   // dQ += dS K
+    bool ok = true;
+    int gs = 0;
+    for (int ic = 0; ok; ++ic) {
+      const int w = read_item(ic, ok);
+      if (w < 0) break;
+      const bool leader = elect_one();
+      const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
+      if (leader) {
+        const Unit u(w, Hq, tab);
+        // S(gj) = Q K(gj)^T and dP(gj) = dO V(gj)^T into buffers gj & 1
+        auto issue_scores = [&](int gj) -> bool {
+          const int ks = gj % KS, vs = gj % VS, b = gj & 1;
+          if (!mbar_wait(&B.k_full[ks], (gj / KS) & 1, status, 363)) return false;
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(smem + OFF_K + ks * SUB_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk)
-          mma_bf16_ts(tS + b * KT, tQ + kk * 8,
-                      sw128_desc(k_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024), ID_SP,
-                      kk > 0 ? 1u : 0u);
-        mma_commit(&B.s_full[b]);
-        if (!mbar_wait(&B.v_full[vs], (j / VS) & 1, status, 364)) return false;
-        tc_fence_after();
-        const uint32_t v_base = smem_u32(smem + OFF_V + vs * SUB_BYTES);
+          for (int kk = 0; kk < HD / 16; ++kk)
+            mma_bf16_ts(tS + b * KT, tQ + kk * 8,
+                        sw128_desc(k_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024),
+                        ID_SP, kk > 0 ? 1u : 0u);
+          mma_commit(&B.s_full[b]);
+          if (!mbar_wait(&B.v_full[vs], (gj / VS) & 1, status, 364)) return false;
+          tc_fence_after();
+          const uint32_t v_base = smem_u32(smem + OFF_V + vs * SUB_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk)
-          mma_bf16_ts(tDP + b * KT, tDO + kk * 8,
-                      sw128_desc(v_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024), ID_SP,
-                      kk > 0 ? 1u : 0u);
-        mma_commit(&B.dp_full[b]);
-        mma_commit(&B.v_empty[vs]);  // V(j) has no other reader
-        return true;
-      };
-      bool ok = mbar_wait(B.qdo_copied, 0, status, 365);
-      if (ok) {
-        tc_fence_after();
-        for (int j = 0; j < 2 && j < n && ok; ++j) ok = issue_scores(j);
+          for (int kk = 0; kk < HD / 16; ++kk)
+            mma_bf16_ts(tDP + b * KT, tDO + kk * 8,
+                        sw128_desc(v_base + (kk >> 2) * SUB_CHUNK + (kk & 3) * 32, 16, 1024),
+                        ID_SP, kk > 0 ? 1u : 0u);
+          mma_commit(&B.dp_full[b]);
+          mma_commit(&B.v_empty[vs]);  // V(gj) has no other reader
+          return true;
+        };
+        // this unit's Q / dO in TMEM (the S / dP buffers it overwrites were read by
+        // the previous unit's dQ MMAs, issued before)
+        ok = mbar_wait(B.qdo_copied, ic & 1, status, 365);
+        if (ok) {
+          tc_fence_after();
+          for (int j = 0; j < 2 && j < u.n && ok; ++j) ok = issue_scores(gs + j);
+        }
+        for (int j = 0; j < u.n && ok; ++j) {
+          const int gj = gs + j, b = gj & 1, ks = gj % KS;
+          // dS(gj) from every compute warp; each drained the previous unit's dQ first,
+          // so the unit's first dQ MMA (which overwrites the accumulator) may go
+          if (!mbar_wait(&B.ds_full[b], (gj >> 1) & 1, status, 366)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(smem + OFF_K + ks * SUB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < KT / 16; ++kk)
+            mma_bf16_ts(tDQ, tS + b * KT + a_col(kk),
+                        sw128_desc(k_base + kk * 2048, SUB_CHUNK, 1024), ID_DQ,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&B.k_empty[ks]);
+          // S(j+2) / dP(j+2) overwrite buffer b after dQ(j) read dS(j) (in order)
+          if (j + 2 < u.n && !issue_scores(gj + 2)) { ok = false; break; }
+        }
+        if (ok) mma_commit(B.dq_full);
+        gs += u.n;
       }
-      for (int j = 0; j < n && ok; ++j) {
-        const int b = j & 1, ks = j % KS;
-        if (!mbar_wait(&B.ds_full[b], (j >> 1) & 1, status, 366)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(smem + OFF_K + ks * SUB_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < KT / 16; ++kk)
-          mma_bf16_ts(tDQ, tS + b * KT + a_col(kk),
-                      sw128_desc(k_base + kk * 2048, SUB_CHUNK, 1024), ID_DQ,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&B.k_empty[ks]);
-        // S(j+2) / dP(j+2) overwrite buffer b after dQ(j) read dS(j) (in order)
-        if (j + 2 < n && !issue_scores(j + 2)) { ok = false; break; }
-      }
-      if (ok) mma_commit(B.dq_full);
+      __syncwarp();
+      ok = __shfl_sync(0xffffffffu, ok, leader_lane);
+      gs = __shfl_sync(0xffffffffu, gs, leader_lane);
     }
   } else if (warp >= 4) {
     // ---------------- compute: thread = query row (TMEM lane) ----------------
@@ -236,101 +299,121 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
     const int cb = part * C;
     const int row = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int s = q0 + row;
-    const bool valid = s < g.S;
-    int qi = -1, qd = 0;
-    float l2 = 0.f, dl = 0.f;
-    if (valid) {
-      decode(g, s, qi, qd);
-      l2 = lse[(int64_t)h * g.S + s] * kLog2e;
-      dl = delta[(int64_t)h * g.S + s];
-    }
-    const int lo = qd > 0 ? g.a1 + (qi - g.a0) * g.km1 : 0;
     const float scale_log2 = scale * kLog2e;
-    const float2 sc2 = make_float2(scale_log2, scale_log2), nl2 = make_float2(-l2, -l2),
-                 ndl2 = make_float2(-dl, -dl);
-    bool ok = mbar_wait(B.qdo_full, 0, status, 367);
-    if (ok) {
-      // one 64-column half of the Q (parts 0, 1) or dO (parts 2, 3) row -> TMEM as
-      // bf16 pairs (A operand)
-      const int ch = part & 1;
-      const uint8_t* src = smem + (part < 2 ? OFF_Q : OFF_DO) + ch * CHUNK;
-      uint32_t r32[32];
+    const float2 sc2 = make_float2(scale_log2, scale_log2);
+    bool ok = true;
+    int gs = 0;
+    // the previous unit's dQ row (this part's 32 head dims), written once that
+    // unit's last dQ MMA completed
+    __nv_bfloat16* pending = nullptr;
+    bool have_pending = false;
+    auto drain = [&](int ic_prev) -> bool {
+      if (!mbar_wait(B.dq_full, ic_prev & 1, status, 370)) return false;
+      tc_fence_after();
+      float v[32];
+      tmem_ld32(tDQ + lane_off + part * 32, v);
+      tmem_wait_ld();
+      if (pending) {
+        uint4* dst = reinterpret_cast<uint4*>(pending);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint4 x = *reinterpret_cast<const uint4*>(src + swz(row, u));
-        r32[u * 4 + 0] = x.x;
-        r32[u * 4 + 1] = x.y;
-        r32[u * 4 + 2] = x.z;
-        r32[u * 4 + 3] = x.w;
+        for (int u = 0; u < 4; ++u)
+          dst[u] = make_uint4(pack_bf16x2(v[8 * u] * scale, v[8 * u + 1] * scale),
+                              pack_bf16x2(v[8 * u + 2] * scale, v[8 * u + 3] * scale),
+                              pack_bf16x2(v[8 * u + 4] * scale, v[8 * u + 5] * scale),
+                              pack_bf16x2(v[8 * u + 6] * scale, v[8 * u + 7] * scale));
       }
-      tmem_st32((part < 2 ? tQ : tDO) + lane_off + ch * 32, r32);
-      tmem_wait_st();
+      return true;
+    };
+    int ic = 0;
+    for (; ok; ++ic) {
+      const int w = read_item(ic, ok);
+      if (w < 0) break;
+      const Unit u(w, Hq, tab);
+      // ---- this unit's Q (parts 0, 1) or dO (parts 2, 3) half row -> TMEM as bf16
+      // pairs (A operand).  The previous unit's S / dP MMAs, which read the old
+      // copy, have all completed: this warp waited for its last dP. ----
+      if (!mbar_wait(B.qdo_full, ic & 1, status, 367)) { ok = false; break; }
+      {
+        const int ch = part & 1;
+        const uint8_t* src = smem + (part < 2 ? OFF_Q : OFF_DO) + ch * CHUNK;
+        uint32_t r32[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 x = *reinterpret_cast<const uint4*>(src + swz(row, q));
+          r32[q * 4 + 0] = x.x;
+          r32[q * 4 + 1] = x.y;
+          r32[q * 4 + 2] = x.z;
+          r32[q * 4 + 3] = x.w;
+        }
+        tmem_st32((part < 2 ? tQ : tDO) + lane_off + ch * 32, r32);
+        tmem_wait_st();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(B.qdo_copied);
-    }
-    for (int j = 0; j < n && ok; ++j) {
-      const int b = j & 1;
-      const int k0 = step_key(j) + cb;
-      if (!mbar_wait(&B.s_full[b], (j >> 1) & 1, status, 368)) { ok = false; break; }
-      tc_fence_after();
-      float sv[C];
-      tmem_ld16(tS + b * KT + lane_off + cb, sv);
-      tmem_wait_ld();
-      // P = 2^(S c - lse') (masked pairs exactly 0)
-      if (k0 + C - 1 <= qi) {  // every key of this warp's slice is real and <= the anchor
+      // ---- the previous unit's dQ, while this unit's first S / dP run ----
+      if (have_pending && !drain(ic - 1)) { ok = false; break; }
+      const int s = u.q0 + row;
+      const bool valid = s < u.g.S;
+      int qi = -1, qd = 0;
+      float l2 = 0.f, dl = 0.f;
+      if (valid) {
+        const int64_t li = (int64_t)Hq * u.r0 + (int64_t)u.h * u.g.S + s;
+        decode(u.g, s, qi, qd);
+        l2 = lse[li] * kLog2e;
+        dl = delta[li];
+      }
+      const int lo = qd > 0 ? u.g.a1 + (qi - u.g.a0) * u.g.km1 : 0;
+      const float2 nl2 = make_float2(-l2, -l2), ndl2 = make_float2(-dl, -dl);
+      pending = valid ? dq + (u.r0 + s) * dq_ss + u.h * HD + part * 32 : nullptr;
+      have_pending = true;
+      for (int j = 0; j < u.n; ++j) {
+        const int gj = gs + j, b = gj & 1;
+        const int k0 = u.key(j) + cb;
+        if (!mbar_wait(&B.s_full[b], (gj >> 1) & 1, status, 368)) { ok = false; break; }
+        tc_fence_after();
+        float sv[C];
+        tmem_ld16(tS + b * KT + lane_off + cb, sv);
+        tmem_wait_ld();
+        // P = 2^(S c - lse') (masked pairs exactly 0)
+        if (k0 + C - 1 <= qi) {  // every key of this warp's slice is real and <= the anchor
+#pragma unroll
+          for (int c = 0; c < C; c += 2) {
+            const float2 a = fma2(make_float2(sv[c], sv[c + 1]), sc2, nl2);
+            sv[c] = ex2_approx(a.x);
+            sv[c + 1] = ex2_approx(a.y);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            const int ks = k0 + c;
+            const bool allow = ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
+            sv[c] = allow ? ex2_approx(fmaf(sv[c], scale_log2, -l2)) : 0.f;
+          }
+        }
+        if (!mbar_wait(&B.dp_full[b], (gj >> 1) & 1, status, 369)) { ok = false; break; }
+        tc_fence_after();
+        float dv[C];
+        tmem_ld16(tDP + b * KT + lane_off + cb, dv);
+        tmem_wait_ld();
+        uint32_t pw[C / 2];
 #pragma unroll
         for (int c = 0; c < C; c += 2) {
-          const float2 a = fma2(make_float2(sv[c], sv[c + 1]), sc2, nl2);
-          sv[c] = ex2_approx(a.x);
-          sv[c + 1] = ex2_approx(a.y);
+          const float2 a =
+              mul2(make_float2(sv[c], sv[c + 1]), add2(make_float2(dv[c], dv[c + 1]), ndl2));
+          pw[c / 2] = pack_bf16x2(a.x, a.y);
         }
-      } else {
-#pragma unroll
-        for (int c = 0; c < C; ++c) {
-          const int ks = k0 + c;
-          const bool allow = ks <= qi || (unsigned)(ks - lo) < (unsigned)qd;
-          sv[c] = allow ? ex2_approx(fmaf(sv[c], scale_log2, -l2)) : 0.f;
-        }
+        tmem_st8(tS + b * KT + lane_off + cb, pw);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B.ds_full[b]);
       }
-      if (!mbar_wait(&B.dp_full[b], (j >> 1) & 1, status, 369)) { ok = false; break; }
-      tc_fence_after();
-      float dv[C];
-      tmem_ld16(tDP + b * KT + lane_off + cb, dv);
-      tmem_wait_ld();
-      uint32_t pw[C / 2];
-#pragma unroll
-      for (int c = 0; c < C; c += 2) {
-        const float2 a =
-            mul2(make_float2(sv[c], sv[c + 1]), add2(make_float2(dv[c], dv[c + 1]), ndl2));
-        pw[c / 2] = pack_bf16x2(a.x, a.y);
-      }
-      tmem_st8(tS + b * KT + lane_off + cb, pw);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B.ds_full[b]);
+      if (!ok) break;
+      gs += u.n;
     }
-    // dQ (query row per lane): part p stores head dims [32 p, 32 p + 32)
-    if (ok && n > 0 && mbar_wait(B.dq_full, 0, status, 370)) {
-      tc_fence_after();
-#pragma unroll 1
-      for (int c = part * 32; c < part * 32 + 32; c += 32) {
-        float v[32];
-        tmem_ld32(tDQ + lane_off + c, v);
-        tmem_wait_ld();
-        if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(dq + (int64_t)s * dq_ss + h * HD + c);
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            dst[u] = make_uint4(pack_bf16x2(v[8 * u] * scale, v[8 * u + 1] * scale),
-                                pack_bf16x2(v[8 * u + 2] * scale, v[8 * u + 3] * scale),
-                                pack_bf16x2(v[8 * u + 4] * scale, v[8 * u + 5] * scale),
-                                pack_bf16x2(v[8 * u + 6] * scale, v[8 * u + 7] * scale));
-        }
-      }
-    }
+    // the last unit's dQ
+    if (ok && have_pending) drain(ic - 1);
   }
 
   tc_fence_before();
@@ -346,7 +429,8 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
 int attn_bwd_q2_launch(int nseg, const PartGeom* g, int Hq, int Hkv, const void* q,
                        int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
                        const void* dout, int64_t do_ss, const float* lse, const float* delta,
-                       void* dq, int64_t dq_ss, int* status, cudaStream_t st) {
+                       void* dq, int64_t dq_ss, int* work_counter, int* status,
+                       cudaStream_t st) {
   PE_CHECK_ARG(nseg >= 1 && nseg <= kMaxSeg, "attention backward: bad segment count");
   SegTable tab;
   memset(&tab, 0, sizeof(tab));
@@ -372,14 +456,16 @@ int attn_bwd_q2_launch(int nseg, const PartGeom* g, int Hq, int Hkv, const void*
   };
   int rc = seg_table_order(tab, [](const PartGeom& sg) { return seg_tiles(sg); }, cost);
   if (rc) return rc;
-  const int ny = tab.nwork > 0 ? tab.nwork : max_units;
-  PE_CHECK_ARG(ny <= 65535, "attention backward: too many query tiles for one launch");
+  // units: (work-list entry or, for a lone segment, query tile) x query head,
+  // claimed from *work_counter by one persistent CTA per SM
+  const int64_t units = (int64_t)Hq * (tab.nwork > 0 ? tab.nwork : max_units);
+  PE_CHECK_ARG(units < (1ll << 31), "attention backward: too many query tiles");
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_q2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)SMEM_Q2));
-  dim3 grid((unsigned)Hq, (unsigned)ny);
+  const int grid = (int)(units < sm_count() ? units : sm_count());
   attn_bwd_q2_kernel<<<grid, kThreads, SMEM_Q2, st>>>(tab, lse, delta, (__nv_bfloat16*)dq, dq_ss,
                                                       Hq, Hq / Hkv, 1.0f / sqrtf((float)HD),
-                                                      status);
+                                                      (int)units, work_counter, status);
   PE_LAUNCHED();
   return PE_OK;
 }
