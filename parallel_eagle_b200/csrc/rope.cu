@@ -80,55 +80,92 @@ __global__ void rope_rowpair_kernel(int64_t rows, int heads, int hd, T* x, int64
   }
 }
 
+// rotate 8 consecutive pairs (a: first half-row, b: second) in place
+__device__ __forceinline__ void rot8(uint4& ua, uint4& ub, const float* cs, const float* sn,
+                                     int inverse) {
+  using T = __nv_bfloat16;
+  __nv_bfloat162* a2 = reinterpret_cast<__nv_bfloat162*>(&ua);
+  __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&ub);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 a = __bfloat1622float2(a2[i]), b = __bfloat1622float2(b2[i]);
+    const float c0 = cs[2 * i], c1 = cs[2 * i + 1], s0 = sn[2 * i], s1 = sn[2 * i + 1];
+    float ya0, ya1, yb0, yb1;
+    if (!inverse) {
+      ya0 = round_to<T>(round_to<T>(a.x * c0) + round_to<T>(-b.x * s0));
+      ya1 = round_to<T>(round_to<T>(a.y * c1) + round_to<T>(-b.y * s1));
+      yb0 = round_to<T>(round_to<T>(b.x * c0) + round_to<T>(a.x * s0));
+      yb1 = round_to<T>(round_to<T>(b.y * c1) + round_to<T>(a.y * s1));
+    } else {
+      ya0 = round_to<T>(round_to<T>(a.x * c0) + round_to<T>(b.x * s0));
+      ya1 = round_to<T>(round_to<T>(a.y * c1) + round_to<T>(b.y * s1));
+      yb0 = round_to<T>(round_to<T>(b.x * c0) - round_to<T>(a.x * s0));
+      yb1 = round_to<T>(round_to<T>(b.y * c1) - round_to<T>(a.y * s1));
+    }
+    a2[i] = __floats2bfloat162_rn(ya0, ya1);
+    b2[i] = __floats2bfloat162_rn(yb0, yb1);
+  }
+}
+
 // bf16, half-width a multiple of 8: one thread per (row, 8 consecutive pairs); the
-// 8 angles' cos / sin once, then every head's two 16-byte half-row segments.
+// block's inverse frequencies once in shared memory, the 8 angles' cos / sin once
+// per thread, then every head's two 16-byte half-row segments, four heads' loads
+// in flight before their rotations and stores.
 __global__ void rope_vec8_kernel(int64_t rows, int heads, int hd, __nv_bfloat16* x, int64_t ldx,
                                  const int64_t* __restrict__ pos, float theta, int inverse) {
   using T = __nv_bfloat16;
+  constexpr int kBatch = 4;
+  extern __shared__ float s_inv_freq[];  // [hd / 2], the same powf as per element
   const int half = hd >> 1;
   const int groups = half >> 3;
+  for (int p = threadIdx.x; p < half; p += blockDim.x)
+    s_inv_freq[p] = 1.0f / powf(theta, (float)(2 * p) / (float)hd);
+  __syncthreads();
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * groups) return;
   const int64_t row = idx / groups;
   const int p0 = (int)(idx - row * groups) * 8;
+  T* base = x + row * ldx + p0;
+  // the first batch's loads go out before the angle arithmetic
+  uint4 ua[kBatch], ub[kBatch];
+  const int nb = heads < kBatch ? heads : kBatch;
+#pragma unroll
+  for (int q = 0; q < kBatch; ++q) {
+    if (q < nb) {
+      ua[q] = *reinterpret_cast<const uint4*>(base + (int64_t)q * hd);
+      ub[q] = *reinterpret_cast<const uint4*>(base + (int64_t)q * hd + half);
+    }
+  }
   const float pr = (float)pos[row];
   float cs[8], sn[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const float inv_freq = 1.0f / powf(theta, (float)(2 * (p0 + k)) / (float)hd);
     float sv, cv;
-    sincosf(pr * inv_freq, &sv, &cv);
+    sincosf(pr * s_inv_freq[p0 + k], &sv, &cv);
     cs[k] = round_to<T>(cv);
     sn[k] = round_to<T>(sv);
   }
-  T* base = x + row * ldx + p0;
-  for (int h = 0; h < heads; ++h) {
-    T* hp = base + (int64_t)h * hd;
-    uint4 ua = *reinterpret_cast<const uint4*>(hp);
-    uint4 ub = *reinterpret_cast<const uint4*>(hp + half);
-    __nv_bfloat162* a2 = reinterpret_cast<__nv_bfloat162*>(&ua);
-    __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&ub);
+  for (int h = 0; h < heads; h += kBatch) {
+    const int n = heads - h < kBatch ? heads - h : kBatch;
+    if (h > 0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 a = __bfloat1622float2(a2[i]), b = __bfloat1622float2(b2[i]);
-      const float c0 = cs[2 * i], c1 = cs[2 * i + 1], s0 = sn[2 * i], s1 = sn[2 * i + 1];
-      float ya0, ya1, yb0, yb1;
-      if (!inverse) {
-        ya0 = round_to<T>(round_to<T>(a.x * c0) + round_to<T>(-b.x * s0));
-        ya1 = round_to<T>(round_to<T>(a.y * c1) + round_to<T>(-b.y * s1));
-        yb0 = round_to<T>(round_to<T>(b.x * c0) + round_to<T>(a.x * s0));
-        yb1 = round_to<T>(round_to<T>(b.y * c1) + round_to<T>(a.y * s1));
-      } else {
-        ya0 = round_to<T>(round_to<T>(a.x * c0) + round_to<T>(b.x * s0));
-        ya1 = round_to<T>(round_to<T>(a.y * c1) + round_to<T>(b.y * s1));
-        yb0 = round_to<T>(round_to<T>(b.x * c0) - round_to<T>(a.x * s0));
-        yb1 = round_to<T>(round_to<T>(b.y * c1) - round_to<T>(a.y * s1));
+      for (int q = 0; q < kBatch; ++q) {
+        if (q < n) {
+          const T* hp = base + (int64_t)(h + q) * hd;
+          ua[q] = *reinterpret_cast<const uint4*>(hp);
+          ub[q] = *reinterpret_cast<const uint4*>(hp + half);
+        }
       }
-      a2[i] = __floats2bfloat162_rn(ya0, ya1);
-      b2[i] = __floats2bfloat162_rn(yb0, yb1);
     }
-    *reinterpret_cast<uint4*>(hp) = ua;
-    *reinterpret_cast<uint4*>(hp + half) = ub;
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      if (q < n) {
+        rot8(ua[q], ub[q], cs, sn, inverse);
+        T* hp = base + (int64_t)(h + q) * hd;
+        *reinterpret_cast<uint4*>(hp) = ua[q];
+        *reinterpret_cast<uint4*>(hp + half) = ub[q];
+      }
+    }
   }
 }
 
@@ -148,7 +185,8 @@ extern "C" int pe_rope(int dtype, int64_t rows, int heads, int head_dim, void* x
                     (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
   if (vec8) {
     const int64_t total = rows * (head_dim / 16);
-    rope_vec8_kernel<<<(unsigned)ceil_div(total, threads), threads, 0, as_stream(stream)>>>(
+    rope_vec8_kernel<<<(unsigned)ceil_div(total, threads), threads,
+                       (size_t)(head_dim / 2) * sizeof(float), as_stream(stream)>>>(
         rows, heads, head_dim, (__nv_bfloat16*)x, ldx, pos, theta, inverse);
     PE_LAUNCHED();
     return PE_OK;
