@@ -479,6 +479,28 @@ def time_case(run, reps, warmup=3, flush=None):
     return sum(times) / len(times)
 
 
+def time_case_graph(run, reps, warmup=3):
+    """Average milliseconds per call of ``run``, captured ``reps`` times into one CUDA
+    graph and replayed (CUDA events on the current stream): device time without the
+    host's per-call launch overhead."""
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            run()
+    g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    g.replay()
+    b.record(s)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
 def profiled_traffic(name):
     """DRAM bytes per launch recorded from an ncu capture in profiles/<name>
     (the ``traffic_bytes_per_launch:`` line), or None."""
@@ -578,7 +600,9 @@ def run_kernel(args):
         hbm, _, _, src = _peaks()
         out = {}
         for name, (run, nbytes) in elementwise_cases(c, dev).items():
-            ms = time_case(run, args.steps, warmup=args.warmup)
+            # tens of microseconds per launch: replay a captured CUDA graph so the
+            # host's per-call overhead does not pace the device
+            ms = time_case_graph(run, args.steps, warmup=args.warmup)
             gbs = nbytes / (ms / 1e3) / 1e9
             out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
                          "frac_of_hbm": round(gbs / hbm, 3)}
