@@ -154,6 +154,47 @@ __global__ void move_rows_kernel(int64_t rows, int64_t H, const int64_t* __restr
     dst[d_row * ldd + c] = src[s_row * lds + c];
 }
 
+// Row moves in 16-byte units (rows whose bytes and strides are multiples of 16):
+// dst row d(r) = src row s(r) with mode 0 gather (s = idx[r], d = r), 1 scatter
+// (s = r, d = idx[r]), 2 broadcast (s = 0, the source stride 0).  Thread = one
+// 16-byte unit of a row; blockIdx.y walks the rows.
+__global__ void move_rows16_kernel(int64_t rows, int n16, const int64_t* __restrict__ idx,
+                                   const uint4* __restrict__ src, int64_t lds16,
+                                   uint4* __restrict__ dst, int64_t ldd16, int mode) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n16) return;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const int64_t s = mode == 0 ? idx[r] : (mode == 1 ? r : 0);
+    const int64_t d = mode == 1 ? idx[r] : r;
+    dst[d * ldd16 + c] = src[s * lds16 + c];
+  }
+}
+
+// true (and the 16-byte row geometry filled in) when every row start is 16-byte aligned
+bool rows16(int64_t H, size_t es, const void* a, int64_t lda, const void* b, int64_t ldb,
+            int& n16, int64_t& lda16, int64_t& ldb16) {
+  const int64_t bytes = H * (int64_t)es;
+  if (bytes % 16 || (lda * (int64_t)es) % 16 || (ldb * (int64_t)es) % 16 ||
+      (reinterpret_cast<uintptr_t>(a) & 15u) || (reinterpret_cast<uintptr_t>(b) & 15u) ||
+      bytes / 16 > (1 << 30))
+    return false;
+  n16 = (int)(bytes / 16);
+  lda16 = lda * (int64_t)es / 16;
+  ldb16 = ldb * (int64_t)es / 16;
+  return true;
+}
+
+int launch_rows16(int64_t rows, int n16, const int64_t* idx, const void* src, int64_t lds16,
+                  void* dst, int64_t ldd16, int mode, cudaStream_t st) {
+  constexpr int kT = 128;
+  dim3 grid((unsigned)ceil_div((int64_t)n16, (int64_t)kT),
+            (unsigned)(rows < 32768 ? rows : 32768));
+  move_rows16_kernel<<<grid, kT, 0, st>>>(rows, n16, idx, static_cast<const uint4*>(src), lds16,
+                                          static_cast<uint4*>(dst), ldd16, mode);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
 template <typename T>
 __global__ void cast_kernel(int64_t n, const float* __restrict__ x, T* __restrict__ y) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -177,6 +218,13 @@ extern "C" int pe_embed_rows(int dtype, int64_t rows, int64_t H, const int64_t* 
                              const void* embed, void* out, int64_t ldo, void* stream) {
   PE_CHECK_ARG(rows >= 0 && H > 0 && ldo >= H, "embed_rows: bad shape");
   if (rows == 0) return PE_OK;
+  {
+    int n16;
+    int64_t le16, lo16;
+    if ((dtype == PE_F32 || dtype == PE_BF16) &&
+        rows16(H, dtype == PE_F32 ? 4 : 2, embed, H, out, ldo, n16, le16, lo16))
+      return launch_rows16(rows, n16, ids, embed, le16, out, lo16, 0, as_stream(stream));
+  }
   PE_CHECK_ARG(rows <= 65535, "embed_rows: rows > 65535");
   dim3 grid((unsigned)ceil_div(H, 256 * 4), (unsigned)rows);
   return PE_DISPATCH(dtype, T, [&] {
@@ -191,6 +239,13 @@ extern "C" int pe_fill_rows(int dtype, int64_t rows, int64_t H, const void* vec,
                             int64_t ldo, void* stream) {
   PE_CHECK_ARG(rows >= 0 && H > 0 && ldo >= H, "fill_rows: bad shape");
   if (rows == 0) return PE_OK;
+  {
+    int n16;
+    int64_t lv16, lo16;
+    if ((dtype == PE_F32 || dtype == PE_BF16) &&
+        rows16(H, dtype == PE_F32 ? 4 : 2, vec, 0, out, ldo, n16, lv16, lo16))
+      return launch_rows16(rows, n16, nullptr, vec, 0, out, lo16, 2, as_stream(stream));
+  }
   return PE_DISPATCH(dtype, T, [&] {
     fill_rows_kernel<T><<<grid_for(rows * H, 256), 256, 0, as_stream(stream)>>>(
         rows, H, (const T*)vec, (T*)out, ldo);
@@ -256,6 +311,14 @@ static int move_rows(int dtype, int64_t rows, int64_t H, const int64_t* idx, con
                      int64_t lds, void* dst, int64_t ldd, int scatter, void* stream) {
   PE_CHECK_ARG(rows >= 0 && H > 0 && lds >= H && ldd >= H, "scatter/gather rows: bad shape");
   if (rows == 0) return PE_OK;
+  {
+    int n16;
+    int64_t ls16, ld16;
+    if ((dtype == PE_F32 || dtype == PE_BF16) &&
+        rows16(H, dtype == PE_F32 ? 4 : 2, src, lds, dst, ldd, n16, ls16, ld16))
+      return launch_rows16(rows, n16, idx, src, ls16, dst, ld16, scatter ? 1 : 0,
+                           as_stream(stream));
+  }
   PE_CHECK_ARG(rows <= 65535, "scatter/gather rows: rows > 65535");
   dim3 grid((unsigned)ceil_div(H, 256 * 4), (unsigned)rows);
   return PE_DISPATCH(dtype, T, [&] {

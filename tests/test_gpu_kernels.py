@@ -476,18 +476,20 @@ def test_swiglu_fwd_bwd(dtype):
     assert rel(dgu.float().cpu(), g.grad) < tol
 
 
-def test_rows_embed_fill_gather_scatter_colsum():
-    H = 40
-    E = _rand(50, H, seed=21)
+# H 40 (bf16 rows of 80 B): element-wise kernels; H 3584 / fp32 H 64: 16-byte row moves
+@pytest.mark.parametrize("H,dtype", [(40, torch.bfloat16), (3584, torch.bfloat16),
+                                     (64, torch.float32)])
+def test_rows_embed_fill_gather_scatter_colsum(H, dtype):
+    E = _rand(50, H, seed=21, dtype=dtype)
     ids = torch.tensor([3, 0, 49, 3], device=DEV)
-    out = torch.zeros(4, 2 * H, dtype=torch.bfloat16, device=DEV)
+    out = torch.zeros(4, 2 * H, dtype=dtype, device=DEV)
     ops.embed_rows(ids, E, out[:, :H])
     assert torch.equal(out[:, :H], E[ids]) and torch.all(out[:, H:] == 0)
-    vec = _rand(H, seed=22)
-    dst = torch.zeros(5, H, dtype=torch.bfloat16, device=DEV)
+    vec = _rand(H, seed=22, dtype=dtype)
+    dst = torch.zeros(5, H, dtype=dtype, device=DEV)
     ops.fill_rows(vec, dst[1:4])
     assert torch.equal(dst[1:4], vec.expand(3, H)) and torch.all(dst[0] == 0)
-    src = _rand(6, H, seed=23)
+    src = _rand(6, H, seed=23, dtype=dtype)
     idx = torch.tensor([5, 1, 2], device=DEV)
     g = ops.gather_rows(src, idx)
     assert torch.equal(g, src[idx])
@@ -496,6 +498,17 @@ def test_rows_embed_fill_gather_scatter_colsum():
     assert torch.equal(back[idx], src[idx]) and torch.all(back[0] == 0)
     s = ops.rowsum_cols(src)
     assert rel(s.cpu(), src.float().sum(0).cpu()) < 1e-6
+
+
+def test_row_moves_beyond_one_grid_row_span():
+    """More rows than the 16-byte row kernel's grid covers in one pass (32768)."""
+    src = _rand(1000, 64, seed=24)
+    idx = torch.randint(0, 1000, (40000,), generator=torch.Generator().manual_seed(3)).to(DEV)
+    g = ops.gather_rows(src, idx)
+    assert torch.equal(g, src[idx])
+    dst = torch.zeros(40000, 64, dtype=torch.bfloat16, device=DEV)
+    ops.fill_rows(src[7], dst)
+    assert torch.equal(dst, src[7].expand(40000, 64))
 
 
 def test_adamw_with_clipping_matches_torch():
