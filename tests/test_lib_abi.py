@@ -39,3 +39,34 @@ def test_host_only_queries_work_without_gpu():
     # argument validation happens before any CUDA call
     assert lib.pe_rope(1, 4, 2, 7, None, 14, None, 10000.0, 0, None) == 1
     assert b"rope" in lib.pe_last_error()
+
+
+def test_segment_attention_and_topk_validate_before_any_cuda_call():
+    import numpy as np
+
+    from parallel_eagle_b200 import _lib
+
+    lib = _lib.load()
+    bf16 = 1
+    # no segments
+    assert lib.pe_attn_fwd_segments(bf16, 0, None, 5, 28, 4, 128, None, 0, None, 0, None, 0,
+                                     None, 0, None, 0, None, None) != 0
+    assert b"segment" in lib.pe_last_error()
+    # a segment with a0 >= a1
+    bad = np.array([0, 512, 700, 700], dtype=np.int64)
+    assert lib.pe_attn_fwd_segments(bf16, 2, bad.ctypes.data, 5, 28, 4, 128, None, 0, None, 0,
+                                     None, 0, None, 0, None, 0, None, None) != 0
+    assert b"segment 1" in lib.pe_last_error()
+    # kernel-variant bits are not accepted by the stacked-segment entry points
+    ok = np.array([0, 512, 512, 1024], dtype=np.int64)
+    assert lib.pe_attn_fwd_segments(bf16, 2, ok.ctypes.data, 5, 28, 4, 128, None, 0, None, 0,
+                                     None, 0, None, 0, None, 1 << 8, None, None) != 0
+    assert b"variant" in lib.pe_last_error()
+    # the stacked-segment workspace covers the deltas of every stacked row
+    rows = (512 + 512 * 4) + (1024 + 512 * 4)
+    assert lib.pe_attn_bwd_segments_workspace(bf16, 2, ok.ctypes.data, 5, 28, 4, 128) >= 28 * rows * 4
+    assert lib.pe_attn_bwd_segments_workspace(bf16, 0, None, 5, 28, 4, 128) == 0
+    # top-k: k must lie in [1, V]
+    assert lib.pe_topk_logprobs(bf16, 2, 7, None, 7, 8, 0, None, None, None) != 0
+    assert b"topk" in lib.pe_last_error()
+    assert lib.pe_topk_logprobs(bf16, 0, 7, None, 7, 3, 0, None, None, None) == 0
