@@ -37,4 +37,6 @@ from .draft import (  # noqa: F401
     propose_chain_from_logits,
     propose_tree_from_logits,
     token_shared_input,
+    tree_allow,
+    tree_positions,
 )

@@ -98,3 +98,34 @@ def propose_tree_from_logits(logits, k: int, top_k: int, max_nodes: int, pending
 def propose_chain_from_logits(logits, pending: int = 0) -> list[int]:
     """Top-1 token per depth (``src/pe/decode/chain.py:15-23``)."""
     return [int(t) for t in logits.argmax(-1)[pending:]]
+
+
+def tree_allow(parents: list[int], prefix_len: int) -> torch.Tensor:
+    """Verification-tree attend mask by a per-pair walk up the parent chain
+    (``src/pe/masks.py:127-147``): prefix causal, nodes see the whole prefix and
+    their ancestors (themselves included)."""
+    t = len(parents)
+    n = prefix_len + t
+    allow = torch.zeros(n, n, dtype=torch.bool)
+    for q in range(n):
+        for kk in range(n):
+            if kk < prefix_len:
+                allow[q, kk] = q >= prefix_len or kk <= q
+            elif q >= prefix_len:
+                a = q - prefix_len
+                while a >= 0 and a != kk - prefix_len:
+                    a = parents[a]
+                allow[q, kk] = a >= 0
+    return allow
+
+
+def tree_positions(parents: list[int], prefix_len: int) -> list[int]:
+    """Prefix positions ``0 .. P-1``, then ``P + depth`` per node, the depth counted
+    by walking to the root (``src/pe/masks.py:118-124,150-156``)."""
+    out = list(range(prefix_len))
+    for t in range(len(parents)):
+        depth, a = 0, parents[t]
+        while a >= 0:
+            depth, a = depth + 1, parents[a]
+        out.append(prefix_len + depth)
+    return out

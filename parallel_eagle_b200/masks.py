@@ -99,3 +99,59 @@ class AmortizedMtpMask:
 
     def bias(self, num_anchors: int, dtype: torch.dtype) -> torch.Tensor:
         return to_additive_bias(self.allow(num_anchors), dtype)
+
+
+# --------------------------------------------------------------------------
+# Verification trees: a drafted token tree appended to a prefix, each node
+# given by the index of its parent (-1: hangs off the prefix), parents before
+# children (reference masks.py:118-156).  These build the target's attend mask
+# and positions for verifying a tree from ``decode.propose_tree``.
+# --------------------------------------------------------------------------
+
+
+def _check_tree(parents) -> list[int]:
+    parents = [int(p) for p in parents]
+    for t, p in enumerate(parents):
+        if not -1 <= p < t:
+            raise ValueError(
+                f"tree node {t} has parent {p}: parents must be -1 or an earlier node"
+            )
+    return parents
+
+
+def tree_depths(parents) -> list[int]:
+    """Distance of each node from the prefix: 0 for a node whose parent is -1
+    (reference ``masks.py:118-124``)."""
+    depths: list[int] = []
+    for p in _check_tree(parents):
+        depths.append(0 if p < 0 else depths[p] + 1)
+    return depths
+
+
+def tree_allow_mask(parents, prefix_len: int, device="cpu") -> torch.Tensor:
+    """Boolean ``(P + T, P + T)`` attend mask over ``[prefix | tree nodes]``
+    (reference ``masks.py:127-147``): causal inside the prefix, every node sees
+    the whole prefix, and among the nodes exactly its ancestor chain, itself
+    included.  Nothing in the prefix sees a node."""
+    parents = _check_tree(parents)
+    t = len(parents)
+    # ancestor sets row by row: a node's row is its parent's row plus itself
+    anc = torch.zeros(t, t, dtype=torch.bool)
+    for node, p in enumerate(parents):
+        if p >= 0:
+            anc[node, :p + 1] = anc[p, :p + 1]
+        anc[node, node] = True
+    n = prefix_len + t
+    allow = torch.zeros(n, n, dtype=torch.bool)
+    allow[:prefix_len, :prefix_len] = torch.ones(prefix_len, prefix_len, dtype=torch.bool).tril()
+    allow[prefix_len:, :prefix_len] = True
+    allow[prefix_len:, prefix_len:] = anc
+    return allow.to(device)
+
+
+def tree_position_ids(parents, prefix_len: int, device="cpu") -> torch.Tensor:
+    """Rotary position per token (reference ``masks.py:150-156``): the prefix at
+    ``0 .. P-1``, a node at ``P + depth`` (siblings share a position)."""
+    depths = torch.tensor(tree_depths(parents), dtype=torch.long)
+    pos = torch.cat([torch.arange(prefix_len, dtype=torch.long), prefix_len + depths])
+    return pos.to(device)

@@ -44,6 +44,56 @@ def test_allow_rule_matches_oracle_on_random_subsets():
     assert torch.equal(masks.allow_from_slots(a, d), oracle.slot_allow(a, d))
 
 
+def _tree_known_answer(allow, pos):
+    # reference tests/test_masks.py:55-75: prefix 2, parents [-1, 0, -1]
+    assert allow.shape == (5, 5)
+    assert allow[0, 0] and not allow[0, 1] and allow[1, 0] and allow[1, 1]
+    assert allow[2:, :2].all()
+    assert allow[3, 2] and allow[3, 3] and not allow[3, 4]
+    assert allow[2, 2] and not allow[2, 3] and not allow[2, 4]
+    assert list(pos) == [0, 1, 2, 3, 2]
+
+
+def test_tree_masks_reference_known_answer():
+    parents = [-1, 0, -1]
+    assert masks.tree_depths(parents) == [0, 1, 0]
+    _tree_known_answer(masks.tree_allow_mask(parents, prefix_len=2),
+                       masks.tree_position_ids(parents, prefix_len=2).tolist())
+    # the checker itself against the same pin
+    _tree_known_answer(oracle.tree_allow(parents, 2), oracle.tree_positions(parents, 2))
+
+
+def _random_tree(g, t):
+    return [-1 if i == 0 else int(torch.randint(-1, i, (1,), generator=g)) for i in range(t)]
+
+
+@pytest.mark.parametrize("prefix_len", [0, 1, 7])
+def test_tree_masks_match_oracle(prefix_len):
+    g = torch.Generator().manual_seed(prefix_len)
+    trees = [[], [-1], [-1, 0, 1, 2], [-1, -1, -1]] + [_random_tree(g, t) for t in (5, 17, 40)]
+    # beam trees as the draft path builds them (top-k per depth, parents from the beam)
+    logits = torch.randn(5, 50, generator=g)
+    trees.append(oracle.propose_tree_from_logits(logits, 5, 4, 20)[1])
+    for parents in trees:
+        allow = masks.tree_allow_mask(parents, prefix_len)
+        assert allow.dtype == torch.bool
+        assert torch.equal(allow, oracle.tree_allow(parents, prefix_len)), parents
+        pos = masks.tree_position_ids(parents, prefix_len)
+        assert pos.dtype == torch.long
+        assert pos.tolist() == oracle.tree_positions(parents, prefix_len), parents
+        assert masks.tree_depths(parents) == [x - prefix_len for x in pos.tolist()[prefix_len:]]
+        b = masks.to_additive_bias(allow, torch.float32)
+        assert torch.all((b[0, 0] == 0) == allow)
+
+
+def test_tree_masks_reject_unordered_parents():
+    for bad in ([0], [-1, 1], [-1, 2, 0], [-2]):
+        with pytest.raises(ValueError):
+            masks.tree_allow_mask(bad, 3)
+        with pytest.raises(ValueError):
+            masks.tree_depths(bad)
+
+
 def test_config_defaults_match_reference():
     assert config.TrainConfig().num_segments == 1
     assert config.TargetConfig().feature_layers is None
