@@ -21,7 +21,15 @@ _MODULES = ("config", "masks", "nn", "drafter", "partition", "train", "features"
 
 
 def install_as_pe() -> None:
-    """Alias this package as ``pe`` (and ``pe.<module>``) in ``sys.modules``."""
+    """Alias this package as ``pe`` (and ``pe.<module>``) in ``sys.modules``.
+
+    The draft proposals live in one module here; it also answers to the
+    reference's ``pe.decode``, ``pe.decode.tree`` and ``pe.decode.chain``."""
     sys.modules["pe"] = sys.modules[__name__]
     for m in _MODULES:
         sys.modules[f"pe.{m}"] = importlib.import_module(f"{__name__}.{m}")
+    dec = importlib.import_module(f"{__name__}.decode")
+    for sub in ("tree", "chain"):
+        sys.modules[f"pe.decode.{sub}"] = dec
+        setattr(dec, sub, dec)
+    sys.modules["pe.decode"] = dec

@@ -181,3 +181,33 @@ def test_flat_params_views_and_grad_attachment():
     # moving the module invalidates the flat views
     d.to(torch.float64)
     assert not fp.valid()
+
+
+def test_install_as_pe_resolves_reference_imports():
+    """After ``install_as_pe()`` the reference's import lines reach this package
+    (run in a child interpreter so this process's ``sys.modules`` stays clean)."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    code = (
+        "import parallel_eagle_b200 as P; P.install_as_pe()\n"
+        "from pe.partition import mtp_backward, mtp_eval_loss\n"
+        "from pe.drafter import ParallelDrafter, load_drafter\n"
+        "from pe.masks import AmortizedMtpMask, tree_allow_mask, tree_position_ids\n"
+        "from pe.config import DrafterConfig, TrainConfig\n"
+        "from pe.train import train\n"
+        "from pe.features import FeatureDataset\n"
+        "from pe.nn import RMSNorm, DecoderLayer\n"
+        "from pe.decode.tree import propose_tree\n"
+        "from pe.decode.chain import propose_chain, propose_chain_sequential\n"
+        "from pe.decode import propose_tree as t2\n"
+        "import pe.decode.tree, pe.partition\n"
+        "assert pe.decode.tree.propose_tree is propose_tree is t2\n"
+        "assert pe.partition.mtp_backward.__module__.startswith('parallel_eagle_b200')\n"
+        "print('ok')\n"
+    )
+    root = Path(__file__).resolve().parents[1]
+    res = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True,
+                         timeout=300)
+    assert res.returncode == 0 and res.stdout.strip() == "ok", res.stderr
