@@ -178,6 +178,8 @@ struct SegTable {
   int row0[kMaxSeg];
   int nseg;
   int nwork;                   // 0: one segment, units in the kernel's built-in order
+  int nsplit;                  // dK / dV kernel: units [0, nsplit) run one item per query
+                               // head, later ones one item per KV head (all its query heads)
   uint32_t work[kMaxWork];     // segment << 24 | unit, in execution order
 };
 constexpr int kWorkSegShift = 24;

@@ -2,10 +2,14 @@
 // persistent kernel: the backward of reference src/pe/nn.py:84-88 under the
 // mask of src/pe/masks.py:43-61, partition slot layout (src/pe/partition.py:41-55).
 //
-// Work item = (query head h, 128-key tile).  One CTA per SM takes items from a
-// global counter in order of decreasing work (key tiles ascending, heads
-// fastest), so TMEM allocation, barrier set-up and the first loads happen once
-// per CTA and the next item's K / V / Q / dO loads overlap the current item.
+// Work item = (query head h, 128-key tile) for key tiles many queries read, and
+// (KV head, 128-key tile) -- all rep query heads of the group in turn, dK / dV
+// summed in TMEM -- for the light tiles of prediction-slot keys (each read by
+// the two 64-query steps of its own anchors).  One CTA per SM takes items from
+// a global counter in order of decreasing work (key tiles ascending, heads
+// fastest; the grouped light tiles last), so TMEM allocation, barrier set-up
+// and the first loads happen once per CTA and the next item's K / V / Q / dO
+// loads overlap the current item.
 // For an item it walks, in 64-query steps, the query rows that can read the key
 // tile (keys on TMEM lanes):
 //   S^T  = K Q^T           dP^T = V dO^T           (N = 64)
@@ -54,6 +58,8 @@ constexpr int kComputeWarps = 16;               // four per TMEM lane quarter
 constexpr int kThreads = 128 + 32 * kComputeWarps;
 constexpr int kParts = kComputeWarps / 4;
 constexpr int kCols = QT / kParts;              // query columns per compute warp
+constexpr int kGroupSteps = 32;                 // a key tile with at most this many steps over
+                                                // a GQA group runs as one item per KV head
 
 // shared memory (offsets from the 1024-aligned base)
 constexpr uint32_t OFF_K = 0;                        // [2] K tiles
@@ -94,17 +100,40 @@ struct Bars {
   }
 };
 
-// the item's segment, key tile and the 64-query steps that read it
+// Items: the first tab.nsplit units (key tiles) run as Hq items, one per query
+// head; every later unit as Hkv items, one per KV head walking all rep query
+// heads of its group, so a key tile few queries read pays the item's fixed cost
+// (K / V load, pipeline fill, dK / dV drain) once per group instead of per head.
+__device__ __forceinline__ int item_total(const SegTable& tab, int Hq, int Hkv) {
+  const int units = tab.nwork > 0 ? tab.nwork : (tab.g[0].S + TK - 1) / TK;
+  return Hq * tab.nsplit + Hkv * (units - tab.nsplit);
+}
+
+// the item's segment, key tile, query heads and the 64-query steps that read it
 struct Item {
-  int seg, h, kvh, k0;
+  int seg, h0, nh, kvh, k0;
   PartGeom g;
   int64_t ml;  // first lse / delta element of the segment: Hq * its first stacked row
   int64_t r0;  // its first stacked row
   Ranges qr;
-  int n;
-  __device__ Item(int w, int Hq, int rep, const SegTable& tab) {
-    const int e = w / Hq;
-    h = w - e * Hq;
+  int nq;      // 64-query steps per query head
+  int n;       // steps of the item: nq for each of its nh heads, head-major
+  __device__ Item(int w, int Hq, int Hkv, int rep, const SegTable& tab) {
+    const int head_items = Hq * tab.nsplit;
+    int e;
+    if (w < head_items) {
+      e = w / Hq;
+      h0 = w - e * Hq;
+      nh = 1;
+      kvh = h0 / rep;
+    } else {
+      const int r = w - head_items;
+      e = r / Hkv;
+      kvh = r - e * Hkv;
+      e += tab.nsplit;
+      h0 = kvh * rep;
+      nh = rep;
+    }
     int kt;
     if (tab.nwork > 0) {
       unpack_work(tab.work[e], seg, kt);
@@ -115,11 +144,14 @@ struct Item {
     g = tab.g[seg];
     r0 = tab.row0[seg];
     ml = (int64_t)Hq * r0;
-    kvh = h / rep;
     k0 = kt * TK;
     qr = query_tiles(g, k0, QT);
-    n = qr.count();
+    nq = qr.count();
+    n = nq * nh;
   }
+  // query head and 64-query tile of step i
+  __device__ __forceinline__ int head(int i) const { return nh > 1 ? h0 + i / nq : h0; }
+  __device__ __forceinline__ int qtile(int i) const { return qr.at(nh > 1 ? i % nq : i); }
 };
 
 // packed P^T / dS^T: the queries of compute part p (columns [p C, p C + C)) sit in
@@ -149,7 +181,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // items: (work-list entry or, for a lone segment, key tile) x query head
-  const int total = Hq * (tab.nwork > 0 ? tab.nwork : (tab.g[0].S + TK - 1) / TK);
+  const int total = item_total(tab, Hq, Hkv);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -222,7 +254,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
         sItem[ic & 1] = w;
         mbar_arrive(&B.item_full[ic & 1]);  // release: publishes the slot write
         if (w < 0) break;
-        const Item it(w, Hq, rep, tab);
+        const Item it(w, Hq, Hkv, rep, tab);
         // K into buffer ic & 1 once the item two back issued its last S^T
         const int kb = ic & 1;
         if (!mbar_wait(&B.k_empty[kb], ((ic >> 1) & 1) ^ 1u, status, 342)) { ok = false; break; }
@@ -241,20 +273,20 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
         last_ph = ic & 1;
         for (int i = 0; i < it.n && ok; ++i) {
           const int gi = gs + i;
-          const int q0 = it.qr.at(i) * QT;
+          const int q0 = it.qtile(i) * QT, hc = it.head(i) * HD;
           const int qs = gi % QS, ds = gi % DS;
           if (!mbar_wait(&B.q_empty[qs], ((gi / QS) & 1) ^ 1u, status, 343)) { ok = false; break; }
           uint8_t* qd = smem + OFF_Q + qs * SUB_BYTES;
           mbar_arrive_expect_tx(&B.q_full[qs], SUB_BYTES);
-          tma_load_2d(qd, &tab.tm[it.seg][0], &B.q_full[qs], it.h * HD, q0);
-          tma_load_2d(qd + SUB_CHUNK, &tab.tm[it.seg][0], &B.q_full[qs], it.h * HD + 64, q0);
+          tma_load_2d(qd, &tab.tm[it.seg][0], &B.q_full[qs], hc, q0);
+          tma_load_2d(qd + SUB_CHUNK, &tab.tm[it.seg][0], &B.q_full[qs], hc + 64, q0);
           last_bar = &B.q_full[qs];
           last_ph = (gi / QS) & 1;
           if (!mbar_wait(&B.do_empty[ds], ((gi / DS) & 1) ^ 1u, status, 344)) { ok = false; break; }
           uint8_t* dd = smem + OFF_DO + ds * SUB_BYTES;
           mbar_arrive_expect_tx(&B.do_full[ds], SUB_BYTES);
-          tma_load_2d(dd, &tab.tm[it.seg][3], &B.do_full[ds], it.h * HD, q0);
-          tma_load_2d(dd + SUB_CHUNK, &tab.tm[it.seg][3], &B.do_full[ds], it.h * HD + 64, q0);
+          tma_load_2d(dd, &tab.tm[it.seg][3], &B.do_full[ds], hc, q0);
+          tma_load_2d(dd + SUB_CHUNK, &tab.tm[it.seg][3], &B.do_full[ds], hc + 64, q0);
           last_bar = &B.do_full[ds];
           last_ph = (gi / DS) & 1;
         }
@@ -276,7 +308,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
       const bool leader = elect_one();
       const int leader_lane = __ffs(__ballot_sync(0xffffffffu, leader)) - 1;
       if (leader) {
-        const Item it(w, Hq, rep, tab);
+        const Item it(w, Hq, Hkv, rep, tab);
         const int kb = ic & 1, last = gs + it.n - 1;
         const uint32_t k_base = smem_u32(sK + kb * TILE_BYTES);
         // S^T(gi) = K Q(gi)^T into buffer gi & 1, both operands in shared memory
@@ -369,10 +401,11 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
     for (int ic = 0; ok; ++ic) {
       const int w = read_item(ic, ok);
       if (w < 0) break;
-      const Item it(w, Hq, rep, tab);
+      const Item it(w, Hq, Hkv, rep, tab);
       for (int i = 0; i < it.n; ++i) {
         const int gi = gs + i, slot = gi % MS;
-        const int q0 = it.qr.at(i) * QT;
+        const int q0 = it.qtile(i) * QT;
+        const int64_t hrow = it.ml + (int64_t)it.head(i) * it.g.S;
         if (!mbar_wait(&B.meta_empty[slot], ((gi / MS) & 1) ^ 1u, status, 350)) ok = false;
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -383,8 +416,8 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
           float lv = -INFINITY, dl = 0.f;
           int qa = -1, qd = 0;
           if (q < it.g.S) {
-            lv = -lse[it.ml + (int64_t)it.h * it.g.S + q] * kLog2e;
-            dl = -delta[it.ml + (int64_t)it.h * it.g.S + q];
+            lv = -lse[hrow + q] * kLog2e;
+            dl = -delta[hrow + q];
             decode(it.g, q, qa, qd);
           }
           sL[slot * QT + r] = lv;
@@ -432,7 +465,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
     for (; ok; ++ic) {
       const int w = read_item(ic, ok);
       if (w < 0) break;
-      const Item it(w, Hq, rep, tab);
+      const Item it(w, Hq, Hkv, rep, tab);
       const int kj = it.k0 + row;
       const bool kvalid = kj < it.g.S;
       int ka = 0, ke = 0;
@@ -445,7 +478,7 @@ attn_bwd_kv2_kernel(const __grid_constant__ SegTable tab, const float* __restric
       have_pending = true;
       for (int i = 0; i < it.n; ++i) {
         const int gi = gs + i, slot = gi % MS, b = gi & 1;
-        const int q0 = it.qr.at(i) * QT;
+        const int q0 = it.qtile(i) * QT;
         const bool full = tile_fully_allowed(it.g, q0, it.k0, QT);
         // ---- P^T = 2^(S^T c - lse') and dS^T = P^T (dP^T - delta): S^T(i) and
         // dP^T(i) were issued together two steps ahead, so one wait, one pair of TMEM
@@ -549,9 +582,30 @@ int attn_bwd_kv2_launch(int nseg, const PartGeom* g, int Hq, int Hkv, const void
   auto cost = [](const PartGeom& sg, int kt) { return query_tiles(sg, kt * TK, QT).count(); };
   int rc = seg_table_order(tab, [](const PartGeom& sg) { return seg_tiles(sg); }, cost);
   if (rc) return rc;
+  // light units (at most kGroupSteps steps over all rep heads of a group) run one
+  // item per KV head after every per-head unit; stable, so both parts keep the
+  // segment-major, heaviest-first order
+  const int rep = Hq / Hkv;
+  auto light = [&](int s, int kt) { return rep > 1 && cost(tab.g[s], kt) * rep <= kGroupSteps; };
+  int64_t units;
+  if (tab.nwork > 0) {
+    units = tab.nwork;
+    auto heavy_w = [&](uint32_t w) {
+      return !light((int)(w >> kWorkSegShift), (int)(w & ((1u << kWorkSegShift) - 1)));
+    };
+    uint32_t* end = std::stable_partition(tab.work, tab.work + tab.nwork, heavy_w);
+    tab.nsplit = (int)(end - tab.work);
+  } else {
+    // a lone segment runs its key tiles in ascending order: the per-head units are
+    // the tiles before the first light one
+    units = lone_tiles;
+    int kt = 0;
+    while (kt < lone_tiles && !light(0, kt)) ++kt;
+    tab.nsplit = kt;
+  }
   PE_CUDA_TRY(cudaFuncSetAttribute(attn_bwd_kv2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)SMEM_KV2));
-  const int64_t items = (int64_t)Hq * (tab.nwork > 0 ? tab.nwork : lone_tiles);
+  const int64_t items = (int64_t)Hq * tab.nsplit + (int64_t)Hkv * (units - tab.nsplit);
   PE_CHECK_ARG(items < (1ll << 31), "attention backward: too many work items");
   const int grid = (int)(items < sm_count() ? items : sm_count());
   attn_bwd_kv2_kernel<<<grid, kThreads, SMEM_KV2, st>>>(tab, lse, delta, dk_acc, dv_acc,
