@@ -704,23 +704,37 @@ def cpu_baseline(args, n=None):
             "seconds": round(sec, 2)}
 
 
+REF_BUDGET_S = 150.0  # the whole --impl reference run, warm-up and timed samples
+
+
+def reference_sample_len(args, sec_at_256: float) -> int:
+    """Sequence length of each reference-arm sample: the workload's own n (--cpu-n)
+    unless warmup + steps samples of it would exceed REF_BUDGET_S, then the longest
+    multiple of 256 that fits (CPU time grows about linearly with n here)."""
+    per_row = 1.1 * sec_at_256 / 256
+    samples = max(0, args.warmup - 1) + max(1, args.steps)
+    fit = int(REF_BUDGET_S / samples / per_row) // 256 * 256
+    return max(256, min(args.cpu_n, fit))
+
+
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
         return
-    samples = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(args)
-        if i >= args.warmup:
-            samples.append(r)
+    # the first warm-up sample is a short one that calibrates the host's speed
+    cal = cpu_baseline(args, n=256)
+    n = reference_sample_len(args, cal["seconds"])
+    for _ in range(max(0, args.warmup - 1)):
+        cpu_baseline(args, n=n)
+    samples = [cpu_baseline(args, n=n) for _ in range(max(1, args.steps))]
     sec = sum(s["seconds"] for s in samples) / len(samples)
-    value = args.cpu_n * CONFIG2["max_depth"] / sec
+    value = n * CONFIG2["max_depth"] / sec
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "BASELINE config 2: 7B-class drafter step", "n": args.cpu_n,
+        "config": {"workload": "BASELINE config 2: 7B-class drafter step", "n": n,
                    "K": 5, "S": 4, "parallelism": "cpu"},
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": samples[0]["cores"],
                          "kind": "port", "sample": samples[0]["sample"]},
@@ -738,7 +752,8 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=None, help="override sequence length")
     ap.add_argument("--batch", type=int, default=None, help="override per-GPU batch")
-    ap.add_argument("--cpu-n", type=int, default=256, help="sequence length of the CPU sample")
+    ap.add_argument("--cpu-n", type=int, default=2048,
+                    help="sequence length of the CPU sample (default: the workload's own n)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2,
                     help="BASELINE workload: 2 (default), 3 soft-target loss, 4 14B-class")
