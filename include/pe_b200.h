@@ -229,6 +229,12 @@ int pe_cast_f32(int dtype, int64_t n, const float* x, void* y, void* stream);
  * ------------------------------------------------------------------------- */
 int pe_topk_logprobs(int dtype, int64_t rows, int64_t V, const void* logits, int64_t ld, int k,
                      int raw, int64_t* idx, float* val, void* stream);
+/* q[r, v] (fp32, row stride ldq) = softmax(z[r, :] / temperature)[v] in fp32 for
+ * logits z (dtype, row stride ld): the per-depth sampling distributions of
+ * reference src/pe/decode/chain.py:50 (torch.softmax(logits.float() / temperature)).
+ * temperature must be positive and finite. */
+int pe_softmax_rows(int dtype, int64_t rows, int64_t V, const void* logits, int64_t ld,
+                    float temperature, float* q, int64_t ldq, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Optimizer (reference src/pe/train.py:26-34,158-159: clip_grad_norm_(1.0) then

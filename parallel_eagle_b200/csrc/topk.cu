@@ -119,10 +119,71 @@ topk_logprobs_kernel(int64_t V, const T* __restrict__ logits, int64_t ld, int k,
   }
 }
 
+__device__ double block_sum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < kThreads / 32 ? red[lane] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  const double out = red[0];
+  __syncthreads();
+  return out;
+}
+
+// q = softmax(z / T) per row in fp32 (reference src/pe/decode/chain.py:50:
+// torch.softmax(logits.float() / temperature)): the division first, then the row
+// maximum, s = sum exp(x - m) and q_v = exp(x_v - m) / s, in torch's order.  The
+// ~150K-term row sum is accumulated in fp64 and rounded once, so s is the correctly
+// rounded sum of the fp32 exponentials whatever the reduction order.
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+softmax_rows_kernel(int64_t V, const T* __restrict__ logits, int64_t ld, float temperature,
+                    float* __restrict__ q, int64_t ldq) {
+  __shared__ float fred[kThreads / 32];
+  __shared__ double dred[kThreads / 32];
+  const T* z = logits + (int64_t)blockIdx.x * ld;
+  float* out = q + (int64_t)blockIdx.x * ldq;
+  float m = -INFINITY;
+  for (int64_t v = threadIdx.x; v < V; v += kThreads) m = fmaxf(m, load_f(z + v) / temperature);
+  m = block_reduce(m, fred, true);
+  double sd = 0.0;
+  for (int64_t v = threadIdx.x; v < V; v += kThreads)
+    sd += (double)expf(load_f(z + v) / temperature - m);
+  const float s = (float)block_sum_d(sd, dred);
+  for (int64_t v = threadIdx.x; v < V; v += kThreads)
+    out[v] = expf(load_f(z + v) / temperature - m) / s;
+}
+
 }  // namespace
 }  // namespace pe
 
 using namespace pe;
+
+extern "C" int pe_softmax_rows(int dtype, int64_t rows, int64_t V, const void* logits,
+                               int64_t ld, float temperature, float* q, int64_t ldq,
+                               void* stream) {
+  PE_CHECK_ARG(rows >= 0 && V >= 1 && ld >= V && ldq >= V,
+               "softmax_rows: need V >= 1, ld >= V and ldq >= V");
+  PE_CHECK_ARG(temperature > 0.f && temperature <= FLT_MAX,
+               "softmax_rows: temperature must be positive and finite");
+  PE_CHECK_ARG(rows <= 0x7fffffff, "softmax_rows: too many rows");
+  if (rows == 0) return PE_OK;
+  PE_CHECK_ARG(logits && q, "softmax_rows: null pointer");
+  cudaStream_t st = as_stream(stream);
+  return PE_DISPATCH(dtype, T, [&] {
+    softmax_rows_kernel<T><<<(unsigned)rows, kThreads, 0, st>>>(V, (const T*)logits, ld,
+                                                                temperature, q, ldq);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
 
 extern "C" int pe_topk_logprobs(int dtype, int64_t rows, int64_t V, const void* logits,
                                 int64_t ld, int k, int raw, int64_t* idx, float* val,

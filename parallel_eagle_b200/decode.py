@@ -65,3 +65,19 @@ def propose_chain_sequential(drafter, context_ids: torch.Tensor, context_feats: 
         return []
     _, toks = ops.topk_logprobs(logits[pending:], 1, raw=True)
     return [int(t) for t in toks[:, 0].tolist()]
+
+
+def propose_chain_sampling(drafter, context_ids: torch.Tensor, context_feats: torch.Tensor,
+                           k: int, temperature: float,
+                           generator: torch.Generator | None = None) -> tuple[list[int], torch.Tensor]:
+    """Sample one token per depth from the drafter's distributions at ``temperature``
+    (reference ``chain.py:38-53``).  Returns the tokens and the ``[k, V]`` fp32
+    distributions ``q`` (for the speculative-sampling residual).  ``q`` comes from
+    ``pe_softmax_rows``; the draw is ``torch.multinomial`` with the caller's generator,
+    as in the reference, so a seeded generator reproduces its tokens."""
+    if not temperature > 0:
+        raise ValueError(f"temperature must be positive, got {temperature}")
+    logits = drafter.draft_logits(context_ids, context_feats, k)
+    q = ops.softmax_rows(logits, temperature)
+    tokens = torch.multinomial(q, 1, generator=generator).squeeze(-1)
+    return [int(t) for t in tokens.tolist()], q

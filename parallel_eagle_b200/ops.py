@@ -335,6 +335,21 @@ def topk_logprobs(logits: torch.Tensor, k: int, raw: bool = False):
     return val, idx
 
 
+def softmax_rows(logits: torch.Tensor, temperature: float) -> torch.Tensor:
+    """``softmax(logits.float() / temperature)`` per row of ``[rows, V]`` logits, fp32
+    (the per-depth sampling distributions of a sampled draft chain)."""
+    L.require_cuda(logits)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise L.PeError("softmax_rows: logits must be [rows, V] with unit column stride")
+    rows, V = logits.shape
+    q = torch.empty(rows, V, dtype=torch.float32, device=logits.device)
+    rc = _lib().pe_softmax_rows(L.dtype_code(logits.dtype), rows, V, logits.data_ptr(),
+                                logits.stride(0), float(temperature), q.data_ptr(), V,
+                                L.stream_ptr(logits.device))
+    L.check(rc, "pe_softmax_rows")
+    return q
+
+
 # --------------------------------------------------------- lm head + loss ----
 
 _ws_cache: dict[tuple, torch.Tensor] = {}

@@ -94,3 +94,42 @@ def test_topk_logprobs_matches_torch(dtype, rows, V, k):
     am_val, am = ops.topk_logprobs(z.to(DEV), 1, raw=True)
     assert torch.equal(am[:, 0].cpu(), z.float().argmax(-1))
     assert torch.equal(am_val[:, 0].cpu(), z.float().max(-1).values)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,V,temp", [(5, 152064, 0.7), (3, 1000, 1.0), (2, 7, 1.6)])
+def test_softmax_rows_matches_torch(dtype, rows, V, temp):
+    from parallel_eagle_b200 import ops
+
+    g = torch.Generator().manual_seed(rows * 17 + V)
+    z = (torch.randn(rows, V, generator=g) * 3).to(dtype)
+    q = ops.softmax_rows(z.to(DEV), temp)
+    x = z.float() / temp  # the reference's fp32 division
+    exact = torch.softmax(x.double(), dim=-1).float()
+    ref = torch.softmax(x, dim=-1)
+    assert q.dtype == torch.float32 and q.shape == (rows, V)
+    # the kernel sums the row in fp64, so it sits within a few ulp of the exact softmax;
+    # torch's own fp32 reduction over up to 152K terms is off by ~1.5e-5 relative
+    assert torch.allclose(q.cpu(), exact, rtol=2e-6, atol=1e-12)
+    assert torch.allclose(q.cpu(), ref, rtol=3e-5, atol=1e-10)
+    assert torch.allclose(q.sum(-1).cpu(), torch.ones(rows), atol=1e-5)
+
+
+def test_propose_chain_sampling_matches_reference_draw():
+    """Reference chain.py:38-53: q = softmax(draft_logits.float() / T), tokens drawn by
+    torch.multinomial with the caller's generator -- the same seed gives the same chain."""
+    from parallel_eagle_b200 import decode
+
+    case = make_case(256, 2, 1, 512, 1000, 1, 5, 300, dtype=torch.bfloat16, seed=7)
+    model = build_drafter(case)
+    ids, feats = case["seqs"][0]
+    ids, feats = ids[:120].to(DEV), feats[:120].to(DEV)
+    for temp, seed in ((0.8, 1), (1.3, 2)):
+        toks, q = decode.propose_chain_sampling(model, ids, feats, 5, temp,
+                                                generator=torch.Generator(device=DEV).manual_seed(seed))
+        logits = model.draft_logits(ids, feats, 5)
+        ref_q = torch.softmax(logits.float() / temp, dim=-1)
+        ref = torch.multinomial(ref_q, 1, generator=torch.Generator(device=DEV).manual_seed(seed))
+        assert torch.allclose(q, ref_q, rtol=1e-5, atol=1e-10)
+        assert toks == [int(t) for t in ref.squeeze(-1).tolist()]
+        assert len(toks) == 5 and all(0 <= t < 1000 for t in toks)

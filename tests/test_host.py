@@ -200,7 +200,7 @@ def test_install_as_pe_resolves_reference_imports():
         "from pe.features import FeatureDataset\n"
         "from pe.nn import RMSNorm, DecoderLayer\n"
         "from pe.decode.tree import propose_tree\n"
-        "from pe.decode.chain import propose_chain, propose_chain_sequential\n"
+        "from pe.decode.chain import propose_chain, propose_chain_sequential, propose_chain_sampling\n"
         "from pe.decode import propose_tree as t2\n"
         "import pe.decode.tree, pe.partition\n"
         "assert pe.decode.tree.propose_tree is propose_tree is t2\n"
@@ -211,3 +211,11 @@ def test_install_as_pe_resolves_reference_imports():
     res = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True,
                          timeout=300)
     assert res.returncode == 0 and res.stdout.strip() == "ok", res.stderr
+
+
+def test_propose_chain_sampling_rejects_non_positive_temperature():
+    from parallel_eagle_b200 import decode
+
+    for t in (0.0, -0.5, float("nan")):
+        with pytest.raises(ValueError):
+            decode.propose_chain_sampling(None, None, None, 3, t)

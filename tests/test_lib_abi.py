@@ -70,3 +70,10 @@ def test_segment_attention_and_topk_validate_before_any_cuda_call():
     assert lib.pe_topk_logprobs(bf16, 2, 7, None, 7, 8, 0, None, None, None) != 0
     assert b"topk" in lib.pe_last_error()
     assert lib.pe_topk_logprobs(bf16, 0, 7, None, 7, 3, 0, None, None, None) == 0
+    # sampling distributions: positive finite temperature, strides covering the row
+    for t in (0.0, -1.0, float("inf"), float("nan")):
+        assert lib.pe_softmax_rows(bf16, 2, 7, None, 7, t, None, 7, None) != 0
+        assert b"temperature" in lib.pe_last_error()
+    assert lib.pe_softmax_rows(bf16, 2, 7, None, 6, 1.0, None, 7, None) != 0
+    assert lib.pe_softmax_rows(bf16, 2, 7, None, 7, 1.0, None, 6, None) != 0
+    assert lib.pe_softmax_rows(bf16, 0, 7, None, 7, 0.7, None, 7, None) == 0
