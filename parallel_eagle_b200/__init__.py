@@ -24,12 +24,13 @@ def install_as_pe() -> None:
     """Alias this package as ``pe`` (and ``pe.<module>``) in ``sys.modules``.
 
     The draft proposals live in one module here; it also answers to the
-    reference's ``pe.decode``, ``pe.decode.tree`` and ``pe.decode.chain``."""
+    reference's ``pe.decode``, ``pe.decode.tree``, ``pe.decode.chain`` and
+    ``pe.decode.verify``."""
     sys.modules["pe"] = sys.modules[__name__]
     for m in _MODULES:
         sys.modules[f"pe.{m}"] = importlib.import_module(f"{__name__}.{m}")
     dec = importlib.import_module(f"{__name__}.decode")
-    for sub in ("tree", "chain"):
+    for sub in ("tree", "chain", "verify"):
         sys.modules[f"pe.decode.{sub}"] = dec
         setattr(dec, sub, dec)
     sys.modules["pe.decode"] = dec

@@ -81,3 +81,110 @@ def propose_chain_sampling(drafter, context_ids: torch.Tensor, context_feats: to
     q = ops.softmax_rows(logits, temperature)
     tokens = torch.multinomial(q, 1, generator=generator).squeeze(-1)
     return [int(t) for t in tokens.tolist()], q
+
+
+# ---------------------------------------------------------------------------
+# Verification: accept the drafts the target agrees with (reference
+# src/pe/decode/verify.py).  The target's argmaxes over every position a rule may
+# visit come from one pe_topk_logprobs launch (raw mode: the first maximal column,
+# as torch.argmax); the walk itself is host bookkeeping over those integers.
+# ---------------------------------------------------------------------------
+
+
+def _argmax_rows(rows: torch.Tensor) -> list[int]:
+    if rows.dtype not in (torch.float32, torch.bfloat16):
+        rows = rows.float()  # exact for fp16, so the argmax is unchanged
+    if rows.stride(-1) != 1:
+        rows = rows.contiguous()
+    _, idx = ops.topk_logprobs(rows, 1, raw=True)
+    return [int(t) for t in idx[:, 0].tolist()]
+
+
+def _check_prefix(prefix_len: int) -> None:
+    if prefix_len < 1:
+        raise ValueError(f"prefix_len must be at least 1, got {prefix_len}")
+
+
+def _tree_walk(truth_after, node_tokens, parents) -> tuple[list[int], int]:
+    # truth_after(node) = the target's token after `node` (-1: after the prefix)
+    children: dict[int, list[int]] = {}
+    for t, par in enumerate(parents):
+        children.setdefault(int(par), []).append(t)
+    path: list[int] = []
+    at = -1
+    while True:
+        want = truth_after(at)
+        nxt = next((t for t in children.get(at, ()) if int(node_tokens[t]) == want), None)
+        if nxt is None:
+            return path, want
+        path.append(nxt)
+        at = nxt
+
+
+def accept_chain_greedy(logits: torch.Tensor, prefix_len: int,
+                        draft_tokens) -> tuple[list[int], int]:
+    """Longest draft prefix equal to the target's greedy tokens, plus the target's
+    token after it (reference ``verify.py:17-32``).  ``logits`` ``[P + K, V]`` covers
+    ``[prefix | drafts]``; rows P-1 .. P-1+K are read."""
+    _check_prefix(prefix_len)
+    k = len(draft_tokens)
+    truth = _argmax_rows(logits[prefix_len - 1:prefix_len + k])
+    a = 0
+    while a < k and int(draft_tokens[a]) == truth[a]:
+        a += 1
+    return [int(t) for t in draft_tokens[:a]], truth[a]
+
+
+def accept_tree_greedy(logits: torch.Tensor, prefix_len: int, node_tokens,
+                       parents) -> tuple[list[int], int]:
+    """Follow the target's argmax down a drafted tree (reference ``verify.py:35-57``):
+    the accepted node indices and the bonus token.  ``logits`` covers
+    ``[prefix | tree nodes]``."""
+    _check_prefix(prefix_len)
+    truth = _argmax_rows(logits[prefix_len - 1:prefix_len + len(parents)])
+    return _tree_walk(lambda node: truth[node + 1], node_tokens, parents)
+
+
+def accept_chain_cached(root_logit: torch.Tensor, node_logits: torch.Tensor,
+                        draft_tokens) -> tuple[list[int], int]:
+    """The chain rule over cached predictions (reference ``verify.py:60-72``):
+    ``root_logit`` ``[V]`` predicts the first draft, ``node_logits[m]`` the one after
+    draft m."""
+    k = len(draft_tokens)
+    rows = torch.cat([root_logit.reshape(1, -1), node_logits[:k].reshape(-1, root_logit.numel())])
+    truth = _argmax_rows(rows)
+    a = 0
+    while a < k and int(draft_tokens[a]) == truth[a]:
+        a += 1
+    return [int(t) for t in draft_tokens[:a]], truth[a]
+
+
+def accept_tree_cached(root_logit: torch.Tensor, node_logits: torch.Tensor, node_tokens,
+                       parents) -> tuple[list[int], int]:
+    """The tree rule over cached predictions (reference ``verify.py:104-125``):
+    ``node_logits[t]`` predicts the token after tree node ``t``."""
+    n = len(parents)
+    rows = torch.cat([root_logit.reshape(1, -1), node_logits[:n].reshape(-1, root_logit.numel())])
+    truth = _argmax_rows(rows)
+    return _tree_walk(lambda node: truth[node + 1], node_tokens, parents)
+
+
+def accept_chain_sampling(target_dists: torch.Tensor, draft_tokens, q_dists: torch.Tensor,
+                          generator: torch.Generator | None = None) -> tuple[list[int], int]:
+    """Lossless speculative-sampling acceptance of a sampled chain (reference
+    ``verify.py:75-101``): draft i is kept with probability min(1, p_i / q_i); the
+    first rejection draws the bonus from relu(p - q) normalised, and a fully accepted
+    chain draws it from the trailing target distribution.  The draws are the same
+    ``torch.rand`` / ``torch.multinomial`` calls in the same order, so a seeded
+    generator reproduces the reference's decisions."""
+    accepted: list[int] = []
+    for i, tok in enumerate(draft_tokens):
+        keep = torch.clamp(target_dists[i, tok] / q_dists[i, tok], max=1.0)
+        u = torch.rand((), generator=generator, device=target_dists.device)
+        if not bool(u < keep):
+            resid = torch.clamp(target_dists[i] - q_dists[i], min=0)
+            resid = resid / resid.sum()
+            return accepted, int(torch.multinomial(resid, 1, generator=generator))
+        accepted.append(int(tok))
+    return accepted, int(torch.multinomial(target_dists[len(draft_tokens)], 1,
+                                           generator=generator))

@@ -3,7 +3,7 @@
 Run from the repository root in a checkout that has the reference project
 available (its ``src`` directory importable as ``pe``)::
 
-    PE_REFERENCE_SRC=<reference>/src python tests/golden/make_golden.py [--draft]
+    PE_REFERENCE_SRC=<reference>/src python tests/golden/make_golden.py [--draft | --verify]
 
 For every case in ``recipe.CASES`` this builds the reference ``ParallelDrafter``
 from seeded synthetic frozen heads, runs the reference ``mtp_backward`` (and
@@ -11,7 +11,9 @@ from seeded synthetic frozen heads, runs the reference ``mtp_backward`` (and
 losses, the accumulated gradients (full tensors for the tiny cases, random-
 projection sketches for the larger one) and checksums of every input.  For the
 cases that store full tensors it also writes ``<case>_draft.pt`` with the
-reference's draft-time outputs (``--draft`` writes only those).
+reference's draft-time outputs (``--draft`` writes only those).  ``--verify``
+writes ``verify_cases.pt``: the reference's draft acceptance decisions
+(``pe.decode.verify``) on seeded target outputs.
 """
 
 from __future__ import annotations
@@ -168,8 +170,55 @@ def build_draft_case(pe, name: str, c: dict) -> dict:
     return out
 
 
+def build_verify_cases() -> list[dict]:
+    """Seeded target outputs over drafted chains / trees and the reference's
+    acceptance decisions for them (pe.decode.verify): greedy and cached forms on
+    logits whose argmax the drafts follow for a varying prefix / share of nodes, and
+    speculative-sampling acceptance with a seeded CPU generator."""
+    from pe.decode import verify as ver
+
+    g = torch.Generator().manual_seed(123)
+    V = 50
+    cases = []
+    for ci in range(12):
+        P, k, T = 1 + ci, 1 + ci % 5, 3 + ci
+        logits = torch.randn(P + k, V, generator=g)
+        top = logits.argmax(-1)
+        a = ci % (k + 1)  # drafts that follow the target
+        draft = [int(top[P - 1 + m]) if m < a else int((top[P - 1 + m] + 1) % V) for m in range(k)]
+        parents = [-1 if t == 0 else int(torch.randint(-1, t, (1,), generator=g)) for t in range(T)]
+        tlog = torch.randn(P + T, V, generator=g)
+        ttop = tlog.argmax(-1)
+        nodes = []
+        for t, par in enumerate(parents):
+            pos = P - 1 if par < 0 else P + par
+            follow = float(torch.rand((), generator=g)) < 0.6
+            nodes.append(int(ttop[pos]) if follow else int(torch.randint(0, V, (1,), generator=g)))
+        tdist = torch.softmax(torch.randn(k + 1, V, generator=g), -1)
+        qdist = torch.softmax(torch.randn(k, V, generator=g), -1)
+        sdraft = [int(torch.multinomial(qdist[i], 1, generator=g)) for i in range(k)]
+        seed = 1000 + ci
+        cases.append({
+            "prefix_len": P, "logits": logits, "draft": draft,
+            "chain": ver.accept_chain_greedy(logits, P, draft),
+            "chain_cached": ver.accept_chain_cached(logits[P - 1], logits[P:P + k], draft),
+            "tree_logits": tlog, "parents": parents, "node_tokens": nodes,
+            "tree": ver.accept_tree_greedy(tlog, P, nodes, parents),
+            "tree_cached": ver.accept_tree_cached(tlog[P - 1], tlog[P:], nodes, parents),
+            "target_dists": tdist, "q_dists": qdist, "sample_draft": sdraft, "seed": seed,
+            "sampling": ver.accept_chain_sampling(tdist, sdraft, qdist,
+                                                  generator=torch.Generator().manual_seed(seed)),
+        })
+    return cases
+
+
 def main():
     pe = _reference()
+    if "--verify" in sys.argv[1:]:
+        cases = build_verify_cases()
+        torch.save(cases, HERE / "verify_cases.pt")
+        print("verify", [(c["chain"], c["tree"], c["sampling"]) for c in cases[:3]])
+        return
     draft_only = "--draft" in sys.argv[1:]
     for name, c in recipe.CASES.items():
         if not draft_only:

@@ -133,3 +133,31 @@ def test_propose_chain_sampling_matches_reference_draw():
         assert torch.allclose(q, ref_q, rtol=1e-5, atol=1e-10)
         assert toks == [int(t) for t in ref.squeeze(-1).tolist()]
         assert len(toks) == 5 and all(0 <= t < 1000 for t in toks)
+
+
+def test_verification_rules_match_reference_golden():
+    """Draft acceptance (reference pe.decode.verify) with the target's logits on the
+    GPU: the greedy and cached rules reproduce the reference's decisions in
+    ``verify_cases.pt``; sampled acceptance matches the oracle draw for draw under the
+    same seeded CUDA generator."""
+    from oracle import verify as ov
+
+    from parallel_eagle_b200 import decode
+
+    cases = torch.load(ROOT / "tests" / "golden" / "verify_cases.pt", weights_only=False)
+    for c in cases:
+        P, k = c["prefix_len"], len(c["draft"])
+        lg, tl = c["logits"].to(DEV), c["tree_logits"].to(DEV)
+        assert decode.accept_chain_greedy(lg, P, c["draft"]) == c["chain"]
+        _, bonus_bf16 = decode.accept_chain_greedy(lg.bfloat16(), P, c["draft"])  # bf16 dispatch
+        assert 0 <= bonus_bf16 < lg.shape[1]
+        assert decode.accept_chain_cached(lg[P - 1], lg[P:P + k], c["draft"]) == c["chain_cached"]
+        assert decode.accept_tree_greedy(tl, P, c["node_tokens"], c["parents"]) == c["tree"]
+        assert decode.accept_tree_cached(tl[P - 1], tl[P:], c["node_tokens"],
+                                         c["parents"]) == c["tree_cached"]
+        td, qd = c["target_dists"].to(DEV), c["q_dists"].to(DEV)
+        got = decode.accept_chain_sampling(td, c["sample_draft"], qd,
+                                           generator=torch.Generator(device=DEV).manual_seed(c["seed"]))
+        ref = ov.accept_chain_sampling(td, c["sample_draft"], qd,
+                                       generator=torch.Generator(device=DEV).manual_seed(c["seed"]))
+        assert got == ref

@@ -201,7 +201,8 @@ def test_install_as_pe_resolves_reference_imports():
         "from pe.nn import RMSNorm, DecoderLayer\n"
         "from pe.decode.tree import propose_tree\n"
         "from pe.decode.chain import propose_chain, propose_chain_sequential, propose_chain_sampling\n"
-        "from pe.decode import propose_tree as t2\n"
+        "from pe.decode import propose_tree as t2, accept_tree_greedy, accept_chain_greedy\n"
+        "from pe.decode.verify import accept_chain_sampling, accept_tree_cached\n"
         "import pe.decode.tree, pe.partition\n"
         "assert pe.decode.tree.propose_tree is propose_tree is t2\n"
         "assert pe.partition.mtp_backward.__module__.startswith('parallel_eagle_b200')\n"
@@ -219,3 +220,12 @@ def test_propose_chain_sampling_rejects_non_positive_temperature():
     for t in (0.0, -0.5, float("nan")):
         with pytest.raises(ValueError):
             decode.propose_chain_sampling(None, None, None, 3, t)
+
+
+def test_verification_rejects_empty_prefix():
+    from parallel_eagle_b200 import decode
+
+    with pytest.raises(ValueError):
+        decode.accept_chain_greedy(torch.zeros(3, 5), 0, [1, 2])
+    with pytest.raises(ValueError):
+        decode.accept_tree_greedy(torch.zeros(3, 5), 0, [1], [-1])
