@@ -229,3 +229,29 @@ def test_verification_rejects_empty_prefix():
         decode.accept_chain_greedy(torch.zeros(3, 5), 0, [1, 2])
     with pytest.raises(ValueError):
         decode.accept_tree_greedy(torch.zeros(3, 5), 0, [1], [-1])
+
+
+def test_reference_arm_sample_length_bounds_the_run():
+    """bench.py --impl reference: each sample is the workload's own n unless the
+    warm-up + timed samples would exceed the run budget, then a shorter multiple of
+    256 (never below 256)."""
+    import argparse
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+
+    def n_for(sec256, warmup=3, steps=5, cpu_n=2048):
+        return bench.reference_sample_len(
+            argparse.Namespace(cpu_n=cpu_n, warmup=warmup, steps=steps), sec256)
+
+    assert n_for(1.6) == 2048                      # fast host: the full sequence
+    assert n_for(5.3) == 768                       # slow host: shortened
+    assert n_for(1.6, warmup=5, steps=20) == 768   # many steps: shortened
+    assert n_for(60.0) == 256                      # never below 256
+    assert n_for(0.1, cpu_n=512) == 512            # never above --cpu-n
+    for sec, w, k in ((1.6, 3, 5), (5.3, 3, 5), (1.6, 5, 20)):
+        n = n_for(sec, w, k)
+        assert n % 256 == 0
+        assert (max(0, w - 1) + k) * 1.1 * sec * n / 256 <= bench.REF_BUDGET_S
