@@ -255,3 +255,22 @@ def test_reference_arm_sample_length_bounds_the_run():
         n = n_for(sec, w, k)
         assert n % 256 == 0
         assert (max(0, w - 1) + k) * 1.1 * sec * n / 256 <= bench.REF_BUDGET_S
+
+
+def test_speculative_sampling_acceptance_is_lossless():
+    """Property of the acceptance rule (reference decode/verify.py:75-101): with the
+    draft drawn from q, the first emitted token -- the first draft if kept, else the
+    residual bonus -- is distributed as the target's p, whatever q is."""
+    from parallel_eagle_b200 import decode
+
+    g = torch.Generator().manual_seed(3)
+    V, trials = 6, 6000
+    p = torch.softmax(torch.randn(2, V, generator=g) * 1.5, -1)
+    q = torch.softmax(torch.randn(1, V, generator=g) * 1.5, -1)
+    counts = torch.zeros(V)
+    for _ in range(trials):
+        draft = [int(torch.multinomial(q[0], 1, generator=g))]
+        acc, bonus = decode.accept_chain_sampling(p, draft, q, generator=g)
+        counts[acc[0] if acc else bonus] += 1
+    tv = 0.5 * (counts / trials - p[0]).abs().sum().item()
+    assert tv < 0.03, tv
