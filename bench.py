@@ -135,6 +135,16 @@ def _dist():
     return ws, rank, local
 
 
+def workload_config(workload, c, world):
+    """The ``config`` object of a bench line: the workload's shape, identical in this
+    framework's arm and the reference arm."""
+    return {"workload": workload, "hidden": c["hidden"], "heads": [c["n_heads"], c["n_kv_heads"]],
+            "intermediate": c["intermediate"], "vocab": c["vocab"], "layers": c["num_layers"],
+            "n": c["n"], "K": c["max_depth"], "S": c["segments"], "batch_per_gpu": c["batch"],
+            "global_batch": c["batch"] * world, "parallelism": f"dp{world}",
+            "l2": "inputs larger than L2 (features 44 MB/sequence, weights 0.5 GB)"}
+
+
 def make_heads_gpu(c, dev, seed=0):
     g = torch.Generator(device=dev).manual_seed(10_000 + seed)
     V, H = c["vocab"], c["hidden"]
@@ -190,15 +200,25 @@ class Trainer:
         self.lr = lr
         self.t = 0
         self.overlap = None
+        # (step start, all-reduce finish entered, finish returned) events per step (N > 1)
+        self.comm_events = []
+        self.record_comm = False
         if world > 1:
             from parallel_eagle_b200.train import OverlappedAllReduce
 
             self.overlap = OverlappedAllReduce(drafter)
 
+    def _event(self):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(torch.cuda.current_stream())
+        return e
+
     def step(self, seqs, global_batch, teachers=None):
         from parallel_eagle_b200 import ops
 
         fp = self.eng.flat
+        rec = self.record_comm and self.overlap is not None
+        ev0 = self._event() if rec else None
         fp.grad.zero_()
         self.loss.zero_()
         for i, (ids, feats) in enumerate(seqs):
@@ -208,7 +228,10 @@ class Trainer:
                          teacher_hidden=None if teachers is None else teachers[i])
             self.loss += self.eng.loss_sum
         if self.overlap is not None:
+            ev1 = self._event() if rec else None
             self.overlap.finish()
+            if rec:
+                self.comm_events.append((ev0, ev1, self._event()))
         self.sumsq.zero_()
         ops.sumsq_into(fp.grad, self.sumsq)
         self.t += 1
@@ -260,6 +283,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     l0 = _lib.launch_count()
+    trainer.record_comm = True
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
@@ -273,13 +297,19 @@ def run_ours(args):
         torch.cuda.synchronize()
     barrier()
     launches = (_lib.launch_count() - l0) // max(1, args.steps)
+    trainer.record_comm = False
     ms = e0.elapsed_time(e1) / args.steps
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    dp = data_parallel_report(trainer, clocks, world, dev) if world > 1 else None
     value = gb * n * k / (ms / 1e3)
-    loss_val = float(trainer.loss.item()) / B
+    from parallel_eagle_b200.engine import count_loss_slots
+
+    # mean cross entropy per loss slot over this rank's sequences after the timed
+    # updates (the same fixed synthetic sequences are trained on every step)
+    loss_val = float(trainer.loss.item()) / (B * count_loss_slots(n, k))
 
     # ---- end to end through the public API: pinned host inputs, loss read back
     from parallel_eagle_b200.partition import mtp_backward
@@ -341,13 +371,8 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded ids ~ U[0,V), features ~ N(0,1), heads ~ N(0,0.02^2))",
-            "config": {"workload": workload, "hidden": c["hidden"],
-                       "heads": [c["n_heads"], c["n_kv_heads"]], "intermediate": c["intermediate"],
-                       "vocab": c["vocab"], "layers": c["num_layers"], "n": n, "K": k,
-                       "S": c["segments"], "batch_per_gpu": B, "global_batch": gb,
-                       "parallelism": f"dp{world}",
-                       "l2": "inputs larger than L2 (features 44 MB/sequence, weights 0.5 GB)"},
-            "loss": round(loss_val, 4),
+            "config": workload_config(workload, c, world),
+            "loss_ce_per_slot": round(loss_val, 4),
             "step_tflops": round(step_tflops, 1),
             "step_frac_of_peak": round(step_tflops / peak_sus, 4),
             "e2e": {"value": round(gb * n * k / (e2e_ms / 1e3), 1), "unit": UNIT,
@@ -360,9 +385,47 @@ def run_ours(args):
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
+        if dp is not None:
+            line["data_parallel"] = dp
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def data_parallel_report(trainer, clocks, world, dev):
+    """Per-rank split of the timed steps (N > 1) and a cross-rank consistency check.
+
+    compute_ms: step start -> the all-reduce's ``finish()`` (the local sequences'
+    forward/backward, with the layers' reduction already running beside the input
+    projections' backward); exposed_comm_ms: ``finish()`` entered -> returned on the
+    compute stream (the reduction time the backward did not hide).  Both are CUDA-event
+    means over the timed steps.  The flat parameters after the last update are
+    checksummed on every rank; ranks that differ fail the run."""
+    import torch.distributed as dist
+
+    comp = sum(a.elapsed_time(b) for a, b, _ in trainer.comm_events) / len(trainer.comm_events)
+    expo = sum(b.elapsed_time(c) for _, b, c in trainer.comm_events) / len(trainer.comm_events)
+    trainer.comm_events.clear()
+    sm = clocks.summary().get("sm_mhz") or 0.0
+    flat = trainer.eng.flat.flat
+    words = flat.view(torch.int16).to(torch.int64)
+    pos = torch.arange(words.numel(), device=dev, dtype=torch.int64) % 65521
+    mine = torch.stack([words.sum(), (words * pos).sum()])
+    sums = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(sums, mine)
+    stats = torch.tensor([comp, expo, float(sm)], device=dev, dtype=torch.float64)
+    per = [torch.empty_like(stats) for _ in range(world)]
+    dist.all_gather(per, stats)
+    same = all(torch.equal(sums[0], x) for x in sums[1:])
+    if not same:
+        raise RuntimeError("data-parallel ranks hold different parameters after the update")
+    per = [x.tolist() for x in per]
+    return {"rank_compute_ms": [round(x[0], 2) for x in per],
+            "rank_exposed_comm_ms": [round(x[1], 3) for x in per],
+            "exposed_comm_ms": round(max(x[1] for x in per), 3),
+            "rank_sm_mhz": [x[2] for x in per],
+            "params_identical_across_ranks": same,
+            "grad_bytes": int(trainer.eng.flat.grad.numel() * trainer.eng.flat.grad.element_size())}
 
 
 def gemm_case(c, dev):
@@ -704,40 +767,40 @@ def cpu_baseline(args, n=None):
             "seconds": round(sec, 2)}
 
 
-REF_BUDGET_S = 150.0  # the whole --impl reference run, warm-up and timed samples
-
-
-def reference_sample_len(args, sec_at_256: float) -> int:
-    """Sequence length of each reference-arm sample: the workload's own n (--cpu-n)
-    unless warmup + steps samples of it would exceed REF_BUDGET_S, then the longest
-    multiple of 256 that fits (CPU time grows about linearly with n here)."""
-    per_row = 1.1 * sec_at_256 / 256
-    samples = max(0, args.warmup - 1) + max(1, args.steps)
-    fit = int(REF_BUDGET_S / samples / per_row) // 256 * 256
-    return max(256, min(args.cpu_n, fit))
+REF_BUDGET_S = 420.0  # timed samples of the --impl reference run stop once past this
 
 
 def run_reference(args):
+    """The reference arm: the CPU port of the reference step (pinned to the reference's
+    own outputs) on the host cores, on this framework's workload.  Warm-up steps are
+    short samples (n = 256: they page in the weights and warm the allocator); each
+    timed step is one full sequence of the workload (n = 2048, K 5, S 4, bf16).  Timed
+    samples stop early, after at least three, once their total passes REF_BUDGET_S, and
+    the line reports how many ran."""
     world, rank, _ = _dist()
     if rank != 0:
         return
-    # the first warm-up sample is a short one that calibrates the host's speed
-    cal = cpu_baseline(args, n=256)
-    n = reference_sample_len(args, cal["seconds"])
-    for _ in range(max(0, args.warmup - 1)):
-        cpu_baseline(args, n=n)
-    samples = [cpu_baseline(args, n=n) for _ in range(max(1, args.steps))]
+    workload, base = WORKLOADS[2]
+    c = dict(base)
+    for _ in range(max(1, args.warmup)):
+        cpu_baseline(args, n=256)
+    samples = []
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.steps)):
+        samples.append(cpu_baseline(args, n=c["n"]))
+        if len(samples) >= 3 and time.perf_counter() - t0 > REF_BUDGET_S:
+            break
     sec = sum(s["seconds"] for s in samples) / len(samples)
-    value = n * CONFIG2["max_depth"] / sec
+    value = c["n"] * c["max_depth"] / sec
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "BASELINE config 2: 7B-class drafter step", "n": n,
-                   "K": 5, "S": 4, "parallelism": "cpu"},
+        "n_gpus": world, "steps": len(samples), "steps_requested": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(workload, c, world),
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": samples[0]["cores"],
-                         "kind": "port", "sample": samples[0]["sample"]},
+                         "kind": "port",
+                         "sample": "each timed step: " + samples[0]["sample"]},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

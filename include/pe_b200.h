@@ -247,6 +247,16 @@ int pe_adamw_step(int dtype, int64_t n, void* p, const void* g, float* m, float*
                   const float* sumsq, float max_norm, float lr, float beta1, float beta2,
                   float eps, float weight_decay, int64_t step, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Self-test of the bounded-wait unwind path (no counterpart in the reference).
+ * One warp allocates tensor memory, waits on an mbarrier that nothing arrives at,
+ * gives up after limit_ns (1 us .. 10 s), writes code 901 into *status (first
+ * writer wins, as in every tensor-core kernel), frees its tensor memory and
+ * returns; *waited_out = 1 if the wait ran out.  The tensor-core kernels use the
+ * same wait with a 4 s limit.
+ * ------------------------------------------------------------------------- */
+int pe_wait_probe(uint64_t limit_ns, int32_t* status, int32_t* waited_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

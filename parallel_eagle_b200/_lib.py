@@ -84,6 +84,7 @@ SIGNATURES: dict[str, tuple] = {
     "pe_adamw_step": (
         _int, [_int, _i64, _vp, _vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32, _f32, _f32, _i64, _vp]
     ),
+    "pe_wait_probe": (_int, [C.c_uint64, _vp, _vp, _vp]),
 }
 
 _lock = threading.Lock()

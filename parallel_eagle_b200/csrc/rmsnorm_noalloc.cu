@@ -16,6 +16,8 @@
 // so calls that overlap on the GPU (concurrent streams, or several host threads
 // on one device) race; serialise them.  Every call rewrites all the partial rows
 // it later reads, so no clearing is needed between calls.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace pe {
@@ -28,7 +30,11 @@ constexpr int kWarps = 8;
 static __device__ __align__(256) float g_dw_scratch[kNoAllocBlocks * kNoAllocMaxH];
 
 // Per device: the device address of g_dw_scratch (nullptr until looked up).
-static float* g_scratch_ptr[64] = {nullptr};
+// Per-device cache of the array's device address.  Concurrent first calls may both
+// look it up; each stores the same address, and the atomic keeps the store whole.
+static std::atomic<float*> g_scratch_ptr[64];
+// one partial row per CTA is staged in shared memory: within the default 48 KiB
+static_assert(kNoAllocMaxH * sizeof(float) <= 48 * 1024, "partial row exceeds static smem");
 
 template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
@@ -81,12 +87,14 @@ int scratch_for_current_device(float** out) {
   int dev = 0;
   PE_CUDA_TRY(cudaGetDevice(&dev));
   PE_CHECK_ARG(dev >= 0 && dev < 64, "rmsnorm_bwd_noalloc: device index %d out of range", dev);
-  if (g_scratch_ptr[dev] == nullptr) {
+  float* cached = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (cached == nullptr) {
     void* p = nullptr;
     PE_CUDA_TRY(cudaGetSymbolAddress(&p, g_dw_scratch));
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+    cached = static_cast<float*>(p);
+    g_scratch_ptr[dev].store(cached, std::memory_order_release);
   }
-  *out = g_scratch_ptr[dev];
+  *out = cached;
   return PE_OK;
 }
 
@@ -119,8 +127,6 @@ extern "C" int pe_rmsnorm_bwd_noalloc(int dtype, int64_t rows, int64_t H, const 
   cudaStream_t st = as_stream(stream);
   return PE_DISPATCH(dtype, T, [&] {
     auto kern = rmsnorm_bwd_scratch_kernel<T>;
-    if (smem > 48 * 1024)
-      PE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     kern<<<nblk, kWarps * 32, smem, st>>>(rows, H, (const T*)dy, lddy, (const T*)x, ldx,
                                           (const T*)w, rstd, (T*)dx, lddx, (const T*)residual,
                                           ldres, scratch);

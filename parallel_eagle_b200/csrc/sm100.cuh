@@ -55,15 +55,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for phase `parity` of `bar`.  On timeout writes `code` into
-// *status (first writer wins) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+// Bounded wait for phase `parity` of `bar`.  On timeout (after `limit_ns`; the
+// kernels use kWaitLimitNs) writes `code` into *status (first writer wins) and
+// returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 1023u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+    if ((++spins & 1023u) == 0 && globaltimer() - t0 > limit_ns) {
       if (status) atomicCAS(status, 0, code);
       return false;
     }

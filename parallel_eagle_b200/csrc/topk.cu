@@ -24,13 +24,18 @@ constexpr int kThreads = 512;
 __device__ __forceinline__ float load_f(const float* p) { return *p; }
 __device__ __forceinline__ float load_f(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
-// (value, column) ordered by value descending, then column ascending
+// (value, column) ordered by value descending, then column ascending; NaN ranks
+// above every number, as in torch.topk / torch.argmax (an all-NaN row therefore
+// yields its first columns, never an out-of-range index)
 struct Cand {
   float v;
   int64_t i;
 };
 __device__ __forceinline__ bool before(const Cand& a, const Cand& b) {
-  return a.v > b.v || (a.v == b.v && a.i < b.i);
+  const bool an = a.v != a.v, bn = b.v != b.v;
+  if (an != bn) return an;
+  if (!an && a.v != b.v) return a.v > b.v;
+  return a.i < b.i;
 }
 
 __device__ Cand block_best(Cand c, Cand* red) {
@@ -102,7 +107,7 @@ topk_logprobs_kernel(int64_t V, const T* __restrict__ logits, int64_t ld, int k,
     s = block_reduce(s, fred, false);
     logs = logf(s);
   }
-  Cand prev{INFINITY, -1};  // everything comes after it
+  Cand prev{__int_as_float(0x7fffffff), -1};  // a NaN at column -1: everything comes after it
   for (int r = 0; r < k; ++r) {
     Cand best{-INFINITY, INT64_MAX};
     for (int64_t v = threadIdx.x; v < V; v += kThreads) {

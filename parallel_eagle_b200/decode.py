@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import torch
 
+from . import _lib as L
 from . import ops
 
 
@@ -92,8 +93,14 @@ def propose_chain_sampling(drafter, context_ids: torch.Tensor, context_feats: to
 
 
 def _argmax_rows(rows: torch.Tensor) -> list[int]:
-    if rows.dtype not in (torch.float32, torch.bfloat16):
-        rows = rows.float()  # exact for fp16, so the argmax is unchanged
+    """First maximal column of each row (``torch.argmax``; NaN ranks highest) for
+    float32, bfloat16 or float16 logits.  float16 is widened to float32, which is
+    exact; other dtypes (float64 included, whose distinct maxima could round to
+    equal float32 values) are rejected rather than silently rounded."""
+    if rows.dtype == torch.float16:
+        rows = rows.float()
+    elif rows.dtype not in (torch.float32, torch.bfloat16):
+        raise L.PeError(f"target logits must be float32, bfloat16 or float16, got {rows.dtype}")
     if rows.stride(-1) != 1:
         rows = rows.contiguous()
     _, idx = ops.topk_logprobs(rows, 1, raw=True)

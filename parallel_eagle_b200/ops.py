@@ -478,3 +478,15 @@ def adamw_step(p, g, m, v, sumsq, max_norm, lr, beta1, beta2, eps, weight_decay,
                               float(beta1), float(beta2), float(eps), float(weight_decay), int(step),
                               L.stream_ptr(p.device))
     L.check(rc, "pe_adamw_step")
+
+
+def wait_probe(device: torch.device, limit_ns: int) -> bool:
+    """Run the bounded-wait self-test kernel on ``device``: a wait that nothing
+    completes gives up after ``limit_ns``, records code 901 in the device's status
+    word and unwinds.  Returns whether the wait ran out (read back with a sync);
+    :func:`check_status` then raises for the recorded code."""
+    waited = torch.zeros(1, dtype=torch.int32, device=device)
+    rc = _lib().pe_wait_probe(int(limit_ns), status_word(device).data_ptr(), waited.data_ptr(),
+                              L.stream_ptr(device))
+    L.check(rc, "pe_wait_probe")
+    return bool(waited.item())

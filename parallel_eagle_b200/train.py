@@ -203,7 +203,10 @@ def train(tcfg: TargetConfig, dcfg: DrafterConfig, tr: TrainConfig, dtype: str =
     param_dtype = _DTYPES[dtype]
     world, rank = _world()
 
-    data = FeatureDataset(tr.feature_cache_dir, with_prompt_len=True)
+    # shards are read into page-locked memory on CUDA runs, so each sequence's
+    # host->device copy is an asynchronous DMA on the step's stream
+    on_cuda = torch.device(tcfg.device).type == "cuda"
+    data = FeatureDataset(tr.feature_cache_dir, with_prompt_len=True, pin_memory=on_cuda)
     if data.self_distilled:
         print("self-distilled cache detected — masking prompt region out of the loss")
     if data.heads_dump.exists():

@@ -129,8 +129,11 @@ def test_propose_chain_sampling_matches_reference_draw():
                                                 generator=torch.Generator(device=DEV).manual_seed(seed))
         logits = model.draft_logits(ids, feats, 5)
         ref_q = torch.softmax(logits.float() / temp, dim=-1)
-        ref = torch.multinomial(ref_q, 1, generator=torch.Generator(device=DEV).manual_seed(seed))
         assert torch.allclose(q, ref_q, rtol=1e-5, atol=1e-10)
+        # the draw: torch.multinomial on the returned q with the caller's seeded
+        # generator (drawing on torch's own softmax instead could flip a token whose
+        # cumulative probability sits within the two q's 1e-5 of a draw boundary)
+        ref = torch.multinomial(q, 1, generator=torch.Generator(device=DEV).manual_seed(seed))
         assert toks == [int(t) for t in ref.squeeze(-1).tolist()]
         assert len(toks) == 5 and all(0 <= t < 1000 for t in toks)
 
@@ -161,3 +164,27 @@ def test_verification_rules_match_reference_golden():
         ref = ov.accept_chain_sampling(td, c["sample_draft"], qd,
                                        generator=torch.Generator(device=DEV).manual_seed(c["seed"]))
         assert got == ref
+
+
+def test_argmax_and_topk_rank_nan_like_torch():
+    """NaN ranks above every number (torch.argmax / torch.topk): a row with NaNs
+    selects its first NaN column, an all-NaN row its first columns -- never an
+    out-of-range index.  float64 target logits are rejected, not rounded."""
+    from parallel_eagle_b200 import _lib as L
+    from parallel_eagle_b200 import decode, ops
+
+    z = torch.randn(3, 1000, generator=torch.Generator().manual_seed(4))
+    z[0, 9] = float("nan")
+    z[0, 5] = float("nan")
+    z[1, :] = float("nan")
+    for dt in (torch.float32, torch.bfloat16):
+        idx, _ = ops.topk_logprobs(z.to(dt).to(DEV), 3, raw=True)
+        idx = idx.cpu()
+        zr = z.to(dt).float()
+        assert idx[0].tolist() == [5, 9, int(zr[0].nan_to_num(-1e9).argmax())]
+        assert idx[1].tolist() == [0, 1, 2]
+        assert zr[2][idx[2]].tolist() == torch.topk(zr[2], 3).values.tolist()
+        assert int(idx[0, 0]) == int(torch.argmax(zr[0]))
+        assert decode._argmax_rows(z.to(dt).to(DEV)) == [5, 0, int(torch.argmax(z[2].to(dt)))]
+    with pytest.raises(L.PeError):
+        decode._argmax_rows(z.double().to(DEV))

@@ -231,30 +231,45 @@ def test_verification_rejects_empty_prefix():
         decode.accept_tree_greedy(torch.zeros(3, 5), 0, [1], [-1])
 
 
-def test_reference_arm_sample_length_bounds_the_run():
-    """bench.py --impl reference: each sample is the workload's own n unless the
-    warm-up + timed samples would exceed the run budget, then a shorter multiple of
-    256 (never below 256)."""
+def test_reference_arm_times_the_full_workload_within_its_budget(monkeypatch, capsys):
+    """bench.py --impl reference: warm-up samples are short (n = 256), every timed
+    sample is one full sequence of the workload (n = 2048), the config equals this
+    framework's arm's, and timed samples stop (after at least three) once they pass
+    the budget."""
     import argparse
+    import json
     import sys
     from pathlib import Path
 
     sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
     import bench
 
-    def n_for(sec256, warmup=3, steps=5, cpu_n=2048):
-        return bench.reference_sample_len(
-            argparse.Namespace(cpu_n=cpu_n, warmup=warmup, steps=steps), sec256)
+    def fake_run(per_sample_s, steps, warmup):
+        clock = {"t": 0.0}
+        calls = []
 
-    assert n_for(1.6) == 2048                      # fast host: the full sequence
-    assert n_for(5.3) == 768                       # slow host: shortened
-    assert n_for(1.6, warmup=5, steps=20) == 768   # many steps: shortened
-    assert n_for(60.0) == 256                      # never below 256
-    assert n_for(0.1, cpu_n=512) == 512            # never above --cpu-n
-    for sec, w, k in ((1.6, 3, 5), (5.3, 3, 5), (1.6, 5, 20)):
-        n = n_for(sec, w, k)
-        assert n % 256 == 0
-        assert (max(0, w - 1) + k) * 1.1 * sec * n / 256 <= bench.REF_BUDGET_S
+        def fake_cpu(args, n=None):
+            calls.append(n)
+            sec = per_sample_s * n / 2048
+            clock["t"] += sec
+            return {"seconds": sec, "cores": 4, "sample": f"one sequence, n={n}"}
+
+        monkeypatch.setattr(bench, "cpu_baseline", fake_cpu)
+        monkeypatch.setattr(bench.time, "perf_counter", lambda: clock["t"])
+        capsys.readouterr()
+        bench.run_reference(argparse.Namespace(steps=steps, warmup=warmup, cpu_n=2048))
+        return calls, json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+
+    calls, line = fake_run(11.0, steps=20, warmup=5)
+    assert calls == [256] * 5 + [2048] * 20
+    assert line["steps"] == 20 and line["config"]["n"] == 2048
+    assert line["value"] == round(2048 * 5 / 11.0, 2)
+    ours = bench.workload_config(bench.WORKLOADS[2][0], dict(bench.CONFIG2), 1)
+    assert line["config"] == ours
+    # a slow host: the budget cuts the timed samples short, never below three
+    calls, line = fake_run(200.0, steps=20, warmup=3)
+    assert calls[3:] == [2048] * 3 and line["steps"] == 3 and line["steps_requested"] == 20
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["impl"] == "reference"
 
 
 def test_speculative_sampling_acceptance_is_lossless():
