@@ -609,47 +609,75 @@ def attention_roofline(c, dev, peak, src):
 
 
 def run_sweep(args):
-    """BASELINE config 5 on one GPU: config-2 dims, batch 4, n in {256..4096}, K in {4, 8},
-    S in {1, 2, 4, 8}; per point one JSON line with peak HBM, slot-tokens/s and the
-    masked-attention fwd+bwd TFLOP/s of one sequence."""
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    """config-2 dims, batch 4 per GPU, n in {256..4096}, K in {4, 8},
+    S in {1, 2, 4, 8} (``--sweep-n`` / ``--sweep-k`` / ``--sweep-s`` pick a subset); per
+    point one JSON line (rank 0) with peak HBM, slot-tokens/s and the masked-attention
+    fwd+bwd TFLOP/s of one sequence.  Under torchrun every rank trains its own 4
+    sequences and the update all-reduces the gradients (weak scaling); step time and
+    peak HBM are the max over ranks."""
+    import torch.distributed as dist
+
     from parallel_eagle_b200 import ops
 
+    world, rank, local = _dist()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=600))
+
+    def max_over_ranks(x):
+        t = torch.tensor([float(x)], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     _, peak_burst, _, src = _peaks()
-    for K in (4, 8):
+    ns = [int(x) for x in args.sweep_n.split(",")]
+    ks = [int(x) for x in args.sweep_k.split(",")]
+    ss = [int(x) for x in args.sweep_s.split(",")]
+    for K in ks:
         c = dict(CONFIG2, batch=4, max_depth=K)
         drafter = build_drafter(c, dev, seed=0)
-        trainer = Trainer(drafter, c, 1)
-        for n in (256, 512, 1024, 2048, 4096):
-            g = torch.Generator(device=dev).manual_seed(n)
+        trainer = Trainer(drafter, c, world)
+        for n in ns:
+            g = torch.Generator(device=dev).manual_seed(n * 131 + rank)
             ids = torch.randint(0, c["vocab"], (c["batch"], n), generator=g, device=dev)
             feats = torch.randn(c["batch"], n, 3 * c["hidden"], generator=g,
                                 device=dev).to(torch.bfloat16)
             seqs = [(ids[b], feats[b]) for b in range(c["batch"])]
-            for S in (1, 2, 4, 8):
+            gb = c["batch"] * world
+            for S in ss:
                 cs = dict(c, n=n, segments=S)
                 trainer.c = cs
-                trainer.step(seqs, c["batch"])
+                trainer.step(seqs, gb)
                 torch.cuda.synchronize()
                 torch.cuda.reset_peak_memory_stats(dev)
                 base = torch.cuda.memory_allocated(dev)
-                ms = time_case(lambda: trainer.step(seqs, c["batch"]), max(1, args.steps), warmup=1)
-                peak = torch.cuda.max_memory_allocated(dev)
+                if world > 1:
+                    dist.barrier()
+                ms = max_over_ranks(time_case(lambda: trainer.step(seqs, gb), max(1, args.steps),
+                                              warmup=1))
+                peak = max_over_ranks(torch.cuda.max_memory_allocated(dev))
+                above = max_over_ranks(torch.cuda.max_memory_allocated(dev) - base)
                 run, flops, _ = attention_case(cs, dev)
-                ams = time_case(run, 3, warmup=1)
+                ams = max_over_ranks(time_case(run, 3, warmup=1))
                 ops.check_status(dev)
-                print(json.dumps({
-                    "sweep": "BASELINE config 5", "n": n, "K": K, "S": S, "batch": c["batch"],
-                    "ms_per_step": round(ms, 3),
-                    "slot_tokens_per_s": round(c["batch"] * n * K / (ms / 1e3), 1),
-                    "peak_hbm_gb": round(peak / 1e9, 2),
-                    "peak_hbm_above_resident_gb": round((peak - base) / 1e9, 2),
-                    "attn_fwd_bwd_tflops": round(flops / (ams / 1e3) / 1e12, 1),
-                    "attn_frac_of_peak": round(flops / (ams / 1e3) / 1e12 / peak_burst, 4),
-                    "peak_source": f"{src} bf16_tflops (burst)"}), flush=True)
+                if rank == 0:
+                    print(json.dumps({
+                        "sweep": "BASELINE config 5", "n_gpus": world, "n": n, "K": K, "S": S,
+                        "batch_per_gpu": c["batch"], "global_batch": gb,
+                        "ms_per_step": round(ms, 3),
+                        "slot_tokens_per_s": round(gb * n * K / (ms / 1e3), 1),
+                        "peak_hbm_gb": round(peak / 1e9, 2),
+                        "peak_hbm_above_resident_gb": round(above / 1e9, 2),
+                        "attn_fwd_bwd_tflops": round(flops / (ams / 1e3) / 1e12, 1),
+                        "attn_frac_of_peak": round(flops / (ams / 1e3) / 1e12 / peak_burst, 4),
+                        "peak_source": f"{src} bf16_tflops (burst)"}), flush=True)
         del trainer, drafter
         torch.cuda.empty_cache()
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def run_kernel(args):
@@ -671,6 +699,29 @@ def run_kernel(args):
                          "frac_of_hbm": round(gbs / hbm, 3)}
         ops.check_status(dev)
         print(json.dumps({"kernel": "elementwise", "hbm_peak_gbs": hbm, "peak_source": src,
+                          "results": out}), flush=True)
+        return
+    if args.kernel == "swiglu":
+        # the step's gate|up projection over one stacked config-2 pass (13312 slot rows):
+        # plain GEMM + element-wise SwiGLU against the GEMM with the SwiGLU epilogue
+        H, I, M = c["hidden"], c["intermediate"], 13312
+        g = torch.Generator(device=dev).manual_seed(19)
+        x = torch.randn(M, H, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(2 * I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        gu = torch.empty(M, 2 * I, dtype=torch.bfloat16, device=dev)
+        act = torch.empty(M, I, dtype=torch.bfloat16, device=dev)
+        flops = 2.0 * M * 2 * I * H
+        out = {}
+        runs = {"gemm_then_swiglu": lambda: ops.swiglu_fwd(ops.linear(x, w, out=gu), I, out=act),
+                "gemm_only": lambda: ops.linear(x, w, out=gu)}
+        for bn in (0, 256, 512):
+            runs[f"fused_bn{bn or 'auto'}"] = (
+                lambda bn=bn: ops.linear_swiglu(x, w, I, gu=gu, act=act, algo=bn << 8))
+        for name, fn in runs.items():
+            ms = time_case(fn, args.steps, warmup=args.warmup)
+            out[name] = {"ms": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
+        ops.check_status(dev)
+        print(json.dumps({"kernel": "gate|up + swiglu", "M": M, "N": 2 * I, "K": H,
                           "results": out}), flush=True)
         return
     case = {"gemm": gemm_case, "attn": attention_case, "lmhead": lmhead_case}[args.kernel]
@@ -821,8 +872,12 @@ def main(argv=None):
     ap.add_argument("--config", type=int, choices=[2, 3, 4], default=2,
                     help="BASELINE workload: 2 (default), 3 soft-target loss, 4 14B-class")
     ap.add_argument("--sweep", action="store_true",
-                    help="BASELINE config 5: peak HBM / throughput over n, K, S (1 GPU)")
-    ap.add_argument("--kernel", choices=["gemm", "attn", "lmhead", "elementwise"], default=None,
+                    help="BASELINE config 5: peak HBM / throughput over n, K, S (torchrun: DP)")
+    ap.add_argument("--sweep-n", default="256,512,1024,2048,4096")
+    ap.add_argument("--sweep-k", default="4,8")
+    ap.add_argument("--sweep-s", default="1,2,4,8")
+    ap.add_argument("--kernel", choices=["gemm", "attn", "lmhead", "elementwise", "swiglu"],
+                    default=None,
                     help="time one kernel family on its bench-sized case instead of the step")
     ap.add_argument("--draft", action="store_true",
                     help="time the draft path (draft_logits / propose_tree) on config-2 dims")

@@ -89,6 +89,13 @@ int pe_colsum_f32(int dtype, int64_t nblk, int64_t H, const float* partial, void
  * ------------------------------------------------------------------------- */
 int pe_rope(int dtype, int64_t rows, int heads, int head_dim, void* x, int64_t ldx,
             const int64_t* pos, float theta, int inverse, void* stream);
+/* The cos / sin table the fused rotations read: row r (stride ld >= head_dim) holds
+ * cos(pos[r] f_p) for p < head_dim/2, then sin(pos[r] f_p), rounded to dtype, with
+ * the same angles and rounding as pe_rope (reference src/pe/nn.py:29-40,
+ * build_rope_cache).  Positions are fixed per slot layout, so a caller builds the
+ * table once per layout and reuses it. */
+int pe_rope_table(int dtype, int64_t rows, int head_dim, const int64_t* pos, float theta,
+                  void* cs, int64_t ld, void* stream);
 
 /* ---------------------------------------------------------------------------
  * GEMM  C[m,n] = alpha * sum_k A(m,k) B(n,k) + beta * Cin[m,n]
@@ -106,6 +113,32 @@ int pe_gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a
             int64_t a_sk, const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc,
             int c_dtype, const void* Cin, int64_t ldcin, float alpha, float beta, int algo,
             int32_t* status, void* stream);
+
+/* y = x w^T (bf16; x [M, K], w [N, K], both row-major with unit column stride) with
+ * the rotary embedding applied in the GEMM epilogue to the head_dim-wide column
+ * blocks of [0, rot_cols) using the pe_rope_table table rope_cs (row m of the table
+ * for row m of y): the fused q|k|v projection + RoPE of reference
+ * src/pe/nn.py:75-80 (q/k/v_proj then apply_rope).  Bit-identical to pe_gemm
+ * followed by pe_rope.  Tensor-core path only: dtype bf16, head_dim 128, N and
+ * rot_cols multiples of 128, 16-byte aligned rows. */
+int pe_linear_rope(int dtype, int64_t M, int64_t N, int64_t K, const void* x, int64_t ldx,
+                   const void* w, int64_t ldw, void* y, int64_t ldy, const void* rope_cs,
+                   int64_t cs_ld, int64_t rot_cols, int head_dim, int32_t* status,
+                   void* stream);
+
+/* gu = x w_gu^T ([M, 2I]: gate columns [0, I), up columns [I, 2I); w_gu rows [0, I)
+ * gate_proj, [I, 2I) up_proj, all row-major with unit column stride) and
+ * act = silu(gate) * up ([M, I]), each rounded to dtype as pe_gemm then
+ * pe_swiglu_fwd would round them (bit-identical): the SwiGLU MLP's gate / up
+ * projections and activation (reference src/pe/nn.py:99-100).  On the bf16
+ * tensor-core path with CTA-pair tiles (M >= 512, I a multiple of half the tile
+ * width) the activation is computed in the GEMM epilogue -- each tile loads
+ * matching gate and up weight rows -- so gu is not re-read; otherwise the GEMM and
+ * the element-wise kernel run back to back.  algo bits 8-17 may force the pair
+ * tile width (256 or 512). */
+int pe_linear_swiglu(int dtype, int64_t M, int64_t I, int64_t K, const void* x, int64_t ldx,
+                     const void* w_gu, int64_t ldw, void* gu, int64_t ldgu, void* act,
+                     int64_t lda, int algo, int32_t* status, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Cross-depth masked attention (GQA, scale = 1/sqrt(head_dim)), flash-style:
@@ -164,13 +197,20 @@ int pe_attn_fwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth,
                          float* lse, int algo, int32_t* status, void* stream);
 size_t pe_attn_bwd_segments_workspace(int dtype, int nseg, const int64_t* bounds, int kdepth,
                                       int Hq, int Hkv, int head_dim);
+/* rope_cs (may be NULL): a pe_rope_table table with one row per stacked slot row
+ * (row stride cs_ld elements, dtype as the operands).  With it q and k are the
+ * rotated projections and dq / dk are returned rotated back by the transpose of the
+ * rotary embedding -- the gradients with respect to the unrotated projections, as
+ * pe_rope(inverse = 1) on the plain result would give, bit for bit.  On the
+ * tensor-core path the rotation is fused into the dQ store and the dK cast. */
 int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth, int Hq,
                          int Hkv, int head_dim, const void* q, int64_t q_ss, const void* k,
                          int64_t k_ss, const void* v, int64_t v_ss, const void* o,
                          int64_t o_ss, const void* dout, int64_t do_ss, const float* lse,
                          void* dq, int64_t dq_ss, void* dk, int64_t dk_ss, void* dv,
-                         int64_t dv_ss, void* workspace, size_t workspace_bytes, int algo,
-                         int32_t* status, void* stream);
+                         int64_t dv_ss, void* workspace, size_t workspace_bytes,
+                         const void* rope_cs, int64_t cs_ld, int algo, int32_t* status,
+                         void* stream);
 
 /* ---------------------------------------------------------------------------
  * Frozen shared LM head fused with the loss and its input gradient, chunked

@@ -36,6 +36,14 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "pe_colsum_f32": (_int, [_int, _i64, _i64, _vp, _vp, _int, _vp]),
     "pe_rope": (_int, [_int, _i64, _int, _int, _vp, _i64, _vp, _f32, _int, _vp]),
+    "pe_rope_table": (_int, [_int, _i64, _int, _vp, _f32, _vp, _i64, _vp]),
+    "pe_linear_swiglu": (
+        _int, [_int, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _vp]
+    ),
+    "pe_linear_rope": (
+        _int, [_int, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _int,
+               _vp, _vp]
+    ),
     "pe_gemm": (
         _int,
         [_int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _int, _vp, _i64,
@@ -62,7 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "pe_attn_bwd_segments": (
         _int,
         [_int, _int, _vp, _int, _int, _int, _int, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64,
-         _vp, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _sz, _int, _vp, _vp],
+         _vp, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _sz, _vp, _i64, _int, _vp, _vp],
     ),
     "pe_lmhead_ce_workspace": (_sz, [_int, _i64, _i64, _i64, _int]),
     "pe_lmhead_ce": (

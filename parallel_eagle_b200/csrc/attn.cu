@@ -197,7 +197,8 @@ extern "C" int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, 
                                     const void* o, int64_t o_ss, const void* dout,
                                     int64_t do_ss, const float* lse, void* dq, int64_t dq_ss,
                                     void* dk, int64_t dk_ss, void* dv, int64_t dv_ss,
-                                    void* workspace, size_t workspace_bytes, int algo,
+                                    void* workspace, size_t workspace_bytes,
+                                    const void* rope_cs, int64_t cs_ld, int algo,
                                     int32_t* status, void* stream) {
   std::vector<attn_tc::PartGeom> g;
   int64_t rows = 0;
@@ -218,9 +219,10 @@ extern "C" int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, 
   if (tc && algo != PE_ALGO_SIMT) {
     float* acc = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + delta_bytes);
     return attn_bwd_tc_segments(nseg, g.data(), Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, dout,
-                                do_ss, lse, dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, acc, status,
-                                as_stream(stream));
+                                do_ss, lse, dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, acc, rope_cs,
+                                cs_ld, status, as_stream(stream));
   }
+  PE_CHECK_ARG(!rope_cs || cs_ld >= head_dim, "attention segments: rotary table rows too short");
   PE_CHECK_ARG(dtype == PE_F32 || dtype == PE_BF16, "attention segments: unknown dtype %d", dtype);
   const size_t es = elem_bytes(dtype);
   auto at = [es](const void* p, int64_t row, int64_t ss) {
@@ -240,6 +242,15 @@ extern "C" int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, 
         at_mut(dv, row0, dv_ss), 0, dv_ss, delta + Hq * row0, m, as_stream(stream));
     if (rc) return rc;
     row0 += S;
+  }
+  if (rope_cs) {
+    // CUDA-core path: the same inverse rotation as a separate pass over dq and dk
+    int rc = rope_apply_table(dtype, rows, Hq, head_dim, dq, dq_ss, rope_cs, cs_ld, 1,
+                              as_stream(stream));
+    if (!rc)
+      rc = rope_apply_table(dtype, rows, Hkv, head_dim, dk, dk_ss, rope_cs, cs_ld, 1,
+                            as_stream(stream));
+    if (rc) return rc;
   }
   return PE_OK;
 }

@@ -84,11 +84,18 @@ int attn_fwd_tc_segments(int nseg, const attn_tc::PartGeom* g, int Hq, int Hkv, 
                          void* o, int64_t o_ss, float* lse, int* status, cudaStream_t st);
 // acc: fp32 dK / dV accumulators and the work counter, attn_tc_seg_acc_bytes(rows)
 size_t attn_tc_seg_acc_bytes(int64_t rows, int Hkv);
+// rope_cs (may be NULL): per stacked row [cos hd/2 | sin hd/2] table (row stride
+// cs_ld); with it dq and dk leave rotated back by the transpose of the rotary
+// embedding (gradients with respect to the unrotated q / k)
 int attn_bwd_tc_segments(int nseg, const attn_tc::PartGeom* g, int Hq, int Hkv, const void* q,
                          int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
                          const void* o, int64_t o_ss, const void* dout, int64_t do_ss,
                          const float* lse, void* dq, int64_t dq_ss, void* dk, int64_t dk_ss,
-                         void* dv, int64_t dv_ss, float* delta, float* acc, int* status,
-                         cudaStream_t st);
+                         void* dv, int64_t dv_ss, float* delta, float* acc,
+                         const void* rope_cs, int64_t cs_ld, int* status, cudaStream_t st);
+// x[r, h * hd + (p, p + hd/2)] rotated (inverse: by the transpose) with the table
+// cs[r * cs_ld + (p, hd/2 + p)] (rope.cu; dtype of x and cs alike)
+int rope_apply_table(int dtype, int64_t rows, int heads, int hd, void* x, int64_t ldx,
+                     const void* cs, int64_t cs_ld, int inverse, cudaStream_t st);
 
 }  // namespace pe

@@ -252,8 +252,8 @@ inline int seg_map(CUtensorMap* map, const void* base, int64_t row, int64_t ss, 
 int attn_bwd_q2_launch(int nseg, const attn_tc::PartGeom* g, int Hq, int Hkv, const void* q,
                        int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
                        const void* dout, int64_t do_ss, const float* lse, const float* delta,
-                       void* dq, int64_t dq_ss, int* work_counter, int* status,
-                       cudaStream_t st);
+                       void* dq, int64_t dq_ss, const void* rope_cs, int64_t cs_ld,
+                       int* work_counter, int* status, cudaStream_t st);
 // persistent dK / dV kernel (attn_tc_bwd_kv.cu): accumulates fp32 dK, dV of every
 // query head into the KV-head accumulators (zeroed beforehand), items claimed from
 // *work_counter (zeroed beforehand); same segment convention

@@ -20,6 +20,7 @@
 //
 // TMEM columns: dK 0..127, dV 128..255, S^T (then dQ_part) 256..383, dP^T 384..511.
 #include "attn_tc.cuh"
+#include "rope.cuh"
 
 namespace pe {
 namespace {
@@ -940,6 +941,56 @@ __global__ void attn_cast_kernel(int S, int cols, const float* __restrict__ acc,
   }
 }
 
+// out (bf16) = mul * acc rounded to bf16, then every 128-wide head rotated back by the
+// transpose of the rotary embedding with the row's cos / sin (cs: [S] rows of
+// [cos 64 | sin 64], row stride cs_ld): one thread per (row, head, 8 pairs)
+__global__ void attn_cast_rope_kernel(int S, int heads, const float* __restrict__ acc, float mul,
+                                      __nv_bfloat16* __restrict__ out, int64_t ld,
+                                      const __nv_bfloat16* __restrict__ cs, int64_t cs_ld) {
+  const int64_t total = (int64_t)S * heads * 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t s = i / (heads * 8);
+    const int r = (int)(i - s * heads * 8);
+    const int h = r >> 3, p0 = (r & 7) * 8;
+    const float* a = acc + (s * heads + h) * HD + p0;
+    float va[8], vb[8], c[8], sn[8];
+    const float4 a0 = reinterpret_cast<const float4*>(a)[0], a1 = reinterpret_cast<const float4*>(a)[1];
+    const float4 b0 = reinterpret_cast<const float4*>(a + 64)[0];
+    const float4 b1 = reinterpret_cast<const float4*>(a + 64)[1];
+    va[0] = a0.x; va[1] = a0.y; va[2] = a0.z; va[3] = a0.w;
+    va[4] = a1.x; va[5] = a1.y; va[6] = a1.z; va[7] = a1.w;
+    vb[0] = b0.x; vb[1] = b0.y; vb[2] = b0.z; vb[3] = b0.w;
+    vb[4] = b1.x; vb[5] = b1.y; vb[6] = b1.z; vb[7] = b1.w;
+    load_bf16_f32<8>(cs + s * cs_ld + p0, c);
+    load_bf16_f32<8>(cs + s * cs_ld + 64 + p0, sn);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      va[j] = rb16(va[j] * mul);
+      vb[j] = rb16(vb[j] * mul);
+      rope_rotate_pair(va[j], vb[j], c[j], sn[j], true);
+    }
+    __nv_bfloat16* o = out + s * ld + h * HD + p0;
+    *reinterpret_cast<uint4*>(o) =
+        make_uint4(pack_bf16x2(va[0], va[1]), pack_bf16x2(va[2], va[3]), pack_bf16x2(va[4], va[5]),
+                   pack_bf16x2(va[6], va[7]));
+    *reinterpret_cast<uint4*>(o + 64) =
+        make_uint4(pack_bf16x2(vb[0], vb[1]), pack_bf16x2(vb[2], vb[3]), pack_bf16x2(vb[4], vb[5]),
+                   pack_bf16x2(vb[6], vb[7]));
+  }
+}
+
+int launch_cast_rope(int S, int heads, const float* acc, float mul, void* out, int64_t ld,
+                     const void* cs, int64_t cs_ld, cudaStream_t st) {
+  const int64_t total = (int64_t)S * heads * 8;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
+  attn_cast_rope_kernel<<<(unsigned)(blocks < 1 ? 1 : blocks), 256, 0, st>>>(
+      S, heads, acc, mul, (__nv_bfloat16*)out, ld, (const __nv_bfloat16*)cs, cs_ld);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
 int launch_cast(int S, int cols, const float* acc, float mul, void* out, int64_t ld,
                 cudaStream_t st) {
   const int64_t total = (int64_t)S * cols / 8;
@@ -983,7 +1034,8 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
   PartGeom g{Si, (int)m.a0, (int)m.a1, m.kd - 1};
   if (variant == 0)
     return attn_bwd_tc_segments(1, &g, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, dout, do_ss,
-                                lse, dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, dk_acc, status, st);
+                                lse, dq, dq_ss, dk, dk_ss, dv, dv_ss, delta, dk_acc, nullptr, 0,
+                                status, st);
   {
     SegRows sr{};
     sr.n = 1;
@@ -1040,11 +1092,14 @@ int attn_bwd_tc_segments(int nseg, const PartGeom* g, int Hq, int Hkv, const voi
                          int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
                          const void* o, int64_t o_ss, const void* dout, int64_t do_ss,
                          const float* lse, void* dq, int64_t dq_ss, void* dk, int64_t dk_ss,
-                         void* dv, int64_t dv_ss, float* delta, float* acc, int* status,
-                         cudaStream_t st) {
+                         void* dv, int64_t dv_ss, float* delta, float* acc,
+                         const void* rope_cs, int64_t cs_ld, int* status, cudaStream_t st) {
   PE_CHECK_ARG(o_ss % 8 == 0 && do_ss % 8 == 0 && dq_ss % 8 == 0 && dk_ss % 8 == 0 &&
                    dv_ss % 8 == 0 && al16(o) && al16(dout) && al16(dq) && al16(dk) && al16(dv),
                "attention backward (tcgen05): operands must be 16-byte aligned");
+  PE_CHECK_ARG(!rope_cs || (cs_ld % 8 == 0 && cs_ld >= HD && al16(rope_cs)),
+               "attention backward (tcgen05): the rotary table must be 16-byte aligned bf16 rows "
+               "of at least head_dim entries");
   std::vector<int64_t> rows(nseg + 1, 0);
   for (int s = 0; s < nseg; ++s) rows[s + 1] = rows[s] + g[s].S;
   const float scale = 1.0f / sqrtf((float)HD);
@@ -1073,14 +1128,17 @@ int attn_bwd_tc_segments(int nseg, const PartGeom* g, int Hq, int Hkv, const voi
           counter);
       PE_LAUNCHED();
     }
+    const void* cs_g = rope_cs ? static_cast<const uint8_t*>(rope_cs) + rb * cs_ld * 2 : nullptr;
     int rc = attn_bwd_q2_launch(e - b, g + b, Hq, Hkv, at(q, q_ss), q_ss, at(k, k_ss), k_ss,
                                 at(v, v_ss), v_ss, at(dout, do_ss), do_ss, lse_g, delta_g,
-                                at_mut(dq, dq_ss), dq_ss, counter + 1, status, st);
+                                at_mut(dq, dq_ss), dq_ss, cs_g, cs_ld, counter + 1, status, st);
     if (!rc)
       rc = attn_bwd_kv2_launch(e - b, g + b, Hq, Hkv, at(q, q_ss), q_ss, at(k, k_ss), k_ss,
                                at(v, v_ss), v_ss, at(dout, do_ss), do_ss, lse_g, delta_g, dk_acc,
                                dv_acc, counter, status, st);
-    if (!rc) rc = launch_cast((int)R, Hkv * HD, dk_acc, scale, at_mut(dk, dk_ss), dk_ss, st);
+    if (!rc)
+      rc = cs_g ? launch_cast_rope((int)R, Hkv, dk_acc, scale, at_mut(dk, dk_ss), dk_ss, cs_g, cs_ld, st)
+                : launch_cast((int)R, Hkv * HD, dk_acc, scale, at_mut(dk, dk_ss), dk_ss, st);
     if (!rc) rc = launch_cast((int)R, Hkv * HD, dv_acc, 1.f, at_mut(dv, dv_ss), dv_ss, st);
     if (rc) return rc;
   }

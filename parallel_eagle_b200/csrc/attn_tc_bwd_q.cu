@@ -32,6 +32,7 @@
 // TMEM: dQ 0..127, Q 128..191, dO 192..255 (bf16 pairs), S buffers 256 / 320,
 //       dP buffers 384 / 448.
 #include "attn_tc.cuh"
+#include "rope.cuh"
 
 namespace pe {
 namespace {
@@ -113,7 +114,8 @@ struct Unit {
 __global__ void __launch_bounds__(kThreads, 1)
 attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict__ lse,
                    const float* __restrict__ delta, __nv_bfloat16* __restrict__ dq, int64_t dq_ss,
-                   int Hq, int rep, float scale, int total, int* work_counter, int* status) {
+                   const __nv_bfloat16* __restrict__ rope_cs, int64_t cs_ld, int Hq, int rep,
+                   float scale, int total, int* work_counter, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -303,24 +305,42 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
     const float2 sc2 = make_float2(scale_log2, scale_log2);
     bool ok = true;
     int gs = 0;
-    // the previous unit's dQ row (this part's 32 head dims), written once that
-    // unit's last dQ MMA completed
+    // the previous unit's dQ row, written once that unit's last dQ MMA completed:
+    // this part's head dims [16 part, 16 part + 16) and their rotary partners 64 on,
+    // rounded to bf16 and, with a cos / sin table, rotated back by the transpose of
+    // the rotary embedding (the gradient with respect to the unrotated q)
     __nv_bfloat16* pending = nullptr;
+    const __nv_bfloat16* pending_cs = nullptr;
     bool have_pending = false;
     auto drain = [&](int ic_prev) -> bool {
       if (!mbar_wait(B.dq_full, ic_prev & 1, status, 370)) return false;
       tc_fence_after();
-      float v[32];
-      tmem_ld32(tDQ + lane_off + part * 32, v);
+      float va[16], vb[16];
+      tmem_ld16(tDQ + lane_off + part * 16, va);
+      tmem_ld16(tDQ + lane_off + 64 + part * 16, vb);
       tmem_wait_ld();
       if (pending) {
-        uint4* dst = reinterpret_cast<uint4*>(pending);
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          dst[u] = make_uint4(pack_bf16x2(v[8 * u] * scale, v[8 * u + 1] * scale),
-                              pack_bf16x2(v[8 * u + 2] * scale, v[8 * u + 3] * scale),
-                              pack_bf16x2(v[8 * u + 4] * scale, v[8 * u + 5] * scale),
-                              pack_bf16x2(v[8 * u + 6] * scale, v[8 * u + 7] * scale));
+        for (int i = 0; i < 16; ++i) {
+          va[i] = rb16(va[i] * scale);
+          vb[i] = rb16(vb[i] * scale);
+        }
+        if (pending_cs) {
+          float c[16], sn[16];
+          load_bf16_f32<16>(pending_cs + part * 16, c);
+          load_bf16_f32<16>(pending_cs + 64 + part * 16, sn);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) rope_rotate_pair(va[i], vb[i], c[i], sn[i], true);
+        }
+        uint4* da = reinterpret_cast<uint4*>(pending + part * 16);
+        uint4* db = reinterpret_cast<uint4*>(pending + 64 + part * 16);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          da[q] = make_uint4(pack_bf16x2(va[8 * q], va[8 * q + 1]), pack_bf16x2(va[8 * q + 2], va[8 * q + 3]),
+                             pack_bf16x2(va[8 * q + 4], va[8 * q + 5]), pack_bf16x2(va[8 * q + 6], va[8 * q + 7]));
+          db[q] = make_uint4(pack_bf16x2(vb[8 * q], vb[8 * q + 1]), pack_bf16x2(vb[8 * q + 2], vb[8 * q + 3]),
+                             pack_bf16x2(vb[8 * q + 4], vb[8 * q + 5]), pack_bf16x2(vb[8 * q + 6], vb[8 * q + 7]));
+        }
       }
       return true;
     };
@@ -365,7 +385,8 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
       }
       const int lo = qd > 0 ? u.g.a1 + (qi - u.g.a0) * u.g.km1 : 0;
       const float2 nl2 = make_float2(-l2, -l2), ndl2 = make_float2(-dl, -dl);
-      pending = valid ? dq + (u.r0 + s) * dq_ss + u.h * HD + part * 32 : nullptr;
+      pending = valid ? dq + (u.r0 + s) * dq_ss + u.h * HD : nullptr;
+      pending_cs = valid && rope_cs ? rope_cs + (u.r0 + s) * cs_ld : nullptr;
       have_pending = true;
       for (int j = 0; j < u.n; ++j) {
         const int gj = gs + j, b = gj & 1;
@@ -429,8 +450,8 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
 int attn_bwd_q2_launch(int nseg, const PartGeom* g, int Hq, int Hkv, const void* q,
                        int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
                        const void* dout, int64_t do_ss, const float* lse, const float* delta,
-                       void* dq, int64_t dq_ss, int* work_counter, int* status,
-                       cudaStream_t st) {
+                       void* dq, int64_t dq_ss, const void* rope_cs, int64_t cs_ld,
+                       int* work_counter, int* status, cudaStream_t st) {
   PE_CHECK_ARG(nseg >= 1 && nseg <= kMaxSeg, "attention backward: bad segment count");
   SegTable tab;
   memset(&tab, 0, sizeof(tab));
@@ -464,7 +485,8 @@ int attn_bwd_q2_launch(int nseg, const PartGeom* g, int Hq, int Hkv, const void*
                                    (int)SMEM_Q2));
   const int grid = (int)(units < sm_count() ? units : sm_count());
   attn_bwd_q2_kernel<<<grid, kThreads, SMEM_Q2, st>>>(tab, lse, delta, (__nv_bfloat16*)dq, dq_ss,
-                                                      Hq, Hq / Hkv, 1.0f / sqrtf((float)HD),
+                                                      (const __nv_bfloat16*)rope_cs, cs_ld, Hq,
+                                                      Hq / Hkv, 1.0f / sqrtf((float)HD),
                                                       (int)units, work_counter, status);
   PE_LAUNCHED();
   return PE_OK;

@@ -16,6 +16,7 @@
 // is one CTA per SM; tiles are walked in L2-sized groups of M-tiles so each
 // operand streams from HBM about once.
 #include "gemm.cuh"
+#include "rope.cuh"
 #include "sm100.cuh"
 
 namespace pe {
@@ -31,6 +32,8 @@ enum : int {
   EPI_STORE = 0,     // C = alpha * acc + beta * Cin
   EPI_STATS = 1,     // C = round(alpha * acc); stats[row, n_tile] = (max, sum exp(c - max))
   EPI_ROWSCALE = 2,  // C = alpha * acc + rowscale[row] * Cin
+  EPI_ROPE = 3,      // C = rotate(round(alpha * acc)) on 128-wide heads below rot_cols
+  EPI_SWIGLU = 4,    // gate|up tile pairs: C[:, j], C[:, I + j] = g, u; act[:, j] = silu(g) u
 };
 struct EpiArgs {
   float2* stats;
@@ -39,7 +42,33 @@ struct EpiArgs {
   // tile order: 0 automatic; G > 0 groups of G M-tiles (all N-tiles of a group
   // before the next); G < 0 groups of -G N-tiles (all M-tiles of a group first)
   int raster;
+  // EPI_ROPE: per-row [cos 64 | sin 64] bf16 table (row stride cs_ld) and the
+  // columns [0, rot_cols) whose 128-wide heads are rotated
+  const __nv_bfloat16* rope_cs = nullptr;
+  int64_t cs_ld = 0;
+  int64_t rot_cols = 0;
+  // EPI_SWIGLU: intermediate size I (B rows [0, I) gate, [I, 2I) up; a tile of BN
+  // columns holds gate rows [tn BN/2, tn BN/2 + BN/2) and the matching up rows) and
+  // the activation output
+  int64_t swiglu_i = 0;
+  __nv_bfloat16* act = nullptr;
+  int64_t ld_act = 0;
 };
+
+// silu(g) = g * sigmoid(g) with sigmoid(g) = 1 / (1 + exp(-g)), the expression the
+// element-wise SwiGLU kernels use, so the fused epilogue gives the same bits
+__device__ __forceinline__ float silu_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// B row of tile column t0 (the first column of a CTA's B sub-tile): the plain
+// layout, or for EPI_SWIGLU the gate (t0 < BN/2) or up row it pairs with
+template <int BN, int EPI>
+__device__ __forceinline__ int b_row_of(int tn, int t0, const EpiArgs& ea) {
+  if constexpr (EPI == EPI_SWIGLU) {
+    return t0 < BN / 2 ? tn * (BN / 2) + t0 : (int)ea.swiglu_i + tn * (BN / 2) + (t0 - BN / 2);
+  } else {
+    return tn * BN + t0;
+  }
+}
 
 constexpr uint32_t pow2_at_least(uint32_t x) {
   uint32_t p = 32;
@@ -202,6 +231,95 @@ __device__ __forceinline__ void store_row32(OutT* dst, const OutT* cin, const fl
   }
 }
 
+// EPI_ROPE drain: columns [c_begin, c_end) are whole 128-wide heads (col0, c_begin,
+// c_end and N multiples of 128).  Each head's pair halves (d, d + 64) are read
+// together 16 columns at a time, rounded to bf16 as the plain store would round
+// them, rotated with the row's table entries when the head lies below rot_cols
+// (the q and k heads of a fused q|k|v projection), and stored.
+__device__ __forceinline__ void epilogue_rope(uint32_t acc_tmem, int c_begin, int c_end, int64_t gm,
+                                              int64_t col0, int M, int N, __nv_bfloat16* C,
+                                              int64_t ldc, float alpha, const EpiArgs& ea) {
+  const bool row_ok = gm < M;
+  const __nv_bfloat16* cs = ea.rope_cs + (row_ok ? gm : 0) * ea.cs_ld;
+#pragma unroll 1
+  for (int h0 = c_begin; h0 < c_end; h0 += 128) {
+    const int64_t gh = col0 + h0;
+    const bool rot = gh < ea.rot_cols;
+#pragma unroll 1
+    for (int jp = 0; jp < 64; jp += 16) {
+      float va[16], vb[16];
+      tmem_ld16(acc_tmem + h0 + jp, va);
+      tmem_ld16(acc_tmem + h0 + 64 + jp, vb);
+      tmem_wait_ld();
+      if (row_ok && gh < N) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          va[i] = rb16(alpha * va[i]);
+          vb[i] = rb16(alpha * vb[i]);
+        }
+        if (rot) {
+          float c[16], sn[16];
+          load_bf16_f32<16>(cs + jp, c);
+          load_bf16_f32<16>(cs + 64 + jp, sn);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) rope_rotate_pair(va[i], vb[i], c[i], sn[i], false);
+        }
+        uint4* da = reinterpret_cast<uint4*>(C + gm * ldc + gh + jp);
+        uint4* db = reinterpret_cast<uint4*>(C + gm * ldc + gh + 64 + jp);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          da[q] = make_uint4(pack_bf16x2(va[8 * q], va[8 * q + 1]), pack_bf16x2(va[8 * q + 2], va[8 * q + 3]),
+                             pack_bf16x2(va[8 * q + 4], va[8 * q + 5]), pack_bf16x2(va[8 * q + 6], va[8 * q + 7]));
+          db[q] = make_uint4(pack_bf16x2(vb[8 * q], vb[8 * q + 1]), pack_bf16x2(vb[8 * q + 2], vb[8 * q + 3]),
+                             pack_bf16x2(vb[8 * q + 4], vb[8 * q + 5]), pack_bf16x2(vb[8 * q + 6], vb[8 * q + 7]));
+        }
+      }
+    }
+  }
+}
+
+// EPI_SWIGLU drain: gate columns [g_begin, g_end) of the tile (TMEM columns from
+// acc_tmem) and their up partners half_bn columns on, for intermediate columns
+// j0 + c.  g and u are rounded to bf16 as the plain store would round them and
+// stored into the gate|up output (the backward reads them); the activation is
+// round(round(silu(g)) * u), the element-wise SwiGLU kernels' rounding.
+__device__ __forceinline__ void epilogue_swiglu(uint32_t acc_tmem, int g_begin, int g_end,
+                                                int half_bn, int64_t gm, int64_t j0, int M,
+                                                __nv_bfloat16* C, int64_t ldc, float alpha,
+                                                const EpiArgs& ea) {
+  const bool row_ok = gm < M;
+  const int64_t I = ea.swiglu_i;
+#pragma unroll 1
+  for (int c = g_begin; c < g_end; c += 16) {
+    float g[16], u[16];
+    tmem_ld16(acc_tmem + c, g);
+    tmem_ld16(acc_tmem + half_bn + c, u);
+    tmem_wait_ld();
+    const int64_t j = j0 + c;
+    if (row_ok && j < I) {
+      float a[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        g[i] = rb16(alpha * g[i]);
+        u[i] = rb16(alpha * u[i]);
+        a[i] = rb16(g[i] * silu_sigmoid(g[i])) * u[i];
+      }
+      uint4* dg = reinterpret_cast<uint4*>(C + gm * ldc + j);
+      uint4* du = reinterpret_cast<uint4*>(C + gm * ldc + I + j);
+      uint4* da = reinterpret_cast<uint4*>(ea.act + gm * ea.ld_act + j);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        dg[q] = make_uint4(pack_bf16x2(g[8 * q], g[8 * q + 1]), pack_bf16x2(g[8 * q + 2], g[8 * q + 3]),
+                           pack_bf16x2(g[8 * q + 4], g[8 * q + 5]), pack_bf16x2(g[8 * q + 6], g[8 * q + 7]));
+        du[q] = make_uint4(pack_bf16x2(u[8 * q], u[8 * q + 1]), pack_bf16x2(u[8 * q + 2], u[8 * q + 3]),
+                           pack_bf16x2(u[8 * q + 4], u[8 * q + 5]), pack_bf16x2(u[8 * q + 6], u[8 * q + 7]));
+        da[q] = make_uint4(pack_bf16x2(a[8 * q], a[8 * q + 1]), pack_bf16x2(a[8 * q + 2], a[8 * q + 3]),
+                           pack_bf16x2(a[8 * q + 4], a[8 * q + 5]), pack_bf16x2(a[8 * q + 6], a[8 * q + 7]));
+      }
+    }
+  }
+}
+
 // Drains accumulator columns [c_begin, c_end) -- TMEM lanes of this warp, starting
 // at TMEM column `acc_tmem` -- into row `gm` of C (tile columns from col0),
 // applying the epilogue.  EPI_STATS writes one (max, sum-exp) pair per 128 columns,
@@ -211,6 +329,12 @@ __device__ __forceinline__ void epilogue_cols(uint32_t acc_tmem, int c_begin, in
                                               int64_t col0, int M, int N, OutT* C, int64_t ldc,
                                               const OutT* Cin, int64_t ldcin, float alpha,
                                               float beta, int vec_ok, const EpiArgs& ea) {
+  if constexpr (EPI == EPI_ROPE) {
+    static_assert(sizeof(OutT) == 2, "the rotary epilogue stores bf16");
+    epilogue_rope(acc_tmem, c_begin, c_end, gm, col0, M, N, reinterpret_cast<__nv_bfloat16*>(C),
+                  ldc, alpha, ea);
+    return;
+  }
   // EPI_ROWSCALE: the accumulated input is scaled per row (online-softmax correction)
   const float beta_row = (EPI == EPI_ROWSCALE && gm < M) ? ea.rowscale[gm] : beta;
   float m_run = -INFINITY, s_run = 0.f;  // EPI_STATS: running max / sum-exp of a 128-col chunk
@@ -522,7 +646,7 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 #pragma unroll
           for (int j = 0; j < NMMA; ++j) {
             // MMA j covers tile columns [j NJ, j NJ + NJ); this CTA holds half of them
-            const int bcol0 = tn * BN + j * NJ + (int)rank * NJH;
+            const int bcol0 = b_row_of<BN, EPI>(tn, j * NJ + (int)rank * NJH, ea);
             uint8_t* bj = b_dst + j * Cfg::BJ_BYTES;
             if constexpr (!B_MN) {
               tma_load_2d_pair(bj, &tmB, bar, kb * BK, bcol0);
@@ -601,10 +725,20 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const uint32_t acc_phase = NACC == 2 ? ((local >> 1) & 1) : (local & 1);
       if (!mbar_wait(&acc_full[acc], acc_phase, status, 114)) break;
       tc_fence_after();
-      epilogue_cols<OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
-                               half * (BN / 2), (half + 1) * (BN / 2),
-                               (int64_t)tm * 2 * BM + rank * BM + row_in_tile, (int64_t)tn * BN, M,
-                               N, C, ldc, Cin, ldcin, alpha, beta, vec_ok, ea);
+      if constexpr (EPI == EPI_SWIGLU) {
+        static_assert(sizeof(OutT) == 2 && BN % 64 == 0, "SwiGLU epilogue: bf16, BN % 64 == 0");
+        // each warp half drains a quarter of the tile's columns from the gate half and
+        // the same quarter from the up half
+        epilogue_swiglu(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, half * (BN / 4),
+                        (half + 1) * (BN / 4), BN / 2,
+                        (int64_t)tm * 2 * BM + rank * BM + row_in_tile, (int64_t)tn * (BN / 2), M,
+                        reinterpret_cast<__nv_bfloat16*>(C), ldc, alpha, ea);
+      } else {
+        epilogue_cols<OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
+                                 half * (BN / 2), (half + 1) * (BN / 2),
+                                 (int64_t)tm * 2 * BM + rank * BM + row_in_tile, (int64_t)tn * BN,
+                                 M, N, C, ldc, Cin, ldcin, alpha, beta, vec_ok, ea);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty_leader + 8u * (uint32_t)acc);
@@ -924,6 +1058,88 @@ int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t
                                                        ldc, 1.f, 0.f, 1, status, stream, ea);
 }
 
+// y = x w^T (bf16, both K-major) with the rotary embedding applied to the 128-wide
+// heads of columns [0, rot_cols) in the epilogue.  Tiles are 256 or 512 columns
+// wide (CTA pairs) or 256 (single CTAs), so every epilogue warp's column range is
+// made of whole heads.
+int gemm_tc_rope(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda, const void* B,
+                 int64_t ldb, void* C, int64_t ldc, const void* cs, int64_t cs_ld,
+                 int64_t rot_cols, int* status, cudaStream_t stream) {
+  PE_CHECK_ARG(M > 0 && N > 0 && K > 0, "linear + rope: empty problem");
+  PE_CHECK_ARG(N % 128 == 0 && rot_cols % 128 == 0 && rot_cols >= 0 && rot_cols <= N,
+               "linear + rope: N and rot_cols must be multiples of head_dim 128 (rot_cols <= N)");
+  PE_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31),
+               "linear + rope: dimensions too large");
+  PE_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 && cs_ld % 8 == 0 && cs_ld >= 128 &&
+                   al16(A) && al16(B) && al16(C) && al16(cs),
+               "linear + rope: operands and the table must be 16-byte aligned bf16");
+  const bool pair = use_pair(M, 0);
+  const int pbn = pair ? (choose_bn_pair(M, N, K, false, 2, sm_count() / 2) > 256 ? 512 : 256) : 256;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
+  if (!rc)
+    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, 64,
+                      pair ? (uint32_t)pair_b_box(pbn) : 256u);
+  if (rc) return rc;
+  EpiArgs ea{nullptr, 0, nullptr, 0};
+  ea.rope_cs = static_cast<const __nv_bfloat16*>(cs);
+  ea.cs_ld = cs_ld;
+  ea.rot_cols = rot_cols;
+  if (pair && pbn == 512)
+    return launch_pair<512, false, false, __nv_bfloat16, EPI_ROPE>(
+        ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
+  if (pair)
+    return launch_pair<256, false, false, __nv_bfloat16, EPI_ROPE>(
+        ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
+  return launch<256, false, false, __nv_bfloat16, EPI_ROPE>(ta, tb, (int)M, (int)N, (int)K, C, ldc,
+                                                            nullptr, 0, 1.f, 0.f, 1, status,
+                                                            stream, ea);
+}
+
+// gu = x w_gu^T and act = silu(gate) * up.  On the tensor-core path with CTA-pair
+// tiles (M >= 512, bf16, I a multiple of BN/2 for the chosen 256- or 512-wide tile,
+// 16-byte aligned rows) the activation is the GEMM epilogue's; otherwise the plain
+// GEMM runs, then the element-wise SwiGLU kernel (same bits either way).  algo bits
+// 8-17 may force the pair tile width (256 or 512).
+int gemm_tc_swiglu(int dtype, int64_t M, int64_t I, int64_t K, const void* A, int64_t lda,
+                   const void* B, int64_t ldb, void* C, int64_t ldc, void* act, int64_t ld_act,
+                   int algo, int* status, cudaStream_t stream) {
+  const int force_bn = (algo >> 8) & 0x3ff;
+  PE_CHECK_ARG(force_bn == 0 || force_bn == 256 || force_bn == 512,
+               "linear + swiglu: forced tile width %d not 256 or 512", force_bn);
+  const int64_t N = 2 * I;
+  int pbn = 0;
+  bool fused = dtype == PE_BF16 && use_pair(M, 0) && M < (1ll << 31) && N < (1ll << 31) &&
+               K < (1ll << 31) && lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 &&
+               ld_act % 8 == 0 && al16(A) && al16(B) && al16(C) && al16(act);
+  if (fused) {
+    pbn = force_bn ? force_bn
+                   : (choose_bn_pair(M, N, K, false, 2, sm_count() / 2) > 256 ? 512 : 256);
+    fused = I % (pbn / 2) == 0;
+  }
+  if (!fused) {
+    int rc = gemm(dtype, M, N, K, A, lda, 1, B, ldb, 1, C, ldc, dtype, nullptr, 0, 1.f, 0.f,
+                  algo & 0xff, status, stream);
+    if (rc) return rc;
+    return ::pe_swiglu_fwd(dtype, M, I, C, ldc, act, ld_act, stream);
+  }
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
+  if (!rc)
+    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, 64,
+                      (uint32_t)pair_b_box(pbn));
+  if (rc) return rc;
+  EpiArgs ea{nullptr, 0, nullptr, 0};
+  ea.swiglu_i = I;
+  ea.act = static_cast<__nv_bfloat16*>(act);
+  ea.ld_act = ld_act;
+  if (pbn == 512)
+    return launch_pair<512, false, false, __nv_bfloat16, EPI_SWIGLU>(
+        ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
+  return launch_pair<256, false, false, __nv_bfloat16, EPI_SWIGLU>(
+      ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
+}
+
 int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
          const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
          const void* Cin, int64_t ldcin, float alpha, float beta, int algo, int* status,
@@ -957,6 +1173,29 @@ int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm
 }
 
 }  // namespace pe
+
+extern "C" int pe_linear_rope(int dtype, int64_t M, int64_t N, int64_t K, const void* x,
+                              int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                              const void* rope_cs, int64_t cs_ld, int64_t rot_cols, int head_dim,
+                              int32_t* status, void* stream) {
+  PE_CHECK_ARG(dtype == PE_BF16 && head_dim == 128,
+               "linear + rope: the fused rotation runs on the bf16 tensor-core path with "
+               "head_dim 128 (got dtype %d, head_dim %d); use pe_gemm + pe_rope",
+               dtype, head_dim);
+  if (M == 0) return PE_OK;
+  return pe::gemm_tc_rope(M, N, K, x, ldx, w, ldw, y, ldy, rope_cs, cs_ld, rot_cols, status,
+                          pe::as_stream(stream));
+}
+
+extern "C" int pe_linear_swiglu(int dtype, int64_t M, int64_t I, int64_t K, const void* x,
+                                int64_t ldx, const void* w_gu, int64_t ldw, void* gu, int64_t ldgu,
+                                void* act, int64_t lda, int algo, int32_t* status, void* stream) {
+  PE_CHECK_ARG(M >= 0 && I > 0 && K > 0, "linear + swiglu: bad shape");
+  PE_CHECK_ARG(ldgu >= 2 * I && lda >= I, "linear + swiglu: output row stride too small");
+  if (M == 0) return PE_OK;
+  return pe::gemm_tc_swiglu(dtype, M, I, K, x, ldx, w_gu, ldw, gu, ldgu, act, lda, algo, status,
+                            pe::as_stream(stream));
+}
 
 extern "C" int pe_gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm,
                        int64_t a_sk, const void* B, int64_t b_sn, int64_t b_sk, void* C,

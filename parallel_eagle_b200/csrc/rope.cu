@@ -169,10 +169,89 @@ __global__ void rope_vec8_kernel(int64_t rows, int heads, int hd, __nv_bfloat16*
   }
 }
 
+// cos / sin table for the fused rotations: row r holds cos(pos_r * f_p) for the hd/2
+// pairs p, then sin(pos_r * f_p), each rounded to the storage type -- the same
+// angle and rounding as every rotation kernel above, so a rotation that reads the
+// table is bit-identical to rope_vec8_kernel.
+template <typename T>
+__global__ void rope_table_kernel(int64_t rows, int hd, const int64_t* __restrict__ pos,
+                                  float theta, T* __restrict__ cs, int64_t ld) {
+  const int half = hd >> 1;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * half) return;
+  const int64_t row = idx / half;
+  const int p = (int)(idx - row * half);
+  const float inv_freq = 1.0f / powf(theta, (float)(2 * p) / (float)hd);
+  float sv, cv;
+  sincosf((float)pos[row] * inv_freq, &sv, &cv);
+  cs[row * ld + p] = from_f<T>(cv);
+  cs[row * ld + half + p] = from_f<T>(sv);
+}
+
+// Rotation from a pe_rope_table table (same arithmetic as the kernels above), one
+// thread per (row, pair) over every head of the row: the generic form of the fused
+// rotations, for operands the fused kernels do not take.
+template <typename T>
+__global__ void rope_apply_table_kernel(int64_t rows, int heads, int hd, T* x, int64_t ldx,
+                                        const T* __restrict__ cs, int64_t cs_ld, int inverse) {
+  const int half = hd >> 1;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * half) return;
+  const int64_t row = idx / half;
+  const int p = (int)(idx - row * half);
+  const float c = to_f(cs[row * cs_ld + p]);
+  const float s = to_f(cs[row * cs_ld + half + p]);
+  T* base = x + row * ldx + p;
+  for (int h = 0; h < heads; ++h) {
+    T* hp = base + (int64_t)h * hd;
+    const float a = to_f(hp[0]);
+    const float b = to_f(hp[half]);
+    float ya, yb;
+    if (!inverse) {
+      ya = round_to<T>(round_to<T>(a * c) + round_to<T>(-b * s));
+      yb = round_to<T>(round_to<T>(b * c) + round_to<T>(a * s));
+    } else {
+      ya = round_to<T>(round_to<T>(a * c) + round_to<T>(b * s));
+      yb = round_to<T>(round_to<T>(b * c) - round_to<T>(a * s));
+    }
+    hp[0] = from_f<T>(ya);
+    hp[half] = from_f<T>(yb);
+  }
+}
+
 }  // namespace
+
+int rope_apply_table(int dtype, int64_t rows, int heads, int hd, void* x, int64_t ldx,
+                     const void* cs, int64_t cs_ld, int inverse, cudaStream_t st) {
+  PE_CHECK_ARG(rows >= 0 && heads > 0 && hd > 0 && hd % 2 == 0 && cs_ld >= hd,
+               "rope (table): bad shape");
+  if (rows == 0) return PE_OK;
+  const int64_t total = rows * (hd / 2);
+  return PE_DISPATCH(dtype, T, [&] {
+    rope_apply_table_kernel<T><<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(
+        rows, heads, hd, (T*)x, ldx, (const T*)cs, cs_ld, inverse);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
 }  // namespace pe
 
 using namespace pe;
+
+extern "C" int pe_rope_table(int dtype, int64_t rows, int head_dim, const int64_t* pos,
+                             float theta, void* cs, int64_t ld, void* stream) {
+  PE_CHECK_ARG(rows >= 0 && head_dim > 0 && head_dim % 2 == 0, "rope table: bad shape");
+  PE_CHECK_ARG(ld >= head_dim, "rope table: ld < head_dim");
+  if (rows == 0) return PE_OK;
+  const int64_t total = rows * (head_dim / 2);
+  return PE_DISPATCH(dtype, T, [&] {
+    rope_table_kernel<T><<<(unsigned)ceil_div(total, 256), 256, 0, as_stream(stream)>>>(
+        rows, head_dim, pos, theta, (T*)cs, ld);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
 
 extern "C" int pe_rope(int dtype, int64_t rows, int heads, int head_dim, void* x, int64_t ldx,
                        const int64_t* pos, float theta, int inverse, void* stream) {

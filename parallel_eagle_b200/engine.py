@@ -7,9 +7,10 @@ autograd graph:
 
 forward  feat RMSNorm -> feat_proj -> [emb | feat] -> in_proj (real slots);
          in_proj([mask_emb; h_shared]) broadcast to the prediction slots;
-         per layer: RMSNorm -> fused q/k/v GEMM -> RoPE -> masked flash
-         attention (mask re-derived from (a0, a1, K)) -> o_proj + residual ->
-         RMSNorm -> fused gate/up GEMM -> SwiGLU -> down_proj + residual;
+         per layer: RMSNorm -> fused q/k/v GEMM with RoPE in its epilogue ->
+         masked flash attention (mask re-derived from (a0, a1, K)) -> o_proj + residual ->
+         RMSNorm -> fused gate/up GEMM with silu * mul in its epilogue ->
+         down_proj + residual;
          frozen final RMSNorm; loss rows gathered; fused LM head + CE.
 backward the exact reverse, with weight gradients accumulated in place into a
          flat gradient buffer whose slices are the parameters' ``.grad``.
@@ -138,6 +139,7 @@ class _PassPlan:
     real_row: torch.Tensor  # int64 [Rt] its row in the stack
     nreal: int  # Rt
     has_pred: bool  # some segment has MTP slots
+    rope_cs: torch.Tensor | None = None  # [q, head_dim] cos | sin table (fused rotations)
 
 
 def count_loss_slots(n: int, k: int, prompt_len: int = 0) -> int:
@@ -312,6 +314,13 @@ class StepEngine:
         eps = d.eps
         E, Wh, wfinal = d.frozen_heads()
         single = len(plan.segs) == 1
+        # bf16 with head_dim 128: RoPE rides in the q|k|v GEMM epilogue and its transpose
+        # in the attention backward's dQ store / dK cast, reading a per-plan cos / sin
+        # table (the slot positions are fixed per plan)
+        fuse_rope = dt == torch.bfloat16 and hd == 128
+        if fuse_rope and plan.rope_cs is None:
+            plan.rope_cs = ops.rope_table(plan.pos, hd, d.rope_theta, dt)
+        rope_cs = plan.rope_cs if fuse_rope else None
         # every segment's attention runs in one call over the stacked rows
         bounds = [(a0, a1) for a0, a1, _, _ in plan.segs]
 
@@ -356,14 +365,17 @@ class StepEngine:
             w_gu = fp.span(p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight", H)
             w_dn = W(p + "mlp.down_proj.weight", (H, I))
             xn, r1 = ops.rmsnorm_fwd(x, W(p + "input_norm.weight"), eps)
-            qkv = ops.linear(xn, w_qkv)
-            ops.rope_(qkv, nh + nkv, hd, plan.pos, d.rope_theta)
+            if fuse_rope:
+                qkv = ops.linear_rope(xn, w_qkv, rope_cs, qc + kc, hd)
+            else:
+                qkv = ops.linear(xn, w_qkv)
+                ops.rope_(qkv, nh + nkv, hd, plan.pos, d.rope_theta)
             o, lse = ops.attn_fwd_segments(qkv[:, :qc], qkv[:, qc : qc + kc], qkv[:, qc + kc :],
                                            nh, nkv, hd, bounds, k)
             x2 = ops.linear(o, w_o, residual=x)
             xn2, r2 = ops.rmsnorm_fwd(x2, W(p + "post_norm.weight"), eps)
-            gu = ops.linear(xn2, w_gu)
-            act = ops.swiglu_fwd(gu, I)
+            # gate|up GEMM with silu(gate) * up in its epilogue (gate|up kept for backward)
+            gu, act = ops.linear_swiglu(xn2, w_gu, I)
             x3 = ops.linear(act, w_dn, residual=x2)
             saved.append((x, xn, r1, qkv, o, lse, x2, xn2, r2, gu, act))
             x = x3
@@ -410,8 +422,10 @@ class StepEngine:
             dqkv = torch.empty(Q, cqkv, dtype=dt, device=dev)
             ops.attn_bwd_segments(qkv[:, :qc], qkv[:, qc : qc + kc], qkv[:, qc + kc :], o, do, lse,
                                   nh, nkv, hd, bounds, k, dq=dqkv[:, :qc],
-                                  dk=dqkv[:, qc : qc + kc], dv=dqkv[:, qc + kc :])
-            ops.rope_(dqkv, nh + nkv, hd, plan.pos, d.rope_theta, inverse=True)
+                                  dk=dqkv[:, qc : qc + kc], dv=dqkv[:, qc + kc :],
+                                  rope_cs=rope_cs)
+            if not fuse_rope:
+                ops.rope_(dqkv, nh + nkv, hd, plan.pos, d.rope_theta, inverse=True)
             dxn = ops.linear_dgrad(dqkv, w_qkv)
             ops.linear_wgrad(
                 dqkv, xn, accumulate=True,

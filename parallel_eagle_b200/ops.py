@@ -111,6 +111,59 @@ def rope_(x: torch.Tensor, heads: int, head_dim: int, pos: torch.Tensor, theta: 
     return x
 
 
+def rope_table(pos: torch.Tensor, head_dim: int, theta: float, dtype: torch.dtype) -> torch.Tensor:
+    """``[rows, head_dim]`` table of ``[cos | sin]`` per position (rounded to ``dtype``)
+    that the fused rotations read: :func:`linear_rope` and
+    :func:`attn_bwd_segments` (``rope_cs``)."""
+    L.require_cuda(pos)
+    rows = pos.shape[0]
+    cs = torch.empty(rows, head_dim, dtype=dtype, device=pos.device)
+    rc = _lib().pe_rope_table(L.dtype_code(dtype), rows, head_dim, pos.data_ptr(), float(theta),
+                              cs.data_ptr(), head_dim, L.stream_ptr(pos.device))
+    L.check(rc, "pe_rope_table")
+    return cs
+
+
+def linear_rope(x, w, rope_cs, rot_cols: int, head_dim: int, out=None):
+    """``out = x w^T`` with the rotary embedding applied in the GEMM epilogue to the
+    ``head_dim`` blocks of columns ``[0, rot_cols)`` (bf16, head_dim 128): the fused
+    q|k|v projection + RoPE, bit-identical to :func:`linear` then :func:`rope_`."""
+    L.require_cuda(x, w, rope_cs)
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    rc = _lib().pe_linear_rope(
+        L.dtype_code(x.dtype), M, N, K, x.data_ptr(), _row_stride(x), w.data_ptr(), _row_stride(w),
+        out.data_ptr(), _row_stride(out), rope_cs.data_ptr(), rope_cs.stride(0), int(rot_cols),
+        int(head_dim), status_word(x.device).data_ptr(), L.stream_ptr(x.device),
+    )
+    L.check(rc, "pe_linear_rope")
+    return out
+
+
+def linear_swiglu(x, w_gu, intermediate: int, gu=None, act=None, algo=L.ALGO_AUTO):
+    """``gu = x w_gu^T`` (``[M, 2I]``: gate | up) and ``act = silu(gate) * up``
+    (``[M, I]``) in one call: the activation comes from the GEMM epilogue on the
+    tensor-core pair path (same bits as :func:`linear` then :func:`swiglu_fwd`)."""
+    L.require_cuda(x, w_gu)
+    M, K = x.shape
+    I = int(intermediate)
+    if w_gu.shape[0] != 2 * I:
+        raise L.PeError(f"linear_swiglu: w_gu has {w_gu.shape[0]} rows, expected 2 * {I}")
+    if gu is None:
+        gu = torch.empty(M, 2 * I, dtype=x.dtype, device=x.device)
+    if act is None:
+        act = torch.empty(M, I, dtype=x.dtype, device=x.device)
+    rc = _lib().pe_linear_swiglu(
+        L.dtype_code(x.dtype), M, I, K, x.data_ptr(), _row_stride(x), w_gu.data_ptr(),
+        _row_stride(w_gu), gu.data_ptr(), _row_stride(gu), act.data_ptr(), _row_stride(act), algo,
+        status_word(x.device).data_ptr(), L.stream_ptr(x.device),
+    )
+    L.check(rc, "pe_linear_swiglu")
+    return gu, act
+
+
 # ------------------------------------------------------------------ gemm ----
 
 
@@ -287,10 +340,17 @@ def attn_fwd_segments(q, k, v, n_heads, n_kv_heads, head_dim, bounds, kdepth, o=
 
 
 def attn_bwd_segments(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, bounds, kdepth,
-                      dq=None, dk=None, dv=None, algo=L.ALGO_AUTO):
+                      dq=None, dk=None, dv=None, algo=L.ALGO_AUTO, rope_cs=None):
     """Backward of :func:`attn_fwd_segments` (same row and lse conventions); dq/dk/dv
-    are overwritten."""
+    are overwritten.  With ``rope_cs`` (a :func:`rope_table` over the stacked rows) q
+    and k are the rotated projections and dq / dk come back rotated by the transpose
+    of the rotary embedding, fused into the dQ store and the dK cast."""
     L.require_cuda(q, k, v, o, do, lse)
+    if rope_cs is not None:
+        L.require_cuda(rope_cs)
+        if rope_cs.dtype != q.dtype or rope_cs.shape[0] != q.shape[0] or rope_cs.stride(1) != 1:
+            raise L.PeError("attention segments: rope_cs must be a [rows, >= head_dim] table "
+                            "in the operands' dtype with one row per stacked slot")
     b = _seg_bounds(bounds)
     R = q.shape[0]
     if R != sum(segment_rows(b.tolist(), kdepth)):
@@ -310,7 +370,8 @@ def attn_bwd_segments(q, k, v, o, do, lse, n_heads, n_kv_heads, head_dim, bounds
         dt, b.shape[0], b.ctypes.data, kdepth, n_heads, n_kv_heads, head_dim, q.data_ptr(),
         _row_ss(q), k.data_ptr(), _row_ss(k), v.data_ptr(), _row_ss(v), o.data_ptr(), _row_ss(o),
         do.data_ptr(), _row_ss(do), lse.data_ptr(), dq.data_ptr(), _row_ss(dq), dk.data_ptr(),
-        _row_ss(dk), dv.data_ptr(), _row_ss(dv), ws.data_ptr(), ws.numel(), algo,
+        _row_ss(dk), dv.data_ptr(), _row_ss(dv), ws.data_ptr(), ws.numel(), L.ptr(rope_cs),
+        rope_cs.stride(0) if rope_cs is not None else 0, algo,
         status_word(q.device).data_ptr(), L.stream_ptr(q.device),
     )
     L.check(rc, "pe_attn_bwd_segments")

@@ -178,7 +178,7 @@ def test_argmax_and_topk_rank_nan_like_torch():
     z[0, 5] = float("nan")
     z[1, :] = float("nan")
     for dt in (torch.float32, torch.bfloat16):
-        idx, _ = ops.topk_logprobs(z.to(dt).to(DEV), 3, raw=True)
+        _, idx = ops.topk_logprobs(z.to(dt).to(DEV), 3, raw=True)
         idx = idx.cpu()
         zr = z.to(dt).float()
         assert idx[0].tolist() == [5, 9, int(zr[0].nan_to_num(-1e9).argmax())]

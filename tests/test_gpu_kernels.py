@@ -202,6 +202,81 @@ def test_rope_matches_reference_rotation(dtype, max_pos):
     assert rel(y.float().cpu(), x.float().cpu()) < (1e-5 if dtype == torch.float32 else 2e-2)
 
 
+@pytest.mark.parametrize("M,I,K,bn", [(300, 512, 256, 0), (600, 512, 320, 256), (600, 1024, 256, 512),
+                                      (4096, 2048, 512, 0), (1500, 768, 192, 256)])
+def test_linear_swiglu_equals_linear_then_swiglu(M, I, K, bn):
+    """gate|up GEMM with silu(gate) * up in the epilogue (256- and 512-wide CTA-pair
+    tiles; below 512 rows the plain GEMM + element-wise kernel) equals the plain GEMM
+    followed by the SwiGLU kernel bit for bit, for both outputs."""
+    x = _rand(M, K, seed=70)
+    w = _rand(2 * I, K, seed=71, scale=0.05)
+    gu_ref = ops.linear(x, w, algo=L.ALGO_TCGEN05)
+    act_ref = ops.swiglu_fwd(gu_ref, I)
+    gu, act = ops.linear_swiglu(x, w, I, algo=L.ALGO_AUTO | (bn << 8))
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert torch.equal(gu, gu_ref)
+    assert torch.equal(act, act_ref)
+
+
+@pytest.mark.parametrize("M,nh,nkv,K", [(200, 4, 2, 256), (700, 4, 2, 320), (1024, 28, 4, 512),
+                                        (1300, 8, 2, 384)])
+def test_linear_rope_equals_linear_then_rope(M, nh, nkv, K):
+    """The q|k|v projection with RoPE in the GEMM epilogue (single-CTA and CTA-pair
+    tiles, 256 and 512 wide) equals the plain GEMM followed by the rotation kernel,
+    bit for bit; the v heads are left unrotated."""
+    hd = 128
+    N = (nh + 2 * nkv) * hd
+    x = _rand(M, K, seed=60)
+    w = _rand(N, K, seed=61, scale=0.05)
+    pos = torch.randint(0, 9000, (M,), generator=torch.Generator().manual_seed(62)).to(DEV)
+    ref = ops.linear(x, w, algo=L.ALGO_TCGEN05)
+    ops.rope_(ref, nh + nkv, hd, pos, 10000.0)
+    cs = ops.rope_table(pos, hd, 10000.0, torch.bfloat16)
+    got = ops.linear_rope(x, w, cs, (nh + nkv) * hd, hd)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("case", [(300, 4, 5, 4, 2), (2048, 4, 5, 28, 4)])
+def test_attention_bwd_fused_rope_equals_separate_rotation(case, dtype):
+    """``attn_bwd_segments(rope_cs=...)`` (the transpose of RoPE fused into the dQ
+    store and the dK cast, or a table pass on the CUDA-core path) equals the plain
+    backward followed by the inverse rotation kernel: dQ bit for bit, dK and dV up
+    to the order of the fp32 atomic GQA-group additions (not reproducible bit for bit
+    from run to run)."""
+    from parallel_eagle_b200.engine import segment_bounds
+
+    n, nseg, k, nh, nkv = case
+    if dtype == torch.float32 and n > 1000:
+        pytest.skip("CUDA-core fp32 path: small cases only")
+    hd = 128
+    bounds = segment_bounds(n, nseg)
+    R = sum(ops.segment_rows(bounds, k))
+    cq, ckv = nh * hd, nkv * hd
+    qkv = _rand(R, cq + 2 * ckv, dtype=dtype, seed=63)
+    do = _rand(R, cq, dtype=dtype, seed=64)
+    q, kt, vt = qkv[:, :cq], qkv[:, cq:cq + ckv], qkv[:, cq + ckv:]
+    pos = torch.randint(0, 4096, (R,), generator=torch.Generator().manual_seed(65)).to(DEV)
+    o, lse = ops.attn_fwd_segments(q, kt, vt, nh, nkv, hd, bounds, k)
+    ref = torch.empty_like(qkv)
+    ops.attn_bwd_segments(q, kt, vt, o, do, lse, nh, nkv, hd, bounds, k, dq=ref[:, :cq],
+                          dk=ref[:, cq:cq + ckv], dv=ref[:, cq + ckv:])
+    ops.rope_(ref, nh + nkv, hd, pos, 10000.0, inverse=True)
+    cs = ops.rope_table(pos, hd, 10000.0, dtype)
+    got = torch.full_like(qkv, float("nan"))
+    ops.attn_bwd_segments(q, kt, vt, o, do, lse, nh, nkv, hd, bounds, k, dq=got[:, :cq],
+                          dk=got[:, cq:cq + ckv], dv=got[:, cq + ckv:], rope_cs=cs)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert torch.equal(got[:, :cq], ref[:, :cq])
+    assert not torch.isnan(got).any()
+    for sl in (slice(cq, cq + ckv), slice(cq + ckv, None)):
+        assert rel(got[:, sl].float().cpu(), ref[:, sl].float().cpu()) < 5e-3
+
+
 # ------------------------------------------------------------- attention ----
 
 

@@ -109,8 +109,10 @@ CASES = {
     "fp32": (dict(hidden=64, heads=4, kv_heads=2, intermediate=128, vocab=256, K=4, seq_len=40),
              "float32", 1e-4, 1e-3, 5e-2),
     # bf16 with head_dim 128: the tcgen05 attention and GEMM kernels
+    # (no moved-distance check: updates of 3e-3 on bf16 weights near 1.0 are below half
+    # an ulp there, so how far such a weight moves is a matter of rounding ties)
     "bf16": (dict(hidden=256, heads=2, kv_heads=1, intermediate=512, vocab=1024, K=5, seq_len=96),
-             "bfloat16", 2e-2, 2e-2, 1e-1),
+             "bfloat16", 2e-2, 2e-2, None),
 }
 
 
@@ -134,7 +136,7 @@ def test_train_loop_on_gpu_matches_cpu_reference_update(name, tmp_path, monkeypa
         # the parameters after 8 updates, and the distance each moved from its init
         assert recipe.rel_fro(got, ref) < param_tol, k
         moved_ref = ref - init_ref[k]
-        if moved_ref.norm() > 0:
+        if moved_tol is not None and moved_ref.norm() > 0:
             assert recipe.rel_fro(got - init_ref[k], moved_ref) < moved_tol, k
 
 
