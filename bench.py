@@ -713,15 +713,33 @@ def run_kernel(args):
         flops = 2.0 * M * 2 * I * H
         out = {}
         runs = {"gemm_then_swiglu": lambda: ops.swiglu_fwd(ops.linear(x, w, out=gu), I, out=act),
-                "gemm_only": lambda: ops.linear(x, w, out=gu)}
+                "gemm_only": lambda: ops.linear(x, w, out=gu),
+                "gemm_only_bn256": lambda: ops.linear(x, w, out=gu, algo=(256 << 8) | (2 << 20)),
+                "gemm_only_evict_first": lambda: ops.linear(x, w, out=gu, algo=1 << 22),
+                "swiglu_only": lambda: ops.swiglu_fwd(gu, I, out=act)}
         for bn in (0, 256, 512):
             runs[f"fused_bn{bn or 'auto'}"] = (
                 lambda bn=bn: ops.linear_swiglu(x, w, I, gu=gu, act=act, algo=bn << 8))
         for name, fn in runs.items():
             ms = time_case(fn, args.steps, warmup=args.warmup)
             out[name] = {"ms": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
+        # the q|k|v projection of the same pass: GEMM + rotation kernel vs RoPE epilogue
+        nh, nkv, hd = c["n_heads"], c["n_kv_heads"], c["hidden"] // c["n_heads"]
+        wq = (torch.randn((nh + 2 * nkv) * hd, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        qkv = torch.empty(M, (nh + 2 * nkv) * hd, dtype=torch.bfloat16, device=dev)
+        pos = torch.randint(0, 4096, (M,), generator=g, device=dev)
+        cs = ops.rope_table(pos, hd, 10000.0, torch.bfloat16)
+        qflops = 2.0 * M * (nh + 2 * nkv) * hd * H
+        qruns = {"qkv_gemm_then_rope": lambda: ops.rope_(ops.linear(x, wq, out=qkv), nh + nkv, hd,
+                                                         pos, 10000.0),
+                 "qkv_gemm_only": lambda: ops.linear(x, wq, out=qkv),
+                 "qkv_gemm_only_evict_first": lambda: ops.linear(x, wq, out=qkv, algo=1 << 22),
+                 "qkv_fused_rope": lambda: ops.linear_rope(x, wq, cs, (nh + nkv) * hd, hd, out=qkv)}
+        for name, fn in qruns.items():
+            ms = time_case(fn, args.steps, warmup=args.warmup)
+            out[name] = {"ms": round(ms, 4), "tflops": round(qflops / (ms / 1e3) / 1e12, 1)}
         ops.check_status(dev)
-        print(json.dumps({"kernel": "gate|up + swiglu", "M": M, "N": 2 * I, "K": H,
+        print(json.dumps({"kernel": "gate|up + swiglu; q|k|v + rope", "M": M, "N": 2 * I, "K": H,
                           "results": out}), flush=True)
         return
     case = {"gemm": gemm_case, "attn": attention_case, "lmhead": lmhead_case}[args.kernel]

@@ -332,15 +332,17 @@ attn_bwd_q2_kernel(const __grid_constant__ SegTable tab, const float* __restrict
 #pragma unroll
           for (int i = 0; i < 16; ++i) rope_rotate_pair(va[i], vb[i], c[i], sn[i], true);
         }
+        // each half's 32 bytes as two back-to-back stores: whole sectors after L1 merging
         uint4* da = reinterpret_cast<uint4*>(pending + part * 16);
-        uint4* db = reinterpret_cast<uint4*>(pending + 64 + part * 16);
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < 2; ++q)
           da[q] = make_uint4(pack_bf16x2(va[8 * q], va[8 * q + 1]), pack_bf16x2(va[8 * q + 2], va[8 * q + 3]),
                              pack_bf16x2(va[8 * q + 4], va[8 * q + 5]), pack_bf16x2(va[8 * q + 6], va[8 * q + 7]));
+        uint4* db = reinterpret_cast<uint4*>(pending + 64 + part * 16);
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
           db[q] = make_uint4(pack_bf16x2(vb[8 * q], vb[8 * q + 1]), pack_bf16x2(vb[8 * q + 2], vb[8 * q + 3]),
                              pack_bf16x2(vb[8 * q + 4], vb[8 * q + 5]), pack_bf16x2(vb[8 * q + 6], vb[8 * q + 7]));
-        }
       }
       return true;
     };

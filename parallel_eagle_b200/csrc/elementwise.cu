@@ -28,7 +28,19 @@ __global__ void fill_rows_kernel(int64_t rows, int64_t H, const T* __restrict__ 
   }
 }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+// sigmoid(x) = 1 / (1 + e^-x).  bf16 storage: from the hardware exp2 and reciprocal
+// approximations (a few ulp in fp32, before the result is rounded to bf16) -- the
+// gate|up GEMM's fused SwiGLU epilogue evaluates the same expression, so the fused and
+// element-wise paths give the same bits.  fp32 storage: the accurate expf and division.
+template <typename T>
+__device__ __forceinline__ float sigmoid_t(float x) {
+  if constexpr (sizeof(T) == 2) {
+    return __fdividef(1.0f, 1.0f + __expf(-x));
+  } else {
+    return 1.0f / (1.0f + expf(-x));
+  }
+}
+__device__ __forceinline__ float sigmoidf_(float x) { return sigmoid_t<__nv_bfloat16>(x); }
 
 template <typename T>
 __global__ void swiglu_fwd_kernel(int64_t rows, int64_t I, const T* __restrict__ gu, int64_t ldgu,
@@ -39,7 +51,7 @@ __global__ void swiglu_fwd_kernel(int64_t rows, int64_t I, const T* __restrict__
     const int64_t r = i / I, c = i - r * I;
     const float g = to_f(gu[r * ldgu + c]);
     const float u = to_f(gu[r * ldgu + I + c]);
-    const float act = round_to<T>(g * sigmoidf_(g));
+    const float act = round_to<T>(g * sigmoid_t<T>(g));
     a[r * lda + c] = from_f<T>(act * u);
   }
 }
@@ -55,7 +67,7 @@ __global__ void swiglu_bwd_kernel(int64_t rows, int64_t I, const T* __restrict__
     const float d = to_f(da[r * ldda + c]);
     const float g = to_f(gu[r * ldgu + c]);
     const float u = to_f(gu[r * ldgu + I + c]);
-    const float s = sigmoidf_(g);
+    const float s = sigmoid_t<T>(g);
     const float act = round_to<T>(g * s);
     const float dact = round_to<T>(d * u);
     dgu[r * lddgu + I + c] = from_f<T>(d * act);

@@ -18,7 +18,8 @@ bool gemm_tc_eligible(int dtype, int64_t M, int64_t N, int64_t K, const void* A,
 int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
             const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
             const void* Cin, int64_t ldcin, float alpha, float beta, int* status,
-            cudaStream_t stream, int force_bn = 0, int mode = 0, int raster = 0);
+            cudaStream_t stream, int force_bn = 0, int mode = 0, int raster = 0,
+            int store_hint = 0);
 
 // Logits GEMM for the fused LM-head loss: C (bf16, [M, N]) = A[M, K] B[N, K]^T with
 // both operands K-major, and per (row, 128-column chunk) the pair (max, sum exp(c - max))

@@ -53,11 +53,15 @@ struct EpiArgs {
   int64_t swiglu_i = 0;
   __nv_bfloat16* act = nullptr;
   int64_t ld_act = 0;
+  // plain epilogues: store C with the L2 evict-first policy (C is not read again by
+  // this kernel; its lines then leave L2 before the operand panels)
+  int store_hint = 0;
 };
 
-// silu(g) = g * sigmoid(g) with sigmoid(g) = 1 / (1 + exp(-g)), the expression the
-// element-wise SwiGLU kernels use, so the fused epilogue gives the same bits
-__device__ __forceinline__ float silu_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+// silu(g) = g * sigmoid(g) with sigmoid(g) = 1 / (1 + e^-g) from the hardware exp2 and
+// reciprocal approximations -- the expression the element-wise SwiGLU kernels use, so
+// the fused epilogue gives the same bits -- cheap enough for the epilogue warps
+__device__ __forceinline__ float silu_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // B row of tile column t0 (the first column of a CTA's B sub-tile): the plain
 // layout, or for EPI_SWIGLU the gate (t0 < BN/2) or up row it pairs with
@@ -175,7 +179,8 @@ __device__ __forceinline__ int raster_group(int raster, int tiles_m, int tiles_n
 
 template <typename OutT>
 __device__ __forceinline__ void store_row32(OutT* dst, const OutT* cin, const float* v, float alpha,
-                                            float beta, int valid, bool vec_ok) {
+                                            float beta, int valid, bool vec_ok,
+                                            const uint64_t* pol = nullptr) {
   float o[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) o[i] = alpha * v[i];
@@ -201,7 +206,10 @@ __device__ __forceinline__ void store_row32(OutT* dst, const OutT* cin, const fl
         u.y = pack_bf16x2(o[q * 8 + 2], o[q * 8 + 3]);
         u.z = pack_bf16x2(o[q * 8 + 4], o[q * 8 + 5]);
         u.w = pack_bf16x2(o[q * 8 + 6], o[q * 8 + 7]);
-        reinterpret_cast<uint4*>(dst)[q] = u;
+        if (pol)
+          st_v4_hint(reinterpret_cast<uint4*>(dst) + q, u, *pol);
+        else
+          reinterpret_cast<uint4*>(dst)[q] = u;
       }
     } else {
       if (cin) {
@@ -215,9 +223,16 @@ __device__ __forceinline__ void store_row32(OutT* dst, const OutT* cin, const fl
         }
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        reinterpret_cast<float4*>(dst)[q] =
-            make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+      for (int q = 0; q < 8; ++q) {
+        const float4 f = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        if (pol)
+          st_v4_hint(reinterpret_cast<float4*>(dst) + q,
+                     make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z),
+                                __float_as_uint(f.w)),
+                     *pol);
+        else
+          reinterpret_cast<float4*>(dst)[q] = f;
+      }
     }
   } else {
 #pragma unroll
@@ -264,15 +279,17 @@ __device__ __forceinline__ void epilogue_rope(uint32_t acc_tmem, int c_begin, in
 #pragma unroll
           for (int i = 0; i < 16; ++i) rope_rotate_pair(va[i], vb[i], c[i], sn[i], false);
         }
+        // each half's 32 bytes as two back-to-back stores: whole sectors after L1 merging
         uint4* da = reinterpret_cast<uint4*>(C + gm * ldc + gh + jp);
-        uint4* db = reinterpret_cast<uint4*>(C + gm * ldc + gh + 64 + jp);
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
+        for (int q = 0; q < 2; ++q)
           da[q] = make_uint4(pack_bf16x2(va[8 * q], va[8 * q + 1]), pack_bf16x2(va[8 * q + 2], va[8 * q + 3]),
                              pack_bf16x2(va[8 * q + 4], va[8 * q + 5]), pack_bf16x2(va[8 * q + 6], va[8 * q + 7]));
+        uint4* db = reinterpret_cast<uint4*>(C + gm * ldc + gh + 64 + jp);
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
           db[q] = make_uint4(pack_bf16x2(vb[8 * q], vb[8 * q + 1]), pack_bf16x2(vb[8 * q + 2], vb[8 * q + 3]),
                              pack_bf16x2(vb[8 * q + 4], vb[8 * q + 5]), pack_bf16x2(vb[8 * q + 6], vb[8 * q + 7]));
-        }
       }
     }
   }
@@ -289,33 +306,43 @@ __device__ __forceinline__ void epilogue_swiglu(uint32_t acc_tmem, int g_begin, 
                                                 const EpiArgs& ea) {
   const bool row_ok = gm < M;
   const int64_t I = ea.swiglu_i;
+  const uint64_t pol = l2_evict_first_policy();
 #pragma unroll 1
-  for (int c = g_begin; c < g_end; c += 16) {
-    float g[16], u[16];
-    tmem_ld16(acc_tmem + c, g);
-    tmem_ld16(acc_tmem + half_bn + c, u);
+  for (int c = g_begin; c < g_end; c += 32) {
+    float g[32], u[32];
+    tmem_ld32(acc_tmem + c, g);
+    tmem_ld32(acc_tmem + half_bn + c, u);
     tmem_wait_ld();
     const int64_t j = j0 + c;
     if (row_ok && j < I) {
-      float a[16];
+      // each output's 64 bytes of this row go out as four back-to-back 16-byte stores,
+      // so L1 merges them into whole 32-byte sectors (interleaving the three outputs'
+      // stores left half-sector writes that L2 must read-modify-write)
+      uint32_t pk[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        g[i] = rb16(alpha * g[i]);
-        u[i] = rb16(alpha * u[i]);
-        a[i] = rb16(g[i] * silu_sigmoid(g[i])) * u[i];
+      for (int e = 0; e < 32; ++e) {
+        g[e] = rb16(alpha * g[e]);
+        u[e] = rb16(alpha * u[e]);
       }
       uint4* dg = reinterpret_cast<uint4*>(C + gm * ldc + j);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(g[2 * e], g[2 * e + 1]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) st_v4_hint(dg + q, make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]), pol);
       uint4* du = reinterpret_cast<uint4*>(C + gm * ldc + I + j);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(u[2 * e], u[2 * e + 1]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) st_v4_hint(du + q, make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]), pol);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float a0 = rb16(g[2 * e] * silu_sigmoid(g[2 * e])) * u[2 * e];
+        const float a1 = rb16(g[2 * e + 1] * silu_sigmoid(g[2 * e + 1])) * u[2 * e + 1];
+        pk[e] = pack_bf16x2(a0, a1);
+      }
       uint4* da = reinterpret_cast<uint4*>(ea.act + gm * ea.ld_act + j);
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        dg[q] = make_uint4(pack_bf16x2(g[8 * q], g[8 * q + 1]), pack_bf16x2(g[8 * q + 2], g[8 * q + 3]),
-                           pack_bf16x2(g[8 * q + 4], g[8 * q + 5]), pack_bf16x2(g[8 * q + 6], g[8 * q + 7]));
-        du[q] = make_uint4(pack_bf16x2(u[8 * q], u[8 * q + 1]), pack_bf16x2(u[8 * q + 2], u[8 * q + 3]),
-                           pack_bf16x2(u[8 * q + 4], u[8 * q + 5]), pack_bf16x2(u[8 * q + 6], u[8 * q + 7]));
-        da[q] = make_uint4(pack_bf16x2(a[8 * q], a[8 * q + 1]), pack_bf16x2(a[8 * q + 2], a[8 * q + 3]),
-                           pack_bf16x2(a[8 * q + 4], a[8 * q + 5]), pack_bf16x2(a[8 * q + 6], a[8 * q + 7]));
-      }
+      for (int q = 0; q < 4; ++q) st_v4_hint(da + q, make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]), pol);
     }
   }
 }
@@ -338,6 +365,8 @@ __device__ __forceinline__ void epilogue_cols(uint32_t acc_tmem, int c_begin, in
   // EPI_ROWSCALE: the accumulated input is scaled per row (online-softmax correction)
   const float beta_row = (EPI == EPI_ROWSCALE && gm < M) ? ea.rowscale[gm] : beta;
   float m_run = -INFINITY, s_run = 0.f;  // EPI_STATS: running max / sum-exp of a 128-col chunk
+  const uint64_t pol_ef = ea.store_hint ? l2_evict_first_policy() : 0ull;
+  const uint64_t* pol = ea.store_hint ? &pol_ef : nullptr;
 #pragma unroll 1
   for (int c0 = c_begin; c0 < c_end; c0 += 32) {
     float v[32];
@@ -364,7 +393,7 @@ __device__ __forceinline__ void epilogue_cols(uint32_t acc_tmem, int c_begin, in
         store_row32<OutT>(C + gm * ldc + gn0, nullptr, v, 1.f, 0.f, valid, vec_ok != 0);
       } else {
         store_row32<OutT>(C + gm * ldc + gn0, Cin ? Cin + gm * ldcin + gn0 : nullptr, v, alpha,
-                          beta_row, valid, vec_ok != 0);
+                          beta_row, valid, vec_ok != 0, pol);
       }
     }
     if constexpr (EPI == EPI_STATS) {
@@ -960,7 +989,7 @@ bool use_pair(int64_t M, int mode) {
 int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
             const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
             const void* Cin, int64_t ldcin, float alpha, float beta, int* status,
-            cudaStream_t stream, int force_bn, int mode, int raster) {
+            cudaStream_t stream, int force_bn, int mode, int raster, int store_hint) {
   const bool a_mn = a_sk != 1;
   const bool b_mn = b_sk != 1;
   const bool pair = use_pair(M, mode);
@@ -993,7 +1022,8 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
   const int vec_ok = (ldc * esz) % 16 == 0 && al16(C) &&
                      (!Cin || ((ldcin * esz) % 16 == 0 && al16(Cin)));
   const int m = (int)M, n = (int)N, k = (int)K;
-  const EpiArgs ea{nullptr, 0, nullptr, raster};
+  EpiArgs ea{nullptr, 0, nullptr, raster};
+  ea.store_hint = store_hint;
   if (pair) {
     if (c_dtype == PE_F32)
       return launch_pair_any_bn<float>(BN, a_mn, b_mn, ta, tb, m, n, k, C, ldc, Cin, ldcin, alpha,
@@ -1159,15 +1189,17 @@ int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm
   // bits 24-29: tile-group size (0 automatic); bit 30: group along N instead of M
   const int group = (algo_bits >> 24) & 0x3f;
   const int raster = ((algo_bits >> 30) & 1) ? -group : group;
+  // bit 22: store C with the L2 evict-first policy
+  const int store_hint = (algo_bits >> 22) & 1;
   const bool tc_ok = gemm_tc_eligible(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, c_dtype);
   if (algo == PE_ALGO_TCGEN05) {
     PE_CHECK_ARG(tc_ok, "gemm: operands not eligible for the tcgen05 path");
     return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
-                   beta, status, stream, force_bn, mode, raster);
+                   beta, status, stream, force_bn, mode, raster, store_hint);
   }
   if (algo == PE_ALGO_AUTO && tc_ok)
     return gemm_tc(M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin, alpha,
-                   beta, status, stream, force_bn, mode, raster);
+                   beta, status, stream, force_bn, mode, raster, store_hint);
   return gemm_simt(dtype, M, N, K, A, a_sm, a_sk, B, b_sn, b_sk, C, ldc, c_dtype, Cin, ldcin,
                    alpha, beta, stream);
 }

@@ -9,8 +9,7 @@ forward  feat RMSNorm -> feat_proj -> [emb | feat] -> in_proj (real slots);
          in_proj([mask_emb; h_shared]) broadcast to the prediction slots;
          per layer: RMSNorm -> fused q/k/v GEMM with RoPE in its epilogue ->
          masked flash attention (mask re-derived from (a0, a1, K)) -> o_proj + residual ->
-         RMSNorm -> fused gate/up GEMM with silu * mul in its epilogue ->
-         down_proj + residual;
+         RMSNorm -> fused gate/up GEMM -> SwiGLU -> down_proj + residual;
          frozen final RMSNorm; loss rows gathered; fused LM head + CE.
 backward the exact reverse, with weight gradients accumulated in place into a
          flat gradient buffer whose slices are the parameters' ``.grad``.
@@ -374,8 +373,11 @@ class StepEngine:
                                            nh, nkv, hd, bounds, k)
             x2 = ops.linear(o, w_o, residual=x)
             xn2, r2 = ops.rmsnorm_fwd(x2, W(p + "post_norm.weight"), eps)
-            # gate|up GEMM with silu(gate) * up in its epilogue (gate|up kept for backward)
-            gu, act = ops.linear_swiglu(xn2, w_gu, I)
+            # gate|up GEMM, then the element-wise SwiGLU: measured faster under the power
+            # cap than ops.linear_swiglu (the activation in the GEMM epilogue), whose
+            # epilogue work confines the GEMM to 256-wide tiles
+            gu = ops.linear(xn2, w_gu)
+            act = ops.swiglu_fwd(gu, I)
             x3 = ops.linear(act, w_dn, residual=x2)
             saved.append((x, xn, r1, qkv, o, lse, x2, xn2, r2, gu, act))
             x = x3

@@ -202,6 +202,26 @@ def test_rope_matches_reference_rotation(dtype, max_pos):
     assert rel(y.float().cpu(), x.float().cpu()) < (1e-5 if dtype == torch.float32 else 2e-2)
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 640, 256), (1024, 1536, 512)])
+@pytest.mark.parametrize("out_f32", [False, True])
+def test_gemm_evict_first_stores_match_plain(M, N, K, out_f32):
+    """algo bit 22 (C stored with the L2 evict-first policy) changes only the cache
+    policy: the results equal the plain GEMM's, accumulate included."""
+    x = _rand(M, K, seed=72)
+    w = _rand(N, K, seed=73, scale=0.05)
+    dt = torch.float32 if out_f32 else torch.bfloat16
+    base = _rand(M, N, dtype=dt, seed=74)
+    ref = base.clone()
+    ops.gemm(M, N, K, x, K, 1, w, K, 1, ref, N, Cin=ref, ldcin=N, alpha=0.5, beta=1.0,
+             algo=L.ALGO_TCGEN05)
+    got = base.clone()
+    ops.gemm(M, N, K, x, K, 1, w, K, 1, got, N, Cin=got, ldcin=N, alpha=0.5, beta=1.0,
+             algo=L.ALGO_TCGEN05 | (1 << 22))
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert torch.equal(got, ref)
+
+
 @pytest.mark.parametrize("M,I,K,bn", [(300, 512, 256, 0), (600, 512, 320, 256), (600, 1024, 256, 512),
                                       (4096, 2048, 512, 0), (1500, 768, 192, 256)])
 def test_linear_swiglu_equals_linear_then_swiglu(M, I, K, bn):
