@@ -548,6 +548,22 @@ def time_case(run, reps, warmup=3, flush=None):
     return sum(times) / len(times)
 
 
+def time_variants(runs: dict, reps: int, warmup: int = 2, rounds: int = 5) -> dict:
+    """Median milliseconds per call of each variant over ``rounds`` interleaved rounds
+    (each round times every variant ``reps`` times, in an order that alternates from
+    round to round), so a clock that drifts under the power cap does not favour
+    whichever variant runs first."""
+    for fn in runs.values():
+        for _ in range(warmup):
+            fn()
+    names = list(runs)
+    samples = {n: [] for n in names}
+    for r in range(rounds):
+        for n in (names if r % 2 == 0 else names[::-1]):
+            samples[n].append(time_case(runs[n], reps, warmup=0))
+    return {n: sorted(v)[len(v) // 2] for n, v in samples.items()}
+
+
 def time_case_graph(run, reps, warmup=3):
     """Average milliseconds per call of ``run``, captured ``reps`` times into one CUDA
     graph and replayed (CUDA events on the current stream): device time without the
@@ -686,6 +702,65 @@ def run_sweep(args):
         dist.destroy_process_group()
 
 
+AB_VARIANTS = {
+    # name -> StepEngine kernel choices (every variant computes the same result)
+    "default": {},
+    "unfused_rope": {"fuse_rope": False},
+    "fused_swiglu": {"fuse_swiglu": True},
+    "lmhead_256_256": {"lmhead_algo": (1 << 24) | (1 << 26)},
+    "lmhead_auto_dh256": {"lmhead_algo": 1 << 26},
+}
+
+
+def run_ab(args):
+    """Step-level A/B of the engine's kernel choices on one GPU: one trainer on the
+    config-2 workload, whole training steps of each variant in interleaved rounds (the
+    order alternating round to round, so a clock drifting under the power cap favours
+    none), median step time per variant."""
+    from parallel_eagle_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    workload, base = WORKLOADS[args.config]
+    c = dict(base)
+    B, n, k = c["batch"], c["n"], c["max_depth"]
+    drafter = build_drafter(c, dev, seed=0)
+    trainer = Trainer(drafter, c, 1)
+    g = torch.Generator(device=dev).manual_seed(1000)
+    ids = torch.randint(0, c["vocab"], (B, n), generator=g, device=dev)
+    feats = torch.randn(B, n, 3 * c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    seqs = [(ids[b], feats[b]) for b in range(B)]
+    teachers = None
+    if c.get("soft"):
+        teachers = torch.randn(B, n, c["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    names = [v for v in args.ab.split(",") if v]
+    eng = trainer.eng
+    defaults = {key: getattr(eng, key) for key in ("fuse_rope", "fuse_swiglu", "lmhead_algo")}
+
+    def use(name):
+        for key, val in defaults.items():
+            setattr(eng, key, AB_VARIANTS[name].get(key, val))
+
+    samples = {nm: [] for nm in names}
+    for nm in names:
+        use(nm)
+        for _ in range(args.warmup):
+            trainer.step(seqs, B, teachers)
+    for r in range(args.ab_rounds):
+        for nm in (names if r % 2 == 0 else names[::-1]):
+            use(nm)
+            samples[nm].append(time_case(lambda: trainer.step(seqs, B, teachers), args.steps,
+                                         warmup=1))
+    ops.check_status(dev)
+    out = {}
+    for nm, v in samples.items():
+        ms = sorted(v)[len(v) // 2]
+        out[nm] = {"ms_per_step": round(ms, 2), "slot_tokens_per_s": round(B * n * k / (ms / 1e3), 1),
+                   "rounds_ms": [round(x, 2) for x in v]}
+    print(json.dumps({"ab": workload, "steps_per_round": args.steps, "rounds": args.ab_rounds,
+                      "results": out}), flush=True)
+
+
 def run_kernel(args):
     """One kernel family on its bench-sized case (the unit an ncu capture covers)."""
     dev = torch.device("cuda", 0)
@@ -726,8 +801,7 @@ def run_kernel(args):
         for bn in (0, 256, 512):
             runs[f"fused_bn{bn or 'auto'}"] = (
                 lambda bn=bn: ops.linear_swiglu(x, w, I, gu=gu, act=act, algo=bn << 8))
-        for name, fn in runs.items():
-            ms = time_case(fn, args.steps, warmup=args.warmup)
+        for name, ms in time_variants(runs, args.steps, warmup=args.warmup).items():
             out[name] = {"ms": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
         # the q|k|v projection of the same pass: GEMM + rotation kernel vs RoPE epilogue
         nh, nkv, hd = c["n_heads"], c["n_kv_heads"], c["hidden"] // c["n_heads"]
@@ -741,14 +815,36 @@ def run_kernel(args):
                  "qkv_gemm_only": lambda: ops.linear(x, wq, out=qkv),
                  "qkv_gemm_only_evict_first": lambda: ops.linear(x, wq, out=qkv, algo=1 << 22),
                  "qkv_fused_rope": lambda: ops.linear_rope(x, wq, cs, (nh + nkv) * hd, hd, out=qkv)}
-        for name, fn in qruns.items():
-            ms = time_case(fn, args.steps, warmup=args.warmup)
+        for name, ms in time_variants(qruns, args.steps, warmup=args.warmup).items():
             out[name] = {"ms": round(ms, 4), "tflops": round(qflops / (ms / 1e3) / 1e12, 1)}
         ops.check_status(dev)
         print(json.dumps({"kernel": "gate|up + swiglu; q|k|v + rope", "M": M, "N": 2 * I, "K": H,
                           "results": out}), flush=True)
         return
-    case = {"gemm": gemm_case, "attn": attention_case, "lmhead": lmhead_case}[args.kernel]
+    if args.kernel == "lmhead":
+        # the fused LM head on all 10240 loss rows of a config-2 sequence (the step's
+        # call), with its logits / dH GEMM tile widths automatic or forced (algo bits
+        # 24-25 / 26-27: 1 = 256-wide, 2 = 512-wide pair tiles)
+        R, H, V = 10240, c["hidden"], c["vocab"]
+        g = torch.Generator(device=dev).manual_seed(13)
+        h = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
+        W = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        lab = torch.randint(0, V, (R,), generator=g, device=dev)
+        loss = torch.zeros(1, device=dev)
+        flops = 2.0 * 2 * R * V * H
+        out = {}
+        variants = {"auto": 0, "logits256_dh512": (1 << 24) | (2 << 26),
+                    "logits512_dh512": (2 << 24) | (2 << 26),
+                    "logits256_dh256": (1 << 24) | (1 << 26),
+                    "logits512_dh256": (2 << 24) | (1 << 26)}
+        runs = {n: (lambda b=b: ops.lmhead_ce(h, W, lab, 1e-4, loss, algo=b))
+                for n, b in variants.items()}
+        for name, ms in time_variants(runs, args.steps, warmup=args.warmup).items():
+            out[name] = {"ms": round(ms, 3), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
+        ops.check_status(dev)
+        print(json.dumps({"kernel": "lmhead", "R": R, "H": H, "V": V, "results": out}), flush=True)
+        return
+    case = {"gemm": gemm_case, "attn": attention_case}[args.kernel]
     run, flops, _ = case(c, dev)
     ms = time_case(run, args.steps, warmup=args.warmup)
     ops.check_status(dev)
@@ -905,10 +1001,16 @@ def main(argv=None):
     ap.add_argument("--kernel", choices=["gemm", "attn", "lmhead", "elementwise", "swiglu"],
                     default=None,
                     help="time one kernel family on its bench-sized case instead of the step")
+    ap.add_argument("--ab", default=None,
+                    help="comma-separated engine variants to A/B at step level (" +
+                    ", ".join(AB_VARIANTS) + ")")
+    ap.add_argument("--ab-rounds", type=int, default=4)
     ap.add_argument("--draft", action="store_true",
                     help="time the draft path (draft_logits / propose_tree) on config-2 dims")
     args = ap.parse_args(argv)
-    if args.draft:
+    if args.ab:
+        run_ab(args)
+    elif args.draft:
         run_draft(args)
     elif args.sweep:
         run_sweep(args)

@@ -26,13 +26,14 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
 // of the stored (rounded) values in stats[row * stats_ld + tile].
 int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
                          const void* B, int64_t ldb, void* C, int64_t ldc, float2* stats,
-                         int stats_ld, int* status, cudaStream_t stream);
+                         int stats_ld, int* status, cudaStream_t stream, int force_bn = 0);
 
 // C (fp32) = A[M, K] B + rowscale[row] * Cin, A K-major, B (n, k) at B[n + k * b_sk]
 // (MN-major): the online-softmax rescaled accumulation of the LM-head input gradient.
 int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
                          const void* B, int64_t b_sk, float* C, int64_t ldc, const float* Cin,
-                         const float* rowscale, int* status, cudaStream_t stream);
+                         const float* rowscale, int* status, cudaStream_t stream,
+                         int force_bn = 0);
 
 // pe_gemm without the C wrapper (used inside the library)
 int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,

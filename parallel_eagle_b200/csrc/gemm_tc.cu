@@ -1040,14 +1040,18 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
 
 int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
                          const void* B, int64_t ldb, void* C, int64_t ldc, float2* stats,
-                         int stats_ld, int* status, cudaStream_t stream) {
+                         int stats_ld, int* status, cudaStream_t stream, int force_bn) {
   PE_CHECK_ARG(M > 0 && N > 0 && K > 0 && lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 &&
                    al16(A) && al16(B) && al16(C),
                "gemm (logits + row stats): operands must be 16-byte aligned bf16");
   PE_CHECK_ARG(stats_ld >= (N + 127) / 128, "gemm (logits + row stats): stats_ld too small");
+  PE_CHECK_ARG(force_bn == 0 || force_bn == 256 || force_bn == 512,
+               "gemm (logits + row stats): tile width %d not 256 or 512", force_bn);
   const bool pair = use_pair(M, 0);
   // pair tiles 256 x 512 or 256 x 256 (the stats need 128-column aligned halves)
-  const int pbn = pair ? (choose_bn_pair(M, N, K, false, 2, sm_count() / 2) > 256 ? 512 : 256) : 256;
+  const int pbn = !pair ? 256
+                  : force_bn ? force_bn
+                  : (choose_bn_pair(M, N, K, false, 2, sm_count() / 2) > 256 ? 512 : 256);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
   if (!rc)
@@ -1068,7 +1072,8 @@ int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t
 
 int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
                          const void* B, int64_t b_sk, float* C, int64_t ldc, const float* Cin,
-                         const float* rowscale, int* status, cudaStream_t stream) {
+                         const float* rowscale, int* status, cudaStream_t stream,
+                         int force_bn) {
   PE_CHECK_ARG(M > 0 && N > 0 && K > 0 && lda % 8 == 0 && b_sk % 8 == 0 && ldc % 4 == 0 &&
                    al16(A) && al16(B) && al16(C),
                "gemm (row-scaled accumulate): operands must be 16-byte aligned");
@@ -1077,8 +1082,11 @@ int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t
   if (!rc) rc = make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)b_sk * 2, 64, 64);
   if (rc) return rc;
   EpiArgs ea{nullptr, 0, rowscale, 0};
+  PE_CHECK_ARG(force_bn == 0 || force_bn == 256 || force_bn == 512,
+               "gemm (row-scaled accumulate): tile width %d not 256 or 512", force_bn);
   if (use_pair(M, 0)) {
-    if (choose_bn_pair(M, N, K, true, 4, sm_count() / 2) == 512)
+    const int bn = force_bn ? force_bn : choose_bn_pair(M, N, K, true, 4, sm_count() / 2);
+    if (bn == 512)
       return launch_pair<512, false, true, float, EPI_ROWSCALE>(
           ta, tb, (int)M, (int)N, (int)K, C, ldc, Cin, ldc, 1.f, 0.f, 1, status, stream, ea);
     return launch_pair<256, false, true, float, EPI_ROWSCALE>(

@@ -235,8 +235,10 @@ static_assert(kMaxChunk / kStatTile <= 128, "combine_kernel folds at most 128 ti
 // 1024 vocabulary rows) and bits 16-23 the group (units of 256 loss rows).
 struct FastPlan {
   int64_t vc, rg;
+  int logits_bn, dh_bn;  // pair tile widths (0: the GEMMs' own choice)
 };
 
+// algo bits 24-25 / 26-27: logits / dH GEMM pair tile width (1: 256, 2: 512, 0: automatic)
 FastPlan fast_plan_of(int64_t R, int64_t V, int algo) {
   int64_t vc = ((algo >> 8) & 0xff) ? ((algo >> 8) & 0xff) * 1024 : kFastChunk;
   int64_t rg = ((algo >> 16) & 0xff) ? ((algo >> 16) & 0xff) * 256 : kRowGroup;
@@ -249,7 +251,8 @@ FastPlan fast_plan_of(int64_t R, int64_t V, int algo) {
     const int64_t ng = (R + rg - 1) / rg;
     rg = ((R + ng - 1) / ng + 127) / 128 * 128;
   }
-  return {vc, rg};
+  const int lb = (algo >> 24) & 3, db = (algo >> 26) & 3;
+  return {vc, rg, lb == 1 ? 256 : lb == 2 ? 512 : 0, db == 1 ? 256 : db == 2 ? 512 : 0};
 }
 
 struct FastLayout {
@@ -428,7 +431,7 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
       const __nv_bfloat16* Wc = (const __nv_bfloat16*)W + v0 * H;
       if (t >= 2) PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_dh[b], 0));
       int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Z[b], VC, stats[b], nt_max,
-                                    status, st);
+                                    status, st, P.logits_bn);
       if (rc) return rc;
       PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
       PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
@@ -437,7 +440,7 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
                                                      alpha + r0);
       PE_LAUNCHED();
       rc = gemm_tc_rowscale_acc(rg, H, vc, Z[b], VC, Wc, H, dHg, H, v0 > 0 ? dHg : nullptr,
-                                alpha + r0, status, side);
+                                alpha + r0, status, side, P.dh_bn);
       if (rc) return rc;
       PE_CUDA_TRY(cudaEventRecord(ev_dh[b], side));
     }
@@ -664,8 +667,11 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
       float2* ss = (float2*)(ws + L.stats_s[b]);
       float2* stt = (float2*)(ws + L.stats_t[b]);
       if (t >= 2) PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_dh[b], 0));
-      int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Zs, VC, ss, nt_max, status, st);
-      if (!rc) rc = gemm_tc_logits_stats(rg, vc, H, tg, ldt, Wc, H, Zt, VC, stt, nt_max, status, st);
+      int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Zs, VC, ss, nt_max, status, st,
+                                    P.logits_bn);
+      if (!rc)
+        rc = gemm_tc_logits_stats(rg, vc, H, tg, ldt, Wc, H, Zt, VC, stt, nt_max, status, st,
+                                  P.logits_bn);
       if (rc) return rc;
       PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
       PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
@@ -674,10 +680,12 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
                                                           lt + r0, szt + r0, alpha_t + r0);
       PE_LAUNCHED();
       rc = gemm_tc_rowscale_acc(rg, H, vc, Zs, VC, Wc, H, dHs + r0 * H, H,
-                                v0 > 0 ? dHs + r0 * H : nullptr, alpha + r0, status, side);
+                                v0 > 0 ? dHs + r0 * H : nullptr, alpha + r0, status, side,
+                                P.dh_bn);
       if (!rc)
         rc = gemm_tc_rowscale_acc(rg, H, vc, Zt, VC, Wc, H, dHt + r0 * H, H,
-                                  v0 > 0 ? dHt + r0 * H : nullptr, alpha_t + r0, status, side);
+                                  v0 > 0 ? dHt + r0 * H : nullptr, alpha_t + r0, status, side,
+                                  P.dh_bn);
       if (rc) return rc;
       PE_CUDA_TRY(cudaEventRecord(ev_dh[b], side));
     }

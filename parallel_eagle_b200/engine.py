@@ -169,6 +169,12 @@ class StepEngine:
         # projections' backward -- so a data-parallel caller can start reducing them
         self.after_layers = None
         self.loss_sum = torch.zeros(1, dtype=torch.float32, device=self.flat.device)
+        # kernel choices (results are identical either way; chosen by step-level timing):
+        # RoPE in the q|k|v GEMM epilogue and the attention backward (bf16, head_dim
+        # 128); SwiGLU in the gate|up GEMM epilogue; the fused LM head's tuning bits
+        self.fuse_rope = True
+        self.fuse_swiglu = False
+        self.lmhead_algo = 0
 
     # --------------------------------------------------------------- plans --
     def _segment_arrays(self, a0: int, a1: int, n: int, prompt_len: int):
@@ -316,7 +322,7 @@ class StepEngine:
         # bf16 with head_dim 128: RoPE rides in the q|k|v GEMM epilogue and its transpose
         # in the attention backward's dQ store / dK cast, reading a per-plan cos / sin
         # table (the slot positions are fixed per plan)
-        fuse_rope = dt == torch.bfloat16 and hd == 128
+        fuse_rope = self.fuse_rope and dt == torch.bfloat16 and hd == 128
         if fuse_rope and plan.rope_cs is None:
             plan.rope_cs = ops.rope_table(plan.pos, hd, d.rope_theta, dt)
         rope_cs = plan.rope_cs if fuse_rope else None
@@ -373,11 +379,12 @@ class StepEngine:
                                            nh, nkv, hd, bounds, k)
             x2 = ops.linear(o, w_o, residual=x)
             xn2, r2 = ops.rmsnorm_fwd(x2, W(p + "post_norm.weight"), eps)
-            # gate|up GEMM, then the element-wise SwiGLU: measured faster under the power
-            # cap than ops.linear_swiglu (the activation in the GEMM epilogue), whose
-            # epilogue work confines the GEMM to 256-wide tiles
-            gu = ops.linear(xn2, w_gu)
-            act = ops.swiglu_fwd(gu, I)
+            if self.fuse_swiglu:
+                # the activation in the gate|up GEMM epilogue (gate|up kept for backward)
+                gu, act = ops.linear_swiglu(xn2, w_gu, I)
+            else:
+                gu = ops.linear(xn2, w_gu)
+                act = ops.swiglu_fwd(gu, I)
             x3 = ops.linear(act, w_dn, residual=x2)
             saved.append((x, xn, r1, qkv, o, lse, x2, xn2, r2, gu, act))
             x = x3
@@ -394,7 +401,8 @@ class StepEngine:
             labels = teacher_labels[plan.tgt - 1].to(torch.int64)
         else:
             labels = ids[plan.tgt]
-        dh = ops.lmhead_ce(hv, Wh, labels, scale, self.loss_sum, teacher=teacher)
+        dh = ops.lmhead_ce(hv, Wh, labels, scale, self.loss_sum, teacher=teacher,
+                           algo=self.lmhead_algo)
         dhf = torch.zeros(Q, H, dtype=dt, device=dev)
         ops.scatter_rows(dh, idx, dhf)
         dx, _ = ops.rmsnorm_bwd(dhf, x, wfinal, rf, want_dw=False)
