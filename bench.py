@@ -468,12 +468,19 @@ def attention_case(c, dev):
     do = torch.randn(R, nh * hd, generator=g, device=dev).to(torch.bfloat16)
     q, kk, vv = qkv[:, : nh * hd], qkv[:, nh * hd:(nh + nkv) * hd], qkv[:, (nh + nkv) * hd:]
     dqkv = torch.empty_like(qkv)
+    # the step's backward also rotates dQ / dK back (RoPE's transpose, fused in the dQ
+    # store and the dK cast): the same table the step builds for these slots
+    from parallel_eagle_b200.engine import StepEngine
+
+    pos = torch.cat([torch.from_numpy(StepEngine._segment_arrays_static(a0, a1, c["n"], k, 0)[0])
+                     for a0, a1 in bounds]).to(dev)
+    cs = ops.rope_table(pos, hd, 10000.0, torch.bfloat16)
 
     def run():
         o, lse = ops.attn_fwd_segments(q, kk, vv, nh, nkv, hd, bounds, k)
         ops.attn_bwd_segments(q, kk, vv, o, do, lse, nh, nkv, hd, bounds, k,
                               dq=dqkv[:, : nh * hd], dk=dqkv[:, nh * hd:(nh + nkv) * hd],
-                              dv=dqkv[:, (nh + nkv) * hd:])
+                              dv=dqkv[:, (nh + nkv) * hd:], rope_cs=cs)
 
     return run, 12.0 * hd * nh * attention_pairs(c["n"], k, c["segments"]), None
 
@@ -821,6 +828,26 @@ def run_kernel(args):
         print(json.dumps({"kernel": "gate|up + swiglu; q|k|v + rope", "M": M, "N": 2 * I, "K": H,
                           "results": out}), flush=True)
         return
+    if args.kernel == "attnfwd":
+        # the masked-attention forward over one config-2 sequence's stacked segments, by
+        # the share of exponentials taken from the FMA-pipe polynomial (one pair in e)
+        from parallel_eagle_b200.engine import segment_bounds
+
+        nh, nkv, hd, k = c["n_heads"], c["n_kv_heads"], c["hidden"] // c["n_heads"], c["max_depth"]
+        g = torch.Generator(device=dev).manual_seed(11)
+        bounds = segment_bounds(c["n"], c["segments"])
+        R = sum(ops.segment_rows(bounds, k))
+        qkv = torch.randn(R, (nh + 2 * nkv) * hd, generator=g, device=dev).to(torch.bfloat16)
+        q, kk, vv = qkv[:, : nh * hd], qkv[:, nh * hd:(nh + nkv) * hd], qkv[:, (nh + nkv) * hd:]
+        flops = 4.0 * hd * nh * attention_pairs(c["n"], k, c["segments"])
+        runs = {f"emu{e}": (lambda e=e: ops.attn_fwd_segments(q, kk, vv, nh, nkv, hd, bounds, k,
+                                                              algo=(e + 1) << 16))
+                for e in (0, 2, 3, 4, 6, 8)}
+        out = {n: {"ms": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
+               for n, ms in time_variants(runs, args.steps, warmup=args.warmup).items()}
+        ops.check_status(dev)
+        print(json.dumps({"kernel": "attention forward", "results": out}), flush=True)
+        return
     if args.kernel == "lmhead":
         # the fused LM head on all 10240 loss rows of a config-2 sequence (the step's
         # call), with its logits / dH GEMM tile widths automatic or forced (algo bits
@@ -998,7 +1025,8 @@ def main(argv=None):
     ap.add_argument("--sweep-n", default="256,512,1024,2048,4096")
     ap.add_argument("--sweep-k", default="4,8")
     ap.add_argument("--sweep-s", default="1,2,4,8")
-    ap.add_argument("--kernel", choices=["gemm", "attn", "lmhead", "elementwise", "swiglu"],
+    ap.add_argument("--kernel", choices=["gemm", "attn", "attnfwd", "lmhead", "elementwise",
+                                         "swiglu"],
                     default=None,
                     help="time one kernel family on its bench-sized case instead of the step")
     ap.add_argument("--ab", default=None,

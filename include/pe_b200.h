@@ -283,6 +283,15 @@ int pe_softmax_rows(int dtype, int64_t rows, int64_t V, const void* logits, int6
  * m, v are fp32 moment buffers.
  * ------------------------------------------------------------------------- */
 int pe_sumsq(int dtype, int64_t n, const void* g, float* sumsq_out, void* stream);
+/* The same sum of squares, deterministic: partials[b] (fp32, b < nblk <= 65535) =
+ * block b's share over a fixed grid of nblk blocks, no atomics; pe_sum_f32 then adds
+ * n floats in a fixed order into out[0] (accumulate = 1: out[0] += the sum).  Used for
+ * the global-norm clip of data-parallel updates, so every rank holding the same
+ * gradient computes the same coefficient (pe_sumsq's atomic order varies from run to
+ * run and rank to rank). */
+int pe_sumsq_partials(int dtype, int64_t n, const void* g, float* partials, int64_t nblk,
+                      void* stream);
+int pe_sum_f32(int64_t n, const float* x, float* out, int accumulate, void* stream);
 int pe_adamw_step(int dtype, int64_t n, void* p, const void* g, float* m, float* v,
                   const float* sumsq, float max_norm, float lr, float beta1, float beta2,
                   float eps, float weight_decay, int64_t step, void* stream);

@@ -89,6 +89,8 @@ SIGNATURES: dict[str, tuple] = {
     "pe_topk_logprobs": (_int, [_int, _i64, _i64, _vp, _i64, _int, _int, _vp, _vp, _vp]),
     "pe_softmax_rows": (_int, [_int, _i64, _i64, _vp, _i64, _f32, _vp, _i64, _vp]),
     "pe_sumsq": (_int, [_int, _i64, _vp, _vp, _vp]),
+    "pe_sumsq_partials": (_int, [_int, _i64, _vp, _vp, _i64, _vp]),
+    "pe_sum_f32": (_int, [_i64, _vp, _vp, _int, _vp]),
     "pe_adamw_step": (
         _int, [_int, _i64, _vp, _vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32, _f32, _f32, _i64, _vp]
     ),

@@ -156,7 +156,13 @@ extern "C" int pe_attn_fwd_segments(int dtype, int nseg, const int64_t* bounds, 
   if (!seg_geoms(nseg, bounds, kdepth, g, rows)) return PE_ERR_ARG;
   PE_CHECK_ARG(Hq >= 1 && Hkv >= 1 && head_dim >= 1 && Hq % Hkv == 0 && Hq <= 65535,
                "attention segments: bad head counts");
-  PE_CHECK_ARG((algo >> 8) == 0, "attention segments: kernel-variant bits are not accepted");
+  // bits 16-19: the forward's exponential-emulation ratio + 1 (0: default); no other
+  // variant bits
+  PE_CHECK_ARG(((algo >> 8) & ~0xf00) == 0,
+               "attention segments: kernel-variant bits other than the forward's "
+               "exp-emulation bits 16-19 are not accepted");
+  const int emu = ((algo >> 16) & 0xf) - 1;
+  algo &= 0xff;
   bool tc = true;
   for (int s = 0; s < nseg; ++s)
     tc = tc && attn_tc_eligible(dtype, 1, g[s].S, Hq, Hkv, head_dim, PE_LAYOUT_PARTITION, q, q_ss,
@@ -164,7 +170,7 @@ extern "C" int pe_attn_fwd_segments(int dtype, int nseg, const int64_t* bounds, 
   if (algo == PE_ALGO_TCGEN05) PE_CHECK_ARG(tc, "attention: inputs not eligible for tcgen05");
   if (tc && algo != PE_ALGO_SIMT)
     return attn_fwd_tc_segments(nseg, g.data(), Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, lse,
-                                status, as_stream(stream));
+                                status, as_stream(stream), emu);
   PE_CHECK_ARG(dtype == PE_F32 || dtype == PE_BF16, "attention segments: unknown dtype %d", dtype);
   const size_t es = elem_bytes(dtype);
   int64_t row0 = 0;

@@ -79,9 +79,12 @@ int attn_bwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
 // Stacked segments (tensor cores): segment s occupies rows [row0_s, row0_s + g[s].S)
 // of every row operand, row0_0 = 0 and row0_{s+1} = row0_s + g[s].S; lse / delta hold
 // one [Hq, g[s].S] block per segment starting at element Hq * row0_s.
+// emu: one exponential pair in `emu` from the FMA-pipe polynomial (0: none; -1: the
+// default ratio)
 int attn_fwd_tc_segments(int nseg, const attn_tc::PartGeom* g, int Hq, int Hkv, const void* q,
                          int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
-                         void* o, int64_t o_ss, float* lse, int* status, cudaStream_t st);
+                         void* o, int64_t o_ss, float* lse, int* status, cudaStream_t st,
+                         int emu = -1);
 // acc: fp32 dK / dV accumulators and the work counter, attn_tc_seg_acc_bytes(rows)
 size_t attn_tc_seg_acc_bytes(int64_t rows, int Hkv);
 // rope_cs (may be NULL): per stacked row [cos hd/2 | sin hd/2] table (row stride

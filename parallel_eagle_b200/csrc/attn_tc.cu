@@ -340,13 +340,11 @@ constexpr int kThreads2 = 384;
 constexpr int kRegsLow = 56, kRegsHigh = 224;  // 128 x 56 + 256 x 224 = 384 x 168
 constexpr size_t SMEM_FWD2 = 1024 + 2 * TILE_BYTES /*Q_A, Q_B*/ + 2 * 2 * TILE_BYTES /*K,V x2*/ + 256;
 constexpr float kRescaleLog2 = 8.f;
-// one pair of scores in kEmuEvery takes its exponential from the FMA-pipe
-// polynomial (0: all on the SFU); the SFU alone runs one exp per score, which at
-// head_dim 128 takes as long as the tile's two MMAs
-#ifndef PE_FWD_EMU_EVERY
-#define PE_FWD_EMU_EVERY 4
-#endif
-constexpr int kEmuEvery = PE_FWD_EMU_EVERY;
+// one pair of scores in EMU takes its exponential from the FMA-pipe polynomial (0:
+// all on the SFU); the SFU alone runs one exp per score, which at head_dim 128 takes
+// as long as the tile's two MMAs.  The kernel is instantiated for a few ratios
+// (attn_fwd_tc_segments' `emu`); kEmuDefault is the one the step uses.
+constexpr int kEmuDefault = 4;
 
 struct PairTiles {
   TileList a, b;  // b empty (count 0) when the second query tile lies past the sequence
@@ -369,6 +367,7 @@ struct PairTiles {
   }
 };
 
+template <int kEmuEvery>
 __global__ void __launch_bounds__(kThreads2, 1)
 attn_fwd_tc2_kernel(const __grid_constant__ SegTable tab, __nv_bfloat16* __restrict__ O,
                     int64_t o_ss, float* __restrict__ lse, int Hq, int rep, float scale_log2,
@@ -702,20 +701,31 @@ int attn_fwd_tc_launch(int64_t S, int Hq, int Hkv, const void* q, int64_t q_ss, 
     PE_LAUNCHED();
     return PE_OK;
   }
-  return attn_fwd_tc_segments(1, &g, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, lse, status, st);
+  return attn_fwd_tc_segments(1, &g, Hq, Hkv, q, q_ss, k, k_ss, v, v_ss, o, o_ss, lse, status, st,
+                              -1);
 }
 
 int attn_fwd_tc_segments(int nseg, const PartGeom* g, int Hq, int Hkv, const void* q,
                          int64_t q_ss, const void* k, int64_t k_ss, const void* v, int64_t v_ss,
-                         void* o, int64_t o_ss, float* lse, int* status, cudaStream_t st) {
+                         void* o, int64_t o_ss, float* lse, int* status, cudaStream_t st,
+                         int emu) {
   PE_CHECK_ARG(o_ss % 8 == 0 && al16(o), "attention (tcgen05): output must be 16-byte aligned");
-  PE_CUDA_TRY(cudaFuncSetAttribute(attn_fwd_tc2_kernel,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_FWD2));
+  if (emu < 0) emu = kEmuDefault;
+  auto kern = emu == 0 ? attn_fwd_tc2_kernel<0>
+              : emu == 2 ? attn_fwd_tc2_kernel<2>
+              : emu == 3 ? attn_fwd_tc2_kernel<3>
+              : emu == 6 ? attn_fwd_tc2_kernel<6>
+              : emu == 8 ? attn_fwd_tc2_kernel<8>
+                         : attn_fwd_tc2_kernel<4>;
+  PE_CHECK_ARG(emu == 0 || emu == 2 || emu == 3 || emu == 4 || emu == 6 || emu == 8,
+               "attention (tcgen05): exp emulation ratio %d not 0/2/3/4/6/8", emu);
+  PE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)SMEM_FWD2));
   {
     // the warpgroups' register re-split assumes the launch grants 168 per thread:
     // with fewer, setmaxnreg.inc would wait for registers that never free up
     cudaFuncAttributes fa;
-    PE_CUDA_TRY(cudaFuncGetAttributes(&fa, attn_fwd_tc2_kernel));
+    PE_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
     PE_CHECK_ARG(fa.numRegs * kThreads2 >= 4 * 32 * kRegsLow + 8 * 32 * kRegsHigh,
                  "attention (tcgen05): forward kernel compiled with too few registers");
   }
@@ -757,8 +767,8 @@ int attn_fwd_tc_segments(int nseg, const PartGeom* g, int Hq, int Hkv, const voi
     PE_CHECK_ARG(ny <= 65535, "attention: too many query tiles for one launch");
     dim3 grid((unsigned)Hq, (unsigned)ny);
     __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(o) + rows[b] * o_ss;
-    attn_fwd_tc2_kernel<<<grid, kThreads2, SMEM_FWD2, st>>>(tab, ob, o_ss, lse + (int64_t)Hq * rows[b],
-                                                           Hq, Hq / Hkv, scale_log2, status);
+    kern<<<grid, kThreads2, SMEM_FWD2, st>>>(tab, ob, o_ss, lse + (int64_t)Hq * rows[b], Hq,
+                                             Hq / Hkv, scale_log2, status);
     PE_LAUNCHED();
   }
   return PE_OK;

@@ -52,6 +52,44 @@ __global__ void adamw_kernel(int64_t n, T* __restrict__ p, const T* __restrict__
   }
 }
 
+// Deterministic sum of squares: block b of a fixed grid reduces elements b * 256 + t,
+// strided by the grid, in a fixed order and writes partials[b] (no atomics), then one
+// block adds the partials in a fixed order.  Every rank of a data-parallel job holding
+// the same gradient therefore computes the same bits -- the clip coefficient, and so
+// the update, cannot drift apart between replicas.
+template <typename T>
+__global__ void sumsq_partials_kernel(int64_t n, const T* __restrict__ g, float* __restrict__ part) {
+  __shared__ float sh[32];
+  float s = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = to_f(g[i]);
+    s += x * x;
+  }
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) part[blockIdx.x] = t;
+  }
+}
+
+__global__ void sum_f32_kernel(int64_t n, const float* __restrict__ x, float* out, int accumulate) {
+  __shared__ float sh[32];
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) out[0] = accumulate ? out[0] + t : t;
+  }
+}
+
 unsigned grid_for(int64_t n) {
   int64_t g = ceil_div(n, 256);
   const int64_t cap = (int64_t)sm_count() * 8;
@@ -71,6 +109,24 @@ extern "C" int pe_sumsq(int dtype, int64_t n, const void* g, float* sumsq_out, v
     PE_LAUNCHED();
     return PE_OK;
   });
+}
+
+extern "C" int pe_sumsq_partials(int dtype, int64_t n, const void* g, float* partials,
+                                 int64_t nblk, void* stream) {
+  PE_CHECK_ARG(n >= 0 && nblk >= 1 && nblk <= 65535, "sumsq_partials: bad size / block count");
+  return PE_DISPATCH(dtype, T, [&] {
+    sumsq_partials_kernel<T><<<(unsigned)nblk, 256, 0, as_stream(stream)>>>(n, (const T*)g,
+                                                                             partials);
+    PE_LAUNCHED();
+    return PE_OK;
+  });
+}
+
+extern "C" int pe_sum_f32(int64_t n, const float* x, float* out, int accumulate, void* stream) {
+  PE_CHECK_ARG(n >= 0, "sum_f32: bad size");
+  sum_f32_kernel<<<1, 1024, 0, as_stream(stream)>>>(n, x, out, accumulate);
+  PE_LAUNCHED();
+  return PE_OK;
 }
 
 extern "C" int pe_adamw_step(int dtype, int64_t n, void* p, const void* g, float* m, float* v,

@@ -379,6 +379,94 @@ rmsnorm_bwd_tiled_kernel(int64_t rows, int64_t H, const T* __restrict__ dy, int6
   }
 }
 
+// bf16 backward for rows of H = 512 W columns (W <= 8), one block of W warps per row at
+// a time: lane l of warp v owns columns 8 (32 (2 v + i) + l) .. + 8 for i = 0, 1, so each
+// thread holds two 16-byte chunks of dy, x and the residual (all loads of a row issued
+// together: one DRAM round trip per row) and the block adds its warps' parts of
+// sum(dy w x) through shared memory (one barrier per row; the slots alternate with the
+// row parity).  Every thread keeps the weight-gradient partial of its 16 columns in
+// registers across all the rows its block visits and writes it once into the block's
+// row of dw_partial -- no per-row shared-memory traffic.  Two blocks per SM (the
+// persistent grid's size) at <= 146 registers: 14 warps per SM at H = 3584, against 8
+// for the one-warp-per-row kernel below.
+template <int W>
+__global__ void __launch_bounds__(W * 32, 2)
+rmsnorm_bwd_rowblock_kernel(int64_t rows, const __nv_bfloat16* __restrict__ dy, int64_t lddy,
+                            const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                            const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                            __nv_bfloat16* dx, int64_t lddx, const __nv_bfloat16* res,
+                            int64_t ldres, float* __restrict__ dw_partial) {
+  constexpr int H = W * 512;
+  __shared__ float s_part[2][W];  // [row parity][warp]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = ((2 * warp) * 32 + lane) * 8, c1 = c0 + 256;
+  float g[16];
+  Vec<__nv_bfloat16, 8>::load(w + c0, g);
+  Vec<__nv_bfloat16, 8>::load(w + c1, g + 8);
+  float dwacc[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) dwacc[k] = 0.f;
+  int parity = 0;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x, parity ^= 1) {
+    const uint4 a0 = *reinterpret_cast<const uint4*>(dy + r * lddy + c0);
+    const uint4 a1 = *reinterpret_cast<const uint4*>(dy + r * lddy + c1);
+    const uint4 b0 = *reinterpret_cast<const uint4*>(x + r * ldx + c0);
+    const uint4 b1 = *reinterpret_cast<const uint4*>(x + r * ldx + c1);
+    uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
+    if (res) {
+      o0 = *reinterpret_cast<const uint4*>(res + r * ldres + c0);
+      o1 = *reinterpret_cast<const uint4*>(res + r * ldres + c1);
+    }
+    const float rr = rstd[r];
+    float fa[16], fb[16];
+    Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&a0), fa);
+    Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&a1), fa + 8);
+    Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&b0), fb);
+    Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&b1), fb + 8);
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sum += (fa[k] * g[k]) * fb[k];
+    sum = warp_sum(sum);
+    if (lane == 0) s_part[parity][warp] = sum;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int v = 0; v < W; ++v) tot += s_part[parity][v];
+    const float cf = tot * rr * rr * rr / (float)H;
+    float fo[16];
+    if (res) {
+      Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&o0), fo);
+      Vec<__nv_bfloat16, 8>::load(reinterpret_cast<const __nv_bfloat16*>(&o1), fo + 8);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) fo[k] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      fo[k] += rr * (fa[k] * g[k]) - fb[k] * cf;
+      dwacc[k] += fa[k] * (fb[k] * rr);
+    }
+    Vec<__nv_bfloat16, 8>::store(dx + r * lddx + c0, fo);
+    Vec<__nv_bfloat16, 8>::store(dx + r * lddx + c1, fo + 8);
+  }
+  if (dw_partial) {
+    Vec<float, 8>::store(dw_partial + (int64_t)blockIdx.x * H + c0, dwacc);
+    Vec<float, 8>::store(dw_partial + (int64_t)blockIdx.x * H + c1, dwacc + 8);
+  }
+}
+
+template <int W>
+int launch_bwd_rowblock(int64_t nblk, int64_t rows, const void* dy, int64_t lddy, const void* x,
+                        int64_t ldx, const void* w, const float* rstd, void* dx, int64_t lddx,
+                        const void* res, int64_t ldres, float* dw_partial, cudaStream_t st) {
+  rmsnorm_bwd_rowblock_kernel<W><<<(unsigned)nblk, W * 32, 0, st>>>(
+      rows, (const __nv_bfloat16*)dy, lddy, (const __nv_bfloat16*)x, ldx,
+      (const __nv_bfloat16*)w, rstd, (__nv_bfloat16*)dx, lddx, (const __nv_bfloat16*)res, ldres,
+      dw_partial);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
 // bf16 backward for rows of H = 256 m <= 4096 columns: one warp per row holds the
 // row's dy and x in registers (16-byte chunks; lane l owns columns 8 (32 i + l) ..
 // + 8 of chunk i), so each is read from HBM once and no second pass touches L2;
@@ -536,7 +624,8 @@ extern "C" int pe_rmsnorm_fwd(int dtype, int64_t rows, int64_t H, const void* x,
 }
 
 extern "C" int64_t pe_rmsnorm_bwd_blocks(int64_t rows) {
-  // persistent tiled backward: about two blocks per SM, one tile of rows at least
+  // persistent backward: two blocks per SM (every kernel below keeps that many
+  // resident, so no block starts after another finished), one tile of rows at least
   const int64_t cap = 2 * (int64_t)sm_count();
   int64_t b = ceil_div(rows, kTileRows);
   return b < 1 ? 1 : (b > cap ? cap : b);
@@ -557,6 +646,18 @@ extern "C" int pe_rmsnorm_bwd(int dtype, int64_t rows, int64_t H, const void* dy
                    (!residual || ldres % 8 == 0) && aligned16(dy) && aligned16(x) &&
                    aligned16(w) && aligned16(dx) && (!residual || aligned16(residual));
   const size_t smem = dw_partial ? (size_t)H * 4 : 0;
+  if (vec && dtype == PE_BF16 && H % 512 == 0 && H <= 4096) {
+    cudaStream_t st = as_stream(stream);
+#define PE_RB(Wn)                                                                            \
+  case Wn:                                                                                   \
+    return launch_bwd_rowblock<Wn>(nblk, rows, dy, lddy, x, ldx, w, rstd, dx, lddx, residual, \
+                                   ldres, dw_partial, st);
+    switch (H / 512) {
+      PE_RB(1) PE_RB(2) PE_RB(3) PE_RB(4) PE_RB(5) PE_RB(6) PE_RB(7) PE_RB(8)
+      default: break;
+    }
+#undef PE_RB
+  }
   if (vec && dtype == PE_BF16 && H % 256 == 0 && H <= 256 * kRowRegChunks) {
     const size_t sm_rr = dw_partial ? (size_t)kRowRegWarps * H * 4 : 0;
     if (sm_rr > 48 * 1024)

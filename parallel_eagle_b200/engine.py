@@ -180,7 +180,10 @@ class StepEngine:
     def _segment_arrays(self, a0: int, a1: int, n: int, prompt_len: int):
         """Slots of one segment (reference ``partition.py:41-55``, ``:101-104``):
         rotary positions, loss-slot indices and their target positions."""
-        k = self.d.max_depth
+        return self._segment_arrays_static(a0, a1, n, self.d.max_depth, prompt_len)
+
+    @staticmethod
+    def _segment_arrays_static(a0: int, a1: int, n: int, k: int, prompt_len: int):
         anchor = np.concatenate([np.arange(a1), np.repeat(np.arange(a0, a1), k - 1)])
         depth = np.concatenate([np.zeros(a1, dtype=np.int64), np.tile(np.arange(1, k), a1 - a0)])
         tgt = anchor + 1 + depth

@@ -526,10 +526,20 @@ def cast_from_f32(x, out):
     return out
 
 
+_SUMSQ_BLOCKS = 1024  # fixed, so the partials (and the sum) do not depend on the device
+
+
 def sumsq_into(g, out):
-    rc = _lib().pe_sumsq(L.dtype_code(g.dtype), g.numel(), g.data_ptr(), out.data_ptr(),
-                         L.stream_ptr(g.device))
-    L.check(rc, "pe_sumsq")
+    """``out[0] += sum(g ** 2)``, deterministic: the same gradient gives the same bits on
+    every run and every data-parallel rank (fixed-grid partials, fixed-order sum)."""
+    lib = _lib()
+    stream = L.stream_ptr(g.device)
+    part = _workspace(g.device, _SUMSQ_BLOCKS * 4, "sumsq").view(torch.float32)[:_SUMSQ_BLOCKS]
+    rc = lib.pe_sumsq_partials(L.dtype_code(g.dtype), g.numel(), g.data_ptr(), part.data_ptr(),
+                               _SUMSQ_BLOCKS, stream)
+    L.check(rc, "pe_sumsq_partials")
+    rc = lib.pe_sum_f32(_SUMSQ_BLOCKS, part.data_ptr(), out.data_ptr(), 1, stream)
+    L.check(rc, "pe_sum_f32")
     return out
 
 

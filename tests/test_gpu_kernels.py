@@ -157,13 +157,17 @@ def test_gemm_rejects_ineligible_tcgen05():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("H,rows", [(64, 37), (3584, 37), (100, 37), (3584, 5003), (4096, 700)])
-def test_rmsnorm_fwd_bwd(dtype, H, rows):
-    # 5003 rows: more row tiles than persistent blocks, ragged last tile
+@pytest.mark.parametrize("H,rows", [(64, 37), (3584, 37), (100, 37), (3584, 5003), (4096, 700),
+                                    (512, 300), (1536, 1000), (5120, 257)])
+@pytest.mark.parametrize("with_res", [True, False])
+def test_rmsnorm_fwd_bwd(dtype, H, rows, with_res):
+    # 5003 rows: more row tiles than persistent blocks, ragged last tile; H = 512 m <= 4096
+    # takes the one-block-per-row bf16 kernel, 5120 the tiled one
     x = _rand(rows, H, dtype=dtype, seed=5) * 3
     w = (1 + 0.1 * _rand(H, dtype=torch.float32, seed=6)).to(dtype)
     dy = _rand(rows, H, dtype=dtype, seed=7)
-    res = _rand(rows, H, dtype=dtype, seed=8)
+    res = _rand(rows, H, dtype=dtype, seed=8) if with_res else torch.zeros(rows, H, dtype=dtype,
+                                                                            device=DEV)
     y, rstd = ops.rmsnorm_fwd(x, w, 1e-5)
     xr = x.float().cpu().requires_grad_(True)
     wr = w.float().cpu().requires_grad_(True)
@@ -171,7 +175,7 @@ def test_rmsnorm_fwd_bwd(dtype, H, rows):
     tol = 1e-6 if dtype == torch.float32 else 1e-2
     assert rel(y.float().cpu(), yr) < tol
     yr.backward(dy.float().cpu())
-    dx, part = ops.rmsnorm_bwd(dy, x, w, rstd, residual=res)
+    dx, part = ops.rmsnorm_bwd(dy, x, w, rstd, residual=res if with_res else None)
     dw = ops.colsum_into(part, torch.zeros(H, dtype=torch.float32, device=DEV), accumulate=False)
     torch.cuda.synchronize()
     assert rel(dx.float().cpu() - res.float().cpu(), xr.grad) < (1e-5 if dtype == torch.float32 else 2e-2)
@@ -626,3 +630,23 @@ def test_adamw_with_clipping_matches_torch():
         ops.adamw_step(p, gd, m, v, ss, 1.0, 1e-2, 0.9, 0.999, 1e-8, 0.1, step)
     torch.cuda.synchronize()
     assert rel(p.cpu(), p_ref.detach()) < 1e-5
+
+
+def test_sumsq_is_deterministic_and_exact():
+    """The global-norm reduction behind the clip (``ops.sumsq_into``): the same gradient
+    gives the same bits on every call -- as every data-parallel rank must, or the
+    replicas' clip coefficients and updates drift apart -- and matches an fp64 sum."""
+    g = _rand(40_000_003, dtype=torch.bfloat16, seed=90, scale=0.01)
+    outs = []
+    for _ in range(3):
+        out = torch.zeros(1, dtype=torch.float32, device=DEV)
+        ops.sumsq_into(g, out)
+        outs.append(out.clone())
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    ref = g.double().pow(2).sum().item()
+    assert abs(outs[0].item() - ref) / ref < 1e-5
+    # accumulates into the existing value
+    acc = torch.full((1,), 2.5, dtype=torch.float32, device=DEV)
+    ops.sumsq_into(g, acc)
+    assert abs(acc.item() - (2.5 + ref)) / ref < 1e-5
