@@ -716,6 +716,9 @@ AB_VARIANTS = {
     "fused_swiglu": {"fuse_swiglu": True},
     "lmhead_256_256": {"lmhead_algo": (1 << 24) | (1 << 26)},
     "lmhead_auto_dh256": {"lmhead_algo": 1 << 26},
+    # one 10240-row group (all loss rows of a config-2 sequence) instead of two of 5120
+    "lmhead_group10240": {"lmhead_algo": 40 << 16},
+    "lmhead_group10240_chunk8k": {"lmhead_algo": (40 << 16) | (8 << 8)},
 }
 
 

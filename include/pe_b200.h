@@ -221,7 +221,7 @@ int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth,
  * Rows with label < 0 are ignored.  No gradient reaches W (frozen).
  * For the bf16 hard-label path, algo bits 8-15 set the vocabulary chunk (units of
  * 1024 rows of W, at most 16) and bits 16-23 the loss-row group (units of 256
- * rows, at most 32); zero keeps the defaults (16384 and 4096).
+ * rows, at most 40); zero keeps the defaults (16384 and 5120).
  * Replaces reference src/pe/partition.py:113-115 (lm_head -> float ->
  * cross_entropy(sum) -> backward) and drafter.py:123-124.
  * ------------------------------------------------------------------------- */

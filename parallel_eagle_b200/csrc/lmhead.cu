@@ -220,13 +220,15 @@ namespace {
 
 constexpr int64_t kFastChunk = 16384;  // vocabulary rows per logits chunk (default)
 // loss rows per group (default).  Groups are equal and a multiple of 128 rows, so the
-// 10240 loss rows of a config-2 sequence run as 2 x 5120: the dH GEMM (N = H = 3584)
-// then fills its CTA-pair grid in 2 whole waves of 512-wide tiles (20 x 7 = 140 of 148
-// tiles) where 3 x 3456 left it 3 waves of 256-wide tiles 88 % full -- measured 5-8 %
-// faster for the whole call although a 5120 x 16384 bf16 chunk no longer fits L2.
-constexpr int64_t kRowGroup = 5120;
+// ~10240 loss rows of a config-2 sequence run as one group: per chunk the logits GEMM
+// has 40 x 32 tiles (17.3 waves of the CTA-pair grid) and the dH GEMM (N = H = 3584)
+// 40 x 7 of 512 wide (3.8 waves), with half as many chunk steps as two groups of 5120
+// (which left the dH GEMM 1.9 waves).  Measured on the config-2 training step
+// (interleaved A/B): 293.4 ms against 294.5 ms for 2 x 5120; 3 x 3456 had been 5-8 %
+// slower than 2 x 5120 for the call alone.
+constexpr int64_t kRowGroup = 10240;
 constexpr int64_t kMaxChunk = 16384;
-constexpr int64_t kMaxGroup = 8192;
+constexpr int64_t kMaxGroup = 10240;
 constexpr int kStatTile = 128;  // columns per (max, sum-exp) pair of the logits GEMM
 static_assert(kMaxChunk / kStatTile <= 128, "combine_kernel folds at most 128 tile stats");
 

@@ -9,7 +9,8 @@ forward  feat RMSNorm -> feat_proj -> [emb | feat] -> in_proj (real slots);
          in_proj([mask_emb; h_shared]) broadcast to the prediction slots;
          per layer: RMSNorm -> fused q/k/v GEMM with RoPE in its epilogue ->
          masked flash attention (mask re-derived from (a0, a1, K)) -> o_proj + residual ->
-         RMSNorm -> fused gate/up GEMM -> SwiGLU -> down_proj + residual;
+         RMSNorm -> fused gate/up GEMM with silu * mul in its epilogue ->
+         down_proj + residual;
          frozen final RMSNorm; loss rows gathered; fused LM head + CE.
 backward the exact reverse, with weight gradients accumulated in place into a
          flat gradient buffer whose slices are the parameters' ``.grad``.
@@ -173,7 +174,7 @@ class StepEngine:
         # RoPE in the q|k|v GEMM epilogue and the attention backward (bf16, head_dim
         # 128); SwiGLU in the gate|up GEMM epilogue; the fused LM head's tuning bits
         self.fuse_rope = True
-        self.fuse_swiglu = False
+        self.fuse_swiglu = True
         self.lmhead_algo = 0
 
     # --------------------------------------------------------------- plans --
