@@ -811,7 +811,11 @@ def run_kernel(args):
         for bn in (0, 256, 512):
             runs[f"fused_bn{bn or 'auto'}"] = (
                 lambda bn=bn: ops.linear_swiglu(x, w, I, gu=gu, act=act, algo=bn << 8))
-        for name, ms in time_variants(runs, args.steps, warmup=args.warmup).items():
+        only = set(args.only.split(",")) if args.only else None
+        if only is not None:
+            runs = {k: v for k, v in runs.items() if k in only}
+        for name, ms in time_variants(runs, args.steps, warmup=args.warmup,
+                                      rounds=args.ab_rounds).items():
             out[name] = {"ms": round(ms, 4), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
         # the q|k|v projection of the same pass: GEMM + rotation kernel vs RoPE epilogue
         nh, nkv, hd = c["n_heads"], c["n_kv_heads"], c["hidden"] // c["n_heads"]
@@ -825,7 +829,10 @@ def run_kernel(args):
                  "qkv_gemm_only": lambda: ops.linear(x, wq, out=qkv),
                  "qkv_gemm_only_evict_first": lambda: ops.linear(x, wq, out=qkv, algo=1 << 22),
                  "qkv_fused_rope": lambda: ops.linear_rope(x, wq, cs, (nh + nkv) * hd, hd, out=qkv)}
-        for name, ms in time_variants(qruns, args.steps, warmup=args.warmup).items():
+        if only is not None:
+            qruns = {k: v for k, v in qruns.items() if k in only}
+        for name, ms in time_variants(qruns, args.steps, warmup=args.warmup,
+                                      rounds=args.ab_rounds).items():
             out[name] = {"ms": round(ms, 4), "tflops": round(qflops / (ms / 1e3) / 1e12, 1)}
         ops.check_status(dev)
         print(json.dumps({"kernel": "gate|up + swiglu; q|k|v + rope", "M": M, "N": 2 * I, "K": H,
@@ -1035,7 +1042,10 @@ def main(argv=None):
     ap.add_argument("--ab", default=None,
                     help="comma-separated engine variants to A/B at step level (" +
                     ", ".join(AB_VARIANTS) + ")")
-    ap.add_argument("--ab-rounds", type=int, default=4)
+    ap.add_argument("--ab-rounds", type=int, default=4,
+                    help="interleaved rounds of --ab and of the --kernel swiglu comparison")
+    ap.add_argument("--only", default=None,
+                    help="--kernel swiglu: comma-separated subset of its variants")
     ap.add_argument("--draft", action="store_true",
                     help="time the draft path (draft_logits / propose_tree) on config-2 dims")
     args = ap.parse_args(argv)

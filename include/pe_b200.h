@@ -27,6 +27,7 @@ extern "C" {
 /* dtype codes */
 #define PE_F32 0
 #define PE_BF16 1
+#define PE_F16 2 /* source features only (pe_feature_norm_*): cached shards are fp16 */
 
 /* error codes */
 #define PE_OK 0
@@ -77,6 +78,23 @@ int pe_rmsnorm_bwd_noalloc(int dtype, int64_t rows, int64_t H, const void* dy, i
                            const void* x, int64_t ldx, const void* w, const float* rstd,
                            void* dx, int64_t lddx, const void* residual, int64_t ldres,
                            void* dw, int accumulate, void* stream);
+/* Feature ingestion fused with the feature RMSNorm (reference src/pe/drafter.py:129-130:
+ * features.to(dtype), viewed as [n, nfl, H], RMSNorm with one shared weight).  Output row
+ * o = t * nfl + b (t < tokens, b < nfl) normalises block b of source row src_tok[t] (row
+ * t when src_tok is NULL) of x (x_dtype: PE_F16, PE_BF16 or PE_F32, row stride ldx),
+ * each element first rounded to dtype as the reference's cast rounds it; rstd[o] is
+ * written.  H a multiple of 256 up to 8192, 16-byte aligned rows.  The step feeds every
+ * stacked segment the real prefix rows this way, with no cast or gathered copy of the
+ * shard.  pe_feature_norm_dw adds the weight gradient only (features take no gradient):
+ * dw_partial[nblk, H] (nblk = pe_rmsnorm_bwd_blocks(tokens * nfl), reduce with
+ * pe_colsum_f32) of sum_o dy[o] * x[o] * rstd[o], x read through the same map. */
+int pe_feature_norm_fwd(int x_dtype, int dtype, int64_t tokens, int nfl, int64_t H,
+                        const void* x, int64_t ldx, const int64_t* src_tok, const void* w,
+                        void* y, int64_t ldy, float* rstd, float eps, void* stream);
+int pe_feature_norm_dw(int x_dtype, int dtype, int64_t tokens, int nfl, int64_t H,
+                       const void* dy, int64_t lddy, const void* x, int64_t ldx,
+                       const int64_t* src_tok, const float* rstd, float* dw_partial,
+                       void* stream);
 /* dw (dtype) = (accumulate ? dw : 0) + sum over nblk partial rows */
 int pe_colsum_f32(int dtype, int64_t nblk, int64_t H, const float* partial, void* dw,
                   int accumulate, void* stream);

@@ -14,7 +14,7 @@ import torch
 
 LIB_PATH = Path(__file__).resolve().parent / "libpe_b200.so"
 
-F32, BF16 = 0, 1
+F32, BF16, F16 = 0, 1, 2
 ALGO_AUTO, ALGO_SIMT, ALGO_TCGEN05 = 0, 1, 2
 LAYOUT_PARTITION, LAYOUT_INDEXED, LAYOUT_BIAS = 0, 1, 2
 
@@ -35,6 +35,12 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_int, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _int, _vp]
     ),
     "pe_colsum_f32": (_int, [_int, _i64, _i64, _vp, _vp, _int, _vp]),
+    "pe_feature_norm_fwd": (
+        _int, [_int, _int, _i64, _int, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _f32, _vp]
+    ),
+    "pe_feature_norm_dw": (
+        _int, [_int, _int, _i64, _int, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp]
+    ),
     "pe_rope": (_int, [_int, _i64, _int, _int, _vp, _i64, _vp, _f32, _int, _vp]),
     "pe_rope_table": (_int, [_int, _i64, _int, _vp, _f32, _vp, _i64, _vp]),
     "pe_linear_swiglu": (

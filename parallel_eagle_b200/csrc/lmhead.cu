@@ -298,6 +298,17 @@ combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __res
   const int64_t r = blockIdx.x;
   const int64_t lab = labels[r];
   __nv_bfloat16* z = Z + r * ldz;
+  // every thread's share of the row (at most kMaxChunk / (256 * 8) = 8 chunks of 16 B)
+  // is loaded before the stats fold, so all of a row's loads are in flight together:
+  // a load-exp-store loop over a row rewritten in place cannot hoist a load above the
+  // previous store, and paid one DRAM round trip per chunk
+  constexpr int kPer = (int)(kMaxChunk / (256 * 8));
+  uint4 buf[kPer];
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+    if (c < vc) buf[q] = *reinterpret_cast<const uint4*>(z + c);
+  }
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     const float2* st = stats + r * stats_ld;
@@ -329,17 +340,21 @@ combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __res
   __syncthreads();
   const float mn = s_mnew;
   const bool ignored = lab < 0;
-  for (int64_t c = (int64_t)threadIdx.x * 8; c < vc; c += 256 * 8) {
-    uint4 u = *reinterpret_cast<const uint4*>(z + c);
-    __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float2 f = __bfloat1622float2(h2[i]);
-      f.x = ignored ? 0.f : __expf(f.x - mn);
-      f.y = ignored ? 0.f : __expf(f.y - mn);
-      h2[i] = __floats2bfloat162_rn(f.x, f.y);
+  for (int q = 0; q < kPer; ++q) {
+    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+    if (c < vc) {
+      uint4 u = buf[q];
+      __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f = __bfloat1622float2(h2[i]);
+        f.x = ignored ? 0.f : __expf(f.x - mn);
+        f.y = ignored ? 0.f : __expf(f.y - mn);
+        h2[i] = __floats2bfloat162_rn(f.x, f.y);
+      }
+      *reinterpret_cast<uint4*>(z + c) = u;
     }
-    *reinterpret_cast<uint4*>(z + c) = u;
   }
 }
 
@@ -544,6 +559,20 @@ combine_soft_kernel(int64_t vc, int nt, int stats_ld, const float2* __restrict__
   __shared__ float s_red[8];
   const int64_t r = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __nv_bfloat16* zs = Zs + r * ldz;
+  __nv_bfloat16* zt = Zt + r * ldz;
+  // the thread's share of both rows is loaded before the stats folds (all loads of the
+  // rows in flight together; see combine_kernel)
+  constexpr int kPer = (int)(kMaxChunk / (256 * 8));
+  uint4 bs[kPer], bt[kPer];
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+    if (c < vc) {
+      bs[q] = *reinterpret_cast<const uint4*>(zs + c);
+      bt[q] = *reinterpret_cast<const uint4*>(zt + c);
+    }
+  }
   if (warp == 0) {
     const float ms = fold_stats(stats_s + r * stats_ld, nt, m + r, l + r, alpha + r, lane);
     if (lane == 0) s_m[0] = ms;
@@ -553,12 +582,13 @@ combine_soft_kernel(int64_t vc, int nt, int stats_ld, const float2* __restrict__
   }
   __syncthreads();
   const float ms = s_m[0], mtn = s_m[1];
-  __nv_bfloat16* zs = Zs + r * ldz;
-  __nv_bfloat16* zt = Zt + r * ldz;
   float acc = 0.f;
-  for (int64_t c = (int64_t)threadIdx.x * 8; c < vc; c += 256 * 8) {
-    uint4 us = *reinterpret_cast<const uint4*>(zs + c);
-    uint4 ut = *reinterpret_cast<const uint4*>(zt + c);
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+    if (c >= vc) continue;
+    uint4 us = bs[q];
+    uint4 ut = bt[q];
     __nv_bfloat162* hs = reinterpret_cast<__nv_bfloat162*>(&us);
     __nv_bfloat162* ht = reinterpret_cast<__nv_bfloat162*>(&ut);
 #pragma unroll

@@ -261,7 +261,11 @@ class StepEngine:
         dev = self.flat.device
         dt = self.flat.dtype
         input_ids = input_ids.to(dev, non_blocking=True)
-        features = features.to(dev, non_blocking=True).to(dt)
+        # features keep their cached dtype (fp16 shards) until the feature-norm kernel
+        # reads and rounds them (reference drafter.py:129 casts first)
+        features = features.to(dev, non_blocking=True)
+        if not ops.feature_norm_ok(features, d.hidden, d.num_feature_layers):
+            features = features.to(dt)
         if teacher_labels is not None:
             teacher_labels = teacher_labels.to(dev, non_blocking=True)
         if teacher_hidden is not None:
@@ -343,14 +347,22 @@ class StepEngine:
         # real rows of every segment: [embedding | feat_proj(RMSNorm(features))] -> in_proj
         x = torch.empty(Q, H, dtype=dt, device=dev)
         u = torch.empty(Rt, 2 * H, dtype=dt, device=dev)
+        fused_fnorm = ops.feature_norm_ok(feats, H, nfl)
+        src_tok = None if single else plan.real_tok
         if single:
             a1 = plan.segs[0][1]
             ops.embed_rows(ids[:a1], E, u[:, :H])
-            f_in = feats[:a1].reshape(a1 * nfl, H)
         else:
             ops.embed_rows(ids.index_select(0, plan.real_tok), E, u[:, :H])
-            f_in = ops.gather_rows(feats, plan.real_tok).view(Rt * nfl, H)
-        fn, rstd_f = ops.rmsnorm_fwd(f_in, W("feat_norm.weight"), eps)
+        if fused_fnorm:
+            # every stacked segment's real prefix rows normalised straight from the shard
+            fn, rstd_f = ops.feature_norm_fwd(feats, W("feat_norm.weight"), nfl, H, dt, eps,
+                                              src_tok=src_tok, tokens=Rt)
+            f_in = None
+        else:
+            f_in = (feats[:plan.segs[0][1]].reshape(Rt * nfl, H) if single
+                    else ops.gather_rows(feats, plan.real_tok).view(Rt * nfl, H))
+            fn, rstd_f = ops.rmsnorm_fwd(f_in, W("feat_norm.weight"), eps)
         w_fp = W("feat_proj.weight", (H, nfl * H))
         w_in = W("in_proj.weight", (H, 2 * H))
         ops.linear(fn.view(Rt, nfl * H), w_fp, out=u[:, H:])
@@ -471,7 +483,11 @@ class StepEngine:
         dfn = ops.linear_dgrad(dfeat, w_fp)
         ops.linear_wgrad(dfeat, fn.view(Rt, nfl * H), grad=G("feat_proj.weight", (H, nfl * H)),
                          accumulate=True)
-        _, part = ops.rmsnorm_bwd(dfn.view(Rt * nfl, H), f_in, W("feat_norm.weight"), rstd_f)
+        if fused_fnorm:
+            part = ops.feature_norm_dw(dfn.view(Rt * nfl, H), feats, rstd_f, nfl, H,
+                                       src_tok=src_tok)
+        else:
+            _, part = ops.rmsnorm_bwd(dfn.view(Rt * nfl, H), f_in, W("feat_norm.weight"), rstd_f)
         ops.colsum_into(part, G("feat_norm.weight"), accumulate=True)
 
 

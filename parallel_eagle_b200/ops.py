@@ -97,6 +97,51 @@ def colsum_into(partial: torch.Tensor, out: torch.Tensor, accumulate: bool) -> t
     return out
 
 
+_SRC_CODES = {torch.float32: L.F32, torch.bfloat16: L.BF16, torch.float16: L.F16}
+
+
+def feature_norm_ok(x: torch.Tensor, hidden: int, nfl: int) -> bool:
+    """Whether :func:`feature_norm_fwd` takes this feature tensor directly."""
+    return (x.is_cuda and x.dtype in _SRC_CODES and x.dim() == 2 and x.stride(1) == 1
+            and x.shape[1] == nfl * hidden and hidden % 256 == 0 and hidden <= 8192
+            and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0)
+
+
+def feature_norm_fwd(x, w, nfl: int, hidden: int, dtype, eps: float, src_tok=None, tokens=None):
+    """RMSNorm of the ``hidden``-wide blocks of feature rows read straight from ``x`` (fp16,
+    bf16 or fp32; row ``src_tok[t]`` for output token ``t``), each element rounded to
+    ``dtype`` first (the reference's ``features.to(dtype)``): returns ``y``
+    ``[tokens * nfl, hidden]`` in ``dtype`` and ``rstd``."""
+    L.require_cuda(x, w)
+    tokens = int(x.shape[0] if tokens is None else tokens)
+    y = torch.empty(tokens * nfl, hidden, dtype=dtype, device=x.device)
+    rstd = torch.empty(tokens * nfl, dtype=torch.float32, device=x.device)
+    rc = _lib().pe_feature_norm_fwd(
+        _SRC_CODES[x.dtype], L.dtype_code(dtype), tokens, nfl, hidden, x.data_ptr(), x.stride(0),
+        L.ptr(src_tok), w.data_ptr(), y.data_ptr(), hidden, rstd.data_ptr(), float(eps),
+        L.stream_ptr(x.device),
+    )
+    L.check(rc, "pe_feature_norm_fwd")
+    return y, rstd
+
+
+def feature_norm_dw(dy, x, rstd, nfl: int, hidden: int, src_tok=None):
+    """Weight-gradient partials of :func:`feature_norm_fwd` (``[nblk, hidden]`` fp32, reduce
+    with :func:`colsum_into`); ``dy`` ``[tokens * nfl, hidden]``."""
+    L.require_cuda(dy, x, rstd)
+    rows = dy.shape[0]
+    lib = _lib()
+    nblk = int(lib.pe_rmsnorm_bwd_blocks(rows))
+    part = torch.empty(nblk, hidden, dtype=torch.float32, device=dy.device)
+    rc = lib.pe_feature_norm_dw(
+        _SRC_CODES[x.dtype], L.dtype_code(dy.dtype), rows // nfl, nfl, hidden, dy.data_ptr(),
+        _row_stride(dy), x.data_ptr(), x.stride(0), L.ptr(src_tok), rstd.data_ptr(),
+        part.data_ptr(), L.stream_ptr(dy.device),
+    )
+    L.check(rc, "pe_feature_norm_dw")
+    return part
+
+
 # ------------------------------------------------------------------ rope ----
 
 

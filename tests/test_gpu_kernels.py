@@ -650,3 +650,36 @@ def test_sumsq_is_deterministic_and_exact():
     acc = torch.full((1,), 2.5, dtype=torch.float32, device=DEV)
     ops.sumsq_into(g, acc)
     assert abs(acc.item() - (2.5 + ref)) / ref < 1e-5
+
+
+@pytest.mark.parametrize("src_dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("H,n,mapped", [(256, 50, False), (3584, 300, True), (512, 97, True)])
+def test_feature_norm_matches_cast_gather_rmsnorm(src_dtype, dtype, H, n, mapped):
+    """The fused ingestion norm (reference drafter.py:129-130) against the unfused
+    sequence -- cast the shard to the run dtype, gather the mapped token rows, RMSNorm
+    the H-wide blocks -- bit for bit in the forward, and its weight gradient against
+    the RMSNorm backward's dW partials."""
+    nfl = 3
+    g = torch.Generator().manual_seed(H + n)
+    feats = (torch.randn(n, nfl * H, generator=g) * 2).to(src_dtype).to(DEV)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).to(dtype).to(DEV)
+    if mapped:  # a stacked pass's real rows: prefixes of two segments
+        tok = torch.cat([torch.arange(n // 2), torch.arange(n)]).to(DEV)
+    else:
+        tok = None
+    T = n + n // 2 if mapped else n
+    y, rstd = ops.feature_norm_fwd(feats, w, nfl, H, dtype, 1e-5, src_tok=tok, tokens=T)
+    src = feats.to(dtype)
+    rows = ops.gather_rows(src, tok) if mapped else src
+    ref, ref_rstd = ops.rmsnorm_fwd(rows.reshape(T * nfl, H), w, 1e-5)
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)
+    assert torch.allclose(rstd, ref_rstd, rtol=1e-6, atol=0)
+    dy = (torch.randn(T * nfl, H, generator=g)).to(dtype).to(DEV)
+    part = ops.feature_norm_dw(dy, feats, rstd, nfl, H, src_tok=tok)
+    dw = ops.colsum_into(part, torch.zeros(H, dtype=torch.float32, device=DEV), accumulate=False)
+    _, rpart = ops.rmsnorm_bwd(dy, rows.reshape(T * nfl, H), w, ref_rstd)
+    rdw = ops.colsum_into(rpart, torch.zeros(H, dtype=torch.float32, device=DEV), accumulate=False)
+    torch.cuda.synchronize()
+    assert rel(dw.cpu(), rdw.cpu()) < 1e-5
