@@ -658,8 +658,10 @@ def test_sumsq_is_deterministic_and_exact():
 def test_feature_norm_matches_cast_gather_rmsnorm(src_dtype, dtype, H, n, mapped):
     """The fused ingestion norm (reference drafter.py:129-130) against the unfused
     sequence -- cast the shard to the run dtype, gather the mapped token rows, RMSNorm
-    the H-wide blocks -- bit for bit in the forward, and its weight gradient against
-    the RMSNorm backward's dW partials."""
+    the H-wide blocks -- and its weight gradient against the RMSNorm backward's dW.
+    The row's sum of squares is reduced in a different order (8 columns per thread
+    across the block, against strided 16-byte chunks in one warp), so rstd agrees to
+    fp32 rounding and y to one unit of the output dtype's last place."""
     nfl = 3
     g = torch.Generator().manual_seed(H + n)
     feats = (torch.randn(n, nfl * H, generator=g) * 2).to(src_dtype).to(DEV)
@@ -674,8 +676,11 @@ def test_feature_norm_matches_cast_gather_rmsnorm(src_dtype, dtype, H, n, mapped
     rows = ops.gather_rows(src, tok) if mapped else src
     ref, ref_rstd = ops.rmsnorm_fwd(rows.reshape(T * nfl, H), w, 1e-5)
     torch.cuda.synchronize()
-    assert torch.equal(y, ref)
-    assert torch.allclose(rstd, ref_rstd, rtol=1e-6, atol=0)
+    assert torch.allclose(rstd, ref_rstd, rtol=2e-6, atol=0)
+    ulp = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -22
+    diff = (y.float() - ref.float()).abs()
+    assert torch.all(diff <= ulp * ref.float().abs().clamp_min(1e-30)), diff.max()
+    assert (diff > 0).float().mean().item() < 0.02  # only rare rounding flips
     dy = (torch.randn(T * nfl, H, generator=g)).to(dtype).to(DEV)
     part = ops.feature_norm_dw(dy, feats, rstd, nfl, H, src_tok=tok)
     dw = ops.colsum_into(part, torch.zeros(H, dtype=torch.float32, device=DEV), accumulate=False)
