@@ -713,12 +713,15 @@ AB_VARIANTS = {
     # name -> StepEngine kernel choices (every variant computes the same result)
     "default": {},
     "unfused_rope": {"fuse_rope": False},
-    "fused_swiglu": {"fuse_swiglu": True},
+    "unfused_swiglu": {"fuse_swiglu": False},
     "lmhead_256_256": {"lmhead_algo": (1 << 24) | (1 << 26)},
     "lmhead_auto_dh256": {"lmhead_algo": 1 << 26},
-    # one 10240-row group (all loss rows of a config-2 sequence) instead of two of 5120
-    "lmhead_group10240": {"lmhead_algo": 40 << 16},
-    "lmhead_group10240_chunk8k": {"lmhead_algo": (40 << 16) | (8 << 8)},
+    # two 5120-row groups instead of one of 10240 (all loss rows of a config-2 sequence)
+    "lmhead_group5120": {"lmhead_algo": 20 << 16},
+    "lmhead_chunk8k": {"lmhead_algo": 8 << 8},
+    # 24K / 32K-column vocabulary chunks: fewer fp32 dH read-modify-write passes
+    "lmhead_chunk24k": {"lmhead_algo": 24 << 8},
+    "lmhead_chunk32k": {"lmhead_algo": 32 << 8},
 }
 
 

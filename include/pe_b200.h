@@ -237,9 +237,11 @@ int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth,
  *   (or, with teacher rows t_r: loss_r = -sum_v softmax(t_r W^T)_v log_softmax(z_r)_v)
  *   loss_sum[0] += sum_r loss_r;  dh = grad_scale * d(sum_r loss_r)/dh
  * Rows with label < 0 are ignored.  No gradient reaches W (frozen).
- * For the bf16 hard-label path, algo bits 8-15 set the vocabulary chunk (units of
- * 1024 rows of W, at most 16) and bits 16-23 the loss-row group (units of 256
- * rows, at most 40); zero keeps the defaults (16384 and 5120).
+ * For the bf16 paths, algo bits 8-15 set the vocabulary chunk (units of 1024 rows
+ * of W, at most 32 with hard labels and 16 with teacher rows) and bits 16-23 the
+ * loss-row group (units of 256 rows, at most 40); zero keeps the defaults (16384
+ * and 10240).  Bits 24-25 / 26-27 pick the logits / dH GEMM tile width (1: 256,
+ * 2: 512, 0: automatic).
  * Replaces reference src/pe/partition.py:113-115 (lm_head -> float ->
  * cross_entropy(sum) -> backward) and drafter.py:123-124.
  * ------------------------------------------------------------------------- */

@@ -227,10 +227,12 @@ constexpr int64_t kFastChunk = 16384;  // vocabulary rows per logits chunk (defa
 // (interleaved A/B): 293.4 ms against 294.5 ms for 2 x 5120; 3 x 3456 had been 5-8 %
 // slower than 2 x 5120 for the call alone.
 constexpr int64_t kRowGroup = 10240;
-constexpr int64_t kMaxChunk = 16384;
+constexpr int64_t kMaxChunk = 32768;      // hard-label path
+constexpr int64_t kMaxChunkSoft = 16384;  // soft-target path (two logits chunks per step)
 constexpr int64_t kMaxGroup = 10240;
 constexpr int kStatTile = 128;  // columns per (max, sum-exp) pair of the logits GEMM
-static_assert(kMaxChunk / kStatTile <= 128, "combine_kernel folds at most 128 tile stats");
+static_assert(kMaxChunk <= 16 * 256 * 8, "combine_kernel<16> covers at most 32K columns");
+static_assert(kMaxChunkSoft / kStatTile <= 128, "fold_stats folds at most 128 tile stats");
 
 // Rows of the loss are processed in groups, which bounds the logits chunk (group x
 // chunk bf16) held between the logits GEMM, the combine pass and the dH GEMM.  ``algo`` bits 8-15 override the chunk (units of
@@ -241,10 +243,10 @@ struct FastPlan {
 };
 
 // algo bits 24-25 / 26-27: logits / dH GEMM pair tile width (1: 256, 2: 512, 0: automatic)
-FastPlan fast_plan_of(int64_t R, int64_t V, int algo) {
+FastPlan fast_plan_of(int64_t R, int64_t V, int algo, int64_t max_chunk) {
   int64_t vc = ((algo >> 8) & 0xff) ? ((algo >> 8) & 0xff) * 1024 : kFastChunk;
   int64_t rg = ((algo >> 16) & 0xff) ? ((algo >> 16) & 0xff) * 256 : kRowGroup;
-  vc = vc > kMaxChunk ? kMaxChunk : vc;
+  vc = vc > max_chunk ? max_chunk : vc;
   rg = rg > kMaxGroup ? kMaxGroup : rg;
   if (V < vc) vc = (V + 7) / 8 * 8;
   if (R <= rg) {
@@ -289,7 +291,8 @@ FastLayout fast_layout_of(int64_t R, int64_t H, int64_t V) {
 
 // per row: fold this chunk's tile stats into (m, l), record the rescale factor,
 // pick the label logit, and overwrite the chunk's logits with exp(z - m_new).
-// Warp 0 folds the (at most 64) tile stats two per lane.
+// Warp 0 folds the (at most 256) tile stats, lane l taking tiles l, l + 32, ...
+template <int kPer>  // 16-byte loads per thread: vc <= kPer * 256 * 8
 __global__ void __launch_bounds__(256)
 combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __restrict__ stats,
                __nv_bfloat16* __restrict__ Z, int64_t ldz, const int64_t* __restrict__ labels,
@@ -298,11 +301,10 @@ combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __res
   const int64_t r = blockIdx.x;
   const int64_t lab = labels[r];
   __nv_bfloat16* z = Z + r * ldz;
-  // every thread's share of the row (at most kMaxChunk / (256 * 8) = 8 chunks of 16 B)
-  // is loaded before the stats fold, so all of a row's loads are in flight together:
-  // a load-exp-store loop over a row rewritten in place cannot hoist a load above the
-  // previous store, and paid one DRAM round trip per chunk
-  constexpr int kPer = (int)(kMaxChunk / (256 * 8));
+  // every thread's share of the row (kPer pieces of 16 B) is loaded before the stats
+  // fold, so all of a row's loads are in flight together: a load-exp-store loop over a
+  // row rewritten in place cannot hoist a load above the previous store, and paid one
+  // DRAM round trip per piece
   uint4 buf[kPer];
 #pragma unroll
   for (int q = 0; q < kPer; ++q) {
@@ -313,11 +315,12 @@ combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __res
     const int lane = threadIdx.x;
     const float2* st = stats + r * stats_ld;
     const float m_old = m[r];
-    // nt <= 128 (kMaxChunk / kStatTile): lane takes tiles lane, lane + 32, ...
-    float2 sv[4];
+    // nt <= kPer * 2048 / kStatTile: lane takes tiles lane, lane + 32, ...
+    constexpr int kSv = kPer * 2048 / kStatTile / 32;
+    float2 sv[kSv];
     float lm = -INFINITY;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < kSv; ++q) {
       const int t = lane + 32 * q;
       sv[q] = t < nt ? st[t] : make_float2(-INFINITY, 0.f);
       lm = fmaxf(lm, sv[q].x);
@@ -325,7 +328,7 @@ combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __res
     const float mn = fmaxf(m_old, warp_max(lm));
     float part = 0.f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
+    for (int q = 0; q < kSv; ++q)
       if (sv[q].x != -INFINITY) part += sv[q].y * expf(sv[q].x - mn);
     const float tile_sum = warp_sum(part);
     if (lane == 0) {
@@ -413,7 +416,7 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
                 const int64_t* labels, float grad_scale, void* dh, int64_t lddh, float* loss_sum,
                 uint8_t* ws, int algo, int* status, cudaStream_t st) {
   const FastLayout L = fast_layout_of(R, H, V);
-  const FastPlan P = fast_plan_of(R, V, algo);
+  const FastPlan P = fast_plan_of(R, V, algo, kMaxChunk);
   float* m = (float*)(ws + L.m);
   float* l = (float*)(ws + L.l);
   float* zlab = (float*)(ws + L.zlab);
@@ -452,9 +455,11 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
       if (rc) return rc;
       PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
       PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
-      combine_kernel<<<(unsigned)rg, 256, 0, side>>>(vc, v0, nt, nt_max, stats[b], Z[b], VC,
-                                                     labels + r0, m + r0, l + r0, zlab + r0,
-                                                     alpha + r0);
+      // 8 loads of 16 B per thread cover chunks up to 16K columns, 16 up to 32K (a
+      // single width would hold 16 in registers and halve the blocks per SM)
+      auto combine = vc <= 16384 ? combine_kernel<8> : combine_kernel<16>;
+      combine<<<(unsigned)rg, 256, 0, side>>>(vc, v0, nt, nt_max, stats[b], Z[b], VC,
+                                              labels + r0, m + r0, l + r0, zlab + r0, alpha + r0);
       PE_LAUNCHED();
       rc = gemm_tc_rowscale_acc(rg, H, vc, Z[b], VC, Wc, H, dHg, H, v0 > 0 ? dHg : nullptr,
                                 alpha + r0, status, side, P.dh_bn);
@@ -490,7 +495,7 @@ struct SoftLayout {
 };
 
 SoftLayout soft_layout_of(int64_t R, int64_t H, int64_t V) {
-  const int64_t vc = V < kMaxChunk ? (V + 7) / 8 * 8 : kMaxChunk;
+  const int64_t vc = V < kMaxChunkSoft ? (V + 7) / 8 * 8 : kMaxChunkSoft;
   const int64_t rg = R < kMaxGroup ? R : kMaxGroup;
   const int64_t nt = (vc + kStatTile - 1) / kStatTile;
   SoftLayout L{};
@@ -563,7 +568,7 @@ combine_soft_kernel(int64_t vc, int nt, int stats_ld, const float2* __restrict__
   __nv_bfloat16* zt = Zt + r * ldz;
   // the thread's share of both rows is loaded before the stats folds (all loads of the
   // rows in flight together; see combine_kernel)
-  constexpr int kPer = (int)(kMaxChunk / (256 * 8));
+  constexpr int kPer = (int)(kMaxChunkSoft / (256 * 8));
   uint4 bs[kPer], bt[kPer];
 #pragma unroll
   for (int q = 0; q < kPer; ++q) {
@@ -657,7 +662,7 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
                      const void* teacher, int64_t ldt, float grad_scale, void* dh, int64_t lddh,
                      float* loss_sum, uint8_t* ws, int algo, int* status, cudaStream_t st) {
   const SoftLayout L = soft_layout_of(R, H, V);
-  const FastPlan P = fast_plan_of(R, V, algo);
+  const FastPlan P = fast_plan_of(R, V, algo, kMaxChunkSoft);
   float* m = (float*)(ws + L.m);
   float* l = (float*)(ws + L.l);
   float* zlab = (float*)(ws + L.zlab);

@@ -498,16 +498,20 @@ def test_lmhead_ce(dtype, soft, R, H, V):
     assert rel(dh.float().cpu(), hr.grad) < (1e-4 if dtype == torch.float32 else 2e-2)
 
 
-def test_lmhead_ce_full_vocab_against_torch():
+@pytest.mark.parametrize("chunk_k", [0, 24, 32])
+def test_lmhead_ce_full_vocab_against_torch(chunk_k):
     # the 7B-class head (vocab 152064) over a segment's worth of loss rows: the
-    # fused one-GEMM path against torch's dense logits -> cross-entropy -> backward
+    # fused one-GEMM path against torch's dense logits -> cross-entropy -> backward,
+    # with the default 16K-column vocabulary chunks and with 24K / 32K ones (up to
+    # 256 tile stats folded per row and chunk)
     R, H, V = 1100, 3584, 152064
     h = _rand(R, H, seed=40)
     W = _rand(V, H, seed=41, scale=0.02)
     labels = torch.randint(0, V, (R,), generator=torch.Generator().manual_seed(5)).to(DEV)
     loss = torch.zeros(1, dtype=torch.float32, device=DEV)
     scale = 1.0 / 3000
-    dh = ops.lmhead_ce(h, W, labels, scale, loss)
+    dh = ops.lmhead_ce(h, W, labels, scale, loss, algo=L.ALGO_AUTO | (chunk_k << 8))
+    ops.check_status(DEV)
     hr = h.detach().clone().requires_grad_(True)
     z = (hr @ W.t()).float()
     lr = torch.nn.functional.cross_entropy(z, labels, reduction="sum")
