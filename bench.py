@@ -714,6 +714,7 @@ AB_VARIANTS = {
     "default": {},
     "unfused_rope": {"fuse_rope": False},
     "unfused_swiglu": {"fuse_swiglu": False},
+    "fused_swiglu_bwd": {"fuse_swiglu_bwd": True},
     "lmhead_256_256": {"lmhead_algo": (1 << 24) | (1 << 26)},
     "lmhead_auto_dh256": {"lmhead_algo": 1 << 26},
     # two 5120-row groups instead of one of 10240 (all loss rows of a config-2 sequence)
@@ -748,7 +749,8 @@ def run_ab(args):
         teachers = torch.randn(B, n, c["hidden"], generator=g, device=dev).to(torch.bfloat16)
     names = [v for v in args.ab.split(",") if v]
     eng = trainer.eng
-    defaults = {key: getattr(eng, key) for key in ("fuse_rope", "fuse_swiglu", "lmhead_algo")}
+    defaults = {key: getattr(eng, key)
+                for key in ("fuse_rope", "fuse_swiglu", "fuse_swiglu_bwd", "lmhead_algo")}
 
     def use(name):
         for key, val in defaults.items():

@@ -158,6 +158,21 @@ int pe_linear_swiglu(int dtype, int64_t M, int64_t I, int64_t K, const void* x, 
                      const void* w_gu, int64_t ldw, void* gu, int64_t ldgu, void* act,
                      int64_t lda, int algo, int32_t* status, void* stream);
 
+/* The SwiGLU MLP's backward through the activation: d act = dy w (dy [M, K] the
+ * down projection's output gradient, w = down_proj.weight [K, I], row stride ldw)
+ * and dgu = swiglu_backward(d act, gu) ([M, 2I]: d gate | d up, with gu the
+ * forward's gate | up rows), each rounded as pe_gemm then pe_swiglu_bwd would
+ * round them (bit-identical).  Replaces the backward of reference
+ * src/pe/nn.py:99-100 (down_proj input gradient, then silu(gate) * up).  On the
+ * bf16 tensor-core path with CTA-pair tiles (M >= 512, I a multiple of 32, 16-byte
+ * aligned rows) the SwiGLU backward runs in the GEMM epilogue and d act is never
+ * stored; otherwise the GEMM writes d act into dgu's up half and pe_swiglu_bwd
+ * rewrites dgu in place.  dgu must not alias gu.  algo bits 8-17 may force the pair
+ * tile width (256 or 512). */
+int pe_linear_swiglu_bwd(int dtype, int64_t M, int64_t I, int64_t K, const void* dy,
+                         int64_t lddy, const void* w, int64_t ldw, const void* gu, int64_t ldgu,
+                         void* dgu, int64_t lddgu, int algo, int32_t* status, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Cross-depth masked attention (GQA, scale = 1/sqrt(head_dim)), flash-style:
  * no score matrix is materialised.  q/k/v/o rows are slots, heads are

@@ -46,6 +46,9 @@ SIGNATURES: dict[str, tuple] = {
     "pe_linear_swiglu": (
         _int, [_int, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _vp]
     ),
+    "pe_linear_swiglu_bwd": (
+        _int, [_int, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _int, _vp, _vp]
+    ),
     "pe_linear_rope": (
         _int, [_int, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _int,
                _vp, _vp]

@@ -34,6 +34,7 @@ enum : int {
   EPI_ROWSCALE = 2,  // C = alpha * acc + rowscale[row] * Cin
   EPI_ROPE = 3,      // C = rotate(round(alpha * acc)) on 128-wide heads below rot_cols
   EPI_SWIGLU = 4,    // gate|up tile pairs: C[:, j], C[:, I + j] = g, u; act[:, j] = silu(g) u
+  EPI_SWIGLU_BWD = 5,  // acc = d act[:, j]: C[:, j], C[:, I + j] = d gate, d up (gate|up read)
 };
 struct EpiArgs {
   float2* stats;
@@ -53,6 +54,10 @@ struct EpiArgs {
   int64_t swiglu_i = 0;
   __nv_bfloat16* act = nullptr;
   int64_t ld_act = 0;
+  // EPI_SWIGLU_BWD: the forward's gate|up rows [M, 2I] (row stride ld_gu); C is the
+  // gate|up gradient and the accumulator the activation's gradient
+  const __nv_bfloat16* gu = nullptr;
+  int64_t ld_gu = 0;
   // plain epilogues: store C with the L2 evict-first policy (C is not read again by
   // this kernel; its lines then leave L2 before the operand panels)
   int store_hint = 0;
@@ -343,6 +348,72 @@ __device__ __forceinline__ void epilogue_swiglu(uint32_t acc_tmem, int g_begin, 
       uint4* da = reinterpret_cast<uint4*>(ea.act + gm * ea.ld_act + j);
 #pragma unroll
       for (int q = 0; q < 4; ++q) st_v4_hint(da + q, make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]), pol);
+    }
+  }
+}
+
+// EPI_SWIGLU_BWD drain: tile columns [c_begin, c_end) (TMEM columns from acc_tmem) hold
+// the activation gradient d of intermediate columns col0 + c.  With g, u the forward's
+// gate and up values: d up = d * round(g s), d gate = round(d u) * s (1 + g (1 - s)),
+// s = sigmoid(g), d rounded to bf16 first -- the element-wise SwiGLU backward applied
+// to the bf16 activation gradient the plain GEMM would store, so both give the same
+// bits.  Each thread's 64-byte pieces of g and u are loaded before the accumulator
+// columns are read, so the loads overlap the TMEM round trip.
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, float* f) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 w = reinterpret_cast<const uint4*>(p)[q];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = __bfloat1622float2(h[e]);
+      f[8 * q + 2 * e] = t.x;
+      f[8 * q + 2 * e + 1] = t.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void epilogue_swiglu_bwd(uint32_t acc_tmem, int c_begin, int c_end,
+                                                    int64_t gm, int64_t col0, int M,
+                                                    __nv_bfloat16* C, int64_t ldc, float alpha,
+                                                    const EpiArgs& ea) {
+  const bool row_ok = gm < M;
+  const int64_t I = ea.swiglu_i;
+#pragma unroll 1
+  for (int c = c_begin; c < c_end; c += 32) {
+    const int64_t j = col0 + c;
+    const bool ok = row_ok && j < I;
+    float g[32], u[32], d[32];
+    if (ok) {
+      load_bf16x32(ea.gu + gm * ea.ld_gu + j, g);
+      load_bf16x32(ea.gu + gm * ea.ld_gu + I + j, u);
+    }
+    tmem_ld32(acc_tmem + c, d);
+    tmem_wait_ld();
+    if (ok) {
+      uint32_t pg[16], pu[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        float dg2[2], du2[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int i = 2 * e + h;
+          const float dv = rb16(alpha * d[i]);
+          const float sg = silu_sigmoid(g[i]);
+          const float act = rb16(g[i] * sg);
+          const float dact = rb16(dv * u[i]);
+          du2[h] = dv * act;
+          dg2[h] = dact * (sg * (1.0f + g[i] * (1.0f - sg)));
+        }
+        pg[e] = pack_bf16x2(dg2[0], dg2[1]);
+        pu[e] = pack_bf16x2(du2[0], du2[1]);
+      }
+      uint4* og = reinterpret_cast<uint4*>(C + gm * ldc + j);
+      uint4* ou = reinterpret_cast<uint4*>(C + gm * ldc + I + j);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) og[q] = make_uint4(pg[4 * q], pg[4 * q + 1], pg[4 * q + 2], pg[4 * q + 3]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) ou[q] = make_uint4(pu[4 * q], pu[4 * q + 1], pu[4 * q + 2], pu[4 * q + 3]);
     }
   }
 }
@@ -762,6 +833,12 @@ gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         (half + 1) * (BN / 4), BN / 2,
                         (int64_t)tm * 2 * BM + rank * BM + row_in_tile, (int64_t)tn * (BN / 2), M,
                         reinterpret_cast<__nv_bfloat16*>(C), ldc, alpha, ea);
+      } else if constexpr (EPI == EPI_SWIGLU_BWD) {
+        static_assert(sizeof(OutT) == 2 && BN % 64 == 0, "SwiGLU backward epilogue: bf16, BN % 64 == 0");
+        epilogue_swiglu_bwd(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
+                            half * (BN / 2), (half + 1) * (BN / 2),
+                            (int64_t)tm * 2 * BM + rank * BM + row_in_tile, (int64_t)tn * BN, M,
+                            reinterpret_cast<__nv_bfloat16*>(C), ldc, alpha, ea);
       } else {
         epilogue_cols<OutT, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
                                  half * (BN / 2), (half + 1) * (BN / 2),
@@ -1178,6 +1255,49 @@ int gemm_tc_swiglu(int dtype, int64_t M, int64_t I, int64_t K, const void* A, in
       ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
 }
 
+// dgu = swiglu_backward(dy w, gu): the down projection's input gradient d act = dy w
+// (dy [M, K], w [K, I] with row stride ldw) with the SwiGLU backward in the epilogue of
+// the CTA-pair GEMM (bf16, M >= 512 rows, I % 32 == 0, 16-byte aligned rows); the
+// activation gradient itself is never stored.  Otherwise the plain GEMM writes d act
+// into the up half of dgu and the element-wise SwiGLU backward rewrites dgu in place
+// (each element's d act is read before its d up is written, by the same thread): the
+// same bits either way.  algo bits 8-17 may force the pair tile width (256 or 512).
+int gemm_tc_swiglu_bwd(int dtype, int64_t M, int64_t I, int64_t K, const void* dy, int64_t lddy,
+                       const void* w, int64_t ldw, const void* gu, int64_t ldgu, void* dgu,
+                       int64_t lddgu, int algo, int* status, cudaStream_t stream) {
+  const int force_bn = (algo >> 8) & 0x3ff;
+  PE_CHECK_ARG(force_bn == 0 || force_bn == 256 || force_bn == 512,
+               "linear + swiglu backward: forced tile width %d not 256 or 512", force_bn);
+  const bool fused = dtype == PE_BF16 && use_pair(M, 0) && M < (1ll << 31) && I < (1ll << 31) &&
+                     K < (1ll << 31) && I % 32 == 0 && lddy % 8 == 0 && ldw % 8 == 0 &&
+                     ldgu % 8 == 0 && lddgu % 8 == 0 && al16(dy) && al16(w) && al16(gu) &&
+                     al16(dgu);
+  if (!fused) {
+    const size_t esz = dtype == PE_F32 ? 4 : 2;
+    void* da = static_cast<uint8_t*>(dgu) + (size_t)I * esz;
+    int rc = gemm(dtype, M, I, K, dy, lddy, 1, w, 1, ldw, da, lddgu, dtype, nullptr, 0, 1.f, 0.f,
+                  algo & 0xff, status, stream);
+    if (rc) return rc;
+    return ::pe_swiglu_bwd(dtype, M, I, da, lddgu, gu, ldgu, dgu, lddgu, stream);
+  }
+  // 256-wide tiles keep two accumulators in TMEM, so a tile's epilogue (which reads
+  // gate|up and writes both gradient halves) runs behind the next tile's main loop
+  const int pbn = force_bn ? force_bn : 256;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, dy, (uint64_t)K, (uint64_t)M, (uint64_t)lddy * 2, 64, 128);
+  if (!rc) rc = make_tmap_2d(&tb, w, (uint64_t)I, (uint64_t)K, (uint64_t)ldw * 2, 64, 64);
+  if (rc) return rc;
+  EpiArgs ea{nullptr, 0, nullptr, 0};
+  ea.swiglu_i = I;
+  ea.gu = static_cast<const __nv_bfloat16*>(gu);
+  ea.ld_gu = ldgu;
+  if (pbn == 512)
+    return launch_pair<512, false, true, __nv_bfloat16, EPI_SWIGLU_BWD>(
+        ta, tb, (int)M, (int)I, (int)K, dgu, lddgu, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
+  return launch_pair<256, false, true, __nv_bfloat16, EPI_SWIGLU_BWD>(
+      ta, tb, (int)M, (int)I, (int)K, dgu, lddgu, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
+}
+
 int gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_t a_sk,
          const void* B, int64_t b_sn, int64_t b_sk, void* C, int64_t ldc, int c_dtype,
          const void* Cin, int64_t ldcin, float alpha, float beta, int algo, int* status,
@@ -1235,6 +1355,19 @@ extern "C" int pe_linear_swiglu(int dtype, int64_t M, int64_t I, int64_t K, cons
   if (M == 0) return PE_OK;
   return pe::gemm_tc_swiglu(dtype, M, I, K, x, ldx, w_gu, ldw, gu, ldgu, act, lda, algo, status,
                             pe::as_stream(stream));
+}
+
+extern "C" int pe_linear_swiglu_bwd(int dtype, int64_t M, int64_t I, int64_t K, const void* dy,
+                                    int64_t lddy, const void* w, int64_t ldw, const void* gu,
+                                    int64_t ldgu, void* dgu, int64_t lddgu, int algo,
+                                    int32_t* status, void* stream) {
+  PE_CHECK_ARG(M >= 0 && I > 0 && K > 0, "linear + swiglu backward: bad shape");
+  PE_CHECK_ARG(lddy >= K && ldw >= I && ldgu >= 2 * I && lddgu >= 2 * I,
+               "linear + swiglu backward: row stride too small");
+  PE_CHECK_ARG(gu != dgu, "linear + swiglu backward: dgu must not overwrite gate|up");
+  if (M == 0) return PE_OK;
+  return pe::gemm_tc_swiglu_bwd(dtype, M, I, K, dy, lddy, w, ldw, gu, ldgu, dgu, lddgu, algo,
+                                status, pe::as_stream(stream));
 }
 
 extern "C" int pe_gemm(int dtype, int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm,

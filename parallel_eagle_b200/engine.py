@@ -172,9 +172,11 @@ class StepEngine:
         self.loss_sum = torch.zeros(1, dtype=torch.float32, device=self.flat.device)
         # kernel choices (results are identical either way; chosen by step-level timing):
         # RoPE in the q|k|v GEMM epilogue and the attention backward (bf16, head_dim
-        # 128); SwiGLU in the gate|up GEMM epilogue; the fused LM head's tuning bits
+        # 128); SwiGLU in the gate|up GEMM epilogue and its backward in the epilogue of
+        # the down projection's input-gradient GEMM; the fused LM head's tuning bits
         self.fuse_rope = True
         self.fuse_swiglu = True
+        self.fuse_swiglu_bwd = False
         self.lmhead_algo = 0
 
     # --------------------------------------------------------------- plans --
@@ -432,9 +434,11 @@ class StepEngine:
             w_gu = fp.span(p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight", H)
             w_dn = W(p + "mlp.down_proj.weight", (H, I))
             # x3 = x2 + act @ W_down^T
-            da = ops.linear_dgrad(dx, w_dn)
+            if self.fuse_swiglu_bwd:
+                dgu = ops.linear_swiglu_bwd(dx, w_dn, gu, I)
+            else:
+                dgu = ops.swiglu_bwd(ops.linear_dgrad(dx, w_dn), gu, I)
             ops.linear_wgrad(dx, act, grad=G(p + "mlp.down_proj.weight", (H, I)), accumulate=True)
-            dgu = ops.swiglu_bwd(da, gu, I)
             dxn2 = ops.linear_dgrad(dgu, w_gu)
             ops.linear_wgrad(
                 dgu, xn2, accumulate=True,

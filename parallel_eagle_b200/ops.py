@@ -209,6 +209,29 @@ def linear_swiglu(x, w_gu, intermediate: int, gu=None, act=None, algo=L.ALGO_AUT
     return gu, act
 
 
+def linear_swiglu_bwd(dy, w_dn, gu, intermediate: int, out=None, algo=L.ALGO_AUTO):
+    """``dgu = swiglu_bwd(dy w_dn, gu)``: the down projection's input gradient
+    (``dy [M, H]``, ``w_dn [H, I]``) carried through the SwiGLU backward into the
+    gate | up gradient ``[M, 2I]`` in one call -- on the tensor-core pair path the
+    SwiGLU backward runs in the GEMM epilogue and the activation gradient is never
+    stored (same bits as :func:`linear_dgrad` then :func:`swiglu_bwd`)."""
+    L.require_cuda(dy, w_dn, gu)
+    M, K = dy.shape
+    I = int(intermediate)
+    if w_dn.shape != (K, I) or gu.shape[0] != M or gu.shape[1] < 2 * I:
+        raise L.PeError(f"linear_swiglu_bwd: shapes dy {tuple(dy.shape)}, w_dn "
+                        f"{tuple(w_dn.shape)}, gu {tuple(gu.shape)} do not match I = {I}")
+    if out is None:
+        out = torch.empty(M, 2 * I, dtype=dy.dtype, device=dy.device)
+    rc = _lib().pe_linear_swiglu_bwd(
+        L.dtype_code(dy.dtype), M, I, K, dy.data_ptr(), _row_stride(dy), w_dn.data_ptr(),
+        _row_stride(w_dn), gu.data_ptr(), _row_stride(gu), out.data_ptr(), _row_stride(out), algo,
+        status_word(dy.device).data_ptr(), L.stream_ptr(dy.device),
+    )
+    L.check(rc, "pe_linear_swiglu_bwd")
+    return out
+
+
 # ------------------------------------------------------------------ gemm ----
 
 

@@ -243,6 +243,29 @@ def test_linear_swiglu_equals_linear_then_swiglu(M, I, K, bn):
     assert torch.equal(act, act_ref)
 
 
+@pytest.mark.parametrize("M,I,K,bn,dtype", [(300, 512, 256, 0, torch.bfloat16),
+                                             (600, 512, 320, 256, torch.bfloat16),
+                                             (600, 1024, 256, 512, torch.bfloat16),
+                                             (4096, 2048, 512, 0, torch.bfloat16),
+                                             (1500, 768, 192, 256, torch.bfloat16),
+                                             (700, 520, 256, 0, torch.bfloat16),
+                                             (600, 512, 256, 0, torch.float32)])
+def test_linear_swiglu_bwd_equals_dgrad_then_swiglu_bwd(M, I, K, bn, dtype):
+    """The down projection's input gradient with the SwiGLU backward in the GEMM
+    epilogue (256- and 512-wide CTA-pair tiles, a ragged last row tile) equals the plain
+    GEMM followed by the element-wise SwiGLU backward bit for bit; below 512 rows, with
+    I not a multiple of 32 or in fp32 the entry point runs that pair itself (the GEMM
+    writing into dgu's up half, the SwiGLU backward in place)."""
+    dy = _rand(M, K, seed=72, dtype=dtype)
+    w = _rand(K, I, seed=73, scale=0.05, dtype=dtype)
+    gu = _rand(M, 2 * I, seed=74, dtype=dtype)
+    ref = ops.swiglu_bwd(ops.linear_dgrad(dy, w), gu, I)
+    got = ops.linear_swiglu_bwd(dy, w, gu, I, algo=L.ALGO_AUTO | (bn << 8))
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    assert torch.equal(got, ref)
+
+
 @pytest.mark.parametrize("M,nh,nkv,K", [(200, 4, 2, 256), (700, 4, 2, 320), (1024, 28, 4, 512),
                                         (1300, 8, 2, 384)])
 def test_linear_rope_equals_linear_then_rope(M, nh, nkv, K):
