@@ -720,9 +720,10 @@ AB_VARIANTS = {
     # two 5120-row groups instead of one of 10240 (all loss rows of a config-2 sequence)
     "lmhead_group5120": {"lmhead_algo": 20 << 16},
     "lmhead_chunk8k": {"lmhead_algo": 8 << 8},
-    # 24K / 32K-column vocabulary chunks: fewer fp32 dH read-modify-write passes
+    # 16K / 24K-column vocabulary chunks (the default is 32K): more fp32 dH
+    # read-modify-write passes
+    "lmhead_chunk16k": {"lmhead_algo": 16 << 8},
     "lmhead_chunk24k": {"lmhead_algo": 24 << 8},
-    "lmhead_chunk32k": {"lmhead_algo": 32 << 8},
 }
 
 

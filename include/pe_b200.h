@@ -254,8 +254,8 @@ int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth,
  * Rows with label < 0 are ignored.  No gradient reaches W (frozen).
  * For the bf16 paths, algo bits 8-15 set the vocabulary chunk (units of 1024 rows
  * of W, at most 32 with hard labels and 16 with teacher rows) and bits 16-23 the
- * loss-row group (units of 256 rows, at most 40); zero keeps the defaults (16384
- * and 10240).  Bits 24-25 / 26-27 pick the logits / dH GEMM tile width (1: 256,
+ * loss-row group (units of 256 rows, at most 40); zero keeps the defaults (32768,
+ * 16384 with teacher rows, and 10240).  Bits 24-25 / 26-27 pick the logits / dH GEMM tile width (1: 256,
  * 2: 512, 0: automatic).
  * Replaces reference src/pe/partition.py:113-115 (lm_head -> float ->
  * cross_entropy(sum) -> backward) and drafter.py:123-124.
@@ -285,6 +285,12 @@ int pe_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* da, int64_t ld
 /* out[c] (fp32) = sum_r x[r, c] (overwrite) */
 int pe_rowsum_cols(int dtype, int64_t rows, int64_t H, const void* x, int64_t ldx, float* out,
                    void* stream);
+/* out[c] (fp32) = sum over rows r of the nranges (1..16) host-side [begin, end) pairs in
+ * `ranges` of x[r, c] (overwrite), in a fixed order: the expand backward of the shared
+ * prediction-slot input over every segment's prediction rows in one launch (reference
+ * src/pe/drafter.py:137).  Rows of overlapping ranges count once per range. */
+int pe_rowsum_cols_ranges(int dtype, int nranges, const int64_t* ranges, int64_t H,
+                          const void* x, int64_t ldx, float* out, void* stream);
 /* dst[idx[r], :] = src[r, :] (scatter, dst rows not listed are left untouched) and the
  * inverse gather dst[r, :] = src[idx[r], :] */
 int pe_scatter_rows(int dtype, int64_t rows, int64_t H, const int64_t* idx, const void* src,

@@ -92,6 +92,7 @@ SIGNATURES: dict[str, tuple] = {
     "pe_swiglu_fwd": (_int, [_int, _i64, _i64, _vp, _i64, _vp, _i64, _vp]),
     "pe_swiglu_bwd": (_int, [_int, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp]),
     "pe_rowsum_cols": (_int, [_int, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "pe_rowsum_cols_ranges": (_int, [_int, _int, _vp, _i64, _vp, _i64, _vp, _vp]),
     "pe_scatter_rows": (_int, [_int, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp]),
     "pe_gather_rows": (_int, [_int, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp]),
     "pe_cast_f32": (_int, [_int, _i64, _vp, _vp, _vp]),

@@ -2,10 +2,14 @@
 // broadcast of the shared prediction-slot input, SwiGLU (reference
 // src/pe/nn.py:99-100, src/pe/drafter.py:126-137), row scatter/gather for the
 // loss-slot compaction, column sums for the shared-input backward, casts.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace pe {
 namespace {
+
+namespace cg = cooperative_groups;
 
 template <typename T>
 __global__ void embed_rows_kernel(int64_t rows, int64_t H, const int64_t* __restrict__ ids,
@@ -135,10 +139,10 @@ bool vec8_ok(const void* p, int64_t ld) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && ld % 8 == 0;
 }
 
-// out[c] = sum_r x[r, c]; 32 columns per block, 8 row lanes, fixed order.
+// out[c] (+)= sum_r x[r, c]; 32 columns per block, 8 row lanes, fixed order.
 template <typename T>
 __global__ void rowsum_cols_kernel(int64_t rows, int64_t H, const T* __restrict__ x, int64_t ldx,
-                                   float* __restrict__ out) {
+                                   float* __restrict__ out, int accumulate) {
   __shared__ float red[8][33];
   const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
@@ -150,8 +154,91 @@ __global__ void rowsum_cols_kernel(int64_t rows, int64_t H, const T* __restrict_
     float t = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) t += red[i][threadIdx.x];
-    out[c] = t;
+    out[c] = accumulate ? out[c] + t : t;
   }
+}
+
+// Column sums over several row ranges of x (16-byte loads, H % 8 == 0): a cluster of
+// kSplit blocks shares one 128-column slab, block k of the cluster taking every
+// kSplit-th group of 16 rows of every range; each block sums its 16 row lanes in a fixed
+// order and block 0 of the cluster adds the kSplit block sums, read from the others'
+// shared memory, in rank order.  Deterministic, and 8x the blocks of one block per slab.
+constexpr int kRowsumSplit = 8;
+constexpr int kRowsumRanges = 16;
+struct RowRanges {
+  int n;
+  int64_t begin[kRowsumRanges], end[kRowsumRanges];
+};
+
+__device__ __forceinline__ void load8f(const __nv_bfloat16* p, float* f) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void load8f(const float* p, float* f) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+template <typename T>
+__global__ void __cluster_dims__(1, kRowsumSplit, 1) __launch_bounds__(256)
+    rowsum_ranges_kernel(const __grid_constant__ RowRanges rr, int64_t H,
+                         const T* __restrict__ x, int64_t ldx, float* __restrict__ out) {
+  __shared__ float red[16][129];
+  __shared__ float part[128];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int lane16 = threadIdx.x & 15, rl = threadIdx.x >> 4;
+  const int64_t c = (int64_t)blockIdx.x * 128 + lane16 * 8;
+  const int rank = (int)cluster.block_rank();
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  if (c < H) {
+    const int64_t step = 16 * kRowsumSplit;
+    for (int g = 0; g < rr.n; ++g) {
+      int64_t r = rr.begin[g] + rank * 16 + rl;
+      const int64_t e = rr.end[g];
+      // two rows' loads in flight per iteration
+      for (; r + step < e; r += 2 * step) {
+        float a[8], b[8];
+        load8f(x + r * ldx + c, a);
+        load8f(x + (r + step) * ldx + c, b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += a[i] + b[i];
+      }
+      if (r < e) {
+        float a[8];
+        load8f(x + r * ldx + c, a);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += a[i];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[rl][lane16 * 8 + i] = acc[i];
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t += red[i][threadIdx.x];
+    part[threadIdx.x] = t;
+  }
+  cluster.sync();  // every block's part[] is written
+  if (rank == 0 && threadIdx.x < 128) {
+    const int64_t col = (int64_t)blockIdx.x * 128 + threadIdx.x;
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < kRowsumSplit; ++k) t += cluster.map_shared_rank(part, k)[threadIdx.x];
+    if (col < H) out[col] = t;
+  }
+  cluster.sync();  // block 0 has read the others' part[] before they exit
 }
 
 template <typename T>
@@ -308,12 +395,59 @@ extern "C" int pe_swiglu_bwd(int dtype, int64_t rows, int64_t I, const void* da,
   });
 }
 
+extern "C" int pe_rowsum_cols_ranges(int dtype, int nranges, const int64_t* ranges, int64_t H,
+                                     const void* x, int64_t ldx, float* out, void* stream) {
+  PE_CHECK_ARG(nranges >= 1 && nranges <= kRowsumRanges && ranges != nullptr,
+               "rowsum_cols_ranges: 1 to %d row ranges (got %d)", kRowsumRanges, nranges);
+  PE_CHECK_ARG(H > 0 && ldx >= H, "rowsum_cols_ranges: bad shape");
+  RowRanges rr{};
+  rr.n = nranges;
+  for (int g = 0; g < nranges; ++g) {
+    PE_CHECK_ARG(ranges[2 * g] >= 0 && ranges[2 * g + 1] >= ranges[2 * g],
+                 "rowsum_cols_ranges: range %d is [%lld, %lld)", g, (long long)ranges[2 * g],
+                 (long long)ranges[2 * g + 1]);
+    rr.begin[g] = ranges[2 * g];
+    rr.end[g] = ranges[2 * g + 1];
+  }
+  const size_t esz = dtype == PE_F32 ? 4 : 2;
+  const bool vec = (dtype == PE_BF16 || dtype == PE_F32) && H % 8 == 0 &&
+                   (ldx * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  if (!vec) {
+    // one range at a time on the scalar kernel, the sums added in range order
+    for (int g = 0; g < nranges; ++g) {
+      const int64_t rows = rr.end[g] - rr.begin[g];
+      const uint8_t* xg = static_cast<const uint8_t*>(x) + (size_t)rr.begin[g] * ldx * esz;
+      int rc = PE_DISPATCH(dtype, T, [&] {
+        rowsum_cols_kernel<T><<<(unsigned)ceil_div(H, 32), dim3(32, 8), 0, as_stream(stream)>>>(
+            rows, H, (const T*)xg, ldx, out, g > 0 ? 1 : 0);
+        PE_LAUNCHED();
+        return PE_OK;
+      });
+      if (rc) return rc;
+    }
+    return PE_OK;
+  }
+  const dim3 grid((unsigned)ceil_div(H, 128), kRowsumSplit);
+  if (dtype == PE_BF16)
+    rowsum_ranges_kernel<__nv_bfloat16><<<grid, 256, 0, as_stream(stream)>>>(
+        rr, H, static_cast<const __nv_bfloat16*>(x), ldx, out);
+  else
+    rowsum_ranges_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(
+        rr, H, static_cast<const float*>(x), ldx, out);
+  PE_LAUNCHED();
+  return PE_OK;
+}
+
 extern "C" int pe_rowsum_cols(int dtype, int64_t rows, int64_t H, const void* x, int64_t ldx,
                               float* out, void* stream) {
   PE_CHECK_ARG(rows >= 0 && H > 0 && ldx >= H, "rowsum_cols: bad shape");
+  if (rows > 0) {
+    const int64_t range[2] = {0, rows};
+    return pe_rowsum_cols_ranges(dtype, 1, range, H, x, ldx, out, stream);
+  }
   return PE_DISPATCH(dtype, T, [&] {
     rowsum_cols_kernel<T><<<(unsigned)ceil_div(H, 32), dim3(32, 8), 0, as_stream(stream)>>>(
-        rows, H, (const T*)x, ldx, out);
+        rows, H, (const T*)x, ldx, out, 0);
     PE_LAUNCHED();
     return PE_OK;
   });

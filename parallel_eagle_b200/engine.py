@@ -473,9 +473,8 @@ class StepEngine:
             # the shared row is broadcast to every prediction slot: its gradient is the
             # column sum over those slots, rounded to the parameter dtype like
             # autograd's expand backward
-            sums = [ops.rowsum_cols(dx[off + a1 : off + q])
-                    for _, a1, q, off in plan.segs if q > a1]
-            dvec32 = sums[0] if len(sums) == 1 else torch.stack(sums).sum(0)
+            dvec32 = ops.rowsum_cols_ranges(
+                dx, [(off + a1, off + q) for _, a1, q, off in plan.segs if q > a1])
             dvec = torch.empty(1, H, dtype=dt, device=dev)
             ops.cast_from_f32(dvec32, dvec)
             ops.linear_wgrad(dvec, cat_vec, grad=g_in, accumulate=True)

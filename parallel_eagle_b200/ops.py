@@ -7,6 +7,8 @@ allocated here (torch owns all memory); the library itself never allocates.
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -564,6 +566,36 @@ def rowsum_cols(x, out=None):
     rc = _lib().pe_rowsum_cols(L.dtype_code(x.dtype), rows, H, x.data_ptr(), _row_stride(x),
                                out.data_ptr(), L.stream_ptr(x.device))
     L.check(rc, "pe_rowsum_cols")
+    return out
+
+
+def rowsum_cols_ranges(x, ranges, out=None):
+    """fp32 ``[H]`` column sums of ``x`` over the row ranges ``[(begin, end), ...]``
+    (host ints), in a fixed order: one launch per 16 ranges."""
+    rows, H = x.shape
+    ranges = [(int(b), int(e)) for b, e in ranges]
+    if not ranges:
+        raise L.PeError("rowsum_cols_ranges: no row ranges")
+    for b, e in ranges:
+        if not 0 <= b <= e <= rows:
+            raise L.PeError(f"rowsum_cols_ranges: range [{b}, {e}) outside {rows} rows")
+    if out is None:
+        out = torch.empty(H, dtype=torch.float32, device=x.device)
+    part = None
+    for i in range(0, len(ranges), 16):
+        grp = ranges[i : i + 16]
+        if i == 0:
+            dst = out
+        else:
+            if part is None:
+                part = torch.empty_like(out)
+            dst = part
+        flat = (ctypes.c_int64 * (2 * len(grp)))(*[v for r in grp for v in r])
+        rc = _lib().pe_rowsum_cols_ranges(L.dtype_code(x.dtype), len(grp), flat, H, x.data_ptr(),
+                                          _row_stride(x), dst.data_ptr(), L.stream_ptr(x.device))
+        L.check(rc, "pe_rowsum_cols_ranges")
+        if i > 0:
+            out += part
     return out
 
 

@@ -626,6 +626,28 @@ def test_rows_embed_fill_gather_scatter_colsum(H, dtype):
     assert rel(s.cpu(), src.float().sum(0).cpu()) < 1e-6
 
 
+@pytest.mark.parametrize("dtype,H,ldx", [(torch.bfloat16, 3584, 3584), (torch.float32, 1000, 1000),
+                                         (torch.bfloat16, 300, 300), (torch.bfloat16, 256, 264)])
+def test_rowsum_cols_ranges(dtype, H, ldx):
+    """Column sums over several row ranges in one launch (the clustered 16-byte kernel,
+    or per range on the scalar one when H is not a multiple of 8): the segments'
+    prediction rows of a stacked pass, an empty and a one-row range, and more than 16
+    ranges (two launches), against fp64 sums."""
+    rows = 9000
+    xs = _rand(rows, ldx, seed=25, dtype=dtype)
+    x = xs[:, :H]
+    cases = [[(2560, 4608), (7680, 9000)], [(0, 0), (5, 6), (100, 3000)],
+             [(i * 400, i * 400 + 37 * (i + 1)) for i in range(20)]]
+    for ranges in cases:
+        got = ops.rowsum_cols_ranges(x, ranges)
+        torch.cuda.synchronize()
+        want = sum(x[b:e].double().sum(0) for b, e in ranges).cpu()
+        err = (got.double().cpu() - want).abs().max().item()
+        assert err <= 1e-4 * (1.0 + want.abs().max().item()), (ranges[:3], err)
+    with pytest.raises(L.PeError):
+        ops.rowsum_cols_ranges(x, [(5, rows + 1)])
+
+
 def test_row_moves_beyond_one_grid_row_span():
     """More rows than the 16-byte row kernel's grid covers in one pass (32768)."""
     src = _rand(1000, 64, seed=24)
