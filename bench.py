@@ -724,6 +724,8 @@ AB_VARIANTS = {
     # read-modify-write passes
     "lmhead_chunk16k": {"lmhead_algo": 16 << 8},
     "lmhead_chunk24k": {"lmhead_algo": 24 << 8},
+    # every vocabulary chunk two-pass (logits stored, then rewritten as exponentials)
+    "lmhead_two_pass": {"lmhead_algo": 1 << 28},
 }
 
 

@@ -35,7 +35,14 @@ enum : int {
   EPI_ROPE = 3,      // C = rotate(round(alpha * acc)) on 128-wide heads below rot_cols
   EPI_SWIGLU = 4,    // gate|up tile pairs: C[:, j], C[:, I + j] = g, u; act[:, j] = silu(g) u
   EPI_SWIGLU_BWD = 5,  // acc = d act[:, j]: C[:, j], C[:, I + j] = d gate, d up (gate|up read)
+  EPI_PEXP = 6,        // z = round(alpha * acc); C = e^(z - rowref[row]); stats = (max z, sum C)
 };
+
+// EPI_PEXP: the largest amount by which a tile's logits may exceed the row's reference
+// (the running maximum of the earlier vocabulary chunks).  e^64 ~ 6e27 keeps every
+// exponential, its 128-column sums and the dH accumulation over a chunk finite in fp32
+// and bf16; a larger excess sets the overflow word and the caller recomputes the call.
+constexpr float kPexpMargin = 64.f;
 struct EpiArgs {
   float2* stats;
   int stats_ld;
@@ -61,6 +68,19 @@ struct EpiArgs {
   // plain epilogues: store C with the L2 evict-first policy (C is not read again by
   // this kernel; its lines then leave L2 before the operand panels)
   int store_hint = 0;
+  // EPI_PEXP: per-row reference (running maximum), labels (the label column of row r
+  // is labels[r] - label_v0; a negative label ignores the row: C = 0), the label
+  // logit output and the overflow word (set to 1 when a logit exceeds its row's
+  // reference by more than kPexpMargin)
+  const float* rowref = nullptr;
+  const int64_t* labels = nullptr;
+  int64_t label_v0 = 0;
+  float* zlab = nullptr;
+  int* overflow = nullptr;
+  // every variant: when non-null and *run_if == 0 the launch does nothing (every CTA
+  // returns before touching its barriers or TMEM) -- a device-side condition for a
+  // pass the host enqueues unconditionally
+  const int* run_if = nullptr;
 };
 
 // silu(g) = g * sigmoid(g) with sigmoid(g) = 1 / (1 + e^-g) from the hardware exp2 and
@@ -436,6 +456,18 @@ __device__ __forceinline__ void epilogue_cols(uint32_t acc_tmem, int c_begin, in
   // EPI_ROWSCALE: the accumulated input is scaled per row (online-softmax correction)
   const float beta_row = (EPI == EPI_ROWSCALE && gm < M) ? ea.rowscale[gm] : beta;
   float m_run = -INFINITY, s_run = 0.f;  // EPI_STATS: running max / sum-exp of a 128-col chunk
+  // EPI_PEXP: the row's reference, label column and whether the row is ignored
+  float p_ref = 0.f;
+  int64_t lab_col = -1;
+  bool p_skip = true;
+  if constexpr (EPI == EPI_PEXP) {
+    if (gm < M) {
+      const int64_t lab = ea.labels[gm];
+      p_ref = ea.rowref[gm];
+      p_skip = lab < 0;
+      lab_col = lab - ea.label_v0;
+    }
+  }
   const uint64_t pol_ef = ea.store_hint ? l2_evict_first_policy() : 0ull;
   const uint64_t* pol = ea.store_hint ? &pol_ef : nullptr;
 #pragma unroll 1
@@ -462,12 +494,33 @@ __device__ __forceinline__ void epilogue_cols(uint32_t acc_tmem, int c_begin, in
         s_run = s_run * __expf(m_run - mn) + cs;
         m_run = mn;
         store_row32<OutT>(C + gm * ldc + gn0, nullptr, v, 1.f, 0.f, valid, vec_ok != 0);
+      } else if constexpr (EPI == EPI_PEXP) {
+        // the logits as EPI_STATS stores them, then p = e^(z - ref): stats are the
+        // tile's maximum logit and its sum of p (relative to ref)
+        float cm = -INFINITY, cs = 0.f, zl = 0.f;
+        const int64_t lc = lab_col - gn0;
+        const bool has_lab = lc >= 0 && lc < valid;
+        const int li = has_lab ? (int)lc : -1;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float z = round_to<OutT>(alpha * v[i]);
+          cm = i < valid ? fmaxf(cm, z) : cm;
+          zl = i == li ? z : zl;
+          const float p = p_skip ? 0.f : __expf(z - p_ref);
+          cs += i < valid ? p : 0.f;
+          v[i] = p;
+        }
+        if (has_lab) ea.zlab[gm] = zl;
+        if (!p_skip && cm - p_ref > kPexpMargin) *ea.overflow = 1;
+        m_run = fmaxf(m_run, cm);
+        s_run += cs;
+        store_row32<OutT>(C + gm * ldc + gn0, nullptr, v, 1.f, 0.f, valid, vec_ok != 0);
       } else {
         store_row32<OutT>(C + gm * ldc + gn0, Cin ? Cin + gm * ldcin + gn0 : nullptr, v, alpha,
                           beta_row, valid, vec_ok != 0, pol);
       }
     }
-    if constexpr (EPI == EPI_STATS) {
+    if constexpr (EPI == EPI_STATS || EPI == EPI_PEXP) {
       if ((c0 & 127) == 96) {  // end of a 128-column chunk
         const int64_t chunk0 = gn0 - 96;
         if (gm < M && chunk0 < N) ea.stats[gm * ea.stats_ld + chunk0 / 128] = make_float2(m_run, s_run);
@@ -483,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                int M, int N, int K, OutT* C, int64_t ldc, const OutT* Cin, int64_t ldcin,
                float alpha, float beta, int vec_ok, EpiArgs ea, int* status) {
+  if (ea.run_if != nullptr && *ea.run_if == 0) return;  // a pass the condition skips
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
@@ -663,6 +717,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     int M, int N, int K, OutT* C, int64_t ldc, const OutT* Cin, int64_t ldcin,
                     float alpha, float beta, int vec_ok, EpiArgs ea, int* status) {
+  // a pass the condition skips: both CTAs of every pair read the same word and return
+  // before any cluster barrier
+  if (ea.run_if != nullptr && *ea.run_if == 0) return;
   using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int NMMA = Cfg::NMMA, NJ = Cfg::NJ, NJH = Cfg::NJH, NACC = Cfg::NACC;
@@ -1117,7 +1174,8 @@ int gemm_tc(int64_t M, int64_t N, int64_t K, const void* A, int64_t a_sm, int64_
 
 int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
                          const void* B, int64_t ldb, void* C, int64_t ldc, float2* stats,
-                         int stats_ld, int* status, cudaStream_t stream, int force_bn) {
+                         int stats_ld, int* status, cudaStream_t stream, int force_bn,
+                         const int* run_if) {
   PE_CHECK_ARG(M > 0 && N > 0 && K > 0 && lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0 &&
                    al16(A) && al16(B) && al16(C),
                "gemm (logits + row stats): operands must be 16-byte aligned bf16");
@@ -1136,6 +1194,7 @@ int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t
                       pair ? (uint32_t)pair_b_box(pbn) : 256u);
   if (rc) return rc;
   EpiArgs ea{stats, stats_ld, nullptr, 0};
+  ea.run_if = run_if;
   if (pair && pbn == 512)
     return launch_pair<512, false, false, __nv_bfloat16, EPI_STATS>(
         ta, tb, (int)M, (int)N, (int)K, C, ldc, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
@@ -1147,10 +1206,56 @@ int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t
                                                              stream, ea);
 }
 
+// P = e^(round(h W^T) - rowref[row]) (bf16; 0 for rows with a negative label), the
+// per-128-column (max logit, sum P) pairs, the label logit of the rows whose label
+// falls in these N columns (labels[r] - label_v0), and *overflow = 1 when a logit
+// exceeds its row's reference by more than kPexpMargin.  Tiles as the logits + stats
+// GEMM.
+int gemm_tc_logits_pexp(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
+                        const void* B, int64_t ldb, void* P, int64_t ldp, float2* stats,
+                        int stats_ld, const float* rowref, const int64_t* labels,
+                        int64_t label_v0, float* zlab, int* overflow, int* status,
+                        cudaStream_t stream, int force_bn) {
+  PE_CHECK_ARG(M > 0 && N > 0 && K > 0 && lda % 8 == 0 && ldb % 8 == 0 && ldp % 8 == 0 &&
+                   al16(A) && al16(B) && al16(P),
+               "gemm (logits -> exponentials): operands must be 16-byte aligned bf16");
+  PE_CHECK_ARG(stats_ld >= (N + 127) / 128, "gemm (logits -> exponentials): stats_ld too small");
+  PE_CHECK_ARG(rowref && labels && zlab && overflow,
+               "gemm (logits -> exponentials): reference, labels, label logits and overflow "
+               "word are required");
+  PE_CHECK_ARG(force_bn == 0 || force_bn == 256 || force_bn == 512,
+               "gemm (logits -> exponentials): tile width %d not 256 or 512", force_bn);
+  const bool pair = use_pair(M, 0);
+  const int pbn = !pair ? 256
+                  : force_bn ? force_bn
+                  : (choose_bn_pair(M, N, K, false, 2, sm_count() / 2) > 256 ? 512 : 256);
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, 64, 128);
+  if (!rc)
+    rc = make_tmap_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, 64,
+                      pair ? (uint32_t)pair_b_box(pbn) : 256u);
+  if (rc) return rc;
+  EpiArgs ea{stats, stats_ld, nullptr, 0};
+  ea.rowref = rowref;
+  ea.labels = labels;
+  ea.label_v0 = label_v0;
+  ea.zlab = zlab;
+  ea.overflow = overflow;
+  if (pair && pbn == 512)
+    return launch_pair<512, false, false, __nv_bfloat16, EPI_PEXP>(
+        ta, tb, (int)M, (int)N, (int)K, P, ldp, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
+  if (pair)
+    return launch_pair<256, false, false, __nv_bfloat16, EPI_PEXP>(
+        ta, tb, (int)M, (int)N, (int)K, P, ldp, nullptr, 0, 1.f, 0.f, 1, status, stream, ea);
+  return launch<256, false, false, __nv_bfloat16, EPI_PEXP>(ta, tb, (int)M, (int)N, (int)K, P, ldp,
+                                                            nullptr, 0, 1.f, 0.f, 1, status,
+                                                            stream, ea);
+}
+
 int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
                          const void* B, int64_t b_sk, float* C, int64_t ldc, const float* Cin,
                          const float* rowscale, int* status, cudaStream_t stream,
-                         int force_bn) {
+                         int force_bn, const int* run_if) {
   PE_CHECK_ARG(M > 0 && N > 0 && K > 0 && lda % 8 == 0 && b_sk % 8 == 0 && ldc % 4 == 0 &&
                    al16(A) && al16(B) && al16(C),
                "gemm (row-scaled accumulate): operands must be 16-byte aligned");
@@ -1159,6 +1264,7 @@ int gemm_tc_rowscale_acc(int64_t M, int64_t N, int64_t K, const void* A, int64_t
   if (!rc) rc = make_tmap_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)b_sk * 2, 64, 64);
   if (rc) return rc;
   EpiArgs ea{nullptr, 0, rowscale, 0};
+  ea.run_if = run_if;
   PE_CHECK_ARG(force_bn == 0 || force_bn == 256 || force_bn == 512,
                "gemm (row-scaled accumulate): tile width %d not 256 or 512", force_bn);
   if (use_pair(M, 0)) {

@@ -265,7 +265,7 @@ FastPlan fast_plan_of(int64_t R, int64_t V, int algo, int64_t max_chunk) {
 }
 
 struct FastLayout {
-  size_t m, l, zlab, lse, alpha, stats[2], Z[2], dH, total;
+  size_t m, l, zlab, lse, alpha, keep[3], keep_last, m0, flag, stats[2], Z[2], dH, total;
 };
 
 // sized for the largest plan any ``algo`` can select, so one workspace serves all
@@ -285,6 +285,10 @@ FastLayout fast_layout_of(int64_t R, int64_t H, int64_t V) {
   L.zlab = take(4 * R);
   L.lse = take(4 * R);
   L.alpha = take(4 * R);
+  for (int b = 0; b < 3; ++b) L.keep[b] = take(4 * R);
+  L.keep_last = take(4 * R);
+  L.m0 = take(4 * R);
+  L.flag = take(4);
   for (int b = 0; b < 2; ++b) {  // double-buffered: chunk j+1's logits overlap chunk j
     L.stats[b] = take(8 * (size_t)rg * nt);
     L.Z[b] = take(2 * (size_t)rg * vc);
@@ -301,7 +305,8 @@ template <int kPer>  // 16-byte loads per thread: vc <= kPer * 256 * 8
 __global__ void __launch_bounds__(256)
 combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __restrict__ stats,
                __nv_bfloat16* __restrict__ Z, int64_t ldz, const int64_t* __restrict__ labels,
-               float* m, float* l, float* zlab, float* alpha) {
+               float* m, float* l, float* zlab, float* alpha, const int* run_if) {
+  if (run_if != nullptr && *run_if == 0) return;
   __shared__ float s_mnew;
   const int64_t r = blockIdx.x;
   const int64_t lab = labels[r];
@@ -366,18 +371,120 @@ combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __res
   }
 }
 
-__global__ void fast_init_kernel(int64_t R, float* m, float* l, float* zlab) {
+// running stats reset; `flag` (when non-null) clears the single-pass overflow word
+__global__ void fast_init_kernel(int64_t R, float* m, float* l, float* zlab, float* keep_last,
+                                 int* flag, const int* run_if) {
+  if (run_if != nullptr && *run_if == 0) return;
+  if (flag != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *flag = 0;
   for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < R;
        r += (int64_t)gridDim.x * blockDim.x) {
     m[r] = -INFINITY;
     l[r] = 0.f;
     zlab[r] = 0.f;
+    keep_last[r] = 1.f;
   }
 }
 
-// dh = scale * (dH / l - W[label])
+// First chunk of a row group (one warp per row): the row maximum m0 and l = sum of
+// e^(z - m0) from the chunk's (tile max, sum e^(z - tile max)) pairs, and the label
+// logit when the label falls in the chunk.  keep = 1: the next chunk's exponentials
+// are taken relative to m0, the reference of this chunk's.
+__global__ void __launch_bounds__(256)
+fold_first_kernel(int64_t R, int64_t vc, int nt, int stats_ld, const float2* __restrict__ stats,
+                  const __nv_bfloat16* __restrict__ Z, int64_t ldz,
+                  const int64_t* __restrict__ labels, float* m, float* l, float* m0, float* zlab,
+                  float* keep, float* keep_last) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const float2* st = stats + r * stats_ld;
+  float lm = -INFINITY;
+  for (int t = lane; t < nt; t += 32) lm = fmaxf(lm, st[t].x);
+  const float mx = warp_max(lm);
+  float part = 0.f;
+  for (int t = lane; t < nt; t += 32) {
+    const float2 v = st[t];
+    if (v.x != -INFINITY) part += v.y * expf(v.x - mx);
+  }
+  const float sum = warp_sum(part);
+  if (lane == 0) {
+    m[r] = mx;
+    m0[r] = mx;
+    l[r] = sum;
+    keep[r] = 1.f;
+    keep_last[r] = 1.f;
+    const int64_t lab = labels[r];
+    if (lab >= 0 && lab < vc) zlab[r] = __bfloat162float(Z[r * ldz + lab]);
+  }
+}
+
+// First chunk of a row group, in place: Z <- e^(z - m0) (0 for an ignored row).  All
+// of a thread's 16-byte pieces of the row are loaded before any is rewritten.
+template <int kPer>
+__global__ void __launch_bounds__(256)
+exp_first_kernel(int64_t vc, __nv_bfloat16* __restrict__ Z, int64_t ldz,
+                 const int64_t* __restrict__ labels, const float* __restrict__ m0) {
+  const int64_t r = blockIdx.x;
+  __nv_bfloat16* z = Z + r * ldz;
+  const bool ignored = labels[r] < 0;
+  const float mx = m0[r];
+  uint4 buf[kPer];
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+    if (c < vc) buf[q] = *reinterpret_cast<const uint4*>(z + c);
+  }
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+    if (c < vc) {
+      uint4 u = buf[q];
+      __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f = __bfloat1622float2(h2[i]);
+        f.x = ignored ? 0.f : __expf(f.x - mx);
+        f.y = ignored ? 0.f : __expf(f.y - mx);
+        h2[i] = __floats2bfloat162_rn(f.x, f.y);
+      }
+      *reinterpret_cast<uint4*>(z + c) = u;
+    }
+  }
+}
+
+// Later chunk (one warp per row): its exponentials were taken relative to the running
+// maximum m_old, so with M = max(m_old, tile maxima) and keep = e^(m_old - M):
+//   l <- l keep + sum_t S_t keep   (S_t: the tile's sum of e^(z - m_old))
+// each S_t scaled before the sum, so the sum stays in range.  keep is also the factor
+// the next chunk's dH accumulation applies to the running dH, and the last chunk's
+// keep the factor the final dH applies (keep_last).
+__global__ void __launch_bounds__(256)
+fold_kernel(int64_t R, int nt, int stats_ld, const float2* __restrict__ stats, float* m, float* l,
+            float* keep, float* keep_last) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const float2* st = stats + r * stats_ld;
+  const float m_old = m[r];
+  float lm = -INFINITY;
+  for (int t = lane; t < nt; t += 32) lm = fmaxf(lm, st[t].x);
+  const float mx = fmaxf(m_old, warp_max(lm));
+  const float kp = expf(m_old - mx);
+  float part = 0.f;
+  for (int t = lane; t < nt; t += 32) part += st[t].y * kp;
+  const float sum = warp_sum(part);
+  if (lane == 0) {
+    m[r] = mx;
+    l[r] = l[r] * kp + sum;
+    keep[r] = kp;
+    keep_last[r] = kp;
+  }
+}
+
+// dh = scale * (dH keep_last / l - W[label])
 __global__ void fast_dh_kernel(int64_t R, int64_t H, const float* __restrict__ dH,
-                               const float* __restrict__ l, const int64_t* __restrict__ labels,
+                               const float* __restrict__ l, const float* __restrict__ keep_last,
+                               const int64_t* __restrict__ labels,
                                const __nv_bfloat16* __restrict__ W, float scale,
                                __nv_bfloat16* __restrict__ dh, int64_t lddh) {
   const int64_t total = R * H / 8;
@@ -388,7 +495,7 @@ __global__ void fast_dh_kernel(int64_t R, int64_t H, const float* __restrict__ d
     const int64_t lab = labels[r];
     uint4 out = make_uint4(0, 0, 0, 0);
     if (lab >= 0) {
-      const float inv = 1.f / l[r];
+      const float inv = keep_last[r] / l[r];
       const float4 a = reinterpret_cast<const float4*>(dH + e)[0];
       const float4 b = reinterpret_cast<const float4*>(dH + e)[1];
       const uint4 wu = *reinterpret_cast<const uint4*>(W + lab * H + c);
@@ -412,11 +519,22 @@ bool fast_eligible(int dtype, int64_t H, int64_t V, const void* h, int64_t ldh, 
          V % 8 == 0 && ldh % 8 == 0 && lddh % 8 == 0 && a16(h) && a16(W) && a16(dh);
 }
 
-// Software pipeline over (row group, vocabulary chunk) steps t: the logits GEMM of
-// step t runs on the caller's stream while the combine pass and dH GEMM of step
-// t-1 run on a side stream, so one GEMM's last partial wave and the combine pass
-// overlap the other GEMM.  Z and the tile stats are double-buffered; the logits
-// GEMM of step t waits for the dH GEMM of step t-2 (same buffer).
+// Software pipeline over (row group, vocabulary chunk) steps t.  The first chunk of a
+// group runs in two passes: the logits GEMM stores the bf16 logits with per-tile
+// (max, sum e^(z - max)) pairs, a fold gives the row maximum m0, and the side stream
+// rewrites the chunk as e^(z - m0) before the dH GEMM.  Every later chunk is one pass:
+// its logits GEMM writes P = e^(z - m) directly, m the running maximum of the earlier
+// chunks (no bf16 logits are stored or re-read), and a fold on the same stream updates
+// (m, l) before the next chunk's GEMM reads m.  The dH GEMM of chunk t (side stream)
+// rescales the running dH by e^(m_{t-2} - m_{t-1}) (the fold of chunk t - 1) and adds
+// P W; the final dH is rescaled once more by the last fold's factor.  So one GEMM's last
+// partial wave, the fold and the first chunk's rewrite overlap the other GEMM.  Z, the
+// stats and the per-chunk factors are double- / triple-buffered: the logits GEMM of
+// step t waits for the dH GEMM of step t-2, which read the factors of step t-3.
+// If some logit exceeds its row's running maximum by more than e^64 allows, the
+// epilogue sets an overflow word and every pass of the classic two-pass algorithm
+// below runs as well (each launch returns at once when the word is 0), recomputing the
+// whole call; the loss and dh always come from the pass that ran last.
 int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, const void* W,
                 const int64_t* labels, float grad_scale, void* dh, int64_t lddh, float* loss_sum,
                 uint8_t* ws, int algo, int* status, cudaStream_t st) {
@@ -427,11 +545,19 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
   float* zlab = (float*)(ws + L.zlab);
   float* lse = (float*)(ws + L.lse);
   float* alpha = (float*)(ws + L.alpha);
+  float* keep[3] = {(float*)(ws + L.keep[0]), (float*)(ws + L.keep[1]), (float*)(ws + L.keep[2])};
+  float* keep_last = (float*)(ws + L.keep_last);
+  float* m0 = (float*)(ws + L.m0);
+  int* flag = (int*)(ws + L.flag);
   float2* stats[2] = {(float2*)(ws + L.stats[0]), (float2*)(ws + L.stats[1])};
   __nv_bfloat16* Z[2] = {(__nv_bfloat16*)(ws + L.Z[0]), (__nv_bfloat16*)(ws + L.Z[1])};
   float* dH = (float*)(ws + L.dH);
   const int64_t VC = P.vc;
   const int nt_max = (int)((VC + kStatTile - 1) / kStatTile);
+  // 8 loads of 16 B per thread cover chunks up to 16K columns, 16 up to 32K (a single
+  // width would hold 16 in registers and halve the blocks per SM)
+  auto exp_first = VC <= 16384 ? exp_first_kernel<8> : exp_first_kernel<16>;
+  auto combine = VC <= 16384 ? combine_kernel<8> : combine_kernel<16>;
   cudaStream_t side = side_stream(0);
   cudaEvent_t ev_fork = pool_event(0), ev_join = pool_event(1);
   cudaEvent_t ev_logits[2] = {pool_event(2), pool_event(3)};
@@ -440,7 +566,9 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
     set_error("lmhead_ce: could not create the side stream or its events");
     return PE_ERR_CUDA;
   }
-  fast_init_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, zlab);
+  // algo bit 28: the two-pass algorithm for every chunk (kept for comparison)
+  const bool two_pass = (algo >> 28) & 1;
+  fast_init_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, zlab, keep_last, flag, nullptr);
   PE_LAUNCHED();
   PE_CUDA_TRY(cudaEventRecord(ev_fork, st));
   PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_fork, 0));
@@ -449,36 +577,90 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
     const int64_t rg = (R - r0) < P.rg ? (R - r0) : P.rg;
     const void* hg = (const __nv_bfloat16*)h + r0 * ldh;
     float* dHg = dH + r0 * H;
+    const unsigned fold_grid = (unsigned)((rg + 7) / 8);
     for (int64_t v0 = 0; v0 < V; v0 += VC, ++t) {
       const int b = (int)(t & 1);
       const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
       const int nt = (int)((vc + kStatTile - 1) / kStatTile);
       const __nv_bfloat16* Wc = (const __nv_bfloat16*)W + v0 * H;
+      float* kt = keep[t % 3] + r0;
       if (t >= 2) PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_dh[b], 0));
-      int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Z[b], VC, stats[b], nt_max,
-                                    status, st, P.logits_bn);
-      if (rc) return rc;
-      PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
-      PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
-      // 8 loads of 16 B per thread cover chunks up to 16K columns, 16 up to 32K (a
-      // single width would hold 16 in registers and halve the blocks per SM)
-      auto combine = vc <= 16384 ? combine_kernel<8> : combine_kernel<16>;
-      combine<<<(unsigned)rg, 256, 0, side>>>(vc, v0, nt, nt_max, stats[b], Z[b], VC,
-                                              labels + r0, m + r0, l + r0, zlab + r0, alpha + r0);
-      PE_LAUNCHED();
-      rc = gemm_tc_rowscale_acc(rg, H, vc, Z[b], VC, Wc, H, dHg, H, v0 > 0 ? dHg : nullptr,
-                                alpha + r0, status, side, P.dh_bn);
+      int rc;
+      if (two_pass) {
+        rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Z[b], VC, stats[b], nt_max, status,
+                                  st, P.logits_bn);
+        if (rc) return rc;
+        PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
+        PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
+        combine<<<(unsigned)rg, 256, 0, side>>>(vc, v0, nt, nt_max, stats[b], Z[b], VC,
+                                                labels + r0, m + r0, l + r0, zlab + r0,
+                                                alpha + r0, nullptr);
+        PE_LAUNCHED();
+        rc = gemm_tc_rowscale_acc(rg, H, vc, Z[b], VC, Wc, H, dHg, H, v0 > 0 ? dHg : nullptr,
+                                  alpha + r0, status, side, P.dh_bn);
+      } else if (v0 == 0) {
+        rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Z[b], VC, stats[b], nt_max, status,
+                                  st, P.logits_bn);
+        if (rc) return rc;
+        fold_first_kernel<<<fold_grid, 256, 0, st>>>(rg, vc, nt, nt_max, stats[b], Z[b], VC,
+                                                     labels + r0, m + r0, l + r0, m0 + r0,
+                                                     zlab + r0, kt, keep_last + r0);
+        PE_LAUNCHED();
+        PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
+        PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
+        exp_first<<<(unsigned)rg, 256, 0, side>>>(vc, Z[b], VC, labels + r0, m0 + r0);
+        PE_LAUNCHED();
+        rc = gemm_tc_rowscale_acc(rg, H, vc, Z[b], VC, Wc, H, dHg, H, nullptr, kt, status, side,
+                                  P.dh_bn);
+      } else {
+        rc = gemm_tc_logits_pexp(rg, vc, H, hg, ldh, Wc, H, Z[b], VC, stats[b], nt_max, m + r0,
+                                 labels + r0, v0, zlab + r0, flag, status, st, P.logits_bn);
+        if (rc) return rc;
+        fold_kernel<<<fold_grid, 256, 0, st>>>(rg, nt, nt_max, stats[b], m + r0, l + r0, kt,
+                                               keep_last + r0);
+        PE_LAUNCHED();
+        PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
+        PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
+        rc = gemm_tc_rowscale_acc(rg, H, vc, Z[b], VC, Wc, H, dHg, H, dHg, keep[(t + 2) % 3] + r0,
+                                  status, side, P.dh_bn);
+      }
       if (rc) return rc;
       PE_CUDA_TRY(cudaEventRecord(ev_dh[b], side));
     }
   }
   PE_CUDA_TRY(cudaEventRecord(ev_join, side));
   PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_join, 0));
+  // recomputation after an overflow: the classic two-pass algorithm on one stream, every
+  // launch conditional on the overflow word
+  if (!two_pass) {
+    fast_init_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, zlab, keep_last, nullptr, flag);
+    PE_LAUNCHED();
+  }
+  for (int64_t r0 = 0; r0 < R && !two_pass; r0 += P.rg) {
+    const int64_t rg = (R - r0) < P.rg ? (R - r0) : P.rg;
+    const void* hg = (const __nv_bfloat16*)h + r0 * ldh;
+    float* dHg = dH + r0 * H;
+    for (int64_t v0 = 0; v0 < V; v0 += VC) {
+      const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
+      const int nt = (int)((vc + kStatTile - 1) / kStatTile);
+      const __nv_bfloat16* Wc = (const __nv_bfloat16*)W + v0 * H;
+      int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Z[0], VC, stats[0], nt_max, status,
+                                    st, P.logits_bn, flag);
+      if (rc) return rc;
+      combine<<<(unsigned)rg, 256, 0, st>>>(vc, v0, nt, nt_max, stats[0], Z[0], VC, labels + r0,
+                                            m + r0, l + r0, zlab + r0, alpha + r0, flag);
+      PE_LAUNCHED();
+      rc = gemm_tc_rowscale_acc(rg, H, vc, Z[0], VC, Wc, H, dHg, H, v0 > 0 ? dHg : nullptr,
+                                alpha + r0, status, st, P.dh_bn, flag);
+      if (rc) return rc;
+    }
+  }
   finalize_kernel<<<1, kThreads, 0, st>>>(R, labels, m, l, zlab, nullptr, nullptr, nullptr, lse,
                                           nullptr, loss_sum);
   PE_LAUNCHED();
-  fast_dh_kernel<<<grid_for(R * H / 8), 256, 0, st>>>(R, H, dH, l, labels, (const __nv_bfloat16*)W,
-                                                      grad_scale, (__nv_bfloat16*)dh, lddh);
+  fast_dh_kernel<<<grid_for(R * H / 8), 256, 0, st>>>(R, H, dH, l, keep_last, labels,
+                                                      (const __nv_bfloat16*)W, grad_scale,
+                                                      (__nv_bfloat16*)dh, lddh);
   PE_LAUNCHED();
   return PE_OK;
 }
