@@ -868,8 +868,8 @@ def run_kernel(args):
         return
     if args.kernel == "lmhead":
         # the fused LM head on all 10240 loss rows of a config-2 sequence (the step's
-        # call), with its logits / dH GEMM tile widths automatic or forced (algo bits
-        # 24-25 / 26-27: 1 = 256-wide, 2 = 512-wide pair tiles)
+        # call): one-pass later chunks (default) against every chunk two-pass (algo bit
+        # 28), at 32K- and 16K-column chunks, and with forced 256-wide logits tiles
         R, H, V = 10240, c["hidden"], c["vocab"]
         g = torch.Generator(device=dev).manual_seed(13)
         h = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
@@ -878,10 +878,9 @@ def run_kernel(args):
         loss = torch.zeros(1, device=dev)
         flops = 2.0 * 2 * R * V * H
         out = {}
-        variants = {"auto": 0, "logits256_dh512": (1 << 24) | (2 << 26),
-                    "logits512_dh512": (2 << 24) | (2 << 26),
-                    "logits256_dh256": (1 << 24) | (1 << 26),
-                    "logits512_dh256": (2 << 24) | (1 << 26)}
+        variants = {"auto": 0, "two_pass": 1 << 28, "chunk16k": 16 << 8,
+                    "chunk16k_two_pass": (16 << 8) | (1 << 28),
+                    "logits256_dh512": (1 << 24) | (2 << 26)}
         runs = {n: (lambda b=b: ops.lmhead_ce(h, W, lab, 1e-4, loss, algo=b))
                 for n, b in variants.items()}
         for name, ms in time_variants(runs, args.steps, warmup=args.warmup).items():
