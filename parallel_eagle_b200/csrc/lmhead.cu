@@ -96,14 +96,15 @@ __global__ void init_stats_kernel(int64_t R, float* m, float* l, float* zlab, fl
   }
 }
 
-// lse per row, loss rows summed in a fixed order by one block
-__global__ void __launch_bounds__(kThreads)
+// lse per row, loss rows summed in a fixed order by one block of 1024 threads
+constexpr int kFinThreads = 1024;
+__global__ void __launch_bounds__(kFinThreads)
 finalize_kernel(int64_t R, const int64_t* labels, const float* m, const float* l, const float* zlab,
                 const float* mt, const float* lt, const float* szt, float* lse, float* lse_t,
                 float* loss_sum) {
-  __shared__ float sh[33];
+  __shared__ float sh[32];
   float acc = 0.f;
-  for (int64_t r = threadIdx.x; r < R; r += kThreads) {
+  for (int64_t r = threadIdx.x; r < R; r += kFinThreads) {
     if (labels && labels[r] < 0) {
       lse[r] = 0.f;
       continue;
@@ -117,8 +118,14 @@ finalize_kernel(int64_t R, const int64_t* labels, const float* m, const float* l
       acc += L - zlab[r];
     }
   }
-  acc = block_reduce(acc, false, sh);
-  if (threadIdx.x == 0) loss_sum[0] += acc;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  acc = warp_sum(acc);
+  if (lane == 0) sh[warp] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    const float t = warp_sum(sh[lane]);
+    if (lane == 0) loss_sum[0] += t;
+  }
 }
 
 template <typename T>
@@ -303,71 +310,76 @@ FastLayout fast_layout_of(int64_t R, int64_t H, int64_t V) {
 // Warp 0 folds the (at most 256) tile stats, lane l taking tiles l, l + 32, ...
 template <int kPer>  // 16-byte loads per thread: vc <= kPer * 256 * 8
 __global__ void __launch_bounds__(256)
-combine_kernel(int64_t vc, int64_t v0, int nt, int stats_ld, const float2* __restrict__ stats,
-               __nv_bfloat16* __restrict__ Z, int64_t ldz, const int64_t* __restrict__ labels,
-               float* m, float* l, float* zlab, float* alpha, const int* run_if) {
+combine_kernel(int64_t R, int64_t vc, int64_t v0, int nt, int stats_ld,
+               const float2* __restrict__ stats, __nv_bfloat16* __restrict__ Z, int64_t ldz,
+               const int64_t* __restrict__ labels, float* m, float* l, float* zlab, float* alpha,
+               const int* run_if) {
+  // a conditional launch (the recomputation after an overflow) has a small grid, so
+  // that skipping it costs little: blocks walk rows r = blockIdx.x, + gridDim.x, ...
   if (run_if != nullptr && *run_if == 0) return;
   __shared__ float s_mnew;
-  const int64_t r = blockIdx.x;
-  const int64_t lab = labels[r];
-  __nv_bfloat16* z = Z + r * ldz;
-  // every thread's share of the row (kPer pieces of 16 B) is loaded before the stats
-  // fold, so all of a row's loads are in flight together: a load-exp-store loop over a
-  // row rewritten in place cannot hoist a load above the previous store, and paid one
-  // DRAM round trip per piece
-  uint4 buf[kPer];
+  for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
+    const int64_t lab = labels[r];
+    __nv_bfloat16* z = Z + r * ldz;
+    // every thread's share of the row (kPer pieces of 16 B) is loaded before the stats
+    // fold, so all of a row's loads are in flight together: a load-exp-store loop over
+    // a row rewritten in place cannot hoist a load above the previous store, and paid
+    // one DRAM round trip per piece
+    uint4 buf[kPer];
 #pragma unroll
-  for (int q = 0; q < kPer; ++q) {
-    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
-    if (c < vc) buf[q] = *reinterpret_cast<const uint4*>(z + c);
-  }
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    const float2* st = stats + r * stats_ld;
-    const float m_old = m[r];
-    // nt <= kPer * 2048 / kStatTile: lane takes tiles lane, lane + 32, ...
-    constexpr int kSv = kPer * 2048 / kStatTile / 32;
-    float2 sv[kSv];
-    float lm = -INFINITY;
-#pragma unroll
-    for (int q = 0; q < kSv; ++q) {
-      const int t = lane + 32 * q;
-      sv[q] = t < nt ? st[t] : make_float2(-INFINITY, 0.f);
-      lm = fmaxf(lm, sv[q].x);
+    for (int q = 0; q < kPer; ++q) {
+      const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+      if (c < vc) buf[q] = *reinterpret_cast<const uint4*>(z + c);
     }
-    const float mn = fmaxf(m_old, warp_max(lm));
-    float part = 0.f;
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      const float2* st = stats + r * stats_ld;
+      const float m_old = m[r];
+      // nt <= kPer * 2048 / kStatTile: lane takes tiles lane, lane + 32, ...
+      constexpr int kSv = kPer * 2048 / kStatTile / 32;
+      float2 sv[kSv];
+      float lm = -INFINITY;
 #pragma unroll
-    for (int q = 0; q < kSv; ++q)
-      if (sv[q].x != -INFINITY) part += sv[q].y * expf(sv[q].x - mn);
-    const float tile_sum = warp_sum(part);
-    if (lane == 0) {
-      const float keep = m_old == -INFINITY ? 0.f : expf(m_old - mn);
-      l[r] = l[r] * keep + tile_sum;
-      alpha[r] = keep;
-      m[r] = mn;
-      if (lab >= v0 && lab < v0 + vc) zlab[r] = __bfloat162float(z[lab - v0]);
-      s_mnew = mn;
-    }
-  }
-  __syncthreads();
-  const float mn = s_mnew;
-  const bool ignored = lab < 0;
-#pragma unroll
-  for (int q = 0; q < kPer; ++q) {
-    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
-    if (c < vc) {
-      uint4 u = buf[q];
-      __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float2 f = __bfloat1622float2(h2[i]);
-        f.x = ignored ? 0.f : __expf(f.x - mn);
-        f.y = ignored ? 0.f : __expf(f.y - mn);
-        h2[i] = __floats2bfloat162_rn(f.x, f.y);
+      for (int q = 0; q < kSv; ++q) {
+        const int t = lane + 32 * q;
+        sv[q] = t < nt ? st[t] : make_float2(-INFINITY, 0.f);
+        lm = fmaxf(lm, sv[q].x);
       }
-      *reinterpret_cast<uint4*>(z + c) = u;
+      const float mn = fmaxf(m_old, warp_max(lm));
+      float part = 0.f;
+#pragma unroll
+      for (int q = 0; q < kSv; ++q)
+        if (sv[q].x != -INFINITY) part += sv[q].y * expf(sv[q].x - mn);
+      const float tile_sum = warp_sum(part);
+      if (lane == 0) {
+        const float keep = m_old == -INFINITY ? 0.f : expf(m_old - mn);
+        l[r] = l[r] * keep + tile_sum;
+        alpha[r] = keep;
+        m[r] = mn;
+        if (lab >= v0 && lab < v0 + vc) zlab[r] = __bfloat162float(z[lab - v0]);
+        s_mnew = mn;
+      }
     }
+    __syncthreads();
+    const float mn = s_mnew;
+    const bool ignored = lab < 0;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+      if (c < vc) {
+        uint4 u = buf[q];
+        __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 f = __bfloat1622float2(h2[i]);
+          f.x = ignored ? 0.f : __expf(f.x - mn);
+          f.y = ignored ? 0.f : __expf(f.y - mn);
+          h2[i] = __floats2bfloat162_rn(f.x, f.y);
+        }
+        *reinterpret_cast<uint4*>(z + c) = u;
+      }
+    }
+    __syncthreads();  // s_mnew is rewritten for the next row
   }
 }
 
@@ -592,7 +604,7 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
         if (rc) return rc;
         PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
         PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
-        combine<<<(unsigned)rg, 256, 0, side>>>(vc, v0, nt, nt_max, stats[b], Z[b], VC,
+        combine<<<(unsigned)rg, 256, 0, side>>>(rg, vc, v0, nt, nt_max, stats[b], Z[b], VC,
                                                 labels + r0, m + r0, l + r0, zlab + r0,
                                                 alpha + r0, nullptr);
         PE_LAUNCHED();
@@ -647,15 +659,16 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
       int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Z[0], VC, stats[0], nt_max, status,
                                     st, P.logits_bn, flag);
       if (rc) return rc;
-      combine<<<(unsigned)rg, 256, 0, st>>>(vc, v0, nt, nt_max, stats[0], Z[0], VC, labels + r0,
-                                            m + r0, l + r0, zlab + r0, alpha + r0, flag);
+      combine<<<(unsigned)(rg < 2 * sm_count() ? rg : 2 * sm_count()), 256, 0, st>>>(
+          rg, vc, v0, nt, nt_max, stats[0], Z[0], VC, labels + r0, m + r0, l + r0, zlab + r0,
+          alpha + r0, flag);
       PE_LAUNCHED();
       rc = gemm_tc_rowscale_acc(rg, H, vc, Z[0], VC, Wc, H, dHg, H, v0 > 0 ? dHg : nullptr,
                                 alpha + r0, status, st, P.dh_bn, flag);
       if (rc) return rc;
     }
   }
-  finalize_kernel<<<1, kThreads, 0, st>>>(R, labels, m, l, zlab, nullptr, nullptr, nullptr, lse,
+  finalize_kernel<<<1, kFinThreads, 0, st>>>(R, labels, m, l, zlab, nullptr, nullptr, nullptr, lse,
                                           nullptr, loss_sum);
   PE_LAUNCHED();
   fast_dh_kernel<<<grid_for(R * H / 8), 256, 0, st>>>(R, H, dH, l, keep_last, labels,
@@ -916,7 +929,7 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
   }
   PE_CUDA_TRY(cudaEventRecord(ev_join, side));
   PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_join, 0));
-  finalize_kernel<<<1, kThreads, 0, st>>>(R, nullptr, m, l, zlab, mt, lt, szt, lse, lse_t,
+  finalize_kernel<<<1, kFinThreads, 0, st>>>(R, nullptr, m, l, zlab, mt, lt, szt, lse, lse_t,
                                           loss_sum);
   PE_LAUNCHED();
   soft_dh_kernel<<<grid_for(R * H / 8), 256, 0, st>>>(R, H, dHs, dHt, l, lt, grad_scale,
@@ -1009,7 +1022,7 @@ extern "C" int pe_lmhead_ce(int dtype, int64_t R, int64_t H, int64_t V, const vo
     });
     if (rc) return rc;
   }
-  finalize_kernel<<<1, kThreads, 0, st>>>(R, lab, m, l, zlab, mt, lt, szt, lse, lse_t, loss_sum);
+  finalize_kernel<<<1, kFinThreads, 0, st>>>(R, lab, m, l, zlab, mt, lt, szt, lse, lse_t, loss_sum);
   PE_LAUNCHED();
   for (int64_t v0 = 0; v0 < V; v0 += VC) {
     const int64_t vc = (V - v0) < VC ? (V - v0) : VC;

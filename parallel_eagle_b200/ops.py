@@ -90,6 +90,7 @@ def rmsnorm_bwd(dy, x, w, rstd, dx=None, residual=None, want_dw: bool = True):
 
 def colsum_into(partial: torch.Tensor, out: torch.Tensor, accumulate: bool) -> torch.Tensor:
     """``out (+)= partial.sum(0)`` with a fixed summation order."""
+    L.require_cuda(partial, out)
     nblk, H = partial.shape
     rc = _lib().pe_colsum_f32(
         L.dtype_code(out.dtype), nblk, H, partial.data_ptr(), out.data_ptr(), int(accumulate),
@@ -523,6 +524,7 @@ def lmhead_ce(h, W, labels, grad_scale, loss_sum, teacher=None, dh=None, algo=L.
 
 
 def embed_rows(ids, embed, out):
+    L.require_cuda(ids, embed, out)
     rows, H = ids.shape[0], embed.shape[1]
     rc = _lib().pe_embed_rows(L.dtype_code(embed.dtype), rows, H, ids.data_ptr(), embed.data_ptr(),
                               out.data_ptr(), _row_stride(out), L.stream_ptr(out.device))
@@ -531,6 +533,7 @@ def embed_rows(ids, embed, out):
 
 
 def fill_rows(vec, out):
+    L.require_cuda(vec, out)
     rows, H = out.shape
     rc = _lib().pe_fill_rows(L.dtype_code(out.dtype), rows, H, vec.data_ptr(), out.data_ptr(),
                              _row_stride(out), L.stream_ptr(out.device))
@@ -539,6 +542,7 @@ def fill_rows(vec, out):
 
 
 def swiglu_fwd(gu, inter, out=None):
+    L.require_cuda(gu, out)
     rows = gu.shape[0]
     if out is None:
         out = torch.empty(rows, inter, dtype=gu.dtype, device=gu.device)
@@ -549,6 +553,7 @@ def swiglu_fwd(gu, inter, out=None):
 
 
 def swiglu_bwd(da, gu, inter, out=None):
+    L.require_cuda(da, gu, out)
     rows = gu.shape[0]
     if out is None:
         out = torch.empty(rows, 2 * inter, dtype=gu.dtype, device=gu.device)
@@ -560,6 +565,7 @@ def swiglu_bwd(da, gu, inter, out=None):
 
 
 def rowsum_cols(x, out=None):
+    L.require_cuda(x, out)
     rows, H = x.shape
     if out is None:
         out = torch.empty(H, dtype=torch.float32, device=x.device)
@@ -572,6 +578,7 @@ def rowsum_cols(x, out=None):
 def rowsum_cols_ranges(x, ranges, out=None):
     """fp32 ``[H]`` column sums of ``x`` over the row ranges ``[(begin, end), ...]``
     (host ints), in a fixed order: one launch per 16 ranges."""
+    L.require_cuda(x, out)
     rows, H = x.shape
     ranges = [(int(b), int(e)) for b, e in ranges]
     if not ranges:
@@ -600,6 +607,7 @@ def rowsum_cols_ranges(x, ranges, out=None):
 
 
 def gather_rows(src, idx, out=None):
+    L.require_cuda(src, idx, out)
     rows, H = idx.shape[0], src.shape[1]
     if out is None:
         out = torch.empty(rows, H, dtype=src.dtype, device=src.device)
@@ -611,6 +619,7 @@ def gather_rows(src, idx, out=None):
 
 
 def scatter_rows(src, idx, out):
+    L.require_cuda(src, idx, out)
     rows, H = src.shape
     rc = _lib().pe_scatter_rows(L.dtype_code(src.dtype), rows, H, idx.data_ptr(), src.data_ptr(),
                                 _row_stride(src), out.data_ptr(), _row_stride(out),
@@ -620,6 +629,7 @@ def scatter_rows(src, idx, out):
 
 
 def cast_from_f32(x, out):
+    L.require_cuda(x, out)
     rc = _lib().pe_cast_f32(L.dtype_code(out.dtype), x.numel(), x.data_ptr(), out.data_ptr(),
                             L.stream_ptr(x.device))
     L.check(rc, "pe_cast_f32")
@@ -632,6 +642,7 @@ _SUMSQ_BLOCKS = 1024  # fixed, so the partials (and the sum) do not depend on th
 def sumsq_into(g, out):
     """``out[0] += sum(g ** 2)``, deterministic: the same gradient gives the same bits on
     every run and every data-parallel rank (fixed-grid partials, fixed-order sum)."""
+    L.require_cuda(g, out)
     lib = _lib()
     stream = L.stream_ptr(g.device)
     part = _workspace(g.device, _SUMSQ_BLOCKS * 4, "sumsq").view(torch.float32)[:_SUMSQ_BLOCKS]
@@ -644,6 +655,7 @@ def sumsq_into(g, out):
 
 
 def adamw_step(p, g, m, v, sumsq, max_norm, lr, beta1, beta2, eps, weight_decay, step):
+    L.require_cuda(p, g, m, v, sumsq)
     rc = _lib().pe_adamw_step(L.dtype_code(p.dtype), p.numel(), p.data_ptr(), g.data_ptr(),
                               m.data_ptr(), v.data_ptr(), L.ptr(sumsq), float(max_norm), float(lr),
                               float(beta1), float(beta2), float(eps), float(weight_decay), int(step),

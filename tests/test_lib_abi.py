@@ -77,3 +77,40 @@ def test_segment_attention_and_topk_validate_before_any_cuda_call():
     assert lib.pe_softmax_rows(bf16, 2, 7, None, 6, 1.0, None, 7, None) != 0
     assert lib.pe_softmax_rows(bf16, 2, 7, None, 7, 1.0, None, 6, None) != 0
     assert lib.pe_softmax_rows(bf16, 0, 7, None, 7, 0.7, None, 7, None) == 0
+
+
+def test_ops_reject_host_tensors_before_any_kernel():
+    """Every Python wrapper raises PeError for a tensor in host memory instead of
+    handing its address to a kernel (there is no CPU fallback); the C side's range
+    checks of the multi-range column sum also run before any launch."""
+    import pytest
+    import torch
+
+    from parallel_eagle_b200 import _lib, ops
+
+    x = torch.zeros(4, 16, dtype=torch.bfloat16)
+    idx = torch.zeros(2, dtype=torch.long)
+    f32 = torch.zeros(16, dtype=torch.float32)
+    calls = [
+        lambda: ops.rowsum_cols(x),
+        lambda: ops.rowsum_cols_ranges(x, [(0, 2)]),
+        lambda: ops.swiglu_fwd(x, 8),
+        lambda: ops.swiglu_bwd(x[:, :8], x, 8),
+        lambda: ops.gather_rows(x, idx),
+        lambda: ops.scatter_rows(x[:2], idx, x),
+        lambda: ops.fill_rows(x[0], x),
+        lambda: ops.cast_from_f32(f32, x[0]),
+        lambda: ops.sumsq_into(x, f32[:1]),
+        lambda: ops.colsum_into(f32.view(1, 16), f32, False),
+        lambda: ops.linear_swiglu_bwd(x, x[:, :8].t().contiguous(), x, 8),
+    ]
+    for call in calls:
+        with pytest.raises(_lib.PeError, match="CUDA tensors only"):
+            call()
+    lib = _lib.load()
+    import numpy as np
+
+    bad = np.array([5, 3], dtype=np.int64)  # end before begin
+    assert lib.pe_rowsum_cols_ranges(1, 1, bad.ctypes.data, 16, None, 16, None, None) != 0
+    assert b"range 0" in lib.pe_last_error()
+    assert lib.pe_rowsum_cols_ranges(1, 17, bad.ctypes.data, 16, None, 16, None, None) != 0
