@@ -726,6 +726,12 @@ AB_VARIANTS = {
     "lmhead_chunk24k": {"lmhead_algo": 24 << 8},
     # every vocabulary chunk two-pass (logits stored, then rewritten as exponentials)
     "lmhead_two_pass": {"lmhead_algo": 1 << 28},
+    # 256-wide CTA-pair tiles (two TMEM accumulators, epilogue hidden) instead of the
+    # automatic 512 for the long-K MLP GEMMs / every weight gradient
+    "mlp_tiles256": {"gemm_algo": {"dn_fwd": 256 << 8, "gu_dgrad": 256 << 8,
+                                   "gu_wgrad": 256 << 8, "dn_wgrad": 256 << 8}},
+    "wgrad_tiles256": {"gemm_algo": {"gu_wgrad": 256 << 8, "dn_wgrad": 256 << 8,
+                                     "o_wgrad": 256 << 8, "qkv_wgrad": 256 << 8}},
 }
 
 
@@ -753,7 +759,8 @@ def run_ab(args):
     names = [v for v in args.ab.split(",") if v]
     eng = trainer.eng
     defaults = {key: getattr(eng, key)
-                for key in ("fuse_rope", "fuse_swiglu", "fuse_swiglu_bwd", "lmhead_algo")}
+                for key in ("fuse_rope", "fuse_swiglu", "fuse_swiglu_bwd", "lmhead_algo",
+                            "gemm_algo")}
 
     def use(name):
         for key, val in defaults.items():

@@ -178,6 +178,10 @@ class StepEngine:
         self.fuse_swiglu = True
         self.fuse_swiglu_bwd = False
         self.lmhead_algo = 0
+        # per-call-site GEMM tuning bits (pe_gemm's algo: tile width, tile order), keyed
+        # "dn_fwd", "gu_dgrad", "gu_wgrad", "dn_dgrad", "dn_wgrad", "o_fwd", "o_dgrad",
+        # "o_wgrad", "qkv_dgrad", "qkv_wgrad"; empty = automatic everywhere
+        self.gemm_algo = {}
 
     # --------------------------------------------------------------- plans --
     def _segment_arrays(self, a0: int, a1: int, n: int, prompt_len: int):
@@ -320,6 +324,7 @@ class StepEngine:
         d, fp = self.d, self.flat
         dt, dev = fp.dtype, fp.device
         H, I = d.hidden, d.intermediate
+        ga = self.gemm_algo.get
         nh, nkv, hd = d.n_heads, d.n_kv_heads, d.head_dim
         qc, kc = nh * hd, nkv * hd
         cqkv = qc + 2 * kc
@@ -395,7 +400,7 @@ class StepEngine:
                 ops.rope_(qkv, nh + nkv, hd, plan.pos, d.rope_theta)
             o, lse = ops.attn_fwd_segments(qkv[:, :qc], qkv[:, qc : qc + kc], qkv[:, qc + kc :],
                                            nh, nkv, hd, bounds, k)
-            x2 = ops.linear(o, w_o, residual=x)
+            x2 = ops.linear(o, w_o, residual=x, algo=ga("o_fwd", 0))
             xn2, r2 = ops.rmsnorm_fwd(x2, W(p + "post_norm.weight"), eps)
             if self.fuse_swiglu:
                 # the activation in the gate|up GEMM epilogue (gate|up kept for backward)
@@ -403,7 +408,7 @@ class StepEngine:
             else:
                 gu = ops.linear(xn2, w_gu)
                 act = ops.swiglu_fwd(gu, I)
-            x3 = ops.linear(act, w_dn, residual=x2)
+            x3 = ops.linear(act, w_dn, residual=x2, algo=ga("dn_fwd", 0))
             saved.append((x, xn, r1, qkv, o, lse, x2, xn2, r2, gu, act))
             x = x3
         hf, rf = ops.rmsnorm_fwd(x, wfinal, eps)
@@ -437,18 +442,21 @@ class StepEngine:
             if self.fuse_swiglu_bwd:
                 dgu = ops.linear_swiglu_bwd(dx, w_dn, gu, I)
             else:
-                dgu = ops.swiglu_bwd(ops.linear_dgrad(dx, w_dn), gu, I)
-            ops.linear_wgrad(dx, act, grad=G(p + "mlp.down_proj.weight", (H, I)), accumulate=True)
-            dxn2 = ops.linear_dgrad(dgu, w_gu)
+                dgu = ops.swiglu_bwd(ops.linear_dgrad(dx, w_dn, algo=ga("dn_dgrad", 0)), gu, I)
+            ops.linear_wgrad(dx, act, grad=G(p + "mlp.down_proj.weight", (H, I)), accumulate=True,
+                             algo=ga("dn_wgrad", 0))
+            dxn2 = ops.linear_dgrad(dgu, w_gu, algo=ga("gu_dgrad", 0))
             ops.linear_wgrad(
                 dgu, xn2, accumulate=True,
                 grad=fp.span(p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight", H, grad=True),
+                algo=ga("gu_wgrad", 0),
             )
             dx2, part = ops.rmsnorm_bwd(dxn2, x2, W(p + "post_norm.weight"), r2, residual=dx)
             ops.colsum_into(part, G(p + "post_norm.weight"), accumulate=True)
             # x2 = x + o @ W_o^T
-            do = ops.linear_dgrad(dx2, w_o)
-            ops.linear_wgrad(dx2, o, grad=G(p + "attn.o_proj.weight", (H, qc)), accumulate=True)
+            do = ops.linear_dgrad(dx2, w_o, algo=ga("o_dgrad", 0))
+            ops.linear_wgrad(dx2, o, grad=G(p + "attn.o_proj.weight", (H, qc)), accumulate=True,
+                             algo=ga("o_wgrad", 0))
             dqkv = torch.empty(Q, cqkv, dtype=dt, device=dev)
             ops.attn_bwd_segments(qkv[:, :qc], qkv[:, qc : qc + kc], qkv[:, qc + kc :], o, do, lse,
                                   nh, nkv, hd, bounds, k, dq=dqkv[:, :qc],
@@ -456,10 +464,11 @@ class StepEngine:
                                   rope_cs=rope_cs)
             if not fuse_rope:
                 ops.rope_(dqkv, nh + nkv, hd, plan.pos, d.rope_theta, inverse=True)
-            dxn = ops.linear_dgrad(dqkv, w_qkv)
+            dxn = ops.linear_dgrad(dqkv, w_qkv, algo=ga("qkv_dgrad", 0))
             ops.linear_wgrad(
                 dqkv, xn, accumulate=True,
                 grad=fp.span(p + "attn.q_proj.weight", p + "attn.v_proj.weight", H, grad=True),
+                algo=ga("qkv_wgrad", 0),
             )
             dx, part = ops.rmsnorm_bwd(dxn, x_in, W(p + "input_norm.weight"), r1, residual=dx2)
             ops.colsum_into(part, G(p + "input_norm.weight"), accumulate=True)
