@@ -253,9 +253,9 @@ int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth,
  *   loss_sum[0] += sum_r loss_r;  dh = grad_scale * d(sum_r loss_r)/dh
  * Rows with label < 0 are ignored.  No gradient reaches W (frozen).
  * For the bf16 paths, algo bits 8-15 set the vocabulary chunk (units of 1024 rows
- * of W, at most 32 with hard labels and 16 with teacher rows) and bits 16-23 the
- * loss-row group (units of 256 rows, at most 40); zero keeps the defaults (32768,
- * 16384 with teacher rows, and 10240).  Bits 24-25 / 26-27 pick the logits / dH GEMM
+ * of W, at most 32) and bits 16-23 the
+ * loss-row group (units of 256 rows, at most 40); zero keeps the defaults (32768
+ * and 10240).  Bits 24-25 / 26-27 pick the logits / dH GEMM
  * tile width (1: 256, 2: 512, 0: automatic).  With hard labels, every vocabulary
  * chunk after a row group's first is one pass (the logits GEMM writes e^(z - running
  * max) directly; a logit more than 64 above its row's running maximum makes the call

@@ -225,7 +225,7 @@ unsigned grid_for(int64_t n) {
 namespace pe {
 namespace {
 
-// vocabulary rows per logits chunk (default; the soft-target path caps it at 16K):
+// vocabulary rows per logits chunk (default, both paths):
 // each chunk ends with a read-modify-write of the fp32 dH accumulator (R x H) in the
 // dH GEMM's epilogue, which a 512-wide tile cannot hide, so fewer, longer chunks pay
 // it less often.  Measured on the config-2 training step (interleaved A/B, 6 rounds):
@@ -240,11 +240,11 @@ constexpr int64_t kFastChunk = 32768;
 // slower than 2 x 5120 for the call alone.
 constexpr int64_t kRowGroup = 10240;
 constexpr int64_t kMaxChunk = 32768;      // hard-label path
-constexpr int64_t kMaxChunkSoft = 16384;  // soft-target path (two logits chunks per step)
+constexpr int64_t kMaxChunkSoft = 32768;  // soft-target path (two logits chunks per step)
 constexpr int64_t kMaxGroup = 10240;
 constexpr int kStatTile = 128;  // columns per (max, sum-exp) pair of the logits GEMM
 static_assert(kMaxChunk <= 16 * 256 * 8, "combine_kernel<16> covers at most 32K columns");
-static_assert(kMaxChunkSoft / kStatTile <= 128, "fold_stats folds at most 128 tile stats");
+static_assert(kMaxChunkSoft <= 512 * 64, "combine_soft_kernel<512> covers at most 32K columns");
 
 // Rows of the loss are processed in groups, which bounds the logits chunk (group x
 // chunk bf16) held between the logits GEMM, the combine pass and the dH GEMM.  ``algo`` bits 8-15 override the chunk (units of
@@ -727,14 +727,15 @@ SoftLayout soft_layout_of(int64_t R, int64_t H, int64_t V) {
   return L;
 }
 
-// fold one chunk's tile stats (at most 128 tiles, lane takes tiles lane + 32 q) into
+// fold one chunk's tile stats (at most 32 kSv tiles, lane takes tiles lane + 32 q) into
 // a running (m, l); returns the new maximum, writes l and the rescale factor
+template <int kSv>
 __device__ __forceinline__ float fold_stats(const float2* st, int nt, float* m, float* l,
                                             float* alpha, int lane) {
-  float2 sv[4];
+  float2 sv[kSv];
   float lm = -INFINITY;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < kSv; ++q) {
     const int t = lane + 32 * q;
     sv[q] = t < nt ? st[t] : make_float2(-INFINITY, 0.f);
     lm = fmaxf(lm, sv[q].x);
@@ -743,7 +744,7 @@ __device__ __forceinline__ float fold_stats(const float2* st, int nt, float* m, 
   const float mn = fmaxf(m_old, warp_max(lm));
   float part = 0.f;
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
+  for (int q = 0; q < kSv; ++q)
     if (sv[q].x != -INFINITY) part += sv[q].y * expf(sv[q].x - mn);
   const float tile_sum = warp_sum(part);
   const float keep = m_old == -INFINITY ? 0.f : expf(m_old - mn);
@@ -755,34 +756,40 @@ __device__ __forceinline__ float fold_stats(const float2* st, int nt, float* m, 
   return __shfl_sync(0xffffffffu, mn, 0);
 }
 
-__global__ void __launch_bounds__(256)
+// kT threads per row (256 or 512), eight 16-byte pieces of each row per thread: chunks
+// of up to kT * 64 columns (16K or 32K)
+template <int kT>
+__global__ void __launch_bounds__(kT)
 combine_soft_kernel(int64_t vc, int nt, int stats_ld, const float2* __restrict__ stats_s,
                     const float2* __restrict__ stats_t, __nv_bfloat16* __restrict__ Zs,
                     __nv_bfloat16* __restrict__ Zt, int64_t ldz, float* m, float* l,
                     float* alpha, float* mt, float* lt, float* szt, float* alpha_t) {
   __shared__ float s_m[2];
-  __shared__ float s_red[8];
+  constexpr int kWarps = kT / 32;
+  constexpr int kSv = kT * 64 / kStatTile / 32;  // tile stats per lane
+  __shared__ float s_red[kWarps];
   const int64_t r = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __nv_bfloat16* zs = Zs + r * ldz;
   __nv_bfloat16* zt = Zt + r * ldz;
   // the thread's share of both rows is loaded before the stats folds (all loads of the
   // rows in flight together; see combine_kernel)
-  constexpr int kPer = (int)(kMaxChunkSoft / (256 * 8));
+  constexpr int kPer = 8;
   uint4 bs[kPer], bt[kPer];
 #pragma unroll
   for (int q = 0; q < kPer; ++q) {
-    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * kT) * 8;
     if (c < vc) {
       bs[q] = *reinterpret_cast<const uint4*>(zs + c);
       bt[q] = *reinterpret_cast<const uint4*>(zt + c);
     }
   }
   if (warp == 0) {
-    const float ms = fold_stats(stats_s + r * stats_ld, nt, m + r, l + r, alpha + r, lane);
+    const float ms = fold_stats<kSv>(stats_s + r * stats_ld, nt, m + r, l + r, alpha + r, lane);
     if (lane == 0) s_m[0] = ms;
   } else if (warp == 1) {
-    const float mtn = fold_stats(stats_t + r * stats_ld, nt, mt + r, lt + r, alpha_t + r, lane);
+    const float mtn =
+        fold_stats<kSv>(stats_t + r * stats_ld, nt, mt + r, lt + r, alpha_t + r, lane);
     if (lane == 0) s_m[1] = mtn;
   }
   __syncthreads();
@@ -790,7 +797,7 @@ combine_soft_kernel(int64_t vc, int nt, int stats_ld, const float2* __restrict__
   float acc = 0.f;
 #pragma unroll
   for (int q = 0; q < kPer; ++q) {
-    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * 256) * 8;
+    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * kT) * 8;
     if (c >= vc) continue;
     uint4 us = bs[q];
     uint4 ut = bt[q];
@@ -813,7 +820,7 @@ combine_soft_kernel(int64_t vc, int nt, int stats_ld, const float2* __restrict__
   if (threadIdx.x == 0) {
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) t += s_red[w];
+    for (int w = 0; w < kWarps; ++w) t += s_red[w];
     szt[r] = szt[r] * alpha_t[r] + t;
   }
 }
@@ -912,9 +919,14 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
       if (rc) return rc;
       PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
       PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
-      combine_soft_kernel<<<(unsigned)rg, 256, 0, side>>>(vc, nt, nt_max, ss, stt, Zs, Zt, VC,
-                                                          m + r0, l + r0, alpha + r0, mt + r0,
-                                                          lt + r0, szt + r0, alpha_t + r0);
+      if (VC <= 16384)
+        combine_soft_kernel<256><<<(unsigned)rg, 256, 0, side>>>(
+            vc, nt, nt_max, ss, stt, Zs, Zt, VC, m + r0, l + r0, alpha + r0, mt + r0, lt + r0,
+            szt + r0, alpha_t + r0);
+      else
+        combine_soft_kernel<512><<<(unsigned)rg, 512, 0, side>>>(
+            vc, nt, nt_max, ss, stt, Zs, Zt, VC, m + r0, l + r0, alpha + r0, mt + r0, lt + r0,
+            szt + r0, alpha_t + r0);
       PE_LAUNCHED();
       rc = gemm_tc_rowscale_acc(rg, H, vc, Zs, VC, Wc, H, dHs + r0 * H, H,
                                 v0 > 0 ? dHs + r0 * H : nullptr, alpha + r0, status, side,
