@@ -568,6 +568,27 @@ def test_lmhead_ce_row_groups_and_chunks(chunk_k, group_r, two_pass):
     assert rel(dh.float().cpu(), hr.grad) < 2e-2
 
 
+@pytest.mark.parametrize("chunk_k", [0, 16, 8])
+def test_lmhead_soft_targets_across_chunk_widths(chunk_k):
+    """Soft-target loss over 40000 vocabulary rows in 32K (default; the 512-thread combine),
+    16K or 8K chunks (the 256-thread one): same loss and gradient as dense fp32 torch."""
+    R, H, V = 600, 256, 40000
+    h = _rand(R, H, seed=45)
+    W = _rand(V, H, seed=46, scale=0.05)
+    teacher = _rand(R, H, seed=47)
+    loss = torch.zeros(1, dtype=torch.float32, device=DEV)
+    dh = ops.lmhead_ce(h, W, None, 0.5, loss, teacher=teacher, algo=L.ALGO_AUTO | (chunk_k << 8))
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    hr = h.float().cpu().requires_grad_(True)
+    z = (hr @ W.float().cpu().t()).bfloat16().float()
+    pt = torch.softmax((teacher.float().cpu() @ W.float().cpu().t()).bfloat16().float(), -1)
+    lr = -(pt * torch.log_softmax(z, -1)).sum()
+    (lr * 0.5).backward()
+    assert abs(loss.item() - lr.item()) / abs(lr.item()) < 1e-4
+    assert rel(dh.float().cpu(), hr.grad) < 2e-2
+
+
 @pytest.mark.parametrize("boost", [40.0, 150.0])
 def test_lmhead_ce_late_chunk_maximum(boost):
     """Rows whose largest logit lies in a late vocabulary chunk, far above the first
