@@ -128,6 +128,16 @@ class ClockSampler:
 # --------------------------------------------------------------------------- #
 
 
+def smi_index(local: int) -> int:
+    """nvidia-smi's index of CUDA device ``local``: CUDA_VISIBLE_DEVICES, when it lists
+    plain indices, renumbers the devices this process sees, nvidia-smi does not."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    ids = [x.strip() for x in vis.split(",") if x.strip()]
+    if ids and all(x.isdigit() for x in ids) and local < len(ids):
+        return int(ids[local])
+    return local
+
+
 def _dist():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -286,7 +296,7 @@ def run_ours(args):
     trainer.record_comm = True
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(smi_index(local)) as clocks:
         e0.record(stream)
         for _ in range(args.steps):
             # the NVTX range lets a profiler select exactly the timed steps' launches

@@ -289,3 +289,18 @@ def test_speculative_sampling_acceptance_is_lossless():
         counts[acc[0] if acc else bonus] += 1
     tv = 0.5 * (counts / trials - p[0]).abs().sum().item()
     assert tv < 0.03, tv
+
+
+def test_clock_sampler_follows_cuda_visible_devices(monkeypatch):
+    """The bench samples the clocks of the GPU it runs on: nvidia-smi numbers GPUs
+    physically, CUDA after CUDA_VISIBLE_DEVICES."""
+    import bench
+
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "6")
+    assert bench.smi_index(0) == 6
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "2,3,4,5")
+    assert [bench.smi_index(i) for i in range(4)] == [2, 3, 4, 5]
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert bench.smi_index(3) == 3
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "GPU-5f1c")  # UUIDs: left to the index
+    assert bench.smi_index(0) == 0
