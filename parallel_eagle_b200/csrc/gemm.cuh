@@ -32,7 +32,8 @@ int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t
 
 // The same logits written as P = e^(z - rowref[row]) (bf16; 0 for rows whose label is
 // negative) with per-128-column (max z, sum P) pairs, the label logit z[labels[r] -
-// label_v0] of rows whose label falls in these columns, and *overflow = 1 when some z
+// label_v0] of rows whose label falls in these columns (labels may be null: no row
+// ignored, no label logit), and *overflow = 1 when some z
 // exceeds its row's reference by more than 64 (P would leave the fp32 range).
 int gemm_tc_logits_pexp(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
                         const void* B, int64_t ldb, void* P, int64_t ldp, float2* stats,

@@ -462,10 +462,11 @@ __device__ __forceinline__ void epilogue_cols(uint32_t acc_tmem, int c_begin, in
   bool p_skip = true;
   if constexpr (EPI == EPI_PEXP) {
     if (gm < M) {
-      const int64_t lab = ea.labels[gm];
+      // without labels (soft targets) no row is ignored and no label logit is taken
+      const int64_t lab = ea.labels ? ea.labels[gm] : -1;
       p_ref = ea.rowref[gm];
-      p_skip = lab < 0;
-      lab_col = lab - ea.label_v0;
+      p_skip = ea.labels != nullptr && lab < 0;
+      lab_col = ea.labels ? lab - ea.label_v0 : -1;
     }
   }
   const uint64_t pol_ef = ea.store_hint ? l2_evict_first_policy() : 0ull;
@@ -1208,9 +1209,9 @@ int gemm_tc_logits_stats(int64_t M, int64_t N, int64_t K, const void* A, int64_t
 
 // P = e^(round(h W^T) - rowref[row]) (bf16; 0 for rows with a negative label), the
 // per-128-column (max logit, sum P) pairs, the label logit of the rows whose label
-// falls in these N columns (labels[r] - label_v0), and *overflow = 1 when a logit
-// exceeds its row's reference by more than kPexpMargin.  Tiles as the logits + stats
-// GEMM.
+// falls in these N columns (labels[r] - label_v0; labels may be null: soft targets),
+// and *overflow = 1 when a logit exceeds its row's reference by more than
+// kPexpMargin.  Tiles as the logits + stats GEMM.
 int gemm_tc_logits_pexp(int64_t M, int64_t N, int64_t K, const void* A, int64_t lda,
                         const void* B, int64_t ldb, void* P, int64_t ldp, float2* stats,
                         int stats_ld, const float* rowref, const int64_t* labels,
@@ -1220,9 +1221,9 @@ int gemm_tc_logits_pexp(int64_t M, int64_t N, int64_t K, const void* A, int64_t 
                    al16(A) && al16(B) && al16(P),
                "gemm (logits -> exponentials): operands must be 16-byte aligned bf16");
   PE_CHECK_ARG(stats_ld >= (N + 127) / 128, "gemm (logits -> exponentials): stats_ld too small");
-  PE_CHECK_ARG(rowref && labels && zlab && overflow,
-               "gemm (logits -> exponentials): reference, labels, label logits and overflow "
-               "word are required");
+  PE_CHECK_ARG(rowref && overflow && (labels == nullptr || zlab != nullptr),
+               "gemm (logits -> exponentials): the reference, the overflow word and, with "
+               "labels, the label-logit output are required");
   PE_CHECK_ARG(force_bn == 0 || force_bn == 256 || force_bn == 512,
                "gemm (logits -> exponentials): tile width %d not 256 or 512", force_bn);
   const bool pair = use_pair(M, 0);

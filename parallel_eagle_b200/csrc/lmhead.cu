@@ -81,6 +81,24 @@ stats_kernel(int64_t vc, int64_t v0, const float* __restrict__ Z, const float* _
   }
 }
 
+// soft-target running stats reset (both rows' (m, l), S_tz, the last rescale factors);
+// `flag` (when non-null) clears the overflow word, `run_if` makes the launch conditional
+__global__ void soft_init_kernel(int64_t R, float* m, float* l, float* mt, float* lt, float* szt,
+                                 float* ks, float* kt, int* flag, const int* run_if) {
+  if (run_if != nullptr && *run_if == 0) return;
+  if (flag != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *flag = 0;
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < R;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+    mt[r] = -INFINITY;
+    lt[r] = 0.f;
+    szt[r] = 0.f;
+    ks[r] = 1.f;
+    kt[r] = 1.f;
+  }
+}
+
 __global__ void init_stats_kernel(int64_t R, float* m, float* l, float* zlab, float* mt, float* lt,
                                   float* szt) {
   for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < R;
@@ -425,7 +443,7 @@ fold_first_kernel(int64_t R, int64_t vc, int nt, int stats_ld, const float2* __r
     l[r] = sum;
     keep[r] = 1.f;
     keep_last[r] = 1.f;
-    const int64_t lab = labels[r];
+    const int64_t lab = labels ? labels[r] : -1;  // soft targets: no labels
     if (lab >= 0 && lab < vc) zlab[r] = __bfloat162float(Z[r * ldz + lab]);
   }
 }
@@ -438,7 +456,7 @@ exp_first_kernel(int64_t vc, __nv_bfloat16* __restrict__ Z, int64_t ldz,
                  const int64_t* __restrict__ labels, const float* __restrict__ m0) {
   const int64_t r = blockIdx.x;
   __nv_bfloat16* z = Z + r * ldz;
-  const bool ignored = labels[r] < 0;
+  const bool ignored = labels != nullptr && labels[r] < 0;
   const float mx = m0[r];
   uint4 buf[kPer];
 #pragma unroll
@@ -690,8 +708,8 @@ int lmhead_fast(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, con
 // Four GEMMs per chunk, every logits chunk bf16 and L2-sized, one pass over W.
 // ------------------------------------------------------------------------ //
 struct SoftLayout {
-  size_t m, l, zlab, lse, alpha, mt, lt, szt, alpha_t, lse_t, stats_s[2], stats_t[2], Zs[2],
-      Zt[2], dHs, dHt, total;
+  size_t m, l, zlab, lse, alpha, mt, lt, szt, alpha_t, lse_t, keep_s[3], keep_t[3], keep_last_s,
+      keep_last_t, m0_s, m0_t, flag, stats_s[2], stats_t[2], Zs[2], Zt[2], dHs, dHt, total;
 };
 
 SoftLayout soft_layout_of(int64_t R, int64_t H, int64_t V) {
@@ -715,6 +733,15 @@ SoftLayout soft_layout_of(int64_t R, int64_t H, int64_t V) {
   L.szt = take(4 * R);
   L.alpha_t = take(4 * R);
   L.lse_t = take(4 * R);
+  for (int b = 0; b < 3; ++b) {
+    L.keep_s[b] = take(4 * R);
+    L.keep_t[b] = take(4 * R);
+  }
+  L.keep_last_s = take(4 * R);
+  L.keep_last_t = take(4 * R);
+  L.m0_s = take(4 * R);
+  L.m0_t = take(4 * R);
+  L.flag = take(4);
   for (int b = 0; b < 2; ++b) {
     L.stats_s[b] = take(8 * (size_t)rg * nt);
     L.stats_t[b] = take(8 * (size_t)rg * nt);
@@ -757,85 +784,120 @@ __device__ __forceinline__ float fold_stats(const float2* st, int nt, float* m, 
 }
 
 // kT threads per row (256 or 512), eight 16-byte pieces of each row per thread: chunks
-// of up to kT * 64 columns (16K or 32K)
+// of up to kT * 64 columns (16K or 32K).  Blocks walk rows r = blockIdx.x, + gridDim.x,
+// ... (the conditional recomputation after an overflow runs with a small grid and
+// returns at once unless *run_if is set).
 template <int kT>
 __global__ void __launch_bounds__(kT)
-combine_soft_kernel(int64_t vc, int nt, int stats_ld, const float2* __restrict__ stats_s,
-                    const float2* __restrict__ stats_t, __nv_bfloat16* __restrict__ Zs,
-                    __nv_bfloat16* __restrict__ Zt, int64_t ldz, float* m, float* l,
-                    float* alpha, float* mt, float* lt, float* szt, float* alpha_t) {
+combine_soft_kernel(int64_t R, int64_t vc, int nt, int stats_ld,
+                    const float2* __restrict__ stats_s, const float2* __restrict__ stats_t,
+                    __nv_bfloat16* __restrict__ Zs, __nv_bfloat16* __restrict__ Zt, int64_t ldz,
+                    float* m, float* l, float* alpha, float* mt, float* lt, float* szt,
+                    float* alpha_t, const int* run_if) {
+  if (run_if != nullptr && *run_if == 0) return;
   __shared__ float s_m[2];
   constexpr int kWarps = kT / 32;
   constexpr int kSv = kT * 64 / kStatTile / 32;  // tile stats per lane
   __shared__ float s_red[kWarps];
-  const int64_t r = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __nv_bfloat16* zs = Zs + r * ldz;
-  __nv_bfloat16* zt = Zt + r * ldz;
-  // the thread's share of both rows is loaded before the stats folds (all loads of the
-  // rows in flight together; see combine_kernel)
-  constexpr int kPer = 8;
-  uint4 bs[kPer], bt[kPer];
+  for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
+    __nv_bfloat16* zs = Zs + r * ldz;
+    __nv_bfloat16* zt = Zt + r * ldz;
+    // the thread's share of both rows is loaded before the stats folds (all loads of
+    // the rows in flight together; see combine_kernel)
+    constexpr int kPer = 8;
+    uint4 bs[kPer], bt[kPer];
 #pragma unroll
-  for (int q = 0; q < kPer; ++q) {
-    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * kT) * 8;
-    if (c < vc) {
-      bs[q] = *reinterpret_cast<const uint4*>(zs + c);
-      bt[q] = *reinterpret_cast<const uint4*>(zt + c);
+    for (int q = 0; q < kPer; ++q) {
+      const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * kT) * 8;
+      if (c < vc) {
+        bs[q] = *reinterpret_cast<const uint4*>(zs + c);
+        bt[q] = *reinterpret_cast<const uint4*>(zt + c);
+      }
     }
-  }
-  if (warp == 0) {
-    const float ms = fold_stats<kSv>(stats_s + r * stats_ld, nt, m + r, l + r, alpha + r, lane);
-    if (lane == 0) s_m[0] = ms;
-  } else if (warp == 1) {
-    const float mtn =
-        fold_stats<kSv>(stats_t + r * stats_ld, nt, mt + r, lt + r, alpha_t + r, lane);
-    if (lane == 0) s_m[1] = mtn;
-  }
-  __syncthreads();
-  const float ms = s_m[0], mtn = s_m[1];
-  float acc = 0.f;
-#pragma unroll
-  for (int q = 0; q < kPer; ++q) {
-    const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * kT) * 8;
-    if (c >= vc) continue;
-    uint4 us = bs[q];
-    uint4 ut = bt[q];
-    __nv_bfloat162* hs = reinterpret_cast<__nv_bfloat162*>(&us);
-    __nv_bfloat162* ht = reinterpret_cast<__nv_bfloat162*>(&ut);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 z = __bfloat1622float2(hs[i]), t = __bfloat1622float2(ht[i]);
-      const float p0 = __expf(t.x - mtn), p1 = __expf(t.y - mtn);
-      acc += p0 * z.x + p1 * z.y;
-      hs[i] = __floats2bfloat162_rn(__expf(z.x - ms), __expf(z.y - ms));
-      ht[i] = __floats2bfloat162_rn(p0, p1);
+    if (warp == 0) {
+      const float ms = fold_stats<kSv>(stats_s + r * stats_ld, nt, m + r, l + r, alpha + r, lane);
+      if (lane == 0) s_m[0] = ms;
+    } else if (warp == 1) {
+      const float mtn =
+          fold_stats<kSv>(stats_t + r * stats_ld, nt, mt + r, lt + r, alpha_t + r, lane);
+      if (lane == 0) s_m[1] = mtn;
     }
-    *reinterpret_cast<uint4*>(zs + c) = us;
-    *reinterpret_cast<uint4*>(zt + c) = ut;
-  }
-  acc = warp_sum(acc);
-  if (lane == 0) s_red[warp] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
+    __syncthreads();
+    const float ms = s_m[0], mtn = s_m[1];
+    float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) t += s_red[w];
-    szt[r] = szt[r] * alpha_t[r] + t;
+    for (int q = 0; q < kPer; ++q) {
+      const int64_t c = ((int64_t)threadIdx.x + (int64_t)q * kT) * 8;
+      if (c >= vc) continue;
+      uint4 us = bs[q];
+      uint4 ut = bt[q];
+      __nv_bfloat162* hs = reinterpret_cast<__nv_bfloat162*>(&us);
+      __nv_bfloat162* ht = reinterpret_cast<__nv_bfloat162*>(&ut);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 z = __bfloat1622float2(hs[i]), t = __bfloat1622float2(ht[i]);
+        const float p0 = __expf(t.x - mtn), p1 = __expf(t.y - mtn);
+        acc += p0 * z.x + p1 * z.y;
+        hs[i] = __floats2bfloat162_rn(__expf(z.x - ms), __expf(z.y - ms));
+        ht[i] = __floats2bfloat162_rn(p0, p1);
+      }
+      *reinterpret_cast<uint4*>(zs + c) = us;
+      *reinterpret_cast<uint4*>(zt + c) = ut;
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) s_red[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) t += s_red[w];
+      szt[r] = szt[r] * alpha_t[r] + t;
+    }
+    __syncthreads();  // s_m / s_red are rewritten for the next row
   }
 }
 
-// dh = scale * (dH_s / l_s - dH_t / l_t)
+// One-pass soft targets (one warp per row): szt = sum_v e^(t_v - m_t) z_v, taken as
+// h . (dH_t keep_last_t), since dH_t = sum_v e^(t_v - m_t') W_v and z_v = h . W_v -- the
+// student's logits themselves are never stored.
+__global__ void __launch_bounds__(256)
+soft_tz_kernel(int64_t R, int64_t H, const __nv_bfloat16* __restrict__ h, int64_t ldh,
+               const float* __restrict__ dHt, const float* __restrict__ keep_last_t,
+               float* __restrict__ szt) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const __nv_bfloat16* hr = h + r * ldh;
+  const float* dr = dHt + r * H;
+  float acc = 0.f;
+  for (int64_t c = (int64_t)lane * 8; c < H; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(hr + c);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const float4 a = reinterpret_cast<const float4*>(dr + c)[0];
+    const float4 b = reinterpret_cast<const float4*>(dr + c)[1];
+    const float2 h0 = __bfloat1622float2(h2[0]), h1 = __bfloat1622float2(h2[1]);
+    const float2 h2f = __bfloat1622float2(h2[2]), h3 = __bfloat1622float2(h2[3]);
+    acc += h0.x * a.x + h0.y * a.y + h1.x * a.z + h1.y * a.w;
+    acc += h2f.x * b.x + h2f.y * b.y + h3.x * b.z + h3.y * b.w;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) szt[r] = acc * keep_last_t[r];
+}
+
+// dh = scale * (dH_s ks / l_s - dH_t kt / l_t), ks / kt the last chunk's rescale factors
+// (1 after the two-pass algorithm)
 __global__ void soft_dh_kernel(int64_t R, int64_t H, const float* __restrict__ dHs,
                                const float* __restrict__ dHt, const float* __restrict__ l,
-                               const float* __restrict__ lt, float scale,
+                               const float* __restrict__ lt, const float* __restrict__ ks,
+                               const float* __restrict__ kt, float scale,
                                __nv_bfloat16* __restrict__ dh, int64_t lddh) {
   const int64_t total = R * H / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = i * 8;
     const int64_t r = e / H, c = e - r * H;
-    const float is = 1.f / l[r], it = 1.f / lt[r];
+    const float is = ks[r] / l[r], it = kt[r] / lt[r];
     float o[8];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
@@ -864,7 +926,13 @@ bool soft_fast_eligible(int dtype, int64_t H, int64_t V, const void* h, int64_t 
 }
 
 // Same two-stream chunk pipeline as lmhead_fast, with the teacher's logits GEMM next
-// to the student's and two dH accumulations on the side stream.
+// to the student's and two dH accumulations on the side stream.  As there, a row
+// group's first chunk is two-pass (both GEMMs store bf16 logits, two folds, two
+// in-place rewrites as e^(z - m0)) and every later chunk one-pass (both GEMMs write
+// e^(z - m) / e^(t - m_t) directly, two folds); the loss's S_tz = sum_v e^(t_v - m_t)
+// z_v is h . dH_t at the end (soft_tz_kernel).  An overflow of either running maximum
+// recomputes the call two-pass (the combine pass, which also accumulates S_tz from the
+// stored logits); algo bit 28 runs every chunk that way.
 int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh, const void* W,
                      const void* teacher, int64_t ldt, float grad_scale, void* dh, int64_t lddh,
                      float* loss_sum, uint8_t* ws, int algo, int* status, cudaStream_t st) {
@@ -880,10 +948,37 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
   float* szt = (float*)(ws + L.szt);
   float* alpha_t = (float*)(ws + L.alpha_t);
   float* lse_t = (float*)(ws + L.lse_t);
+  float* ks[3] = {(float*)(ws + L.keep_s[0]), (float*)(ws + L.keep_s[1]),
+                  (float*)(ws + L.keep_s[2])};
+  float* kt[3] = {(float*)(ws + L.keep_t[0]), (float*)(ws + L.keep_t[1]),
+                  (float*)(ws + L.keep_t[2])};
+  float* ks_last = (float*)(ws + L.keep_last_s);
+  float* kt_last = (float*)(ws + L.keep_last_t);
+  float* m0s = (float*)(ws + L.m0_s);
+  float* m0t = (float*)(ws + L.m0_t);
+  int* flag = (int*)(ws + L.flag);
   float* dHs = (float*)(ws + L.dHs);
   float* dHt = (float*)(ws + L.dHt);
   const int64_t VC = P.vc;
   const int nt_max = (int)((VC + kStatTile - 1) / kStatTile);
+  const bool two_pass = (algo >> 28) & 1;
+  auto exp_first = VC <= 16384 ? exp_first_kernel<8> : exp_first_kernel<16>;
+  // the two-pass combine over rows [r0, r0 + rg): one row per block, or (conditional
+  // recomputation) a small grid walking the rows
+  auto combine_soft = [&](int64_t rg, int64_t r0, int64_t vc, int nt, const float2* ss,
+                          const float2* stt, __nv_bfloat16* Zs, __nv_bfloat16* Zt,
+                          const int* run_if, cudaStream_t s) {
+    const int64_t cap = 2 * (int64_t)sm_count();
+    const unsigned grid = (unsigned)(run_if && rg > cap ? cap : rg);
+    if (VC <= 16384)
+      combine_soft_kernel<256><<<grid, 256, 0, s>>>(rg, vc, nt, nt_max, ss, stt, Zs, Zt, VC,
+                                                    m + r0, l + r0, alpha + r0, mt + r0, lt + r0,
+                                                    szt + r0, alpha_t + r0, run_if);
+    else
+      combine_soft_kernel<512><<<grid, 512, 0, s>>>(rg, vc, nt, nt_max, ss, stt, Zs, Zt, VC,
+                                                    m + r0, l + r0, alpha + r0, mt + r0, lt + r0,
+                                                    szt + r0, alpha_t + r0, run_if);
+  };
   cudaStream_t side = side_stream(0);
   cudaEvent_t ev_fork = pool_event(0), ev_join = pool_event(1);
   cudaEvent_t ev_logits[2] = {pool_event(2), pool_event(3)};
@@ -892,7 +987,8 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
     set_error("lmhead_ce: could not create the side stream or its events");
     return PE_ERR_CUDA;
   }
-  init_stats_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, zlab, mt, lt, szt);
+  soft_init_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, mt, lt, szt, ks_last, kt_last, flag,
+                                                nullptr);
   PE_LAUNCHED();
   PE_CUDA_TRY(cudaEventRecord(ev_fork, st));
   PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_fork, 0));
@@ -901,6 +997,9 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
     const int64_t rg = (R - r0) < P.rg ? (R - r0) : P.rg;
     const void* hg = (const __nv_bfloat16*)h + r0 * ldh;
     const void* tg = (const __nv_bfloat16*)teacher + r0 * ldt;
+    float* dHsg = dHs + r0 * H;
+    float* dHtg = dHt + r0 * H;
+    const unsigned fold_grid = (unsigned)((rg + 7) / 8);
     for (int64_t v0 = 0; v0 < V; v0 += VC, ++t) {
       const int b = (int)(t & 1);
       const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
@@ -910,42 +1009,116 @@ int lmhead_fast_soft(int64_t R, int64_t H, int64_t V, const void* h, int64_t ldh
       __nv_bfloat16* Zt = (__nv_bfloat16*)(ws + L.Zt[b]);
       float2* ss = (float2*)(ws + L.stats_s[b]);
       float2* stt = (float2*)(ws + L.stats_t[b]);
+      float* kst = ks[t % 3] + r0;
+      float* ktt = kt[t % 3] + r0;
       if (t >= 2) PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_dh[b], 0));
-      int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Zs, VC, ss, nt_max, status, st,
-                                    P.logits_bn);
-      if (!rc)
-        rc = gemm_tc_logits_stats(rg, vc, H, tg, ldt, Wc, H, Zt, VC, stt, nt_max, status, st,
+      int rc;
+      if (two_pass || v0 == 0) {
+        rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Zs, VC, ss, nt_max, status, st,
                                   P.logits_bn);
-      if (rc) return rc;
-      PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
-      PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
-      if (VC <= 16384)
-        combine_soft_kernel<256><<<(unsigned)rg, 256, 0, side>>>(
-            vc, nt, nt_max, ss, stt, Zs, Zt, VC, m + r0, l + r0, alpha + r0, mt + r0, lt + r0,
-            szt + r0, alpha_t + r0);
-      else
-        combine_soft_kernel<512><<<(unsigned)rg, 512, 0, side>>>(
-            vc, nt, nt_max, ss, stt, Zs, Zt, VC, m + r0, l + r0, alpha + r0, mt + r0, lt + r0,
-            szt + r0, alpha_t + r0);
-      PE_LAUNCHED();
-      rc = gemm_tc_rowscale_acc(rg, H, vc, Zs, VC, Wc, H, dHs + r0 * H, H,
-                                v0 > 0 ? dHs + r0 * H : nullptr, alpha + r0, status, side,
-                                P.dh_bn);
-      if (!rc)
-        rc = gemm_tc_rowscale_acc(rg, H, vc, Zt, VC, Wc, H, dHt + r0 * H, H,
-                                  v0 > 0 ? dHt + r0 * H : nullptr, alpha_t + r0, status, side,
-                                  P.dh_bn);
+        if (!rc)
+          rc = gemm_tc_logits_stats(rg, vc, H, tg, ldt, Wc, H, Zt, VC, stt, nt_max, status, st,
+                                    P.logits_bn);
+        if (rc) return rc;
+        if (!two_pass) {
+          fold_first_kernel<<<fold_grid, 256, 0, st>>>(rg, vc, nt, nt_max, ss, Zs, VC, nullptr,
+                                                       m + r0, l + r0, m0s + r0, zlab + r0, kst,
+                                                       ks_last + r0);
+          PE_LAUNCHED();
+          fold_first_kernel<<<fold_grid, 256, 0, st>>>(rg, vc, nt, nt_max, stt, Zt, VC, nullptr,
+                                                       mt + r0, lt + r0, m0t + r0, zlab + r0,
+                                                       ktt, kt_last + r0);
+          PE_LAUNCHED();
+        }
+        PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
+        PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
+        if (two_pass) {
+          combine_soft(rg, r0, vc, nt, ss, stt, Zs, Zt, nullptr, side);
+        } else {
+          exp_first<<<(unsigned)rg, 256, 0, side>>>(vc, Zs, VC, nullptr, m0s + r0);
+          PE_LAUNCHED();
+          exp_first<<<(unsigned)rg, 256, 0, side>>>(vc, Zt, VC, nullptr, m0t + r0);
+        }
+        PE_LAUNCHED();
+        // two-pass chunks rescale by the combine's alpha; a first chunk ignores the
+        // factor (no accumulated input)
+        rc = gemm_tc_rowscale_acc(rg, H, vc, Zs, VC, Wc, H, dHsg, H, v0 > 0 ? dHsg : nullptr,
+                                  two_pass ? alpha + r0 : kst, status, side, P.dh_bn);
+        if (!rc)
+          rc = gemm_tc_rowscale_acc(rg, H, vc, Zt, VC, Wc, H, dHtg, H, v0 > 0 ? dHtg : nullptr,
+                                    two_pass ? alpha_t + r0 : ktt, status, side, P.dh_bn);
+      } else {
+        rc = gemm_tc_logits_pexp(rg, vc, H, hg, ldh, Wc, H, Zs, VC, ss, nt_max, m + r0, nullptr,
+                                 v0, nullptr, flag, status, st, P.logits_bn);
+        if (!rc)
+          rc = gemm_tc_logits_pexp(rg, vc, H, tg, ldt, Wc, H, Zt, VC, stt, nt_max, mt + r0,
+                                   nullptr, v0, nullptr, flag, status, st, P.logits_bn);
+        if (rc) return rc;
+        fold_kernel<<<fold_grid, 256, 0, st>>>(rg, nt, nt_max, ss, m + r0, l + r0, kst,
+                                               ks_last + r0);
+        PE_LAUNCHED();
+        fold_kernel<<<fold_grid, 256, 0, st>>>(rg, nt, nt_max, stt, mt + r0, lt + r0, ktt,
+                                               kt_last + r0);
+        PE_LAUNCHED();
+        PE_CUDA_TRY(cudaEventRecord(ev_logits[b], st));
+        PE_CUDA_TRY(cudaStreamWaitEvent(side, ev_logits[b], 0));
+        rc = gemm_tc_rowscale_acc(rg, H, vc, Zs, VC, Wc, H, dHsg, H, dHsg, ks[(t + 2) % 3] + r0,
+                                  status, side, P.dh_bn);
+        if (!rc)
+          rc = gemm_tc_rowscale_acc(rg, H, vc, Zt, VC, Wc, H, dHtg, H, dHtg,
+                                    kt[(t + 2) % 3] + r0, status, side, P.dh_bn);
+      }
       if (rc) return rc;
       PE_CUDA_TRY(cudaEventRecord(ev_dh[b], side));
     }
   }
   PE_CUDA_TRY(cudaEventRecord(ev_join, side));
   PE_CUDA_TRY(cudaStreamWaitEvent(st, ev_join, 0));
+  if (!two_pass) {
+    // S_tz from the teacher's dH (before a recomputation, which would overwrite it)
+    soft_tz_kernel<<<(unsigned)((R + 7) / 8), 256, 0, st>>>(R, H, (const __nv_bfloat16*)h, ldh,
+                                                            dHt, kt_last, szt);
+    PE_LAUNCHED();
+    // recomputation after an overflow: every launch conditional on the overflow word
+    soft_init_kernel<<<grid_for(R), 256, 0, st>>>(R, m, l, mt, lt, szt, ks_last, kt_last,
+                                                  nullptr, flag);
+    PE_LAUNCHED();
+    __nv_bfloat16* Zs = (__nv_bfloat16*)(ws + L.Zs[0]);
+    __nv_bfloat16* Zt = (__nv_bfloat16*)(ws + L.Zt[0]);
+    float2* ss = (float2*)(ws + L.stats_s[0]);
+    float2* stt = (float2*)(ws + L.stats_t[0]);
+    for (int64_t r0 = 0; r0 < R; r0 += P.rg) {
+      const int64_t rg = (R - r0) < P.rg ? (R - r0) : P.rg;
+      const void* hg = (const __nv_bfloat16*)h + r0 * ldh;
+      const void* tg = (const __nv_bfloat16*)teacher + r0 * ldt;
+      float* dHsg = dHs + r0 * H;
+      float* dHtg = dHt + r0 * H;
+      for (int64_t v0 = 0; v0 < V; v0 += VC) {
+        const int64_t vc = (V - v0) < VC ? (V - v0) : VC;
+        const int nt = (int)((vc + kStatTile - 1) / kStatTile);
+        const __nv_bfloat16* Wc = (const __nv_bfloat16*)W + v0 * H;
+        int rc = gemm_tc_logits_stats(rg, vc, H, hg, ldh, Wc, H, Zs, VC, ss, nt_max, status, st,
+                                      P.logits_bn, flag);
+        if (!rc)
+          rc = gemm_tc_logits_stats(rg, vc, H, tg, ldt, Wc, H, Zt, VC, stt, nt_max, status, st,
+                                    P.logits_bn, flag);
+        if (rc) return rc;
+        combine_soft(rg, r0, vc, nt, ss, stt, Zs, Zt, flag, st);
+        PE_LAUNCHED();
+        rc = gemm_tc_rowscale_acc(rg, H, vc, Zs, VC, Wc, H, dHsg, H, v0 > 0 ? dHsg : nullptr,
+                                  alpha + r0, status, st, P.dh_bn, flag);
+        if (!rc)
+          rc = gemm_tc_rowscale_acc(rg, H, vc, Zt, VC, Wc, H, dHtg, H, v0 > 0 ? dHtg : nullptr,
+                                    alpha_t + r0, status, st, P.dh_bn, flag);
+        if (rc) return rc;
+      }
+    }
+  }
   finalize_kernel<<<1, kFinThreads, 0, st>>>(R, nullptr, m, l, zlab, mt, lt, szt, lse, lse_t,
-                                          loss_sum);
+                                             loss_sum);
   PE_LAUNCHED();
-  soft_dh_kernel<<<grid_for(R * H / 8), 256, 0, st>>>(R, H, dHs, dHt, l, lt, grad_scale,
-                                                      (__nv_bfloat16*)dh, lddh);
+  soft_dh_kernel<<<grid_for(R * H / 8), 256, 0, st>>>(R, H, dHs, dHt, l, lt, ks_last, kt_last,
+                                                      grad_scale, (__nv_bfloat16*)dh, lddh);
   PE_LAUNCHED();
   return PE_OK;
 }

@@ -590,6 +590,38 @@ def test_lmhead_soft_targets_across_chunk_widths(chunk_k):
 
 
 @pytest.mark.parametrize("boost", [40.0, 150.0])
+@pytest.mark.parametrize("who", ["student", "teacher"])
+def test_lmhead_soft_late_chunk_maximum(who, boost):
+    """Soft targets with a late-chunk maximum in the student's or the teacher's logits:
+    carried by the folds' rescale factors (~40 above the first chunk's maximum) or, past
+    e^64 (~150), by the two-pass recomputation.  Against dense fp32 torch."""
+    R, H, V = 600, 256, 5000
+    g = torch.Generator().manual_seed(48)
+    u = torch.randn(H, generator=g)
+    u = u / u.norm()
+    h = torch.randn(R, H, generator=g)
+    tch = torch.randn(R, H, generator=g)
+    big = torch.arange(0, R, 3)
+    (h if who == "student" else tch)[big] += (boost / 1.5) * u
+    W = torch.randn(V, H, generator=g) * 0.05
+    W[3500] = 1.5 * u
+    h, tch, W = h.bfloat16(), tch.bfloat16(), W.bfloat16()
+    loss = torch.zeros(1, dtype=torch.float32, device=DEV)
+    dh = ops.lmhead_ce(h.to(DEV), W.to(DEV), None, 0.01, loss, teacher=tch.to(DEV),
+                       algo=L.ALGO_AUTO | (1 << 8))  # 1024-column chunks: five chunks
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    hr = h.float().requires_grad_(True)
+    z = (hr @ W.float().t()).bfloat16().float()
+    pt = torch.softmax((tch.float() @ W.float().t()).bfloat16().float(), -1)
+    lr = -(pt * torch.log_softmax(z, -1)).sum()
+    (lr * 0.01).backward()
+    assert torch.isfinite(dh.float()).all()
+    assert abs(loss.item() - lr.item()) / abs(lr.item()) < 1e-4
+    assert rel(dh.float().cpu(), hr.grad) < 2e-2
+
+
+@pytest.mark.parametrize("boost", [40.0, 150.0])
 def test_lmhead_ce_late_chunk_maximum(boost):
     """Rows whose largest logit lies in a late vocabulary chunk, far above the first
     chunk's maximum.  Every chunk after the first writes e^(z - running max) straight
