@@ -256,8 +256,8 @@ int pe_attn_bwd_segments(int dtype, int nseg, const int64_t* bounds, int kdepth,
  * of W, at most 32) and bits 16-23 the
  * loss-row group (units of 256 rows, at most 40); zero keeps the defaults (32768
  * and 10240).  Bits 24-25 / 26-27 pick the logits / dH GEMM
- * tile width (1: 256, 2: 512, 0: automatic).  With hard labels, every vocabulary
- * chunk after a row group's first is one pass (the logits GEMM writes e^(z - running
+ * tile width (1: 256, 2: 512, 0: automatic).  On both bf16 paths every vocabulary
+ * chunk after a row group's first is one pass (the logits GEMMs write e^(z - running
  * max) directly; a logit more than 64 above its row's running maximum makes the call
  * recompute itself two-pass on the device); bit 28 runs every chunk two-pass.
  * Replaces reference src/pe/partition.py:113-115 (lm_head -> float ->
